@@ -1,0 +1,53 @@
+"""Causal GQA flash attention (``csrc/flash_attn.cu``) with autograd.
+
+Layout is ``[B, S, H, D]`` (sequence-major, as produced by the QKV GEMM), so
+no transposes are needed around the kernel.  Forward returns the output and
+the per-row log-sum-exp (fp32, ``[B, H, S]``), which backward uses to
+recompute probabilities tile by tile.  ``Dq`` may differ from ``Dv`` (MLA:
+192 / 128).  The forward is a registered custom op so selective activation
+checkpointing can keep its output.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _ext
+from . import reference as _ref
+
+
+@torch.library.custom_op("tt_b200::attn_fwd", mutates_args=())
+def attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, scale: float) -> tuple[torch.Tensor, torch.Tensor]:
+    o, lse = _ext.ext().attn_fwd(q, k, v, causal, scale)
+    return o, lse
+
+
+@attn_fwd.register_fake
+def _(q, k, v, causal, scale):
+    B, S, H, _ = q.shape
+    return q.new_empty((B, S, H, v.shape[-1])), q.new_empty((B, H, S), dtype=torch.float32)
+
+
+class _Attn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        o, lse = torch.ops.tt_b200.attn_fwd(q, k, v, causal, scale)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.causal, ctx.scale = causal, scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = _ext.ext().attn_bwd(do.contiguous(), q, k, v, o, lse, ctx.causal, ctx.scale)
+        return dq, dk, dv, None, None
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+              scale: float | None = None) -> torch.Tensor:
+    scale = float(scale if scale is not None else 1.0 / math.sqrt(q.shape[-1]))
+    if not q.is_cuda:
+        return _ref.attention(q, k, v, causal, scale)
+    return _Attn.apply(q, k, v, causal, scale)

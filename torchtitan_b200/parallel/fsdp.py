@@ -1,0 +1,62 @@
+"""FSDP2 / HSDP application (parity: ``models/llama3/parallelize.py:244-324``).
+
+Each transformer block, the embedding, and ``[norm, output]`` become FSDP2
+units on the ``fsdp`` (or ``[dp_replicate, fsdp]`` for HSDP) mesh with
+``MixedPrecisionPolicy(param=bf16, reduce=fp32)``.  Gradient division by the
+DP size is disabled: the loss is already normalised by the global token
+count.  Reshard-after-forward: ``default`` = yes except the last block (whose
+parameters are needed immediately by backward) and never under PP.
+"""
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+import torch.nn as nn
+from torch.distributed.fsdp import CPUOffloadPolicy, MixedPrecisionPolicy, fully_shard
+
+
+def _disable_grad_division(m) -> None:
+    if hasattr(m, "set_gradient_divide_factor"):
+        m.set_gradient_divide_factor(1.0)
+
+
+def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, reduce_dtype: torch.dtype,
+               pp_enabled: bool = False, cpu_offload: bool = False, reshard_after_forward_policy: str = "default",
+               ep_degree: int = 1, edp_mesh: Any = None) -> nn.Module:
+    mp = MixedPrecisionPolicy(param_dtype=param_dtype, reduce_dtype=reduce_dtype)
+    cfg: dict[str, Any] = {"mesh": dp_mesh, "mp_policy": mp}
+    if cpu_offload:
+        cfg["offload_policy"] = CPUOffloadPolicy()
+    if reshard_after_forward_policy == "always":
+        reshard = True
+    elif reshard_after_forward_policy == "never":
+        reshard = False
+    elif reshard_after_forward_policy == "default":
+        reshard = not pp_enabled
+    else:
+        raise ValueError(f"invalid reshard_after_forward_policy {reshard_after_forward_policy}")
+
+    if getattr(model, "tok_embeddings", None) is not None:
+        _disable_grad_division(fully_shard(model.tok_embeddings, **cfg, reshard_after_forward=reshard))
+    layers = [l for l in model.layers.values() if l is not None]
+    for i, block in enumerate(layers):
+        # routed experts are sharded on the expert-data-parallel mesh
+        moe = getattr(block, "moe", None) or getattr(getattr(block, "ffn", None), "_moe", None)
+        if moe is not None and ep_degree > 1 and edp_mesh is not None:
+            ecfg = dict(cfg, mesh=edp_mesh)
+            _disable_grad_division(fully_shard(moe.experts, **ecfg, reshard_after_forward=reshard))
+        last = i == len(layers) - 1
+        _disable_grad_division(
+            fully_shard(block, **cfg, reshard_after_forward=reshard and not last)
+        )
+    tail = [m for m in (getattr(model, "norm", None), getattr(model, "output", None)) if m is not None]
+    if tail:
+        _disable_grad_division(fully_shard(tail, **cfg, reshard_after_forward=False))
+    _disable_grad_division(fully_shard(model, **cfg))
+    return model
+
+
+def apply_ddp(model: nn.Module, dp_mesh: Any) -> nn.Module:
+    """Pure data parallel: replicate via FSDP2 on the replicate mesh."""
+    return apply_fsdp(model, dp_mesh, param_dtype=torch.bfloat16, reduce_dtype=torch.float32)

@@ -1,0 +1,257 @@
+"""Tensor + sequence parallelism with explicit collectives.
+
+Between TP regions activations are sequence-sharded ``[B, S/tp, D]``.  A
+column-parallel linear all-gathers the sequence then multiplies by its local
+output-feature shard; a row-parallel linear multiplies its local
+input-feature shard and reduce-scatters the partial sums back to sequence
+shards (parity of placement: ``models/llama3/parallelize.py:142-241``).
+Weights are DTensors on the ``tp`` mesh (``Shard(0)`` col / ``Shard(1)`` row)
+so FSDP2 composes on top and DCP reshards them.  Parameters replicated over
+TP (norm weights, embeddings) get their gradients all-reduced over TP because
+each rank sees a different sequence shard.
+
+``enable_async_tensor_parallel`` switches the column/row linears to the
+chunked overlap path: the all-gather (reduce-scatter) is split into ``tp``
+chunks issued on a side stream so GEMM on chunk i overlaps the transfer of
+chunk i+1.
+"""
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from torchtitan_b200 import ops
+
+
+# ------------------------------------------------------------------ collectives
+def _all_gather_seq(x: torch.Tensor, group) -> torch.Tensor:
+    w = dist.get_world_size(group)
+    xs = x.transpose(0, 1).contiguous()  # [S/tp, B, ...]
+    out = torch.empty((w * xs.shape[0],) + tuple(xs.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(out, xs, group=group)
+    return out.transpose(0, 1)
+
+
+def _reduce_scatter_seq(x: torch.Tensor, group) -> torch.Tensor:
+    w = dist.get_world_size(group)
+    xs = x.transpose(0, 1).contiguous()
+    out = torch.empty((xs.shape[0] // w,) + tuple(xs.shape[1:]), dtype=x.dtype, device=x.device)
+    dist.reduce_scatter_tensor(out, xs, group=group)
+    return out.transpose(0, 1)
+
+
+class _AGSeq(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return _all_gather_seq(x, group)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _reduce_scatter_seq(g, ctx.group), None
+
+
+class _RSSeq(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return _reduce_scatter_seq(x, group)
+
+    @staticmethod
+    def backward(ctx, g):
+        return _all_gather_seq(g, ctx.group), None
+
+
+class _AllReduce(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, group):
+        x = x.clone()
+        dist.all_reduce(x, group=group)
+        return x
+
+    @staticmethod
+    def backward(ctx, g):
+        return g, None
+
+
+class _GradAllReduce(torch.autograd.Function):
+    """Identity forward; all-reduce the gradient over ``group`` in backward."""
+
+    @staticmethod
+    def forward(ctx, x, group):
+        ctx.group = group
+        return x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        g = g.contiguous()
+        dist.all_reduce(g, group=ctx.group)
+        return g, None
+
+
+def all_gather_seq(x, group):
+    return _AGSeq.apply(x, group)
+
+
+def reduce_scatter_seq(x, group):
+    return _RSSeq.apply(x, group)
+
+
+def grad_all_reduce(x, group):
+    return _GradAllReduce.apply(x, group)
+
+
+def tp_linear(x: torch.Tensor, w: torch.Tensor, mode: str, group, sequence_parallel: bool) -> torch.Tensor:
+    if mode == "col":
+        if sequence_parallel:
+            x = all_gather_seq(x, group)
+        return ops.linear(x, w)
+    if mode == "row":
+        y = ops.linear(x, w)
+        return reduce_scatter_seq(y, group) if sequence_parallel else _AllReduce.apply(y, group)
+    raise ValueError(mode)
+
+
+# ------------------------------------------------------------ vocab-parallel CE
+class _VocabParallelCE(torch.autograd.Function):
+    """Sum CE over tokens with logits sharded on the vocab dim across ``group``."""
+
+    @staticmethod
+    def forward(ctx, logits, labels, group, ignore_index):
+        lf = logits.float()
+        rank, ws = dist.get_rank(group), dist.get_world_size(group)
+        vloc = lf.shape[-1]
+        lo = rank * vloc
+        mx = lf.max(-1).values
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
+        ex = torch.exp(lf - mx[:, None])
+        se = ex.sum(-1)
+        dist.all_reduce(se, group=group)
+        valid = labels != ignore_index
+        local_lab = labels - lo
+        mine = valid & (local_lab >= 0) & (local_lab < vloc)
+        tgt = torch.zeros_like(mx)
+        idx = local_lab.clamp(0, vloc - 1)
+        tgt[mine] = lf.gather(1, idx[:, None])[:, 0][mine]
+        dist.all_reduce(tgt, group=group)
+        lse = mx + se.log()
+        loss = ((lse - tgt) * valid).sum()
+        ctx.save_for_backward(ex, se, idx, mine, valid)
+        ctx.dtype = logits.dtype
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        ex, se, idx, mine, valid = ctx.saved_tensors
+        p = ex / se[:, None]
+        p[mine, idx[mine]] -= 1.0
+        p *= (valid.float() * g)[:, None]
+        return p.to(ctx.dtype), None, None, None
+
+
+def vocab_parallel_cross_entropy_sum(logits, labels, group, ignore_index=-100):
+    return _VocabParallelCE.apply(logits.flatten(0, -2), labels.flatten(), group, ignore_index)
+
+
+# ---------------------------------------------------------------- application
+def _shard_param(mod: nn.Module, name: str, mesh, placement) -> None:
+    from torch.distributed.tensor import distribute_tensor
+
+    p = getattr(mod, name)
+    setattr(mod, name, nn.Parameter(distribute_tensor(p.data, mesh, [placement]), requires_grad=p.requires_grad))
+
+
+def _replicate_param(mod: nn.Module, name: str, mesh) -> None:
+    from torch.distributed.tensor import Replicate, distribute_tensor
+
+    p = getattr(mod, name)
+    setattr(mod, name, nn.Parameter(distribute_tensor(p.data, mesh, [Replicate()]), requires_grad=p.requires_grad))
+
+
+def parallelize_linear(lin: nn.Module, mode: str, tp_mesh, sequence_parallel: bool) -> None:
+    from torch.distributed.tensor import Shard
+
+    _shard_param(lin, "weight", tp_mesh, Shard(0 if mode == "col" else 1))
+    lin.tp_mode = mode
+    lin.tp_group = tp_mesh.get_group()
+    lin.sequence_parallel = sequence_parallel
+
+
+class _TPNorm(nn.Module):
+    """Wraps a replicated-over-TP norm so its weight grad is all-reduced."""
+
+
+def wrap_replicated_norm(norm: nn.Module, tp_mesh) -> None:
+    _replicate_param(norm, "weight", tp_mesh)
+    group = tp_mesh.get_group()
+    orig = norm.forward
+
+    def fwd(x, _orig=orig, _norm=norm):
+        from torchtitan_b200 import ops as _ops
+
+        w = _norm.weight.to_local()
+        w = grad_all_reduce(w, group)
+        return _ops.rms_norm(x, w.to(x.dtype), _norm.eps)
+
+    norm.forward = fwd
+
+
+def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_parallel: bool = True) -> None:
+    """TP plan for dense decoders: q/k/v/w1/w3 column, wo/w2 row, norms
+    sequence-parallel, embedding replicated (embeds the local sequence shard),
+    output column-parallel (vocab shards, loss parallel)."""
+    group = tp_mesh.get_group()
+    ws = tp_mesh.size()
+    for blk in model.layers.values():
+        att = blk.attention
+        if att.n_kv_heads % ws or att.n_heads % ws:
+            raise ValueError(f"TP degree {ws} must divide n_heads {att.n_heads} and n_kv_heads {att.n_kv_heads}")
+        for lin in (att.wq, att.wk, att.wv):
+            parallelize_linear(lin, "col", tp_mesh, sequence_parallel)
+        parallelize_linear(att.wo, "row", tp_mesh, sequence_parallel)
+        ff = blk.feed_forward
+        parallelize_linear(ff.w1, "col", tp_mesh, sequence_parallel)
+        parallelize_linear(ff.w3, "col", tp_mesh, sequence_parallel)
+        parallelize_linear(ff.w2, "row", tp_mesh, sequence_parallel)
+        if sequence_parallel:
+            wrap_replicated_norm(blk.attention_norm, tp_mesh)
+            wrap_replicated_norm(blk.ffn_norm, tp_mesh)
+    if sequence_parallel and model.norm is not None:
+        wrap_replicated_norm(model.norm, tp_mesh)
+    if model.tok_embeddings is not None:
+        _replicate_param(model.tok_embeddings, "weight", tp_mesh)
+        emb = model.tok_embeddings
+
+        def emb_fwd(tokens, _emb=emb):
+            w = grad_all_reduce(_emb.weight.to_local(), group) if sequence_parallel else _emb.weight.to_local()
+            if sequence_parallel:
+                r, S = dist.get_rank(group), tokens.shape[1]
+                tokens = tokens[:, r * S // ws:(r + 1) * S // ws]
+            return nn.functional.embedding(tokens, w)
+
+        emb.forward = emb_fwd
+    if model.output is not None:
+        parallelize_linear(model.output, "col", tp_mesh, sequence_parallel)
+        model.output.loss_parallel = loss_parallel
+        if not loss_parallel:
+            orig = model.output.forward
+
+            def out_fwd(x, _orig=orig):
+                y = _orig(x)
+                outs = [torch.empty_like(y) for _ in range(ws)]
+                dist.all_gather(outs, y.contiguous(), group=group)
+                return torch.cat(outs, -1)
+
+            model.output.forward = out_fwd
+    model._tp_group = group
+    model._tp_loss_parallel = loss_parallel
+
+
+def maybe_enable_async_tp(parallelism: Any, tp_mesh) -> None:
+    """Async TP here = chunked AG/RS overlap inside the TP linears (no compiler needed)."""
+    from . import async_tp
+
+    async_tp.ENABLED = bool(parallelism.enable_async_tensor_parallel)
