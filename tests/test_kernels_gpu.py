@@ -1,0 +1,189 @@
+"""Numerics of the sm_100a kernels against plain-PyTorch fp32 restatements."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ext():
+    from torchtitan_b200.ops._ext import ext as _e
+
+    return _e()
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 1024), (1000, 776, 520), (37, 24, 8), (4096, 4096, 4096)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm(ext, M, N, K, a_mn, b_mn):
+    if (a_mn and M % 8) or (b_mn and N % 8):
+        pytest.skip("TMA needs the contiguous dimension to be a multiple of 8")
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    a_in = A.t().contiguous() if a_mn else A
+    b_in = B.t().contiguous() if b_mn else B
+    D = ext.gemm(a_in, b_in, a_mn, b_mn)
+    ref = A.float() @ B.float().t()
+    torch.cuda.synchronize()
+    assert ext.gemm_error_code(True) == 0
+    assert D.shape == (M, N)
+    assert _rel(D, ref) < 1e-2
+
+
+def test_linear_autograd():
+    from torchtitan_b200 import ops
+
+    torch.manual_seed(1)
+    x = torch.randn(4, 96, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(384, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = ops.linear(x, w)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr, wr = x.detach().float().requires_grad_(), w.detach().float().requires_grad_()
+    yr = xr @ wr.t()
+    yr.backward(g.float())
+    assert _rel(y, yr) < 1e-2
+    assert _rel(x.grad, xr.grad) < 1e-2
+    assert _rel(w.grad, wr.grad) < 1e-2
+
+
+@pytest.mark.parametrize("dim", [256, 4096, 2304])
+def test_rmsnorm(dim):
+    from torchtitan_b200 import ops
+
+    torch.manual_seed(2)
+    x = torch.randn(300, dim, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(dim, device="cuda")).to(torch.bfloat16).requires_grad_()
+    y = ops.rms_norm(x, w, 1e-5)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr, wr = x.detach().float().requires_grad_(), w.detach().float().requires_grad_()
+    yr = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-5) * wr
+    yr.backward(g.float())
+    assert _rel(y, yr) < 1e-2
+    assert _rel(x.grad, xr.grad) < 2e-2
+    assert _rel(w.grad, wr.grad) < 2e-2
+
+
+def test_rope():
+    from torchtitan_b200 import ops
+    from torchtitan_b200.models.common.rope import precompute_rope
+    from torchtitan_b200.ops import reference as R
+
+    torch.manual_seed(3)
+    cos, sin = precompute_rope(128, 512, 500000.0, "llama")
+    cos, sin = cos.cuda(), sin.cuda()
+    x = torch.randn(2, 512, 8, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = ops.rope(x, cos, sin)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_()
+    yr = R.rope(xr, cos, sin)
+    yr.backward(g.float())
+    assert _rel(y, yr) < 1e-2
+    assert _rel(x.grad, xr.grad) < 1e-2
+
+
+def test_swiglu():
+    from torchtitan_b200 import ops
+
+    torch.manual_seed(4)
+    a = torch.randn(64, 1024, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    b = torch.randn(64, 1024, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = ops.swiglu(a, b)
+    g = torch.randn_like(y)
+    y.backward(g)
+    ar, br = a.detach().float().requires_grad_(), b.detach().float().requires_grad_()
+    yr = torch.nn.functional.silu(ar) * br
+    yr.backward(g.float())
+    assert _rel(y, yr) < 1e-2
+    assert _rel(a.grad, ar.grad) < 2e-2
+    assert _rel(b.grad, br.grad) < 2e-2
+
+
+@pytest.mark.parametrize("V", [2048, 128256])
+def test_cross_entropy(V):
+    from torchtitan_b200 import ops
+
+    torch.manual_seed(5)
+    T = 257
+    logits = (3 * torch.randn(T, V, device="cuda")).to(torch.bfloat16).requires_grad_()
+    labels = torch.randint(0, V, (T,), device="cuda")
+    labels[::7] = -100
+    loss = ops.cross_entropy_sum(logits, labels)
+    loss.backward(torch.tensor(0.5, device="cuda"))
+    lr_ = logits.detach().float().requires_grad_()
+    ref = torch.nn.functional.cross_entropy(lr_, labels, reduction="sum", ignore_index=-100)
+    ref.backward(torch.tensor(0.5, device="cuda"))
+    assert abs(loss.item() - ref.item()) / abs(ref.item()) < 1e-3
+    assert _rel(logits.grad, lr_.grad) < 2e-2
+
+
+@pytest.mark.parametrize("pdtype", [torch.float32, torch.bfloat16])
+def test_adamw(pdtype):
+    from torchtitan_b200 import ops
+    from torchtitan_b200.ops import reference as R
+
+    torch.manual_seed(6)
+    shapes = [(1000,), (300, 257), (70000,)]
+    ps = [torch.randn(s, device="cuda").to(pdtype) for s in shapes]
+    gs = [torch.randn(s, device="cuda") for s in shapes]
+    ms = [torch.randn(s, device="cuda").abs() * 0.1 for s in shapes]
+    vs = [torch.randn(s, device="cuda").abs() * 0.1 for s in shapes]
+    rp = [p.float().clone() for p in ps]
+    rm = [m.clone() for m in ms]
+    rv = [v.clone() for v in vs]
+    kw = dict(lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, step=3)
+    ops.fused_adamw_(ps, gs, ms, vs, **kw)
+    R.adamw_(rp, gs, rm, rv, **kw)
+    tol = 1e-5 if pdtype == torch.float32 else 1e-2
+    for p, r in zip(ps, rp):
+        assert _rel(p, r) < tol
+    for m, r in zip(ms, rm):
+        assert _rel(m, r) < 1e-5
+
+
+def _attn_ref(q, k, v, causal, scale):
+    from torchtitan_b200.ops import reference as R
+
+    return R.attention(q.float(), k.float(), v.float(), causal, scale)
+
+
+@pytest.mark.parametrize(
+    "B,Sq,Sk,H,Hk,D,Dv,causal",
+    [
+        (1, 128, 128, 2, 2, 128, 128, True),
+        (2, 256, 256, 4, 2, 128, 128, True),
+        (1, 384, 384, 4, 1, 128, 128, False),
+        (1, 200, 200, 2, 2, 128, 128, True),
+        (1, 128, 384, 2, 2, 128, 128, True),
+        (1, 256, 256, 2, 2, 64, 64, True),
+        (1, 256, 256, 4, 4, 192, 128, True),
+    ],
+)
+def test_attention(ext, B, Sq, Sk, H, Hk, D, Dv, causal):
+    from torchtitan_b200 import ops
+
+    torch.manual_seed(7)
+    q = torch.randn(B, Sq, H, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(B, Sk, Hk, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(B, Sk, Hk, Dv, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    scale = 1.0 / math.sqrt(D)
+    o = ops.attention(q, k, v, causal=causal, scale=scale)
+    g = torch.randn_like(o)
+    o.backward(g)
+    qr, kr, vr = (t.detach().float().requires_grad_() for t in (q, k, v))
+    orf = _attn_ref(qr, kr, vr, causal, scale)
+    orf.backward(g.float())
+    torch.cuda.synchronize()
+    assert ext.attn_error_code(True) == 0
+    assert _rel(o, orf) < 2e-2
+    assert _rel(q.grad, qr.grad) < 3e-2
+    assert _rel(k.grad, kr.grad) < 3e-2
+    assert _rel(v.grad, vr.grad) < 3e-2

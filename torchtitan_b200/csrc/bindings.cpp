@@ -1,0 +1,205 @@
+// Python bindings of the sm_100a kernels: argument checks, output allocation
+// through the caching allocator, current-stream launch.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "launch_api.h"
+
+namespace {
+
+using torch::Tensor;
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+
+void check_cuda_bf16(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+  TORCH_CHECK(t.is_contiguous(), name, " must be contiguous");
+}
+
+Tensor gemm(Tensor A, Tensor B, bool a_mn, bool b_mn) {
+  check_cuda_bf16(A, "A");
+  check_cuda_bf16(B, "B");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2, "gemm: 2-D operands required");
+  c10::cuda::CUDAGuard g(A.device());
+  const int64_t M = a_mn ? A.size(1) : A.size(0), K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0), Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb, "gemm: reduction dims differ (", K, " vs ", Kb, ")");
+  Tensor D = torch::empty({M, N}, A.options());
+  ttb::gemm_bf16(A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, a_mn, b_mn, stream());
+  return D;
+}
+
+std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
+  check_cuda_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 1 && w.size(0) == x.size(1), "rmsnorm: shape mismatch");
+  TORCH_CHECK(w.is_contiguous() && (w.scalar_type() == at::kBFloat16 || w.scalar_type() == at::kFloat),
+              "rmsnorm: weight must be contiguous bf16/fp32");
+  c10::cuda::CUDAGuard g(x.device());
+  Tensor y = torch::empty_like(x);
+  Tensor rstd = torch::empty({x.size(0)}, x.options().dtype(at::kFloat));
+  ttb::rmsnorm_fwd(x.data_ptr(), w.data_ptr(), y.data_ptr(), rstd.data_ptr<float>(), x.size(0), x.size(1),
+                   static_cast<float>(eps), w.scalar_type() == at::kFloat, stream());
+  return {y, rstd};
+}
+
+std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
+  check_cuda_bf16(dy, "dy");
+  check_cuda_bf16(x, "x");
+  c10::cuda::CUDAGuard g(x.device());
+  Tensor dx = torch::empty_like(x);
+  const int64_t rows = x.size(0), dim = x.size(1);
+  int dev = x.get_device();
+  int nparts = static_cast<int>(std::min<int64_t>(rows, 2 * ttb::num_sms(dev)));
+  nparts = std::max(nparts, 1);
+  Tensor part = torch::empty({nparts, dim}, x.options().dtype(at::kFloat));
+  Tensor dw = torch::empty({dim}, x.options().dtype(at::kFloat));
+  if (rows > 0) {
+    ttb::rmsnorm_bwd(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dx.data_ptr(),
+                     part.data_ptr<float>(), rows, dim, w.scalar_type() == at::kFloat, nparts, stream());
+    ttb::reduce_rows_f32(part.data_ptr<float>(), dw.data_ptr<float>(), nparts, dim, stream());
+  } else {
+    dw.zero_();
+  }
+  return {dx, dw};
+}
+
+Tensor rope(Tensor x, Tensor cos, Tensor sin, bool inverse) {
+  check_cuda_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 4, "rope: x must be [B,S,H,D]");
+  TORCH_CHECK(cos.scalar_type() == at::kFloat && sin.scalar_type() == at::kFloat, "rope: fp32 tables");
+  cos = cos.contiguous();
+  sin = sin.contiguous();
+  const int64_t B = x.size(0), S = x.size(1), H = x.size(2), D = x.size(3);
+  int64_t bstride = 0;
+  if (cos.dim() == 3) {
+    TORCH_CHECK(cos.size(0) == B && cos.size(1) == S && cos.size(2) == D / 2, "rope: table shape");
+    bstride = S * (D / 2);
+  } else {
+    TORCH_CHECK(cos.dim() == 2 && cos.size(0) >= S && cos.size(1) == D / 2, "rope: table shape");
+  }
+  c10::cuda::CUDAGuard g(x.device());
+  Tensor y = torch::empty_like(x);
+  ttb::rope_apply(x.data_ptr(), y.data_ptr(), cos.data_ptr<float>(), sin.data_ptr<float>(), B, S, H, D, bstride,
+                  inverse, stream());
+  return y;
+}
+
+Tensor swiglu_fwd(Tensor a, Tensor b) {
+  check_cuda_bf16(a, "a");
+  check_cuda_bf16(b, "b");
+  TORCH_CHECK(a.sizes() == b.sizes(), "swiglu: shape mismatch");
+  c10::cuda::CUDAGuard g(a.device());
+  Tensor y = torch::empty_like(a);
+  ttb::swiglu_fwd(a.data_ptr(), b.data_ptr(), y.data_ptr(), a.numel(), stream());
+  return y;
+}
+
+std::vector<Tensor> swiglu_bwd(Tensor dy, Tensor a, Tensor b) {
+  check_cuda_bf16(dy, "dy");
+  c10::cuda::CUDAGuard g(a.device());
+  Tensor da = torch::empty_like(a), db = torch::empty_like(b);
+  ttb::swiglu_bwd(dy.data_ptr(), a.data_ptr(), b.data_ptr(), da.data_ptr(), db.data_ptr(), a.numel(), stream());
+  return {da, db};
+}
+
+std::vector<Tensor> ce_fwd(Tensor logits, Tensor labels, int64_t ignore_index) {
+  check_cuda_bf16(logits, "logits");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "labels must be contiguous int64");
+  TORCH_CHECK(logits.dim() == 2 && labels.numel() == logits.size(0), "ce: shape mismatch");
+  c10::cuda::CUDAGuard g(logits.device());
+  const int64_t T = logits.size(0), V = logits.size(1);
+  auto f32 = logits.options().dtype(at::kFloat);
+  Tensor rows = torch::empty({T}, f32), lse = torch::empty({T}, f32), loss = torch::empty({}, f32);
+  ttb::ce_fwd(logits.data_ptr(), labels.data_ptr<int64_t>(), rows.data_ptr<float>(), lse.data_ptr<float>(),
+              loss.data_ptr<float>(), T, V, ignore_index, stream());
+  return {loss, lse};
+}
+
+Tensor ce_bwd(Tensor logits, Tensor labels, Tensor lse, Tensor gscale, int64_t ignore_index) {
+  c10::cuda::CUDAGuard g(logits.device());
+  Tensor d = torch::empty_like(logits);
+  ttb::ce_bwd(logits.data_ptr(), labels.data_ptr<int64_t>(), lse.data_ptr<float>(), gscale.data_ptr<float>(),
+              d.data_ptr(), logits.size(0), logits.size(1), ignore_index, stream());
+  return d;
+}
+
+void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Tensor> ms, std::vector<Tensor> vs,
+           double lr, double b1, double b2, double eps, double wd, int64_t step) {
+  TORCH_CHECK(params.size() == grads.size() && params.size() == ms.size() && params.size() == vs.size(),
+              "adamw: list lengths differ");
+  if (params.empty()) return;
+  c10::cuda::CUDAGuard g(params[0].device());
+  std::vector<ttb::AdamWTensor> list;
+  list.reserve(params.size());
+  for (size_t i = 0; i < params.size(); ++i) {
+    auto &p = params[i], &gr = grads[i], &m = ms[i], &v = vs[i];
+    TORCH_CHECK(p.is_cuda() && p.is_contiguous() && gr.is_contiguous() && m.is_contiguous() && v.is_contiguous(),
+                "adamw: tensors must be contiguous CUDA tensors");
+    TORCH_CHECK(m.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat, "adamw: fp32 moments required");
+    TORCH_CHECK(p.numel() == gr.numel() && p.numel() == m.numel() && p.numel() == v.numel(), "adamw: numel mismatch");
+    TORCH_CHECK(p.scalar_type() == at::kFloat || p.scalar_type() == at::kBFloat16, "adamw: param fp32/bf16");
+    TORCH_CHECK(gr.scalar_type() == at::kFloat || gr.scalar_type() == at::kBFloat16, "adamw: grad fp32/bf16");
+    list.push_back({p.data_ptr(), gr.data_ptr(), m.data_ptr<float>(), v.data_ptr<float>(), p.numel(),
+                    p.scalar_type() == at::kBFloat16 ? 1 : 0, gr.scalar_type() == at::kBFloat16 ? 1 : 0});
+  }
+  ttb::adamw_multi(list.data(), static_cast<int>(list.size()), static_cast<float>(lr), static_cast<float>(b1),
+                   static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd), static_cast<int>(step),
+                   stream());
+}
+
+std::vector<Tensor> attn_fwd(Tensor q, Tensor k, Tensor v, bool causal, double scale) {
+  check_cuda_bf16(q, "q");
+  check_cuda_bf16(k, "k");
+  check_cuda_bf16(v, "v");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "attention: [B,S,H,D] tensors");
+  const int B = q.size(0), Sq = q.size(1), H = q.size(2), Dqk = q.size(3);
+  const int Sk = k.size(1), Hk = k.size(2), Dv = v.size(3);
+  TORCH_CHECK(k.size(0) == B && v.size(0) == B && v.size(1) == Sk && v.size(2) == Hk && k.size(3) == Dqk,
+              "attention: shape mismatch");
+  TORCH_CHECK(H % Hk == 0, "attention: n_heads must be a multiple of n_kv_heads");
+  c10::cuda::CUDAGuard g(q.device());
+  Tensor o = torch::empty({B, Sq, H, Dv}, q.options());
+  Tensor lse = torch::empty({B, H, Sq}, q.options().dtype(at::kFloat));
+  ttb::attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), B, Sq, Sk, H, Hk, Dqk,
+                Dv, causal, static_cast<float>(scale), stream());
+  return {o, lse};
+}
+
+std::vector<Tensor> attn_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, bool causal,
+                             double scale) {
+  check_cuda_bf16(dout, "dout");
+  const int B = q.size(0), Sq = q.size(1), H = q.size(2), Dqk = q.size(3);
+  const int Sk = k.size(1), Hk = k.size(2), Dv = v.size(3);
+  c10::cuda::CUDAGuard g(q.device());
+  Tensor dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  Tensor delta = torch::empty({B, H, Sq}, q.options().dtype(at::kFloat));
+  ttb::attn_bwd(dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
+                dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), nullptr, delta.data_ptr<float>(), B, Sq, Sk, H, Hk, Dqk,
+                Dv, causal, static_cast<float>(scale), stream());
+  return {dq, dk, dv};
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "torchtitan_b200 sm_100a kernels";
+  m.def("gemm", &gemm, "bf16 GEMM on tcgen05: D = A(m,k) * B(n,k)");
+  m.def("gemm_error_code", &ttb::gemm_error_code, "read (and optionally clear) the GEMM timeout word",
+        py::arg("reset") = true);
+  m.def("attn_error_code", &ttb::attn_error_code, "read (and optionally clear) the attention timeout word",
+        py::arg("reset") = true);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope", &rope);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("ce_fwd", &ce_fwd);
+  m.def("ce_bwd", &ce_bwd);
+  m.def("adamw", &adamw);
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+}

@@ -1,0 +1,148 @@
+// Cross entropy (sum over valid tokens) on bf16 logits without fp32 copies.
+// Forward: one CTA per token row, single pass with an online (max, sum-exp)
+// pair per thread, merged by shuffles; writes per-row loss and log-sum-exp,
+// then a one-CTA deterministic sum.  Backward: one CTA per row writes
+// (softmax - onehot) * g directly in bf16; g is read from device memory so no
+// host synchronisation is needed.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "launch_api.h"
+
+namespace ttb {
+namespace {
+
+using bf16 = __nv_bfloat16;
+constexpr int NT = 512;
+
+struct alignas(16) V8 {
+  __nv_bfloat162 h[4];
+};
+
+__device__ __forceinline__ void merge(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;
+  s = s * __expf(m - mn) + s2 * __expf(m2 - mn);
+  m = mn;
+}
+
+__global__ void __launch_bounds__(NT) ce_fwd_kernel(const bf16* __restrict__ logits, const int64_t* __restrict__ labels,
+                                                    float* __restrict__ loss_rows, float* __restrict__ lse_out,
+                                                    int64_t V, int64_t ignore_index) {
+  const int64_t row = blockIdx.x;
+  const bf16* x = logits + row * V;
+  float m = -INFINITY, s = 0.f;
+  const int64_t nv = V / 8;
+  for (int64_t i = threadIdx.x; i < nv; i += NT) {
+    V8 v = reinterpret_cast<const V8*>(x)[i];
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 t = __bfloat1622float2(v.h[j]);
+      f[2 * j] = t.x;
+      f[2 * j + 1] = t.y;
+    }
+    float lm = f[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) lm = fmaxf(lm, f[j]);
+    float ls = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ls += __expf(f[j] - lm);
+    merge(m, s, lm, ls);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    merge(m, s, m2, s2);
+  }
+  __shared__ float sm[NT / 32], ssum[NT / 32];
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) {
+    sm[w] = m;
+    ssum[w] = s;
+  }
+  __syncthreads();
+  if (w == 0) {
+    m = l < NT / 32 ? sm[l] : -INFINITY;
+    s = l < NT / 32 ? ssum[l] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      merge(m, s, m2, s2);
+    }
+    if (l == 0) {
+      const float lse = m + __logf(s);
+      lse_out[row] = lse;
+      const int64_t lab = labels[row];
+      float loss = 0.f;
+      if (lab != ignore_index && lab >= 0 && lab < V) loss = lse - __bfloat162float(x[lab]);
+      loss_rows[row] = loss;
+    }
+  }
+}
+
+__global__ void sum_kernel(const float* __restrict__ v, float* __restrict__ out, int64_t n) {
+  __shared__ double sh[1024 / 32];
+  double acc = 0.0;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) acc += v[i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (threadIdx.x % 32 == 0) sh[threadIdx.x / 32] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    acc = threadIdx.x < blockDim.x / 32 ? sh[threadIdx.x] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (threadIdx.x == 0) out[0] = static_cast<float>(acc);
+  }
+}
+
+__global__ void __launch_bounds__(NT) ce_bwd_kernel(const bf16* __restrict__ logits, const int64_t* __restrict__ labels,
+                                                    const float* __restrict__ lse, const float* __restrict__ gscale,
+                                                    bf16* __restrict__ dlogits, int64_t V, int64_t ignore_index) {
+  const int64_t row = blockIdx.x;
+  const int64_t lab = labels[row];
+  const bool valid = lab != ignore_index;
+  const float g = valid ? gscale[0] : 0.f;
+  const float L = lse[row];
+  const bf16* x = logits + row * V;
+  bf16* dx = dlogits + row * V;
+  const int64_t nv = V / 8;
+  for (int64_t i = threadIdx.x; i < nv; i += NT) {
+    V8 v = reinterpret_cast<const V8*>(x)[i];
+    V8 o;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 t = __bfloat1622float2(v.h[j]);
+      const int64_t c = i * 8 + 2 * j;
+      float a = __expf(t.x - L) - (c == lab ? 1.f : 0.f);
+      float b = __expf(t.y - L) - (c + 1 == lab ? 1.f : 0.f);
+      o.h[j] = __floats2bfloat162_rn(a * g, b * g);
+    }
+    reinterpret_cast<V8*>(dx)[i] = o;
+  }
+}
+
+}  // namespace
+
+void ce_fwd(const void* logits, const int64_t* labels, float* loss_rows, float* lse, float* loss_sum, int64_t T,
+            int64_t V, int64_t ignore_index, cudaStream_t s) {
+  if (V % 8) throw std::runtime_error("cross entropy: vocab must be a multiple of 8");
+  if (T > 0)
+    ce_fwd_kernel<<<static_cast<unsigned>(T), NT, 0, s>>>(static_cast<const bf16*>(logits), labels, loss_rows, lse, V,
+                                                         ignore_index);
+  sum_kernel<<<1, 1024, 0, s>>>(loss_rows, loss_sum, T);
+  check_cuda(cudaGetLastError(), "ce_fwd");
+}
+
+void ce_bwd(const void* logits, const int64_t* labels, const float* lse, const float* gscale, void* dlogits, int64_t T,
+            int64_t V, int64_t ignore_index, cudaStream_t s) {
+  if (T == 0) return;
+  ce_bwd_kernel<<<static_cast<unsigned>(T), NT, 0, s>>>(static_cast<const bf16*>(logits), labels, lse, gscale,
+                                                       static_cast<bf16*>(dlogits), V, ignore_index);
+  check_cuda(cudaGetLastError(), "ce_bwd");
+}
+
+}  // namespace ttb

@@ -1,0 +1,1043 @@
+// Flash attention for sm_100a on tcgen05 (forward) with GQA and a
+// bottom-right-aligned causal mask (query i sees keys j <= i + Sk - Sq).
+//
+// Layout: q [B,Sq,H,Dqk], k [B,Sk,Hk,Dqk], v [B,Sk,Hk,Dv] bf16; o like q
+// with Dv; lse [B,H,Sq] fp32 (natural log).
+//
+// Forward CTA = one 128-query tile of one head; warps:
+//   0      TMA producer: Q once, then K/V tiles into a 2-stage ring
+//   1      TMEM allocator + MMA issuer: S_j = Q K_j^T -> TMEM (2 buffers),
+//          PV_j = P_j V_j -> TMEM (2 buffers)
+//   2..5   softmax: thread r owns query row r; reads S_j from TMEM (two
+//          passes: row max, then exp2 + row sum), writes P_j (bf16) into a
+//          128B-swizzled smem tile (2 buffers) for the PV MMA, and folds
+//          PV_{j-1} into its fp32 O row kept in registers.
+// The MMA warp interleaves S_{j+1} and PV_{j-1} so the tensor cores work
+// while the softmax warps process tile j.  All waits are bounded.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <stdexcept>
+
+#include "launch_api.h"
+#include "sm100_ptx.cuh"
+#include "tma_host.h"
+
+namespace ttb {
+namespace attn_impl {
+
+__device__ int g_err;
+
+constexpr int BM = 128;  // queries per CTA
+constexpr int NUM_SM_WARPS = 8;                    // softmax / epilogue warps
+constexpr int NUM_THREADS = 64 + 32 * NUM_SM_WARPS;  // + producer + MMA warp
+
+template <int DQK, int DV, int BN>
+struct Cfg {
+  static constexpr int Q_BYTES = BM * DQK * 2;
+  static constexpr int K_BYTES = BN * DQK * 2;
+  static constexpr int V_BYTES = BN * DV * 2;
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_OFF + Q_BYTES;
+  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;
+  static constexpr int P_OFF = V_OFF + 2 * V_BYTES;
+  static constexpr int RED_OFF = P_OFF + 2 * P_BYTES;      // float [2 stages][2 halves][BM] row maxima
+  static constexpr int BAR_OFF = RED_OFF + 2 * 2 * BM * 4;  // struct Bars
+  static constexpr int SMEM = BAR_OFF + 256;                // dynamic base is 1024-aligned (checked)
+  static constexpr int S_COL = 0;        // 2 x BN columns
+  static constexpr int PV_COL = 2 * BN;  // 2 x DV columns
+  static constexpr int TMEM_COLS = 512;
+  static_assert(2 * BN + 2 * DV <= 512, "TMEM budget");
+  static_assert(DQK % 64 == 0 && DV % 64 == 0 && BN % 64 == 0, "tile dims");
+};
+
+struct Params {
+  int B, Sq, Sk, H, Hk;
+  int causal;
+  float scale_log2;  // softmax scale * log2(e)
+  __nv_bfloat16* o;
+  float* lse;
+  int num_qtiles;
+};
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[2], v_full[2], kv_empty[2];
+  uint64_t s_full[2], s_free[2];
+  uint64_t p_full[2], p_empty[2];
+  uint64_t pv_full[2], pv_free[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// number of KV tiles visible to query tile [q0, q0+BM)
+__device__ __forceinline__ int kv_tiles(const Params& p, int q0, int BN) {
+  const int all = (p.Sk + BN - 1) / BN;
+  if (!p.causal) return all;
+  const int last_key = q0 + BM - 1 + (p.Sk - p.Sq);  // last key any row may see
+  if (last_key < 0) return 0;
+  const int t = last_key / BN + 1;
+  return t < all ? t : all;
+}
+
+template <int DQK, int DV, int BN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, Params p) {
+  using C = Cfg<DQK, DV, BN>;
+  static_assert(sizeof(Bars) <= 256, "Bars must fit its slot");
+  extern __shared__ __align__(1024) uint8_t smem[];
+  // The 128B-swizzle atoms assume 1024-byte aligned tiles; this kernel has no
+  // static shared memory, so the dynamic base is the start of the CTA window.
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicCAS(&g_err, 0, 99);
+    return;
+  }
+  Bars& bar = *reinterpret_cast<Bars*>(smem + C::BAR_OFF);
+  float (*red_max)[2][BM] = reinterpret_cast<float (*)[2][BM]>(smem + C::RED_OFF);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  // heaviest (causal) tiles first
+  const int qt = p.num_qtiles - 1 - (blockIdx.x % p.num_qtiles);
+  const int bh = blockIdx.x / p.num_qtiles;
+  const int h = bh % p.H, b = bh / p.H;
+  const int hk = h / (p.H / p.Hk);
+  const int q0 = qt * BM;
+  const int nkv = kv_tiles(p, q0, BN);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar.q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar.k_full[i], 1);
+      mbar_init(&bar.v_full[i], 1);
+      mbar_init(&bar.kv_empty[i], 1);
+      mbar_init(&bar.s_full[i], 1);
+      mbar_init(&bar.s_free[i], NUM_SM_WARPS);
+      mbar_init(&bar.p_full[i], NUM_SM_WARPS);
+      mbar_init(&bar.p_empty[i], 1);
+      mbar_init(&bar.pv_full[i], 1);
+      mbar_init(&bar.pv_free[i], NUM_SM_WARPS);
+    }
+    bar.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) tmem_alloc(&bar.tmem_base, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 && nkv > 0) {
+      mbar_arrive_expect_tx(&bar.q_full, C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < DQK / 64; ++c)
+        tma_load_3d(smem + C::Q_OFF + c * (BM * 128), &tq, &bar.q_full, h * DQK + c * 64, q0, b);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&bar.kv_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 11)) break;
+        const int k0 = j * BN;
+        mbar_arrive_expect_tx(&bar.k_full[st], C::K_BYTES);
+#pragma unroll
+        for (int c = 0; c < DQK / 64; ++c)
+          tma_load_3d(smem + C::K_OFF + st * C::K_BYTES + c * (BN * 128), &tk, &bar.k_full[st], hk * DQK + c * 64, k0,
+                      b);
+        mbar_arrive_expect_tx(&bar.v_full[st], C::V_BYTES);
+#pragma unroll
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_3d(smem + C::V_OFF + st * C::V_BYTES + c * (BN * 128), &tv, &bar.v_full[st], hk * DV + c * 64, k0,
+                      b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nkv > 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(BM, DV, false, true);
+      const uint32_t q_addr = smem_u32(smem + C::Q_OFF);
+      bool ok = mbar_wait(&bar.q_full, 0, &bar.abort_flag, &g_err, 12);
+      auto issue_pv = [&](int i) -> bool {
+        const int st = i & 1;
+        if (!mbar_wait(&bar.v_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 13)) return false;
+        if (!mbar_wait(&bar.p_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 14)) return false;
+        if (!mbar_wait(&bar.pv_free[st], ((i >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 15)) return false;
+        tc_fence_after();
+        const uint32_t p_addr = smem_u32(smem + C::P_OFF + st * C::P_BYTES);
+        const uint32_t v_addr = smem_u32(smem + C::V_OFF + st * C::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024);
+          umma_bf16(tmem + C::PV_COL + st * DV, ad, bd, idesc_pv, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar.pv_full[st]);
+        umma_commit(&bar.kv_empty[st]);
+        umma_commit(&bar.p_empty[st]);
+        return true;
+      };
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&bar.k_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 16)) break;
+        if (!mbar_wait(&bar.s_free[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 17)) break;
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + C::K_OFF + st * C::K_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < DQK / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+          umma_bf16(tmem + C::S_COL + st * BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar.s_full[st]);
+        if (j > 0 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok) issue_pv(nkv - 1);
+    }
+  } else {
+    // ---------------- softmax / output warps ----------------
+    // Warp pair (w, w+4) shares TMEM lane quarter q (rows q*32..q*32+31);
+    // half hh of the pair owns S columns [hh*HB, hh*HB+HB) and O columns
+    // [hh*HD, hh*HD+HD).  Row maxima are exchanged through smem.
+    constexpr int HB = BN / 2, HD = DV / 2;
+    const int sw = warp - 2;
+    const int q = warp & 3;
+    const int hh = sw >> 2;
+    const int r = q * 32 + lane;  // row within the tile (== TMEM lane)
+    const int qrow = q0 + r;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int diag = qrow + (p.Sk - p.Sq);  // last visible key for this row
+    const float c2 = p.scale_log2;
+    float o_acc[HD];
+#pragma unroll
+    for (int i = 0; i < HD; ++i) o_acc[i] = 0.f;
+    float m_run = -INFINITY;   // running max (log2 domain, scaled) used for P_j
+    float m_o = -INFINITY;     // normalisation of o_acc
+    float l_run = 0.f;         // partial row sum over this warp's columns
+    float m_prev = -INFINITY;  // max used for P_{j-1}
+    bool ok = true;
+
+    auto fold_pv = [&](int i, float m_i) -> bool {
+      const int st = i & 1;
+      if (!mbar_wait(&bar.pv_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 21)) return false;
+      tc_fence_after();
+      const float alpha = (m_o == -INFINITY) ? 0.f : ex2(m_o - m_i);
+      uint32_t v[HD];
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c)
+        tmem_ld_32x32b_x32(tmem + lane_base + C::PV_COL + st * DV + hh * HD + c * 32,
+                           *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < HD; ++e) o_acc[e] = fmaf(o_acc[e], alpha, __uint_as_float(v[e]));
+      m_o = m_i;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.pv_free[st]);
+      return true;
+    };
+
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      const int k0 = j * BN;
+      if (!mbar_wait(&bar.s_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 22)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[HB];
+#pragma unroll
+      for (int c = 0; c < HB / 32; ++c)
+        tmem_ld_32x32b_x32(tmem + lane_base + C::S_COL + st * BN + hh * HB + c * 32,
+                           *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+      tmem_ld_wait();
+      const int kbase = k0 + hh * HB;
+      const bool need_mask = (p.causal && kbase + HB - 1 > q0 + (p.Sk - p.Sq)) || (kbase + HB > p.Sk);
+      if (need_mask) {
+#pragma unroll
+        for (int e = 0; e < HB; ++e) {
+          const int key = kbase + e;
+          if (key >= p.Sk || (p.causal && key > diag)) sv[e] = __float_as_uint(-INFINITY);
+        }
+      }
+      float mx = __uint_as_float(sv[0]);
+#pragma unroll
+      for (int e = 1; e < HB; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
+      red_max[st][hh][r] = mx;
+      named_bar_sync(1 + q, 64);
+      mx = fmaxf(mx, red_max[st][hh ^ 1][r]);
+      const float m_new = fmaxf(m_run, mx * c2);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      // P_j buffer must be free (PV_{j-2} done)
+      if (!mbar_wait(&bar.p_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 23)) {
+        ok = false;
+        break;
+      }
+      uint8_t* rowp = smem + C::P_OFF + st * C::P_BYTES + ((hh * HB) / 64) * (BM * 128) + r * 128;
+      const int chunk_base = ((hh * HB) % 64) / 8;
+      float rs = 0.f;
+#pragma unroll
+      for (int u = 0; u < HB / 8; ++u) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pv[e] = ex2(fmaf(__uint_as_float(sv[u * 8 + e]), c2, -m_use));
+          rs += pv[e];
+        }
+        const int ch = (chunk_base + u) ^ (r & 7);
+        *reinterpret_cast<uint4*>(rowp + ch * 16) = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]),
+                                                               pack_bf16x2(pv[4], pv[5]), pack_bf16x2(pv[6], pv[7]));
+      }
+      // S buffer may be overwritten now; P is visible to the async proxy
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar.s_free[st]);
+        mbar_arrive(&bar.p_full[st]);
+      }
+      const float alpha_l = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_use);
+      l_run = l_run * alpha_l + rs;
+      m_run = m_new;
+      if (j > 0 && !fold_pv(j - 1, m_prev)) {
+        ok = false;
+        break;
+      }
+      m_prev = m_use;
+    }
+    if (ok && nkv > 0) ok = fold_pv(nkv - 1, m_prev);
+    // exchange partial row sums through the stage slot no tile of this row touches last
+    float (*red_l)[BM] = red_max[nkv & 1];
+    red_l[hh][r] = l_run;
+    named_bar_sync(1 + q, 64);
+    const float l_tot = red_l[0][r] + red_l[1][r];
+    if (qrow < p.Sq) {
+      const size_t row_off = ((static_cast<size_t>(b) * p.Sq + qrow) * p.H + h);
+      __nv_bfloat16* orow = p.o + row_off * DV + hh * HD;
+      const float inv = (ok && l_tot > 0.f) ? 1.f / l_tot : 0.f;
+      // o_acc is normalised at m_o; l at m_run (equal unless trailing tiles were fully masked)
+      const float fix = (m_o == -INFINITY || m_run == -INFINITY) ? 0.f : ex2(m_o - m_run) * inv;
+#pragma unroll
+      for (int c = 0; c < HD; c += 8) {
+        uint4 w;
+        w.x = pack_bf16x2(o_acc[c] * fix, o_acc[c + 1] * fix);
+        w.y = pack_bf16x2(o_acc[c + 2] * fix, o_acc[c + 3] * fix);
+        w.z = pack_bf16x2(o_acc[c + 4] * fix, o_acc[c + 5] * fix);
+        w.w = pack_bf16x2(o_acc[c + 6] * fix, o_acc[c + 7] * fix);
+        *reinterpret_cast<uint4*>(orow + c) = w;
+      }
+      if (hh == 0) {
+        const float lse = (l_tot > 0.f && m_run != -INFINITY) ? (m_run + __log2f(l_tot)) * 0.69314718055994531f
+                                                               : -INFINITY;
+        p.lse[(static_cast<size_t>(b) * p.H + h) * p.Sq + qrow] = lse;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int DQK, int DV, int BN>
+void launch_fwd(const void* q, const void* k, const void* v, Params& p, int Dqk, int Dv, cudaStream_t s) {
+  using C = Cfg<DQK, DV, BN>;
+  static bool attr = false;
+  auto* kern = attn_fwd_kernel<DQK, DV, BN>;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM), "attn smem");
+    attr = true;
+  }
+  const CUtensorMap tq = make_tmap_bf16_3d(q, (uint64_t)p.H * Dqk, p.Sq, p.B, (uint64_t)p.H * Dqk,
+                                           (uint64_t)p.Sq * p.H * Dqk, 64, BM, 1);
+  const CUtensorMap tk = make_tmap_bf16_3d(k, (uint64_t)p.Hk * Dqk, p.Sk, p.B, (uint64_t)p.Hk * Dqk,
+                                           (uint64_t)p.Sk * p.Hk * Dqk, 64, BN, 1);
+  const CUtensorMap tv = make_tmap_bf16_3d(v, (uint64_t)p.Hk * Dv, p.Sk, p.B, (uint64_t)p.Hk * Dv,
+                                           (uint64_t)p.Sk * p.Hk * Dv, 64, BN, 1);
+  const int grid = p.B * p.H * p.num_qtiles;
+  kern<<<grid, NUM_THREADS, C::SMEM, s>>>(tq, tk, tv, p);
+  check_cuda(cudaGetLastError(), "attn_fwd launch");
+}
+
+
+// ============================================================================
+// Backward.
+//   delta[b,h,q] = sum_d dO * O                                   (prep kernel)
+//   dK/dV kernel: CTA = 128 keys of one KV head; iterates over the 64-query
+//     tiles of every query head in the GQA group:
+//       S^T = K Q^T, dP^T = V dO^T  (TMEM, double-buffered)
+//       P^T = exp2(S^T*c - lse2), dS^T = P^T (dP^T - delta)    (softmax warps -> smem)
+//       dV += P^T dO, dK += dS^T Q  (TMEM accumulators; no atomics)
+//   dQ kernel: CTA = 128 queries of one head; iterates over 64-key tiles:
+//       S = Q K^T, dP = dO V^T, dS = P (dP - delta), dQ += dS K
+// ============================================================================
+
+__global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
+                                      float* __restrict__ delta, int B, int S, int H, int Dv) {
+  // one warp per (b, s, h) row
+  const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x % 32;
+  const int64_t rows = (int64_t)B * S * H;
+  if (row >= rows) return;
+  const __nv_bfloat16* a = dout + row * Dv;
+  const __nv_bfloat16* c = o + row * Dv;
+  float acc = 0.f;
+  for (int d = lane * 2; d < Dv; d += 64) {
+    const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a + d));
+    const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(c + d));
+    acc += x.x * y.x + x.y * y.y;
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    const int h = row % H;
+    const int64_t bs = row / H;
+    const int sidx = bs % S;
+    const int bidx = bs / S;
+    delta[((int64_t)bidx * H + h) * S + sidx] = acc;
+  }
+}
+
+struct BwdParams {
+  int B, Sq, Sk, H, Hk;
+  int causal;
+  float scale;       // softmax scale
+  float scale_log2;  // scale * log2(e)
+  const float* lse;  // [B,H,Sq] natural log
+  const float* delta;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  __nv_bfloat16* dq;
+};
+
+
+// element (r, c) of a [rows x 64] bf16 tile in the 128-byte-swizzled K-major layout
+__device__ __forceinline__ void store_sw128_chunk(uint8_t* tile, int r, int chunk, uint4 v) {
+  *reinterpret_cast<uint4*>(tile + r * 128 + ((chunk ^ (r & 7)) * 16)) = v;
+}
+
+template <int DQK, int DV, int NBUF>
+struct DKVCfg {
+  static constexpr int BK = 128;  // keys per CTA
+  static constexpr int BQ = 64;   // queries per step
+  static constexpr int K_BYTES = BK * DQK * 2;
+  static constexpr int V_BYTES = BK * DV * 2;
+  static constexpr int Q_BYTES = BQ * DQK * 2;
+  static constexpr int O_BYTES = BQ * DV * 2;  // dO tile
+  static constexpr int P_BYTES = BK * BQ * 2;
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = K_OFF + K_BYTES;
+  static constexpr int Q_OFF = V_OFF + V_BYTES;
+  static constexpr int DO_OFF = Q_OFF + 2 * Q_BYTES;
+  static constexpr int PT_OFF = DO_OFF + 2 * O_BYTES;
+  static constexpr int DST_OFF = PT_OFF + 2 * P_BYTES;
+  static constexpr int SMEM = DST_OFF + 2 * P_BYTES + 1024;
+  static constexpr int ST_COL = 0;                 // NBUF x BQ
+  static constexpr int DPT_COL = NBUF * BQ;        // NBUF x BQ
+  static constexpr int DV_COL = 2 * NBUF * BQ;     // DV
+  static constexpr int DK_COL = DV_COL + DV;       // DQK
+  static_assert(DK_COL + DQK <= 512, "TMEM budget");
+};
+
+struct DKVBars {
+  uint64_t kv_full;
+  uint64_t qd_full[2], qd_empty[2];
+  uint64_t s_full[2], s_free[2];
+  uint64_t p_full[2], p_empty[2];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort_flag;
+  float lse2[2][64];
+  float dlt[2][64];
+};
+
+template <int DQK, int DV, int NBUF>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                         const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, BwdParams p) {
+  using C = DKVCfg<DQK, DV, NBUF>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ DKVBars bar;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nkt = (p.Sk + C::BK - 1) / C::BK;
+  const int kt = blockIdx.x % nkt;
+  const int bhk = blockIdx.x / nkt;
+  const int hk = bhk % p.Hk, b = bhk / p.Hk;
+  const int group = p.H / p.Hk;
+  const int k0 = kt * C::BK;
+  const int offset = p.Sk - p.Sq;
+  const int nqt = (p.Sq + C::BQ - 1) / C::BQ;
+  int qt_first = 0;
+  if (p.causal) {
+    const int first_q = k0 - offset;  // smallest query that sees key k0
+    qt_first = first_q <= 0 ? 0 : first_q / C::BQ;
+  }
+  const int per_head = nqt > qt_first ? nqt - qt_first : 0;
+  const int items = per_head * group;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar.kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar.qd_full[i], 1);
+      mbar_init(&bar.qd_empty[i], 1);
+      mbar_init(&bar.s_full[i], 1);
+      mbar_init(&bar.s_free[i], NUM_SM_WARPS);
+      mbar_init(&bar.p_full[i], NUM_SM_WARPS);
+      mbar_init(&bar.p_empty[i], 1);
+    }
+    mbar_init(&bar.acc_full, 1);
+    bar.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tdo);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) tmem_alloc(&bar.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 && items > 0) {
+      mbar_arrive_expect_tx(&bar.kv_full, C::K_BYTES + C::V_BYTES);
+#pragma unroll
+      for (int c = 0; c < DQK / 64; ++c)
+        tma_load_3d(smem + C::K_OFF + c * (C::BK * 128), &tk, &bar.kv_full, hk * DQK + c * 64, k0, b);
+#pragma unroll
+      for (int c = 0; c < DV / 64; ++c)
+        tma_load_3d(smem + C::V_OFF + c * (C::BK * 128), &tv, &bar.kv_full, hk * DV + c * 64, k0, b);
+      for (int i = 0; i < items; ++i) {
+        const int st = i & 1;
+        const int h = hk * group + i / per_head;
+        const int q0 = (qt_first + i % per_head) * C::BQ;
+        if (!mbar_wait(&bar.qd_empty[st], ((i >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 31)) break;
+        mbar_arrive_expect_tx(&bar.qd_full[st], C::Q_BYTES + C::O_BYTES);
+#pragma unroll
+        for (int c = 0; c < DQK / 64; ++c)
+          tma_load_3d(smem + C::Q_OFF + st * C::Q_BYTES + c * (C::BQ * 128), &tq, &bar.qd_full[st], h * DQK + c * 64,
+                      q0, b);
+#pragma unroll
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_3d(smem + C::DO_OFF + st * C::O_BYTES + c * (C::BQ * 128), &tdo, &bar.qd_full[st], h * DV + c * 64,
+                      q0, b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && items > 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(C::BK, C::BQ, false, false);   // S^T, dP^T
+      constexpr uint32_t idesc_dv = umma_idesc_bf16(C::BK, DV, false, true);      // dV += P^T dO
+      constexpr uint32_t idesc_dk = umma_idesc_bf16(C::BK, DQK, false, true);     // dK += dS^T Q
+      const uint32_t k_addr = smem_u32(smem + C::K_OFF), v_addr = smem_u32(smem + C::V_OFF);
+      bool ok = mbar_wait(&bar.kv_full, 0, &bar.abort_flag, &g_err, 32);
+      auto issue_grads = [&](int i) -> bool {
+        const int st = i & 1;
+        const int sb = i % NBUF;
+        (void)sb;
+        if (!mbar_wait(&bar.p_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 33)) return false;
+        tc_fence_after();
+        const uint32_t pt = smem_u32(smem + C::PT_OFF + st * C::P_BYTES);
+        const uint32_t dst = smem_u32(smem + C::DST_OFF + st * C::P_BYTES);
+        const uint32_t qa = smem_u32(smem + C::Q_OFF + st * C::Q_BYTES);
+        const uint32_t da = smem_u32(smem + C::DO_OFF + st * C::O_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < C::BQ / 16; ++kk) {
+          const uint64_t a1 = umma_desc_sw128(pt + kk * 32, 16, 1024);
+          const uint64_t b1 = umma_desc_sw128(da + kk * 2048, C::BQ * 128, 1024);
+          umma_bf16(tmem + C::DV_COL, a1, b1, idesc_dv, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < C::BQ / 16; ++kk) {
+          const uint64_t a2 = umma_desc_sw128(dst + kk * 32, 16, 1024);
+          const uint64_t b2 = umma_desc_sw128(qa + kk * 2048, C::BQ * 128, 1024);
+          umma_bf16(tmem + C::DK_COL, a2, b2, idesc_dk, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bar.qd_empty[st]);
+        umma_commit(&bar.p_empty[st]);
+        return true;
+      };
+      for (int i = 0; ok && i < items; ++i) {
+        const int st = i & 1;
+        const int sb = i % NBUF;
+        if (!mbar_wait(&bar.qd_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 34)) { ok = false; break; }
+        if (!mbar_wait(&bar.s_free[sb], ((i / NBUF) & 1) ^ 1, &bar.abort_flag, &g_err, 35)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t qa = smem_u32(smem + C::Q_OFF + st * C::Q_BYTES);
+        const uint32_t da = smem_u32(smem + C::DO_OFF + st * C::O_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < DQK / 16; ++kk) {
+          const uint64_t a = umma_desc_sw128(k_addr + (kk >> 2) * (C::BK * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bq = umma_desc_sw128(qa + (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32, 16, 1024);
+          umma_bf16(tmem + C::ST_COL + sb * C::BQ, a, bq, idesc_s, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < DV / 16; ++kk) {
+          const uint64_t a = umma_desc_sw128(v_addr + (kk >> 2) * (C::BK * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bo = umma_desc_sw128(da + (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32, 16, 1024);
+          umma_bf16(tmem + C::DPT_COL + sb * C::BQ, a, bo, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar.s_full[sb]);
+        if (i > 0 && !issue_grads(i - 1)) { ok = false; break; }
+      }
+      if (ok) ok = issue_grads(items - 1);
+      if (ok) umma_commit(&bar.acc_full);
+    }
+  } else {
+    const int q = warp & 3;
+    const int hh = (warp - 2) >> 2;  // which 32-query half of the tile this warp handles
+    const int r = q * 32 + lane;     // key row within the tile
+    const int kidx = k0 + r;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const int t = threadIdx.x - 64;  // 0..255 among the softmax warps
+    bool ok = true;
+    for (int i = 0; i < items; ++i) {
+      const int st = i & 1;
+      const int sb = i % NBUF;
+      const int h = hk * group + i / per_head;
+      const int q0 = (qt_first + i % per_head) * C::BQ;
+      // stage lse2 / delta of this query tile
+      if (t < 64) {
+        const int qi = q0 + t;
+        bar.lse2[st][t] = qi < p.Sq ? p.lse[((size_t)b * p.H + h) * p.Sq + qi] * 1.4426950408889634f : INFINITY;
+      } else {
+        const int qi = q0 + t - 64;
+        bar.dlt[st][t - 64] = qi < p.Sq ? p.delta[((size_t)b * p.H + h) * p.Sq + qi] : 0.f;
+      }
+      named_bar_sync(1, 32 * NUM_SM_WARPS);
+      if (!mbar_wait(&bar.s_full[sb], (i / NBUF) & 1, &bar.abort_flag, &g_err, 36)) { ok = false; break; }
+      if (!mbar_wait(&bar.p_empty[st], ((i >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 37)) { ok = false; break; }
+      tc_fence_after();
+      uint8_t* pt = smem + C::PT_OFF + st * C::P_BYTES;
+      uint8_t* dst = smem + C::DST_OFF + st * C::P_BYTES;
+      const bool need_mask = (kidx >= p.Sk) || (q0 + C::BQ > p.Sq) || (p.causal && k0 + C::BK - 1 > q0 + offset);
+      {
+        const int c = hh;
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + C::ST_COL + sb * C::BQ + c * 32, sv);
+        tmem_ld_32x32b_x32(tmem + lane_base + C::DPT_COL + sb * C::BQ + c * 32, dv);
+        tmem_ld_wait();
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pr[2], ds[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int col = c * 32 + e + u;
+            const int qi = q0 + col;
+            float pv = ex2(__uint_as_float(sv[e + u]) * p.scale_log2 - bar.lse2[st][col]);
+            if (need_mask && (kidx >= p.Sk || qi >= p.Sq || (p.causal && kidx > qi + offset))) pv = 0.f;
+            pr[u] = pv;
+            ds[u] = pv * (__uint_as_float(dv[e + u]) - bar.dlt[st][col]);
+          }
+          pk[e / 2] = pack_bf16x2(pr[0], pr[1]);
+          dk[e / 2] = pack_bf16x2(ds[0], ds[1]);
+        }
+        const int chunk0 = (c * 32) / 8;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          store_sw128_chunk(pt, r, chunk0 + u, make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]));
+          store_sw128_chunk(dst, r, chunk0 + u, make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]));
+        }
+      }
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar.s_free[sb]);
+        mbar_arrive(&bar.p_full[st]);
+      }
+      // lse2/dlt[st] reused two items later; the barrier at the top orders it
+    }
+    // epilogue: dV, dK rows (TMEM loads are warp-collective: every lane loads, valid rows store)
+    bool have = ok && items > 0 && mbar_wait(&bar.acc_full, 0, &bar.abort_flag, &g_err, 38);
+    have = __all_sync(0xffffffffu, have);
+    if (have) tc_fence_after();
+    const bool store = kidx < p.Sk;
+    const size_t row = ((size_t)b * p.Sk + (store ? kidx : 0)) * p.Hk + hk;
+    __nv_bfloat16* dvrow = p.dv + row * DV;
+    __nv_bfloat16* dkrow = p.dk + row * DQK;
+#pragma unroll 1
+    for (int c = hh; c < (DV + DQK) / 32; c += 2) {
+      uint32_t v[32];
+      if (have) {
+        tmem_ld_32x32b_x32(tmem + lane_base + C::DV_COL + c * 32, v);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = 0u;
+      }
+      const bool is_dv = c < DV / 32;
+      const float sc = is_dv ? 1.f : p.scale;
+      __nv_bfloat16* dstp = is_dv ? dvrow + c * 32 : dkrow + (c - DV / 32) * 32;
+      if (store) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 8)
+          *reinterpret_cast<uint4*>(dstp + e) =
+              make_uint4(pack_bf16x2(__uint_as_float(v[e]) * sc, __uint_as_float(v[e + 1]) * sc),
+                         pack_bf16x2(__uint_as_float(v[e + 2]) * sc, __uint_as_float(v[e + 3]) * sc),
+                         pack_bf16x2(__uint_as_float(v[e + 4]) * sc, __uint_as_float(v[e + 5]) * sc),
+                         pack_bf16x2(__uint_as_float(v[e + 6]) * sc, __uint_as_float(v[e + 7]) * sc));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int DQK, int DV>
+struct DQCfg {
+  static constexpr int BQ = 128;  // queries per CTA
+  static constexpr int BK = 64;   // keys per step
+  static constexpr int Q_BYTES = BQ * DQK * 2;
+  static constexpr int O_BYTES = BQ * DV * 2;
+  static constexpr int K_BYTES = BK * DQK * 2;
+  static constexpr int V_BYTES = BK * DV * 2;
+  static constexpr int DS_BYTES = BQ * BK * 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int DO_OFF = Q_OFF + Q_BYTES;
+  static constexpr int K_OFF = DO_OFF + O_BYTES;
+  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;
+  static constexpr int DS_OFF = V_OFF + 2 * V_BYTES;
+  static constexpr int SMEM = DS_OFF + 2 * DS_BYTES + 1024;
+  static constexpr int S_COL = 0;          // 2 x BK
+  static constexpr int DP_COL = 2 * BK;    // 2 x BK
+  static constexpr int DQ_COL = 4 * BK;    // DQK
+  static_assert(DQ_COL + DQK <= 512, "TMEM budget");
+};
+
+struct DQBars {
+  uint64_t qd_full;
+  uint64_t kv_full[2], kv_empty[2];
+  uint64_t s_full[2], s_free[2];
+  uint64_t ds_full[2], ds_empty[2];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+template <int DQK, int DV>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                       const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, BwdParams p) {
+  using C = DQCfg<DQK, DV>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ DQBars bar;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nqt = (p.Sq + C::BQ - 1) / C::BQ;
+  const int qt = nqt - 1 - (blockIdx.x % nqt);
+  const int bh = blockIdx.x / nqt;
+  const int h = bh % p.H, b = bh / p.H;
+  const int hk = h / (p.H / p.Hk);
+  const int q0 = qt * C::BQ;
+  const int offset = p.Sk - p.Sq;
+  int nkv = (p.Sk + C::BK - 1) / C::BK;
+  if (p.causal) {
+    const int last_key = q0 + C::BQ - 1 + offset;
+    nkv = last_key < 0 ? 0 : min(nkv, last_key / C::BK + 1);
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar.qd_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar.kv_full[i], 1);
+      mbar_init(&bar.kv_empty[i], 1);
+      mbar_init(&bar.s_full[i], 1);
+      mbar_init(&bar.s_free[i], NUM_SM_WARPS);
+      mbar_init(&bar.ds_full[i], NUM_SM_WARPS);
+      mbar_init(&bar.ds_empty[i], 1);
+    }
+    mbar_init(&bar.acc_full, 1);
+    bar.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tdo);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) tmem_alloc(&bar.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 && nkv > 0) {
+      mbar_arrive_expect_tx(&bar.qd_full, C::Q_BYTES + C::O_BYTES);
+#pragma unroll
+      for (int c = 0; c < DQK / 64; ++c)
+        tma_load_3d(smem + C::Q_OFF + c * (C::BQ * 128), &tq, &bar.qd_full, h * DQK + c * 64, q0, b);
+#pragma unroll
+      for (int c = 0; c < DV / 64; ++c)
+        tma_load_3d(smem + C::DO_OFF + c * (C::BQ * 128), &tdo, &bar.qd_full, h * DV + c * 64, q0, b);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&bar.kv_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 41)) break;
+        mbar_arrive_expect_tx(&bar.kv_full[st], C::K_BYTES + C::V_BYTES);
+#pragma unroll
+        for (int c = 0; c < DQK / 64; ++c)
+          tma_load_3d(smem + C::K_OFF + st * C::K_BYTES + c * (C::BK * 128), &tk, &bar.kv_full[st], hk * DQK + c * 64,
+                      j * C::BK, b);
+#pragma unroll
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_3d(smem + C::V_OFF + st * C::V_BYTES + c * (C::BK * 128), &tv, &bar.kv_full[st], hk * DV + c * 64,
+                      j * C::BK, b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nkv > 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(C::BQ, C::BK, false, false);
+      constexpr uint32_t idesc_dq = umma_idesc_bf16(C::BQ, DQK, false, true);
+      const uint32_t qa = smem_u32(smem + C::Q_OFF), da = smem_u32(smem + C::DO_OFF);
+      bool ok = mbar_wait(&bar.qd_full, 0, &bar.abort_flag, &g_err, 42);
+      auto issue_dq = [&](int i) -> bool {
+        const int st = i & 1;
+        if (!mbar_wait(&bar.ds_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 43)) return false;
+        tc_fence_after();
+        const uint32_t ds = smem_u32(smem + C::DS_OFF + st * C::DS_BYTES);
+        const uint32_t ka = smem_u32(smem + C::K_OFF + st * C::K_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; ++kk) {
+          const uint64_t a = umma_desc_sw128(ds + kk * 32, 16, 1024);
+          const uint64_t bb = umma_desc_sw128(ka + kk * 2048, C::BK * 128, 1024);
+          umma_bf16(tmem + C::DQ_COL, a, bb, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&bar.kv_empty[st]);
+        umma_commit(&bar.ds_empty[st]);
+        return true;
+      };
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&bar.kv_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 44)) { ok = false; break; }
+        if (!mbar_wait(&bar.s_free[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 45)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ka = smem_u32(smem + C::K_OFF + st * C::K_BYTES);
+        const uint32_t va = smem_u32(smem + C::V_OFF + st * C::V_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < DQK / 16; ++kk) {
+          const uint64_t a = umma_desc_sw128(qa + (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bb = umma_desc_sw128(ka + (kk >> 2) * (C::BK * 128) + (kk & 3) * 32, 16, 1024);
+          umma_bf16(tmem + C::S_COL + st * C::BK, a, bb, idesc_s, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < DV / 16; ++kk) {
+          const uint64_t a = umma_desc_sw128(da + (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bb = umma_desc_sw128(va + (kk >> 2) * (C::BK * 128) + (kk & 3) * 32, 16, 1024);
+          umma_bf16(tmem + C::DP_COL + st * C::BK, a, bb, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar.s_full[st]);
+        if (j > 0 && !issue_dq(j - 1)) { ok = false; break; }
+      }
+      if (ok) ok = issue_dq(nkv - 1);
+      if (ok) umma_commit(&bar.acc_full);
+    }
+  } else {
+    const int q = warp & 3;
+    const int hh = (warp - 2) >> 2;  // which 32-key half of each tile this warp handles
+    const int r = q * 32 + lane;
+    const int qi = q0 + r;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const bool qvalid = qi < p.Sq;
+    const float lse2 = qvalid ? p.lse[((size_t)b * p.H + h) * p.Sq + qi] * 1.4426950408889634f : INFINITY;
+    const float dl = qvalid ? p.delta[((size_t)b * p.H + h) * p.Sq + qi] : 0.f;
+    const int diag = qi + offset;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      const int k0 = j * C::BK;
+      if (!mbar_wait(&bar.s_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 46)) { ok = false; break; }
+      if (!mbar_wait(&bar.ds_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 47)) { ok = false; break; }
+      tc_fence_after();
+      const bool need_mask = !qvalid || (k0 + C::BK > p.Sk) || (p.causal && k0 + C::BK - 1 > diag);
+      uint8_t* dsb = smem + C::DS_OFF + st * C::DS_BYTES;
+      {
+        const int c = hh;
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + C::S_COL + st * C::BK + c * 32, sv);
+        tmem_ld_32x32b_x32(tmem + lane_base + C::DP_COL + st * C::BK + c * 32, dv);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float d2[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int key = k0 + c * 32 + e + u;
+            float pv = ex2(__uint_as_float(sv[e + u]) * p.scale_log2 - lse2);
+            if (need_mask && (!qvalid || key >= p.Sk || (p.causal && key > diag))) pv = 0.f;
+            d2[u] = pv * (__uint_as_float(dv[e + u]) - dl);
+          }
+          pk[e / 2] = pack_bf16x2(d2[0], d2[1]);
+        }
+        const int chunk0 = (c * 32) / 8;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          store_sw128_chunk(dsb, r, chunk0 + u, make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]));
+      }
+      tc_fence_before();
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bar.s_free[st]);
+        mbar_arrive(&bar.ds_full[st]);
+      }
+    }
+    bool have = ok && nkv > 0 && mbar_wait(&bar.acc_full, 0, &bar.abort_flag, &g_err, 48);
+    have = __all_sync(0xffffffffu, have);
+    if (have) tc_fence_after();
+    __nv_bfloat16* dqrow = p.dq + (((size_t)b * p.Sq + (qvalid ? qi : 0)) * p.H + h) * DQK;
+#pragma unroll 1
+    for (int c = hh; c < DQK / 32; c += 2) {
+      uint32_t v[32];
+      if (have) {
+        tmem_ld_32x32b_x32(tmem + lane_base + C::DQ_COL + c * 32, v);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = 0u;
+      }
+      const float sc = p.scale;
+      if (qvalid) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 8)
+          *reinterpret_cast<uint4*>(dqrow + c * 32 + e) =
+              make_uint4(pack_bf16x2(__uint_as_float(v[e]) * sc, __uint_as_float(v[e + 1]) * sc),
+                         pack_bf16x2(__uint_as_float(v[e + 2]) * sc, __uint_as_float(v[e + 3]) * sc),
+                         pack_bf16x2(__uint_as_float(v[e + 4]) * sc, __uint_as_float(v[e + 5]) * sc),
+                         pack_bf16x2(__uint_as_float(v[e + 6]) * sc, __uint_as_float(v[e + 7]) * sc));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int DQK, int DV, int NBUF>
+void launch_bwd(const void* dout, const void* q, const void* k, const void* v, BwdParams& p, cudaStream_t s) {
+  using CK = DKVCfg<DQK, DV, NBUF>;
+  using CQ = DQCfg<DQK, DV>;
+  static bool attr = false;
+  auto* kdkv = attn_bwd_dkdv_kernel<DQK, DV, NBUF>;
+  auto* kdq = attn_bwd_dq_kernel<DQK, DV>;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(kdkv, cudaFuncAttributeMaxDynamicSharedMemorySize, CK::SMEM), "attn bwd smem");
+    check_cuda(cudaFuncSetAttribute(kdq, cudaFuncAttributeMaxDynamicSharedMemorySize, CQ::SMEM), "attn bwd smem");
+    attr = true;
+  }
+  const uint64_t qs = (uint64_t)p.H * DQK, os = (uint64_t)p.H * DV, ks = (uint64_t)p.Hk * DQK, vs = (uint64_t)p.Hk * DV;
+  // dK/dV kernel: 64-query tiles, 128-key tiles
+  {
+    const CUtensorMap tq = make_tmap_bf16_3d(q, qs, p.Sq, p.B, qs, qs * p.Sq, 64, CK::BQ, 1);
+    const CUtensorMap tdo = make_tmap_bf16_3d(dout, os, p.Sq, p.B, os, os * p.Sq, 64, CK::BQ, 1);
+    const CUtensorMap tk = make_tmap_bf16_3d(k, ks, p.Sk, p.B, ks, ks * p.Sk, 64, CK::BK, 1);
+    const CUtensorMap tv = make_tmap_bf16_3d(v, vs, p.Sk, p.B, vs, vs * p.Sk, 64, CK::BK, 1);
+    const int grid = p.B * p.Hk * ((p.Sk + CK::BK - 1) / CK::BK);
+    kdkv<<<grid, NUM_THREADS, CK::SMEM, s>>>(tq, tdo, tk, tv, p);
+    check_cuda(cudaGetLastError(), "attn_bwd_dkdv launch");
+  }
+  {
+    const CUtensorMap tq = make_tmap_bf16_3d(q, qs, p.Sq, p.B, qs, qs * p.Sq, 64, CQ::BQ, 1);
+    const CUtensorMap tdo = make_tmap_bf16_3d(dout, os, p.Sq, p.B, os, os * p.Sq, 64, CQ::BQ, 1);
+    const CUtensorMap tk = make_tmap_bf16_3d(k, ks, p.Sk, p.B, ks, ks * p.Sk, 64, CQ::BK, 1);
+    const CUtensorMap tv = make_tmap_bf16_3d(v, vs, p.Sk, p.B, vs, vs * p.Sk, 64, CQ::BK, 1);
+    const int grid = p.B * p.H * ((p.Sq + CQ::BQ - 1) / CQ::BQ);
+    kdq<<<grid, NUM_THREADS, CQ::SMEM, s>>>(tq, tdo, tk, tv, p);
+    check_cuda(cudaGetLastError(), "attn_bwd_dq launch");
+  }
+}
+}  // namespace attn_impl
+
+void attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Sq, int Sk, int H, int Hk,
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s) {
+  using namespace attn_impl;
+  if (B == 0 || Sq == 0) return;
+  Params p;
+  p.B = B;
+  p.Sq = Sq;
+  p.Sk = Sk;
+  p.H = H;
+  p.Hk = Hk;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o = static_cast<__nv_bfloat16*>(o);
+  p.lse = lse;
+  p.num_qtiles = (Sq + BM - 1) / BM;
+  if (Dqk == 128 && Dv == 128) launch_fwd<128, 128, 128>(q, k, v, p, Dqk, Dv, s);
+  else if (Dqk == 64 && Dv == 64) launch_fwd<64, 64, 128>(q, k, v, p, Dqk, Dv, s);
+  else if (Dqk == 192 && Dv == 128) launch_fwd<192, 128, 64>(q, k, v, p, Dqk, Dv, s);
+  else throw std::runtime_error("attention: unsupported head dims (supported: 64/64, 128/128, 192/128)");
+}
+
+void attn_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
+              void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int Sq, int Sk, int H, int Hk,
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s) {
+  using namespace attn_impl;
+  (void)dq_acc;
+  if (B == 0 || Sq == 0 || Sk == 0) return;
+  const int64_t rows = (int64_t)B * Sq * H;
+  attn_bwd_delta_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, s>>>(
+      static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(o), delta, B, Sq, H, Dv);
+  check_cuda(cudaGetLastError(), "attn_bwd_delta");
+  BwdParams p;
+  p.B = B;
+  p.Sq = Sq;
+  p.Sk = Sk;
+  p.H = H;
+  p.Hk = Hk;
+  p.causal = causal ? 1 : 0;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.lse = lse;
+  p.delta = delta;
+  p.dk = static_cast<__nv_bfloat16*>(dk);
+  p.dv = static_cast<__nv_bfloat16*>(dv);
+  p.dq = static_cast<__nv_bfloat16*>(dq);
+  if (Dqk == 128 && Dv == 128) launch_bwd<128, 128, 2>(dout, q, k, v, p, s);
+  else if (Dqk == 64 && Dv == 64) launch_bwd<64, 64, 2>(dout, q, k, v, p, s);
+  else if (Dqk == 192 && Dv == 128) launch_bwd<192, 128, 1>(dout, q, k, v, p, s);
+  else throw std::runtime_error("attention bwd: unsupported head dims (supported: 64/64, 128/128, 192/128)");
+}
+
+int attn_error_code(bool reset) {
+  int v = 0;
+  check_cuda(cudaMemcpyFromSymbol(&v, attn_impl::g_err, sizeof(int)), "attn error read");
+  if (reset) {
+    int z = 0;
+    check_cuda(cudaMemcpyToSymbol(attn_impl::g_err, &z, sizeof(int)), "attn error reset");
+  }
+  return v;
+}
+
+}  // namespace ttb

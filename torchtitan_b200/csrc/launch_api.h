@@ -1,0 +1,69 @@
+// Plain C++ launch interface of the sm_100a kernels (no torch headers), so
+// the .cu translation units compile quickly; tensor checks and allocation
+// live in bindings.cpp.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+namespace ttb {
+
+inline void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+inline int num_sms(int dev) {
+  static int cache[64] = {0};
+  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+  int n = 0;
+  check_cuda(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev), "sm count");
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+// gemm_tcgen05.cu
+void gemm_bf16(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn,
+               cudaStream_t stream);
+int gemm_error_code(bool reset);
+
+// elementwise.cu
+void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows, int64_t dim, float eps, int w_fp32,
+                 cudaStream_t s);
+void rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw_partial,
+                 int64_t rows, int64_t dim, int w_fp32, int nparts, cudaStream_t s);
+void reduce_rows_f32(const float* partial, float* out, int64_t nparts, int64_t dim, cudaStream_t s);
+void rope_apply(const void* x, void* y, const float* cos, const float* sin, int64_t B, int64_t S, int64_t H,
+                int64_t D, int64_t cs_batch_stride, bool inverse, cudaStream_t s);
+void swiglu_fwd(const void* a, const void* b, void* y, int64_t n, cudaStream_t s);
+void swiglu_bwd(const void* dy, const void* a, const void* b, void* da, void* db, int64_t n, cudaStream_t s);
+
+// cross_entropy.cu
+void ce_fwd(const void* logits, const int64_t* labels, float* loss_rows, float* lse, float* loss_sum, int64_t T,
+            int64_t V, int64_t ignore_index, cudaStream_t s);
+void ce_bwd(const void* logits, const int64_t* labels, const float* lse, const float* gscale, void* dlogits, int64_t T,
+            int64_t V, int64_t ignore_index, cudaStream_t s);
+
+// adamw.cu
+struct AdamWTensor {
+  void* p;
+  const void* g;
+  float* m;
+  float* v;
+  int64_t n;
+  int p_dtype;  // 0 fp32, 1 bf16
+  int g_dtype;
+};
+void adamw_multi(const AdamWTensor* host_list, int count, float lr, float beta1, float beta2, float eps, float wd,
+                 int step, cudaStream_t s);
+
+// flash_attn.cu
+void attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Sq, int Sk, int H, int Hk,
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s);
+void attn_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
+              void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int Sq, int Sk, int H, int Hk,
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s);
+int attn_error_code(bool reset);
+
+}  // namespace ttb

@@ -1,0 +1,151 @@
+"""Kernel micro-benchmarks: ``python -m torchtitan_b200.ops.benchmark [--only gemm,attn,...]``.
+
+Times each sm_100a kernel with CUDA events on the launching stream after
+warm-up, flushing L2 (a 256 MB write) before every timed launch, and prints
+one JSON line per case with the achieved TFLOP/s or GB/s next to the same
+operation done by the library path (cuBLAS ``torch.matmul`` / torch SDPA)
+on the same shapes.  Shapes are those of the Llama-3 8B benchmark config
+(seq 8192, dim 4096, FFN 14336, vocab 128256, 32 heads / 8 KV heads).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+
+def _flush(buf):
+    buf.zero_()
+
+
+def time_fn(fn, iters=10, warmup=3, flush=True):
+    buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda") if flush else None
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if buf is not None:
+            _flush(buf)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        e.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]  # median ms
+
+
+def bench_gemm(ext, out):
+    shapes = [  # (name, M, N, K, a_mn, b_mn)
+        ("qkv_fwd", 8192, 6144, 4096, False, False),
+        ("w13_fwd", 8192, 28672, 4096, False, False),
+        ("w2_fwd", 8192, 4096, 14336, False, False),
+        ("w2_dgrad", 8192, 14336, 4096, False, True),
+        ("w2_wgrad", 4096, 14336, 8192, True, True),
+        ("out_fwd", 8192, 128256, 4096, False, False),
+        ("sq8192", 8192, 8192, 8192, False, False),
+    ]
+    for name, M, N, K, amn, bmn in shapes:
+        A = torch.randn((K, M) if amn else (M, K), device="cuda", dtype=torch.bfloat16)
+        B = torch.randn((K, N) if bmn else (N, K), device="cuda", dtype=torch.bfloat16)
+        ours = time_fn(lambda: ext.gemm(A, B, amn, bmn))
+        At = A.t() if amn else A
+        Bt = B if bmn else B.t()
+        lib = time_fn(lambda: torch.matmul(At, Bt))
+        fl = 2.0 * M * N * K
+        out.append({"kernel": "gemm_tcgen05", "case": name, "M": M, "N": N, "K": K, "ms": ours,
+                    "tflops": fl / ours / 1e9, "cublas_ms": lib, "cublas_tflops": fl / lib / 1e9,
+                    "ratio_vs_cublas": lib / ours, "err": ext.gemm_error_code(True)})
+        print(json.dumps(out[-1]), flush=True)
+
+
+def bench_attn(ext, out):
+    from torchtitan_b200 import ops
+
+    for (B, S, H, Hk, D, Dv) in [(1, 8192, 32, 8, 128, 128), (2, 4096, 32, 32, 192, 128)]:
+        q = torch.randn(B, S, H, D, device="cuda", dtype=torch.bfloat16)
+        k = torch.randn(B, S, Hk, D, device="cuda", dtype=torch.bfloat16)
+        v = torch.randn(B, S, Hk, Dv, device="cuda", dtype=torch.bfloat16)
+        sc = 1 / math.sqrt(D)
+        o, lse = ext.attn_fwd(q, k, v, True, sc)
+        do = torch.randn_like(o)
+        f_ms = time_fn(lambda: ext.attn_fwd(q, k, v, True, sc))
+        b_ms = time_fn(lambda: ext.attn_bwd(do, q, k, v, o, lse, True, sc))
+        # causal FLOPs (half of the full S x S)
+        fwd_fl = 2.0 * B * H * S * S * (D + Dv) / 2
+        bwd_fl = 2.0 * B * H * S * S * (2 * D + 3 * Dv) / 2  # dS K, dS^T Q, P^T dO, dO V^T, (S recompute counted)
+        qt, kt, vt = (t.transpose(1, 2) for t in (q, k, v))
+        try:
+            lib_f = time_fn(lambda: torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, is_causal=True,
+                                                                                     enable_gqa=True, scale=sc))
+        except Exception as e:  # noqa: BLE001
+            lib_f = float("nan")
+        rec = {"kernel": "flash_attn_tcgen05", "B": B, "S": S, "H": H, "Hk": Hk, "D": D, "Dv": Dv,
+               "fwd_ms": f_ms, "fwd_tflops": fwd_fl / f_ms / 1e9, "bwd_ms": b_ms, "bwd_tflops": bwd_fl / b_ms / 1e9,
+               "sdpa_fwd_ms": lib_f, "sdpa_fwd_tflops": fwd_fl / lib_f / 1e9, "err": ext.attn_error_code(True)}
+        out.append(rec)
+        print(json.dumps(rec), flush=True)
+
+
+def bench_memory_bound(ext, out):
+    from torchtitan_b200 import ops
+
+    T, Dm, V = 8192, 4096, 128256
+    x = torch.randn(T, Dm, device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(Dm, device="cuda", dtype=torch.bfloat16)
+    ms = time_fn(lambda: ext.rmsnorm_fwd(x, w, 1e-5))
+    out.append({"kernel": "rmsnorm_fwd", "ms": ms, "gbs": 2 * x.numel() * 2 / ms / 1e6})
+    print(json.dumps(out[-1]), flush=True)
+    a = torch.randn(T, 14336, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn_like(a)
+    ms = time_fn(lambda: ext.swiglu_fwd(a, b))
+    out.append({"kernel": "swiglu_fwd", "ms": ms, "gbs": 3 * a.numel() * 2 / ms / 1e6})
+    print(json.dumps(out[-1]), flush=True)
+    logits = torch.randn(T, V, device="cuda", dtype=torch.bfloat16)
+    labels = torch.randint(0, V, (T,), device="cuda")
+    ms = time_fn(lambda: ext.ce_fwd(logits, labels, -100))
+    out.append({"kernel": "ce_fwd", "ms": ms, "gbs": logits.numel() * 2 / ms / 1e6})
+    print(json.dumps(out[-1]), flush=True)
+    loss, lse = ext.ce_fwd(logits, labels, -100)
+    g = torch.ones(1, device="cuda")
+    ms = time_fn(lambda: ext.ce_bwd(logits, labels, lse, g, -100))
+    out.append({"kernel": "ce_bwd", "ms": ms, "gbs": 2 * logits.numel() * 2 / ms / 1e6})
+    print(json.dumps(out[-1]), flush=True)
+    n = 256 * 1024 * 1024
+    p = torch.randn(n, device="cuda")
+    gr = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda")
+    vv = torch.zeros(n, device="cuda")
+    ms = time_fn(lambda: ext.adamw([p], [gr], [m], [vv], 1e-3, 0.9, 0.95, 1e-8, 0.1, 1))
+    out.append({"kernel": "adamw", "ms": ms, "gbs": n * 4 * 7 / ms / 1e6})
+    print(json.dumps(out[-1]), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="gemm,attn,mem")
+    ap.add_argument("--out", default=None)
+    a = ap.parse_args()
+    from torchtitan_b200.ops._ext import ext as _e
+
+    ext = _e()
+    out: list = []
+    sel = set(a.only.split(","))
+    if "gemm" in sel:
+        bench_gemm(ext, out)
+    if "attn" in sel:
+        bench_attn(ext, out)
+    if "mem" in sel:
+        bench_memory_bound(ext, out)
+    if a.out:
+        with open(a.out, "w") as f:
+            for r in out:
+                f.write(json.dumps(r) + "\n")
+
+
+if __name__ == "__main__":
+    main()
