@@ -36,6 +36,7 @@ def _parse():
     ap.add_argument("--seq-len", type=int, default=8192)
     ap.add_argument("--flavor", default="8B")
     ap.add_argument("--ac", default="selective")
+    ap.add_argument("--profile-out", default=None, help="write a per-kernel time table of one extra step here")
     return ap.parse_args()
 
 
@@ -176,6 +177,12 @@ def run_ours(a):
     torch.cuda.synchronize()
     e2e_s = _max_over_ranks(time.perf_counter() - t0)
     per_step_launches = _count_launches(step)
+    if a.profile_out and rank == 0:
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+        with open(a.profile_out, "w") as f:
+            f.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=40, max_name_column_width=90))
     peak_mem = torch.cuda.max_memory_reserved() / 1024 ** 3
     value = tokens_per_step * a.steps / dev_s
     flops_tok = trainer.metrics_processor.num_flops_per_token

@@ -24,7 +24,9 @@ def _disable_grad_division(m) -> None:
 def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, reduce_dtype: torch.dtype,
                pp_enabled: bool = False, cpu_offload: bool = False, reshard_after_forward_policy: str = "default",
                ep_degree: int = 1, edp_mesh: Any = None) -> nn.Module:
-    mp = MixedPrecisionPolicy(param_dtype=param_dtype, reduce_dtype=reduce_dtype)
+    # forward inputs are not cast: activations are already in the param dtype
+    # (bf16 embedding output) and the fp32 RoPE tables must stay fp32
+    mp = MixedPrecisionPolicy(param_dtype=param_dtype, reduce_dtype=reduce_dtype, cast_forward_inputs=False)
     cfg: dict[str, Any] = {"mesh": dp_mesh, "mp_policy": mp}
     if cpu_offload:
         cfg["offload_policy"] = CPUOffloadPolicy()
