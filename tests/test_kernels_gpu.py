@@ -187,3 +187,17 @@ def test_attention(ext, B, Sq, Sk, H, Hk, D, Dv, causal):
     assert _rel(q.grad, qr.grad) < 3e-2
     assert _rel(k.grad, kr.grad) < 3e-2
     assert _rel(v.grad, vr.grad) < 3e-2
+
+
+def test_grad_clip_kernels(ext):
+    torch.manual_seed(8)
+    xs = [torch.randn(s, device="cuda") for s in [(1000,), (333, 77), (70001,)]] + \
+         [torch.randn(4096, device="cuda").bfloat16()]
+    ref = sum(float(x.float().pow(2).sum()) for x in xs)
+    tot = ext.multi_sumsq(xs)
+    assert abs(tot.item() - ref) / ref < 1e-5
+    before = [x.float().clone() for x in xs]
+    ext.multi_clip_scale(xs, tot, 1.0)
+    coef = 1.0 / (ref ** 0.5 + 1e-6)
+    for x, b in zip(xs, before):
+        assert _rel(x, b * coef) < 1e-2

@@ -28,6 +28,7 @@ struct Chunk {
   int n;
   int8_t p_bf16;
   int8_t g_bf16;
+  int8_t vec4;  // every pointer 16-byte aligned and n % 4 == 0: float4 path
 };
 
 struct Table {
@@ -38,27 +39,125 @@ __device__ __forceinline__ float ldv(const void* base, int64_t i, int8_t is_bf16
   return is_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]) : static_cast<const float*>(base)[i];
 }
 
+__device__ __forceinline__ float adam_update(float& pv, float g, float& m, float& v, float b1, float b2, float eps,
+                                             float decay, float step_size, float bc2_sqrt) {
+  m = b1 * m + (1.f - b1) * g;
+  v = b2 * v + (1.f - b2) * g * g;
+  pv = pv * decay - step_size * m / (sqrtf(v) / bc2_sqrt + eps);
+  return pv;
+}
+
 __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table t, float lr, float b1, float b2,
                                                    float eps, float wd, float bc1, float bc2_sqrt) {
   const Chunk c = t.c[blockIdx.x];
   const float step_size = lr / bc1;
   const float decay = 1.f - lr * wd;
+  if (c.vec4 && !c.p_bf16 && !c.g_bf16) {
+    // fp32 master / fp32 grad: 16-byte loads and stores of all four streams
+    float4* p4 = static_cast<float4*>(c.p);
+    const float4* g4 = static_cast<const float4*>(c.g);
+    float4* m4 = reinterpret_cast<float4*>(c.m);
+    float4* v4 = reinterpret_cast<float4*>(c.v);
+    const int n4 = c.n / 4;
+    for (int i = threadIdx.x; i < n4; i += NT) {
+      float4 p = p4[i], g = g4[i], m = m4[i], v = v4[i];
+      adam_update(p.x, g.x, m.x, v.x, b1, b2, eps, decay, step_size, bc2_sqrt);
+      adam_update(p.y, g.y, m.y, v.y, b1, b2, eps, decay, step_size, bc2_sqrt);
+      adam_update(p.z, g.z, m.z, v.z, b1, b2, eps, decay, step_size, bc2_sqrt);
+      adam_update(p.w, g.w, m.w, v.w, b1, b2, eps, decay, step_size, bc2_sqrt);
+      p4[i] = p;
+      m4[i] = m;
+      v4[i] = v;
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < c.n; i += NT) {
     const float g = ldv(c.g, i, c.g_bf16);
     float m = c.m[i], v = c.v[i];
-    m = b1 * m + (1.f - b1) * g;
-    v = b2 * v + (1.f - b2) * g * g;
+    float pv = c.p_bf16 ? __bfloat162float(static_cast<__nv_bfloat16*>(c.p)[i]) : static_cast<float*>(c.p)[i];
+    adam_update(pv, g, m, v, b1, b2, eps, decay, step_size, bc2_sqrt);
     c.m[i] = m;
     c.v[i] = v;
-    const float denom = sqrtf(v) / bc2_sqrt + eps;
-    if (c.p_bf16) {
-      __nv_bfloat16* p = static_cast<__nv_bfloat16*>(c.p);
-      float pv = __bfloat162float(p[i]) * decay - step_size * m / denom;
-      p[i] = __float2bfloat16(pv);
-    } else {
-      float* p = static_cast<float*>(c.p);
-      p[i] = p[i] * decay - step_size * m / denom;
+    if (c.p_bf16) static_cast<__nv_bfloat16*>(c.p)[i] = __float2bfloat16(pv);
+    else static_cast<float*>(c.p)[i] = pv;
+  }
+}
+
+// ---- gradient clipping: sum of squares over many tensors, then in-place scale
+struct SqChunk {
+  const void* x;
+  int n;
+  int8_t bf16;
+  int8_t vec4;
+};
+struct SqTable {
+  SqChunk c[MAX_CHUNKS];
+  int base;  // index of this launch's first chunk in the partials array
+};
+
+__global__ void __launch_bounds__(NT) sumsq_kernel(const __grid_constant__ SqTable t, float* __restrict__ partial) {
+  const SqChunk c = t.c[blockIdx.x];
+  float acc = 0.f;
+  if (c.vec4 && !c.bf16) {
+    const float4* x4 = static_cast<const float4*>(c.x);
+    for (int i = threadIdx.x; i < c.n / 4; i += NT) {
+      const float4 v = x4[i];
+      acc += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
+  } else {
+    for (int i = threadIdx.x; i < c.n; i += NT) {
+      const float v = ldv(c.x, i, c.bf16);
+      acc += v * v;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  __shared__ float sh[NT / 32];
+  if (threadIdx.x % 32 == 0) sh[threadIdx.x / 32] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    acc = threadIdx.x < NT / 32 ? sh[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (threadIdx.x == 0) partial[t.base + blockIdx.x] = acc;
+  }
+}
+
+__global__ void reduce_partials_kernel(const float* __restrict__ partial, int n, float* __restrict__ out) {
+  __shared__ double sh[32];
+  double acc = 0.0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) acc += partial[i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (threadIdx.x % 32 == 0) sh[threadIdx.x / 32] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    acc = threadIdx.x < blockDim.x / 32 ? sh[threadIdx.x] : 0.0;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (threadIdx.x == 0) out[0] = static_cast<float>(acc);
+  }
+}
+
+// x *= clamp(max_norm / (sqrt(total) + 1e-6), max=1); total read on the device
+__global__ void __launch_bounds__(NT) clip_scale_kernel(const __grid_constant__ SqTable t, const float* __restrict__ total,
+                                                        float max_norm) {
+  const SqChunk c = t.c[blockIdx.x];
+  const float coef = fminf(max_norm / (sqrtf(*total) + 1e-6f), 1.f);
+  if (coef >= 1.f) return;
+  if (c.vec4 && !c.bf16) {
+    float4* x4 = static_cast<float4*>(const_cast<void*>(c.x));
+    for (int i = threadIdx.x; i < c.n / 4; i += NT) {
+      float4 v = x4[i];
+      v.x *= coef; v.y *= coef; v.z *= coef; v.w *= coef;
+      x4[i] = v;
+    }
+  } else if (c.bf16) {
+    __nv_bfloat16* x = static_cast<__nv_bfloat16*>(const_cast<void*>(c.x));
+    for (int i = threadIdx.x; i < c.n; i += NT) x[i] = __float2bfloat16(__bfloat162float(x[i]) * coef);
+  } else {
+    float* x = static_cast<float*>(const_cast<void*>(c.x));
+    for (int i = threadIdx.x; i < c.n; i += NT) x[i] *= coef;
   }
 }
 
@@ -89,10 +188,62 @@ void adamw_multi(const AdamWTensor* list, int count, float lr, float beta1, floa
       c.n = static_cast<int>(t.n - off < CHUNK ? t.n - off : CHUNK);
       c.p_bf16 = static_cast<int8_t>(t.p_dtype);
       c.g_bf16 = static_cast<int8_t>(t.g_dtype);
+      c.vec4 = static_cast<int8_t>(((reinterpret_cast<uintptr_t>(c.p) | reinterpret_cast<uintptr_t>(c.g) |
+                                     reinterpret_cast<uintptr_t>(c.m) | reinterpret_cast<uintptr_t>(c.v)) & 15) == 0 &&
+                                   c.n % 4 == 0);
       if (++nc == MAX_CHUNKS) flush();
     }
   }
   flush();
+}
+
+namespace {
+template <class F>
+void for_each_sq_batch(const SumSqTensor* list, int count, F&& fn) {
+  SqTable tab;
+  tab.base = 0;
+  int nc = 0, total = 0;
+  for (int i = 0; i < count; ++i) {
+    const int esz = list[i].bf16 ? 2 : 4;
+    for (int64_t off = 0; off < list[i].n; off += CHUNK) {
+      SqChunk& c = tab.c[nc];
+      c.x = static_cast<const char*>(list[i].x) + off * esz;
+      c.n = static_cast<int>(list[i].n - off < CHUNK ? list[i].n - off : CHUNK);
+      c.bf16 = static_cast<int8_t>(list[i].bf16);
+      c.vec4 = static_cast<int8_t>((reinterpret_cast<uintptr_t>(c.x) & 15) == 0 && c.n % 4 == 0);
+      ++total;
+      if (++nc == MAX_CHUNKS) {
+        fn(tab, nc);
+        tab.base += nc;
+        nc = 0;
+      }
+    }
+  }
+  if (nc) fn(tab, nc);
+}
+}  // namespace
+
+int64_t sumsq_num_chunks(const SumSqTensor* list, int count) {
+  int64_t n = 0;
+  for (int i = 0; i < count; ++i) n += (list[i].n + CHUNK - 1) / CHUNK;
+  return n;
+}
+
+void multi_sumsq(const SumSqTensor* list, int count, float* partial, float* out, cudaStream_t s) {
+  int n = 0;
+  for_each_sq_batch(list, count, [&](const SqTable& t, int nc) {
+    sumsq_kernel<<<nc, NT, 0, s>>>(t, partial);
+    n = t.base + nc;
+  });
+  reduce_partials_kernel<<<1, 1024, 0, s>>>(partial, n, out);
+  check_cuda(cudaGetLastError(), "multi_sumsq");
+}
+
+void multi_clip_scale(const SumSqTensor* list, int count, const float* total, float max_norm, cudaStream_t s) {
+  for_each_sq_batch(list, count, [&](const SqTable& t, int nc) {
+    clip_scale_kernel<<<nc, NT, 0, s>>>(t, total, max_norm);
+  });
+  check_cuda(cudaGetLastError(), "multi_clip_scale");
 }
 
 }  // namespace ttb

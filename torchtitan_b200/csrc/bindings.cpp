@@ -151,6 +151,37 @@ void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Te
                    stream());
 }
 
+std::vector<ttb::SumSqTensor> sq_list(const std::vector<Tensor>& xs) {
+  std::vector<ttb::SumSqTensor> l;
+  l.reserve(xs.size());
+  for (auto& x : xs) {
+    TORCH_CHECK(x.is_cuda() && x.is_contiguous(), "grad norm: contiguous CUDA tensors required");
+    TORCH_CHECK(x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16, "grad norm: fp32/bf16 only");
+    l.push_back({x.data_ptr(), x.numel(), x.scalar_type() == at::kBFloat16 ? 1 : 0});
+  }
+  return l;
+}
+
+// sum of squares of all tensors (fp32 scalar tensor on the device)
+Tensor multi_sumsq(std::vector<Tensor> xs) {
+  TORCH_CHECK(!xs.empty(), "multi_sumsq: empty list");
+  c10::cuda::CUDAGuard g(xs[0].device());
+  auto l = sq_list(xs);
+  const int64_t nchunks = std::max<int64_t>(1, ttb::sumsq_num_chunks(l.data(), (int)l.size()));
+  auto opts = xs[0].options().dtype(at::kFloat);
+  Tensor partial = torch::empty({nchunks}, opts);
+  Tensor out = torch::empty({}, opts);
+  ttb::multi_sumsq(l.data(), (int)l.size(), partial.data_ptr<float>(), out.data_ptr<float>(), stream());
+  return out;
+}
+
+void multi_clip_scale(std::vector<Tensor> xs, Tensor total, double max_norm) {
+  if (xs.empty()) return;
+  c10::cuda::CUDAGuard g(xs[0].device());
+  auto l = sq_list(xs);
+  ttb::multi_clip_scale(l.data(), (int)l.size(), total.data_ptr<float>(), static_cast<float>(max_norm), stream());
+}
+
 std::vector<Tensor> attn_fwd(Tensor q, Tensor k, Tensor v, bool causal, double scale) {
   check_cuda_bf16(q, "q");
   check_cuda_bf16(k, "k");
@@ -200,6 +231,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_fwd", &ce_fwd);
   m.def("ce_bwd", &ce_bwd);
   m.def("adamw", &adamw);
+  m.def("multi_sumsq", &multi_sumsq, "sum of squares over a list of fp32/bf16 tensors");
+  m.def("multi_clip_scale", &multi_clip_scale, "scale tensors by min(1, max_norm/(sqrt(total)+1e-6))");
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
 }

@@ -58,6 +58,17 @@ struct AdamWTensor {
 void adamw_multi(const AdamWTensor* host_list, int count, float lr, float beta1, float beta2, float eps, float wd,
                  int step, cudaStream_t s);
 
+struct SumSqTensor {
+  const void* x;
+  int64_t n;
+  int bf16;
+};
+int64_t sumsq_num_chunks(const SumSqTensor* list, int count);
+// partial: >= sumsq_num_chunks floats of scratch; out: 1 float (sum of squares)
+void multi_sumsq(const SumSqTensor* list, int count, float* partial, float* out, cudaStream_t s);
+// scale every tensor by min(1, max_norm / (sqrt(*total) + 1e-6)) with *total read on the device
+void multi_clip_scale(const SumSqTensor* list, int count, const float* total, float max_norm, cudaStream_t s);
+
 // flash_attn.cu
 void attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Sq, int Sk, int H, int Hk,
               int Dqk, int Dv, bool causal, float scale, cudaStream_t s);

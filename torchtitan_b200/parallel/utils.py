@@ -163,8 +163,13 @@ def clip_grad_norm_(parameters, max_norm: float, norm_type: float = 2.0, foreach
             per_sig.setdefault(("plain",), [None, (), []])[2].append(g)
     total = None
     for mesh, shard_dims, locs in per_sig.values():
-        norms = torch._foreach_norm([t.float() if t.dtype != torch.float32 else t for t in locs], 2.0) if foreach else [t.float().norm() for t in locs]
-        sq = torch.stack(list(norms)).pow(2).sum()
+        if locs[0].is_cuda:
+            from torchtitan_b200.ops._ext import ext
+
+            sq = ext().multi_sumsq([t if t.is_contiguous() else t.contiguous() for t in locs])
+        else:
+            norms = torch._foreach_norm([t.float() for t in locs], 2.0)
+            sq = torch.stack(list(norms)).pow(2).sum()
         if mesh is not None:
             for d in shard_dims:
                 dist.all_reduce(sq, group=mesh.get_group(d))
@@ -173,9 +178,14 @@ def clip_grad_norm_(parameters, max_norm: float, norm_type: float = 2.0, foreach
         dist.all_reduce(total, group=pp_mesh.get_group())
     norm = total.sqrt()
     if max_norm and max_norm > 0:
-        coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
         locs = [g.to_local() if isinstance(g, DTensor) else g for g in grads]
-        torch._foreach_mul_(locs, coef.to(locs[0].device))
+        if locs[0].is_cuda and all(t.is_contiguous() for t in locs):
+            from torchtitan_b200.ops._ext import ext
+
+            ext().multi_clip_scale(locs, total.float().contiguous(), float(max_norm))
+        else:
+            coef = (max_norm / (norm + 1e-6)).clamp(max=1.0)
+            torch._foreach_mul_(locs, coef.to(locs[0].device))
     return norm
 
 
