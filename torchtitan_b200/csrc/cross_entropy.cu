@@ -146,3 +146,63 @@ void ce_bwd(const void* logits, const int64_t* labels, const float* lse, const f
 }
 
 }  // namespace ttb
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant (declared in ce_noalloc.h): the per-row loss scratch
+// is a fixed device array in this file instead of a buffer from the caller's
+// allocator.
+#include <cstdio>
+
+#include "ce_noalloc.h"
+
+namespace {
+
+static __device__ __align__(256) float g_ce_rows_scratch[TTB_CE_NOALLOC_MAX_ROWS];
+
+constexpr int kMaxDevices = 64;
+float* g_scratch_ptr[kMaxDevices] = {nullptr};  // device address per device, resolved once
+int g_last_cuda_error = 0;
+
+}  // namespace
+
+extern "C" int ttb_ce_fwd_noalloc_max_rows(void) { return TTB_CE_NOALLOC_MAX_ROWS; }
+
+extern "C" int ttb_ce_fwd_noalloc_last_cuda_error(void) { return g_last_cuda_error; }
+
+extern "C" int ttb_ce_fwd_noalloc(const void* logits, const int64_t* labels, int64_t T, int64_t V,
+                                  int64_t ignore_index, float* lse, float* loss_sum, cudaStream_t stream) {
+  if (T > TTB_CE_NOALLOC_MAX_ROWS) {
+    std::fprintf(stderr, "ttb_ce_fwd_noalloc: %lld rows exceed the fixed scratch of %d rows\n",
+                 static_cast<long long>(T), TTB_CE_NOALLOC_MAX_ROWS);
+    return TTB_CE_NOALLOC_ETOOBIG;
+  }
+  if (T < 0 || V <= 0 || V % 8 || !lse || !loss_sum || (T > 0 && (!logits || !labels)))
+    return TTB_CE_NOALLOC_EINVAL;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    g_last_cuda_error = static_cast<int>(e);
+    return TTB_CE_NOALLOC_ECUDA;
+  }
+  if (g_scratch_ptr[dev] == nullptr) {
+    // host code only knows a stand-in for the array; ask the runtime for its address on this device
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_ce_rows_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      g_last_cuda_error = static_cast<int>(e);
+      return TTB_CE_NOALLOC_ECUDA;
+    }
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  float* rows = g_scratch_ptr[dev];
+  if (T > 0)
+    ttb::ce_fwd_kernel<<<static_cast<unsigned>(T), ttb::NT, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(logits), labels, rows, lse, V, ignore_index);
+  ttb::sum_kernel<<<1, 1024, 0, stream>>>(rows, loss_sum, T);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    g_last_cuda_error = static_cast<int>(e);
+    return TTB_CE_NOALLOC_ECUDA;
+  }
+  return TTB_CE_NOALLOC_OK;
+}
