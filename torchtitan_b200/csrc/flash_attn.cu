@@ -79,6 +79,68 @@ __device__ __forceinline__ float ex2(float x) {
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
+
+// ---- packed fp32x2 arithmetic (sm_100) and exp2 helpers -------------------
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void up2(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+// 2^x on the FMA pipe for x <= 0 (values below -126 flush to ~0):
+// x = n + f with n = round(x), f in [-1/2, 1/2]; 2^f by a cubic fitted in
+// relative error on Chebyshev nodes (max rel. error 7.8e-5, far below bf16's
+// 3.9e-3); 2^n is added directly into the exponent field.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x) {
+  float a, b;
+  up2(x, a, b);
+  x = pk2(fmaxf(a, -126.f), fmaxf(b, -126.f));  // n >= -126 keeps the exponent sum >= 0
+  const uint64_t magic = pk2(12582912.f, 12582912.f);  // 1.5 * 2^23: rounds to an integer
+  const uint64_t t = add2(x, magic);
+  const uint64_t n = add2(t, pk2(-12582912.f, -12582912.f));
+  const uint64_t f = fma2(n, pk2(-1.f, -1.f), x);
+  uint64_t q = fma2(pk2(0.05508868396f, 0.05508868396f), f, pk2(0.24260404706f, 0.24260404706f));
+  q = fma2(q, f, pk2(0.69327622652f, 0.69327622652f));
+  q = fma2(q, f, pk2(0.99992895126f, 0.99992895126f));
+  float qa, qb, ta, tb;
+  up2(q, qa, qb);
+  up2(t, ta, tb);
+  return pk2(__uint_as_float(__float_as_uint(qa) + (__float_as_uint(ta) << 23)),
+             __uint_as_float(__float_as_uint(qb) + (__float_as_uint(tb) << 23)));
+}
+__device__ __forceinline__ uint64_t ex2_mufu2(uint64_t x) {
+  float a, b;
+  up2(x, a, b);
+  return pk2(ex2(a), ex2(b));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2_u64(uint64_t v) {
+  float a, b;
+  up2(v, a, b);
+  return pack_bf16x2(a, b);
+}
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // number of KV tiles visible to query tile [q0, q0+BM)
@@ -244,8 +306,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_ld_32x32b_x32(tmem + lane_base + C::PV_COL + st * DV + hh * HD + c * 32,
                            *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
       tmem_ld_wait();
+      const uint64_t al = pk2(alpha, alpha);
 #pragma unroll
-      for (int e = 0; e < HD; ++e) o_acc[e] = fmaf(o_acc[e], alpha, __uint_as_float(v[e]));
+      for (int e = 0; e < HD; e += 2) {
+        const uint64_t o = fma2(pk2(o_acc[e], o_acc[e + 1]), al, pk2(__uint_as_float(v[e]), __uint_as_float(v[e + 1])));
+        up2(o, o_acc[e], o_acc[e + 1]);
+      }
       m_o = m_i;
       tc_fence_before();
       __syncwarp();
@@ -276,9 +342,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (key >= p.Sk || (p.causal && key > diag)) sv[e] = __float_as_uint(-INFINITY);
         }
       }
-      float mx = __uint_as_float(sv[0]);
+      float mc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int e = 1; e < HB; ++e) mx = fmaxf(mx, __uint_as_float(sv[e]));
+      for (int e = 0; e < HB; e += 8) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          mc[u] = max3(mc[u], __uint_as_float(sv[e + 2 * u]), __uint_as_float(sv[e + 2 * u + 1]));
+      }
+      float mx = max3(mc[0], mc[1], fmaxf(mc[2], mc[3]));
       red_max[st][hh][r] = mx;
       named_bar_sync(1 + q, 64);
       mx = fmaxf(mx, red_max[st][hh ^ 1][r]);
@@ -291,19 +362,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       }
       uint8_t* rowp = smem + C::P_OFF + st * C::P_BYTES + ((hh * HB) / 64) * (BM * 128) + r * 128;
       const int chunk_base = ((hh * HB) % 64) / 8;
-      float rs = 0.f;
+      const uint64_t cc = pk2(c2, c2), nm = pk2(-m_use, -m_use);
+      uint64_t rs2 = pk2(0.f, 0.f);
 #pragma unroll
       for (int u = 0; u < HB / 8; ++u) {
-        float pv[8];
+        uint32_t pk[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = ex2(fmaf(__uint_as_float(sv[u * 8 + e]), c2, -m_use));
-          rs += pv[e];
+        for (int e = 0; e < 4; ++e) {
+          const uint64_t x = fma2(pk2(__uint_as_float(sv[u * 8 + 2 * e]), __uint_as_float(sv[u * 8 + 2 * e + 1])),
+                                  cc, nm);
+          // one pair in four goes to the FMA pipe so MUFU is not the limiter
+          const uint64_t pv = (e == 3) ? exp2_poly2(x) : ex2_mufu2(x);
+          rs2 = add2(rs2, pv);
+          pk[e] = pack_bf16x2_u64(pv);
         }
         const int ch = (chunk_base + u) ^ (r & 7);
-        *reinterpret_cast<uint4*>(rowp + ch * 16) = make_uint4(pack_bf16x2(pv[0], pv[1]), pack_bf16x2(pv[2], pv[3]),
-                                                               pack_bf16x2(pv[4], pv[5]), pack_bf16x2(pv[6], pv[7]));
+        *reinterpret_cast<uint4*>(rowp + ch * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
       }
+      float rsa, rsb;
+      up2(rs2, rsa, rsb);
+      const float rs = rsa + rsb;
       // S buffer may be overwritten now; P is visible to the async proxy
       tc_fence_before();
       fence_async_smem();
@@ -355,6 +433,347 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+// ============================================================================
+// Forward, two query tiles per CTA (head dims 64/64 and 128/128).
+//
+// CTA = 256 queries of one head as tiles A (rows 0..127) and B (128..255)
+// sharing every K/V tile.  TMEM (512 columns): tile t owns S_t (128 fp32
+// columns, t*256) and O_t (DV fp32 columns, t*256+128).  The softmax warps
+// of a tile (one per TMEM lane quarter, thread = query row) read S_t into
+// registers, write P_t as packed bf16 back over the first 64 columns of S_t
+// (tcgen05.st) and the PV MMA reads A = P_t straight from TMEM.  O_t stays
+// in TMEM: it is rescaled only when a row's running max grows by more than
+// 8 (log2 units), so P <= 256 and the rescale is rare.  While one tile's
+// warps run softmax the tensor cores work on the other tile.
+// Warps: 0 TMA producer, 1 MMA issuer, 2..5 softmax tile A, 6..9 tile B.
+// ============================================================================
+template <int DQK, int DV>
+struct Cfg2 {
+  static constexpr int BN = 128;
+  static constexpr int Q_BYTES = BM * DQK * 2;  // per tile
+  static constexpr int K_BYTES = BN * DQK * 2;
+  static constexpr int V_BYTES = BN * DV * 2;
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = 2 * Q_BYTES;
+  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;
+  static constexpr int BAR_OFF = V_OFF + 2 * V_BYTES;
+  static constexpr int SMEM = BAR_OFF + 256;
+  static_assert(DV <= 128, "O_t must fit next to S_t");
+};
+
+struct Bars2 {
+  uint64_t q_full;
+  uint64_t k_full[2], v_full[2], kv_empty[2];
+  uint64_t s_full[2], p_full[2], pv_done[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem desc]
+__device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+template <int DQK, int DV>
+__global__ void __maxnreg__(192)
+    attn_fwd2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                     const __grid_constant__ CUtensorMap tv, Params p) {
+  using C = Cfg2<DQK, DV>;
+  constexpr int BN = C::BN;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicCAS(&g_err, 0, 99);
+    return;
+  }
+  Bars2& bar = *reinterpret_cast<Bars2*>(smem + C::BAR_OFF);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int npairs = (p.num_qtiles + 1) / 2;
+  const int qp = npairs - 1 - (blockIdx.x % npairs);  // heaviest pairs first
+  const int bh = blockIdx.x / npairs;
+  const int h = bh % p.H, b = bh / p.H;
+  const int hk = h / (p.H / p.Hk);
+  const int q0 = qp * 2 * BM;
+  int nkv_t[2];
+  nkv_t[0] = kv_tiles(p, q0, BN);
+  nkv_t[1] = (q0 + BM < p.Sq) ? kv_tiles(p, q0 + BM, BN) : 0;
+  const int nkv = max(nkv_t[0], nkv_t[1]);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar.q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar.k_full[i], 1);
+      mbar_init(&bar.v_full[i], 1);
+      mbar_init(&bar.kv_empty[i], 1);
+      mbar_init(&bar.s_full[i], 1);
+      mbar_init(&bar.p_full[i], 4);
+      mbar_init(&bar.pv_done[i], 1);
+    }
+    bar.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tq);
+    tma_prefetch_desc(&tk);
+    tma_prefetch_desc(&tv);
+  }
+  if (warp == 1) tmem_alloc(&bar.tmem_base, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar.tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0 && nkv > 0) {
+      mbar_arrive_expect_tx(&bar.q_full, 2 * C::Q_BYTES);
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+#pragma unroll
+        for (int c = 0; c < DQK / 64; ++c)
+          tma_load_3d(smem + C::Q_OFF + t * C::Q_BYTES + c * (BM * 128), &tq, &bar.q_full, h * DQK + c * 64,
+                      q0 + t * BM, b);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&bar.kv_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 51)) break;
+        const int k0 = j * BN;
+        mbar_arrive_expect_tx(&bar.k_full[st], C::K_BYTES);
+#pragma unroll
+        for (int c = 0; c < DQK / 64; ++c)
+          tma_load_3d(smem + C::K_OFF + st * C::K_BYTES + c * (BN * 128), &tk, &bar.k_full[st], hk * DQK + c * 64, k0,
+                      b);
+        mbar_arrive_expect_tx(&bar.v_full[st], C::V_BYTES);
+#pragma unroll
+        for (int c = 0; c < DV / 64; ++c)
+          tma_load_3d(smem + C::V_OFF + st * C::V_BYTES + c * (BN * 128), &tv, &bar.v_full[st], hk * DV + c * 64, k0,
+                      b);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nkv > 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(BM, BN, false, false);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16(BM, DV, false, true);
+      bool ok = mbar_wait(&bar.q_full, 0, &bar.abort_flag, &g_err, 52);
+      for (int j = 0; ok && j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait(&bar.k_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 53)) break;
+        const uint32_t k_addr = smem_u32(smem + C::K_OFF + st * C::K_BYTES);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (j >= nkv_t[t]) continue;
+          // S_t is overwritten: the previous PV_t (reading P_t from these columns) must be done
+          if (j > 0 && !mbar_wait(&bar.pv_done[t], (j - 1) & 1, &bar.abort_flag, &g_err, 54)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t q_addr = smem_u32(smem + C::Q_OFF + t * C::Q_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < DQK / 16; ++kk) {
+            const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+            umma_bf16(tmem + t * 256, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          }
+          umma_commit(&bar.s_full[t]);
+        }
+        if (!ok) break;
+        if (!mbar_wait(&bar.v_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 55)) break;
+        const uint32_t v_addr = smem_u32(smem + C::V_OFF + st * C::V_BYTES);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (j >= nkv_t[t]) continue;
+          if (!mbar_wait(&bar.p_full[t], j & 1, &bar.abort_flag, &g_err, 56)) { ok = false; break; }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t bd = umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024);
+            umma_bf16_ts(tmem + t * 256 + 128, tmem + t * 256 + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&bar.pv_done[t]);
+        }
+        if (!ok) break;
+        umma_commit(&bar.kv_empty[st]);
+      }
+    }
+  } else {
+    const int t = (warp - 2) >> 2;  // query tile of this warp
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int qrow = q0 + t * BM + r;
+    const int nk = nkv_t[t];
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t s_col = tmem + lane_base + t * 256;
+    const uint32_t o_col = s_col + 128;
+    const int diag = qrow + (p.Sk - p.Sq);
+    const int qt0 = q0 + t * BM;
+    const float c2 = p.scale_log2;
+    float m_used = -INFINITY;  // max (log2 units) that P and O are currently normalised to
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      if (!mbar_wait(&bar.s_full[t], j & 1, &bar.abort_flag, &g_err, 57)) { ok = false; break; }
+      tc_fence_after();
+      const int k0 = j * BN;
+      const bool need_mask = (p.causal && k0 + BN - 1 > qt0 + (p.Sk - p.Sq)) || (k0 + BN > p.Sk);
+      // pass 1: row max (S read 64 columns at a time to bound register use)
+      float mc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[64];
+        tmem_ld_32x32b_x32(s_col + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld_32x32b_x32(s_col + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld_wait();
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const int key = k0 + half * 64 + e;
+            if (key >= p.Sk || (p.causal && key > diag)) sv[e] = __float_as_uint(-INFINITY);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 64; e += 8) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            mc[u] = max3(mc[u], __uint_as_float(sv[e + 2 * u]), __uint_as_float(sv[e + 2 * u + 1]));
+        }
+      }
+      const float cand = max3(mc[0], mc[1], fmaxf(mc[2], mc[3])) * c2;
+      // lazy rescale: only when the max grows by more than 8 (P stays <= 2^8)
+      const bool grow = cand > (m_used == -INFINITY ? -INFINITY : m_used + 8.f);
+      if (__any_sync(0xffffffffu, grow)) {
+        const float m_new = fmaxf(m_used, cand);
+        const float alpha = (m_used == -INFINITY || m_new == -INFINITY) ? 0.f : ex2(m_used - m_new);
+        l_run *= alpha;
+        if (j > 0) {  // O_t holds PV of earlier tiles (complete: S_t was issued after it)
+          const uint64_t al = pk2(alpha, alpha);
+#pragma unroll
+          for (int c = 0; c < DV / 32; ++c) {
+            uint32_t ov[32];
+            tmem_ld_32x32b_x32(o_col + c * 32, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              float a0, a1;
+              up2(mul2(pk2(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])), al), a0, a1);
+              ov[e] = __float_as_uint(a0);
+              ov[e + 1] = __float_as_uint(a1);
+            }
+            tmem_st_32x32b_x32(o_col + c * 32, ov);
+          }
+          tmem_st_wait();
+        }
+        m_used = m_new;
+      }
+      const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
+      const uint64_t cc = pk2(c2, c2), nm = pk2(-m_eff, -m_eff);
+      uint64_t rs2 = pk2(0.f, 0.f);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[64];
+        tmem_ld_32x32b_x32(s_col + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld_32x32b_x32(s_col + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld_wait();
+        if (need_mask) {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) {
+            const int key = k0 + half * 64 + e;
+            if (key >= p.Sk || (p.causal && key > diag)) sv[e] = __float_as_uint(-INFINITY);
+          }
+        }
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 64; e += 2) {
+          const uint64_t x = fma2(pk2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), cc, nm);
+          const uint64_t pv = ((e & 7) == 6) ? exp2_poly2(x) : ex2_mufu2(x);
+          rs2 = add2(rs2, pv);
+          pk[e / 2] = pack_bf16x2_u64(pv);
+        }
+        // P columns [half*32, half*32+32) hold keys [half*64, half*64+64); S of those keys was
+        // already read (pass 2 reads half 0 before writing it; half 1 columns 64.. are untouched)
+        tmem_st_32x32b_x32(s_col + half * 32, pk);
+      }
+      tmem_st_wait();
+      float ra, rb;
+      up2(rs2, ra, rb);
+      l_run += ra + rb;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.p_full[t]);
+    }
+    // final: wait for the last PV_t, normalise O_t and store
+    bool have = ok && nk > 0 && mbar_wait(&bar.pv_done[t], (nk - 1) & 1, &bar.abort_flag, &g_err, 58);
+    have = __all_sync(0xffffffffu, have);
+    if (have) tc_fence_after();
+    const float inv = (have && l_run > 0.f) ? 1.f / l_run : 0.f;
+    const bool store = qrow < p.Sq;
+    __nv_bfloat16* orow = p.o + ((static_cast<size_t>(b) * p.Sq + (store ? qrow : 0)) * p.H + h) * DV;
+#pragma unroll
+    for (int c = 0; c < DV / 32; ++c) {
+      uint32_t ov[32];
+      if (have) {
+        tmem_ld_32x32b_x32(o_col + c * 32, ov);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ov[e] = 0u;
+      }
+      if (store) {
+#pragma unroll
+        for (int e = 0; e < 32; e += 8)
+          *reinterpret_cast<uint4*>(orow + c * 32 + e) =
+              make_uint4(pack_bf16x2(__uint_as_float(ov[e]) * inv, __uint_as_float(ov[e + 1]) * inv),
+                         pack_bf16x2(__uint_as_float(ov[e + 2]) * inv, __uint_as_float(ov[e + 3]) * inv),
+                         pack_bf16x2(__uint_as_float(ov[e + 4]) * inv, __uint_as_float(ov[e + 5]) * inv),
+                         pack_bf16x2(__uint_as_float(ov[e + 6]) * inv, __uint_as_float(ov[e + 7]) * inv));
+      }
+    }
+    if (store) {
+      const float lse = (l_run > 0.f && m_used != -INFINITY && have) ? (m_used + __log2f(l_run)) * 0.69314718055994531f
+                                                                     : -INFINITY;
+      p.lse[(static_cast<size_t>(b) * p.H + h) * p.Sq + qrow] = lse;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int DQK, int DV>
+void launch_fwd2(const void* q, const void* k, const void* v, Params& p, cudaStream_t s) {
+  using C = Cfg2<DQK, DV>;
+  static bool attr = false;
+  auto* kern = attn_fwd2_kernel<DQK, DV>;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM), "attn2 smem");
+    attr = true;
+  }
+  const CUtensorMap tq = make_tmap_bf16_3d(q, (uint64_t)p.H * DQK, p.Sq, p.B, (uint64_t)p.H * DQK,
+                                           (uint64_t)p.Sq * p.H * DQK, 64, BM, 1);
+  const CUtensorMap tk = make_tmap_bf16_3d(k, (uint64_t)p.Hk * DQK, p.Sk, p.B, (uint64_t)p.Hk * DQK,
+                                           (uint64_t)p.Sk * p.Hk * DQK, 64, C::BN, 1);
+  const CUtensorMap tv = make_tmap_bf16_3d(v, (uint64_t)p.Hk * DV, p.Sk, p.B, (uint64_t)p.Hk * DV,
+                                           (uint64_t)p.Sk * p.Hk * DV, 64, C::BN, 1);
+  const int grid = p.B * p.H * ((p.num_qtiles + 1) / 2);
+  kern<<<grid, NUM_THREADS, C::SMEM, s>>>(tq, tk, tv, p);
+  check_cuda(cudaGetLastError(), "attn_fwd2 launch");
 }
 
 template <int DQK, int DV, int BN>
@@ -465,8 +884,8 @@ struct DKVBars {
   uint64_t acc_full;
   uint32_t tmem_base;
   int abort_flag;
-  float lse2[2][64];
-  float dlt[2][64];
+  alignas(8) float lse2[2][64];  // -lse * log2(e) per query of the staged tile
+  alignas(8) float dlt[2][64];   // -delta per query
 };
 
 template <int DQK, int DV, int NBUF>
@@ -620,10 +1039,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // stage lse2 / delta of this query tile
       if (t < 64) {
         const int qi = q0 + t;
-        bar.lse2[st][t] = qi < p.Sq ? p.lse[((size_t)b * p.H + h) * p.Sq + qi] * 1.4426950408889634f : INFINITY;
+        bar.lse2[st][t] = qi < p.Sq ? -p.lse[((size_t)b * p.H + h) * p.Sq + qi] * 1.4426950408889634f : -INFINITY;
       } else {
         const int qi = q0 + t - 64;
-        bar.dlt[st][t - 64] = qi < p.Sq ? p.delta[((size_t)b * p.H + h) * p.Sq + qi] : 0.f;
+        bar.dlt[st][t - 64] = qi < p.Sq ? -p.delta[((size_t)b * p.H + h) * p.Sq + qi] : 0.f;
       }
       named_bar_sync(1, 32 * NUM_SM_WARPS);
       if (!mbar_wait(&bar.s_full[sb], (i / NBUF) & 1, &bar.abort_flag, &g_err, 36)) { ok = false; break; }
@@ -639,20 +1058,25 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_ld_32x32b_x32(tmem + lane_base + C::DPT_COL + sb * C::BQ + c * 32, dv);
         tmem_ld_wait();
         uint32_t pk[16], dk[16];
+        const uint64_t cc = pk2(p.scale_log2, p.scale_log2);
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float pr[2], ds[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int col = c * 32 + e + u;
+          const int col = c * 32 + e;
+          const float2 nl = *reinterpret_cast<const float2*>(&bar.lse2[st][col]);
+          const float2 nd = *reinterpret_cast<const float2*>(&bar.dlt[st][col]);
+          const uint64_t x = fma2(pk2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), cc, pk2(nl.x, nl.y));
+          uint64_t pv = ((e & 7) == 6) ? exp2_poly2(x) : ex2_mufu2(x);
+          if (need_mask) {
+            float a0, a1;
+            up2(pv, a0, a1);
             const int qi = q0 + col;
-            float pv = ex2(__uint_as_float(sv[e + u]) * p.scale_log2 - bar.lse2[st][col]);
-            if (need_mask && (kidx >= p.Sk || qi >= p.Sq || (p.causal && kidx > qi + offset))) pv = 0.f;
-            pr[u] = pv;
-            ds[u] = pv * (__uint_as_float(dv[e + u]) - bar.dlt[st][col]);
+            if (kidx >= p.Sk || qi >= p.Sq || (p.causal && kidx > qi + offset)) a0 = 0.f;
+            if (kidx >= p.Sk || qi + 1 >= p.Sq || (p.causal && kidx > qi + 1 + offset)) a1 = 0.f;
+            pv = pk2(a0, a1);
           }
-          pk[e / 2] = pack_bf16x2(pr[0], pr[1]);
-          dk[e / 2] = pack_bf16x2(ds[0], ds[1]);
+          const uint64_t ds = mul2(pv, add2(pk2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), pk2(nd.x, nd.y)));
+          pk[e / 2] = pack_bf16x2_u64(pv);
+          dk[e / 2] = pack_bf16x2_u64(ds);
         }
         const int chunk0 = (c * 32) / 8;
 #pragma unroll
@@ -885,17 +1309,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_ld_32x32b_x32(tmem + lane_base + C::DP_COL + st * C::BK + c * 32, dv);
         tmem_ld_wait();
         uint32_t pk[16];
+        const uint64_t cc = pk2(p.scale_log2, p.scale_log2), nl = pk2(-lse2, -lse2), nd = pk2(-dl, -dl);
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float d2[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int key = k0 + c * 32 + e + u;
-            float pv = ex2(__uint_as_float(sv[e + u]) * p.scale_log2 - lse2);
-            if (need_mask && (!qvalid || key >= p.Sk || (p.causal && key > diag))) pv = 0.f;
-            d2[u] = pv * (__uint_as_float(dv[e + u]) - dl);
+          const uint64_t x = fma2(pk2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), cc, nl);
+          uint64_t pv = ((e & 7) == 6) ? exp2_poly2(x) : ex2_mufu2(x);
+          if (need_mask) {
+            float a0, a1;
+            up2(pv, a0, a1);
+            const int key = k0 + c * 32 + e;
+            if (!qvalid || key >= p.Sk || (p.causal && key > diag)) a0 = 0.f;
+            if (!qvalid || key + 1 >= p.Sk || (p.causal && key + 1 > diag)) a1 = 0.f;
+            pv = pk2(a0, a1);
           }
-          pk[e / 2] = pack_bf16x2(d2[0], d2[1]);
+          pk[e / 2] = pack_bf16x2_u64(mul2(pv, add2(pk2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nd)));
         }
         const int chunk0 = (c * 32) / 8;
 #pragma unroll
@@ -994,8 +1421,8 @@ void attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, 
   p.o = static_cast<__nv_bfloat16*>(o);
   p.lse = lse;
   p.num_qtiles = (Sq + BM - 1) / BM;
-  if (Dqk == 128 && Dv == 128) launch_fwd<128, 128, 128>(q, k, v, p, Dqk, Dv, s);
-  else if (Dqk == 64 && Dv == 64) launch_fwd<64, 64, 128>(q, k, v, p, Dqk, Dv, s);
+  if (Dqk == 128 && Dv == 128) launch_fwd2<128, 128>(q, k, v, p, s);
+  else if (Dqk == 64 && Dv == 64) launch_fwd2<64, 64>(q, k, v, p, s);
   else if (Dqk == 192 && Dv == 128) launch_fwd<192, 128, 64>(q, k, v, p, Dqk, Dv, s);
   else throw std::runtime_error("attention: unsupported head dims (supported: 64/64, 128/128, 192/128)");
 }

@@ -125,6 +125,37 @@ def bench_memory_bound(ext, out):
     print(json.dumps(out[-1]), flush=True)
 
 
+def small_cases(ext, out):
+    """A few launches of each kernel on small shapes (for ncu captures)."""
+    B, S, H, Hk, D = 1, 2048, 8, 8, 128
+    q = torch.randn(B, S, H, D, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, S, Hk, D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, S, Hk, D, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):
+        o, lse = ext.attn_fwd(q, k, v, True, 1 / math.sqrt(D))
+        ext.attn_bwd(torch.randn_like(o), q, k, v, o, lse, True, 1 / math.sqrt(D))
+    A = torch.randn(2048, 4096, device="cuda", dtype=torch.bfloat16)
+    W = torch.randn(4096, 4096, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):
+        ext.gemm(A, W, False, False)
+    torch.cuda.synchronize()
+    out.append({"small_cases": "ok", "attn_err": ext.attn_error_code(True), "gemm_err": ext.gemm_error_code(True)})
+    print(json.dumps(out[-1]), flush=True)
+
+
+def attn_large(ext, out):
+    """One forward + backward at the Llama-3 8B shape (B1, S8192, H32/8, D128) for ncu."""
+    B, S, H, Hk, D = 1, 8192, 32, 8, 128
+    q = torch.randn(B, S, H, D, device="cuda", dtype=torch.bfloat16)
+    k = torch.randn(B, S, Hk, D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(B, S, Hk, D, device="cuda", dtype=torch.bfloat16)
+    o, lse = ext.attn_fwd(q, k, v, True, 1 / math.sqrt(D))
+    ext.attn_bwd(torch.randn_like(o), q, k, v, o, lse, True, 1 / math.sqrt(D))
+    torch.cuda.synchronize()
+    out.append({"attn_large": "ok", "attn_err": ext.attn_error_code(True)})
+    print(json.dumps(out[-1]), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,mem")
@@ -139,6 +170,10 @@ def main():
         bench_gemm(ext, out)
     if "attn" in sel:
         bench_attn(ext, out)
+    if "attn_large" in sel:
+        attn_large(ext, out)
+    if "small" in sel:
+        small_cases(ext, out)
     if "mem" in sel:
         bench_memory_bound(ext, out)
     if a.out:
