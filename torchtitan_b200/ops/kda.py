@@ -1,0 +1,173 @@
+"""Kimi Delta Attention (KDA): gated delta rule with per-channel decay.
+
+Recurrence for one head (state S in R^{K x V}, per-channel log decay g_t <= 0):
+
+    S'_t = diag(exp(g_t)) S_{t-1}
+    S_t  = S'_t + beta_t k_t (v_t - S'_t^T k_t)^T
+    o_t  = S_t^T q_t                      (q scaled by 1/sqrt(K), q/k L2-normalised)
+
+``chunk_kda`` evaluates it chunk-parallel (chunk C = 64) in the WY form of
+the delta rule (Yang et al., "Parallelizing Linear Transformers with the
+Delta Rule over Sequence Length", 2024), with G = within-chunk cumulative
+log decay:
+
+    A_kk[i,j] = beta_i sum_d k_i k_j exp(G_i - G_j)        (j < i)
+    T         = (I + A_kk)^{-1} diag(beta)
+    w = T (exp(G) * k),   u = T v
+    per chunk: v' = u - w S;  o = (q * exp(G)) S + A_qk v'   (A_qk: j <= i)
+               S <- diag(exp(G_C)) S + (exp(G_C - G) * k)^T v'
+
+Pairwise decayed products are formed per column j with exp(G_i - G_j) <= 1
+(never the overflow-prone factorisation exp(G_i) exp(-G_j)); the custom
+backward recomputes them instead of saving C x C x K tensors.
+Reference semantics: ``fla/ops/kda/naive.py`` (naive_recurrent_kda).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+
+class _DecayedGram(torch.autograd.Function):
+    """out[n, i, j] = sum_d a[n,i,d] b[n,j,d] exp(G[n,i,d] - G[n,j,d]) for j < i
+    (``strict``) or j <= i, else 0.  a, b, G: [N, C, K] fp32."""
+
+    @staticmethod
+    def forward(ctx, a, b, G, strict):
+        N, C, K = a.shape
+        out = a.new_zeros(N, C, C)
+        idx = torch.arange(C, device=a.device)
+        for j in range(C):
+            e = torch.exp((G - G[:, j : j + 1, :]).clamp(max=0.0))
+            col = (a * e * b[:, j : j + 1, :]).sum(-1)  # [N, C]
+            keep = (idx > j) if strict else (idx >= j)
+            out[:, :, j] = col * keep
+        ctx.save_for_backward(a, b, G)
+        ctx.strict = strict
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        a, b, G = ctx.saved_tensors
+        N, C, K = a.shape
+        da, db, dG = torch.zeros_like(a), torch.zeros_like(b), torch.zeros_like(G)
+        idx = torch.arange(C, device=a.device)
+        for j in range(C):
+            keep = (idx > j) if ctx.strict else (idx >= j)
+            w = (dout[:, :, j] * keep)[:, :, None]  # [N, C, 1]
+            e = torch.exp((G - G[:, j : j + 1, :]).clamp(max=0.0))
+            bj = b[:, j : j + 1, :]
+            t = w * e  # [N, C, K]
+            da += t * bj
+            term = t * a  # dO[i,j] a_i e_ij
+            db[:, j, :] += term.sum(1)
+            full = term * bj
+            dG += full
+            dG[:, j, :] -= full.sum(1)
+        return da, db, dG, None
+
+
+def decayed_gram(a, b, G, strict: bool):
+    return _DecayedGram.apply(a, b, G, strict)
+
+
+def kda_gate(g_raw: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor | None) -> torch.Tensor:
+    """g = -exp(A_log[h]) * softplus(g_raw + dt_bias): [..., H, K] fp32 log decay."""
+    H, K = g_raw.shape[-2:]
+    x = g_raw.float()
+    if dt_bias is not None:
+        x = x + dt_bias.float().view(H, K)
+    return -A_log.float().exp().view(H, 1) * F.softplus(x)
+
+
+def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    xf = x.float()
+    return xf * torch.rsqrt(xf.pow(2).sum(-1, keepdim=True) + eps)
+
+
+def chunk_kda(q, k, v, g, beta, scale: float | None = None, chunk_size: int = 64,
+              initial_state: torch.Tensor | None = None, output_final_state: bool = False,
+              use_qk_l2norm: bool = True):
+    """q, k: [B, T, H, K]; v: [B, T, H, V]; g: [B, T, H, K] (log decay, fp32); beta: [B, T, H].
+
+    Returns o [B, T, H, V] (dtype of v) and the final state [B, H, K, V] if requested.
+    """
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    C = chunk_size
+    scale = K ** -0.5 if scale is None else scale
+    dtype = v.dtype
+    if use_qk_l2norm:
+        q, k = l2norm(q), l2norm(k)
+    q = q.float() * scale
+    k, v, g, beta = k.float(), v.float(), g.float(), beta.float()
+    pad = (-T) % C
+    if pad:
+        # padded steps: g = 0 (no decay), k = v = q = 0, beta = 0 -> state unchanged
+        q, k, v, g = (F.pad(x, (0, 0, 0, 0, 0, pad)) for x in (q, k, v, g))
+        beta = F.pad(beta, (0, 0, 0, pad))
+    Tp = T + pad
+    NT = Tp // C
+
+    def chunks(x):  # [B, Tp, H, D] -> [B*H, NT, C, D]
+        return x.view(B, NT, C, H, -1).permute(0, 3, 1, 2, 4).reshape(B * H, NT, C, -1)
+
+    qc, kc, vc, gc = chunks(q), chunks(k), chunks(v), chunks(g)
+    bc = beta.view(B, NT, C, H).permute(0, 3, 1, 2).reshape(B * H, NT, C)
+    G = gc.cumsum(2)
+    N = B * H * NT
+    Akk = decayed_gram(kc.reshape(N, C, K), kc.reshape(N, C, K), G.reshape(N, C, K), True).view(B * H, NT, C, C)
+    Akk = Akk * bc[..., :, None]
+    eye = torch.eye(C, device=q.device, dtype=torch.float32)
+    Tm = torch.linalg.solve_triangular(eye + Akk, eye.expand_as(Akk), upper=False, unitriangular=True)
+    Tm = Tm * bc[..., None, :]
+    w = Tm @ (G.exp() * kc)
+    u = Tm @ vc
+    Aqk = decayed_gram(qc.reshape(N, C, K), kc.reshape(N, C, K), G.reshape(N, C, K), False).view(B * H, NT, C, C)
+    qg = qc * G.exp()
+    Glast = G[:, :, -1:, :]  # [BH, NT, 1, K]
+    kdec = (Glast - G).exp() * kc
+    S = q.new_zeros(B * H, K, V) if initial_state is None else initial_state.float().reshape(B * H, K, V)
+    outs = []
+    for n in range(NT):
+        vn = u[:, n] - w[:, n] @ S
+        outs.append(qg[:, n] @ S + Aqk[:, n] @ vn)
+        S = Glast[:, n, 0, :, None].exp() * S + kdec[:, n].transpose(1, 2) @ vn
+    o = torch.stack(outs, 1)  # [BH, NT, C, V]
+    o = o.view(B, H, NT, C, V).permute(0, 2, 3, 1, 4).reshape(B, Tp, H, V)[:, :T]
+    final = S.view(B, H, K, V) if output_final_state else None
+    return o.to(dtype), final
+
+
+def naive_recurrent_kda(q, k, v, g, beta, scale=None, use_qk_l2norm: bool = True):
+    """Token-by-token recurrence (test oracle)."""
+    B, T, H, K = q.shape
+    V = v.shape[-1]
+    scale = K ** -0.5 if scale is None else scale
+    if use_qk_l2norm:
+        q, k = l2norm(q), l2norm(k)
+    q, k, v, g, beta = (x.float() for x in (q, k, v, g, beta))
+    q = q * scale
+    S = q.new_zeros(B, H, K, V)
+    o = torch.zeros(B, T, H, V, dtype=torch.float32, device=q.device)
+    for t in range(T):
+        S = S * g[:, t, :, :, None].exp()
+        kS = (k[:, t, :, :, None] * S).sum(-2)
+        S = S + (beta[:, t, :, None] * k[:, t])[..., None] * (v[:, t] - kS)[..., None, :]
+        o[:, t] = (q[:, t, :, :, None] * S).sum(-2)
+    return o, S
+
+
+def short_conv_silu(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """Causal depthwise conv (kernel [C, 1, W]) over time then SiLU; x: [B, T, C]."""
+    W = weight.shape[-1]
+    xt = F.pad(x.transpose(1, 2), (W - 1, 0))
+    y = F.conv1d(xt, weight.to(x.dtype), groups=x.shape[-1])
+    return F.silu(y).transpose(1, 2)
+
+
+def gated_rms_norm(x: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm over the last dim, times weight, times sigmoid(gate)."""
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * weight.float()
+    return (y * torch.sigmoid(gate.float())).to(x.dtype)
