@@ -123,6 +123,10 @@ def cross_entropy_sum(logits: torch.Tensor, labels: torch.Tensor, ignore_index: 
     return _CESum.apply(logits, labels, ignore_index)
 
 
+# ---------------------------------------------------------------- MoE experts
+from .moe import grouped_swiglu  # noqa: E402
+
+
 # -------------------------------------------------------------------------- AdamW
 def fused_adamw_(params, grads, exp_avgs, exp_avg_sqs, *, lr: float, beta1: float, beta2: float,
                  eps: float, weight_decay: float, step: int) -> None:
