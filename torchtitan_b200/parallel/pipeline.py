@@ -23,12 +23,13 @@ from torchtitan_b200.utils.logging import logger
 
 
 def generate_llm_fqn_per_model_part(num_stages: int, num_layers: int, input_weight: int = 1,
-                                    output_weight: int = 1) -> list[list[str]]:
+                                    output_weight: int = 1, first: str = "tok_embeddings",
+                                    last: tuple[str, ...] = ("norm", "output")) -> list[list[str]]:
     """Split ``num_layers`` decoder layers (+ embedding / head weights) evenly into stages."""
     if num_stages < 1:
         raise ValueError("num_stages must be >= 1")
     if num_stages == 1:
-        return [["tok_embeddings"] + [f"layers.{i}" for i in range(num_layers)] + ["norm", "output"]]
+        return [[first] + [f"layers.{i}" for i in range(num_layers)] + list(last)]
     total = num_layers + input_weight + output_weight
     base, extra = divmod(total, num_stages)
     sizes = [base + (1 if s < extra else 0) for s in range(num_stages)]
@@ -38,7 +39,7 @@ def generate_llm_fqn_per_model_part(num_stages: int, num_layers: int, input_weig
         names: list[str] = []
         budget = size
         if s == 0:
-            names.append("tok_embeddings")
+            names.append(first)
             budget -= input_weight
         if s == num_stages - 1:
             budget -= output_weight
@@ -52,7 +53,7 @@ def generate_llm_fqn_per_model_part(num_stages: int, num_layers: int, input_weig
             while layer < num_layers:
                 names.append(f"layers.{layer}")
                 layer += 1
-            names += ["norm", "output"]
+            names += list(last)
         parts.append(names)
     return parts
 
@@ -73,7 +74,9 @@ def _prune(model: nn.Module, keep: list[str]) -> nn.Module:
     for k in list(m.layers.keys()):
         if k not in keep_layers:
             del m.layers[k]
-    for attr in ("tok_embeddings", "norm", "output"):
+    first = getattr(model, "pp_first_module", "tok_embeddings")
+    last = tuple(getattr(model, "pp_last_modules", ("norm", "output")))
+    for attr in (first, *last):
         if attr not in keep and getattr(m, attr, None) is not None:
             setattr(m, attr, None)
     return m
@@ -108,7 +111,9 @@ def pipeline_llm(model: nn.Module, *, parallel_dims: Any, training: Any, paralle
         raise ValueError("single-stage schedule needs exactly one stage per rank")
     if not single and per_rank < 2:
         raise ValueError("multi-stage schedule needs >= 2 stages per rank")
-    fqns = parallelism.module_fqns_per_model_part or generate_llm_fqn_per_model_part(n_stages, n_layers, iw, ow)
+    fqns = parallelism.module_fqns_per_model_part or generate_llm_fqn_per_model_part(
+        n_stages, n_layers, iw, ow, getattr(model, "pp_first_module", "tok_embeddings"),
+        tuple(getattr(model, "pp_last_modules", ("norm", "output"))))
     style = "v" if parallelism.pipeline_parallel_schedule in ("ZBVZeroBubble", "DualPipeV") else "loop"
     pp_rank = pp_mesh.get_local_rank()
     stages, parts = [], []
