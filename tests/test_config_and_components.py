@@ -1,0 +1,201 @@
+"""CPU unit tests: config system, registry, parallel dims, LR schedule, data, optimizers, adapters."""
+import dataclasses
+import math
+
+import pytest
+import torch
+
+from torchtitan_b200.components.dataloader import SyntheticDataLoader
+from torchtitan_b200.components.lr_scheduler import wsd_factor
+from torchtitan_b200.config import Configurable
+from torchtitan_b200.config.manager import ConfigManager, split_module_and_config
+from torchtitan_b200.parallel.parallel_dims import ParallelDims
+from torchtitan_b200.parallel.pipeline import generate_llm_fqn_per_model_part
+
+
+def test_configurable_requires_kw_only_slots():
+    with pytest.raises(TypeError):
+        class Bad(Configurable):
+            @dataclasses.dataclass
+            class Config(Configurable.Config):
+                x: int = 1
+
+    class Good(Configurable):
+        @dataclasses.dataclass(kw_only=True, slots=True)
+        class Config(Configurable.Config):
+            x: int = 1
+
+        def __init__(self, config, **kw):
+            self.config, self.kw = config, kw
+
+    g = Good.Config(x=3).build(extra=5)
+    assert g.config.x == 3 and g.kw == {"extra": 5}
+    with pytest.raises(ValueError):
+        Good.Config().build(x=2)
+
+
+def test_split_module_and_config():
+    m, c, rest = split_module_and_config(["--module=llama3", "--config", "llama3_8b", "--training.steps", "5"])
+    assert (m, c, rest) == ("llama3", "llama3_8b", ["--training.steps", "5"])
+
+
+def test_config_manager_overrides():
+    cfg = ConfigManager().parse_args(["--module", "llama3", "--config", "llama3_debugmodel",
+                                      "--training.steps", "7", "--optimizer.lr", "0.01"])
+    assert cfg.training.steps == 7 and cfg.optimizer.lr == 0.01
+    assert cfg.model_spec.flavor == "debugmodel"
+    d = cfg.to_dict()
+    assert d["model_spec"] == {"name": "llama3", "flavor": "debugmodel"}
+
+
+def test_kimi_registry_flavors():
+    from torchtitan_b200.models.kimi_linear import config_registry as r
+    from torchtitan_b200.models.kimi_linear import kimi_linear_args
+
+    for name in ("kimi_linear_194m_baseline", "kimi_linear_48b_block_attn_res", "kimi_linear_528m_full_attn_res"):
+        assert callable(getattr(r, name))
+    a = kimi_linear_args["48b_baseline"]
+    assert a.full_attn_layers == [4, 8, 12, 16, 20, 24, 27] and len(a.kda_layers) == 20
+    assert a.num_experts == 256 and a.hidden_size == 2304
+
+
+def test_parallel_dims():
+    class P:
+        data_parallel_replicate_degree = 1
+        data_parallel_shard_degree = -1
+        context_parallel_degree = 2
+        tensor_parallel_degree = 2
+        pipeline_parallel_degree = 1
+        expert_parallel_degree = 4
+        expert_tensor_parallel_degree = 1
+
+    pd = ParallelDims.from_config(P, 8)
+    assert pd.dp_shard == 2 and pd.fsdp_enabled and pd.seq_len_divisor == 8 and pd.efsdp == 2
+    with pytest.raises(ValueError):
+        P.pipeline_parallel_degree = 3
+        ParallelDims.from_config(P, 8)
+
+
+def test_wsd_schedule():
+    f = lambda s: wsd_factor(s, warmup=2, stable=5, decay=4, kind="linear", min_factor=0.1)  # noqa: E731
+    assert f(0) == 0.5 and f(1) == 1.0 and f(3) == 1.0
+    assert math.isclose(f(10), 0.1)
+    c = wsd_factor(9, warmup=2, stable=5, decay=4, kind="cosine", min_factor=0.0)
+    assert 0.0 <= c <= 1.0
+
+
+def test_synthetic_loader_resume():
+    cfg = SyntheticDataLoader.Config(vocab_size=100, pin_memory=False)
+    a = cfg.build(dp_rank=1, dp_world_size=2, seq_len=16, local_batch_size=2)
+    it = iter(a)
+    next(it)
+    st = a.state_dict()
+    x2, y2 = next(it)
+    b = cfg.build(dp_rank=1, dp_world_size=2, seq_len=16, local_batch_size=2)
+    b.load_state_dict(st)
+    xb, yb = next(iter(b))
+    assert torch.equal(x2["input"], xb["input"]) and torch.equal(y2, yb)
+    assert torch.equal(x2["input"][:, 1:], y2[:, :-1])
+    assert int(x2["input"].max()) < 100
+
+
+def test_pipeline_fqn_split():
+    parts = generate_llm_fqn_per_model_part(4, 6)
+    flat = [n for p in parts for n in p]
+    assert flat[0] == "tok_embeddings" and flat[-2:] == ["norm", "output"]
+    assert [n for n in flat if n.startswith("layers")] == [f"layers.{i}" for i in range(6)]
+    assert len(parts) == 4
+
+
+def test_muon_newton_schulz_orthogonalizes():
+    from torchtitan_b200.components.optimizer import zeropower_via_newtonschulz5
+
+    torch.manual_seed(0)
+    G = torch.randn(64, 32)
+    X = zeropower_via_newtonschulz5(G, steps=5)
+    s = torch.linalg.svdvals(X)
+    assert s.min() > 0.5 and s.max() < 1.5  # quintic NS pushes all singular values near 1
+
+
+def test_muon_optimizer_steps():
+    from torchtitan_b200.components.optimizer import OptimizersContainer
+
+    m = torch.nn.Sequential(torch.nn.Linear(16, 16, bias=False), torch.nn.LayerNorm(16))
+    opt = OptimizersContainer.Config(name="Muon", lr=1e-3, muon_lr=0.02,
+                                     muon_exclude_patterns=["1\\."]).build(model_parts=[m])
+    groups = opt.optimizers[0].param_groups
+    assert any(g["use_muon"] for g in groups) and any(not g["use_muon"] for g in groups)
+    w0 = m[0].weight.detach().clone()
+    m(torch.randn(4, 16)).sum().backward()
+    opt.step()
+    assert not torch.equal(w0, m[0].weight)
+
+
+def test_adamw_matches_torch():
+    from torchtitan_b200.components.optimizer import AdamW
+
+    torch.manual_seed(0)
+    p1 = torch.nn.Parameter(torch.randn(10, 5))
+    p2 = torch.nn.Parameter(p1.detach().clone())
+    o1 = AdamW([p1], lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    o2 = torch.optim.AdamW([p2], lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    for _ in range(3):
+        g = torch.randn(10, 5)
+        p1.grad, p2.grad = g.clone(), g.clone()
+        o1.step()
+        o2.step()
+    assert torch.allclose(p1, p2, atol=1e-6)
+
+
+def test_llama_hf_adapter_roundtrip():
+    from torchtitan_b200.models.llama3 import llama3_args
+    from torchtitan_b200.models.llama3.state_dict_adapter import Llama3StateDictAdapter
+
+    a = llama3_args["debugmodel"]
+    ad = Llama3StateDictAdapter(a)
+    sd = {"layers.0.attention.wq.weight": torch.randn(256, 256), "layers.0.attention.wk.weight": torch.randn(128, 256),
+          "layers.3.feed_forward.w1.weight": torch.randn(768, 256), "tok_embeddings.weight": torch.randn(2048, 256)}
+    hf = ad.to_hf(sd)
+    assert "model.layers.0.self_attn.q_proj.weight" in hf and "model.embed_tokens.weight" in hf
+    back = ad.from_hf(hf)
+    for k, v in sd.items():
+        assert torch.equal(back[k], v)
+
+
+def test_kimi_hf_adapter_roundtrip():
+    from torchtitan_b200.models.kimi_linear.state_dict_adapter import KimiLinearStateDictAdapter
+
+    ad = KimiLinearStateDictAdapter()
+    sd = {"layers.1.ffn._moe.experts.w1": torch.randn(4, 8, 6), "layers.0.self_attn.A_log": torch.randn(2),
+          "layers.1.ffn._moe.router.gate.weight": torch.randn(4, 6), "lm_head.weight": torch.randn(10, 6)}
+    hf = ad.to_hf(sd)
+    assert "model.layers.1.block_sparse_moe.experts.3.w1.weight" in hf
+    back = ad.from_hf(hf)
+    for k, v in sd.items():
+        assert torch.equal(back[k], v)
+
+
+def test_moe_forward_backward_and_aux():
+    from torchtitan_b200.models.common.moe import MoE
+
+    torch.manual_seed(0)
+    m = MoE(16, 32, num_experts=4, top_k=2, route_norm=True, route_scale=2.0, shared_hidden_dim=32,
+            aux_loss_coeff=0.01)
+    m.init_weights(0.02)
+    x = torch.randn(2, 5, 16, requires_grad=True)
+    y = m(x)
+    y.sum().backward()
+    assert y.shape == x.shape and x.grad is not None
+    assert m.router.gate.weight.grad is not None and m.last_aux_loss is not None
+    assert float(m.tokens_per_expert.sum()) == 2 * 5 * 2
+
+
+def test_kimi_flops_counts_active_experts_only():
+    from torchtitan_b200.models.kimi_linear import build_args
+
+    a = build_args("debugmodel")
+    with torch.device("meta"):
+        model = a.build()
+    n, flops = a.get_nparams_and_flops(model, 128)
+    routed = sum(p.numel() for k, p in model.named_parameters() if "_moe.experts." in k)
+    assert flops < 6 * (n - routed * 0.5)

@@ -1,0 +1,162 @@
+"""Multi-process tests on CPU with the gloo backend (world size 2)."""
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(fn, world=2, *args):
+    port = _port()
+    mp.spawn(_entry, args=(world, port, fn, args), nprocs=world, join=True)
+
+
+def _entry(rank, world, port, fn, args):
+    os.environ.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        fn(rank, world, *args)
+    finally:
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- FSDP trainer
+def _train_llama_fsdp(rank, world, out_dir):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    cfg = ConfigManager().parse_args(["--module", "llama3", "--config", "llama3_debugmodel_cpu",
+                                      "--training.steps", "4", "--checkpoint.enable", "--checkpoint.interval", "2",
+                                      "--dump-folder", out_dir, "--checkpoint.keep-latest-k", "5",
+                                      "--validator.enable", "--validator.freq", "4", "--validator.steps", "1"])
+    t = Trainer(cfg)
+    t.train()
+    losses = t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"]
+    assert 5.0 < losses < 9.0
+    t.close()
+    # resume from the step-4 checkpoint into a fresh trainer
+    cfg2 = ConfigManager().parse_args(["--module", "llama3", "--config", "llama3_debugmodel_cpu",
+                                       "--training.steps", "5", "--checkpoint.enable", "--checkpoint.interval", "10",
+                                       "--dump-folder", out_dir])
+    t2 = Trainer(cfg2)
+    t2.checkpointer.load()
+    assert t2.step == 4 and t2.ntokens_seen == t.ntokens_seen
+    assert t2.dataloader.batches_emitted == t.dataloader.batches_emitted
+    t2.close()
+
+
+def test_fsdp_gloo_training_and_resume():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_train_llama_fsdp, 2, d)
+        assert os.path.exists(os.path.join(d, "checkpoint", "step-4", ".metadata"))
+
+
+# ---------------------------------------------------------------- Ulysses a2a
+def _ulysses(rank, world):
+    from torchtitan_b200.ops import reference as R
+    from torchtitan_b200.parallel.context_parallel import head_to_seq, seq_to_head, ulysses_hook
+
+    torch.manual_seed(0)
+    B, S, H, D = 1, 8, 4, 4
+    q, k, v = (torch.randn(B, S, H, D) for _ in range(3))
+    full = R.attention(q, k, v, True)
+    sl = slice(rank * S // world, (rank + 1) * S // world)
+    x = q[:, sl].contiguous()
+    assert torch.equal(head_to_seq(seq_to_head(x, dist.group.WORLD), dist.group.WORLD), x)
+    hook = ulysses_hook(dist.group.WORLD)
+    o = hook(lambda a, b, c, m: R.attention(a, b, c, True), q[:, sl].contiguous(), k[:, sl].contiguous(),
+             v[:, sl].contiguous(), None)
+    assert torch.allclose(o, full[:, sl], atol=1e-5)
+
+
+def test_ulysses_all_to_all_matches_full_attention():
+    _run(_ulysses, 2)
+
+
+# ---------------------------------------------------------------- expert parallel
+def _ep(rank, world):
+    from torchtitan_b200.models.common.moe import MoE
+    from torchtitan_b200.parallel.expert_parallel import make_ep_dispatch
+
+    torch.manual_seed(0)
+    m = MoE(8, 16, num_experts=4, top_k=2)
+    m.init_weights(0.1)
+    for p in m.parameters():
+        dist.broadcast(p.data, 0)
+    x = torch.randn(1, 6, 8) + rank
+    ref = m(x)
+    # shard experts: this rank keeps experts [2r, 2r+2)
+    e = m.experts
+    full = [p.data.clone() for p in (e.w1, e.w2, e.w3)]
+    for name, f in zip(("w1", "w2", "w3"), full):
+        setattr(e, name, torch.nn.Parameter(f[rank * 2:(rank + 1) * 2].clone()))
+    m.ep_dispatch = make_ep_dispatch(dist.group.WORLD, 4)
+    xr = x.clone().requires_grad_()
+    out = m(xr)
+    assert torch.allclose(out, ref, atol=1e-5)
+    out.sum().backward()
+    assert xr.grad is not None and e.w1.grad.shape[0] == 2
+
+
+def test_expert_parallel_dispatch_matches_local():
+    _run(_ep, 2)
+
+
+# ---------------------------------------------------------------- DistMuon
+def _distmuon(rank, world):
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Shard, distribute_tensor
+
+    from torchtitan_b200.components.optimizer import Muon
+
+    mesh = init_device_mesh("cpu", (world,), mesh_dim_names=("fsdp",))
+    torch.manual_seed(0)
+    w = torch.randn(8, 6)
+    g = torch.randn(8, 6)
+    p_ref = torch.nn.Parameter(w.clone())
+    p_ref.grad = g.clone()
+    Muon([{"params": [p_ref], "use_muon": True}], lr=0.02).step()
+    p = torch.nn.Parameter(distribute_tensor(w.clone(), mesh, [Shard(0)]))
+    p.grad = distribute_tensor(g.clone(), mesh, [Shard(0)])
+    Muon([{"params": [p], "use_muon": True}], lr=0.02, distributed=True).step()
+    assert torch.allclose(p.full_tensor(), p_ref.detach(), atol=1e-5)
+
+
+def test_distmuon_matches_muon():
+    _run(_distmuon, 2)
+
+
+# ---------------------------------------------------------------- failure detection
+def _rank_dies(rank, world):
+    import datetime
+
+    t = torch.ones(1)
+    dist.all_reduce(t)
+    if rank == 1:
+        os._exit(0)  # leaves between steps, no collective in flight
+    pg = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=3))
+    with pytest.raises(Exception):
+        dist.all_reduce(t, group=pg)
+
+
+def test_peer_exit_surfaces_as_error_not_hang():
+    port = _port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_entry, args=(r, 2, port, _rank_dies, ())) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(60)
+    assert all(not p.is_alive() for p in procs)

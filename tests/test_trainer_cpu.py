@@ -1,0 +1,26 @@
+"""End-to-end trainer steps on CPU (single process, gloo world of 1)."""
+import os
+
+import pytest
+import torch
+
+from torchtitan_b200.config.manager import ConfigManager
+
+
+@pytest.mark.parametrize("module,config,extra", [
+    ("llama3", "llama3_debugmodel_cpu", []),
+    ("llama3", "llama3_debugmodel", ["--training.seq-len", "128", "--training.local-batch-size", "2",
+                                     "--training.dtype", "float32", "--training.mixed-precision-param", "float32"]),
+    ("kimi_linear", "kimi_linear_debugmodel", []),
+    ("kimi_linear", "kimi_linear_debugmodel_block_attn_res", []),
+])
+def test_trainer_steps(module, config, extra, tmp_path):
+    from torchtitan_b200.trainer import Trainer
+
+    cfg = ConfigManager().parse_args(["--module", module, "--config", config, "--training.steps", "2",
+                                      "--dump-folder", str(tmp_path), *extra])
+    t = Trainer(cfg)
+    t.train()
+    loss = t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"]
+    assert torch.isfinite(torch.tensor(loss)) and 4.0 < loss < 12.0
+    t.close()

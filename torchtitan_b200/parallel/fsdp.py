@@ -16,8 +16,13 @@ import torch.nn as nn
 from torch.distributed.fsdp import CPUOffloadPolicy, MixedPrecisionPolicy, fully_shard
 
 
+_GLOO = False
+
+
 def _disable_grad_division(m) -> None:
-    if hasattr(m, "set_gradient_divide_factor"):
+    # gloo has no PREMUL_SUM: keep FSDP's mean there and let the trainer scale
+    # the backward seed by the DP size instead (model._fsdp_grad_compensation)
+    if not _GLOO and hasattr(m, "set_gradient_divide_factor"):
         m.set_gradient_divide_factor(1.0)
 
 
@@ -39,8 +44,14 @@ def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, redu
     else:
         raise ValueError(f"invalid reshard_after_forward_policy {reshard_after_forward_policy}")
 
-    if getattr(model, "tok_embeddings", None) is not None:
-        _disable_grad_division(fully_shard(model.tok_embeddings, **cfg, reshard_after_forward=reshard))
+    global _GLOO
+    import torch.distributed as dist
+
+    _GLOO = dist.is_initialized() and dist.get_backend() == "gloo"
+    model._fsdp_grad_compensation = dp_mesh.size() if _GLOO else 1
+    first = getattr(model, "pp_first_module", "tok_embeddings")
+    if getattr(model, first, None) is not None:
+        _disable_grad_division(fully_shard(getattr(model, first), **cfg, reshard_after_forward=reshard))
     layers = [l for l in model.layers.values() if l is not None]
     for i, block in enumerate(layers):
         # routed experts are sharded on the expert-data-parallel mesh
@@ -52,7 +63,8 @@ def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, redu
         _disable_grad_division(
             fully_shard(block, **cfg, reshard_after_forward=reshard and not last)
         )
-    tail = [m for m in (getattr(model, "norm", None), getattr(model, "output", None)) if m is not None]
+    last = getattr(model, "pp_last_modules", ("norm", "output"))
+    tail = [getattr(model, n) for n in last if getattr(model, n, None) is not None]
     if tail:
         _disable_grad_division(fully_shard(tail, **cfg, reshard_after_forward=False))
     _disable_grad_division(fully_shard(model, **cfg))

@@ -263,7 +263,8 @@ class Trainer(Stateful, Configurable):
             pred = self.model_parts[0](inputs, **extra_inputs, **extra_kwargs)
             loss = self._loss(pred, labels) / global_valid_tokens
             del pred
-            loss.backward()
+            comp = getattr(self.model_parts[0], "_fsdp_grad_compensation", 1)
+            (loss * comp if comp != 1 else loss).backward()
         return loss
 
     def train_step(self, data_iterator: Iterator) -> torch.Tensor:
