@@ -201,3 +201,40 @@ def test_grad_clip_kernels(ext):
     coef = 1.0 / (ref ** 0.5 + 1e-6)
     for x, b in zip(xs, before):
         assert _rel(x, b * coef) < 1e-2
+
+
+@pytest.mark.parametrize("E,D,H", [(8, 256, 512), (4, 2304, 1024)])
+def test_grouped_swiglu_experts(E, D, H):
+    from torchtitan_b200.ops.moe import _reference, grouped_swiglu
+
+    torch.manual_seed(9)
+    counts = torch.tensor([0, 300, 5, 128][:E] + [77] * max(0, E - 4), device="cuda")
+    n = int(counts.sum())
+    x = (torch.randn(n, D, device="cuda") * 0.5).bfloat16().requires_grad_()
+    w = [(torch.randn(E, H, D, device="cuda") * 0.05).bfloat16().requires_grad_(),
+         (torch.randn(E, D, H, device="cuda") * 0.05).bfloat16().requires_grad_(),
+         (torch.randn(E, H, D, device="cuda") * 0.05).bfloat16().requires_grad_()]
+    y = grouped_swiglu(x, w[0], w[1], w[2], counts)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_()
+    wr = [t.detach().float().requires_grad_() for t in w]
+    yr = _reference(xr, wr[0], wr[1], wr[2], counts)
+    yr.backward(g.float())
+    assert _rel(y, yr) < 2e-2
+    assert _rel(x.grad, xr.grad) < 3e-2
+    for a, b in zip(w, wr):
+        assert _rel(a.grad, b.grad) < 3e-2
+
+
+def test_attention_padded_head_dims():
+    from torchtitan_b200 import ops
+
+    torch.manual_seed(10)
+    q = torch.randn(1, 128, 2, 111, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(1, 128, 2, 111, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(1, 128, 2, 74, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    o = ops.attention(q, k, v, causal=True)
+    o.sum().backward()
+    ref = _attn_ref(q.detach(), k.detach(), v.detach(), True, 111 ** -0.5)
+    assert o.shape == (1, 128, 2, 74) and _rel(o, ref) < 2e-2 and q.grad.shape == q.shape

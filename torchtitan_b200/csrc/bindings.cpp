@@ -33,6 +33,33 @@ Tensor gemm(Tensor A, Tensor B, bool a_mn, bool b_mn) {
   return D;
 }
 
+// mode 1 (grouped rows): A [Mp, K] padded rows, B [G*N, K] (or [G*K, N] if b_mn), tile_group [Mp/128] int32
+Tensor gemm_grouped_rows(Tensor A, Tensor B, Tensor tile_group, int64_t n_out, int64_t b_group_rows, bool b_mn) {
+  check_cuda_bf16(A, "A");
+  check_cuda_bf16(B, "B");
+  TORCH_CHECK(tile_group.scalar_type() == at::kInt && tile_group.is_contiguous(), "tile_group int32");
+  c10::cuda::CUDAGuard g(A.device());
+  const int64_t M = A.size(0), K = A.size(1);
+  TORCH_CHECK(M % 128 == 0 && tile_group.numel() == M / 128, "padded rows must be a multiple of 128");
+  Tensor D = torch::empty({M, n_out}, A.options());
+  ttb::gemm_bf16_grouped(A.data_ptr(), B.data_ptr(), D.data_ptr(), M, n_out, K, false, b_mn, 1, 1,
+                         tile_group.data_ptr<int>(), nullptr, nullptr, B.size(0), (int)b_group_rows, stream());
+  return D;
+}
+
+// mode 2 (grouped reduction): A [Ktot, M], B [Ktot, N]; D [G, M, N]; kstart/klen int32 [G]
+Tensor gemm_grouped_k(Tensor A, Tensor B, Tensor kstart, Tensor klen) {
+  check_cuda_bf16(A, "A");
+  check_cuda_bf16(B, "B");
+  c10::cuda::CUDAGuard g(A.device());
+  const int64_t G = kstart.numel(), M = A.size(1), N = B.size(1), Ktot = A.size(0);
+  TORCH_CHECK(B.size(0) == Ktot, "grouped K: row counts differ");
+  Tensor D = torch::empty({G, M, N}, A.options());
+  ttb::gemm_bf16_grouped(A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, Ktot, true, true, 2, (int)G, nullptr,
+                         kstart.data_ptr<int>(), klen.data_ptr<int>(), Ktot, 0, stream());
+  return D;
+}
+
 std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor w, double eps) {
   check_cuda_bf16(x, "x");
   TORCH_CHECK(x.dim() == 2 && w.dim() == 1 && w.size(0) == x.size(1), "rmsnorm: shape mismatch");
@@ -219,6 +246,8 @@ std::vector<Tensor> attn_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor o
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "torchtitan_b200 sm_100a kernels";
   m.def("gemm", &gemm, "bf16 GEMM on tcgen05: D = A(m,k) * B(n,k)");
+  m.def("gemm_grouped_rows", &gemm_grouped_rows, "grouped GEMM over 128-row padded expert segments");
+  m.def("gemm_grouped_k", &gemm_grouped_k, "grouped GEMM reducing over per-group row ranges (expert wgrad)");
   m.def("gemm_error_code", &ttb::gemm_error_code, "read (and optionally clear) the GEMM timeout word",
         py::arg("reset") = true);
   m.def("attn_error_code", &ttb::attn_error_code, "read (and optionally clear) the attention timeout word",

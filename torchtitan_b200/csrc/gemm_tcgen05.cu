@@ -42,7 +42,51 @@ struct Params {
   int num_m, num_n, num_k;
   __nv_bfloat16* D;
   int ldd;
+  // grouped modes (0 = plain GEMM)
+  //  1: per-M-tile group id tile_group[tm] (-1 = skip) selects B rows [g*b_group_rows, ...)
+  //  2: group g = tile / (num_m*num_n) reduces over K rows [kstart[g], kstart[g]+klen[g]) and
+  //     writes D + g*d_group_stride (klen = 0 writes zeros)
+  int mode;
+  int num_groups;
+  const int* tile_group;
+  const int* group_kstart;
+  const int* group_klen;
+  int b_group_rows;
+  long long d_group_stride;
 };
+
+struct TileInfo {
+  int tm, tn, g, k_base, nk;
+  bool valid;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int& tn);
+
+__device__ __forceinline__ int total_tiles(const Params& p) {
+  return p.num_m * p.num_n * (p.mode == 2 ? p.num_groups : 1);
+}
+
+__device__ __forceinline__ TileInfo tile_info(int t, const Params& p) {
+  TileInfo ti;
+  ti.g = 0;
+  ti.k_base = 0;
+  ti.nk = p.num_k;
+  ti.valid = true;
+  if (p.mode == 2) {
+    const int per = p.num_m * p.num_n;
+    ti.g = t / per;
+    tile_coords(t - ti.g * per, p, ti.tm, ti.tn);
+    ti.k_base = p.group_kstart[ti.g];
+    ti.nk = (p.group_klen[ti.g] + 63) / 64;
+  } else {
+    tile_coords(t, p, ti.tm, ti.tn);
+    if (p.mode == 1) {
+      ti.g = p.tile_group[ti.tm];
+      ti.valid = ti.g >= 0;
+    }
+  }
+  return ti;
+}
 
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int& tn) {
   const int per_group = GROUP_M * p.num_n;
@@ -65,16 +109,18 @@ __device__ __forceinline__ void run_producer(const CUtensorMap* tmA, const CUten
                                              Shared& sh, uint8_t* sA, uint8_t* sB) {
   int stage = 0;
   uint32_t phase = 0;
-  const int tiles = p.num_m * p.num_n;
+  const int tiles = total_tiles(p);
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-    int tm, tn;
-    tile_coords(t, p, tm, tn);
-    for (int kb = 0; kb < p.num_k; ++kb) {
+    const TileInfo ti = tile_info(t, p);
+    if (!ti.valid) continue;
+    const int tm = ti.tm, tn = ti.tn;
+    const int bgo = (p.mode == 1) ? ti.g * p.b_group_rows : 0;
+    for (int kb = 0; kb < ti.nk; ++kb) {
       if (!mbar_wait(&sh.empty[stage], phase ^ 1, &sh.abort_flag, &g_err, 1)) return;
       mbar_arrive_expect_tx(&sh.full[stage], STAGE_BYTES);
       uint8_t* a = sA + stage * A_BYTES;
       uint8_t* b = sB + stage * B_BYTES;
-      const int k0 = kb * BK;
+      const int k0 = ti.k_base + kb * BK;
       if constexpr (!A_MN) {
         tma_load_2d(a, tmA, &sh.full[stage], k0, tm * BM);
       } else {
@@ -82,10 +128,11 @@ __device__ __forceinline__ void run_producer(const CUtensorMap* tmA, const CUten
         for (int j = 0; j < BM / 64; ++j) tma_load_2d(a + j * 8192, tmA, &sh.full[stage], tm * BM + j * 64, k0);
       }
       if constexpr (!B_MN) {
-        tma_load_2d(b, tmB, &sh.full[stage], k0, tn * BN);
+        tma_load_2d(b, tmB, &sh.full[stage], k0, bgo + tn * BN);
       } else {
 #pragma unroll
-        for (int j = 0; j < BN / 64; ++j) tma_load_2d(b + j * 8192, tmB, &sh.full[stage], tn * BN + j * 64, k0);
+        for (int j = 0; j < BN / 64; ++j)
+          tma_load_2d(b + j * 8192, tmB, &sh.full[stage], tn * BN + j * 64, bgo + k0);
       }
       if (++stage == STAGES) {
         stage = 0;
@@ -109,14 +156,17 @@ __device__ __forceinline__ void run_mma(const Params& p, Shared& sh, uint8_t* sA
   int stage = 0;
   uint32_t phase = 0;
   int it = 0;
-  const int tiles = p.num_m * p.num_n;
-  for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+  const int tiles = total_tiles(p);
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const TileInfo ti = tile_info(t, p);
+    if (!ti.valid || ti.nk == 0) continue;  // the epilogue skips / zero-fills these too
     const int acc = it & 1;
     const uint32_t acc_phase = (it >> 1) & 1;
+    ++it;
     if (!mbar_wait(&sh.tempty[acc], acc_phase ^ 1, &sh.abort_flag, &g_err, 3)) return;
     tc_fence_after();
     const uint32_t d_tmem = sh.tmem_base + acc * BN;
-    for (int kb = 0; kb < p.num_k; ++kb) {
+    for (int kb = 0; kb < ti.nk; ++kb) {
       if (!mbar_wait(&sh.full[stage], phase, &sh.abort_flag, &g_err, 4)) return;
       tc_fence_after();
       const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
@@ -140,17 +190,25 @@ __device__ __forceinline__ void run_mma(const Params& p, Shared& sh, uint8_t* sA
 __device__ __forceinline__ void run_epilogue(const Params& p, Shared& sh, int warp, int lane) {
   const int q = warp & 3;  // TMEM lane quarter this warp may access
   int it = 0;
-  const int tiles = p.num_m * p.num_n;
+  const int tiles = total_tiles(p);
   const bool vec_ok = (p.ldd % 8) == 0;
-  for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const TileInfo ti = tile_info(t, p);
+    if (!ti.valid) continue;
+    const int tm = ti.tm, tn = ti.tn;
+    const int row = tm * BM + q * 32 + lane;
+    __nv_bfloat16* dbase = p.D + (p.mode == 2 ? ti.g * p.d_group_stride : 0ll);
+    __nv_bfloat16* drow = dbase + static_cast<size_t>(row) * p.ldd;
+    if (ti.nk == 0) {  // empty group: its slice of D is zero
+      if (row < p.M)
+        for (int col = tn * BN; col < min(p.N, tn * BN + BN); ++col) drow[col] = __float2bfloat16(0.f);
+      continue;
+    }
     const int acc = it & 1;
     const uint32_t acc_phase = (it >> 1) & 1;
-    int tm, tn;
-    tile_coords(t, p, tm, tn);
+    ++it;
     if (!mbar_wait(&sh.tfull[acc], acc_phase, &sh.abort_flag, &g_err, 5)) return;
     tc_fence_after();
-    const int row = tm * BM + q * 32 + lane;
-    __nv_bfloat16* drow = p.D + static_cast<size_t>(row) * p.ldd;
 #pragma unroll 1
     for (int c = 0; c < BN / 32; ++c) {
       uint32_t r[32];
@@ -241,8 +299,9 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, cudaS
     check_cuda(cudaGetDevice(&dev), "gemm dev");
     sms = num_sms(dev);
   }
-  const int tiles = p.num_m * p.num_n;
+  const int tiles = p.num_m * p.num_n * (p.mode == 2 ? p.num_groups : 1);
   const int grid = tiles < sms ? tiles : sms;
+  if (grid == 0) return;
   k<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
   check_cuda(cudaGetLastError(), "gemm launch");
 }
@@ -271,6 +330,45 @@ void gemm_bf16(const void* A, const void* B, void* D, int64_t M, int64_t N, int6
   p.num_k = (int)((K + BK - 1) / BK);
   p.D = reinterpret_cast<__nv_bfloat16*>(D);
   p.ldd = (int)N;
+  p.mode = 0;
+  p.num_groups = 1;
+  p.tile_group = p.group_kstart = p.group_klen = nullptr;
+  p.b_group_rows = 0;
+  p.d_group_stride = 0;
+  if (!a_mn && !b_mn) launch<false, false>(ta, tb, p, stream);
+  else if (!a_mn && b_mn) launch<false, true>(ta, tb, p, stream);
+  else if (a_mn && !b_mn) launch<true, false>(ta, tb, p, stream);
+  else launch<true, true>(ta, tb, p, stream);
+}
+
+void gemm_bf16_grouped(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K, bool a_mn,
+                       bool b_mn, int mode, int num_groups, const int* tile_group, const int* kstart,
+                       const int* klen, int64_t b_total_rows, int b_group_rows, cudaStream_t stream) {
+  using namespace gemm_impl;
+  if (M == 0 || N == 0 || num_groups == 0) return;
+  if ((a_mn ? M : K) % 8 != 0 || (b_mn ? N : K) % 8 != 0)
+    throw std::runtime_error("grouped gemm: contiguous dimension of each operand must be a multiple of 8");
+  // mode 1: A is [M, K] (or [K, M]) over all padded rows; B holds num_groups stacked matrices
+  // mode 2: A is [Ktot, M], B is [Ktot, N] (both M/N-major); D is [num_groups, M, N]
+  const CUtensorMap ta = a_mn ? make_tmap_bf16_2d(A, K, M, M, 64, 64) : make_tmap_bf16_2d(A, M, K, K, BM, 64);
+  const CUtensorMap tb = b_mn ? make_tmap_bf16_2d(B, b_total_rows, N, N, 64, 64)
+                              : make_tmap_bf16_2d(B, b_total_rows, K, K, BN, 64);
+  Params p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.num_m = (int)((M + BM - 1) / BM);
+  p.num_n = (int)((N + BN - 1) / BN);
+  p.num_k = (int)((K + BK - 1) / BK);
+  p.D = reinterpret_cast<__nv_bfloat16*>(D);
+  p.ldd = (int)N;
+  p.mode = mode;
+  p.num_groups = num_groups;
+  p.tile_group = tile_group;
+  p.group_kstart = kstart;
+  p.group_klen = klen;
+  p.b_group_rows = b_group_rows;
+  p.d_group_stride = (long long)M * N;
   if (!a_mn && !b_mn) launch<false, false>(ta, tb, p, stream);
   else if (!a_mn && b_mn) launch<false, true>(ta, tb, p, stream);
   else if (a_mn && !b_mn) launch<true, false>(ta, tb, p, stream);

@@ -46,7 +46,7 @@ def build_args(size: str, *, num_experts: int | None = None, attn_res_blocks: in
     if size == "debugmodel":
         return KimiLinearModelArgs(vocab_size=2048, hidden_size=256, num_hidden_layers=4, intermediate_size=512,
                                    num_attention_heads=4, kv_lora_rank=64, qk_nope_head_dim=64,
-                                   qk_rope_head_dim=64, v_head_dim=64, kda_num_heads=4, kda_head_dim=64,
+                                   qk_rope_head_dim=64, v_head_dim=128, kda_num_heads=4, kda_head_dim=64,
                                    kda_layers=[1, 2, 3], full_attn_layers=[4], num_experts=8,
                                    num_experts_per_token=2, moe_intermediate_size=128, use_grouped_topk=False,
                                    tie_word_embeddings=False, attn_res_blocks=attn_res_blocks)

@@ -45,9 +45,27 @@ class _Attn(torch.autograd.Function):
         return dq, dk, dv, None, None
 
 
+_SUPPORTED = ((64, 64), (128, 128), (192, 128))
+
+
+def _padded_dims(dqk: int, dv: int) -> tuple[int, int]:
+    for a, b in _SUPPORTED:
+        if dqk <= a and dv <= b:
+            return a, b
+    raise ValueError(f"attention head dims ({dqk}, {dv}) exceed the supported maximum (192, 128)")
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
               scale: float | None = None) -> torch.Tensor:
     scale = float(scale if scale is not None else 1.0 / math.sqrt(q.shape[-1]))
     if not q.is_cuda:
         return _ref.attention(q, k, v, causal, scale)
+    dqk, dv = q.shape[-1], v.shape[-1]
+    pq, pv = _padded_dims(dqk, dv)
+    if (pq, pv) != (dqk, dv):
+        # zero-padding q/k leaves every dot product unchanged; extra v columns are dropped
+        F = torch.nn.functional
+        q, k = F.pad(q, (0, pq - dqk)), F.pad(k, (0, pq - dqk))
+        v = F.pad(v, (0, pv - dv))
+        return _Attn.apply(q, k, v, causal, scale)[..., :dv]
     return _Attn.apply(q, k, v, causal, scale)

@@ -1,0 +1,80 @@
+"""Grouped SwiGLU experts on the grouped tcgen05 GEMM.
+
+Rows arrive sorted by expert with ``counts[e]`` rows each.  They are copied
+into a padded buffer where expert e's rows start at a multiple of 128 (the
+GEMM's M tile), so every 128-row tile belongs to exactly one expert and every
+expert's K range (for the weight gradient) is 128-aligned.  The layout is
+computed on the device from ``counts`` with a fixed upper bound on the padded
+size (rows + 127 * E), so no device-to-host synchronisation is needed.
+
+  forward:  h1 = X W1[e]^T, h3 = X W3[e]^T, a = silu(h1) h3, Y = a W2[e]^T   (grouped rows)
+  backward: da = dY W2[e],  dh1, dh3 = swiglu'(da),  dX = dh1 W1[e] + dh3 W3[e]
+            dW2[e] = dY_e^T a_e,  dW1[e] = dh1_e^T X_e,  dW3[e] = dh3_e^T X_e    (grouped K)
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _ext
+
+TILE = 128
+
+
+def padded_layout(counts: torch.Tensor, n_rows: int):
+    """Returns (dest [n_rows] padded row of each input row, tile_group [P/128] int32,
+    kstart [E] int32, klen [E] int32, P)."""
+    E = counts.numel()
+    counts = counts.to(torch.int64)
+    padded = (counts + TILE - 1) // TILE * TILE
+    pend = torch.cumsum(padded, 0)
+    pstart = pend - padded
+    start = torch.cumsum(counts, 0) - counts
+    P = ((n_rows + (TILE - 1) * E) + TILE - 1) // TILE * TILE
+    expert_of_row = torch.repeat_interleave(torch.arange(E, device=counts.device), counts, output_size=n_rows)
+    dest = pstart[expert_of_row] + (torch.arange(n_rows, device=counts.device) - start[expert_of_row])
+    tile_start = torch.arange(P // TILE, device=counts.device) * TILE
+    g = torch.searchsorted(pend, tile_start, right=True)
+    tile_group = torch.where(tile_start < pend[-1], g, torch.full_like(g, -1)).to(torch.int32)
+    return dest, tile_group, pstart.to(torch.int32), padded.to(torch.int32), P
+
+
+class _GroupedSwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w1, w2, w3, counts):
+        ext = _ext.ext()
+        E, H, D = w1.shape
+        n = x.shape[0]
+        dest, tg, kst, kln, P = padded_layout(counts, n)
+        xp = x.new_zeros(P, D)
+        xp[dest] = x
+        w1f, w3f, w2f = w1.reshape(E * H, D), w3.reshape(E * H, D), w2.reshape(E * D, H)
+        h1 = ext.gemm_grouped_rows(xp, w1f, tg, H, H, False)
+        h3 = ext.gemm_grouped_rows(xp, w3f, tg, H, H, False)
+        a = ext.swiglu_fwd(h1, h3)
+        yp = ext.gemm_grouped_rows(a, w2f, tg, D, D, False)
+        ctx.save_for_backward(xp, h1, h3, a, w1, w2, w3, dest, tg, kst, kln)
+        return yp[dest]
+
+    @staticmethod
+    def backward(ctx, dy):
+        ext = _ext.ext()
+        xp, h1, h3, a, w1, w2, w3, dest, tg, kst, kln = ctx.saved_tensors
+        E, H, D = w1.shape
+        P = xp.shape[0]
+        dyp = dy.new_zeros(P, D)
+        dyp[dest] = dy.contiguous()
+        # dgrad through w2: B = W2[e] read as [D(red), H(out)] rows of the stacked [E*D, H]
+        da = ext.gemm_grouped_rows(dyp, w2.reshape(E * D, H), tg, H, D, True)
+        dh1, dh3 = ext.swiglu_bwd(da, h1, h3)
+        dx = ext.gemm_grouped_rows(dh1, w1.reshape(E * H, D), tg, D, H, True)
+        dx = dx + ext.gemm_grouped_rows(dh3, w3.reshape(E * H, D), tg, D, H, True)
+        dw2 = ext.gemm_grouped_k(dyp, a, kst, kln)    # [E, D, H]
+        dw1 = ext.gemm_grouped_k(dh1, xp, kst, kln)   # [E, H, D]
+        dw3 = ext.gemm_grouped_k(dh3, xp, kst, kln)
+        return dx[dest], dw1.to(w1.dtype), dw2.to(w2.dtype), dw3.to(w3.dtype), None
+
+
+def grouped_swiglu_cuda(x, w1, w2, w3, counts):
+    dt = torch.bfloat16
+    return _GroupedSwiGLU.apply(x.to(dt).contiguous(), w1.to(dt).contiguous(), w2.to(dt).contiguous(),
+                                w3.to(dt).contiguous(), counts)
