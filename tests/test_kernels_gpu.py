@@ -238,3 +238,14 @@ def test_attention_padded_head_dims():
     o.sum().backward()
     ref = _attn_ref(q.detach(), k.detach(), v.detach(), True, 111 ** -0.5)
     assert o.shape == (1, 128, 2, 74) and _rel(o, ref) < 2e-2 and q.grad.shape == q.shape
+
+
+def test_linear_unaligned_dims():
+    from torchtitan_b200 import ops
+
+    x = torch.randn(64, 250, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(3, 250, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = ops.linear(x, w)
+    y.sum().backward()
+    assert y.shape == (64, 3) and _rel(y, x.float() @ w.float().t()) < 1e-2
+    assert w.grad.shape == w.shape and x.grad.shape == x.shape

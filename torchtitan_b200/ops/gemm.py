@@ -68,6 +68,13 @@ def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         return torch.nn.functional.linear(x, w)
     if x.dtype != w.dtype:
         x = x.to(w.dtype)
+    n, k = w.shape
+    pn, pk = (-n) % 8, (-k) % 8
+    if pn or pk:
+        # TMA rows must be 16-byte multiples: zero-pad the feature dims (exact) and slice
+        F = torch.nn.functional
+        y = _Linear.apply(F.pad(x, (0, pk)) if pk else x, F.pad(w, (0, pk, 0, pn)))
+        return y[..., :n] if pn else y
     return _Linear.apply(x, w)
 
 
