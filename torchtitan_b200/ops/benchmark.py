@@ -156,6 +156,27 @@ def attn_large(ext, out):
     print(json.dumps(out[-1]), flush=True)
 
 
+def mem_small(ext, out):
+    """One launch each of the memory-bound kernels on >L2-sized inputs (for ncu)."""
+    T, Dm, V = 8192, 4096, 32768
+    x = torch.randn(T, Dm, device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(Dm, device="cuda", dtype=torch.bfloat16)
+    y, rstd = ext.rmsnorm_fwd(x, w, 1e-5)
+    ext.rmsnorm_bwd(x, x, w, rstd)
+    a = torch.randn(T, 14336, device="cuda", dtype=torch.bfloat16)
+    ext.swiglu_fwd(a, a)
+    logits = torch.randn(T, V, device="cuda", dtype=torch.bfloat16)
+    labels = torch.randint(0, V, (T,), device="cuda")
+    loss, lse = ext.ce_fwd(logits, labels, -100)
+    ext.ce_bwd(logits, labels, lse, torch.ones(1, device="cuda"), -100)
+    n = 64 * 1024 * 1024
+    p_, g_, m_, v_ = (torch.randn(n, device="cuda") for _ in range(4))
+    ext.adamw([p_], [g_], [m_], [v_.abs()], 1e-3, 0.9, 0.95, 1e-8, 0.1, 1)
+    torch.cuda.synchronize()
+    out.append({"mem_small": "ok"})
+    print(json.dumps(out[-1]), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,mem")
@@ -172,6 +193,8 @@ def main():
         bench_attn(ext, out)
     if "attn_large" in sel:
         attn_large(ext, out)
+    if "mem_small" in sel:
+        mem_small(ext, out)
     if "small" in sel:
         small_cases(ext, out)
     if "mem" in sel:
