@@ -249,3 +249,19 @@ def test_linear_unaligned_dims():
     y.sum().backward()
     assert y.shape == (64, 3) and _rel(y, x.float() @ w.float().t()) < 1e-2
     assert w.grad.shape == w.shape and x.grad.shape == x.shape
+
+
+def test_adamw_master_with_bf16_copy():
+    from torchtitan_b200 import ops
+    from torchtitan_b200.ops import reference as R
+
+    torch.manual_seed(12)
+    p = torch.randn(4096 + 4, device="cuda")
+    g = torch.randn_like(p).bfloat16()
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    copy = torch.empty_like(p, dtype=torch.bfloat16)
+    rp, rm, rv = p.clone(), m.clone(), v.clone()
+    kw = dict(lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, step=1)
+    ops.fused_adamw_([p], [g], [m], [v], copies=[copy], **kw)
+    R.adamw_([rp], [g.float()], [rm], [rv], **kw)
+    assert _rel(p, rp) < 1e-5 and _rel(copy, rp) < 1e-2

@@ -44,12 +44,26 @@ class ModelWrapper(Stateful):
     def state_dict(self) -> dict[str, Any]:
         out: dict[str, Any] = {}
         for m in self.model:
-            out.update(get_model_state_dict(m))
+            sd = get_model_state_dict(m)
+            # single-replica mixed precision: save the fp32 masters, not the bf16 compute weights
+            masters = {n.replace("_checkpoint_wrapped_module.", ""): p._master
+                       for n, p in m.named_parameters() if hasattr(p, "_master")}
+            out.update({k: masters.get(k, v) for k, v in sd.items()})
         return out
 
     def load_state_dict(self, sd: dict[str, Any]) -> None:
         for m in self.model:
-            set_model_state_dict(m, sd, options=StateDictOptions(strict=False))
+            named = {n.replace("_checkpoint_wrapped_module.", ""): p for n, p in m.named_parameters()}
+            with torch.no_grad():
+                rest = {}
+                for k, v in sd.items():
+                    p = named.get(k)
+                    if p is not None and hasattr(p, "_master"):
+                        p._master.copy_(v)
+                        p.data.copy_(p._master)
+                    else:
+                        rest[k] = v
+            set_model_state_dict(m, rest, options=StateDictOptions(strict=False))
 
 
 def _is_rank0() -> bool:

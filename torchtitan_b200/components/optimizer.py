@@ -58,17 +58,25 @@ class AdamW(torch.optim.Optimizer):
     def step(self, closure=None):
         loss = closure() if closure is not None else None
         for group in self.param_groups:
-            ps, gs, ms, vs, steps = [], [], [], [], []
+            ps, gs, ms, vs, steps, copies = [], [], [], [], [], []
             for p in group["params"]:
                 if p.grad is None:
                     continue
                 st = self.state[p]
+                master = getattr(p, "_master", None)
                 if not st:
                     st["step"] = torch.zeros((), dtype=torch.float32)
-                    st["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
-                    st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                    ref = master if master is not None else p
+                    st["exp_avg"] = torch.zeros_like(ref, memory_format=torch.preserve_format)
+                    st["exp_avg_sq"] = torch.zeros_like(ref, memory_format=torch.preserve_format)
+                    if master is not None:
+                        st["master"] = master  # saved with the optimizer state
                 st["step"] += 1
-                ps.append(_local(p)); gs.append(_local(p.grad))
+                if master is not None:
+                    ps.append(master); copies.append(p.data)
+                else:
+                    ps.append(_local(p)); copies.append(None)
+                gs.append(_local(p.grad))
                 ms.append(_local(st["exp_avg"])); vs.append(_local(st["exp_avg_sq"]))
                 steps.append(int(st["step"].item()))
             if not ps:
@@ -78,8 +86,21 @@ class AdamW(torch.optim.Optimizer):
             lr = float(lr.item()) if torch.is_tensor(lr) else float(lr)
             # all params of a group advance together, so a single step count is used
             ops.fused_adamw_(ps, gs, ms, vs, lr=lr, beta1=b1, beta2=b2, eps=group["eps"],
-                             weight_decay=group["weight_decay"], step=steps[0])
+                             weight_decay=group["weight_decay"], step=steps[0],
+                             copies=copies if any(c is not None for c in copies) else None)
         return loss
+
+    def load_state_dict(self, state_dict):
+        super().load_state_dict(state_dict)
+        # masters restored from a checkpoint drive the compute weights
+        with torch.no_grad():
+            for group in self.param_groups:
+                for p in group["params"]:
+                    m = self.state.get(p, {}).get("master")
+                    if m is not None and hasattr(p, "_master"):
+                        p._master.copy_(m)
+                        self.state[p]["master"] = p._master
+                        p.data.copy_(p._master)
 
 
 def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
@@ -138,35 +159,45 @@ class Muon(torch.optim.Optimizer):
             lr, wd = float(group["lr"]), group["weight_decay"]
             if not group["use_muon"]:
                 ps, gs, ms, vs = [], [], [], []
+                copies = []
                 for p in params:
                     st = self.state[p]
+                    master = getattr(p, "_master", None)
+                    ref = master if master is not None else p
                     if not st:
                         st["step"] = torch.zeros(())
-                        st["exp_avg"] = torch.zeros_like(p)
-                        st["exp_avg_sq"] = torch.zeros_like(p)
+                        st["exp_avg"] = torch.zeros_like(ref)
+                        st["exp_avg_sq"] = torch.zeros_like(ref)
                     st["step"] += 1
-                    ps.append(_local(p)); gs.append(_local(p.grad))
+                    ps.append(master if master is not None else _local(p))
+                    copies.append(p.data if master is not None else None)
+                    gs.append(_local(p.grad))
                     ms.append(_local(st["exp_avg"])); vs.append(_local(st["exp_avg_sq"]))
                 b1, b2 = group["betas"]
                 ops.fused_adamw_(ps, gs, ms, vs, lr=lr, beta1=b1, beta2=b2, eps=group["eps"], weight_decay=wd,
-                                 step=int(self.state[params[0]]["step"].item()))
+                                 step=int(self.state[params[0]]["step"].item()),
+                                 copies=copies if any(c is not None for c in copies) else None)
                 continue
             mom = group["momentum"]
             items = []
             for p in params:
                 st = self.state[p]
                 if "momentum_buffer" not in st:
-                    st["momentum_buffer"] = torch.zeros_like(p)
+                    st["momentum_buffer"] = torch.zeros_like(getattr(p, "_master", p))
                 buf = st["momentum_buffer"]
-                buf.mul_(mom).add_(p.grad)
-                upd = p.grad.add(buf, alpha=mom) if group["nesterov"] else buf
+                grad = p.grad.to(buf.dtype)
+                buf.mul_(mom).add_(grad)
+                upd = grad.add(buf, alpha=mom) if group["nesterov"] else buf
                 items.append((p, upd))
             updates = self._orthogonalize_all(items, group["ns_steps"])
             for (p, _), u in zip(items, updates):
-                pl = _local(p)
+                master = getattr(p, "_master", None)
+                pl = master if master is not None else _local(p)
                 if wd:
                     pl.mul_(1 - lr * wd)
                 pl.add_(u.to(pl.dtype), alpha=-lr * _muon_scale(p.shape))
+                if master is not None:
+                    p.data.copy_(master)
         return loss
 
 

@@ -29,6 +29,7 @@ struct Chunk {
   int8_t p_bf16;
   int8_t g_bf16;
   int8_t vec4;  // every pointer 16-byte aligned and n % 4 == 0: float4 path
+  __nv_bfloat16* p_copy;  // optional bf16 copy written with the updated fp32 param
 };
 
 struct Table {
@@ -52,7 +53,34 @@ __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table
   const Chunk c = t.c[blockIdx.x];
   const float step_size = lr / bc1;
   const float decay = 1.f - lr * wd;
-  if (c.vec4 && !c.p_bf16 && !c.g_bf16) {
+  if (c.vec4 && !c.p_bf16 && c.g_bf16) {
+    // fp32 master, bf16 grad (and optionally a bf16 compute copy): vector loads and stores
+    float4* p4 = static_cast<float4*>(c.p);
+    const uint2* g4 = static_cast<const uint2*>(c.g);
+    float4* m4 = reinterpret_cast<float4*>(c.m);
+    float4* v4 = reinterpret_cast<float4*>(c.v);
+    uint2* c4 = reinterpret_cast<uint2*>(c.p_copy);
+    const int n4 = c.n / 4;
+    for (int i = threadIdx.x; i < n4; i += NT) {
+      float4 p = p4[i], m = m4[i], v = v4[i];
+      const uint2 gr = g4[i];
+      const float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.x));
+      const float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.y));
+      adam_update(p.x, g01.x, m.x, v.x, b1, b2, eps, decay, step_size, bc2_sqrt);
+      adam_update(p.y, g01.y, m.y, v.y, b1, b2, eps, decay, step_size, bc2_sqrt);
+      adam_update(p.z, g23.x, m.z, v.z, b1, b2, eps, decay, step_size, bc2_sqrt);
+      adam_update(p.w, g23.y, m.w, v.w, b1, b2, eps, decay, step_size, bc2_sqrt);
+      p4[i] = p;
+      m4[i] = m;
+      v4[i] = v;
+      if (c4) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
+        c4[i] = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+      }
+    }
+    return;
+  }
+  if (c.vec4 && !c.p_bf16 && !c.g_bf16 && !c.p_copy) {
     // fp32 master / fp32 grad: 16-byte loads and stores of all four streams
     float4* p4 = static_cast<float4*>(c.p);
     const float4* g4 = static_cast<const float4*>(c.g);
@@ -80,6 +108,7 @@ __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table
     c.v[i] = v;
     if (c.p_bf16) static_cast<__nv_bfloat16*>(c.p)[i] = __float2bfloat16(pv);
     else static_cast<float*>(c.p)[i] = pv;
+    if (c.p_copy) c.p_copy[i] = __float2bfloat16(pv);
   }
 }
 
@@ -188,9 +217,11 @@ void adamw_multi(const AdamWTensor* list, int count, float lr, float beta1, floa
       c.n = static_cast<int>(t.n - off < CHUNK ? t.n - off : CHUNK);
       c.p_bf16 = static_cast<int8_t>(t.p_dtype);
       c.g_bf16 = static_cast<int8_t>(t.g_dtype);
-      c.vec4 = static_cast<int8_t>(((reinterpret_cast<uintptr_t>(c.p) | reinterpret_cast<uintptr_t>(c.g) |
-                                     reinterpret_cast<uintptr_t>(c.m) | reinterpret_cast<uintptr_t>(c.v)) & 15) == 0 &&
-                                   c.n % 4 == 0);
+      c.p_copy = t.p_copy ? static_cast<__nv_bfloat16*>(t.p_copy) + off : nullptr;
+      c.vec4 = static_cast<int8_t>(((reinterpret_cast<uintptr_t>(c.p) | reinterpret_cast<uintptr_t>(c.m) |
+                                     reinterpret_cast<uintptr_t>(c.v)) & 15) == 0 &&
+                                   (reinterpret_cast<uintptr_t>(c.g) & (t.g_dtype ? 7 : 15)) == 0 &&
+                                   (reinterpret_cast<uintptr_t>(c.p_copy) & 7) == 0 && c.n % 4 == 0);
       if (++nc == MAX_CHUNKS) flush();
     }
   }

@@ -155,7 +155,8 @@ Tensor ce_bwd(Tensor logits, Tensor labels, Tensor lse, Tensor gscale, int64_t i
 }
 
 void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Tensor> ms, std::vector<Tensor> vs,
-           double lr, double b1, double b2, double eps, double wd, int64_t step) {
+           double lr, double b1, double b2, double eps, double wd, int64_t step, std::vector<Tensor> copies) {
+  TORCH_CHECK(copies.empty() || copies.size() == params.size(), "adamw: copies must be empty or match params");
   TORCH_CHECK(params.size() == grads.size() && params.size() == ms.size() && params.size() == vs.size(),
               "adamw: list lengths differ");
   if (params.empty()) return;
@@ -170,8 +171,15 @@ void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Te
     TORCH_CHECK(p.numel() == gr.numel() && p.numel() == m.numel() && p.numel() == v.numel(), "adamw: numel mismatch");
     TORCH_CHECK(p.scalar_type() == at::kFloat || p.scalar_type() == at::kBFloat16, "adamw: param fp32/bf16");
     TORCH_CHECK(gr.scalar_type() == at::kFloat || gr.scalar_type() == at::kBFloat16, "adamw: grad fp32/bf16");
+    void* cp = nullptr;
+    if (!copies.empty() && copies[i].defined() && copies[i].numel() > 0) {
+      TORCH_CHECK(copies[i].scalar_type() == at::kBFloat16 && copies[i].is_contiguous() &&
+                      copies[i].numel() == p.numel() && p.scalar_type() == at::kFloat,
+                  "adamw: a copy must be a contiguous bf16 tensor of an fp32 param");
+      cp = copies[i].data_ptr();
+    }
     list.push_back({p.data_ptr(), gr.data_ptr(), m.data_ptr<float>(), v.data_ptr<float>(), p.numel(),
-                    p.scalar_type() == at::kBFloat16 ? 1 : 0, gr.scalar_type() == at::kBFloat16 ? 1 : 0});
+                    p.scalar_type() == at::kBFloat16 ? 1 : 0, gr.scalar_type() == at::kBFloat16 ? 1 : 0, cp});
   }
   ttb::adamw_multi(list.data(), static_cast<int>(list.size()), static_cast<float>(lr), static_cast<float>(b1),
                    static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd), static_cast<int>(step),
@@ -259,7 +267,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("ce_fwd", &ce_fwd);
   m.def("ce_bwd", &ce_bwd);
-  m.def("adamw", &adamw);
+  m.def("adamw", &adamw, py::arg("params"), py::arg("grads"), py::arg("exp_avgs"), py::arg("exp_avg_sqs"),
+        py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("weight_decay"), py::arg("step"),
+        py::arg("copies") = std::vector<Tensor>());
   m.def("multi_sumsq", &multi_sumsq, "sum of squares over a list of fp32/bf16 tensors");
   m.def("multi_clip_scale", &multi_clip_scale, "scale tensors by min(1, max_norm/(sqrt(total)+1e-6))");
   m.def("attn_fwd", &attn_fwd);

@@ -59,6 +59,7 @@ struct AdamWTensor {
   int64_t n;
   int p_dtype;  // 0 fp32, 1 bf16
   int g_dtype;
+  void* p_copy = nullptr;  // optional bf16 copy of the updated fp32 param (compute weights)
 };
 void adamw_multi(const AdamWTensor* host_list, int count, float lr, float beta1, float beta2, float eps, float wd,
                  int step, cudaStream_t s);

@@ -18,7 +18,11 @@ from torchtitan_b200.config import TORCH_DTYPE_MAP
 from torchtitan_b200.parallel.activation_checkpoint import apply_ac
 from torchtitan_b200.parallel.context_parallel import ulysses_hook
 from torchtitan_b200.parallel.expert_parallel import apply_ep
-from torchtitan_b200.parallel.fsdp import apply_fsdp
+from torchtitan_b200.parallel.fsdp import (
+    apply_fsdp,
+    apply_replica_mixed_precision,
+    replica_mixed_precision_applicable,
+)
 from torchtitan_b200.utils.logging import logger
 
 
@@ -46,6 +50,8 @@ def parallelize_kimi(model: nn.Module, *, parallel_dims: Any, training: Any, par
         logger.info(f"applied expert parallel (ep={pd.ep}) to {len(moes)} MoE layers")
     if ac_config.mode != "none":
         apply_ac(model, ac_config)
+    if replica_mixed_precision_applicable(pd, training):
+        return apply_replica_mixed_precision(model)
     names = ["dp_replicate", "fsdp"] if pd.dp_replicate_enabled else "fsdp"
     apply_fsdp(model, pd.get_mesh(names), param_dtype=TORCH_DTYPE_MAP[training.mixed_precision_param],
                reduce_dtype=TORCH_DTYPE_MAP[training.mixed_precision_reduce], pp_enabled=pd.pp_enabled,

@@ -9,7 +9,11 @@ import torch.nn as nn
 from torchtitan_b200.config import TORCH_DTYPE_MAP
 from torchtitan_b200.parallel.activation_checkpoint import apply_ac
 from torchtitan_b200.parallel.context_parallel import apply_cp_to_attention_modules
-from torchtitan_b200.parallel.fsdp import apply_fsdp
+from torchtitan_b200.parallel.fsdp import (
+    apply_fsdp,
+    apply_replica_mixed_precision,
+    replica_mixed_precision_applicable,
+)
 from torchtitan_b200.parallel.tensor_parallel import apply_tp_llama, maybe_enable_async_tp
 from torchtitan_b200.utils.logging import logger
 
@@ -33,7 +37,10 @@ def parallelize_llama(model: nn.Module, *, parallel_dims: Any, training: Any, mo
     if ac_config.mode != "none":
         apply_ac(model, ac_config)
         logger.info(f"applied {ac_config.mode} activation checkpointing")
-    if parallel_dims.fsdp_enabled or parallel_dims.dp_enabled or True:
+    if replica_mixed_precision_applicable(parallel_dims, training):
+        apply_replica_mixed_precision(model)
+        logger.info("single replica: bf16 compute weights with fp32 masters in the optimizer (no FSDP wrap)")
+    else:
         names = ["dp_replicate", "fsdp"] if parallel_dims.dp_replicate_enabled else ["fsdp"]
         dp_mesh = parallel_dims.get_mesh(names if len(names) > 1 else names[0])
         apply_fsdp(model, dp_mesh, param_dtype=TORCH_DTYPE_MAP[training.mixed_precision_param],

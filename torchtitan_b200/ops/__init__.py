@@ -129,11 +129,17 @@ from .moe import grouped_swiglu  # noqa: E402
 
 # -------------------------------------------------------------------------- AdamW
 def fused_adamw_(params, grads, exp_avgs, exp_avg_sqs, *, lr: float, beta1: float, beta2: float,
-                 eps: float, weight_decay: float, step: int) -> None:
+                 eps: float, weight_decay: float, step: int, copies=None) -> None:
+    """``copies``: optional bf16 tensors receiving the updated fp32 params (compute weights)."""
     if not params:
         return
     if not params[0].is_cuda:
-        return _ref.adamw_(params, grads, exp_avgs, exp_avg_sqs, lr=lr, beta1=beta1, beta2=beta2, eps=eps,
-                           weight_decay=weight_decay, step=step)
+        _ref.adamw_(params, grads, exp_avgs, exp_avg_sqs, lr=lr, beta1=beta1, beta2=beta2, eps=eps,
+                    weight_decay=weight_decay, step=step)
+        for p, c in zip(params, copies or []):
+            if c is not None:
+                c.copy_(p)
+        return
+    cp = [c if c is not None else torch.empty(0, device=params[0].device) for c in (copies or [])]
     ext().adamw(list(params), list(grads), list(exp_avgs), list(exp_avg_sqs), float(lr), float(beta1),
-                float(beta2), float(eps), float(weight_decay), int(step))
+                float(beta2), float(eps), float(weight_decay), int(step), cp)

@@ -74,3 +74,35 @@ def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, redu
 def apply_ddp(model: nn.Module, dp_mesh: Any) -> nn.Module:
     """Pure data parallel: replicate via FSDP2 on the replicate mesh."""
     return apply_fsdp(model, dp_mesh, param_dtype=torch.bfloat16, reduce_dtype=torch.float32)
+
+
+def replica_mixed_precision_applicable(parallel_dims, training) -> bool:
+    """One data-parallel rank and nothing to shard: FSDP2 would only add cast/copy traffic."""
+    return (torch.cuda.is_available() and parallel_dims.world_size == 1 and not parallel_dims.pp_enabled
+            and training.mixed_precision_param == "bfloat16" and training.dtype == "float32"
+            and not training.enable_cpu_offload)
+
+
+def apply_replica_mixed_precision(model: nn.Module) -> nn.Module:
+    """Mark ``model`` for single-replica mixed precision: after weight init the
+    trainer calls ``materialize_replica_mixed_precision`` which keeps an fp32
+    master copy of every parameter (``param._master``) and turns the parameter
+    itself into the bf16 compute weight.  The fused AdamW updates the master
+    and rewrites the bf16 weight in the same kernel pass."""
+    model._replica_param_dtype = torch.bfloat16
+    return model
+
+
+@torch.no_grad()
+def materialize_replica_mixed_precision(model: nn.Module) -> None:
+    dt = getattr(model, "_replica_param_dtype", None)
+    if dt is None:
+        return
+    seen = set()
+    for p in model.parameters():
+        if id(p) in seen or p.dtype != torch.float32:
+            continue
+        seen.add(id(p))
+        master = p.data.clone()
+        p.data = p.data.to(dt)
+        p._master = master

@@ -169,6 +169,9 @@ class Trainer(Stateful, Configurable):
             model.to_empty(device=init_device)
             with torch.no_grad():
                 model.init_weights(buffer_device=None)
+            from torchtitan_b200.parallel.fsdp import materialize_replica_mixed_precision
+
+            materialize_replica_mixed_precision(model)
             model.train()
             self.model_parts = [model]
             self.pp_has_first_stage = self.pp_has_last_stage = True
