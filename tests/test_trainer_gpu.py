@@ -22,7 +22,7 @@ def test_replica_mixed_precision_and_checkpoint(tmp_path):
     assert 5.0 < loss < 9.0
     master = w._master.clone()
     t.close()
-    t2 = Trainer(ConfigManager().parse_args(args[:4] + ["5"] + args[5:]))
+    t2 = Trainer(ConfigManager().parse_args(args[:5] + ["5"] + args[6:]))
     t2.checkpointer.load()
     w2 = t2.model_parts[0].layers["0"]._checkpoint_wrapped_module.attention.wq.weight
     assert t2.step == 3 and torch.equal(w2._master, master) and torch.equal(w2.data, master.bfloat16())
