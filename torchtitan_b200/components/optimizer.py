@@ -47,6 +47,14 @@ def _local(t: torch.Tensor) -> torch.Tensor:
     return t.to_local() if isinstance(t, DTensor) else t
 
 
+def _keep_fp32_state(param, value, param_id, param_groups, key=None):
+    """State of parameters with an fp32 master stays fp32 on load (torch casts to
+    the parameter's dtype, which here is the bf16 compute weight)."""
+    if key != "step" and torch.is_tensor(value) and hasattr(param, "_master"):
+        return value.to(device=param.device)
+    return torch.optim.Optimizer._process_value_according_to_param_policy(param, value, param_id, param_groups, key)
+
+
 class AdamW(torch.optim.Optimizer):
     """AdamW with decoupled weight decay.  ``fused=True`` on CUDA runs one
     multi-tensor kernel per (dtype, device) group and step."""
@@ -90,6 +98,8 @@ class AdamW(torch.optim.Optimizer):
                              copies=copies if any(c is not None for c in copies) else None)
         return loss
 
+    _process_value_according_to_param_policy = staticmethod(_keep_fp32_state)
+
     def load_state_dict(self, state_dict):
         super().load_state_dict(state_dict)
         # masters restored from a checkpoint drive the compute weights
@@ -127,6 +137,7 @@ def _muon_scale(shape: torch.Size) -> float:
 
 
 class Muon(torch.optim.Optimizer):
+    _process_value_according_to_param_policy = staticmethod(_keep_fp32_state)
     """Muon for 2-D ``muon`` groups, AdamW (fused kernel) for the rest.
 
     Param groups carry ``use_muon``.  Parameters may be DTensors: in that
