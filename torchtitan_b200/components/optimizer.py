@@ -47,12 +47,27 @@ def _local(t: torch.Tensor) -> torch.Tensor:
     return t.to_local() if isinstance(t, DTensor) else t
 
 
-def _keep_fp32_state(param, value, param_id, param_groups, key=None):
-    """State of parameters with an fp32 master stays fp32 on load (torch casts to
-    the parameter's dtype, which here is the bf16 compute weight)."""
-    if key != "step" and torch.is_tensor(value) and hasattr(param, "_master"):
-        return value.to(device=param.device)
-    return torch.optim.Optimizer._process_value_according_to_param_policy(param, value, param_id, param_groups, key)
+def _load_keeping_fp32(opt: torch.optim.Optimizer, state_dict) -> None:
+    """torch casts loaded state to each parameter's dtype; master-backed
+    parameters are bf16 compute weights, so they are pointed at their fp32
+    masters while loading, then the masters restored from the state drive them."""
+    swapped = []
+    for group in opt.param_groups:
+        for p in group["params"]:
+            if hasattr(p, "_master") and p.dtype != p._master.dtype:
+                swapped.append((p, p.data))
+                p.data = p._master
+    try:
+        torch.optim.Optimizer.load_state_dict(opt, state_dict)
+    finally:
+        with torch.no_grad():
+            for p, compute in swapped:
+                m = opt.state.get(p, {}).get("master")
+                if m is not None:
+                    p._master.copy_(m)
+                    opt.state[p]["master"] = p._master
+                compute.copy_(p._master)
+                p.data = compute
 
 
 class AdamW(torch.optim.Optimizer):
@@ -98,19 +113,8 @@ class AdamW(torch.optim.Optimizer):
                              copies=copies if any(c is not None for c in copies) else None)
         return loss
 
-    _process_value_according_to_param_policy = staticmethod(_keep_fp32_state)
-
     def load_state_dict(self, state_dict):
-        super().load_state_dict(state_dict)
-        # masters restored from a checkpoint drive the compute weights
-        with torch.no_grad():
-            for group in self.param_groups:
-                for p in group["params"]:
-                    m = self.state.get(p, {}).get("master")
-                    if m is not None and hasattr(p, "_master"):
-                        p._master.copy_(m)
-                        self.state[p]["master"] = p._master
-                        p.data.copy_(p._master)
+        _load_keeping_fp32(self, state_dict)
 
 
 def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
@@ -137,7 +141,6 @@ def _muon_scale(shape: torch.Size) -> float:
 
 
 class Muon(torch.optim.Optimizer):
-    _process_value_according_to_param_policy = staticmethod(_keep_fp32_state)
     """Muon for 2-D ``muon`` groups, AdamW (fused kernel) for the rest.
 
     Param groups carry ``use_muon``.  Parameters may be DTensors: in that
@@ -149,6 +152,9 @@ class Muon(torch.optim.Optimizer):
         super().__init__(params, dict(lr=lr, momentum=momentum, nesterov=nesterov, ns_steps=ns_steps,
                                       betas=betas, eps=eps, weight_decay=weight_decay, use_muon=True))
         self.distributed = distributed
+
+    def load_state_dict(self, state_dict):
+        _load_keeping_fp32(self, state_dict)
 
     def _orthogonalize_all(self, items: list[tuple[torch.Tensor, torch.Tensor]], ns_steps: int) -> list[torch.Tensor]:
         """``items``: (param, momentum-update) pairs; returns per-param local updates."""
