@@ -265,3 +265,15 @@ def test_adamw_master_with_bf16_copy():
     ops.fused_adamw_([p], [g], [m], [v], copies=[copy], **kw)
     R.adamw_([rp], [g.float()], [rm], [rv], **kw)
     assert _rel(p, rp) < 1e-5 and _rel(copy, rp) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 1024), (1000, 776, 520), (4096, 4096, 4096)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+def test_gemm_2sm(ext, M, N, K, a_mn, b_mn):
+    torch.manual_seed(13)
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    D = ext.gemm_2sm(A.t().contiguous() if a_mn else A, B.t().contiguous() if b_mn else B, a_mn, b_mn)
+    torch.cuda.synchronize()
+    assert ext.gemm2_error_code(True) == 0
+    assert _rel(D, A.float() @ B.float().t()) < 1e-2

@@ -33,6 +33,19 @@ Tensor gemm(Tensor A, Tensor B, bool a_mn, bool b_mn) {
   return D;
 }
 
+Tensor gemm_2sm(Tensor A, Tensor B, bool a_mn, bool b_mn) {
+  check_cuda_bf16(A, "A");
+  check_cuda_bf16(B, "B");
+  c10::cuda::CUDAGuard g(A.device());
+  const int64_t M = a_mn ? A.size(1) : A.size(0), K = a_mn ? A.size(0) : A.size(1);
+  const int64_t N = b_mn ? B.size(1) : B.size(0), Kb = b_mn ? B.size(0) : B.size(1);
+  TORCH_CHECK(K == Kb, "gemm_2sm: reduction dims differ");
+  TORCH_CHECK((a_mn ? M : K) % 8 == 0 && (b_mn ? N : K) % 8 == 0, "gemm_2sm: contiguous dims must be multiples of 8");
+  Tensor D = torch::empty({M, N}, A.options());
+  if (M > 0 && N > 0 && K > 0) ttb::gemm_bf16_2sm(A.data_ptr(), B.data_ptr(), D.data_ptr(), M, N, K, a_mn, b_mn, stream());
+  return D;
+}
+
 // mode 1 (grouped rows): A [Mp, K] padded rows, B [G*N, K] (or [G*K, N] if b_mn), tile_group [Mp/128] int32
 Tensor gemm_grouped_rows(Tensor A, Tensor B, Tensor tile_group, int64_t n_out, int64_t b_group_rows, bool b_mn) {
   check_cuda_bf16(A, "A");
@@ -254,6 +267,8 @@ std::vector<Tensor> attn_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor o
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "torchtitan_b200 sm_100a kernels";
   m.def("gemm", &gemm, "bf16 GEMM on tcgen05: D = A(m,k) * B(n,k)");
+  m.def("gemm_2sm", &gemm_2sm, "bf16 GEMM on tcgen05 CTA pairs (cta_group::2)");
+  m.def("gemm2_error_code", &ttb::gemm2_error_code, py::arg("reset") = true);
   m.def("gemm_grouped_rows", &gemm_grouped_rows, "grouped GEMM over 128-row padded expert segments");
   m.def("gemm_grouped_k", &gemm_grouped_k, "grouped GEMM reducing over per-group row ranges (expert wgrad)");
   m.def("gemm_error_code", &ttb::gemm_error_code, "read (and optionally clear) the GEMM timeout word",

@@ -27,6 +27,10 @@ inline int num_sms(int dev) {
 void gemm_bf16(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn,
                cudaStream_t stream);
 int gemm_error_code(bool reset);
+// gemm_2sm.cu: same contract as gemm_bf16 on CTA pairs (256x256 tiles)
+void gemm_bf16_2sm(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K, bool a_mn, bool b_mn,
+                   cudaStream_t stream);
+int gemm2_error_code(bool reset);
 // mode 1: per-M-tile group (tile_group[m_tile], -1 = skip) picks B rows [g*b_group_rows, ...);
 // mode 2: group g reduces over K rows [kstart[g], kstart[g]+klen[g]) into D[g] (A, B M/N-major).
 void gemm_bf16_grouped(const void* A, const void* B, void* D, int64_t M, int64_t N, int64_t K, bool a_mn,

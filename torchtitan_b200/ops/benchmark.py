@@ -53,12 +53,13 @@ def bench_gemm(ext, out):
         A = torch.randn((K, M) if amn else (M, K), device="cuda", dtype=torch.bfloat16)
         B = torch.randn((K, N) if bmn else (N, K), device="cuda", dtype=torch.bfloat16)
         ours = time_fn(lambda: ext.gemm(A, B, amn, bmn))
+        ours2 = time_fn(lambda: ext.gemm_2sm(A, B, amn, bmn)) if hasattr(ext, "gemm_2sm") else float("nan")
         At = A.t() if amn else A
         Bt = B if bmn else B.t()
         lib = time_fn(lambda: torch.matmul(At, Bt))
         fl = 2.0 * M * N * K
         out.append({"kernel": "gemm_tcgen05", "case": name, "M": M, "N": N, "K": K, "ms": ours,
-                    "tflops": fl / ours / 1e9, "cublas_ms": lib, "cublas_tflops": fl / lib / 1e9,
+                    "tflops": fl / ours / 1e9, "tflops_2sm": fl / ours2 / 1e9, "cublas_ms": lib, "cublas_tflops": fl / lib / 1e9,
                     "ratio_vs_cublas": lib / ours, "err": ext.gemm_error_code(True)})
         print(json.dumps(out[-1]), flush=True)
 
