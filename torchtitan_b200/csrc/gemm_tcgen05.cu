@@ -16,6 +16,7 @@
 // GROUP_M-row bands so consecutive CTAs share A/B panels in L2.
 // All barrier waits are bounded (see sm100_ptx.cuh); a timeout sets
 // gemm_error_code() and the kernel exits after releasing TMEM.
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -319,6 +320,15 @@ void gemm_bf16(const void* A, const void* B, void* D, int64_t M, int64_t N, int6
   if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) throw std::runtime_error("gemm: dims too large");
   if ((a_mn ? M : K) % 8 != 0 || (b_mn ? N : K) % 8 != 0)
     throw std::runtime_error("gemm: contiguous dimension of each operand must be a multiple of 8");
+  // CTA-pair kernel for large tiles (measured faster except for very wide N)
+  static const bool pair_enabled = [] {
+    const char* e = std::getenv("TTB_GEMM_2SM");
+    return !(e && e[0] == '0');
+  }();
+  if (pair_enabled && M >= 512 && N >= 256 && N <= 32768) {
+    gemm_bf16_2sm(A, B, D, M, N, K, a_mn, b_mn, stream);
+    return;
+  }
   const CUtensorMap ta = a_mn ? make_tmap_bf16_2d(A, K, M, M, 64, 64) : make_tmap_bf16_2d(A, M, K, K, BM, 64);
   const CUtensorMap tb = b_mn ? make_tmap_bf16_2d(B, K, N, N, 64, 64) : make_tmap_bf16_2d(B, N, K, K, BN, 64);
   Params p;

@@ -60,7 +60,7 @@ def bench_gemm(ext, out):
         fl = 2.0 * M * N * K
         out.append({"kernel": "gemm_tcgen05", "case": name, "M": M, "N": N, "K": K, "ms": ours,
                     "tflops": fl / ours / 1e9, "tflops_2sm": fl / ours2 / 1e9, "cublas_ms": lib, "cublas_tflops": fl / lib / 1e9,
-                    "ratio_vs_cublas": lib / ours, "err": ext.gemm_error_code(True)})
+                    "ratio_vs_cublas": lib / ours, "err": ext.gemm_error_code(True) + ext.gemm2_error_code(True)})
         print(json.dumps(out[-1]), flush=True)
 
 
