@@ -199,3 +199,21 @@ def test_kimi_flops_counts_active_experts_only():
     n, flops = a.get_nparams_and_flops(model, 128)
     routed = sum(p.numel() for k, p in model.named_parameters() if "_moe.experts." in k)
     assert flops < 6 * (n - routed * 0.5)
+
+
+def test_fused_clip_matches_explicit_clip():
+    from torchtitan_b200.components.optimizer import AdamW
+    from torchtitan_b200.parallel.utils import clip_grad_norm_
+
+    torch.manual_seed(1)
+    w = torch.randn(6, 4)
+    g = torch.randn(6, 4) * 10
+    p1, p2 = torch.nn.Parameter(w.clone()), torch.nn.Parameter(w.clone())
+    p1.grad, p2.grad = g.clone(), g.clone()
+    o1, o2 = AdamW([p1], lr=1e-2), AdamW([p2], lr=1e-2)
+    clip_grad_norm_([p1], 1.0)
+    o1.step()
+    n, total = clip_grad_norm_([p2], 1.0, defer_scaling=True)
+    o2.pending_clip = (total, 1.0)
+    o2.step()
+    assert torch.allclose(p1, p2, atol=1e-6) and o2.pending_clip is None

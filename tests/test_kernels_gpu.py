@@ -277,3 +277,20 @@ def test_gemm_2sm(ext, M, N, K, a_mn, b_mn):
     torch.cuda.synchronize()
     assert ext.gemm2_error_code(True) == 0
     assert _rel(D, A.float() @ B.float().t()) < 1e-2
+
+
+def test_adamw_fused_clip(ext):
+    from torchtitan_b200 import ops
+    from torchtitan_b200.ops import reference as R
+
+    torch.manual_seed(14)
+    p = torch.randn(10000, device="cuda")
+    g = torch.randn_like(p) * 3
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    rp, rm, rv = p.clone(), m.clone(), v.clone()
+    total = g.pow(2).sum()
+    coef = min(1.0, 1.0 / (total.sqrt().item() + 1e-6))
+    kw = dict(lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, step=2)
+    ops.fused_adamw_([p], [g], [m], [v], clip_total=total, clip_max=1.0, **kw)
+    R.adamw_([rp], [g * coef], [rm], [rv], **kw)
+    assert _rel(p, rp) < 1e-5 and _rel(m, rm) < 1e-5

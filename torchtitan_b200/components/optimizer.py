@@ -76,6 +76,9 @@ class AdamW(torch.optim.Optimizer):
 
     def __init__(self, params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, fused=True):
         super().__init__(params, dict(lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, fused=fused))
+        self.pending_clip: tuple[torch.Tensor, float] | None = None  # (sum of squares, max_norm) for the next step
+
+    supports_fused_clip = True
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -108,9 +111,12 @@ class AdamW(torch.optim.Optimizer):
             lr = group["lr"]
             lr = float(lr.item()) if torch.is_tensor(lr) else float(lr)
             # all params of a group advance together, so a single step count is used
+            clip_total, clip_max = self.pending_clip if self.pending_clip is not None else (None, 0.0)
             ops.fused_adamw_(ps, gs, ms, vs, lr=lr, beta1=b1, beta2=b2, eps=group["eps"],
                              weight_decay=group["weight_decay"], step=steps[0],
-                             copies=copies if any(c is not None for c in copies) else None)
+                             copies=copies if any(c is not None for c in copies) else None,
+                             clip_total=clip_total, clip_max=clip_max)
+        self.pending_clip = None
         return loss
 
     def load_state_dict(self, state_dict):

@@ -48,9 +48,13 @@ __device__ __forceinline__ float adam_update(float& pv, float g, float& m, float
   return pv;
 }
 
+// clip_total (optional): device sum of squared grad norms; grads are scaled by
+// min(1, clip_max / (sqrt(total) + 1e-6)) on the fly (clipping fused into the step)
 __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table t, float lr, float b1, float b2,
-                                                   float eps, float wd, float bc1, float bc2_sqrt) {
+                                                   float eps, float wd, float bc1, float bc2_sqrt,
+                                                   const float* __restrict__ clip_total, float clip_max) {
   const Chunk c = t.c[blockIdx.x];
+  const float gs = clip_total ? fminf(clip_max / (sqrtf(*clip_total) + 1e-6f), 1.f) : 1.f;
   const float step_size = lr / bc1;
   const float decay = 1.f - lr * wd;
   if (c.vec4 && !c.p_bf16 && c.g_bf16) {
@@ -61,11 +65,13 @@ __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table
     float4* v4 = reinterpret_cast<float4*>(c.v);
     uint2* c4 = reinterpret_cast<uint2*>(c.p_copy);
     const int n4 = c.n / 4;
+#pragma unroll 2
     for (int i = threadIdx.x; i < n4; i += NT) {
       float4 p = p4[i], m = m4[i], v = v4[i];
       const uint2 gr = g4[i];
-      const float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.x));
-      const float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.y));
+      float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.x));
+      float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.y));
+      g01.x *= gs; g01.y *= gs; g23.x *= gs; g23.y *= gs;
       adam_update(p.x, g01.x, m.x, v.x, b1, b2, eps, decay, step_size, bc2_sqrt);
       adam_update(p.y, g01.y, m.y, v.y, b1, b2, eps, decay, step_size, bc2_sqrt);
       adam_update(p.z, g23.x, m.z, v.z, b1, b2, eps, decay, step_size, bc2_sqrt);
@@ -87,8 +93,10 @@ __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table
     float4* m4 = reinterpret_cast<float4*>(c.m);
     float4* v4 = reinterpret_cast<float4*>(c.v);
     const int n4 = c.n / 4;
+#pragma unroll 2
     for (int i = threadIdx.x; i < n4; i += NT) {
       float4 p = p4[i], g = g4[i], m = m4[i], v = v4[i];
+      g.x *= gs; g.y *= gs; g.z *= gs; g.w *= gs;
       adam_update(p.x, g.x, m.x, v.x, b1, b2, eps, decay, step_size, bc2_sqrt);
       adam_update(p.y, g.y, m.y, v.y, b1, b2, eps, decay, step_size, bc2_sqrt);
       adam_update(p.z, g.z, m.z, v.z, b1, b2, eps, decay, step_size, bc2_sqrt);
@@ -100,7 +108,7 @@ __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table
     return;
   }
   for (int i = threadIdx.x; i < c.n; i += NT) {
-    const float g = ldv(c.g, i, c.g_bf16);
+    const float g = ldv(c.g, i, c.g_bf16) * gs;
     float m = c.m[i], v = c.v[i];
     float pv = c.p_bf16 ? __bfloat162float(static_cast<__nv_bfloat16*>(c.p)[i]) : static_cast<float*>(c.p)[i];
     adam_update(pv, g, m, v, b1, b2, eps, decay, step_size, bc2_sqrt);
@@ -193,7 +201,7 @@ __global__ void __launch_bounds__(NT) clip_scale_kernel(const __grid_constant__ 
 }  // namespace
 
 void adamw_multi(const AdamWTensor* list, int count, float lr, float beta1, float beta2, float eps, float wd, int step,
-                 cudaStream_t s) {
+                 cudaStream_t s, const float* clip_total, float clip_max) {
   const double bc1 = 1.0 - std::pow(static_cast<double>(beta1), step);
   const double bc2 = 1.0 - std::pow(static_cast<double>(beta2), step);
   Table tab;
@@ -201,7 +209,7 @@ void adamw_multi(const AdamWTensor* list, int count, float lr, float beta1, floa
   auto flush = [&]() {
     if (nc == 0) return;
     adamw_kernel<<<nc, NT, 0, s>>>(tab, lr, beta1, beta2, eps, wd, static_cast<float>(bc1),
-                                   static_cast<float>(std::sqrt(bc2)));
+                                   static_cast<float>(std::sqrt(bc2)), clip_total, clip_max);
     check_cuda(cudaGetLastError(), "adamw");
     nc = 0;
   };

@@ -168,7 +168,8 @@ Tensor ce_bwd(Tensor logits, Tensor labels, Tensor lse, Tensor gscale, int64_t i
 }
 
 void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Tensor> ms, std::vector<Tensor> vs,
-           double lr, double b1, double b2, double eps, double wd, int64_t step, std::vector<Tensor> copies) {
+           double lr, double b1, double b2, double eps, double wd, int64_t step, std::vector<Tensor> copies,
+           c10::optional<Tensor> clip_total, double clip_max) {
   TORCH_CHECK(copies.empty() || copies.size() == params.size(), "adamw: copies must be empty or match params");
   TORCH_CHECK(params.size() == grads.size() && params.size() == ms.size() && params.size() == vs.size(),
               "adamw: list lengths differ");
@@ -196,7 +197,8 @@ void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Te
   }
   ttb::adamw_multi(list.data(), static_cast<int>(list.size()), static_cast<float>(lr), static_cast<float>(b1),
                    static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd), static_cast<int>(step),
-                   stream());
+                   stream(), clip_total.has_value() ? clip_total->data_ptr<float>() : nullptr,
+                   static_cast<float>(clip_max));
 }
 
 std::vector<ttb::SumSqTensor> sq_list(const std::vector<Tensor>& xs) {
@@ -284,7 +286,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_bwd", &ce_bwd);
   m.def("adamw", &adamw, py::arg("params"), py::arg("grads"), py::arg("exp_avgs"), py::arg("exp_avg_sqs"),
         py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("weight_decay"), py::arg("step"),
-        py::arg("copies") = std::vector<Tensor>());
+        py::arg("copies") = std::vector<Tensor>(), py::arg("clip_total") = py::none(), py::arg("clip_max") = 0.0);
   m.def("multi_sumsq", &multi_sumsq, "sum of squares over a list of fp32/bf16 tensors");
   m.def("multi_clip_scale", &multi_clip_scale, "scale tensors by min(1, max_norm/(sqrt(total)+1e-6))");
   m.def("attn_fwd", &attn_fwd);

@@ -66,7 +66,7 @@ struct AdamWTensor {
   void* p_copy = nullptr;  // optional bf16 copy of the updated fp32 param (compute weights)
 };
 void adamw_multi(const AdamWTensor* host_list, int count, float lr, float beta1, float beta2, float eps, float wd,
-                 int step, cudaStream_t s);
+                 int step, cudaStream_t s, const float* clip_total = nullptr, float clip_max = 0.f);
 
 struct SumSqTensor {
   const void* x;

@@ -129,11 +129,17 @@ from .moe import grouped_swiglu  # noqa: E402
 
 # -------------------------------------------------------------------------- AdamW
 def fused_adamw_(params, grads, exp_avgs, exp_avg_sqs, *, lr: float, beta1: float, beta2: float,
-                 eps: float, weight_decay: float, step: int, copies=None) -> None:
-    """``copies``: optional bf16 tensors receiving the updated fp32 params (compute weights)."""
+                 eps: float, weight_decay: float, step: int, copies=None, clip_total=None,
+                 clip_max: float = 0.0) -> None:
+    """``copies``: optional bf16 tensors receiving the updated fp32 params (compute weights).
+    ``clip_total``: optional device scalar (sum of squared grad norms); grads are scaled by
+    min(1, clip_max / (sqrt(clip_total) + 1e-6)) inside the kernel."""
     if not params:
         return
     if not params[0].is_cuda:
+        if clip_total is not None:
+            coef = float(torch.clamp(clip_max / (clip_total.sqrt() + 1e-6), max=1.0))
+            grads = [g * coef for g in grads]
         _ref.adamw_(params, grads, exp_avgs, exp_avg_sqs, lr=lr, beta1=beta1, beta2=beta2, eps=eps,
                     weight_decay=weight_decay, step=step)
         for p, c in zip(params, copies or []):
@@ -142,4 +148,5 @@ def fused_adamw_(params, grads, exp_avgs, exp_avg_sqs, *, lr: float, beta1: floa
         return
     cp = [c if c is not None else torch.empty(0, device=params[0].device) for c in (copies or [])]
     ext().adamw(list(params), list(grads), list(exp_avgs), list(exp_avg_sqs), float(lr), float(beta1),
-                float(beta2), float(eps), float(weight_decay), int(step), cp)
+                float(beta2), float(eps), float(weight_decay), int(step), cp,
+                clip_total.float().reshape(()).contiguous() if clip_total is not None else None, float(clip_max))

@@ -142,7 +142,7 @@ def set_determinism(parallel_dims: Any, device: torch.device, debug: Any,
 
 @torch.no_grad()
 def clip_grad_norm_(parameters, max_norm: float, norm_type: float = 2.0, foreach: bool = True,
-                    pp_mesh: Any = None, ep_enabled: bool = False) -> torch.Tensor:
+                    pp_mesh: Any = None, ep_enabled: bool = False, defer_scaling: bool = False):
     """Global grad-norm (over DTensor shards, PP stages) and in-place clipping.
 
     Local squared norms are summed per (mesh, shard-dims) signature, reduced
@@ -151,7 +151,7 @@ def clip_grad_norm_(parameters, max_norm: float, norm_type: float = 2.0, foreach
     """
     grads = [p.grad for p in parameters if p.grad is not None]
     if not grads:
-        return torch.zeros(())
+        return (torch.zeros(()), torch.zeros(())) if defer_scaling else torch.zeros(())
     assert norm_type == 2.0, "only the 2-norm is supported"
     per_sig: dict[Any, list[torch.Tensor]] = {}
     for g in grads:
@@ -177,6 +177,8 @@ def clip_grad_norm_(parameters, max_norm: float, norm_type: float = 2.0, foreach
     if pp_mesh is not None:
         dist.all_reduce(total, group=pp_mesh.get_group())
     norm = total.sqrt()
+    if defer_scaling:
+        return norm, total  # the fused optimizer applies the clip coefficient itself
     if max_norm and max_norm > 0:
         locs = [g.to_local() if isinstance(g, DTensor) else g for g in grads]
         if locs[0].is_cuda and all(t.is_contiguous() for t in locs):

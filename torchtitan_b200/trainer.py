@@ -288,9 +288,18 @@ class Trainer(Stateful, Configurable):
             labels = labels.to(self.device, non_blocking=True)
             losses.append(self.forward_backward_step(input_dict=inp, labels=labels,
                                                      global_valid_tokens=global_valid).detach())
-        grad_norm = dist_utils.clip_grad_norm_([p for m in self.model_parts for p in m.parameters()],
-                                               self.config.training.max_norm,
-                                               pp_mesh=pd.get_optional_mesh("pp"), ep_enabled=pd.ep_enabled)
+        max_norm = self.config.training.max_norm
+        fused_clip = max_norm > 0 and all(getattr(o, "supports_fused_clip", False)
+                                          for o in self.optimizers.optimizers)
+        clip = dist_utils.clip_grad_norm_([p for m in self.model_parts for p in m.parameters()], max_norm,
+                                          pp_mesh=pd.get_optional_mesh("pp"), ep_enabled=pd.ep_enabled,
+                                          defer_scaling=fused_clip)
+        if fused_clip:
+            grad_norm, total = clip
+            for o in self.optimizers.optimizers:
+                o.pending_clip = (total, max_norm)
+        else:
+            grad_norm = clip
         self.checkpointer.maybe_wait_for_staging()
         self.optimizers.step()
         self.lr_schedulers.step()
