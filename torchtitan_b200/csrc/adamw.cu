@@ -17,7 +17,7 @@ namespace ttb {
 namespace {
 
 constexpr int CHUNK = 65536;
-constexpr int MAX_CHUNKS = 320;  // per launch: fits the 32 KB kernel-parameter budget
+constexpr int MAX_CHUNKS = 640;  // per launch: 640 x 48 B fits the 32 KB kernel-parameter budget
 constexpr int NT = 512;
 
 struct Chunk {

@@ -244,7 +244,8 @@ std::vector<Tensor> attn_fwd(Tensor q, Tensor k, Tensor v, bool causal, double s
   TORCH_CHECK(H % Hk == 0, "attention: n_heads must be a multiple of n_kv_heads");
   c10::cuda::CUDAGuard g(q.device());
   Tensor o = torch::empty({B, Sq, H, Dv}, q.options());
-  Tensor lse = torch::empty({B, H, Sq}, q.options().dtype(at::kFloat));
+  // rows padded to a multiple of 64 and zero-filled (the backward bulk-copies 64-query slices)
+  Tensor lse = torch::zeros({B, H, (Sq + 63) / 64 * 64}, q.options().dtype(at::kFloat));
   ttb::attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), B, Sq, Sk, H, Hk, Dqk,
                 Dv, causal, static_cast<float>(scale), stream());
   return {o, lse};
@@ -257,7 +258,7 @@ std::vector<Tensor> attn_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor o
   const int Sk = k.size(1), Hk = k.size(2), Dv = v.size(3);
   c10::cuda::CUDAGuard g(q.device());
   Tensor dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
-  Tensor delta = torch::empty({B, H, Sq}, q.options().dtype(at::kFloat));
+  Tensor delta = torch::zeros({B, H, (Sq + 63) / 64 * 64}, q.options().dtype(at::kFloat));
   ttb::attn_bwd(dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
                 dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), nullptr, delta.data_ptr<float>(), B, Sq, Sk, H, Hk, Dqk,
                 Dv, causal, static_cast<float>(scale), stream());

@@ -28,6 +28,17 @@ namespace attn_impl {
 
 __device__ int g_err;
 
+// lse / delta rows are padded to a multiple of 64 queries (zero-filled by the
+// allocator) so 64-query slices can be bulk-copied without running off a row
+__host__ __device__ __forceinline__ int lse_stride(int Sq) { return (Sq + 63) / 64 * 64; }
+
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 constexpr int BM = 128;  // queries per CTA
 constexpr int NUM_SM_WARPS = 8;                    // softmax / epilogue warps
 constexpr int NUM_THREADS = 64 + 32 * NUM_SM_WARPS;  // + producer + MMA warp
@@ -423,7 +434,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       if (hh == 0) {
         const float lse = (l_tot > 0.f && m_run != -INFINITY) ? (m_run + __log2f(l_tot)) * 0.69314718055994531f
                                                                : -INFINITY;
-        p.lse[(static_cast<size_t>(b) * p.H + h) * p.Sq + qrow] = lse;
+        p.lse[(static_cast<size_t>(b) * p.H + h) * lse_stride(p.Sq) + qrow] = lse;
       }
     }
   }
@@ -745,7 +756,7 @@ __global__ void __maxnreg__(192)
     if (store) {
       const float lse = (l_run > 0.f && m_used != -INFINITY && have) ? (m_used + __log2f(l_run)) * 0.69314718055994531f
                                                                      : -INFINITY;
-      p.lse[(static_cast<size_t>(b) * p.H + h) * p.Sq + qrow] = lse;
+      p.lse[(static_cast<size_t>(b) * p.H + h) * lse_stride(p.Sq) + qrow] = lse;
     }
   }
   tc_fence_before();
@@ -831,7 +842,7 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ dout, co
     const int64_t bs = row / H;
     const int sidx = bs % S;
     const int bidx = bs / S;
-    delta[((int64_t)bidx * H + h) * S + sidx] = acc;
+    delta[((int64_t)bidx * H + h) * lse_stride(S) + sidx] = acc;
   }
 }
 
@@ -884,8 +895,8 @@ struct DKVBars {
   uint64_t acc_full;
   uint32_t tmem_base;
   int abort_flag;
-  alignas(8) float lse2[2][64];  // -lse * log2(e) per query of the staged tile
-  alignas(8) float dlt[2][64];   // -delta per query
+  alignas(16) float lse2[2][64];  // lse (natural log) of the staged 64 queries (bulk-copied)
+  alignas(16) float dlt[2][64];   // delta of the staged 64 queries (bulk-copied)
 };
 
 template <int DQK, int DV, int NBUF>
@@ -953,7 +964,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int h = hk * group + i / per_head;
         const int q0 = (qt_first + i % per_head) * C::BQ;
         if (!mbar_wait(&bar.qd_empty[st], ((i >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 31)) break;
-        mbar_arrive_expect_tx(&bar.qd_full[st], C::Q_BYTES + C::O_BYTES);
+        mbar_arrive_expect_tx(&bar.qd_full[st], C::Q_BYTES + C::O_BYTES + 2 * 64 * 4);
+        const size_t row = ((size_t)b * p.H + h) * lse_stride(p.Sq) + q0;
+        bulk_copy_g2s(&bar.lse2[st][0], p.lse + row, 256, &bar.qd_full[st]);
+        bulk_copy_g2s(&bar.dlt[st][0], p.delta + row, 256, &bar.qd_full[st]);
 #pragma unroll
         for (int c = 0; c < DQK / 64; ++c)
           tma_load_3d(smem + C::Q_OFF + st * C::Q_BYTES + c * (C::BQ * 128), &tq, &bar.qd_full[st], h * DQK + c * 64,
@@ -1036,15 +1050,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int sb = i % NBUF;
       const int h = hk * group + i / per_head;
       const int q0 = (qt_first + i % per_head) * C::BQ;
-      // stage lse2 / delta of this query tile
-      if (t < 64) {
-        const int qi = q0 + t;
-        bar.lse2[st][t] = qi < p.Sq ? -p.lse[((size_t)b * p.H + h) * p.Sq + qi] * 1.4426950408889634f : -INFINITY;
-      } else {
-        const int qi = q0 + t - 64;
-        bar.dlt[st][t - 64] = qi < p.Sq ? -p.delta[((size_t)b * p.H + h) * p.Sq + qi] : 0.f;
-      }
-      named_bar_sync(1, 32 * NUM_SM_WARPS);
+      // lse / delta of this query tile arrive with the Q/dO tiles
+      if (!mbar_wait(&bar.qd_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 39)) { ok = false; break; }
       if (!mbar_wait(&bar.s_full[sb], (i / NBUF) & 1, &bar.abort_flag, &g_err, 36)) { ok = false; break; }
       if (!mbar_wait(&bar.p_empty[st], ((i >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 37)) { ok = false; break; }
       tc_fence_after();
@@ -1062,9 +1069,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const int col = c * 32 + e;
-          const float2 nl = *reinterpret_cast<const float2*>(&bar.lse2[st][col]);
-          const float2 nd = *reinterpret_cast<const float2*>(&bar.dlt[st][col]);
-          const uint64_t x = fma2(pk2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), cc, pk2(nl.x, nl.y));
+          const float2 ls = *reinterpret_cast<const float2*>(&bar.lse2[st][col]);
+          const float2 dl = *reinterpret_cast<const float2*>(&bar.dlt[st][col]);
+          const uint64_t nl = mul2(pk2(ls.x, ls.y), pk2(-1.4426950408889634f, -1.4426950408889634f));
+          const uint64_t x = fma2(pk2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), cc, nl);
           uint64_t pv = ((e & 7) == 6) ? exp2_poly2(x) : ex2_mufu2(x);
           if (need_mask) {
             float a0, a1;
@@ -1074,7 +1082,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (kidx >= p.Sk || qi + 1 >= p.Sq || (p.causal && kidx > qi + 1 + offset)) a1 = 0.f;
             pv = pk2(a0, a1);
           }
-          const uint64_t ds = mul2(pv, add2(pk2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), pk2(nd.x, nd.y)));
+          const uint64_t ds = mul2(pv, add2(pk2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), pk2(-dl.x, -dl.y)));
           pk[e / 2] = pack_bf16x2_u64(pv);
           dk[e / 2] = pack_bf16x2_u64(ds);
         }
@@ -1290,8 +1298,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int qi = q0 + r;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     const bool qvalid = qi < p.Sq;
-    const float lse2 = qvalid ? p.lse[((size_t)b * p.H + h) * p.Sq + qi] * 1.4426950408889634f : INFINITY;
-    const float dl = qvalid ? p.delta[((size_t)b * p.H + h) * p.Sq + qi] : 0.f;
+    const float lse2 = qvalid ? p.lse[((size_t)b * p.H + h) * lse_stride(p.Sq) + qi] * 1.4426950408889634f : INFINITY;
+    const float dl = qvalid ? p.delta[((size_t)b * p.H + h) * lse_stride(p.Sq) + qi] : 0.f;
     const int diag = qi + offset;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {

@@ -2,7 +2,7 @@
 
 Layout is ``[B, S, H, D]`` (sequence-major, as produced by the QKV GEMM), so
 no transposes are needed around the kernel.  Forward returns the output and
-the per-row log-sum-exp (fp32, ``[B, H, S]``), which backward uses to
+the per-row log-sum-exp (fp32, ``[B, H, S]`` padded to a multiple of 64), which backward uses to
 recompute probabilities tile by tile.  ``Dq`` may differ from ``Dv`` (MLA:
 192 / 128).  The forward is a registered custom op so selective activation
 checkpointing can keep its output.
@@ -26,7 +26,7 @@ def attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, sc
 @attn_fwd.register_fake
 def _(q, k, v, causal, scale):
     B, S, H, _ = q.shape
-    return q.new_empty((B, S, H, v.shape[-1])), q.new_empty((B, H, S), dtype=torch.float32)
+    return q.new_empty((B, S, H, v.shape[-1])), q.new_empty((B, H, (S + 63) // 64 * 64), dtype=torch.float32)
 
 
 class _Attn(torch.autograd.Function):
