@@ -876,8 +876,9 @@ struct DKVCfg {
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = K_OFF + K_BYTES;
   static constexpr int Q_OFF = V_OFF + V_BYTES;
-  static constexpr int DO_OFF = Q_OFF + 2 * Q_BYTES;
-  static constexpr int PT_OFF = DO_OFF + 2 * O_BYTES;
+  static constexpr int QS = (DQK > 128) ? 2 : 3;  // Q/dO stages: 3 hide the TMA latency where smem allows
+  static constexpr int DO_OFF = Q_OFF + QS * Q_BYTES;
+  static constexpr int PT_OFF = DO_OFF + QS * O_BYTES;
   static constexpr int DST_OFF = PT_OFF + 2 * P_BYTES;
   static constexpr int SMEM = DST_OFF + 2 * P_BYTES + 1024;
   static constexpr int ST_COL = 0;                 // NBUF x BQ
@@ -889,14 +890,14 @@ struct DKVCfg {
 
 struct DKVBars {
   uint64_t kv_full;
-  uint64_t qd_full[2], qd_empty[2];
+  uint64_t qd_full[3], qd_empty[3];
   uint64_t s_full[2], s_free[2];
   uint64_t p_full[2], p_empty[2];
   uint64_t acc_full;
   uint32_t tmem_base;
   int abort_flag;
-  alignas(16) float lse2[2][64];  // lse (natural log) of the staged 64 queries (bulk-copied)
-  alignas(16) float dlt[2][64];   // delta of the staged 64 queries (bulk-copied)
+  alignas(16) float lse2[3][64];  // lse (natural log) of the staged 64 queries (bulk-copied)
+  alignas(16) float dlt[3][64];   // delta of the staged 64 queries (bulk-copied)
 };
 
 template <int DQK, int DV, int NBUF>
@@ -929,6 +930,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar.qd_full[i], 1);
       mbar_init(&bar.qd_empty[i], 1);
+      if (i == 1) {
+        mbar_init(&bar.qd_full[2], 1);
+        mbar_init(&bar.qd_empty[2], 1);
+      }
       mbar_init(&bar.s_full[i], 1);
       mbar_init(&bar.s_free[i], NUM_SM_WARPS);
       mbar_init(&bar.p_full[i], NUM_SM_WARPS);
@@ -960,10 +965,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int c = 0; c < DV / 64; ++c)
         tma_load_3d(smem + C::V_OFF + c * (C::BK * 128), &tv, &bar.kv_full, hk * DV + c * 64, k0, b);
       for (int i = 0; i < items; ++i) {
-        const int st = i & 1;
+        const int st = i % C::QS;
         const int h = hk * group + i / per_head;
         const int q0 = (qt_first + i % per_head) * C::BQ;
-        if (!mbar_wait(&bar.qd_empty[st], ((i >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 31)) break;
+        if (!mbar_wait(&bar.qd_empty[st], ((i / C::QS) & 1) ^ 1, &bar.abort_flag, &g_err, 31)) break;
         mbar_arrive_expect_tx(&bar.qd_full[st], C::Q_BYTES + C::O_BYTES + 2 * 64 * 4);
         const size_t row = ((size_t)b * p.H + h) * lse_stride(p.Sq) + q0;
         bulk_copy_g2s(&bar.lse2[st][0], p.lse + row, 256, &bar.qd_full[st]);
@@ -993,8 +998,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         const uint32_t pt = smem_u32(smem + C::PT_OFF + st * C::P_BYTES);
         const uint32_t dst = smem_u32(smem + C::DST_OFF + st * C::P_BYTES);
-        const uint32_t qa = smem_u32(smem + C::Q_OFF + st * C::Q_BYTES);
-        const uint32_t da = smem_u32(smem + C::DO_OFF + st * C::O_BYTES);
+        const int qs = i % C::QS;
+        const uint32_t qa = smem_u32(smem + C::Q_OFF + qs * C::Q_BYTES);
+        const uint32_t da = smem_u32(smem + C::DO_OFF + qs * C::O_BYTES);
 #pragma unroll
         for (int kk = 0; kk < C::BQ / 16; ++kk) {
           const uint64_t a1 = umma_desc_sw128(pt + kk * 32, 16, 1024);
@@ -1007,18 +1013,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t b2 = umma_desc_sw128(qa + kk * 2048, C::BQ * 128, 1024);
           umma_bf16(tmem + C::DK_COL, a2, b2, idesc_dk, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bar.qd_empty[st]);
+        umma_commit(&bar.qd_empty[qs]);
         umma_commit(&bar.p_empty[st]);
         return true;
       };
       for (int i = 0; ok && i < items; ++i) {
-        const int st = i & 1;
+        const int qs = i % C::QS;
         const int sb = i % NBUF;
-        if (!mbar_wait(&bar.qd_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 34)) { ok = false; break; }
+        if (!mbar_wait(&bar.qd_full[qs], (i / C::QS) & 1, &bar.abort_flag, &g_err, 34)) { ok = false; break; }
         if (!mbar_wait(&bar.s_free[sb], ((i / NBUF) & 1) ^ 1, &bar.abort_flag, &g_err, 35)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t qa = smem_u32(smem + C::Q_OFF + st * C::Q_BYTES);
-        const uint32_t da = smem_u32(smem + C::DO_OFF + st * C::O_BYTES);
+        const uint32_t qa = smem_u32(smem + C::Q_OFF + qs * C::Q_BYTES);
+        const uint32_t da = smem_u32(smem + C::DO_OFF + qs * C::O_BYTES);
 #pragma unroll
         for (int kk = 0; kk < DQK / 16; ++kk) {
           const uint64_t a = umma_desc_sw128(k_addr + (kk >> 2) * (C::BK * 128) + (kk & 3) * 32, 16, 1024);
@@ -1051,7 +1057,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int h = hk * group + i / per_head;
       const int q0 = (qt_first + i % per_head) * C::BQ;
       // lse / delta of this query tile arrive with the Q/dO tiles
-      if (!mbar_wait(&bar.qd_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 39)) { ok = false; break; }
+      const int qs = i % C::QS;
+      if (!mbar_wait(&bar.qd_full[qs], (i / C::QS) & 1, &bar.abort_flag, &g_err, 39)) { ok = false; break; }
       if (!mbar_wait(&bar.s_full[sb], (i / NBUF) & 1, &bar.abort_flag, &g_err, 36)) { ok = false; break; }
       if (!mbar_wait(&bar.p_empty[st], ((i >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 37)) { ok = false; break; }
       tc_fence_after();
@@ -1069,8 +1076,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           const int col = c * 32 + e;
-          const float2 ls = *reinterpret_cast<const float2*>(&bar.lse2[st][col]);
-          const float2 dl = *reinterpret_cast<const float2*>(&bar.dlt[st][col]);
+          const float2 ls = *reinterpret_cast<const float2*>(&bar.lse2[qs][col]);
+          const float2 dl = *reinterpret_cast<const float2*>(&bar.dlt[qs][col]);
           const uint64_t nl = mul2(pk2(ls.x, ls.y), pk2(-1.4426950408889634f, -1.4426950408889634f));
           const uint64_t x = fma2(pk2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), cc, nl);
           uint64_t pv = ((e & 7) == 6) ? exp2_poly2(x) : ex2_mufu2(x);
@@ -1100,7 +1107,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         mbar_arrive(&bar.s_free[sb]);
         mbar_arrive(&bar.p_full[st]);
       }
-      // lse2/dlt[st] reused two items later; the barrier at the top orders it
     }
     // epilogue: dV, dK rows (TMEM loads are warp-collective: every lane loads, valid rows store)
     bool have = ok && items > 0 && mbar_wait(&bar.acc_full, 0, &bar.abort_flag, &g_err, 38);
@@ -1154,8 +1160,9 @@ struct DQCfg {
   static constexpr int Q_OFF = 0;
   static constexpr int DO_OFF = Q_OFF + Q_BYTES;
   static constexpr int K_OFF = DO_OFF + O_BYTES;
-  static constexpr int V_OFF = K_OFF + 2 * K_BYTES;
-  static constexpr int DS_OFF = V_OFF + 2 * V_BYTES;
+  static constexpr int KS = (DQK > 128) ? 2 : 4;  // K/V stages
+  static constexpr int V_OFF = K_OFF + KS * K_BYTES;
+  static constexpr int DS_OFF = V_OFF + KS * V_BYTES;
   static constexpr int SMEM = DS_OFF + 2 * DS_BYTES + 1024;
   static constexpr int S_COL = 0;          // 2 x BK
   static constexpr int DP_COL = 2 * BK;    // 2 x BK
@@ -1165,7 +1172,7 @@ struct DQCfg {
 
 struct DQBars {
   uint64_t qd_full;
-  uint64_t kv_full[2], kv_empty[2];
+  uint64_t kv_full[4], kv_empty[4];
   uint64_t s_full[2], s_free[2];
   uint64_t ds_full[2], ds_empty[2];
   uint64_t acc_full;
@@ -1197,9 +1204,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar.qd_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 4; ++i) {
       mbar_init(&bar.kv_full[i], 1);
       mbar_init(&bar.kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bar.s_full[i], 1);
       mbar_init(&bar.s_free[i], NUM_SM_WARPS);
       mbar_init(&bar.ds_full[i], NUM_SM_WARPS);
@@ -1231,8 +1240,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int c = 0; c < DV / 64; ++c)
         tma_load_3d(smem + C::DO_OFF + c * (C::BQ * 128), &tdo, &bar.qd_full, h * DV + c * 64, q0, b);
       for (int j = 0; j < nkv; ++j) {
-        const int st = j & 1;
-        if (!mbar_wait(&bar.kv_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 41)) break;
+        const int st = j % C::KS;
+        if (!mbar_wait(&bar.kv_empty[st], ((j / C::KS) & 1) ^ 1, &bar.abort_flag, &g_err, 41)) break;
         mbar_arrive_expect_tx(&bar.kv_full[st], C::K_BYTES + C::V_BYTES);
 #pragma unroll
         for (int c = 0; c < DQK / 64; ++c)
@@ -1254,25 +1263,27 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int st = i & 1;
         if (!mbar_wait(&bar.ds_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 43)) return false;
         tc_fence_after();
+        const int ks = i % C::KS;
         const uint32_t ds = smem_u32(smem + C::DS_OFF + st * C::DS_BYTES);
-        const uint32_t ka = smem_u32(smem + C::K_OFF + st * C::K_BYTES);
+        const uint32_t ka = smem_u32(smem + C::K_OFF + ks * C::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < C::BK / 16; ++kk) {
           const uint64_t a = umma_desc_sw128(ds + kk * 32, 16, 1024);
           const uint64_t bb = umma_desc_sw128(ka + kk * 2048, C::BK * 128, 1024);
           umma_bf16(tmem + C::DQ_COL, a, bb, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&bar.kv_empty[st]);
+        umma_commit(&bar.kv_empty[ks]);
         umma_commit(&bar.ds_empty[st]);
         return true;
       };
       for (int j = 0; ok && j < nkv; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&bar.kv_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 44)) { ok = false; break; }
+        const int ks = j % C::KS;
+        if (!mbar_wait(&bar.kv_full[ks], (j / C::KS) & 1, &bar.abort_flag, &g_err, 44)) { ok = false; break; }
         if (!mbar_wait(&bar.s_free[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 45)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t ka = smem_u32(smem + C::K_OFF + st * C::K_BYTES);
-        const uint32_t va = smem_u32(smem + C::V_OFF + st * C::V_BYTES);
+        const uint32_t ka = smem_u32(smem + C::K_OFF + ks * C::K_BYTES);
+        const uint32_t va = smem_u32(smem + C::V_OFF + ks * C::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < DQK / 16; ++kk) {
           const uint64_t a = umma_desc_sw128(qa + (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32, 16, 1024);
