@@ -476,7 +476,7 @@ struct Cfg2 {
 
 struct Bars2 {
   uint64_t q_full;
-  uint64_t k_full[2], v_full[2], kv_empty[2];
+  uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
   uint64_t s_full[2], p_full[2], pv_done[2];
   uint32_t tmem_base;
   int abort_flag;
@@ -534,7 +534,8 @@ __global__ void __maxnreg__(192)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar.k_full[i], 1);
       mbar_init(&bar.v_full[i], 1);
-      mbar_init(&bar.kv_empty[i], 1);
+      mbar_init(&bar.k_empty[i], 1);
+      mbar_init(&bar.v_empty[i], 1);
       mbar_init(&bar.s_full[i], 1);
       mbar_init(&bar.p_full[i], 4);
       mbar_init(&bar.pv_done[i], 1);
@@ -564,13 +565,15 @@ __global__ void __maxnreg__(192)
                       q0 + t * BM, b);
       for (int j = 0; j < nkv; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&bar.kv_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 51)) break;
+        if (!mbar_wait(&bar.k_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 51)) break;
         const int k0 = j * BN;
         mbar_arrive_expect_tx(&bar.k_full[st], C::K_BYTES);
 #pragma unroll
         for (int c = 0; c < DQK / 64; ++c)
           tma_load_3d(smem + C::K_OFF + st * C::K_BYTES + c * (BN * 128), &tk, &bar.k_full[st], hk * DQK + c * 64, k0,
                       b);
+        // K is released after the S MMAs, V only after PV: K of step j+2 streams in earlier
+        if (!mbar_wait(&bar.v_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 59)) break;
         mbar_arrive_expect_tx(&bar.v_full[st], C::V_BYTES);
 #pragma unroll
         for (int c = 0; c < DV / 64; ++c)
@@ -603,6 +606,7 @@ __global__ void __maxnreg__(192)
           umma_commit(&bar.s_full[t]);
         }
         if (!ok) break;
+        umma_commit(&bar.k_empty[st]);
         if (!mbar_wait(&bar.v_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 55)) break;
         const uint32_t v_addr = smem_u32(smem + C::V_OFF + st * C::V_BYTES);
 #pragma unroll
@@ -618,7 +622,7 @@ __global__ void __maxnreg__(192)
           umma_commit(&bar.pv_done[t]);
         }
         if (!ok) break;
-        umma_commit(&bar.kv_empty[st]);
+        umma_commit(&bar.v_empty[st]);
       }
     }
   } else {
