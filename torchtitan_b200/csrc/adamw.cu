@@ -17,7 +17,7 @@ namespace ttb {
 namespace {
 
 constexpr int CHUNK = 65536;
-constexpr int MAX_CHUNKS = 640;  // per launch: 640 x 48 B fits the 32 KB kernel-parameter budget
+constexpr int MAX_CHUNKS = 560;  // per launch: 560 x 56 B (+ peer table) fits the 32 KB kernel-parameter budget
 constexpr int NT = 512;
 
 struct Chunk {
@@ -30,6 +30,13 @@ struct Chunk {
   int8_t g_bf16;
   int8_t vec4;  // every pointer 16-byte aligned and n % 4 == 0: float4 path
   __nv_bfloat16* p_copy;  // optional bf16 copy written with the updated fp32 param
+  int64_t peer_off;       // >= 0: also write the bf16 copy at this element offset of every peer buffer
+};
+
+// bf16 weight buffers of all data-parallel ranks (NVLink peer mappings, own rank included)
+struct Peers {
+  __nv_bfloat16* base[8];
+  int n;
 };
 
 struct Table {
@@ -52,50 +59,32 @@ __device__ __forceinline__ float adam_update(float& pv, float g, float& m, float
 // min(1, clip_max / (sqrt(total) + 1e-6)) on the fly (clipping fused into the step)
 __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table t, float lr, float b1, float b2,
                                                    float eps, float wd, float bc1, float bc2_sqrt,
-                                                   const float* __restrict__ clip_total, float clip_max) {
+                                                   const float* __restrict__ clip_total, float clip_max,
+                                                   const __grid_constant__ Peers peers) {
   const Chunk c = t.c[blockIdx.x];
   const float gs = clip_total ? fminf(clip_max / (sqrtf(*clip_total) + 1e-6f), 1.f) : 1.f;
   const float step_size = lr / bc1;
   const float decay = 1.f - lr * wd;
-  if (c.vec4 && !c.p_bf16 && c.g_bf16) {
-    // fp32 master, bf16 grad (and optionally a bf16 compute copy): vector loads and stores
+  if (c.vec4 && !c.p_bf16) {
+    // fp32 master, bf16 or fp32 grad (and optionally bf16 compute copies): vector loads and stores
     float4* p4 = static_cast<float4*>(c.p);
-    const uint2* g4 = static_cast<const uint2*>(c.g);
     float4* m4 = reinterpret_cast<float4*>(c.m);
     float4* v4 = reinterpret_cast<float4*>(c.v);
     uint2* c4 = reinterpret_cast<uint2*>(c.p_copy);
+    const bool copy = c4 != nullptr || c.peer_off >= 0;
     const int n4 = c.n / 4;
 #pragma unroll 2
     for (int i = threadIdx.x; i < n4; i += NT) {
       float4 p = p4[i], m = m4[i], v = v4[i];
-      const uint2 gr = g4[i];
-      float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.x));
-      float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.y));
-      g01.x *= gs; g01.y *= gs; g23.x *= gs; g23.y *= gs;
-      adam_update(p.x, g01.x, m.x, v.x, b1, b2, eps, decay, step_size, bc2_sqrt);
-      adam_update(p.y, g01.y, m.y, v.y, b1, b2, eps, decay, step_size, bc2_sqrt);
-      adam_update(p.z, g23.x, m.z, v.z, b1, b2, eps, decay, step_size, bc2_sqrt);
-      adam_update(p.w, g23.y, m.w, v.w, b1, b2, eps, decay, step_size, bc2_sqrt);
-      p4[i] = p;
-      m4[i] = m;
-      v4[i] = v;
-      if (c4) {
-        __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
-        c4[i] = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+      float4 g;
+      if (c.g_bf16) {
+        const uint2 gr = static_cast<const uint2*>(c.g)[i];
+        const float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.x));
+        const float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gr.y));
+        g = make_float4(g01.x, g01.y, g23.x, g23.y);
+      } else {
+        g = static_cast<const float4*>(c.g)[i];
       }
-    }
-    return;
-  }
-  if (c.vec4 && !c.p_bf16 && !c.g_bf16 && !c.p_copy) {
-    // fp32 master / fp32 grad: 16-byte loads and stores of all four streams
-    float4* p4 = static_cast<float4*>(c.p);
-    const float4* g4 = static_cast<const float4*>(c.g);
-    float4* m4 = reinterpret_cast<float4*>(c.m);
-    float4* v4 = reinterpret_cast<float4*>(c.v);
-    const int n4 = c.n / 4;
-#pragma unroll 2
-    for (int i = threadIdx.x; i < n4; i += NT) {
-      float4 p = p4[i], g = g4[i], m = m4[i], v = v4[i];
       g.x *= gs; g.y *= gs; g.z *= gs; g.w *= gs;
       adam_update(p.x, g.x, m.x, v.x, b1, b2, eps, decay, step_size, bc2_sqrt);
       adam_update(p.y, g.y, m.y, v.y, b1, b2, eps, decay, step_size, bc2_sqrt);
@@ -104,6 +93,14 @@ __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table
       p4[i] = p;
       m4[i] = m;
       v4[i] = v;
+      if (copy) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(p.x, p.y), hi = __floats2bfloat162_rn(p.z, p.w);
+        const uint2 w = make_uint2(*reinterpret_cast<uint32_t*>(&lo), *reinterpret_cast<uint32_t*>(&hi));
+        if (c4) c4[i] = w;
+        // all-gather fused into the update: the new weights go straight to every rank's buffer
+        if (c.peer_off >= 0)
+          for (int j = 0; j < peers.n; ++j) reinterpret_cast<uint2*>(peers.base[j] + c.peer_off)[i] = w;
+      }
     }
     return;
   }
@@ -117,6 +114,7 @@ __global__ void __launch_bounds__(NT) adamw_kernel(const __grid_constant__ Table
     if (c.p_bf16) static_cast<__nv_bfloat16*>(c.p)[i] = __float2bfloat16(pv);
     else static_cast<float*>(c.p)[i] = pv;
     if (c.p_copy) c.p_copy[i] = __float2bfloat16(pv);
+    for (int j = 0; j < peers.n && c.peer_off >= 0; ++j) peers.base[j][c.peer_off + i] = __float2bfloat16(pv);
   }
 }
 
@@ -201,7 +199,10 @@ __global__ void __launch_bounds__(NT) clip_scale_kernel(const __grid_constant__ 
 }  // namespace
 
 void adamw_multi(const AdamWTensor* list, int count, float lr, float beta1, float beta2, float eps, float wd, int step,
-                 cudaStream_t s, const float* clip_total, float clip_max) {
+                 cudaStream_t s, const float* clip_total, float clip_max, void* const* peer_bases, int n_peers) {
+  Peers peers;
+  peers.n = n_peers;
+  for (int j = 0; j < 8; ++j) peers.base[j] = j < n_peers ? static_cast<__nv_bfloat16*>(peer_bases[j]) : nullptr;
   const double bc1 = 1.0 - std::pow(static_cast<double>(beta1), step);
   const double bc2 = 1.0 - std::pow(static_cast<double>(beta2), step);
   Table tab;
@@ -209,7 +210,7 @@ void adamw_multi(const AdamWTensor* list, int count, float lr, float beta1, floa
   auto flush = [&]() {
     if (nc == 0) return;
     adamw_kernel<<<nc, NT, 0, s>>>(tab, lr, beta1, beta2, eps, wd, static_cast<float>(bc1),
-                                   static_cast<float>(std::sqrt(bc2)), clip_total, clip_max);
+                                   static_cast<float>(std::sqrt(bc2)), clip_total, clip_max, peers);
     check_cuda(cudaGetLastError(), "adamw");
     nc = 0;
   };
@@ -226,10 +227,12 @@ void adamw_multi(const AdamWTensor* list, int count, float lr, float beta1, floa
       c.p_bf16 = static_cast<int8_t>(t.p_dtype);
       c.g_bf16 = static_cast<int8_t>(t.g_dtype);
       c.p_copy = t.p_copy ? static_cast<__nv_bfloat16*>(t.p_copy) + off : nullptr;
+      c.peer_off = t.peer_off >= 0 ? t.peer_off + off : -1;
       c.vec4 = static_cast<int8_t>(((reinterpret_cast<uintptr_t>(c.p) | reinterpret_cast<uintptr_t>(c.m) |
                                      reinterpret_cast<uintptr_t>(c.v)) & 15) == 0 &&
                                    (reinterpret_cast<uintptr_t>(c.g) & (t.g_dtype ? 7 : 15)) == 0 &&
-                                   (reinterpret_cast<uintptr_t>(c.p_copy) & 7) == 0 && c.n % 4 == 0);
+                                   (reinterpret_cast<uintptr_t>(c.p_copy) & 7) == 0 && c.n % 4 == 0 &&
+                                   (c.peer_off < 0 || c.peer_off % 4 == 0));
       if (++nc == MAX_CHUNKS) flush();
     }
   }

@@ -169,7 +169,10 @@ Tensor ce_bwd(Tensor logits, Tensor labels, Tensor lse, Tensor gscale, int64_t i
 
 void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Tensor> ms, std::vector<Tensor> vs,
            double lr, double b1, double b2, double eps, double wd, int64_t step, std::vector<Tensor> copies,
-           c10::optional<Tensor> clip_total, double clip_max) {
+           c10::optional<Tensor> clip_total, double clip_max, std::vector<int64_t> peer_offsets,
+           std::vector<int64_t> peer_bases) {
+  TORCH_CHECK(peer_offsets.empty() || peer_offsets.size() == params.size(), "adamw: peer_offsets size");
+  TORCH_CHECK(peer_bases.size() <= 8, "adamw: at most 8 peers");
   TORCH_CHECK(copies.empty() || copies.size() == params.size(), "adamw: copies must be empty or match params");
   TORCH_CHECK(params.size() == grads.size() && params.size() == ms.size() && params.size() == vs.size(),
               "adamw: list lengths differ");
@@ -193,12 +196,14 @@ void adamw(std::vector<Tensor> params, std::vector<Tensor> grads, std::vector<Te
       cp = copies[i].data_ptr();
     }
     list.push_back({p.data_ptr(), gr.data_ptr(), m.data_ptr<float>(), v.data_ptr<float>(), p.numel(),
-                    p.scalar_type() == at::kBFloat16 ? 1 : 0, gr.scalar_type() == at::kBFloat16 ? 1 : 0, cp});
+                    p.scalar_type() == at::kBFloat16 ? 1 : 0, gr.scalar_type() == at::kBFloat16 ? 1 : 0, cp,
+                    peer_offsets.empty() ? -1 : peer_offsets[i]});
   }
   ttb::adamw_multi(list.data(), static_cast<int>(list.size()), static_cast<float>(lr), static_cast<float>(b1),
                    static_cast<float>(b2), static_cast<float>(eps), static_cast<float>(wd), static_cast<int>(step),
                    stream(), clip_total.has_value() ? clip_total->data_ptr<float>() : nullptr,
-                   static_cast<float>(clip_max));
+                   static_cast<float>(clip_max), reinterpret_cast<void* const*>(peer_bases.data()),
+                   static_cast<int>(peer_bases.size()));
 }
 
 std::vector<ttb::SumSqTensor> sq_list(const std::vector<Tensor>& xs) {
@@ -287,7 +292,23 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_bwd", &ce_bwd);
   m.def("adamw", &adamw, py::arg("params"), py::arg("grads"), py::arg("exp_avgs"), py::arg("exp_avg_sqs"),
         py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("weight_decay"), py::arg("step"),
-        py::arg("copies") = std::vector<Tensor>(), py::arg("clip_total") = py::none(), py::arg("clip_max") = 0.0);
+        py::arg("copies") = std::vector<Tensor>(), py::arg("clip_total") = py::none(), py::arg("clip_max") = 0.0,
+        py::arg("peer_offsets") = std::vector<int64_t>(), py::arg("peer_bases") = std::vector<int64_t>());
+  m.def("dp_reduce_scatter_bucket", [](std::vector<int64_t> grads, std::vector<int64_t> sigs, int rank,
+                                       int64_t off, int64_t len, Tensor out, double scale, int slot, int64_t epoch,
+                                       int ctas) {
+    TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous(), "out: fp32 CUDA");
+    TORCH_CHECK((int64_t)grads.size() == (int64_t)sigs.size(), "grads / signal pads differ");
+    c10::cuda::CUDAGuard g(out.device());
+    ttb::dp_reduce_scatter_bucket(reinterpret_cast<const void* const*>(grads.data()),
+                                  reinterpret_cast<uint32_t* const*>(sigs.data()), (int)grads.size(), rank, off, len,
+                                  out.data_ptr<float>(), (float)scale, slot, (uint32_t)epoch, ctas, stream());
+  });
+  m.def("dp_barrier", [](std::vector<int64_t> sigs, int rank, int slot, int64_t epoch) {
+    ttb::dp_barrier(reinterpret_cast<uint32_t* const*>(sigs.data()), (int)sigs.size(), rank, slot, (uint32_t)epoch,
+                    stream());
+  });
+  m.def("dp_error_code", &ttb::dp_error_code, py::arg("reset") = true);
   m.def("multi_sumsq", &multi_sumsq, "sum of squares over a list of fp32/bf16 tensors");
   m.def("multi_clip_scale", &multi_clip_scale, "scale tensors by min(1, max_norm/(sqrt(total)+1e-6))");
   m.def("attn_fwd", &attn_fwd);

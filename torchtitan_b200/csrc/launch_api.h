@@ -64,9 +64,18 @@ struct AdamWTensor {
   int p_dtype;  // 0 fp32, 1 bf16
   int g_dtype;
   void* p_copy = nullptr;  // optional bf16 copy of the updated fp32 param (compute weights)
+  int64_t peer_off = -1;   // >= 0: write the bf16 copy at this offset of every peer weight buffer
 };
 void adamw_multi(const AdamWTensor* host_list, int count, float lr, float beta1, float beta2, float eps, float wd,
-                 int step, cudaStream_t s, const float* clip_total = nullptr, float clip_max = 0.f);
+                 int step, cudaStream_t s, const float* clip_total = nullptr, float clip_max = 0.f,
+                 void* const* peer_bases = nullptr, int n_peers = 0);
+
+// dp_comm.cu: data-parallel collectives over NVLink peer memory
+void dp_reduce_scatter_bucket(const void* const* peer_grads, uint32_t* const* peer_sigs, int world, int rank,
+                              int64_t bucket_off, int64_t bucket_len, float* out_shard, float scale, int slot,
+                              uint32_t epoch, int num_ctas, cudaStream_t s);
+void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint32_t epoch, cudaStream_t s);
+int dp_error_code(bool reset);
 
 struct SumSqTensor {
   const void* x;
