@@ -63,6 +63,61 @@ def test_fsdp_gloo_training_and_resume():
         assert os.path.exists(os.path.join(d, "checkpoint", "step-4", ".metadata"))
 
 
+# ---------------------------------------------------------------- peer data parallel (host logic)
+def _train_peer_vs_fsdp(rank, world, out_dir):
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    def make(comm, steps, extra=()):
+        return Trainer(ConfigManager().parse_args([
+            "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", str(steps),
+            "--metrics.log-freq", "1", "--parallelism.data-parallel-comm", comm, "--dump-folder",
+            os.path.join(out_dir, comm), "--training.global-batch-size", "8", *extra]))
+
+    tf = make("fsdp2", 3)
+    tp = make("peer", 3, ("--checkpoint.enable", "--checkpoint.interval", "3"))
+    rt = tp.model_parts[0]._dp_runtime
+    assert rt.comm == "collective"
+    # identical starting weights: FSDP2's full state loaded through the checkpoint wrapper
+    full = get_model_state_dict(tf.model_parts[0], options=StateDictOptions(full_state_dict=True))
+    tp.checkpointer.states["model"].load_state_dict(full)
+    for t in (tf, tp):
+        t.train()
+    mf, mp_ = (t.metrics_processor.last_metrics for t in (tf, tp))
+    lf, lp = mf["loss_metrics/global_avg_loss"], mp_["loss_metrics/global_avg_loss"]
+    gf, gp = mf["grad_norm"], mp_["grad_norm"]
+    assert abs(lf - lp) < 1e-4 * max(1.0, abs(lf)), (lf, lp)
+    assert abs(gf - gp) < 1e-3 * max(1.0, abs(gf)), (gf, gp)
+    # the updated weights equal FSDP2's, and every rank holds the same copy
+    full = get_model_state_dict(tf.model_parts[0], options=StateDictOptions(full_state_dict=True))
+    for n, p in tp.model_parts[0].named_parameters():
+        n = n.replace("_checkpoint_wrapped_module.", "")
+        torch.testing.assert_close(p.detach(), full[n], rtol=1e-4, atol=1e-5)
+    w = rt.wbuf.clone()
+    ws = [torch.empty_like(w) for _ in range(world)]
+    dist.all_gather(ws, w)
+    assert torch.equal(ws[0], ws[1])
+    tf.close()
+    tp.close()
+    # resume: masters, moments and step count come back and the weights are rebuilt from them
+    t2 = make("peer", 4, ("--checkpoint.enable",))
+    rt2 = t2.model_parts[0]._dp_runtime
+    master_before = rt2.master.clone()
+    t2.checkpointer.load()
+    assert t2.step == 3 and t2.optimizers.optimizers[0].step_count == 3
+    assert torch.equal(rt2.master, rt.master) and not torch.equal(rt2.master, master_before)
+    assert torch.equal(rt2.wbuf, w)
+    torch.testing.assert_close(t2.optimizers.optimizers[0].exp_avg, tp.optimizers.optimizers[0].exp_avg)
+    t2.close()
+
+
+def test_peer_data_parallel_matches_fsdp2_and_resumes():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_train_peer_vs_fsdp, 2, d)
+
+
 # ---------------------------------------------------------------- Ulysses a2a
 def _ulysses(rank, world):
     from torchtitan_b200.ops import reference as R

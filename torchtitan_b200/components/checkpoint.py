@@ -64,6 +64,9 @@ class ModelWrapper(Stateful):
                     else:
                         rest[k] = v
             set_model_state_dict(m, rest, options=StateDictOptions(strict=False))
+            rt = getattr(m, "_dp_runtime", None)
+            if rt is not None:  # weights are views of the runtime's buffer; its masters follow them
+                rt.masters_from_weights()
 
 
 def _is_rank0() -> bool:

@@ -123,6 +123,65 @@ class AdamW(torch.optim.Optimizer):
         _load_keeping_fp32(self, state_dict)
 
 
+class PeerShardedAdamW(torch.optim.Optimizer):
+    """AdamW over the sharded fp32 state of a :class:`PeerDataParallel` runtime.
+
+    ``param_groups`` list the model's parameters (so LR schedulers work as
+    usual); the state is three flat fp32 shards (master, exp_avg, exp_avg_sq)
+    covering this rank's 1/W slice of every gradient bucket.  One fused kernel
+    updates them and writes the new bf16 weights into every rank's buffer."""
+
+    supports_fused_clip = True
+
+    def __init__(self, groups, runtime):
+        super().__init__(groups, {})
+        keys = ("lr", "betas", "eps", "weight_decay")
+        g0 = self.param_groups[0]
+        for g in self.param_groups[1:]:
+            if any(g[k] != g0[k] for k in keys):
+                raise ValueError("peer data parallelism runs one AdamW hyper-parameter set over the flat shard; "
+                                 "use data_parallel_comm='fsdp2' for per-group settings")
+        self.rt = runtime
+        self.exp_avg = torch.zeros_like(runtime.master)
+        self.exp_avg_sq = torch.zeros_like(runtime.master)
+        self.step_count = 0
+        self.pending_clip: tuple[torch.Tensor, float] | None = None
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = closure() if closure is not None else None
+        g = self.param_groups[0]
+        lr = float(g["lr"].item()) if torch.is_tensor(g["lr"]) else float(g["lr"])
+        self.step_count += 1
+        self.rt.adamw_step(self.exp_avg, self.exp_avg_sq, lr=lr, beta1=g["betas"][0], beta2=g["betas"][1],
+                           eps=g["eps"], weight_decay=g["weight_decay"], step=self.step_count, clip=self.pending_clip)
+        self.pending_clip = None
+        return loss
+
+    def zero_grad(self, set_to_none: bool = True):
+        pass  # gradients never stay on the parameters: the runtime's hooks move them into its buffers
+
+    def _dtensor(self, t: torch.Tensor):
+        from torch.distributed.tensor import DTensor, Shard
+
+        return DTensor.from_local(t.view(1, -1), self.rt.flat_mesh, [Shard(0)], run_check=False)
+
+    def flat_state_dict(self) -> dict[str, Any]:
+        return {"peer_dp.master": self._dtensor(self.rt.master), "peer_dp.exp_avg": self._dtensor(self.exp_avg),
+                "peer_dp.exp_avg_sq": self._dtensor(self.exp_avg_sq),
+                "peer_dp.step": torch.tensor(self.step_count, dtype=torch.int64)}
+
+    @torch.no_grad()
+    def load_flat_state_dict(self, sd: dict[str, Any]) -> None:
+        for key, t in (("master", self.rt.master), ("exp_avg", self.exp_avg), ("exp_avg_sq", self.exp_avg_sq)):
+            v = sd[f"peer_dp.{key}"]
+            v = v.to_local() if hasattr(v, "to_local") else v
+            if v.data_ptr() != t.data_ptr():
+                t.copy_(v.reshape(-1))
+        self.step_count = int(sd["peer_dp.step"])
+        self.rt.gather_weights()
+
+
 def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
     """Approximate the orthogonal polar factor of ``G`` (Muon's quintic
     Newton-Schulz iteration, coefficients from Jordan et al. 2024)."""
@@ -323,6 +382,15 @@ class OptimizersContainer(Stateful, Configurable):
         c = self.config
         base = dict(lr=c.lr, betas=(c.beta1, c.beta2), eps=c.eps, weight_decay=c.weight_decay)
         groups = self._groups(model, base)
+        rt = getattr(model, "_dp_runtime", None)
+        if rt is not None:
+            if c.name not in ("AdamW", "Adam"):
+                raise NotImplementedError(f"peer data parallelism runs AdamW/Adam, not {c.name}; "
+                                          "use data_parallel_comm='fsdp2'")
+            for g in groups:
+                g["params"] = [p for _, p in g["params"]]
+                g["weight_decay"] *= 1.0 if c.name == "AdamW" else 0.0
+            return PeerShardedAdamW(groups, rt)
         if c.name in ("AdamW", "Adam"):
             wd_scale = 1.0 if c.name == "AdamW" else 0.0
             for g in groups:
@@ -380,14 +448,17 @@ class OptimizersContainer(Stateful, Configurable):
         fn = functools.partial(get_optimizer_state_dict, options=StateDictOptions(flatten_optimizer_state_dict=True))
         out: dict[str, Any] = {}
         for m, o in zip(self.model_parts, self.optimizers):
-            out.update(fn(m, o))
+            out.update(o.flat_state_dict() if hasattr(o, "flat_state_dict") else fn(m, o))
         return out
 
     def load_state_dict(self, sd: dict[str, Any]) -> None:
         fn = functools.partial(set_optimizer_state_dict, optim_state_dict=sd,
                                options=StateDictOptions(flatten_optimizer_state_dict=True))
         for m, o in zip(self.model_parts, self.optimizers):
-            fn(m, o)
+            if hasattr(o, "load_flat_state_dict"):
+                o.load_flat_state_dict(sd)
+            else:
+                fn(m, o)
 
 
 def build_optimizers_with_moe_load_balancing(optimizers: OptimizersContainer, model_parts: list[nn.Module],

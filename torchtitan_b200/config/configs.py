@@ -55,6 +55,11 @@ class ParallelismConfig:
     expert_tensor_parallel_degree: int = 1
     expert_parallel_comm_backend: Literal["standard", "fused"] = "standard"
     """``standard`` = NCCL all-to-all; ``fused`` = peer-memory dispatch/combine kernels."""
+    data_parallel_comm: Literal["auto", "fsdp2", "peer"] = "auto"
+    """Pure data parallelism: ``peer`` = replicated bf16 weights + sharded optimizer with
+    reduce-scatter / all-gather kernels over NVLink peer memory; ``fsdp2`` = FSDP2 over
+    NCCL; ``auto`` = ``peer`` on one node of CUDA devices, else ``fsdp2``."""
+    data_parallel_bucket_mb: int = 256
 
 
 @dataclass(kw_only=True, slots=True)

@@ -304,10 +304,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                                   reinterpret_cast<uint32_t* const*>(sigs.data()), (int)grads.size(), rank, off, len,
                                   out.data_ptr<float>(), (float)scale, slot, (uint32_t)epoch, ctas, stream());
   });
-  m.def("dp_barrier", [](std::vector<int64_t> sigs, int rank, int slot, int64_t epoch) {
-    ttb::dp_barrier(reinterpret_cast<uint32_t* const*>(sigs.data()), (int)sigs.size(), rank, slot, (uint32_t)epoch,
-                    stream());
-  });
+  m.def(
+      "dp_barrier",
+      [](std::vector<int64_t> sigs, int rank, int slot, int64_t epoch, double limit_s) {
+        ttb::dp_barrier(reinterpret_cast<uint32_t* const*>(sigs.data()), (int)sigs.size(), rank, slot,
+                        (uint32_t)epoch, stream(), limit_s);
+      },
+      py::arg("sigs"), py::arg("rank"), py::arg("slot"), py::arg("epoch"), py::arg("limit_s") = 0.0);
   m.def("dp_error_code", &ttb::dp_error_code, py::arg("reset") = true);
   m.def("multi_sumsq", &multi_sumsq, "sum of squares over a list of fp32/bf16 tensors");
   m.def("multi_clip_scale", &multi_clip_scale, "scale tensors by min(1, max_norm/(sqrt(total)+1e-6))");

@@ -10,7 +10,7 @@
 // * dp_barrier: epoch barrier across the W ranks through the same flags (used
 //   after the optimizer's P2P stores of updated weights).
 // Flags are uint32 epochs in each rank's signal pad; every wait gives up after
-// ~2 s, records an error code readable by dp_error_code() and returns.
+// ~20 s, records an error code readable by dp_error_code() and returns.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -20,13 +20,15 @@ namespace ttb {
 namespace dp_impl {
 
 __device__ int g_err;
-constexpr uint64_t kLimitNs = 2000000000ull;
+// generous: ranks may drift apart by a data-loader hiccup, a checkpoint write or a slow first step
+constexpr uint64_t kDefaultLimitNs = 20000000000ull;
 constexpr int kMaxWorld = 8;
 
 struct PeerTable {
   const __nv_bfloat16* g[kMaxWorld];  // each rank's flat gradient buffer
   uint32_t* sig[kMaxWorld];           // each rank's signal pad (uint32 slots)
   int world, rank;
+  uint64_t limit_ns;  // give up a wait after this long
 };
 
 __device__ __forceinline__ uint64_t now_ns() {
@@ -50,6 +52,7 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
 
 // slot layout in each signal pad: [slot_base + bucket * W + src_rank]
 __device__ bool signal_and_wait(const PeerTable& t, int slot, uint32_t epoch, int code) {
+  const uint64_t limit = t.limit_ns;
   __shared__ int ok;
   if (threadIdx.x == 0) ok = 1;
   __syncthreads();
@@ -62,7 +65,7 @@ __device__ bool signal_and_wait(const PeerTable& t, int slot, uint32_t epoch, in
     const uint64_t t0 = now_ns();
     for (int j = 0; j < t.world; ++j) {
       while (static_cast<int32_t>(ld_acquire_sys(mine + j) - epoch) < 0) {
-        if (now_ns() - t0 > kLimitNs) {
+        if (now_ns() - t0 > limit) {
           atomicCAS(&g_err, 0, code);
           ok = 0;
           j = t.world;
@@ -83,10 +86,17 @@ __global__ void __launch_bounds__(256) rs_bucket_kernel(PeerTable t, int64_t buc
   const int64_t n8 = shard_len / 8;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < t.world; ++j) {
+    uint4 v[kMaxWorld];
+    // issue every peer's 16-byte load before consuming any: W requests in flight per thread
+#pragma unroll
+    for (int j = 0; j < kMaxWorld; ++j) {
       const int src = (t.rank + j) % t.world;  // stagger sources across ranks
-      const uint4 v = ld_cg_v4(t.g[src] + base + i * 8);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+      if (j < t.world) v[j] = ld_cg_v4(t.g[src] + base + i * 8);
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxWorld; ++j) {
+      if (j >= t.world) break;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v[j]);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const float2 f = __bfloat1622float2(h[u]);
@@ -102,7 +112,7 @@ __global__ void __launch_bounds__(256) rs_bucket_kernel(PeerTable t, int64_t buc
 
 __global__ void dp_barrier_kernel(PeerTable t, int slot, uint32_t epoch) { signal_and_wait(t, slot, epoch, 72); }
 
-PeerTable make_table(const void* const* grads, uint32_t* const* sigs, int world, int rank) {
+PeerTable make_table(const void* const* grads, uint32_t* const* sigs, int world, int rank, double limit_s) {
   if (world < 1 || world > kMaxWorld) throw std::runtime_error("dp: world size must be 1..8");
   PeerTable t;
   for (int j = 0; j < kMaxWorld; ++j) {
@@ -111,6 +121,7 @@ PeerTable make_table(const void* const* grads, uint32_t* const* sigs, int world,
   }
   t.world = world;
   t.rank = rank;
+  t.limit_ns = limit_s > 0 ? static_cast<uint64_t>(limit_s * 1e9) : kDefaultLimitNs;
   return t;
 }
 
@@ -121,14 +132,15 @@ void dp_reduce_scatter_bucket(const void* const* peer_grads, uint32_t* const* pe
                               uint32_t epoch, int num_ctas, cudaStream_t s) {
   using namespace dp_impl;
   if (bucket_len % (8 * world)) throw std::runtime_error("dp: bucket length must be a multiple of 8 * world");
-  const PeerTable t = make_table(peer_grads, peer_sigs, world, rank);
+  const PeerTable t = make_table(peer_grads, peer_sigs, world, rank, 0.0);
   rs_bucket_kernel<<<num_ctas, 256, 0, s>>>(t, bucket_off, bucket_len / world, out_shard, scale, slot, epoch);
   check_cuda(cudaGetLastError(), "dp rs launch");
 }
 
-void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint32_t epoch, cudaStream_t s) {
+void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint32_t epoch, cudaStream_t s,
+                double limit_s) {
   using namespace dp_impl;
-  const PeerTable t = make_table(nullptr, peer_sigs, world, rank);
+  const PeerTable t = make_table(nullptr, peer_sigs, world, rank, limit_s);
   dp_barrier_kernel<<<1, 32, 0, s>>>(t, slot, epoch);
   check_cuda(cudaGetLastError(), "dp barrier launch");
 }

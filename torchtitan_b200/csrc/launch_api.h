@@ -74,7 +74,8 @@ void adamw_multi(const AdamWTensor* host_list, int count, float lr, float beta1,
 void dp_reduce_scatter_bucket(const void* const* peer_grads, uint32_t* const* peer_sigs, int world, int rank,
                               int64_t bucket_off, int64_t bucket_len, float* out_shard, float scale, int slot,
                               uint32_t epoch, int num_ctas, cudaStream_t s);
-void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint32_t epoch, cudaStream_t s);
+void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint32_t epoch, cudaStream_t s,
+                double limit_s = 0.0);
 int dp_error_code(bool reset);
 
 struct SumSqTensor {

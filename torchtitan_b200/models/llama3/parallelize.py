@@ -14,6 +14,7 @@ from torchtitan_b200.parallel.fsdp import (
     apply_replica_mixed_precision,
     replica_mixed_precision_applicable,
 )
+from torchtitan_b200.parallel.peer_dp import apply_peer_dp, peer_dp_applicable
 from torchtitan_b200.parallel.tensor_parallel import apply_tp_llama, maybe_enable_async_tp
 from torchtitan_b200.utils.logging import logger
 
@@ -37,7 +38,12 @@ def parallelize_llama(model: nn.Module, *, parallel_dims: Any, training: Any, mo
     if ac_config.mode != "none":
         apply_ac(model, ac_config)
         logger.info(f"applied {ac_config.mode} activation checkpointing")
-    if replica_mixed_precision_applicable(parallel_dims, training):
+    if peer_dp_applicable(parallel_dims, training, parallelism):
+        names = ["dp_replicate", "fsdp"] if parallel_dims.dp_replicate_enabled else ["fsdp"]
+        apply_peer_dp(model, parallel_dims.get_mesh(names if len(names) > 1 else names[0]),
+                      bucket_mb=parallelism.data_parallel_bucket_mb)
+        logger.info("data parallel: replicated bf16 weights, sharded fp32 optimizer, peer-memory collectives")
+    elif replica_mixed_precision_applicable(parallel_dims, training):
         apply_replica_mixed_precision(model)
         logger.info("single replica: bf16 compute weights with fp32 masters in the optimizer (no FSDP wrap)")
     else:

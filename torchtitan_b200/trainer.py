@@ -169,9 +169,9 @@ class Trainer(Stateful, Configurable):
             model.to_empty(device=init_device)
             with torch.no_grad():
                 model.init_weights(buffer_device=None)
-            from torchtitan_b200.parallel.fsdp import materialize_replica_mixed_precision
+            from torchtitan_b200.parallel.peer_dp import materialize_data_parallel
 
-            materialize_replica_mixed_precision(model)
+            materialize_data_parallel(model)
             model.train()
             self.model_parts = [model]
             self.pp_has_first_stage = self.pp_has_last_stage = True
@@ -283,7 +283,10 @@ class Trainer(Stateful, Configurable):
         local_valid_t = torch.tensor(float(local_valid), device=self.device)
         global_valid = dist_utils.dist_sum(local_valid_t, pd.get_mesh("batch")) if pd.dp_enabled else local_valid_t
         losses = []
-        for inp, labels in mbs:
+        dp_rt = getattr(self.model_parts[0], "_dp_runtime", None)
+        for i, (inp, labels) in enumerate(mbs):
+            if dp_rt is not None:
+                dp_rt.begin_microbatch(i, len(mbs))
             inp = {k: (v.to(self.device, non_blocking=True) if torch.is_tensor(v) else v) for k, v in inp.items()}
             labels = labels.to(self.device, non_blocking=True)
             losses.append(self.forward_backward_step(input_dict=inp, labels=labels,
@@ -291,10 +294,19 @@ class Trainer(Stateful, Configurable):
         max_norm = self.config.training.max_norm
         fused_clip = max_norm > 0 and all(getattr(o, "supports_fused_clip", False)
                                           for o in self.optimizers.optimizers)
-        clip = dist_utils.clip_grad_norm_([p for m in self.model_parts for p in m.parameters()], max_norm,
-                                          pp_mesh=pd.get_optional_mesh("pp"), ep_enabled=pd.ep_enabled,
-                                          defer_scaling=fused_clip)
-        if fused_clip:
+        if dp_rt is not None:
+            # gradients live in the data-parallel runtime's fp32 shards
+            dp_rt.finish_backward()
+            total = dp_rt.grad_sumsq()
+            clip = (total.sqrt(), total)
+            fused_clip = max_norm > 0
+        else:
+            clip = dist_utils.clip_grad_norm_([p for m in self.model_parts for p in m.parameters()], max_norm,
+                                              pp_mesh=pd.get_optional_mesh("pp"), ep_enabled=pd.ep_enabled,
+                                              defer_scaling=fused_clip)
+        if dp_rt is not None and not fused_clip:
+            grad_norm = clip[0]
+        elif fused_clip:
             grad_norm, total = clip
             for o in self.optimizers.optimizers:
                 o.pending_clip = (total, max_norm)
@@ -307,6 +319,8 @@ class Trainer(Stateful, Configurable):
         self.last_loss = loss
         if not self.metrics_processor.should_log(self.step):
             return loss
+        if dp_rt is not None:
+            dp_rt.check()
         if pd.dp_cp_enabled:
             mesh = pd.get_optional_mesh("loss")
             avg = float(dist_utils.dist_sum(loss, mesh))
