@@ -201,7 +201,10 @@ def run_ours(a):
         "dtype": "bf16",
         "data": "synthetic uniform tokens, random-init weights",
         "config": {"model": f"llama3_{a.flavor}", "global_batch": world, "seq_len": a.seq_len,
-                   "parallelism": f"fsdp{world}", "ac": a.ac, "optimizer": "AdamW (fused, fp32 master)",
+                   "parallelism": (f"dp{world} (replicated bf16 weights, sharded fp32 AdamW, peer-memory reduce-scatter"
+                                   " and optimizer-fused all-gather)"
+                                   if getattr(trainer.model_parts[0], "_dp_runtime", None) is not None
+                                   else f"fsdp{world}"), "ac": a.ac, "optimizer": "AdamW (fused, fp32 master)",
                    "l2": "inputs larger than L2 (no flush)"},
         "mfu_pct": round(mfu, 2),
         "tokens_per_sec_per_gpu": round(value / world, 1),

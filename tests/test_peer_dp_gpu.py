@@ -98,21 +98,33 @@ def test_peer_reduce_scatter_and_fused_all_gather():
 
 
 def _trainer(rank, world, out_dir):
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
     from torchtitan_b200.config.manager import ConfigManager
     from torchtitan_b200.trainer import Trainer
 
-    res = {}
-    for comm in ("fsdp2", "peer"):
-        t = Trainer(ConfigManager().parse_args([
+    def make(comm):
+        return Trainer(ConfigManager().parse_args([
             "--module", "llama3", "--config", "llama3_debugmodel", "--training.steps", "6",
             "--metrics.log-freq", "1", "--parallelism.data-parallel-comm", comm, "--dump-folder",
             os.path.join(out_dir, comm), "--training.global-batch-size", "16"]))
-        assert (getattr(t.model_parts[0], "_dp_runtime", None) is not None) == (comm == "peer")
+
+    tf, tp = make("fsdp2"), make("peer")
+    assert getattr(tf.model_parts[0], "_dp_runtime", None) is None
+    assert tp.model_parts[0]._dp_runtime.comm == "peer"
+    full = get_model_state_dict(tf.model_parts[0], options=StateDictOptions(full_state_dict=True))
+    tp.checkpointer.states["model"].load_state_dict(full)  # same starting weights
+    res = {}
+    for name, t in (("fsdp2", tf), ("peer", tp)):
         t.train()
-        res[comm] = t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"]
-        t.close()
-    # different initial weights (FSDP2 initializes sharded); both must train to a similar loss
-    assert res["peer"] < 7.5 and abs(res["peer"] - res["fsdp2"]) < 0.5, res
+        m = t.metrics_processor.last_metrics
+        res[name] = (m["loss_metrics/global_avg_loss"], m["grad_norm"])
+    # bf16 compute on both sides: FSDP2 reduces in fp32, the peer kernel sums bf16 grads in fp32
+    assert abs(res["peer"][0] - res["fsdp2"][0]) < 2e-2, res
+    assert abs(res["peer"][1] - res["fsdp2"][1]) < 5e-2 * res["fsdp2"][1], res
+    tp.model_parts[0]._dp_runtime.check()
+    tf.close()
+    tp.close()
 
 
 @two_gpus
