@@ -22,8 +22,10 @@ _GLOO = False
 def _disable_grad_division(m) -> None:
     # gloo has no PREMUL_SUM: keep FSDP's mean there and let the trainer scale
     # the backward seed by the DP size instead (model._fsdp_grad_compensation)
-    if not _GLOO and hasattr(m, "set_gradient_divide_factor"):
-        m.set_gradient_divide_factor(1.0)
+    # (fully_shard of a list of modules returns the list: each is an FSDP module)
+    for mod in (m if isinstance(m, (list, tuple)) else [m]):
+        if not _GLOO and hasattr(mod, "set_gradient_divide_factor"):
+            mod.set_gradient_divide_factor(1.0)
 
 
 def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, reduce_dtype: torch.dtype,
