@@ -296,13 +296,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("peer_offsets") = std::vector<int64_t>(), py::arg("peer_bases") = std::vector<int64_t>());
   m.def("dp_reduce_scatter_bucket", [](std::vector<int64_t> grads, std::vector<int64_t> sigs, int rank,
                                        int64_t off, int64_t len, Tensor out, double scale, int slot, int64_t epoch,
-                                       int ctas) {
+                                       int ctas, double limit_s) {
     TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous(), "out: fp32 CUDA");
     TORCH_CHECK((int64_t)grads.size() == (int64_t)sigs.size(), "grads / signal pads differ");
     c10::cuda::CUDAGuard g(out.device());
     ttb::dp_reduce_scatter_bucket(reinterpret_cast<const void* const*>(grads.data()),
                                   reinterpret_cast<uint32_t* const*>(sigs.data()), (int)grads.size(), rank, off, len,
-                                  out.data_ptr<float>(), (float)scale, slot, (uint32_t)epoch, ctas, stream());
+                                  out.data_ptr<float>(), (float)scale, slot, (uint32_t)epoch, ctas, stream(),
+                                  limit_s);
   });
   m.def(
       "dp_barrier",
@@ -312,6 +313,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       },
       py::arg("sigs"), py::arg("rank"), py::arg("slot"), py::arg("epoch"), py::arg("limit_s") = 0.0);
   m.def("dp_error_code", &ttb::dp_error_code, py::arg("reset") = true);
+  m.def("dp_error_info", []() {
+    int v[4];
+    ttb::dp_error_info(v);
+    return std::vector<int>(v, v + 4);
+  });
   m.def("multi_sumsq", &multi_sumsq, "sum of squares over a list of fp32/bf16 tensors");
   m.def("multi_clip_scale", &multi_clip_scale, "scale tensors by min(1, max_norm/(sqrt(total)+1e-6))");
   m.def("attn_fwd", &attn_fwd);

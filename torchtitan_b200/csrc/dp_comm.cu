@@ -20,6 +20,7 @@ namespace ttb {
 namespace dp_impl {
 
 __device__ int g_err;
+__device__ int g_err_info[4];  // slot, epoch awaited, source rank, value seen (first failure)
 // generous: ranks may drift apart by a data-loader hiccup, a checkpoint write or a slow first step
 constexpr uint64_t kDefaultLimitNs = 20000000000ull;
 constexpr int kMaxWorld = 8;
@@ -66,7 +67,12 @@ __device__ bool signal_and_wait(const PeerTable& t, int slot, uint32_t epoch, in
     for (int j = 0; j < t.world; ++j) {
       while (static_cast<int32_t>(ld_acquire_sys(mine + j) - epoch) < 0) {
         if (now_ns() - t0 > limit) {
-          atomicCAS(&g_err, 0, code);
+          if (atomicCAS(&g_err, 0, code) == 0) {
+            g_err_info[0] = slot;
+            g_err_info[1] = static_cast<int>(epoch);
+            g_err_info[2] = j;
+            g_err_info[3] = static_cast<int>(ld_acquire_sys(mine + j));
+          }
           ok = 0;
           j = t.world;
           break;
@@ -129,10 +135,10 @@ PeerTable make_table(const void* const* grads, uint32_t* const* sigs, int world,
 
 void dp_reduce_scatter_bucket(const void* const* peer_grads, uint32_t* const* peer_sigs, int world, int rank,
                               int64_t bucket_off, int64_t bucket_len, float* out_shard, float scale, int slot,
-                              uint32_t epoch, int num_ctas, cudaStream_t s) {
+                              uint32_t epoch, int num_ctas, cudaStream_t s, double limit_s) {
   using namespace dp_impl;
   if (bucket_len % (8 * world)) throw std::runtime_error("dp: bucket length must be a multiple of 8 * world");
-  const PeerTable t = make_table(peer_grads, peer_sigs, world, rank, 0.0);
+  const PeerTable t = make_table(peer_grads, peer_sigs, world, rank, limit_s);
   rs_bucket_kernel<<<num_ctas, 256, 0, s>>>(t, bucket_off, bucket_len / world, out_shard, scale, slot, epoch);
   check_cuda(cudaGetLastError(), "dp rs launch");
 }
@@ -143,6 +149,10 @@ void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint3
   const PeerTable t = make_table(nullptr, peer_sigs, world, rank, limit_s);
   dp_barrier_kernel<<<1, 32, 0, s>>>(t, slot, epoch);
   check_cuda(cudaGetLastError(), "dp barrier launch");
+}
+
+void dp_error_info(int* out4) {
+  check_cuda(cudaMemcpyFromSymbol(out4, dp_impl::g_err_info, 4 * sizeof(int)), "dp error info read");
 }
 
 int dp_error_code(bool reset) {

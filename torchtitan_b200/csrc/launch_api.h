@@ -73,10 +73,11 @@ void adamw_multi(const AdamWTensor* host_list, int count, float lr, float beta1,
 // dp_comm.cu: data-parallel collectives over NVLink peer memory
 void dp_reduce_scatter_bucket(const void* const* peer_grads, uint32_t* const* peer_sigs, int world, int rank,
                               int64_t bucket_off, int64_t bucket_len, float* out_shard, float scale, int slot,
-                              uint32_t epoch, int num_ctas, cudaStream_t s);
+                              uint32_t epoch, int num_ctas, cudaStream_t s, double limit_s = 0.0);
 void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint32_t epoch, cudaStream_t s,
                 double limit_s = 0.0);
 int dp_error_code(bool reset);
+void dp_error_info(int* out4);  // slot, epoch, source rank, flag value of the first failed wait
 
 struct SumSqTensor {
   const void* x;

@@ -27,6 +27,7 @@ everything else — layout, hooks, buckets, optimizer, checkpoint — is shared.
 from __future__ import annotations
 
 import dataclasses
+import os
 from typing import Any
 
 import torch
@@ -88,10 +89,10 @@ def peer_dp_applicable(parallel_dims: Any, training: Any, parallelism: Any) -> b
         if not pure_dp:
             raise ValueError("data_parallel_comm='peer' supports pure data parallelism only")
         return True
-    import os
-
     one_node = int(os.environ.get("LOCAL_WORLD_SIZE", parallel_dims.world_size)) == parallel_dims.world_size
-    return (pure_dp and one_node and parallel_dims.world_size <= 8 and torch.cuda.is_available()
+    # 8 ranks: a run of the 8B bench stalled at its second step (cause not yet found), so
+    # ``auto`` keeps FSDP2 there; ``peer`` still selects this runtime explicitly
+    return (pure_dp and one_node and parallel_dims.world_size <= 4 and torch.cuda.is_available()
             and training.mixed_precision_param == "bfloat16" and training.dtype == "float32"
             and not training.enable_cpu_offload)
 
@@ -130,6 +131,8 @@ class PeerDataParallel:
                                                              bucket_mb * 2**20 // elem)
         self.shard_total = self.total // self.world
         self.epoch = 0
+        # a wait for the other ranks gives up after this long (error code readable by check())
+        self.wait_limit_s = float(os.environ.get("TTB_DP_WAIT_S", "20"))
         self.sync = True
         self._got: list[bool] = []
         self._first_micro = True
@@ -148,8 +151,6 @@ class PeerDataParallel:
     def _alloc_buffers(self) -> None:
         dev, n = self.device, self.total
         if self.comm == "peer":
-            import os
-
             # these buffers are read and written with plain peer loads/stores only
             os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
             from torch.distributed import _symmetric_memory as symm
@@ -243,7 +244,7 @@ class PeerDataParallel:
             self._stream.wait_stream(cur)
             with torch.cuda.stream(self._stream):
                 self._ext.dp_reduce_scatter_bucket(self.g_ptrs, self.f_ptrs, self.rank, b.offset, b.length, out,
-                                                   1.0, b.index, self.epoch + 1, 64)
+                                                   1.0, b.index, self.epoch + 1, 64, self.wait_limit_s)
         else:
             full = self.gbuf[b.offset:b.offset + b.length].float()
             dist.all_reduce(full, group=self.group)
@@ -320,16 +321,19 @@ class PeerDataParallel:
     def barrier(self) -> None:
         if self.comm == "peer":
             self.epoch_barrier_count = getattr(self, "epoch_barrier_count", 0) + 1
-            self._ext.dp_barrier(self.f_ptrs, self.rank, len(self.buckets), self.epoch_barrier_count)
+            self._ext.dp_barrier(self.f_ptrs, self.rank, len(self.buckets), self.epoch_barrier_count,
+                                 limit_s=self.wait_limit_s)
         else:
             dist.barrier(group=self.group)
 
     def check(self) -> None:
         """Raise if a peer wait gave up (a rank stopped answering) since the last check."""
         if self.comm == "peer":
+            info = self._ext.dp_error_info()
             code = self._ext.dp_error_code(True)
             if code:
-                raise RuntimeError(f"peer data parallel: a wait for the other ranks timed out (code {code})")
+                raise RuntimeError(f"peer data parallel: a wait for the other ranks timed out (code {code}; slot "
+                                   f"{info[0]}, epoch {info[1]}, source rank {info[2]}, flag seen {info[3]})")
 
 
 @torch.no_grad()
