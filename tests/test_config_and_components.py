@@ -217,3 +217,26 @@ def test_fused_clip_matches_explicit_clip():
     o2.pending_clip = (total, 1.0)
     o2.step()
     assert torch.allclose(p1, p2, atol=1e-6) and o2.pending_clip is None
+
+
+def test_optimizer_step_in_backward_matches_regular_step(tmp_path):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    def run(extra):
+        cfg = ConfigManager().parse_args(["--module", "llama3", "--config", "llama3_debugmodel", "--training.steps",
+                                          "3", "--training.seq-len", "128", "--training.local-batch-size", "2",
+                                          "--training.dtype", "float32", "--training.mixed-precision-param",
+                                          "float32", "--training.max-norm", "0", "--activation-checkpoint.mode",
+                                          "none", "--dump-folder", str(tmp_path), *extra])
+        torch.manual_seed(0)
+        t = Trainer(cfg)
+        t.train()
+        w = {n: p.detach().clone() for n, p in t.model_parts[0].named_parameters()}
+        t.close()
+        return w
+
+    a = run([])
+    b = run(["--optimizer.early-step-in-backward"])
+    for n in a:
+        torch.testing.assert_close(a[n], b[n], rtol=1e-5, atol=1e-6)

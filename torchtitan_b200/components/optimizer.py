@@ -347,6 +347,10 @@ class OptimizersContainer(Stateful, Configurable):
         muon_exclude_patterns: list[str] = field(
             default_factory=lambda: ["tok_embeddings", "embed_tokens", "output", "lm_head", "norm", "router", "bias"]
         )
+        early_step_in_backward: bool = False
+        """Step each parameter inside backward, as soon as its gradient is accumulated, and free
+        the gradient right away (the reference's ``OptimizersInBackwardContainer``): gradient
+        memory drops to one parameter's worth; no gradient clipping, no gradient accumulation."""
 
     def __init__(self, config: Config, *, model_parts: list[nn.Module], **kw: Any):
         self.config = config
@@ -354,8 +358,33 @@ class OptimizersContainer(Stateful, Configurable):
         self.optimizers: list[torch.optim.Optimizer] = []
         self._pre_hooks: list[Any] = []
         self._post_hooks: list[Any] = []
+        self._parts_of: list[nn.Module] = []  # model part of each optimizer (state-dict flattening)
+        if config.early_step_in_backward:
+            self._build_in_backward(model_parts)
+            return
         for m in model_parts:
             self.optimizers.append(self._build_one(m))
+            self._parts_of.append(m)
+
+    def _build_in_backward(self, model_parts: list[nn.Module]) -> None:
+        """One optimizer per parameter, stepped from its post-accumulate-grad hook
+        (parity: ``components/optimizer.py:277-335`` of the reference)."""
+        if self.config.name not in ("AdamW", "Adam"):
+            raise NotImplementedError("early_step_in_backward supports AdamW/Adam")
+        for m in model_parts:
+            opt = self._build_one(m)
+            for g in opt.param_groups:
+                hp = {k: v for k, v in g.items() if k != "params"}
+                for p in g["params"]:
+                    single = type(opt)([{"params": [p], **hp}], **({"fused": True} if isinstance(opt, AdamW) else {}))
+                    self.optimizers.append(single)
+                    self._parts_of.append(m)
+
+                    def hook(param, _o=single):
+                        _o.step()
+                        _o.zero_grad(set_to_none=True)
+
+                    p.register_post_accumulate_grad_hook(hook)
 
     def _groups(self, model: nn.Module, base: dict[str, Any]) -> list[dict[str, Any]]:
         pats = [re.compile(pg.pattern) for pg in self.config.param_groups]
@@ -435,8 +464,9 @@ class OptimizersContainer(Stateful, Configurable):
     def step(self, *args, **kwargs) -> None:
         for h in self._pre_hooks:
             h(self, args, kwargs)
-        for o in self.optimizers:
-            o.step(*args, **kwargs)
+        if not self.config.early_step_in_backward:  # else every parameter already stepped in backward
+            for o in self.optimizers:
+                o.step(*args, **kwargs)
         for h in self._post_hooks:
             h(self, args, kwargs)
 
@@ -447,6 +477,10 @@ class OptimizersContainer(Stateful, Configurable):
     def state_dict(self) -> dict[str, Any]:
         fn = functools.partial(get_optimizer_state_dict, options=StateDictOptions(flatten_optimizer_state_dict=True))
         out: dict[str, Any] = {}
+        if self.config.early_step_in_backward:
+            for m in self.model_parts:
+                out.update(fn(m, [o for o, part in zip(self.optimizers, self._parts_of) if part is m]))
+            return out
         for m, o in zip(self.model_parts, self.optimizers):
             out.update(o.flat_state_dict() if hasattr(o, "flat_state_dict") else fn(m, o))
         return out
@@ -454,6 +488,10 @@ class OptimizersContainer(Stateful, Configurable):
     def load_state_dict(self, sd: dict[str, Any]) -> None:
         fn = functools.partial(set_optimizer_state_dict, optim_state_dict=sd,
                                options=StateDictOptions(flatten_optimizer_state_dict=True))
+        if self.config.early_step_in_backward:
+            for m in self.model_parts:
+                fn(m, [o for o, part in zip(self.optimizers, self._parts_of) if part is m])
+            return
         for m, o in zip(self.model_parts, self.optimizers):
             if hasattr(o, "load_flat_state_dict"):
                 o.load_flat_state_dict(sd)

@@ -145,6 +145,8 @@ class Trainer(Stateful, Configurable):
         if gbs % (c.training.local_batch_size * dp_degree):
             raise ValueError("global_batch_size must be a multiple of local_batch_size * dp degree")
         self.gradient_accumulation_steps = gbs // (c.training.local_batch_size * dp_degree)
+        if c.optimizer.early_step_in_backward and (self.gradient_accumulation_steps > 1 or pd.pp_enabled):
+            raise ValueError("optimizer.early_step_in_backward needs one microbatch per step and no PP")
 
         init_device = "cpu" if c.checkpoint.create_seed_checkpoint else self.device.type
         if pd.pp_enabled:
@@ -292,6 +294,8 @@ class Trainer(Stateful, Configurable):
             losses.append(self.forward_backward_step(input_dict=inp, labels=labels,
                                                      global_valid_tokens=global_valid).detach())
         max_norm = self.config.training.max_norm
+        if self.optimizers.config.early_step_in_backward:
+            max_norm = 0.0  # parameters already stepped inside backward: nothing left to clip
         fused_clip = max_norm > 0 and all(getattr(o, "supports_fused_clip", False)
                                           for o in self.optimizers.optimizers)
         if dp_rt is not None:
