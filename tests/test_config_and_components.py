@@ -240,3 +240,54 @@ def test_optimizer_step_in_backward_matches_regular_step(tmp_path):
     b = run(["--optimizer.early-step-in-backward"])
     for n in a:
         torch.testing.assert_close(a[n], b[n], rtol=1e-5, atol=1e-6)
+
+
+def test_mx_quantize_rceil_blocks():
+    from torchtitan_b200.ops.quant import mx_dequantize, mx_quantize
+
+    torch.manual_seed(0)
+    x = torch.randn(4, 64) * torch.logspace(-3, 3, 64)
+    q, s = mx_quantize(x)
+    assert q.dtype == torch.float8_e4m3fn and s.shape == (4, 2)
+    amax = x.view(4, 2, 32).abs().amax(-1)
+    exp = s.float() - 127
+    assert torch.all(amax / torch.exp2(exp) <= 448) and torch.all(amax / torch.exp2(exp - 1) > 448)
+    back = mx_dequantize(q, s, torch.float32)
+    rel = ((back - x).abs() / x.view(4, 2, 32).abs().amax(-1).repeat_interleave(32, 1)).max()
+    assert rel < 2 ** -3  # e4m3 has 3 mantissa bits
+
+
+@pytest.mark.parametrize("names", [["mxfp8"], ["float8"], ["float8_rowwise"], ["float8_rowwise_with_gw_hp"]])
+def test_quantized_training_converters(names, tmp_path):
+    from torchtitan_b200.components.quantization.float8 import Float8Linear
+    from torchtitan_b200.components.quantization.mx import MXFP8Linear
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    cfg = ConfigManager().parse_args(["--module", "llama3", "--config", "llama3_debugmodel", "--training.steps", "3",
+                                      "--training.seq-len", "128", "--training.local-batch-size", "2",
+                                      "--training.dtype", "float32", "--training.mixed-precision-param", "float32",
+                                      "--activation-checkpoint.mode", "none", "--dump-folder", str(tmp_path),
+                                      "--model-converters.names", *names])
+    t = Trainer(cfg)
+    cls = MXFP8Linear if names == ["mxfp8"] else Float8Linear
+    lins = [m for m in t.model_parts[0].modules() if isinstance(m, cls)]
+    assert len(lins) == 6 * 7 and type(t.model_parts[0].output) is not cls  # output head excluded
+    t.train()
+    loss = t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"]
+    assert 6.0 < loss < 9.0
+    t.close()
+
+
+def test_mx_linear_gradients_close_to_bf16():
+    from torchtitan_b200.components.quantization.mx import _MXLinearFn
+
+    torch.manual_seed(0)
+    x = torch.randn(64, 128, requires_grad=True)
+    w = torch.randn(96, 128, requires_grad=True)
+    y = _MXLinearFn.apply(x, w)
+    y.square().sum().backward()
+    x2, w2 = x.detach().requires_grad_(), w.detach().requires_grad_()
+    (x2 @ w2.t()).square().sum().backward()
+    for a, b in ((y, x2 @ w2.t()), (x.grad, x2.grad), (w.grad, w2.grad)):
+        assert ((a - b).norm() / b.norm()) < 0.08

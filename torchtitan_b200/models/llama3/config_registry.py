@@ -15,6 +15,7 @@ from torchtitan_b200.components.optimizer import OptimizersContainer
 from torchtitan_b200.components.tokenizer import SyntheticTokenizer
 from torchtitan_b200.components.validate import Validator
 from torchtitan_b200.config import ActivationCheckpointConfig, ParallelismConfig, TrainingConfig
+from torchtitan_b200.protocols.model_converter import ModelConvertersContainer
 from torchtitan_b200.trainer import Trainer
 
 from . import model_registry
@@ -87,6 +88,7 @@ def llama3_70b_fsdp2_tp4() -> Trainer.Config:
     c = llama3_70b()
     c.training = TrainingConfig(local_batch_size=1, seq_len=8192, steps=1000)
     c.parallelism = ParallelismConfig(tensor_parallel_degree=4, enable_async_tensor_parallel=True)
+    c.model_converters = ModelConvertersContainer.Config(names=["mxfp8"])
     return c
 
 

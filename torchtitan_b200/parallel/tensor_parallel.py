@@ -104,13 +104,17 @@ def grad_all_reduce(x, group):
     return _GradAllReduce.apply(x, group)
 
 
-def tp_linear(x: torch.Tensor, w: torch.Tensor, mode: str, group, sequence_parallel: bool) -> torch.Tensor:
+def tp_linear(x: torch.Tensor, w: torch.Tensor, mode: str, group, sequence_parallel: bool,
+              matmul=None) -> torch.Tensor:
+    """``matmul(x, w)`` (default ``ops.linear``; quantized recipes pass their own) with the
+    TP collectives around it."""
+    mm = matmul or ops.linear
     if mode == "col":
         if sequence_parallel:
             x = all_gather_seq(x, group)
-        return ops.linear(x, w)
+        return mm(x, w)
     if mode == "row":
-        y = ops.linear(x, w)
+        y = mm(x, w)
         return reduce_scatter_seq(y, group) if sequence_parallel else _AllReduce.apply(y, group)
     raise ValueError(mode)
 

@@ -31,13 +31,28 @@ class ModelConverter(Configurable):
         pass
 
 
+def _named_converter(name: str) -> Any:
+    from torchtitan_b200.components.quantization import Float8LinearConverter, MXFP8Converter
+
+    if name in ("mx", "mxfp8"):
+        return MXFP8Converter.Config()
+    if name.startswith("float8"):
+        recipe = name[len("float8_"):] if name != "float8" else "tensorwise"
+        return Float8LinearConverter.Config(recipe_name=recipe)
+    raise ValueError(f"unknown model converter '{name}'")
+
+
 class ModelConvertersContainer(Configurable):
     @dataclass(kw_only=True, slots=True)
     class Config(Configurable.Config):
         converters: list[Any] = field(default_factory=list)
+        names: list[str] = field(default_factory=list)
+        """Shortcut for the command line: ``mxfp8``, ``float8``, ``float8_rowwise``,
+        ``float8_rowwise_with_gw_hp`` (default settings of each converter)."""
 
     def __init__(self, config: Config, **kwargs: Any):
-        self.converters = [c.build(**kwargs) for c in config.converters]
+        cfgs = list(config.converters) + [_named_converter(n) for n in config.names]
+        self.converters = [c.build(**kwargs) for c in cfgs]
         nq = sum(1 for c in self.converters if getattr(c, "is_quantization", False))
         if nq > 1:
             raise ValueError("at most one quantization converter may be configured")
