@@ -1,0 +1,67 @@
+"""HF conversion, loss comparison and generation utilities on CPU."""
+import os
+
+import torch
+
+
+def test_hf_conversion_round_trip(tmp_path):
+    from safetensors.torch import load_file, save_file
+
+    from torchtitan_b200.checkpoint_conversion import convert_from_hf, convert_to_hf
+    from torchtitan_b200.models.llama3 import model_registry
+
+    spec = model_registry("debugmodel")
+    torch.manual_seed(0)
+    model = spec.model.build()
+    model.init_weights()
+    hf = spec.state_dict_adapter(spec.model, None).to_hf({k: v.detach() for k, v in model.state_dict().items()})
+    hf_dir = tmp_path / "hf"
+    hf_dir.mkdir()
+    save_file({k: v.contiguous() for k, v in hf.items()}, str(hf_dir / "model.safetensors"))
+    state = convert_from_hf(str(hf_dir), str(tmp_path / "dcp"), "llama3", "debugmodel")
+    for k, v in model.state_dict().items():
+        assert torch.equal(state[k], v), k
+    convert_to_hf(str(tmp_path / "dcp"), str(tmp_path / "hf_out"), "llama3", "debugmodel", "float32")
+    back = load_file(str(tmp_path / "hf_out" / "model.safetensors"))
+    assert set(back) == set(hf)
+    for k in hf:
+        assert torch.equal(back[k], hf[k]), k
+    assert os.path.exists(tmp_path / "hf_out" / "model.safetensors.index.json")
+
+
+def test_loss_compare_detects_differences(tmp_path):
+    from torchtitan_b200.loss_compare import compare, main
+
+    assert compare({1: 1.0, 2: 0.5}, {1: 1.0, 2: 0.5}, True, 0.0) == []
+    assert len(compare({1: 1.0, 2: 0.5}, {1: 1.0, 2: 0.50001}, True, 0.0)) == 1
+    assert compare({1: 1.0}, {1: 1.00001}, False, 1e-4) == []
+    args = ("--module llama3 --config llama3_debugmodel --training.seq-len 64 --training.local-batch-size 2 "
+            "--training.dtype float32 --training.mixed-precision-param float32 --activation-checkpoint.mode none")
+    rc = main(["--baseline", args, "--test", args, "--steps", "3", "--assert-equal", "--output-folder",
+               str(tmp_path)])
+    assert rc == 0
+    rc = main(["--baseline", args, "--test", args + " --optimizer.lr 1e-2", "--steps", "3", "--assert-equal",
+               "--output-folder", str(tmp_path / "b")])
+    assert rc == 1
+
+
+def test_generate_greedy_and_eos():
+    from torchtitan_b200.generate import generate
+    from torchtitan_b200.models.llama3 import model_registry
+
+    spec = model_registry("debugmodel")
+    torch.manual_seed(0)
+    model = spec.model.build()
+    model.init_weights()
+    model.eval()
+    p = torch.tensor([[1, 2, 3]])
+    a = generate(model, p, 5)
+    b = generate(model, p, 5)
+    assert a.shape == (1, 8) and torch.equal(a, b)
+    assert int(a[0, 3]) == int(model(p)[0, -1].argmax())
+    eos = int(a[0, 3])
+    c = generate(model, p, 5, eos_id=eos)
+    assert c.shape == (1, 4)
+    g = torch.Generator().manual_seed(0)
+    s = generate(model, p, 4, temperature=1.0, top_k=5, generator=g)
+    assert s.shape == (1, 7)

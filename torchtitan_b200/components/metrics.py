@@ -87,6 +87,37 @@ class WandBLogger(BaseLogger):
         self.run.finish()
 
 
+class JsonlLogger(BaseLogger):
+    """One JSON object per logged step (``{"step": N, <metric>: value, ...}``): the format
+    ``torchtitan_b200.loss_compare`` reads."""
+
+    def __init__(self, path: str):
+        os.makedirs(os.path.dirname(path), exist_ok=True)
+        self.f = open(path, "a")
+
+    def log(self, metrics, step):
+        import json
+
+        self.f.write(json.dumps({"step": step, **{k: float(v) for k, v in metrics.items()}}) + "\n")
+        self.f.flush()
+
+    def close(self):
+        self.f.close()
+
+
+class _Fanout(BaseLogger):
+    def __init__(self, loggers):
+        self.loggers = loggers
+
+    def log(self, metrics, step):
+        for lg in self.loggers:
+            lg.log(metrics, step)
+
+    def close(self):
+        for lg in self.loggers:
+            lg.close()
+
+
 class MetricsProcessor(Configurable):
     @dataclass(kw_only=True, slots=True)
     class Config(Configurable.Config):
@@ -96,6 +127,8 @@ class MetricsProcessor(Configurable):
         save_tb_folder: str = "tb"
         save_for_all_ranks: bool = False
         enable_wandb: bool = False
+        enable_jsonl: bool = False
+        """Append every logged step to ``<dump_folder>/<save_tb_folder>/rank_<r>/metrics.jsonl``."""
 
     def __init__(self, config: Config, *, parallel_dims: Any = None, dump_folder: str = "./outputs",
                  pp_schedule: str = "1F1B", config_dict: dict | None = None, has_quantization: bool = False,
@@ -114,10 +147,15 @@ class MetricsProcessor(Configurable):
         rank = dist.get_rank() if dist.is_initialized() else 0
         if config.save_for_all_ranks or rank == 0:
             d = os.path.join(dump_folder, config.save_tb_folder, f"rank_{rank}")
+            loggers: list[BaseLogger] = []
             if config.enable_tensorboard:
-                self.logger = TensorBoardLogger(d)
+                loggers.append(TensorBoardLogger(d))
             elif config.enable_wandb:
-                self.logger = WandBLogger(d, config_dict)
+                loggers.append(WandBLogger(d, config_dict))
+            if config.enable_jsonl:
+                loggers.append(JsonlLogger(os.path.join(d, "metrics.jsonl")))
+            if loggers:
+                self.logger = loggers[0] if len(loggers) == 1 else _Fanout(loggers)
         self._t_host = time.perf_counter()
         self._ev_start = self._new_event()
         self.last_metrics: dict[str, float] = {}
