@@ -215,3 +215,57 @@ def test_peer_exit_surfaces_as_error_not_hang():
     for p in procs:
         p.join(60)
     assert all(not p.is_alive() for p in procs)
+
+
+# ---------------------------------------------------------------- semi-synchronous replicas
+def _semi_sync(rank, world, out_dir):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    def make(method, extra=()):
+        return Trainer(ConfigManager().parse_args([
+            "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "4",
+            "--training.seq-len", "128", "--parallelism.data-parallel-replicate-degree", "2",
+            "--parallelism.data-parallel-shard-degree", "1", "--fault-tolerance.enable",
+            "--fault-tolerance.semi-sync-method", method, "--fault-tolerance.sync-steps", "2",
+            "--dump-folder", os.path.join(out_dir, method), *extra]))
+
+    def gathered(t):
+        w = torch.cat([p.detach().to_local().reshape(-1) if hasattr(p, "to_local") else p.detach().reshape(-1)
+                       for p in t.model_parts[0].parameters()])
+        ws = [torch.empty_like(w) for _ in range(world)]
+        dist.all_gather(ws, w)
+        return ws
+
+    t = make("local_sgd")
+    for step in range(1, 4):
+        t.step = step
+        t.train_step(t.batch_generator(t.dataloader))
+        ws = gathered(t)
+        # replicas see different data: they agree only right after a synchronisation (steps 2, 4, ...)
+        assert torch.equal(ws[0], ws[1]) == (step % 2 == 0), step
+    t.close()
+    # DiLoCo with outer lr 1 and no momentum is exactly weight averaging
+    t = make("diloco", ("--fault-tolerance.outer-lr", "1.0", "--fault-tolerance.outer-momentum", "0.0"))
+    it = t.batch_generator(t.dataloader)
+    for step in range(1, 3):
+        t.step = step
+        t.train_step(it)
+    ws = gathered(t)
+    torch.testing.assert_close(ws[0], ws[1])
+    t.close()
+
+
+def test_semi_sync_local_sgd_and_diloco():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_semi_sync, 2, d)
+
+
+def test_semi_sync_fragment_schedule():
+    from torchtitan_b200.parallel.semi_sync import FaultToleranceConfig, SemiSync
+
+    s = SemiSync.__new__(SemiSync)
+    s.cfg = FaultToleranceConfig(enable=True, semi_sync_method="diloco", sync_steps=8, num_fragments=4)
+    s.offsets = [0, 2, 4, 6]
+    assert [s.due(k) for k in range(1, 17)] == [[], [], [], [], [], [], [], [0], [], [1], [], [2], [], [3], [],
+                                                 [0]]

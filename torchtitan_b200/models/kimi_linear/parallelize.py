@@ -19,6 +19,7 @@ from torchtitan_b200.parallel.activation_checkpoint import apply_ac
 from torchtitan_b200.parallel.context_parallel import ulysses_hook
 from torchtitan_b200.parallel.expert_parallel import apply_ep
 from torchtitan_b200.parallel.fsdp import (
+    dp_mesh,
     apply_fsdp,
     apply_replica_mixed_precision,
     replica_mixed_precision_applicable,
@@ -52,8 +53,7 @@ def parallelize_kimi(model: nn.Module, *, parallel_dims: Any, training: Any, par
         apply_ac(model, ac_config)
     if replica_mixed_precision_applicable(pd, training):
         return apply_replica_mixed_precision(model)
-    names = ["dp_replicate", "fsdp"] if pd.dp_replicate_enabled else "fsdp"
-    apply_fsdp(model, pd.get_mesh(names), param_dtype=TORCH_DTYPE_MAP[training.mixed_precision_param],
+    apply_fsdp(model, dp_mesh(pd), param_dtype=TORCH_DTYPE_MAP[training.mixed_precision_param],
                reduce_dtype=TORCH_DTYPE_MAP[training.mixed_precision_reduce], pp_enabled=pd.pp_enabled,
                cpu_offload=training.enable_cpu_offload,
                reshard_after_forward_policy=parallelism.fsdp_reshard_after_forward,

@@ -10,6 +10,7 @@ from torchtitan_b200.config import TORCH_DTYPE_MAP
 from torchtitan_b200.parallel.activation_checkpoint import apply_ac
 from torchtitan_b200.parallel.context_parallel import apply_cp_to_attention_modules
 from torchtitan_b200.parallel.fsdp import (
+    dp_mesh,
     apply_fsdp,
     apply_replica_mixed_precision,
     replica_mixed_precision_applicable,
@@ -39,17 +40,13 @@ def parallelize_llama(model: nn.Module, *, parallel_dims: Any, training: Any, mo
         apply_ac(model, ac_config)
         logger.info(f"applied {ac_config.mode} activation checkpointing")
     if peer_dp_applicable(parallel_dims, training, parallelism):
-        names = ["dp_replicate", "fsdp"] if parallel_dims.dp_replicate_enabled else ["fsdp"]
-        apply_peer_dp(model, parallel_dims.get_mesh(names if len(names) > 1 else names[0]),
-                      bucket_mb=parallelism.data_parallel_bucket_mb)
+        apply_peer_dp(model, dp_mesh(parallel_dims), bucket_mb=parallelism.data_parallel_bucket_mb)
         logger.info("data parallel: replicated bf16 weights, sharded fp32 optimizer, peer-memory collectives")
     elif replica_mixed_precision_applicable(parallel_dims, training):
         apply_replica_mixed_precision(model)
         logger.info("single replica: bf16 compute weights with fp32 masters in the optimizer (no FSDP wrap)")
     else:
-        names = ["dp_replicate", "fsdp"] if parallel_dims.dp_replicate_enabled else ["fsdp"]
-        dp_mesh = parallel_dims.get_mesh(names if len(names) > 1 else names[0])
-        apply_fsdp(model, dp_mesh, param_dtype=TORCH_DTYPE_MAP[training.mixed_precision_param],
+        apply_fsdp(model, dp_mesh(parallel_dims), param_dtype=TORCH_DTYPE_MAP[training.mixed_precision_param],
                    reduce_dtype=TORCH_DTYPE_MAP[training.mixed_precision_reduce],
                    pp_enabled=parallel_dims.pp_enabled, cpu_offload=training.enable_cpu_offload,
                    reshard_after_forward_policy=parallelism.fsdp_reshard_after_forward)

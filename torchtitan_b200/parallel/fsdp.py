@@ -73,6 +73,20 @@ def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, redu
     return model
 
 
+def dp_mesh_names(parallel_dims) -> list[str]:
+    """Mesh dims that data-parallel gradient reduction spans: ``dp_replicate`` is left out
+    when it holds semi-synchronous replicas (LocalSGD / DiLoCo), which reduce nothing
+    between their synchronisations."""
+    if parallel_dims.dp_replicate_enabled and not getattr(parallel_dims, "semi_sync_replicas", False):
+        return ["dp_replicate", "fsdp"]
+    return ["fsdp"]
+
+
+def dp_mesh(parallel_dims):
+    names = dp_mesh_names(parallel_dims)
+    return parallel_dims.get_mesh(names if len(names) > 1 else names[0])
+
+
 def apply_ddp(model: nn.Module, dp_mesh: Any) -> nn.Module:
     """Pure data parallel: replicate via FSDP2 on the replicate mesh."""
     return apply_fsdp(model, dp_mesh, param_dtype=torch.bfloat16, reduce_dtype=torch.float32)

@@ -23,7 +23,12 @@ from torchtitan_b200.config import TORCH_DTYPE_MAP
 from torchtitan_b200.parallel.activation_checkpoint import apply_ac
 from torchtitan_b200.parallel.context_parallel import apply_cp_to_attention_modules
 from torchtitan_b200.parallel.expert_parallel import apply_ep
-from torchtitan_b200.parallel.fsdp import apply_fsdp, apply_replica_mixed_precision, replica_mixed_precision_applicable
+from torchtitan_b200.parallel.fsdp import (
+    apply_fsdp,
+    apply_replica_mixed_precision,
+    dp_mesh,
+    replica_mixed_precision_applicable,
+)
 from torchtitan_b200.parallel.peer_dp import apply_peer_dp, peer_dp_applicable
 from torchtitan_b200.utils.logging import logger
 
@@ -65,13 +70,10 @@ def parallelize_decoder(model: nn.Module, *, parallel_dims: Any, training: Any, 
         apply_ac(model, ac_config)
         logger.info(f"applied {ac_config.mode} activation checkpointing")
     if peer_dp_applicable(pd, training, parallelism):
-        names = ["dp_replicate", "fsdp"] if pd.dp_replicate_enabled else ["fsdp"]
-        return apply_peer_dp(model, pd.get_mesh(names if len(names) > 1 else names[0]),
-                             bucket_mb=parallelism.data_parallel_bucket_mb)
+        return apply_peer_dp(model, dp_mesh(pd), bucket_mb=parallelism.data_parallel_bucket_mb)
     if replica_mixed_precision_applicable(pd, training):
         return apply_replica_mixed_precision(model)
-    names = ["dp_replicate", "fsdp"] if pd.dp_replicate_enabled else "fsdp"
-    apply_fsdp(model, pd.get_mesh(names), param_dtype=TORCH_DTYPE_MAP[training.mixed_precision_param],
+    apply_fsdp(model, dp_mesh(pd), param_dtype=TORCH_DTYPE_MAP[training.mixed_precision_param],
                reduce_dtype=TORCH_DTYPE_MAP[training.mixed_precision_reduce], pp_enabled=pd.pp_enabled,
                cpu_offload=training.enable_cpu_offload,
                reshard_after_forward_policy=parallelism.fsdp_reshard_after_forward,

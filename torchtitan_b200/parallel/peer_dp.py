@@ -81,7 +81,7 @@ def plan_layout(numels: list[int], world: int, bucket_elems: int, align: int = _
 def peer_dp_applicable(parallel_dims: Any, training: Any, parallelism: Any) -> bool:
     """Pure data parallelism on one node of CUDA devices with bf16 compute over fp32 masters."""
     mode = getattr(parallelism, "data_parallel_comm", "auto")
-    if mode == "fsdp2" or parallel_dims.world_size < 2:
+    if mode == "fsdp2" or parallel_dims.world_size < 2 or getattr(parallel_dims, "semi_sync_replicas", False):
         return False
     pure_dp = not (parallel_dims.tp_enabled or parallel_dims.cp_enabled or parallel_dims.pp_enabled
                    or parallel_dims.ep_enabled)

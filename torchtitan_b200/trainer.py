@@ -46,6 +46,7 @@ from torchtitan_b200.config import (
     TrainingConfig,
 )
 from torchtitan_b200.parallel import ParallelDims
+from torchtitan_b200.parallel.semi_sync import FaultToleranceConfig
 from torchtitan_b200.parallel import utils as dist_utils
 from torchtitan_b200.protocols import ModelConvertersContainer, ModelSpec
 from torchtitan_b200.utils import device as dev_utils
@@ -74,6 +75,7 @@ class Trainer(Stateful, Configurable):
         comm: CommConfig = field(default_factory=CommConfig)
         validator: Validator.Config = field(default_factory=Validator.Config)
         debug: DebugConfig = field(default_factory=DebugConfig)
+        fault_tolerance: FaultToleranceConfig = field(default_factory=FaultToleranceConfig)
 
         def to_dict(self) -> dict[str, Any]:
             d = {}
@@ -104,6 +106,10 @@ class Trainer(Stateful, Configurable):
         world = dist_utils.init_distributed(c.comm, enable_cpu_backend=c.training.enable_cpu_offload,
                                             base_folder=c.dump_folder)
         self.parallel_dims = pd = ParallelDims.from_config(c.parallelism, world)
+        ft = c.fault_tolerance
+        pd.semi_sync_replicas = bool(ft.enable and ft.semi_sync_method)
+        if pd.semi_sync_replicas and not pd.dp_replicate_enabled:
+            raise ValueError("semi-synchronous training needs data_parallel_replicate_degree > 1 (the replicas)")
         if c.debug.print_config:
             logger.info(json.dumps(c.to_dict(), indent=2))
         if pd.dp_enabled:
@@ -181,6 +187,13 @@ class Trainer(Stateful, Configurable):
         self.optimizers = c.optimizer.build(model_parts=self.model_parts)
         if spec.post_optimizer_build_fn is not None:
             spec.post_optimizer_build_fn(self.optimizers, self.model_parts, pd)
+        self.semi_sync = None
+        if pd.semi_sync_replicas:
+            from torchtitan_b200.parallel.semi_sync import SemiSync
+
+            self.semi_sync = SemiSync(ft, self.model_parts, pd.get_mesh("dp_replicate").get_group())
+            logger.info(f"semi-synchronous replicas: {ft.semi_sync_method} every {ft.sync_steps} steps "
+                        f"({len(self.semi_sync.fragments)} fragments, {pd.dp_replicate} replicas)")
         self.lr_schedulers = c.lr_scheduler.build(optimizers=self.optimizers, training_steps=c.training.steps)
         self.optimizers.register_step_post_hook(lambda *a, **k: converters.post_optimizer_hook(self.model_parts))
         self.metrics_processor.optimizers = self.optimizers
@@ -189,7 +202,8 @@ class Trainer(Stateful, Configurable):
         self.ntokens_seen = 0
         self.checkpointer = c.checkpoint.build(
             dataloader=self.dataloader, model_parts=self.model_parts, optimizers=self.optimizers,
-            lr_schedulers=self.lr_schedulers, states={"train_state": self},
+            lr_schedulers=self.lr_schedulers,
+            states={"train_state": self, **({"semi_sync": self.semi_sync} if self.semi_sync is not None else {})},
             sd_adapter=spec.state_dict_adapter(margs, c.hf_assets_path) if spec.state_dict_adapter else None,
             base_folder=c.dump_folder)
         self.train_context = dist_utils.get_train_context(False)
@@ -283,7 +297,11 @@ class Trainer(Stateful, Configurable):
             local_valid += int((labels != IGNORE_INDEX).sum())
             mbs.append((inp, labels))
         local_valid_t = torch.tensor(float(local_valid), device=self.device)
-        global_valid = dist_utils.dist_sum(local_valid_t, pd.get_mesh("batch")) if pd.dp_enabled else local_valid_t
+        if pd.semi_sync_replicas:  # each replica normalises by its own tokens
+            global_valid = (dist_utils.dist_sum(local_valid_t, pd.get_mesh("dp_shard")) if pd.dp_shard > 1
+                            else local_valid_t)
+        else:
+            global_valid = dist_utils.dist_sum(local_valid_t, pd.get_mesh("batch")) if pd.dp_enabled else local_valid_t
         losses = []
         dp_rt = getattr(self.model_parts[0], "_dp_runtime", None)
         for i, (inp, labels) in enumerate(mbs):
@@ -318,6 +336,8 @@ class Trainer(Stateful, Configurable):
             grad_norm = clip
         self.checkpointer.maybe_wait_for_staging()
         self.optimizers.step()
+        if self.semi_sync is not None:
+            self.semi_sync.after_step(self.step)
         self.lr_schedulers.step()
         loss = torch.sum(torch.stack([l.reshape(()) for l in losses]))
         self.last_loss = loss
@@ -328,6 +348,8 @@ class Trainer(Stateful, Configurable):
         if pd.dp_cp_enabled:
             mesh = pd.get_optional_mesh("loss")
             avg = float(dist_utils.dist_sum(loss, mesh))
+            if pd.semi_sync_replicas:
+                avg /= pd.dp_replicate
             local_avg = loss * global_valid / max(local_valid, 1)
             mx = float(dist_utils.dist_max(local_avg, mesh))
         else:
