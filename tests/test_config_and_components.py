@@ -291,3 +291,38 @@ def test_mx_linear_gradients_close_to_bf16():
     (x2 @ w2.t()).square().sum().backward()
     for a, b in ((y, x2 @ w2.t()), (x.grad, x2.grad), (w.grad, w2.grad)):
         assert ((a - b).norm() / b.norm()) < 0.08
+
+
+def test_chat_dataloader_masks_prompts_and_packs(tmp_path):
+    import json
+
+    from torchtitan_b200.components.dataloader import ChatDataLoader
+    from torchtitan_b200.components.loss import IGNORE_INDEX
+
+    class CharTok:
+        bos_id, eos_id = 1, 2
+
+        def encode(self, text):
+            return [3 + (ord(c) % 50) for c in text]
+
+    recs = [{"messages": [{"role": "user", "content": "hi"}, {"role": "assistant", "content": "yo"}]},
+            {"messages": [{"role": "user", "content": "abc"}, {"role": "assistant", "content": "de"}]}]
+    path = tmp_path / "chat.jsonl"
+    path.write_text("\n".join(json.dumps(r) for r in recs))
+    dl = ChatDataLoader(ChatDataLoader.Config(dataset_path=str(path), infinite=False), tokenizer=CharTok(),
+                        seq_len=64, local_batch_size=1)
+    (inp, labels), = list(dl)
+    ids, lab, pos = inp["input"][0], labels[0], inp["positions"][0]
+    tok = CharTok()
+    user1 = tok.encode("<|user|>\nhi\n")
+    asst1 = tok.encode("<|assistant|>\nyo\n")
+    n1 = 1 + len(user1) + len(asst1) + 1
+    # labels are the next tokens; prompt tokens and the leading BOS are ignored
+    assert (lab[:len(user1)] == IGNORE_INDEX).all()
+    assert lab[len(user1):len(user1) + len(asst1)].tolist() == asst1
+    assert lab[len(user1) + len(asst1)] == 2  # eos is trained
+    # second sample packed right after the first, positions restart
+    assert pos[n1] == 0 and ids[n1] == 1
+    assert pos[n1 - 1] == n1 - 1
+    n2 = 1 + len(tok.encode("<|user|>\nabc\n")) + len(tok.encode("<|assistant|>\nde\n")) + 1
+    assert (lab[n1 + n2 - 1:] == IGNORE_INDEX).all()  # padding

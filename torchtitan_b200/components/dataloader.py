@@ -173,3 +173,118 @@ class HuggingFaceTextDataLoader(BaseDataLoader):
 
     def _load_local_state(self, st):
         self.sample_idx = int(st["sample_idx"])
+
+
+def _iter_local_records(path: str) -> Iterator[dict]:
+    files = sorted(glob.glob(os.path.join(path, "**", "*.jsonl"), recursive=True)) if os.path.isdir(path) else [path]
+    for fn in files:
+        with open(fn) as f:
+            for line in f:
+                line = line.strip()
+                if line:
+                    yield json.loads(line)
+
+
+def render_chat(messages: list[dict], template: str | None = None) -> list[tuple[str, bool]]:
+    """Split a conversation into (text, trainable) segments.  With a jinja
+    ``template`` (the tokenizer's chat template) each message is rendered
+    alone; otherwise a plain ``<|role|>\\ncontent\\n`` layout is used.  Only
+    assistant turns are trainable."""
+    out = []
+    for m in messages:
+        if template:
+            import jinja2
+
+            text = jinja2.Template(template).render(messages=[m], add_generation_prompt=False)
+        else:
+            text = f"<|{m['role']}|>\n{m['content']}\n"
+        out.append((text, m["role"] == "assistant"))
+    return out
+
+
+class ChatDataLoader(BaseDataLoader):
+    """Supervised fine-tuning data (parity: reference ``hf_datasets/text_datasets.py:262-408``
+    ``ChatDataset``): JSONL records with ``messages: [{role, content}, ...]`` are
+    tokenised turn by turn, labels of non-assistant tokens are ``IGNORE_INDEX``,
+    and samples are greedily packed into ``seq_len + 1`` windows (a sample that
+    does not fit starts a new window, padded with ``pad_id`` / ignored labels;
+    one longer than the window is truncated).  ``positions`` restart at every
+    sample so document-masked attention sees sample boundaries."""
+
+    @dataclass(kw_only=True, slots=True)
+    class Config(BaseDataLoader.Config):
+        infinite: bool = True
+        pad_id: int = 0
+        chat_template: str | None = None
+
+    def __init__(self, config: Config, **kw: Any):
+        super().__init__(config, **kw)
+        if config.dataset_path is None:
+            raise ValueError("ChatDataLoader needs dataset_path (local JSONL with a 'messages' field)")
+        self.sample_idx = 0
+
+    def _samples(self) -> Iterator[tuple[list[int], list[int]]]:
+        from .loss import IGNORE_INDEX
+
+        while True:
+            for i, rec in enumerate(_iter_local_records(self.config.dataset_path)):
+                if i % self.dp_world_size != self.dp_rank:
+                    continue
+                ids, labels = [], []
+                bos = getattr(self.tokenizer, "bos_id", None)
+                if bos is not None:
+                    ids.append(bos)
+                    labels.append(IGNORE_INDEX)
+                for text, train in render_chat(rec["messages"], self.config.chat_template):
+                    t = self.tokenizer.encode(text)
+                    ids += t
+                    labels += t if train else [IGNORE_INDEX] * len(t)
+                eos = getattr(self.tokenizer, "eos_id", None)
+                if eos is not None:
+                    ids.append(eos)
+                    labels.append(eos)
+                yield ids, labels
+            if not self.config.infinite:
+                return
+
+    def _windows(self) -> Iterator[tuple[list[int], list[int], list[int]]]:
+        from .loss import IGNORE_INDEX
+
+        W = self.seq_len + 1
+        ids, lab, pos = [], [], []
+        for s_ids, s_lab in self._samples():
+            s_ids, s_lab = s_ids[:W], s_lab[:W]
+            if len(ids) + len(s_ids) > W:
+                pad = W - len(ids)
+                yield ids + [self.config.pad_id] * pad, lab + [IGNORE_INDEX] * pad, pos + list(range(pad))
+                ids, lab, pos = [], [], []
+            ids += s_ids
+            lab += s_lab
+            pos += list(range(len(s_ids)))
+        if ids:
+            pad = W - len(ids)
+            yield ids + [self.config.pad_id] * pad, lab + [IGNORE_INDEX] * pad, pos + list(range(pad))
+
+    def __iter__(self):
+        batch, skipped = [], 0
+        for w in self._windows():
+            batch.append(w)
+            if len(batch) < self.local_batch_size:
+                continue
+            ids = torch.tensor([b[0] for b in batch])
+            lab = torch.tensor([b[1] for b in batch])
+            pos = torch.tensor([b[2] for b in batch])
+            batch = []
+            if skipped < self.sample_idx:
+                skipped += 1
+                continue
+            self.sample_idx += 1
+            skipped += 1
+            # input t predicts label t+1
+            yield {"input": ids[:, :-1], "positions": pos[:, :-1]}, lab[:, 1:]
+
+    def _local_state(self):
+        return {"sample_idx": self.sample_idx}
+
+    def _load_local_state(self, st):
+        self.sample_idx = int(st["sample_idx"])
