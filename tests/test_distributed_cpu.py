@@ -269,3 +269,71 @@ def test_semi_sync_fragment_schedule():
     s.offsets = [0, 2, 4, 6]
     assert [s.due(k) for k in range(1, 17)] == [[], [], [], [], [], [], [], [0], [], [1], [], [2], [], [3], [],
                                                  [0]]
+
+
+# ---------------------------------------------------------------- async TP collective matmuls
+def _async_tp(rank, world):
+    from torchtitan_b200.parallel import async_tp
+    from torchtitan_b200.parallel.tensor_parallel import all_gather_seq, reduce_scatter_seq
+
+    g = dist.group.WORLD
+    torch.manual_seed(0)
+    B, S, K, N = 2, 8 * world, 16, 12
+    x_full = torch.randn(B, S, K, dtype=torch.float64)
+    w_col = torch.randn(N, K, dtype=torch.float64)  # this rank's column shard (same on all ranks here)
+    s = S // world
+    x = x_full[:, rank * s:(rank + 1) * s].clone().requires_grad_()
+    w1 = w_col.clone().requires_grad_()
+    y = async_tp.ag_matmul(x, w1, g)
+    x_ref = x.detach().clone().requires_grad_()
+    w_ref = w_col.clone().requires_grad_()
+    y_ref = all_gather_seq(x_ref, g) @ w_ref.t()
+    torch.testing.assert_close(y, y_ref)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    y_ref.backward(gy)
+    torch.testing.assert_close(x.grad, x_ref.grad)
+    torch.testing.assert_close(w1.grad, w_ref.grad)
+    # row-parallel: each rank holds a different K shard of the input features
+    xr = torch.randn(B, S, K, dtype=torch.float64, generator=torch.Generator().manual_seed(rank + 1))
+    wr = torch.randn(N, K, dtype=torch.float64, generator=torch.Generator().manual_seed(rank + 7))
+    a, b = xr.clone().requires_grad_(), wr.clone().requires_grad_()
+    out = async_tp.matmul_rs(a, b, g)
+    a2, b2 = xr.clone().requires_grad_(), wr.clone().requires_grad_()
+    ref = reduce_scatter_seq(a2 @ b2.t(), g)
+    torch.testing.assert_close(out, ref)
+    go = torch.randn_like(out)
+    out.backward(go)
+    ref.backward(go)
+    torch.testing.assert_close(a.grad, a2.grad)
+    torch.testing.assert_close(b.grad, b2.grad)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_async_tp_ring_matmuls_match_collectives(world):
+    _run(_async_tp, world)
+
+
+def _tp_async_trainer(rank, world, out_dir):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    res = []
+    for extra in ([], ["--parallelism.enable-async-tensor-parallel"]):
+        t = Trainer(ConfigManager().parse_args([
+            "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "2",
+            "--training.seq-len", "128", "--parallelism.tensor-parallel-degree", "2",
+            "--parallelism.data-parallel-shard-degree", "1", "--metrics.log-freq", "1",
+            "--debug.seed", "0", "--dump-folder", os.path.join(out_dir, str(len(extra))), *extra]))
+        t.train()
+        res.append(t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"])
+        t.close()
+    from torchtitan_b200.parallel import async_tp
+
+    async_tp.ENABLED = False
+    assert abs(res[0] - res[1]) < 1e-5 * abs(res[0]), res
+
+
+def test_async_tp_trainer_matches_sync_tp():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_tp_async_trainer, 2, d)

@@ -24,7 +24,9 @@ class Decoder(BaseModel):
 
     def forward(self, tokens: torch.Tensor, attention_masks=None, positions: torch.Tensor | None = None):
         h = self.tok_embeddings(tokens) if self.tok_embeddings is not None else tokens
-        cos, sin = self._rope_tables(h.shape[1], positions)
+        # under sequence parallelism h holds this rank's sequence shard; attention sees the full sequence
+        seq = tokens.shape[1] if self.tok_embeddings is not None else h.shape[1] * getattr(self, "_sp_degree", 1)
+        cos, sin = self._rope_tables(seq, positions)
         for layer in self.layers.values():
             h = layer(h, cos, sin, attention_masks)
         h = self.norm(h) if self.norm is not None else h

@@ -11,9 +11,8 @@ TP (norm weights, embeddings) get their gradients all-reduced over TP because
 each rank sees a different sequence shard.
 
 ``enable_async_tensor_parallel`` switches the column/row linears to the
-chunked overlap path: the all-gather (reduce-scatter) is split into ``tp``
-chunks issued on a side stream so GEMM on chunk i overlaps the transfer of
-chunk i+1.
+ring-decomposed collective matmuls of ``parallel.async_tp``: GEMM on the
+sequence chunk present overlaps the transfer of the next one.
 """
 from __future__ import annotations
 
@@ -109,6 +108,13 @@ def tp_linear(x: torch.Tensor, w: torch.Tensor, mode: str, group, sequence_paral
     """``matmul(x, w)`` (default ``ops.linear``; quantized recipes pass their own) with the
     TP collectives around it."""
     mm = matmul or ops.linear
+    from . import async_tp
+
+    if async_tp.ENABLED and sequence_parallel and matmul is None and dist.get_world_size(group) > 1:
+        if mode == "col":
+            return async_tp.ag_matmul(x, w, group)
+        if mode == "row":
+            return async_tp.matmul_rs(x, w, group)
     if mode == "col":
         if sequence_parallel:
             x = all_gather_seq(x, group)
@@ -252,10 +258,11 @@ def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_p
             model.output.forward = out_fwd
     model._tp_group = group
     model._tp_loss_parallel = loss_parallel
+    model._sp_degree = ws if sequence_parallel else 1
 
 
 def maybe_enable_async_tp(parallelism: Any, tp_mesh) -> None:
-    """Async TP here = chunked AG/RS overlap inside the TP linears (no compiler needed)."""
+    """Async TP = ring-decomposed AG->GEMM / GEMM->RS inside the TP linears (no compiler needed)."""
     from . import async_tp
 
     async_tp.ENABLED = bool(parallelism.enable_async_tensor_parallel)
