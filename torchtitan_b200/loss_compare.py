@@ -42,7 +42,10 @@ def run(args: str, steps: int, dump: str, ngpus: int, seed: int) -> dict[int, fl
     cmd = base + ["torchtitan_b200.train", *shlex.split(args), "--training.steps", str(steps),
                   "--metrics.log-freq", "1", "--metrics.enable-jsonl", "--dump-folder", dump,
                   "--debug.seed", str(seed), "--debug.deterministic"]
-    env = dict(os.environ)
+    # a fresh job: no rendezvous settings inherited from the calling process
+    env = {k: v for k, v in os.environ.items()
+           if k not in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "LOCAL_WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT",
+                        "GROUP_RANK", "ROLE_RANK", "TORCHELASTIC_RUN_ID")}
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))  # so the child imports this package
     env["PYTHONPATH"] = root + (os.pathsep + env["PYTHONPATH"] if env.get("PYTHONPATH") else "")
     subprocess.run(cmd, check=True, env=env)
