@@ -326,3 +326,32 @@ def test_chat_dataloader_masks_prompts_and_packs(tmp_path):
     assert pos[n1 - 1] == n1 - 1
     n2 = 1 + len(tok.encode("<|user|>\nabc\n")) + len(tok.encode("<|assistant|>\nde\n")) + 1
     assert (lab[n1 + n2 - 1:] == IGNORE_INDEX).all()  # padding
+
+
+def test_module_protocol_recursive_init():
+    import torch.nn as nn
+
+    from torchtitan_b200.protocols.module import Module
+
+    class Block(Module):
+        def __init__(self):
+            super().__init__()
+            self.w = nn.Parameter(torch.empty(4))
+            self.lin = Module.from_nn_module(nn.Linear(3, 3), {"weight": nn.init.ones_, "bias": nn.init.zeros_})
+            self.plain = nn.Linear(2, 2)
+            self.param_init = {"w": lambda t: t.fill_(2.0)}
+            self.touched = False
+
+        def init_self(self, buffer_device=None):
+            self.touched = True
+
+    b = Block()
+    b.plain.weight.data.fill_(123.0)
+    b.init_states()
+    assert torch.equal(b.w, torch.full((4,), 2.0)) and b.touched
+    assert torch.equal(b.lin.weight, torch.ones(3, 3)) and torch.equal(b.lin.bias, torch.zeros(3))
+    assert isinstance(b.lin, nn.Linear) and isinstance(b.lin, Module)
+    assert not torch.all(b.plain.weight == 123.0)  # reset_parameters ran
+    bad = Module.from_nn_module(nn.Linear(2, 2), {"nope": nn.init.zeros_})
+    with pytest.raises(KeyError):
+        bad.init_states()
