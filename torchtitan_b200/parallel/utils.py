@@ -89,7 +89,8 @@ def set_pg_timeouts(timeout: datetime.timedelta, parallel_dims: Any = None) -> N
 def _reduce(x: torch.Tensor | float, op, mesh: Any = None) -> float:
     t = x.detach().clone() if torch.is_tensor(x) else torch.tensor(float(x))
     if mesh is not None and dist.is_initialized():
-        if t.device.type == "cpu" and dist.get_backend(mesh.get_group()) != "gloo":
+        if t.device.type == "cpu" and dist.get_backend(mesh.get_group()) not in ("gloo", "fake") \
+                and torch.cuda.is_available():
             t = t.cuda()
         dist.all_reduce(t, op=op, group=mesh.get_group())
     return t
