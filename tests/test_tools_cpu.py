@@ -65,3 +65,22 @@ def test_generate_greedy_and_eos():
     g = torch.Generator().manual_seed(0)
     s = generate(model, p, 4, temperature=1.0, top_k=5, generator=g)
     assert s.shape == (1, 7)
+
+
+def test_forge_engine_steps_on_given_batches(tmp_path):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.forge import ForgeEngine
+
+    cfg = ConfigManager().parse_args(["--module", "llama3", "--config", "llama3_debugmodel", "--training.seq-len", "64",
+                                      "--training.local-batch-size", "2", "--training.dtype", "float32",
+                                      "--training.mixed-precision-param", "float32", "--activation-checkpoint.mode",
+                                      "none", "--dump-folder", str(tmp_path)])
+    eng = ForgeEngine(cfg)
+    tokens = torch.randint(0, 2048, (2, 65))
+    batch = ({"input": tokens[:, :-1]}, tokens[:, 1:])
+    l1 = float(eng.train_on_batches([batch]))
+    for _ in range(4):
+        l2 = float(eng.train_on_batches([batch]))
+    assert eng.step == 5 and l2 < l1  # the same batch is being memorised
+    assert eng.forward(batch[0]).shape == (2, 64, 2048)
+    eng.close()
