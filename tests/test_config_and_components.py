@@ -355,3 +355,20 @@ def test_module_protocol_recursive_init():
     bad = Module.from_nn_module(nn.Linear(2, 2), {"nope": nn.init.zeros_})
     with pytest.raises(KeyError):
         bad.init_states()
+
+
+def test_quantized_grouped_experts_train(tmp_path):
+    from torchtitan_b200.components.quantization.grouped import QuantGroupedExperts
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    cfg = ConfigManager().parse_args(["--module", "qwen3", "--config", "qwen3_debugmodel_moe", "--training.steps", "2",
+                                      "--training.seq-len", "128", "--training.local-batch-size", "2",
+                                      "--training.dtype", "float32", "--training.mixed-precision-param", "float32",
+                                      "--activation-checkpoint.mode", "none", "--dump-folder", str(tmp_path),
+                                      "--model-converters.names", "mxfp8", "mxfp8_grouped"])
+    t = Trainer(cfg)
+    assert sum(isinstance(m, QuantGroupedExperts) for m in t.model_parts[0].modules()) == 8
+    t.train()
+    assert 6.0 < t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"] < 9.0
+    t.close()

@@ -36,6 +36,10 @@ def _named_converter(name: str) -> Any:
 
     if name in ("mx", "mxfp8"):
         return MXFP8Converter.Config()
+    if name in ("mxfp8_grouped", "float8_rowwise_grouped"):
+        from torchtitan_b200.components.quantization.grouped import QuantGroupedExpertsConverter
+
+        return QuantGroupedExpertsConverter.Config(recipe_name=name[: -len("_grouped")])
     if name.startswith("float8"):
         recipe = name[len("float8_"):] if name != "float8" else "tensorwise"
         return Float8LinearConverter.Config(recipe_name=recipe)
@@ -48,12 +52,14 @@ class ModelConvertersContainer(Configurable):
         converters: list[Any] = field(default_factory=list)
         names: list[str] = field(default_factory=list)
         """Shortcut for the command line: ``mxfp8``, ``float8``, ``float8_rowwise``,
-        ``float8_rowwise_with_gw_hp`` (default settings of each converter)."""
+        ``float8_rowwise_with_gw_hp`` for linears; ``mxfp8_grouped``, ``float8_rowwise_grouped``
+        for routed experts (default settings of each converter)."""
 
     def __init__(self, config: Config, **kwargs: Any):
         cfgs = list(config.converters) + [_named_converter(n) for n in config.names]
         self.converters = [c.build(**kwargs) for c in cfgs]
-        nq = sum(1 for c in self.converters if getattr(c, "is_quantization", False))
+        nq = sum(1 for c in self.converters if getattr(c, "is_quantization", False)
+                 and type(c).__name__ != "QuantGroupedExpertsConverter")
         if nq > 1:
             raise ValueError("at most one quantization converter may be configured")
 
