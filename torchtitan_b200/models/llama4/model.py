@@ -2,7 +2,7 @@
 and top-1 sigmoid routing (scores applied before the experts), interleaved
 with dense layers every ``interleave_moe_layer_step`` layers, and iRoPE:
 every ``every_n_layers_nope``-th layer uses no positional encoding and full
-causal attention, the others use RoPE with chunked attention (causal within
+causal attention (with position-dependent query temperature for long contexts), the others use RoPE with chunked attention (causal within
 blocks of ``fixed_attn_block_size`` tokens) and optional weightless q/k RMS
 normalisation.
 
@@ -42,6 +42,9 @@ class Llama4ModelArgs(BaseModelArgs):
     every_n_layers_nope: int | None = 4
     fixed_attn_block_size: int = 8192
     use_qk_norm: bool = True
+    attn_temperature_tuning: bool = True
+    floor_scale: float = 8192.0
+    attn_scale: float = 0.1
     # MoE
     interleave_moe_layer_step: int = 1
     num_experts: int = 16
@@ -71,6 +74,8 @@ class Llama4Attention(GQAttention):
         self.use_rope = use_rope
         self.block = a.fixed_attn_block_size if use_rope else 0
         self.qk_l2 = a.use_qk_norm and use_rope
+        # NoPE layers: queries scaled by 1 + attn_scale * log(1 + floor((pos + 1) / floor_scale))
+        self.temp = (a.floor_scale, a.attn_scale) if (a.attn_temperature_tuning and not use_rope) else None
 
     def inner_attention(self, q, k, v, attention_masks=None):
         B, S = q.shape[:2]
@@ -90,6 +95,11 @@ class Llama4Attention(GQAttention):
             q, k = ops.rope(q, cos, sin), ops.rope(k, cos, sin)
         if self.qk_l2:
             q, k = _rms(q), _rms(k)
+        if self.temp is not None:
+            floor_scale, attn_scale = self.temp
+            pos = torch.arange(S, device=x.device, dtype=torch.float32)
+            scale = torch.log(torch.floor((pos + 1) / floor_scale) + 1) * attn_scale + 1
+            q = (q.float() * scale.view(1, S, 1, 1)).to(q.dtype)
         if self.cp_hook is not None:
             o = self.cp_hook(self.inner_attention, q, k, v, attention_masks)
         else:
