@@ -337,3 +337,29 @@ def _tp_async_trainer(rank, world, out_dir):
 def test_async_tp_trainer_matches_sync_tp():
     with tempfile.TemporaryDirectory() as d:
         _run(_tp_async_trainer, 2, d)
+
+
+# ---------------------------------------------------------------- pipeline parallel
+def _pp(rank, world, out_dir, module, config):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", module, "--config", config, "--training.steps", "2", "--training.seq-len", "128",
+        "--parallelism.pipeline-parallel-degree", "2", "--parallelism.data-parallel-shard-degree", "1",
+        "--parallelism.pipeline-parallel-microbatch-size", "2", "--training.local-batch-size", "4",
+        "--parallelism.pipeline-parallel-schedule", "Interleaved1F1B", "--training.dtype", "float32",
+        "--training.mixed-precision-param", "float32", "--dump-folder", out_dir]))
+    t.train()
+    loss = t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"]
+    assert t.pp_has_last_stage == (rank == 1)
+    if rank == 1:
+        assert 6.0 < loss < 9.0
+    t.close()
+
+
+@pytest.mark.parametrize("module,config", [("llama3", "llama3_debugmodel_cpu"),
+                                           ("kimi_linear", "kimi_linear_debugmodel_block_attn_res")])
+def test_pipeline_parallel_interleaved_1f1b(module, config):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_pp, 2, d, module, config)

@@ -263,7 +263,8 @@ class Trainer(Stateful, Configurable):
                 inputs, labels, extra_kwargs, pd.get_mesh("cp"), self.device,
                 self.config.parallelism.context_parallel_load_balancer,
                 self.config.parallelism.context_parallel_method)
-        return inputs, labels, extra_inputs, extra_kwargs
+        # pipeline stages check shapes and strides of what they receive
+        return inputs.contiguous(), labels.contiguous(), extra_inputs, extra_kwargs
 
     def forward_backward_step(self, *, input_dict, labels, global_valid_tokens) -> torch.Tensor:
         inputs, labels, extra_inputs, extra_kwargs = self.post_dataloading_process(input_dict, labels)
