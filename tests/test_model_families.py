@@ -6,7 +6,8 @@ import torch
 import torch.nn.functional as F
 
 FAMILIES = [("qwen3", "debugmodel"), ("qwen3", "debugmodel_moe"), ("deepseek_v3", "debugmodel"),
-            ("deepseek_v3", "debugmodel_qlora"), ("llama4", "debugmodel"), ("gpt_oss", "debugmodel")]
+            ("deepseek_v3", "debugmodel_qlora"), ("llama4", "debugmodel"), ("gpt_oss", "debugmodel"), ("attention_residual", "debugmodel"),
+            ("attention_residual", "debugmodel_full")]
 
 
 def _build(module, flavor, seq=64):
@@ -134,3 +135,21 @@ def test_trainer_runs_family_configs(module, config, tmp_path):
     assert t.step == 2
     assert torch.isfinite(torch.tensor(t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"]))
     t.close()
+
+
+def test_block_attn_res_uniform_at_init_and_softmax_weights():
+    from torchtitan_b200.models.common import RMSNorm
+    from torchtitan_b200.models.common.attn_res import block_attn_res
+
+    torch.manual_seed(0)
+    norm = RMSNorm(8)
+    norm.init_weights()
+    blocks = [torch.randn(2, 3, 8) for _ in range(3)]
+    partial = torch.randn(2, 3, 8)
+    out = block_attn_res(blocks, partial, torch.zeros(1, 8), norm)
+    torch.testing.assert_close(out, torch.stack(blocks + [partial]).mean(0))
+    q = torch.randn(1, 8)
+    V = torch.stack(blocks + [partial])
+    Kn = V * torch.rsqrt(V.pow(2).mean(-1, keepdim=True) + 1e-5)
+    w = torch.softmax((Kn @ q[0]), 0)
+    torch.testing.assert_close(block_attn_res(blocks, partial, q, norm), (w[..., None] * V).sum(0))

@@ -30,6 +30,7 @@ from torchtitan_b200 import ops
 from torchtitan_b200.ops import kda as K
 from torchtitan_b200.protocols import BaseModel, BaseModelArgs
 
+from ..common.attn_res import block_attn_res
 from ..common.layers import Embedding, Linear, RMSNorm, _local
 from ..common.moe import MoE
 
@@ -259,15 +260,6 @@ class KimiMoE(nn.Module):
 
     def forward(self, x):
         return self._moe(x)
-
-
-def block_attn_res(blocks: list[torch.Tensor], partial: torch.Tensor, query: torch.Tensor, norm: RMSNorm):
-    """softmax_n(<w, RMSNorm(V_n)>) weighted sum of V = blocks + [partial] (all [B,T,D])."""
-    V = torch.stack(blocks + [partial], 0)
-    Kn = norm(V)
-    w = _local(query).reshape(-1).to(Kn.dtype)
-    logits = torch.einsum("d,nbtd->nbt", w, Kn).float()
-    return torch.einsum("nbt,nbtd->btd", torch.softmax(logits, 0).to(V.dtype), V)
 
 
 class KimiDecoderLayer(nn.Module):
