@@ -1,4 +1,4 @@
-"""CPU tests for the Qwen3, DeepSeek-V3, Llama 4 and GPT-OSS families:
+"""CPU tests for the Qwen3, DeepSeek-V3, Llama 4, GPT-OSS and dense AttnRes families:
 forward/backward, HF name mapping round trips, and the attention variants
 against plain PyTorch formulations."""
 import pytest
@@ -6,8 +6,8 @@ import torch
 import torch.nn.functional as F
 
 FAMILIES = [("qwen3", "debugmodel"), ("qwen3", "debugmodel_moe"), ("deepseek_v3", "debugmodel"),
-            ("deepseek_v3", "debugmodel_qlora"), ("llama4", "debugmodel"), ("gpt_oss", "debugmodel"), ("attention_residual", "debugmodel"),
-            ("attention_residual", "debugmodel_full")]
+            ("deepseek_v3", "debugmodel_qlora"), ("llama4", "debugmodel"), ("gpt_oss", "debugmodel"),
+            ("attention_residual", "debugmodel"), ("attention_residual", "debugmodel_full")]
 
 
 def _build(module, flavor, seq=64):
