@@ -372,3 +372,15 @@ def test_quantized_grouped_experts_train(tmp_path):
     t.train()
     assert 6.0 < t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"] < 9.0
     t.close()
+
+
+def test_batch_invariant_env(monkeypatch):
+    import os
+
+    from torchtitan_b200.parallel.utils import apply_batch_invariant_env
+
+    for k in ("NCCL_ALGO", "NCCL_PROTO", "NCCL_MIN_NCHANNELS", "NCCL_MAX_NCHANNELS", "NCCL_NVLS_ENABLE",
+              "NCCL_COLLNET_ENABLE"):
+        monkeypatch.delenv(k, raising=False)
+    env = apply_batch_invariant_env()
+    assert os.environ["NCCL_ALGO"] == "Ring" and os.environ["NCCL_NVLS_ENABLE"] == "0" and len(env) == 6

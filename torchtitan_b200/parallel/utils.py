@@ -109,6 +109,22 @@ def dist_mean(x, mesh: Any = None):
     return t / (mesh.size() if mesh is not None else 1)
 
 
+BATCH_INVARIANT_NCCL_ENV = {"NCCL_ALGO": "Ring", "NCCL_PROTO": "Simple", "NCCL_MIN_NCHANNELS": "1",
+                            "NCCL_MAX_NCHANNELS": "1", "NCCL_NVLS_ENABLE": "0", "NCCL_COLLNET_ENABLE": "0"}
+
+
+def apply_batch_invariant_env() -> dict[str, str]:
+    """Fix NCCL's reduction order (ring, one channel, simple protocol, no in-switch or
+    in-network reduction) so collectives give bit-identical results whatever the
+    message size (parity: reference ``distributed/utils.py:218-273``).  Must run before
+    the process group exists.  This framework's GEMM, attention and cross-entropy
+    kernels reduce each output element in a fixed order with no split-K, so they are
+    batch-invariant already."""
+    for k, v in BATCH_INVARIANT_NCCL_ENV.items():
+        os.environ[k] = v
+    return dict(BATCH_INVARIANT_NCCL_ENV)
+
+
 def set_determinism(parallel_dims: Any, device: torch.device, debug: Any,
                     distinct_seed_mesh_dims: list[str] | None = None) -> None:
     if debug.deterministic:

@@ -103,6 +103,8 @@ class Trainer(Stateful, Configurable):
         else:
             self.device = torch.device("cpu")
 
+        if c.debug.batch_invariant:
+            dist_utils.apply_batch_invariant_env()
         world = dist_utils.init_distributed(c.comm, enable_cpu_backend=c.training.enable_cpu_offload,
                                             base_folder=c.dump_folder)
         self.parallel_dims = pd = ParallelDims.from_config(c.parallelism, world)
