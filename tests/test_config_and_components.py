@@ -384,3 +384,22 @@ def test_batch_invariant_env(monkeypatch):
         monkeypatch.delenv(k, raising=False)
     env = apply_batch_invariant_env()
     assert os.environ["NCCL_ALGO"] == "Ring" and os.environ["NCCL_NVLS_ENABLE"] == "0" and len(env) == 6
+
+
+def test_grouped_swiglu_padded_reference_matches_loop():
+    from torchtitan_b200.ops.grouped import expert_segments, grouped_swiglu_padded
+
+    torch.manual_seed(0)
+    counts = torch.tensor([5, 0, 3])
+    w1, w3 = torch.randn(3, 6, 4), torch.randn(3, 6, 4)
+    w2 = torch.randn(3, 4, 6)
+    x = torch.randn(8, 4)
+    tg, kst, kln, P = expert_segments(counts)
+    assert P == 256 and kst.tolist() == [0, 128, 128]
+    xp = torch.zeros(P, 4)
+    xp[:5], xp[128:131] = x[:5], x[5:]
+    yp = grouped_swiglu_padded(xp, w1, w2, w3, counts)
+    f = lambda xs, e: (torch.nn.functional.silu(xs @ w1[e].t()) * (xs @ w3[e].t())) @ w2[e].t()  # noqa: E731
+    torch.testing.assert_close(yp[:5], f(x[:5], 0))
+    torch.testing.assert_close(yp[128:131], f(x[5:], 2))
+    assert torch.count_nonzero(yp[5:128]) == 0

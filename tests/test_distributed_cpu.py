@@ -363,3 +363,62 @@ def _pp(rank, world, out_dir, module, config):
 def test_pipeline_parallel_interleaved_1f1b(module, config):
     with tempfile.TemporaryDirectory() as d:
         _run(_pp, 2, d, module, config)
+
+
+# ---------------------------------------------------------------- fused (peer-memory layout) EP
+def _ep_fused(rank, world):
+    from torchtitan_b200.models.common.moe import MoE
+    from torchtitan_b200.parallel.ep_fused import make_fused_ep_dispatch
+
+    torch.manual_seed(0)
+    E = 2 * world
+    m = MoE(8, 16, num_experts=E, top_k=2, load_balance_coeff=None)
+    m.init_weights(0.1)
+    for p in m.parameters():
+        dist.broadcast(p.data, 0)
+    x = (torch.randn(1, 40 + 7 * rank, 8, generator=torch.Generator().manual_seed(rank)) + rank).requires_grad_()
+    ref = m(x)
+    ref.square().sum().backward()
+    gx_ref = x.grad.clone()
+    e = m.experts
+    gw_ref = []
+    for w in (e.w1, e.w2, e.w3):
+        g = w.grad.clone()
+        dist.all_reduce(g)  # the local reference saw only this rank's tokens
+        gw_ref.append(g[rank * 2:(rank + 1) * 2])
+    full = [p.data.clone() for p in (e.w1, e.w2, e.w3)]
+    for name, f in zip(("w1", "w2", "w3"), full):
+        setattr(e, name, torch.nn.Parameter(f[rank * 2:(rank + 1) * 2].clone()))
+    m.zero_grad()
+    m.ep_dispatch = make_fused_ep_dispatch(dist.group.WORLD, E)
+    assert m.ep_dispatch.comm.comm is None
+    xr = x.detach().clone().requires_grad_()
+    out = m(xr)
+    assert m.ep_dispatch.comm.comm == "collective"
+    torch.testing.assert_close(out, ref, rtol=1e-5, atol=1e-5)
+    out.square().sum().backward()
+    torch.testing.assert_close(xr.grad, gx_ref, rtol=1e-5, atol=1e-5)
+    # expert weight gradients are summed over every rank's routed rows
+    for g, w in zip(gw_ref, (e.w1, e.w2, e.w3)):
+        torch.testing.assert_close(w.grad, g, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_fused_expert_parallel_matches_local(world):
+    _run(_ep_fused, world)
+
+
+def test_fused_ep_plan_layout():
+    from torchtitan_b200.parallel.ep_fused import Plan
+
+    M = torch.tensor([[3, 0, 5, 1], [2, 130, 0, 4]])  # 2 ranks x 4 experts (2 per rank)
+    p0, p1 = Plan(M, 0, torch.device("cpu")), Plan(M, 1, torch.device("cpu"))
+    # owner 0: expert 0 gets 3 + 2 rows -> [0, 128); expert 1 gets 130 -> [128, 384)
+    assert p0.P == 384 and p1.P == 256 and p0.P_max == 384
+    assert p0.local_counts.tolist() == [5, 130]
+    # rank 0's rows: expert 0 -> owner 0 rows 0..2; expert 2 -> owner 1 rows 0..4; expert 3 -> owner 1 row 128
+    assert p0.dest_rank.tolist() == [0, 0, 0, 1, 1, 1, 1, 1, 1]
+    assert p0.dest_row.tolist() == [0, 1, 2, 0, 1, 2, 3, 4, 128]
+    # rank 1's rows for expert 0 follow rank 0's; expert 1 starts at 128; expert 3 after rank 0's row
+    assert p1.dest_row[:3].tolist() == [3, 4, 128] and p1.dest_row[-4:].tolist() == [129, 130, 131, 132]
+    assert p0.pad_rows.numel() == 384 - 135 and p1.real_rows.numel() == 10

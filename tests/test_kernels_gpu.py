@@ -294,3 +294,22 @@ def test_adamw_fused_clip(ext):
     ops.fused_adamw_([p], [g], [m], [v], clip_total=total, clip_max=1.0, **kw)
     R.adamw_([rp], [g * coef], [rm], [rv], **kw)
     assert _rel(p, rp) < 1e-5 and _rel(m, rm) < 1e-5
+
+
+def test_grouped_swiglu_padded_matches_unpadded():
+    from torchtitan_b200.ops.grouped import expert_segments, grouped_swiglu_padded
+
+    torch.manual_seed(0)
+    E, D, H = 3, 256, 384
+    counts = torch.tensor([70, 0, 200], device="cuda")
+    x = torch.randn(int(counts.sum()), D, device="cuda", dtype=torch.bfloat16)
+    w1, w3 = (torch.randn(E, H, D, device="cuda", dtype=torch.bfloat16) * 0.05 for _ in range(2))
+    w2 = torch.randn(E, D, H, device="cuda", dtype=torch.bfloat16) * 0.05
+    tg, kst, kln, P = expert_segments(counts)
+    xp = torch.zeros(P, D, device="cuda", dtype=torch.bfloat16)
+    xp[0:70] = x[:70]
+    xp[int(kst[2]):int(kst[2]) + 200] = x[70:]
+    y = ops.grouped_swiglu(x, w1, w2, w3, counts)
+    yp = grouped_swiglu_padded(xp, w1, w2, w3, counts)
+    torch.testing.assert_close(yp[:70], y[:70], rtol=0, atol=0)
+    torch.testing.assert_close(yp[int(kst[2]):int(kst[2]) + 200], y[70:], rtol=0, atol=0)

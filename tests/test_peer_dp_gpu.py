@@ -131,3 +131,40 @@ def _trainer(rank, world, out_dir):
 def test_peer_data_parallel_trainer_two_gpus():
     with tempfile.TemporaryDirectory() as d:
         _run(_trainer, 2, d)
+
+
+def _ep_peer(rank, world):
+    from torchtitan_b200.models.common.moe import MoE
+    from torchtitan_b200.parallel.ep_fused import make_fused_ep_dispatch
+
+    torch.manual_seed(0)
+    E = 4 * world
+    m = MoE(256, 512, num_experts=E, top_k=2, load_balance_coeff=None).cuda()
+    m.init_weights(0.05)
+    for p in m.parameters():
+        dist.broadcast(p.data, 0)
+    m = m.to(torch.bfloat16)
+    x = torch.randn(1, 300 + 64 * rank, 256, device="cuda", dtype=torch.bfloat16,
+                    generator=torch.Generator(device="cuda").manual_seed(rank)).requires_grad_()
+    ref = m(x)
+    ref.float().square().sum().backward()
+    gx_ref = x.grad.clone()
+    e = m.experts
+    for name in ("w1", "w2", "w3"):
+        setattr(e, name, torch.nn.Parameter(getattr(e, name).data[rank * 4:(rank + 1) * 4].clone()))
+    m.ep_dispatch = make_fused_ep_dispatch(dist.group.WORLD, E)
+    xr = x.detach().clone().requires_grad_()
+    out = m(xr)
+    assert m.ep_dispatch.comm.comm == "peer"
+    torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
+    out.float().square().sum().backward()
+    torch.testing.assert_close(xr.grad.float(), gx_ref.float(), rtol=5e-2, atol=5e-2)
+    torch.cuda.synchronize()
+    from torchtitan_b200.ops._ext import ext
+
+    assert ext().dp_error_code(True) == 0
+
+
+@two_gpus
+def test_fused_expert_parallel_peer_memory():
+    _run(_ep_peer, 2)

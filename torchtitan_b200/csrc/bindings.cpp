@@ -313,6 +313,26 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       },
       py::arg("sigs"), py::arg("rank"), py::arg("slot"), py::arg("epoch"), py::arg("limit_s") = 0.0);
   m.def("dp_error_code", &ttb::dp_error_code, py::arg("reset") = true);
+  m.def("ep_scatter_rows", [](Tensor src, Tensor dest_rank, Tensor dest_row, std::vector<int64_t> bases) {
+    check_cuda_bf16(src, "src");
+    TORCH_CHECK(src.dim() == 2 && src.is_contiguous(), "src: contiguous [n, D]");
+    TORCH_CHECK(dest_rank.scalar_type() == at::kInt && dest_row.scalar_type() == at::kLong, "index dtypes");
+    TORCH_CHECK(dest_rank.numel() == src.size(0) && dest_row.numel() == src.size(0), "index lengths");
+    c10::cuda::CUDAGuard g(src.device());
+    ttb::ep_scatter_rows(src.data_ptr(), src.size(0), (int)src.size(1), dest_rank.data_ptr<int32_t>(),
+                         dest_row.data_ptr<int64_t>(), reinterpret_cast<void* const*>(bases.data()),
+                         (int)bases.size(), stream());
+  });
+  m.def("ep_gather_rows", [](Tensor dst, Tensor src_rank, Tensor src_row, std::vector<int64_t> bases) {
+    check_cuda_bf16(dst, "dst");
+    TORCH_CHECK(dst.dim() == 2 && dst.is_contiguous(), "dst: contiguous [n, D]");
+    TORCH_CHECK(src_rank.scalar_type() == at::kInt && src_row.scalar_type() == at::kLong, "index dtypes");
+    TORCH_CHECK(src_rank.numel() == dst.size(0) && src_row.numel() == dst.size(0), "index lengths");
+    c10::cuda::CUDAGuard g(dst.device());
+    ttb::ep_gather_rows(dst.data_ptr(), dst.size(0), (int)dst.size(1), src_rank.data_ptr<int32_t>(),
+                        src_row.data_ptr<int64_t>(), reinterpret_cast<void* const*>(bases.data()),
+                        (int)bases.size(), stream());
+  });
   m.def("dp_error_info", []() {
     int v[4];
     ttb::dp_error_info(v);

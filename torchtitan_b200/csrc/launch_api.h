@@ -77,7 +77,13 @@ void dp_reduce_scatter_bucket(const void* const* peer_grads, uint32_t* const* pe
 void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint32_t epoch, cudaStream_t s,
                 double limit_s = 0.0);
 int dp_error_code(bool reset);
-void dp_error_info(int* out4);  // slot, epoch, source rank, flag value of the first failed wait
+void dp_error_info(int* out4);
+
+// ep_comm.cu: expert-parallel row movement over NVLink peer memory
+void ep_scatter_rows(const void* src, int64_t n, int d, const int32_t* dest_rank, const int64_t* dest_row,
+                     void* const* peer_bases, int world, cudaStream_t s);
+void ep_gather_rows(void* dst, int64_t n, int d, const int32_t* src_rank, const int64_t* src_row,
+                    void* const* peer_bases, int world, cudaStream_t s);  // slot, epoch, source rank, flag value of the first failed wait
 
 struct SumSqTensor {
   const void* x;

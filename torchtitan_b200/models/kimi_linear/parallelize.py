@@ -47,7 +47,7 @@ def parallelize_kimi(model: nn.Module, *, parallel_dims: Any, training: Any, par
         logger.info(f"applied Ulysses context parallel (cp={pd.cp})")
     moes = [blk.moe for blk in model.layers.values() if getattr(blk, "moe", None) is not None]
     if pd.ep_enabled and moes:
-        apply_ep(moes, pd.get_mesh("ep"))
+        apply_ep(moes, pd.get_mesh("ep"), backend=parallelism.expert_parallel_comm_backend)
         logger.info(f"applied expert parallel (ep={pd.ep}) to {len(moes)} MoE layers")
     if ac_config.mode != "none":
         apply_ac(model, ac_config)

@@ -78,3 +78,67 @@ def grouped_swiglu_cuda(x, w1, w2, w3, counts):
     dt = torch.bfloat16
     return _GroupedSwiGLU.apply(x.to(dt).contiguous(), w1.to(dt).contiguous(), w2.to(dt).contiguous(),
                                 w3.to(dt).contiguous(), counts)
+
+
+def expert_segments(counts: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, int]:
+    """Padded expert-major layout for ``counts`` rows per expert: (tile_group [P/128],
+    kstart [E], klen [E], P) with every expert segment starting on a 128-row boundary."""
+    counts = counts.to(torch.int64)
+    padded = (counts + TILE - 1) // TILE * TILE
+    pend = torch.cumsum(padded, 0)
+    P = int(pend[-1]) if counts.numel() else 0
+    tile_start = torch.arange(P // TILE, device=counts.device) * TILE
+    tg = torch.searchsorted(pend, tile_start, right=True).to(torch.int32)
+    return tg, (pend - padded).to(torch.int32), padded.to(torch.int32), P
+
+
+class _GroupedSwiGLUPadded(torch.autograd.Function):
+    """Grouped SwiGLU on rows already laid out in padded expert segments (padding rows
+    zero), e.g. written there directly by a peer-memory expert-parallel dispatch."""
+
+    @staticmethod
+    def forward(ctx, xp, w1, w2, w3, tg, kst, kln):
+        ext = _ext.ext()
+        E, H, D = w1.shape
+        h1 = ext.gemm_grouped_rows(xp, w1.reshape(E * H, D), tg, H, H, False)
+        h3 = ext.gemm_grouped_rows(xp, w3.reshape(E * H, D), tg, H, H, False)
+        a = ext.swiglu_fwd(h1, h3)
+        yp = ext.gemm_grouped_rows(a, w2.reshape(E * D, H), tg, D, D, False)
+        ctx.save_for_backward(xp, h1, h3, a, w1, w2, w3, tg, kst, kln)
+        return yp
+
+    @staticmethod
+    def backward(ctx, dyp):
+        ext = _ext.ext()
+        xp, h1, h3, a, w1, w2, w3, tg, kst, kln = ctx.saved_tensors
+        E, H, D = w1.shape
+        dyp = dyp.contiguous()
+        da = ext.gemm_grouped_rows(dyp, w2.reshape(E * D, H), tg, H, D, True)
+        dh1, dh3 = ext.swiglu_bwd(da, h1, h3)
+        dx = ext.gemm_grouped_rows(dh1, w1.reshape(E * H, D), tg, D, H, True)
+        dx = dx + ext.gemm_grouped_rows(dh3, w3.reshape(E * H, D), tg, D, H, True)
+        dw2 = ext.gemm_grouped_k(dyp, a, kst, kln)
+        dw1 = ext.gemm_grouped_k(dh1, xp, kst, kln)
+        dw3 = ext.gemm_grouped_k(dh3, xp, kst, kln)
+        return dx, dw1.to(w1.dtype), dw2.to(w2.dtype), dw3.to(w3.dtype), None, None, None
+
+
+def _grouped_swiglu_padded_ref(xp, w1, w2, w3, kst, kln):
+    outs = []
+    for e in range(w1.shape[0]):
+        seg = xp[int(kst[e]):int(kst[e]) + int(kln[e])]
+        h = torch.nn.functional.silu(seg @ w1[e].t()) * (seg @ w3[e].t())
+        outs.append(h @ w2[e].t())
+    return torch.cat(outs) if outs else xp.new_zeros(0, w2.shape[1])
+
+
+def grouped_swiglu_padded(xp, w1, w2, w3, counts):
+    """``xp``: [P, D] rows in the padded expert-major layout of ``counts`` (zero padding)."""
+    tg, kst, kln, P = expert_segments(counts)
+    if xp.shape[0] != P:
+        raise ValueError(f"padded input has {xp.shape[0]} rows, layout needs {P}")
+    if not xp.is_cuda:
+        return _grouped_swiglu_padded_ref(xp, w1, w2, w3, kst, kln)
+    dt = torch.bfloat16
+    return _GroupedSwiGLUPadded.apply(xp.to(dt).contiguous(), w1.to(dt).contiguous(), w2.to(dt).contiguous(),
+                                      w3.to(dt).contiguous(), tg, kst, kln)

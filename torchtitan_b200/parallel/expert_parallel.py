@@ -51,7 +51,10 @@ def make_ep_dispatch(ep_group, num_experts: int):
     return dispatch
 
 
-def apply_ep(moe_modules: list[nn.Module], ep_mesh) -> None:
+def apply_ep(moe_modules: list[nn.Module], ep_mesh, backend: str = "standard") -> None:
+    """``backend``: ``standard`` = NCCL all-to-all dispatch above; ``fused`` = rows stored
+    straight into the owners' padded expert-major buffers over peer memory
+    (``parallel.ep_fused``)."""
     from torch.distributed.tensor import Shard, distribute_tensor
 
     group = ep_mesh.get_group()
@@ -60,4 +63,9 @@ def apply_ep(moe_modules: list[nn.Module], ep_mesh) -> None:
         for name in ("w1", "w2", "w3"):
             p = getattr(ex, name)
             setattr(ex, name, nn.Parameter(distribute_tensor(p.data, ep_mesh, [Shard(0)])))
-        moe.ep_dispatch = make_ep_dispatch(group, moe.num_experts)
+        if backend == "fused":
+            from .ep_fused import make_fused_ep_dispatch
+
+            moe.ep_dispatch = make_fused_ep_dispatch(group, moe.num_experts)
+        else:
+            moe.ep_dispatch = make_ep_dispatch(group, moe.num_experts)

@@ -64,7 +64,7 @@ def parallelize_decoder(model: nn.Module, *, parallel_dims: Any, training: Any, 
         logger.info(f"applied context parallel ({parallelism.context_parallel_method}, cp={pd.cp})")
     moes = [blk.moe for blk in model.layers.values() if getattr(blk, "moe", None) is not None]
     if pd.ep_enabled and moes:
-        apply_ep(moes, pd.get_mesh("ep"))
+        apply_ep(moes, pd.get_mesh("ep"), backend=parallelism.expert_parallel_comm_backend)
         logger.info(f"applied expert parallel (ep={pd.ep}) to {len(moes)} MoE layers")
     if ac_config.mode != "none":
         apply_ac(model, ac_config)
