@@ -297,6 +297,7 @@ def test_adamw_fused_clip(ext):
 
 
 def test_grouped_swiglu_padded_matches_unpadded():
+    from torchtitan_b200 import ops
     from torchtitan_b200.ops.grouped import expert_segments, grouped_swiglu_padded
 
     torch.manual_seed(0)
