@@ -422,3 +422,26 @@ def test_fused_ep_plan_layout():
     # rank 1's rows for expert 0 follow rank 0's; expert 1 starts at 128; expert 3 after rank 0's row
     assert p1.dest_row[:3].tolist() == [3, 4, 128] and p1.dest_row[-4:].tolist() == [129, 130, 131, 132]
     assert p0.pad_rows.numel() == 384 - 135 and p1.real_rows.numel() == 10
+
+
+def _ep_trainer(rank, world, out_dir):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    res = []
+    for backend in ("standard", "fused"):
+        t = Trainer(ConfigManager().parse_args([
+            "--module", "qwen3", "--config", "qwen3_debugmodel_moe", "--training.steps", "2",
+            "--training.seq-len", "64", "--training.local-batch-size", "2", "--training.dtype", "float32",
+            "--training.mixed-precision-param", "float32", "--activation-checkpoint.mode", "none",
+            "--parallelism.expert-parallel-degree", "2", "--parallelism.expert-parallel-comm-backend", backend,
+            "--debug.seed", "0", "--metrics.log-freq", "1", "--dump-folder", os.path.join(out_dir, backend)]))
+        t.train()
+        res.append(t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"])
+        t.close()
+    assert abs(res[0] - res[1]) < 1e-5 * abs(res[0]), res
+
+
+def test_fused_ep_trainer_matches_standard():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_ep_trainer, 2, d)
