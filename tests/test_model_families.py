@@ -153,3 +153,31 @@ def test_block_attn_res_uniform_at_init_and_softmax_weights():
     Kn = V * torch.rsqrt(V.pow(2).mean(-1, keepdim=True) + 1e-5)
     w = torch.softmax((Kn @ q[0]), 0)
     torch.testing.assert_close(block_attn_res(blocks, partial, q, norm), (w[..., None] * V).sum(0))
+
+
+def test_kimi_multimodal_splices_projected_patches():
+    from torchtitan_b200.models.kimi_linear import model_registry
+    from torchtitan_b200.models.kimi_linear.multimodal import (KimiLinearMultimodal, PatchVisionTower,
+                                                               image_label_mask)
+
+    spec = model_registry("debugmodel")
+    torch.manual_seed(0)
+    llm = spec.model.build()
+    tower = PatchVisionTower(image_size=28, patch=14, dim=32)
+    mm = KimiLinearMultimodal(llm, vision_tower=tower, vision_dim=32, projector_dim=64)
+    mm.init_weights()
+    tokens = torch.randint(0, spec.model.vocab_size, (2, 64))
+    tokens[0, 5:9] = -200   # one image = 4 patches per sample
+    tokens[1, 20:24] = -200
+    pix = torch.randn(2, 1, 3, 28, 28)
+    emb = mm.embed(tokens, pix)
+    proj = mm.projector(tower(pix.flatten(0, 1)))
+    torch.testing.assert_close(emb[0, 5:9], proj[0])
+    torch.testing.assert_close(emb[1, 20:24], proj[1])
+    torch.testing.assert_close(emb[0, :5], llm.embed_tokens(tokens[0, :5]))
+    logits = mm(tokens, pix)
+    labels = image_label_mask(tokens.roll(-1, 1), tokens)
+    loss = F.cross_entropy(logits.flatten(0, 1).float(), labels.flatten(), ignore_index=-100)
+    loss.backward()
+    assert mm.projector.fc1.weight.grad is not None and tower.proj.weight.grad is None
+    assert (labels[0, 4:9] == -100).all()

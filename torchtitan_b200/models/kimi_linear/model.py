@@ -349,8 +349,11 @@ class KimiLinearModel(BaseModel):
             self.final_res_proj.weight.zero_()
             self.final_res_norm.init_weights()
 
-    def forward(self, tokens, attention_masks=None, positions=None, **kw):
-        h = self.embed_tokens(tokens) if self.embed_tokens is not None else tokens
+    def forward(self, tokens, attention_masks=None, positions=None, inputs_embeds=None, **kw):
+        if inputs_embeds is not None:
+            h = inputs_embeds
+        else:
+            h = self.embed_tokens(tokens) if self.embed_tokens is not None else tokens
         if self.model_args.attn_res_blocks > 0:
             state = ([], h)
             for layer in self.layers.values():
