@@ -403,3 +403,36 @@ def test_grouped_swiglu_padded_reference_matches_loop():
     torch.testing.assert_close(yp[:5], f(x[:5], 0))
     torch.testing.assert_close(yp[128:131], f(x[5:], 2))
     assert torch.count_nonzero(yp[5:128]) == 0
+
+
+def test_multimodal_dataloader_packs_images(tmp_path):
+    import json
+
+    from PIL import Image
+
+    from torchtitan_b200.components.loss import IGNORE_INDEX
+    from torchtitan_b200.components.mm_dataloader import MultimodalDataLoader
+
+    for n in ("a.png", "b.png"):
+        Image.new("RGB", (40, 30), (255, 0, 0) if n == "a.png" else (0, 0, 255)).save(tmp_path / n)
+    recs = [{"text": "see <image> here", "images": ["a.png"]},
+            {"text": "two <image> and <image>.", "images": ["a.png", "b.png"]}]
+    (tmp_path / "d.jsonl").write_text("\n".join(json.dumps(r) for r in recs))
+
+    class Tok:
+        bos_id, eos_id = 1, 2
+
+        def encode(self, t):
+            return [3 + ord(ch) % 40 for ch in t]
+
+    dl = MultimodalDataLoader(MultimodalDataLoader.Config(dataset_path=str(tmp_path / "d.jsonl"), image_size=28,
+                                                          patch_size=14, infinite=False),
+                              tokenizer=Tok(), seq_len=128, local_batch_size=1)
+    (inp, labels), = list(dl)
+    ids = inp["input"][0]
+    assert inp["pixel_values"].shape == (3, 3, 28, 28)
+    assert int((ids == -200).sum()) == 12  # 3 images x 4 patches
+    full_next = torch.cat([ids[1:], labels[0][-1:]])
+    assert (labels[0][full_next == -200] == IGNORE_INDEX).all()
+    # red image first, blue last (order of appearance), normalised to [-1, 1]
+    assert inp["pixel_values"][0, 0].mean() > 0.9 and inp["pixel_values"][2, 2].mean() > 0.9
