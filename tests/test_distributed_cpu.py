@@ -445,3 +445,80 @@ def _ep_trainer(rank, world, out_dir):
 def test_fused_ep_trainer_matches_standard():
     with tempfile.TemporaryDirectory() as d:
         _run(_ep_trainer, 2, d)
+
+
+# ---------------------------------------------------------------- Kimi-Linear tensor parallel
+def _kimi_tp(rank, world, out_dir):
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.components.loss import cross_entropy_loss
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.models.kimi_linear import model_registry
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", "kimi_linear", "--config", "kimi_linear_debugmodel", "--training.steps", "1",
+        "--training.seq-len", "64", "--training.local-batch-size", "2", "--training.dtype", "float32",
+        "--training.mixed-precision-param", "float32", "--activation-checkpoint.mode", "none",
+        "--parallelism.tensor-parallel-degree", "2", "--parallelism.data-parallel-shard-degree", "1",
+        "--debug.seed", "0", "--dump-folder", out_dir]))
+    model = t.model_parts[0]
+    full = get_model_state_dict(model, options=StateDictOptions(full_state_dict=True))
+    ref = model_registry("debugmodel").model.build()
+    ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in full.items()}, strict=False)
+    tokens = torch.randint(0, 2048, (2, 64), generator=torch.Generator().manual_seed(3))
+    labels = tokens.roll(-1, 1)
+    loss_ref = cross_entropy_loss(ref(tokens), labels)
+    loss_ref.backward()
+    loss_tp = t._loss(model(tokens), labels)
+    torch.testing.assert_close(loss_tp, loss_ref, rtol=1e-5, atol=1e-4)
+    loss_tp.backward()
+    named = dict(ref.named_parameters())
+    for n, p in model.named_parameters():
+        g = p.grad.full_tensor() if hasattr(p.grad, "full_tensor") else p.grad
+        r = named[n.replace("_checkpoint_wrapped_module.", "")].grad
+        # fp32 summation-order noise only: relative to the gradient's scale
+        assert float((g - r).abs().max()) <= 2e-4 * float(r.abs().max()) + 1e-7, n
+    t.close()
+
+
+def test_kimi_tensor_parallel_matches_single_device():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_kimi_tp, 2, d)
+
+
+def _llama_tp_grads(rank, world, out_dir, sp):
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.components.loss import cross_entropy_loss
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.models.llama3 import model_registry
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "1",
+        "--training.seq-len", "64", "--parallelism.tensor-parallel-degree", "2",
+        "--parallelism.data-parallel-shard-degree", "1", "--debug.seed", "0", "--dump-folder", out_dir,
+        *([] if sp else ["--parallelism.no-enable-sequence-parallel"])]))
+    model = t.model_parts[0]
+    full = get_model_state_dict(model, options=StateDictOptions(full_state_dict=True))
+    ref = model_registry("debugmodel").model.build()
+    ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in full.items()}, strict=False)
+    ref.rope.init_weights()
+    tokens = torch.randint(0, 2048, (2, 64), generator=torch.Generator().manual_seed(3))
+    labels = tokens.roll(-1, 1)
+    cross_entropy_loss(ref(tokens), labels).backward()
+    loss_tp = t._loss(model(tokens), labels)
+    loss_tp.backward()
+    named = dict(ref.named_parameters())
+    for n, p in model.named_parameters():
+        g = p.grad.full_tensor() if hasattr(p.grad, "full_tensor") else p.grad
+        r = named[n.replace("_checkpoint_wrapped_module.", "")].grad
+        assert float((g - r).abs().max()) <= 2e-4 * float(r.abs().max()) + 1e-7, (n, sp)
+    t.close()
+
+
+@pytest.mark.parametrize("sp", [True, False])
+def test_llama_tensor_parallel_gradients(sp):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_llama_tp_grads, 2, d, sp)

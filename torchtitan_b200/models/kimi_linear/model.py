@@ -147,6 +147,11 @@ class KimiMLAAttention(nn.Module):
         H = q.shape[2]
         ckv = self.kv_a_proj_with_mqa(x)
         k_pass, k_rot = ckv.split([self.kv_lora_rank, self.rope], dim=-1)
+        if getattr(self, "tp_group", None) is not None:
+            # the shared key slice feeds only this rank's heads: its gradient is a partial sum
+            from torchtitan_b200.parallel.tensor_parallel import grad_all_reduce
+
+            k_rot = grad_all_reduce(k_rot, self.tp_group)
         kv = self.kv_b_proj(self.kv_a_layernorm(k_pass.contiguous())).view(B, T, H, self.nope + self.vd)
         k_nope, v = kv.split([self.nope, self.vd], dim=-1)
         k = torch.cat([k_nope, k_rot[:, :, None, :].expand(B, T, H, self.rope)], dim=-1)

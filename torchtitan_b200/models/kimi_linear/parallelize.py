@@ -32,7 +32,12 @@ def parallelize_kimi(model: nn.Module, *, parallel_dims: Any, training: Any, par
                      **_: Any) -> nn.Module:
     pd = parallel_dims
     if pd.tp_enabled:
-        raise NotImplementedError("tensor parallelism for Kimi-Linear is not wired; use EP/CP/FSDP/PP")
+        from torchtitan_b200.parallel.tensor_parallel import apply_tp_kimi
+
+        if model.model_args.tie_word_embeddings:
+            raise NotImplementedError("tensor parallelism with tied embeddings is not wired")
+        apply_tp_kimi(model, pd.get_mesh("tp"), loss_parallel=not parallelism.disable_loss_parallel)
+        logger.info(f"applied tensor parallel to MLA heads and dense MLPs (tp={pd.tp})")
     if pd.cp_enabled:
         if parallelism.context_parallel_method != "ulysses":
             raise ValueError("Kimi-Linear context parallelism uses Ulysses (KDA needs the whole sequence per head)")

@@ -116,8 +116,8 @@ def tp_linear(x: torch.Tensor, w: torch.Tensor, mode: str, group, sequence_paral
         if mode == "row":
             return async_tp.matmul_rs(x, w, group)
     if mode == "col":
-        if sequence_parallel:
-            x = all_gather_seq(x, group)
+        # replicated input: each rank's dgrad is a partial sum over its output shard
+        x = all_gather_seq(x, group) if sequence_parallel else grad_all_reduce(x, group)
         return mm(x, w)
     if mode == "row":
         y = mm(x, w)
@@ -259,6 +259,44 @@ def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_p
     model._tp_group = group
     model._tp_loss_parallel = loss_parallel
     model._sp_degree = ws if sequence_parallel else 1
+
+
+def apply_tp_kimi(model: nn.Module, tp_mesh, *, loss_parallel: bool) -> None:
+    """Kimi-Linear TP plan (parity: reference ``kimi_linear/parallelize.py:73-259``): MLA
+    heads (``q_proj``, ``kv_b_proj`` column, ``o_proj`` row) and dense MLPs are sharded;
+    KDA layers, the latent projection, norms and routed experts are computed replicated
+    on every TP rank (activations are replicated, no sequence parallelism); the LM head
+    is column-parallel over the vocabulary (loss parallel)."""
+    group = tp_mesh.get_group()
+    ws = tp_mesh.size()
+    for blk in model.layers.values():
+        att = blk.self_attn
+        if not blk.is_linear_attn:
+            if att.h % ws:
+                raise ValueError(f"TP degree {ws} must divide num_attention_heads {att.h}")
+            parallelize_linear(att.q_proj, "col", tp_mesh, False)
+            parallelize_linear(att.kv_b_proj, "col", tp_mesh, False)
+            parallelize_linear(att.o_proj, "row", tp_mesh, False)
+            att.tp_group = group
+        if not blk.is_moe:
+            parallelize_linear(blk.ffn.gate_proj, "col", tp_mesh, False)
+            parallelize_linear(blk.ffn.up_proj, "col", tp_mesh, False)
+            parallelize_linear(blk.ffn.down_proj, "row", tp_mesh, False)
+    if model.lm_head is not None:
+        parallelize_linear(model.lm_head, "col", tp_mesh, False)
+        if not loss_parallel:
+            orig = model.lm_head.forward
+
+            def out_fwd(x, _orig=orig):
+                y = _orig(x)
+                outs = [torch.empty_like(y) for _ in range(ws)]
+                dist.all_gather(outs, y.contiguous(), group=group)
+                return torch.cat(outs, -1)
+
+            model.lm_head.forward = out_fwd
+    model._tp_group = group
+    model._tp_loss_parallel = loss_parallel
+    model._sp_degree = 1
 
 
 def maybe_enable_async_tp(parallelism: Any, tp_mesh) -> None:
