@@ -522,3 +522,54 @@ def _llama_tp_grads(rank, world, out_dir, sp):
 def test_llama_tensor_parallel_gradients(sp):
     with tempfile.TemporaryDirectory() as d:
         _run(_llama_tp_grads, 2, d, sp)
+
+
+# ---------------------------------------------------------------- context parallel, gradient-exact
+def _cp_grads(rank, world, out_dir, module, config, method):
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.components.loss import cross_entropy_loss
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+    import importlib
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", module, "--config", config, "--training.steps", "1", "--training.seq-len", "64",
+        "--training.local-batch-size", "2", "--training.dtype", "float32",
+        "--training.mixed-precision-param", "float32", "--activation-checkpoint.mode", "none",
+        "--parallelism.context-parallel-degree", "2", "--parallelism.context-parallel-method", method,
+        "--parallelism.data-parallel-shard-degree", "1", "--debug.seed", "0", "--dump-folder", out_dir]))
+    model = t.model_parts[0]
+    full = get_model_state_dict(model, options=StateDictOptions(full_state_dict=True))
+    spec = importlib.import_module(f"torchtitan_b200.models.{module}").model_registry("debugmodel")
+    ref = spec.model.build()
+    ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in full.items()}, strict=False)
+    if hasattr(ref, "rope"):
+        ref.rope.init_weights()
+    tokens = torch.randint(0, spec.model.vocab_size, (2, 64), generator=torch.Generator().manual_seed(3))
+    labels = tokens.roll(-1, 1)
+    loss_ref = cross_entropy_loss(ref(tokens), labels)
+    loss_ref.backward()
+    inp, lab, _, kw = t.post_dataloading_process({"input": tokens}, labels)
+    loss_local = t._loss(model(inp, **kw), lab)
+    total = loss_local.detach().clone()
+    dist.all_reduce(total)
+    torch.testing.assert_close(total, loss_ref, rtol=1e-5, atol=1e-4)
+    loss_local.backward()
+    named = dict(ref.named_parameters())
+    for n, p in model.named_parameters():
+        g = p.grad.full_tensor() if hasattr(p.grad, "full_tensor") else p.grad.clone()
+        # FSDP on gloo averaged the shards' gradients over the cp ranks (the trainer scales the
+        # loss by that degree to compensate); summing the average over ranks gives the full gradient
+        dist.all_reduce(g)
+        r = named[n.replace("_checkpoint_wrapped_module.", "")].grad
+        assert float((g - r).abs().max()) <= 2e-4 * float(r.abs().max()) + 1e-7, (n, method)
+    t.close()
+
+
+@pytest.mark.parametrize("module,config,method", [("llama3", "llama3_debugmodel_cpu", "ring"),
+                                                  ("llama3", "llama3_debugmodel_cpu", "ulysses"),
+                                                  ("kimi_linear", "kimi_linear_debugmodel", "ulysses")])
+def test_context_parallel_gradients_match_single_device(module, config, method):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_cp_grads, 2, d, module, config, method)
