@@ -573,3 +573,51 @@ def _cp_grads(rank, world, out_dir, module, config, method):
 def test_context_parallel_gradients_match_single_device(module, config, method):
     with tempfile.TemporaryDirectory() as d:
         _run(_cp_grads, 2, d, module, config, method)
+
+
+def _pp_grads(rank, world, out_dir, schedule):
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.components.loss import cross_entropy_loss
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.models.llama3 import model_registry
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "1",
+        "--training.seq-len", "64", "--parallelism.pipeline-parallel-degree", "2",
+        "--parallelism.data-parallel-shard-degree", "1", "--parallelism.pipeline-parallel-microbatch-size", "1",
+        "--training.local-batch-size", "4", "--parallelism.pipeline-parallel-schedule", schedule,
+        "--debug.seed", "0", "--dump-folder", out_dir]))
+    full = {}
+    for part in t.model_parts:
+        full.update(get_model_state_dict(part, options=StateDictOptions(full_state_dict=True)))
+    gathered = [None] * world
+    dist.all_gather_object(gathered, {k: v for k, v in full.items()})
+    merged = {}
+    for d in gathered:
+        merged.update(d)
+    ref = model_registry("debugmodel").model.build()
+    ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in merged.items()}, strict=False)
+    ref.rope.init_weights()
+    tokens = torch.randint(0, 2048, (4, 64), generator=torch.Generator().manual_seed(3))
+    labels = tokens.roll(-1, 1)
+    loss_ref = cross_entropy_loss(ref(tokens), labels) / labels.numel()
+    loss_ref.backward()
+    loss = t.forward_backward_step(input_dict={"input": tokens}, labels=labels,
+                                   global_valid_tokens=torch.tensor(float(labels.numel())))
+    if t.pp_has_last_stage:
+        torch.testing.assert_close(loss.reshape(()), loss_ref, rtol=1e-5, atol=1e-5)
+    named = dict(ref.named_parameters())
+    for part in t.model_parts:
+        for n, p in part.named_parameters():
+            g = p.grad.full_tensor() if hasattr(p.grad, "full_tensor") else p.grad
+            r = named[n.replace("_checkpoint_wrapped_module.", "")].grad
+            assert float((g - r).abs().max()) <= 2e-4 * float(r.abs().max()) + 1e-8, (n, schedule)
+    t.close()
+
+
+@pytest.mark.parametrize("schedule", ["1F1B", "Interleaved1F1B", "GPipe"])
+def test_pipeline_parallel_gradients_match_single_device(schedule):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_pp_grads, 2, d, schedule)

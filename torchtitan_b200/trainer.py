@@ -230,7 +230,10 @@ class Trainer(Stateful, Configurable):
         return self.loss_fn(pred, labels)
 
     def _pp_loss(self, pred, labels):
-        return self._loss(pred, labels)
+        # the schedule backpropagates this value: normalise by the step's global token count
+        # here, as the non-PP path does before its backward
+        comp = getattr(self.model_parts[0], "_fsdp_grad_compensation", 1)  # see forward_backward_step
+        return self._loss(pred, labels) / self._pp_token_norm * comp
 
     def batch_generator(self, data: Iterable) -> Iterator:
         it = iter(data)
@@ -272,6 +275,7 @@ class Trainer(Stateful, Configurable):
         inputs, labels, extra_inputs, extra_kwargs = self.post_dataloading_process(input_dict, labels)
         pd = self.parallel_dims
         if pd.pp_enabled:
+            self._pp_token_norm = global_valid_tokens
             with self.train_context():
                 targets, losses = (labels, []) if self.pp_has_last_stage else (None, None)
                 if self.pp_has_first_stage:
@@ -279,7 +283,8 @@ class Trainer(Stateful, Configurable):
                 else:
                     self.pp_schedule.step(**extra_kwargs, target=targets, losses=losses)
             if self.pp_has_last_stage:
-                return (torch.sum(torch.stack(losses)) / global_valid_tokens).to(self.device)
+                comp = getattr(self.model_parts[0], "_fsdp_grad_compensation", 1)
+                return (torch.sum(torch.stack(losses)) / comp).to(self.device)
             return torch.tensor([-1.0], device=self.device)
         with self.train_context():
             pred = self.model_parts[0](inputs, **extra_inputs, **extra_kwargs)
