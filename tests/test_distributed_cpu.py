@@ -621,3 +621,65 @@ def _pp_grads(rank, world, out_dir, schedule):
 def test_pipeline_parallel_gradients_match_single_device(schedule):
     with tempfile.TemporaryDirectory() as d:
         _run(_pp_grads, 2, d, schedule)
+
+
+# ---------------------------------------------------------------- data parallel, gradient-exact
+def _dp_grads(rank, world, out_dir, module, config, extra):
+    import importlib
+
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.components.loss import cross_entropy_loss
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", module, "--config", config, "--training.steps", "1", "--training.seq-len", "64",
+        "--training.local-batch-size", "2", "--training.dtype", "float32",
+        "--training.mixed-precision-param", "float32", "--activation-checkpoint.mode", "none",
+        "--debug.seed", "0", "--dump-folder", out_dir, *extra]))
+    model = t.model_parts[0]
+    rt = getattr(model, "_dp_runtime", None)
+    full = get_model_state_dict(model, options=StateDictOptions(full_state_dict=True))
+    spec = importlib.import_module(f"torchtitan_b200.models.{module}").model_registry(t.config.model_spec.flavor)
+    ref = spec.model.build()
+    res = ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in full.items()}, strict=False)
+    assert not res.unexpected_keys and all("tokens_per_expert" in k for k in res.missing_keys), res
+    if hasattr(ref, "rope"):
+        ref.rope.init_weights()
+    tokens = torch.randint(0, spec.model.vocab_size, (2 * world, 64), generator=torch.Generator().manual_seed(3))
+    labels = tokens.roll(-1, 1)
+    (cross_entropy_loss(ref(tokens), labels) / labels.numel()).backward()
+    mine = slice(2 * rank, 2 * rank + 2)
+    if rt is not None:
+        rt.begin_microbatch(0, 1)
+    t.forward_backward_step(input_dict={"input": tokens[mine]}, labels=labels[mine],
+                            global_valid_tokens=torch.tensor(float(labels.numel())))
+    named = dict(ref.named_parameters())
+    if rt is not None:  # peer runtime: compare this rank's fp32 gradient shard
+        rt.finish_backward()
+        flat = torch.zeros(rt.total)
+        for i, p in enumerate(rt.params):
+            n = [k for k, q in model.named_parameters() if q is p][0]
+            flat[rt.offsets[i]:rt.offsets[i] + p.numel()] = named[n.replace("_checkpoint_wrapped_module.", "")].grad.flatten()
+        for b, sh in zip(rt.buckets, rt.shard_views(rt.grad_shard)):
+            sl = b.shard_len(world)
+            r = flat[b.offset + rank * sl:b.offset + (rank + 1) * sl]
+            assert float((sh - r).abs().max()) <= 2e-4 * float(r.abs().max()) + 1e-8
+    else:
+        for n, p in model.named_parameters():
+            g = p.grad.full_tensor() if hasattr(p.grad, "full_tensor") else p.grad
+            r = named[n.replace("_checkpoint_wrapped_module.", "")].grad
+            assert float((g - r).abs().max()) <= 2e-4 * float(r.abs().max()) + 1e-8, n
+    t.close()
+
+
+@pytest.mark.parametrize("module,config,extra", [
+    ("llama3", "llama3_debugmodel_cpu", ()),
+    ("llama3", "llama3_debugmodel_cpu", ("--parallelism.data-parallel-comm", "peer")),
+    ("qwen3", "qwen3_debugmodel_moe", ()),
+    ("qwen3", "qwen3_debugmodel_moe", ("--parallelism.expert-parallel-degree", "2")),
+])
+def test_data_parallel_gradients_match_single_device(module, config, extra):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_dp_grads, 2, d, module, config, extra)

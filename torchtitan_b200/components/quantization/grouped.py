@@ -16,7 +16,6 @@ import torch
 import torch.nn as nn
 
 from torchtitan_b200 import ops
-from torchtitan_b200.models.common.layers import _local
 from torchtitan_b200.models.common.moe import GroupedExperts
 from torchtitan_b200.ops.quant import float8_fake_quant, mx_fake_quant
 from torchtitan_b200.protocols.model_converter import ModelConverter
@@ -45,7 +44,7 @@ class QuantGroupedExperts(GroupedExperts):
     recipe = "mxfp8"
 
     def forward(self, x: torch.Tensor, counts: torch.Tensor) -> torch.Tensor:
-        w1, w2, w3 = (_local(w) for w in (self.w1, self.w2, self.w3))
+        w1, w2, w3 = self.weights()
         if x.shape[-1] % 32 or w2.shape[-1] % 32:
             return super().forward(x, counts)
         # w1/w3 [E, H, D] contract over D (last); w2 [E, D, H] contracts over H (last)

@@ -84,7 +84,20 @@ class TokenChoiceTopKRouter(nn.Module):
         return top, idx, counts, scores
 
 
+class _GradScale(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, w, s):
+        ctx.s = s
+        return w.view_as(w)
+
+    @staticmethod
+    def backward(ctx, g):
+        return g * ctx.s, None
+
+
 class GroupedExperts(nn.Module):
+    grad_scale = 1.0  # set by FSDP on gloo, where expert and dense reductions average over different meshes
+
     def __init__(self, dim: int, hidden_dim: int, num_experts: int):
         super().__init__()
         self.num_experts, self.dim, self.hidden_dim = num_experts, dim, hidden_dim
@@ -98,7 +111,13 @@ class GroupedExperts(nn.Module):
 
     def forward(self, x: torch.Tensor, counts: torch.Tensor) -> torch.Tensor:
         """x: [sum(counts), D] rows sorted by (local) expert."""
-        return ops.grouped_swiglu(x, _local(self.w1), _local(self.w2), _local(self.w3), counts)
+        return ops.grouped_swiglu(x, *self.weights(), counts)
+
+    def weights(self):
+        ws = [_local(w) for w in (self.w1, self.w2, self.w3)]
+        if self.grad_scale != 1.0:
+            ws = [_GradScale.apply(w, self.grad_scale) for w in ws]
+        return ws
 
 
 class MoE(nn.Module):

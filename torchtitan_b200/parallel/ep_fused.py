@@ -231,7 +231,6 @@ def make_fused_ep_dispatch(ep_group, num_experts: int, comm: str | None = None):
 
     def dispatch(routed: torch.Tensor, counts: torch.Tensor, experts: nn.Module) -> torch.Tensor:
         from torchtitan_b200 import ops
-        from torchtitan_b200.models.common.layers import _local
         from torchtitan_b200.models.common.moe import GroupedExperts
 
         M = pc.exchange_counts(counts)
@@ -240,8 +239,7 @@ def make_fused_ep_dispatch(ep_group, num_experts: int, comm: str | None = None):
             routed = routed.to(torch.bfloat16)
         xp = _Dispatch.apply(routed.contiguous(), pc, plan)
         if type(experts) is GroupedExperts:
-            yp = ops.grouped_swiglu_padded(xp, _local(experts.w1), _local(experts.w2), _local(experts.w3),
-                                           plan.local_counts)
+            yp = ops.grouped_swiglu_padded(xp, *experts.weights(), plan.local_counts)
         else:  # any other expert module sees its rows unpadded
             y = experts(xp[plan.real_rows], plan.local_counts)
             yp = y.new_zeros(plan.P, y.shape[1]).index_copy(0, plan.real_rows, y)

@@ -60,6 +60,8 @@ def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, redu
         moe = getattr(block, "moe", None) or getattr(getattr(block, "ffn", None), "_moe", None)
         if moe is not None and ep_degree > 1 and edp_mesh is not None:
             ecfg = dict(cfg, mesh=edp_mesh)
+            if _GLOO:  # experts average over efsdp, the compensated loss assumed the dp mesh
+                moe.experts.grad_scale = edp_mesh.size() / dp_mesh.size()
             _disable_grad_division(fully_shard(moe.experts, **ecfg, reshard_after_forward=reshard))
         last = i == len(layers) - 1
         _disable_grad_division(
