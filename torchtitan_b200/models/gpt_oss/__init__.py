@@ -10,6 +10,7 @@ from torchtitan_b200.parallel.pipeline import pipeline_llm
 from torchtitan_b200.protocols import ModelSpec
 
 from .model import GptOssModel, GptOssModelArgs
+from .state_dict_adapter import GptOssStateDictAdapter
 
 A = GptOssModelArgs
 gptoss_args = {
@@ -25,7 +26,7 @@ def model_registry(flavor: str) -> ModelSpec:
         raise ValueError(f"unknown gpt_oss flavor '{flavor}', available: {sorted(gptoss_args)}")
     return ModelSpec(name="gpt_oss", flavor=flavor, model=copy.deepcopy(gptoss_args[flavor]),
                      parallelize_fn=parallelize_decoder, pipelining_fn=pipeline_llm,
-                     build_loss_fn=build_cross_entropy_loss)
+                     build_loss_fn=build_cross_entropy_loss, state_dict_adapter=GptOssStateDictAdapter)
 
 
 __all__ = ["GptOssModel", "GptOssModelArgs", "model_registry", "gptoss_args"]

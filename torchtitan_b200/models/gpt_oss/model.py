@@ -15,6 +15,7 @@ in the tcgen05 flash kernel); its cost is O(S^2) memory per head.
 from __future__ import annotations
 
 import dataclasses
+import math
 from typing import Any
 
 import torch
@@ -88,6 +89,8 @@ class GptOssAttention(nn.Module):
         self.sinks = nn.Parameter(torch.empty(a.n_heads))
         self.window = a.sliding_window if layer_id % 2 == 0 else 0
         self.scale = a.head_dim ** -0.5
+        if a.max_seq_len > a.original_seq_len:  # YaRN attention factor, applied to q and k (squared)
+            self.scale *= (0.1 * math.log(a.rope_factor) + 1.0) ** 2
         self.cp_hook = None
 
     def init_weights(self, init_std: float) -> None:
@@ -183,7 +186,7 @@ class GptOssModel(Decoder):
         self.tok_embeddings = Embedding(a.vocab_size, a.dim)
         scaling = "yarn" if a.max_seq_len > a.original_seq_len else None
         self.rope = RotaryEmbedding(a.head_dim, a.max_seq_len, a.rope_theta, scaling, a.rope_factor,
-                                    a.original_seq_len)
+                                    a.original_seq_len, yarn_truncate=False)
         self.layers = nn.ModuleDict({
             str(i): DecoderBlock(i, a.dim, GptOssAttention(a, i), a.norm_eps, moe=GptOssMoE(a),
                                  init_std=0.02 / (2 * (i + 1)) ** 0.5)
