@@ -118,3 +118,22 @@ def test_gpt_oss_matches_hf(yarn):
         rms_norm_eps=a.norm_eps, tie_word_embeddings=False,
         layer_types=["sliding_attention" if i % 2 == 0 else "full_attention" for i in range(a.n_layers)], **kw)
     _compare(m, transformers.GptOssForCausalLM(cfg), sd, a.vocab_size, seq=200)  # 200 > sliding window
+
+
+def test_llama4_matches_hf():
+    a, m, sd = _ours("llama4", "debugmodel")
+    for mod in m.modules():
+        if getattr(mod, "expert_bias", None) is not None:
+            mod.expert_bias.zero_()  # no HF counterpart
+    hidden = m.layers["0"].feed_forward.w1.weight.shape[0]
+    cfg = transformers.Llama4TextConfig(
+        vocab_size=a.vocab_size, hidden_size=a.dim, intermediate_size=hidden, intermediate_size_mlp=hidden,
+        num_hidden_layers=a.n_layers, num_attention_heads=a.n_heads, num_key_value_heads=a.n_kv_heads,
+        head_dim=a.dim // a.n_heads, num_local_experts=a.num_experts, num_experts_per_tok=a.top_k,
+        interleave_moe_layer_step=a.interleave_moe_layer_step, rms_norm_eps=a.norm_eps,
+        attention_chunk_size=a.fixed_attn_block_size, use_qk_norm=a.use_qk_norm,
+        attn_temperature_tuning=a.attn_temperature_tuning, floor_scale=int(a.floor_scale), attn_scale=a.attn_scale,
+        max_position_embeddings=a.max_seq_len, tie_word_embeddings=False,
+        rope_parameters={"rope_type": "llama3", "rope_theta": a.rope_theta, "factor": a.rope_scaling_factor,
+                         "low_freq_factor": 1.0, "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
+    _compare(m, transformers.Llama4ForCausalLM(cfg), sd, a.vocab_size, seq=512)  # 2 attention chunks

@@ -10,6 +10,7 @@ from torchtitan_b200.parallel.pipeline import pipeline_llm
 from torchtitan_b200.protocols import ModelSpec
 
 from .model import Llama4Model, Llama4ModelArgs
+from .state_dict_adapter import Llama4StateDictAdapter
 
 A = Llama4ModelArgs
 llama4_args = {
@@ -31,7 +32,8 @@ def model_registry(flavor: str) -> ModelSpec:
     return ModelSpec(name="llama4", flavor=flavor, model=copy.deepcopy(llama4_args[flavor]),
                      parallelize_fn=parallelize_decoder, pipelining_fn=pipeline_llm,
                      build_loss_fn=build_cross_entropy_loss,
-                     post_optimizer_build_fn=build_optimizers_with_moe_load_balancing)
+                     post_optimizer_build_fn=build_optimizers_with_moe_load_balancing,
+                     state_dict_adapter=Llama4StateDictAdapter)
 
 
 __all__ = ["Llama4Model", "Llama4ModelArgs", "model_registry", "llama4_args"]
