@@ -79,9 +79,8 @@ class ActivationCheckpointConfig:
 
 @dataclass(kw_only=True, slots=True)
 class CompileConfig:
-    """Accepted for CLI parity.  This framework's hot path is CUDA kernels and
-    CUDA graphs, not a tracing compiler; ``enable`` only switches on CUDA-graph
-    capture of the optimizer step."""
+    """Accepted for CLI parity and ignored: this framework's hot path is
+    hand-written CUDA kernels, not a tracing compiler."""
     enable: bool = False
     components: list[str] = field(default_factory=lambda: ["model", "loss"])
     backend: str = "cudagraph"
