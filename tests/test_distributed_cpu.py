@@ -683,3 +683,49 @@ def _dp_grads(rank, world, out_dir, module, config, extra):
 def test_data_parallel_gradients_match_single_device(module, config, extra):
     with tempfile.TemporaryDirectory() as d:
         _run(_dp_grads, 2, d, module, config, extra)
+
+
+# ---------------------------------------------------------------- exact resume
+def _resume_exact(rank, world, out_dir, extra):
+    import json
+
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    def make(steps, folder, ckpt):
+        return Trainer(ConfigManager().parse_args([
+            "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", str(steps),
+            "--training.seq-len", "64", "--metrics.log-freq", "1", "--metrics.enable-jsonl", "--debug.seed", "0",
+            "--dump-folder", os.path.join(out_dir, folder), *(["--checkpoint.enable", "--checkpoint.interval", "2"]
+                                                              if ckpt else []), *extra]))
+
+    def losses(folder):
+        with open(os.path.join(out_dir, folder, "tb", "rank_0", "metrics.jsonl")) as f:
+            return {r["step"]: r["loss_metrics/global_avg_loss"] for r in map(json.loads, f)}
+
+    t = make(4, "straight", False)
+    t.train()
+    t.close()
+    t = make(2, "resumed", True)
+    t.train()
+    t.close()
+    t = make(4, "resumed", True)
+    t.checkpointer.load()
+    assert t.step == 2
+    t.train()
+    t.close()
+    if rank == 0:
+        a, b = losses("straight"), losses("resumed")
+        for s in (3, 4):
+            assert a[s] == b[s], (s, a[s], b[s], extra)
+
+
+@pytest.mark.parametrize("extra", [
+    (), ("--parallelism.data-parallel-comm", "peer"),
+    ("--parallelism.tensor-parallel-degree", "2", "--parallelism.data-parallel-shard-degree", "1"),
+    ("--parallelism.pipeline-parallel-degree", "2", "--parallelism.data-parallel-shard-degree", "1",
+     "--parallelism.pipeline-parallel-microbatch-size", "2"),
+])
+def test_resume_reproduces_uninterrupted_losses(extra):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_resume_exact, 2, d, extra)

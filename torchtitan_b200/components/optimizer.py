@@ -169,7 +169,9 @@ class PeerShardedAdamW(torch.optim.Optimizer):
     def flat_state_dict(self) -> dict[str, Any]:
         return {"peer_dp.master": self._dtensor(self.rt.master), "peer_dp.exp_avg": self._dtensor(self.exp_avg),
                 "peer_dp.exp_avg_sq": self._dtensor(self.exp_avg_sq),
-                "peer_dp.step": torch.tensor(self.step_count, dtype=torch.int64)}
+                "peer_dp.step": torch.tensor(self.step_count, dtype=torch.int64),
+                # the LR scheduler restores its counter only; the current lr lives in the groups
+                "peer_dp.lr": torch.tensor([float(g["lr"]) for g in self.param_groups], dtype=torch.float64)}
 
     @torch.no_grad()
     def load_flat_state_dict(self, sd: dict[str, Any]) -> None:
@@ -179,6 +181,9 @@ class PeerShardedAdamW(torch.optim.Optimizer):
             if v.data_ptr() != t.data_ptr():
                 t.copy_(v.reshape(-1))
         self.step_count = int(sd["peer_dp.step"])
+        if "peer_dp.lr" in sd:
+            for g, lr in zip(self.param_groups, sd["peer_dp.lr"].tolist()):
+                g["lr"] = lr
         self.rt.gather_weights()
 
 

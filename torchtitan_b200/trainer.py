@@ -24,6 +24,7 @@ from datetime import timedelta
 from typing import Annotated, Any
 
 import torch
+import torch.distributed as dist
 import tyro
 from torch.distributed.checkpoint.stateful import Stateful
 
@@ -353,6 +354,12 @@ class Trainer(Stateful, Configurable):
             return loss
         if dp_rt is not None:
             dp_rt.check()
+        if pd.pp_enabled:
+            # only the last stage computed a loss: every stage logs the last stage's value
+            pp = pd.get_mesh("pp")
+            t = loss.detach().reshape(-1)[:1].clone().to(self.device if dist.get_backend() != "gloo" else "cpu")
+            dist.broadcast(t, src=dist.get_global_rank(pp.get_group(), pp.size() - 1), group=pp.get_group())
+            loss = t.reshape(()).to(loss.device)
         if pd.dp_cp_enabled:
             mesh = pd.get_optional_mesh("loss")
             avg = float(dist_utils.dist_sum(loss, mesh))
