@@ -729,3 +729,28 @@ def _resume_exact(rank, world, out_dir, extra):
 def test_resume_reproduces_uninterrupted_losses(extra):
     with tempfile.TemporaryDirectory() as d:
         _run(_resume_exact, 2, d, extra)
+
+
+# ---------------------------------------------------------------- gradient accumulation
+def _grad_accum(rank, world, out_dir, extra):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    res = []
+    for lbs in ("4", "2"):  # one microbatch of 4 vs two of 2 per rank, same global batch
+        t = Trainer(ConfigManager().parse_args([
+            "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "3",
+            "--training.seq-len", "64", "--training.local-batch-size", lbs, "--training.global-batch-size",
+            str(4 * world), "--metrics.log-freq", "1", "--debug.seed", "0",
+            "--dump-folder", os.path.join(out_dir, lbs), *extra]))
+        assert t.gradient_accumulation_steps == (1 if lbs == "4" else 2)
+        t.train()
+        res.append(t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"])
+        t.close()
+    assert abs(res[0] - res[1]) <= 2e-5 * abs(res[0]), (res, extra)
+
+
+@pytest.mark.parametrize("extra", [(), ("--parallelism.data-parallel-comm", "peer")])
+def test_gradient_accumulation_matches_large_batch(extra):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_grad_accum, 2, d, extra)

@@ -90,8 +90,14 @@ class SyntheticDataLoader(BaseDataLoader):
         self.batches_emitted = 0
 
     def _batch(self, index: int) -> torch.Tensor:
-        g = torch.Generator().manual_seed(self.config.seed * 1_000_003 + self.dp_rank * 7919 + index)
-        t = torch.randint(0, self.vocab_size, (self.local_batch_size, self.seq_len + 1), generator=g)
+        # every sample is seeded by its own index, so the token stream does not depend on how it
+        # is cut into batches (a batch of 4 equals two consecutive batches of 2)
+        rows = []
+        for j in range(self.local_batch_size):
+            sample = index * self.local_batch_size + j
+            g = torch.Generator().manual_seed(hash((self.config.seed, self.dp_rank, sample)) & (2**63 - 1))
+            rows.append(torch.randint(0, self.vocab_size, (self.seq_len + 1,), generator=g))
+        t = torch.stack(rows)
         if self.config.pin_memory and torch.cuda.is_available():
             t = t.pin_memory()
         return t
