@@ -436,3 +436,24 @@ def test_multimodal_dataloader_packs_images(tmp_path):
     assert (labels[0][full_next == -200] == IGNORE_INDEX).all()
     # red image first, blue last (order of appearance), normalised to [-1, 1]
     assert inp["pixel_values"][0, 0].mean() > 0.9 and inp["pixel_values"][2, 2].mean() > 0.9
+
+
+def test_peer_watchdog_reports_device_error_word():
+    import time
+
+    from torchtitan_b200.parallel.watchdog import ErrorWatchdog, describe
+
+    sink = torch.zeros(8, dtype=torch.int32)
+    seen = []
+    wd = ErrorWatchdog(sink, interval_s=0.01, on_error=seen.append)
+    time.sleep(0.05)
+    assert wd.error is None
+    sink[1:5] = torch.tensor([3, 17, 2, 16], dtype=torch.int32)
+    sink[0] = 71  # written last by the kernel
+    for _ in range(200):
+        if seen:
+            break
+        time.sleep(0.01)
+    assert seen and seen[0][:5] == [71, 3, 17, 2, 16]
+    assert "reduce-scatter wait timed out: slot 3, waiting for epoch 17 from rank 2" in describe(wd.error)
+    wd.stop()

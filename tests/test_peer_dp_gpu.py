@@ -17,14 +17,19 @@ def test_dp_barrier_gives_up_and_reports():
     the context stays usable."""
     from torchtitan_b200.ops._ext import ext
 
+    from torchtitan_b200.parallel.watchdog import install
+
     e = ext()
     e.dp_error_code(True)
+    wd = install(e)
     flags = torch.zeros(8, dtype=torch.int32, device="cuda")
     # world 2 with both "peers" pointing at this GPU's flags: slot entry of rank 1 is never written
     e.dp_barrier([flags.data_ptr(), flags.data_ptr()], 0, 1, 1, limit_s=0.2)
     torch.cuda.synchronize()
     assert e.dp_error_code(True) == 72
     assert int(flags[2]) == 1 and int(flags[3]) == 0
+    # the pinned host word saw it too: slot 1, epoch 1, source rank 1, flag value 0
+    assert wd.poll() is not None and wd.error[:5] == [72, 1, 1, 1, 0]
     assert float(torch.ones(4, device="cuda").sum()) == 4.0
 
 

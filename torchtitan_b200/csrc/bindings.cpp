@@ -313,6 +313,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       },
       py::arg("sigs"), py::arg("rank"), py::arg("slot"), py::arg("epoch"), py::arg("limit_s") = 0.0);
   m.def("dp_error_code", &ttb::dp_error_code, py::arg("reset") = true);
+  m.def("dp_set_error_sink", [](Tensor sink) {
+    TORCH_CHECK(!sink.is_cuda() && sink.is_pinned() && sink.scalar_type() == at::kInt && sink.numel() >= 8,
+                "sink: pinned host int32 tensor of >= 8 elements");
+    ttb::dp_set_error_sink(sink.data_ptr());
+  });
   m.def("ep_scatter_rows", [](Tensor src, Tensor dest_rank, Tensor dest_row, std::vector<int64_t> bases) {
     check_cuda_bf16(src, "src");
     TORCH_CHECK(src.dim() == 2 && src.is_contiguous(), "src: contiguous [n, D]");

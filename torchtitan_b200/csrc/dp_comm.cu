@@ -21,6 +21,9 @@ namespace dp_impl {
 
 __device__ int g_err;
 __device__ int g_err_info[4];  // slot, epoch awaited, source rank, value seen (first failure)
+// optional host-mapped (pinned) int[8]: [code, slot, epoch, source, value, ...] written on the first
+// failure so a host thread sees it without any CUDA call while the stream is still busy
+__device__ int* g_host_sink;
 // generous: ranks may drift apart by a data-loader hiccup, a checkpoint write or a slow first step
 constexpr uint64_t kDefaultLimitNs = 20000000000ull;
 constexpr int kMaxWorld = 8;
@@ -72,6 +75,16 @@ __device__ bool signal_and_wait(const PeerTable& t, int slot, uint32_t epoch, in
             g_err_info[1] = static_cast<int>(epoch);
             g_err_info[2] = j;
             g_err_info[3] = static_cast<int>(ld_acquire_sys(mine + j));
+            if (g_host_sink != nullptr) {
+              volatile int* h = g_host_sink;
+              h[1] = slot;
+              h[2] = static_cast<int>(epoch);
+              h[3] = j;
+              h[4] = g_err_info[3];
+              __threadfence_system();
+              h[0] = code;
+              __threadfence_system();
+            }
           }
           ok = 0;
           j = t.world;
@@ -149,6 +162,11 @@ void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint3
   const PeerTable t = make_table(nullptr, peer_sigs, world, rank, limit_s);
   dp_barrier_kernel<<<1, 32, 0, s>>>(t, slot, epoch);
   check_cuda(cudaGetLastError(), "dp barrier launch");
+}
+
+void dp_set_error_sink(void* host_mapped_int8) {
+  int* p = static_cast<int*>(host_mapped_int8);
+  check_cuda(cudaMemcpyToSymbol(dp_impl::g_host_sink, &p, sizeof(int*)), "dp error sink");
 }
 
 void dp_error_info(int* out4) {

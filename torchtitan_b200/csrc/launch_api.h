@@ -77,6 +77,7 @@ void dp_reduce_scatter_bucket(const void* const* peer_grads, uint32_t* const* pe
 void dp_barrier(uint32_t* const* peer_sigs, int world, int rank, int slot, uint32_t epoch, cudaStream_t s,
                 double limit_s = 0.0);
 int dp_error_code(bool reset);
+void dp_set_error_sink(void* host_mapped_int8);  // pinned host int[8] written on the first wait failure
 void dp_error_info(int* out4);
 
 // ep_comm.cu: expert-parallel row movement over NVLink peer memory

@@ -158,6 +158,9 @@ class PeerDataParallel:
             from torchtitan_b200.ops._ext import ext
 
             self._ext = ext()
+            from .watchdog import install
+
+            self.watchdog = install(self._ext)
             name = self.group.group_name
             self.wbuf = symm.empty(n, dtype=torch.bfloat16, device=dev)
             self.gbuf = symm.empty(n, dtype=torch.bfloat16, device=dev)
@@ -328,6 +331,11 @@ class PeerDataParallel:
 
     def check(self) -> None:
         """Raise if a peer wait gave up (a rank stopped answering) since the last check."""
+        wd = getattr(self, "watchdog", None)
+        if wd is not None and wd.poll() is not None:
+            from .watchdog import describe
+
+            raise RuntimeError(f"peer data parallel: {describe(wd.error)}")
         if self.comm == "peer":
             info = self._ext.dp_error_info()
             code = self._ext.dp_error_code(True)

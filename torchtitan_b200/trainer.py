@@ -350,6 +350,9 @@ class Trainer(Stateful, Configurable):
         self.lr_schedulers.step()
         loss = torch.sum(torch.stack([l.reshape(()) for l in losses]))
         self.last_loss = loss
+        wd = getattr(dp_rt, "watchdog", None)
+        if wd is not None and wd.poll() is not None:  # host read, no CUDA call
+            dp_rt.check()
         if not self.metrics_processor.should_log(self.step):
             return loss
         if dp_rt is not None:
