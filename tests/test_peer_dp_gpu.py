@@ -30,6 +30,7 @@ def test_dp_barrier_gives_up_and_reports():
     assert int(flags[2]) == 1 and int(flags[3]) == 0
     # the pinned host word saw it too: slot 1, epoch 1, source rank 1, flag value 0
     assert wd.poll() is not None and wd.error[:5] == [72, 1, 1, 1, 0]
+    wd.reset()
     assert float(torch.ones(4, device="cuda").sum()) == 4.0
 
 

@@ -50,6 +50,15 @@ class ErrorWatchdog:
                 self.on_error(self.error)
         return self.error
 
+    def reset(self) -> None:
+        """Clear a reported failure (after it was handled) and resume watching."""
+        self.sink.zero_()
+        self.error = None
+        if not self._thread.is_alive():
+            self._stop.clear()
+            self._thread = threading.Thread(target=self._run, name="ttb-peer-watchdog", daemon=True)
+            self._thread.start()
+
     def _run(self) -> None:
         while not self._stop.wait(self.interval_s):
             if self.poll() is not None:
