@@ -754,3 +754,65 @@ def _grad_accum(rank, world, out_dir, extra):
 def test_gradient_accumulation_matches_large_batch(extra):
     with tempfile.TemporaryDirectory() as d:
         _run(_grad_accum, 2, d, extra)
+
+
+# ---------------------------------------------------------------- failure handling
+def _slow_rank(rank, world):
+    import datetime
+    import time
+
+    pg = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=2))
+    t = torch.ones(1)
+    dist.all_reduce(t, group=pg)
+    if rank == 1:
+        time.sleep(6)  # misses the next collective's deadline; nothing of it is in flight yet
+    else:
+        with pytest.raises(Exception):
+            dist.all_reduce(t, group=pg)
+
+
+def test_rank_delayed_past_timeout_surfaces_as_error():
+    port = _port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_entry, args=(r, 2, port, _slow_rank, ())) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+    assert all(not p.is_alive() for p in procs)
+    assert procs[0].exitcode == 0
+
+
+def _corrupt_resume(rank, world, out_dir):
+    import glob
+
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    def make(steps):
+        return Trainer(ConfigManager().parse_args([
+            "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", str(steps),
+            "--training.seq-len", "64", "--checkpoint.enable", "--checkpoint.interval", "2", "--debug.seed", "0",
+            "--dump-folder", out_dir]))
+
+    t = make(4)
+    t.train()
+    t.close()
+    dist.barrier()
+    if rank == 0:  # truncate one shard of the newest checkpoint
+        shard = sorted(glob.glob(os.path.join(out_dir, "checkpoint", "step-4", "*.distcp")))[0]
+        with open(shard, "r+b") as f:
+            f.truncate(64)
+    dist.barrier()
+    t = make(6)
+    assert t.checkpointer.load()
+    assert t.step == 2  # fell back to the last good checkpoint
+    t.checkpointer.config.fallback_on_load_error = False
+    with pytest.raises(RuntimeError, match="no loadable checkpoint"):
+        t.checkpointer.load()
+    t.close()
+
+
+def test_corrupt_checkpoint_falls_back_to_previous_step():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_corrupt_resume, 2, d)

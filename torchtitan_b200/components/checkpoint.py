@@ -25,6 +25,7 @@ from typing import Any, Literal
 import torch
 import torch.distributed as dist
 import torch.distributed.checkpoint as dcp
+from torch.distributed.checkpoint.api import CheckpointException
 import torch.nn as nn
 from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict, set_model_state_dict
 from torch.distributed.checkpoint.stateful import Stateful
@@ -89,6 +90,9 @@ class CheckpointManager(Configurable):
         keep_latest_k: int = 10
         load_step: int = -1
         exclude_from_loading: list[str] = field(default_factory=list)
+        fallback_on_load_error: bool = True
+        """Resuming from the latest step: if that checkpoint cannot be read (a truncated or
+        corrupt shard, a missing file), try the next older one instead of failing."""
         enable_first_step_checkpoint: bool = False
         create_seed_checkpoint: bool = False
         load_only: bool = False
@@ -197,15 +201,26 @@ class CheckpointManager(Configurable):
             if c.initial_load_path:
                 return self._initial_load(c.initial_load_path)
             return False
-        step = steps[-1] if step == -1 else step
-        path = self._step_dir(step)
-        if not os.path.exists(os.path.join(path, ".metadata")):
-            raise FileNotFoundError(f"no checkpoint at {path}")
+        candidates = sorted(steps, reverse=True) if step == -1 else [step]
+        if step != -1 or not c.fallback_on_load_error:
+            candidates = candidates[:1]
         keys = [k for k in self.states if k not in c.exclude_from_loading]
-        states = {k: self.states[k] for k in keys}
-        dcp.load(states, checkpoint_id=path)
-        logger.info(f"loaded checkpoint step {step} from {path} (keys {keys})")
-        return True
+        errors = []
+        for s in candidates:
+            path = self._step_dir(s)
+            try:
+                if not os.path.exists(os.path.join(path, ".metadata")):
+                    raise FileNotFoundError(f"no checkpoint at {path}")
+                dcp.load({k: self.states[k] for k in keys}, checkpoint_id=path)
+            except (Exception, CheckpointException) as e:  # noqa: BLE001 - reported, then an older step is tried
+                errors.append(f"step {s}: {type(e).__name__}: {e}")
+                if len(candidates) > 1:
+                    logger.warning(f"checkpoint step {s} could not be loaded ({type(e).__name__}: {e}); "
+                                   "trying an older one")
+                continue
+            logger.info(f"loaded checkpoint step {s} from {path} (keys {keys})")
+            return True
+        raise RuntimeError("no loadable checkpoint: " + "; ".join(errors))
 
     def _initial_load(self, path: str) -> bool:
         if self.config.initial_load_in_hf:
