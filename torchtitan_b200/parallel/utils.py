@@ -51,6 +51,10 @@ def init_distributed(comm: Any, *, enable_cpu_backend: bool = False, base_folder
         ws = int(os.environ.get("NGPU", os.environ["WORLD_SIZE"]))
         dist.init_process_group("fake", store=FakeStore(), rank=0, world_size=ws)
         return ws
+    if mode == "local_tensor":
+        raise NotImplementedError("comm.mode=local_tensor (all ranks simulated numerically in one process) is "
+                                  "not supported: this framework's CUDA kernels have no LocalTensor dispatch; use "
+                                  "fake_backend for dry runs or gloo ranks on CPU")
     if backend is None:
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if enable_cpu_backend and backend == "nccl":
