@@ -457,3 +457,27 @@ def test_peer_watchdog_reports_device_error_word():
     assert seen and seen[0][:5] == [71, 3, 17, 2, 16]
     assert "reduce-scatter wait timed out: slot 3, waiting for epoch 17 from rank 2" in describe(wd.error)
     wd.stop()
+
+
+def test_mx_blocked_scale_layout_round_trip():
+    from torchtitan_b200.ops.mx_gemm import mx_dequantize_ref, mx_gemm, mx_quantize_ref, sf_byte_index
+    from torchtitan_b200.ops.quant import mx_fake_quant
+
+    idx = sf_byte_index(130, 256)
+    assert idx.shape == (256, 8) and idx.unique().numel() == idx.numel() and int(idx.max()) == 2 * 2 * 512 - 1
+    # row 33, group 5 -> record (0, 1), byte 1*16 + 1*4 + 1
+    assert int(idx[33, 5]) == 512 + 16 + 4 + 1
+    torch.manual_seed(0)
+    x = torch.randn(130, 200) * torch.logspace(-2, 2, 200)
+    codes, sf = mx_quantize_ref(x)
+    assert codes.shape == (130, 256) and sf.numel() == 256 * 256 // 32
+    back = mx_dequantize_ref(codes, sf)
+    torch.testing.assert_close(back[:, :200], mx_fake_quant(torch.cat([x, torch.zeros(130, 56)], 1), -1)[:, :200],
+                               rtol=0, atol=0)
+    assert torch.count_nonzero(back[:, 200:]) == 0
+    w = torch.randn(70, 200)
+    qw, sw = mx_quantize_ref(w)
+    y = mx_gemm(codes, sf, qw, sw).float()
+    ref = mx_dequantize_ref(codes, sf) @ mx_dequantize_ref(qw, sw).t()
+    torch.testing.assert_close(y, ref.bfloat16().float())
+    assert ((y - x @ w.t()).norm() / (x @ w.t()).norm()) < 0.08

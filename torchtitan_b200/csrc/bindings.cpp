@@ -338,6 +338,31 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                         src_row.data_ptr<int64_t>(), reinterpret_cast<void* const*>(bases.data()),
                         (int)bases.size(), stream());
   });
+  m.def("mx_quantize", [](Tensor x) {
+    check_cuda_bf16(x, "x");
+    TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "mx_quantize: [R, C] with contiguous rows");
+    const int64_t R = x.size(0), C = x.size(1);
+    const int64_t Cp = (C + 127) / 128 * 128, Rp = (R + 127) / 128 * 128;
+    c10::cuda::CUDAGuard g(x.device());
+    auto codes = torch::empty({R, Cp}, x.options().dtype(at::kByte));
+    auto sf = torch::empty({Rp * Cp / 32}, x.options().dtype(at::kByte));
+    ttb::mx_quantize(x.data_ptr(), R, C, x.stride(0), codes.data_ptr(), sf.data_ptr(), stream());
+    return std::vector<Tensor>{codes, sf};
+  });
+  m.def("gemm_mxfp8", [](Tensor a, Tensor sfa, Tensor b, Tensor sfb) {
+    TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kByte && b.scalar_type() == at::kByte,
+                "gemm_mxfp8: uint8 FP8 codes on CUDA");
+    TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.is_contiguous() && b.is_contiguous(),
+                "gemm_mxfp8: A [M, K], B [N, K] contiguous");
+    const int64_t M = a.size(0), N = b.size(0), K = a.size(1);
+    TORCH_CHECK(sfa.numel() >= (M + 127) / 128 * 128 * K / 32 && sfb.numel() >= (N + 127) / 128 * 128 * K / 32,
+                "gemm_mxfp8: scale records too small");
+    c10::cuda::CUDAGuard g(a.device());
+    auto d = torch::empty({M, N}, a.options().dtype(at::kBFloat16));
+    ttb::gemm_mxfp8(a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), d.data_ptr(), M, N, K, stream());
+    return d;
+  });
+  m.def("mxgemm_error_code", &ttb::mxgemm_error_code, py::arg("reset") = true);
   m.def("dp_error_info", []() {
     int v[4];
     ttb::dp_error_info(v);

@@ -1,0 +1,328 @@
+// MXFP8 block-scaled GEMM for sm_100a (tcgen05.mma kind::mxf8f6f4.block_scale).
+//
+//   D[M,N] (bf16) = sum_k A(m,k) * 2^(sa(m,k/32)-127) * B(n,k) * 2^(sb(n,k/32)-127)
+//
+// A [M,K] and B [N,K] are FP8 E4M3 codes, K contiguous (every GEMM of the MX
+// training recipe -- forward, dgrad, wgrad -- is given operands quantized
+// along its contraction dimension, so both are always K-major).  The E8M0
+// scale factors use the tcgen05 "blocked" layout: for every 128-row block mb
+// and every 128-element K block kb a 512-byte record at (mb * nKB + kb) * 512
+// holds, at byte m0 * 16 + m1 * 4 + j, the scale of row mb*128 + 32*m1 + m0
+// for the j-th 32-element group -- i.e. each 32-bit word holds the four
+// scales one row needs for 128 K, which is the TMEM word the MMA reads.
+//
+// Tile 128x128x128 (one scale record per operand per stage), 6-stage ring:
+//   warp 0      producer: TMA for the A/B tiles (128-byte swizzle) and two
+//               512-byte bulk copies for the scale records, one mbarrier
+//   warp 1      TMEM allocator + MMA issuer: per stage, tcgen05.cp of the two
+//               scale records into TMEM (32x128b, broadcast to the 4 lane
+//               quadrants), then 4 MMAs of K=32 selecting scale byte j
+//   warps 2..5  epilogue: TMEM -> registers -> bf16 -> global
+// Two 128-column accumulators let the epilogue of tile i overlap tile i+1.
+// Every wait is bounded; a timeout sets mxgemm_error_code() and the kernel
+// returns after releasing TMEM.  K must be a multiple of 128 (callers pad).
+#include <stdexcept>
+
+#include "launch_api.h"
+#include "sm100_ptx.cuh"
+#include "tma_host.h"
+
+namespace ttb {
+namespace mx_impl {
+
+constexpr int BM = 128, BN = 128, BK = 128, STAGES = 6;
+constexpr int A_BYTES = BM * BK;  // fp8
+constexpr int B_BYTES = BN * BK;
+constexpr int SF_BYTES = 512;     // one blocked scale record
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGES * 2 * SF_BYTES + 1024;
+constexpr int NUM_THREADS = 192;
+constexpr int GROUP_M = 8;
+constexpr int TMEM_COLS = 512;
+constexpr int ACC_COLS = BN;                 // fp32 accumulator columns per tile
+constexpr int SF_COL0 = 2 * ACC_COLS;        // scale records after the two accumulators
+constexpr int SF_COLS_PER_STAGE = 8;         // 4 columns SFA + 4 columns SFB
+
+__device__ int g_err;
+
+struct Params {
+  int M, N, K;
+  int num_m, num_n, num_k;
+  const uint8_t* sfa;  // blocked scale records of A
+  const uint8_t* sfb;
+  __nv_bfloat16* D;
+  int ldd;
+};
+
+struct Shared {
+  uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int& tn) {
+  const int per_group = GROUP_M * p.num_n;
+  const int g = t / per_group;
+  const int first_m = g * GROUP_M;
+  const int gs = min(p.num_m - first_m, GROUP_M);
+  const int r = t - g * per_group;
+  tm = first_m + r % gs;
+  tn = r / gs;
+}
+
+// 1-D bulk copy global -> shared, completing on an mbarrier (no multicast)
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory descriptor without swizzle for the tcgen05.cp source: 32 rows of
+// 16 bytes = four 8x16-byte core matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t sf_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(512u >> 4) << 16;  // leading (K) offset: a single core-matrix column
+  d |= static_cast<uint64_t>(128u >> 4) << 32;  // stride between 8-row core matrices
+  d |= static_cast<uint64_t>(1) << 46;          // descriptor version for sm100
+  return d;                                     // layout type 0 = no swizzle
+}
+
+// 32 lanes x 128 bits from shared memory into TMEM, replicated to all four lane quadrants
+__device__ __forceinline__ void tmem_cp_32x128b_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Instruction descriptor, kind::mxf8f6f4 with E4M3 A/B, E8M0 scales, K-major A and B
+__host__ __device__ constexpr uint32_t idesc_mx(int M, int N, int a_sf_id, int b_sf_id) {
+  return (static_cast<uint32_t>(b_sf_id & 3) << 4) |   // B scale byte
+         (0u << 7) | (0u << 10) |                       // A, B format E4M3
+         (static_cast<uint32_t>(N >> 3) << 17) |        // N
+         (1u << 23) |                                   // scale format E8M0
+         (static_cast<uint32_t>(M >> 4) << 24) |        // M
+         (static_cast<uint32_t>(a_sf_id & 3) << 29);    // A scale byte
+}
+
+__device__ __forceinline__ void umma_mx(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t tsfa, uint32_t tsfb, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+}
+
+__device__ __forceinline__ void run_producer(const CUtensorMap* tmA, const CUtensorMap* tmB, const Params& p,
+                                             Shared& sh, uint8_t* sA, uint8_t* sB, uint8_t* sSF) {
+  int stage = 0;
+  uint32_t phase = 0;
+  const int tiles = p.num_m * p.num_n;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    int tm, tn;
+    tile_coords(t, p, tm, tn);
+    for (int kb = 0; kb < p.num_k; ++kb) {
+      if (!mbar_wait(&sh.empty[stage], phase ^ 1, &sh.abort_flag, &g_err, 1)) return;
+      mbar_arrive_expect_tx(&sh.full[stage], STAGE_BYTES + 2 * SF_BYTES);
+      tma_load_2d(sA + stage * A_BYTES, tmA, &sh.full[stage], kb * BK, tm * BM);
+      tma_load_2d(sB + stage * B_BYTES, tmB, &sh.full[stage], kb * BK, tn * BN);
+      uint8_t* sf = sSF + stage * 2 * SF_BYTES;
+      bulk_load(sf, p.sfa + (static_cast<size_t>(tm) * p.num_k + kb) * SF_BYTES, SF_BYTES, &sh.full[stage]);
+      bulk_load(sf + SF_BYTES, p.sfb + (static_cast<size_t>(tn) * p.num_k + kb) * SF_BYTES, SF_BYTES,
+                &sh.full[stage]);
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+  }
+  for (int s = 0; s < STAGES; ++s) {  // drain: every filled stage consumed
+    if (!mbar_wait(&sh.empty[stage], phase ^ 1, &sh.abort_flag, &g_err, 2)) return;
+    if (++stage == STAGES) {
+      stage = 0;
+      phase ^= 1;
+    }
+  }
+}
+
+__device__ __forceinline__ void run_mma(const Params& p, Shared& sh, uint8_t* sA, uint8_t* sB, uint8_t* sSF) {
+  int stage = 0;
+  uint32_t phase = 0;
+  int it = 0;
+  const int tiles = p.num_m * p.num_n;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int acc = it & 1;
+    const uint32_t acc_phase = (it >> 1) & 1;
+    ++it;
+    if (!mbar_wait(&sh.tempty[acc], acc_phase ^ 1, &sh.abort_flag, &g_err, 3)) return;
+    tc_fence_after();
+    const uint32_t d_tmem = sh.tmem_base + acc * ACC_COLS;
+    for (int kb = 0; kb < p.num_k; ++kb) {
+      if (!mbar_wait(&sh.full[stage], phase, &sh.abort_flag, &g_err, 4)) return;
+      tc_fence_after();
+      const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
+      const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+      const uint32_t sf_addr = smem_u32(sSF + stage * 2 * SF_BYTES);
+      const uint32_t tsfa = sh.tmem_base + SF_COL0 + stage * SF_COLS_PER_STAGE;
+      const uint32_t tsfb = tsfa + 4;
+      // scale records -> TMEM; tcgen05 operations of this thread execute in issue order,
+      // so the copies land before the MMAs below read them
+      tmem_cp_32x128b_x4(tsfa, sf_desc(sf_addr));
+      tmem_cp_32x128b_x4(tsfb, sf_desc(sf_addr + SF_BYTES));
+#pragma unroll
+      for (int j = 0; j < BK / 32; ++j) {
+        const uint64_t ad = umma_desc_sw128(a_addr + j * 32, 16, 1024);
+        const uint64_t bd = umma_desc_sw128(b_addr + j * 32, 16, 1024);
+        umma_mx(d_tmem, ad, bd, idesc_mx(BM, BN, j, j), tsfa, tsfb, (kb | j) != 0 ? 1u : 0u);
+      }
+      umma_commit(&sh.empty[stage]);
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1;
+      }
+    }
+    umma_commit(&sh.tfull[acc]);
+  }
+}
+
+__device__ __forceinline__ void run_epilogue(const Params& p, Shared& sh, int warp, int lane) {
+  const int q = warp & 3;  // TMEM lane quarter this warp may access
+  int it = 0;
+  const int tiles = p.num_m * p.num_n;
+  const bool vec_ok = (p.ldd % 8) == 0;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    int tm, tn;
+    tile_coords(t, p, tm, tn);
+    const int row = tm * BM + q * 32 + lane;
+    __nv_bfloat16* drow = p.D + static_cast<size_t>(row) * p.ldd;
+    const int acc = it & 1;
+    const uint32_t acc_phase = (it >> 1) & 1;
+    ++it;
+    if (!mbar_wait(&sh.tfull[acc], acc_phase, &sh.abort_flag, &g_err, 5)) return;
+    tc_fence_after();
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(sh.tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * ACC_COLS + c * 32, r);
+      tmem_ld_wait();
+      const int col = tn * BN + c * 32;
+      if (row < p.M && col < p.N) {
+        if (vec_ok && col + 32 <= p.N) {
+          uint4* dst = reinterpret_cast<uint4*>(drow + col);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 o;
+            o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+            o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+            o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+            o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+            dst[v] = o;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col + j < p.N) drow[col + j] = __float2bfloat16(__uint_as_float(r[j]));
+        }
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&sh.tempty[acc]);
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    mx_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ Shared sh;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* sSF = sB + STAGES * B_BYTES;  // 1024-aligned: the stage tiles are 16 KB each
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sh.full[s], 1);
+      mbar_init(&sh.empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&sh.tfull[a], 1);
+      mbar_init(&sh.tempty[a], 4);
+    }
+    sh.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(&sh.tmem_base, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) {
+    if (lane == 0) run_producer(&tmA, &tmB, p, sh, sA, sB, sSF);
+  } else if (warp == 1) {
+    if (lane == 0) run_mma(p, sh, sA, sB, sSF);
+  } else {
+    run_epilogue(p, sh, warp, lane);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(sh.tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace mx_impl
+
+void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
+                int64_t K, cudaStream_t stream) {
+  using namespace mx_impl;
+  if (M == 0 || N == 0) return;
+  if (K % BK) throw std::runtime_error("gemm_mxfp8: K must be a multiple of 128");
+  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) throw std::runtime_error("gemm_mxfp8: dims");
+  if ((reinterpret_cast<uintptr_t>(sfa) & 15) || (reinterpret_cast<uintptr_t>(sfb) & 15))
+    throw std::runtime_error("gemm_mxfp8: scale records must be 16-byte aligned");
+  const CUtensorMap ta = make_tmap_u8_2d(A, M, K, K, BM, BK);
+  const CUtensorMap tb = make_tmap_u8_2d(B, N, K, K, BN, BK);
+  Params p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.num_m = (int)((M + BM - 1) / BM);
+  p.num_n = (int)((N + BN - 1) / BN);
+  p.num_k = (int)(K / BK);
+  p.sfa = static_cast<const uint8_t*>(sfa);
+  p.sfb = static_cast<const uint8_t*>(sfb);
+  p.D = static_cast<__nv_bfloat16*>(D);
+  p.ldd = (int)N;
+  static bool attr_set = false;
+  if (!attr_set) {
+    check_cuda(cudaFuncSetAttribute(mx_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+               "mx gemm smem attr");
+    attr_set = true;
+  }
+  static int sms = 0;
+  if (sms == 0) {
+    int dev;
+    check_cuda(cudaGetDevice(&dev), "mx gemm dev");
+    sms = num_sms(dev);
+  }
+  const int tiles = p.num_m * p.num_n;
+  mx_gemm_kernel<<<tiles < sms ? tiles : sms, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
+  check_cuda(cudaGetLastError(), "mx gemm launch");
+}
+
+int mxgemm_error_code(bool reset) {
+  int v = 0;
+  check_cuda(cudaMemcpyFromSymbol(&v, mx_impl::g_err, sizeof(int)), "mx gemm error read");
+  if (reset) {
+    int z = 0;
+    check_cuda(cudaMemcpyToSymbol(mx_impl::g_err, &z, sizeof(int)), "mx gemm error reset");
+  }
+  return v;
+}
+
+}  // namespace ttb

@@ -80,6 +80,12 @@ int dp_error_code(bool reset);
 void dp_set_error_sink(void* host_mapped_int8);  // pinned host int[8] written on the first wait failure
 void dp_error_info(int* out4);
 
+// gemm_mxfp8.cu / mx_quant.cu: MXFP8 block-scaled GEMM and its quantizer
+void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
+                int64_t K, cudaStream_t stream);
+int mxgemm_error_code(bool reset);
+void mx_quantize(const void* x, int64_t R, int64_t C, int64_t ldx, void* codes, void* sf, cudaStream_t s);
+
 // ep_comm.cu: expert-parallel row movement over NVLink peer memory
 void ep_scatter_rows(const void* src, int64_t n, int d, const int32_t* dest_rank, const int64_t* dest_row,
                      void* const* peer_bases, int world, cudaStream_t s);

@@ -53,6 +53,25 @@ inline CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t rows, uint64_t c
   return m;
 }
 
+// 2-D byte matrix [rows, cols] (fp8 codes), box = [box_rows, box_cols] bytes,
+// 128-byte swizzle (box_cols <= 128).
+inline CUtensorMap make_tmap_u8_2d(const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_bytes,
+                                   uint32_t box_rows, uint32_t box_cols) {
+  ensure_current_context();
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (strides[0] & 15))
+    throw std::runtime_error("TMA operand must be 16-byte aligned with a 16-byte multiple row pitch");
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (u8) failed: " + std::to_string((int)r));
+  return m;
+}
+
 // 3-D bf16 tensor [d2, d1, d0] (d0 contiguous) with explicit strides in elements.
 inline CUtensorMap make_tmap_bf16_3d(const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_elems,
                                      uint64_t s2_elems, uint32_t b0, uint32_t b1, uint32_t b2,

@@ -25,8 +25,11 @@ def mx_quantize(x: torch.Tensor, block: int = MX_BLOCK) -> tuple[torch.Tensor, t
         raise ValueError(f"MX quantization needs the last dim divisible by {block}, got {x.shape[-1]}")
     xb = x.float().reshape(*x.shape[:-1], x.shape[-1] // block, block)
     amax = xb.abs().amax(-1, keepdim=True)
-    # RCEIL: smallest power of two s with amax / s <= 448; zero blocks get the smallest scale
-    exp = torch.ceil(torch.log2(amax.clamp_min(2.0 ** -126) / E4M3_MAX)).clamp(-127, 127)
+    # RCEIL: smallest power of two s with amax / s <= 448, i.e. ceil(log2(amax / 448)), taken
+    # exactly from the binary exponent (frexp: y = m * 2^p, m in [0.5, 1)); zero blocks get 2^-127
+    m, p = torch.frexp(amax / E4M3_MAX)
+    exp = torch.where(m == 0.5, p - 1, p).float().clamp(-127, 127)
+    exp = torch.where(amax == 0, torch.full_like(exp, -127.0), exp)
     scaled = (xb * torch.exp2(-exp)).clamp(-E4M3_MAX, E4M3_MAX)
     codes = scaled.to(torch.float8_e4m3fn).reshape(x.shape)
     return codes, (exp.squeeze(-1) + 127).to(torch.uint8)
