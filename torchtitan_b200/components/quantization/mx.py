@@ -2,6 +2,7 @@
 MXFP8 1x32 E8M0 blocks with RCEIL scale rounding on linear layers matched by FQN)."""
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -18,16 +19,32 @@ from torchtitan_b200.utils.logging import logger
 from .utils import swap_linears
 
 
+def _use_block_scaled_kernel(t: torch.Tensor) -> bool:
+    # the tcgen05 block-scaled GEMM is opt-in until it has been validated on a B200
+    return t.is_cuda and os.environ.get("TTB_MXFP8_KERNEL") == "1"
+
+
 class _MXLinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w):
         ctx.save_for_backward(x, w)
+        if _use_block_scaled_kernel(x):
+            from torchtitan_b200.ops.mx_gemm import mx_linear
+
+            return mx_linear(x, w).to(x.dtype)
         return ops.linear(mx_fake_quant(x, -1), mx_fake_quant(w, -1))
 
     @staticmethod
     def backward(ctx, dy):
         x, w = ctx.saved_tensors
         x2, dy2 = x.reshape(-1, x.shape[-1]), dy.reshape(-1, dy.shape[-1])
+        if _use_block_scaled_kernel(dy):
+            from torchtitan_b200.ops.mx_gemm import mx_linear
+
+            # every operand quantized along its GEMM's contraction dimension
+            dx = mx_linear(dy2.contiguous(), w.t().contiguous()).view(x.shape).to(x.dtype)
+            dw = mx_linear(dy2.t().contiguous(), x2.t().contiguous()).to(w.dtype)
+            return dx, dw
         # dgrad: contraction over `out` -> dy blocked along its last dim, W blocked along dim 0
         dx = ops.matmul(mx_fake_quant(dy2, -1), mx_fake_quant(w, 0)).view(x.shape)
         # wgrad: contraction over tokens -> both blocked along dim 0
