@@ -44,3 +44,26 @@ def test_decayed_gram_gradcheck():
     G = (-torch.rand(2, 5, 3, generator=g, dtype=torch.float64)).cumsum(1).requires_grad_()
     for strict in (True, False):
         assert torch.autograd.gradcheck(lambda a, b, G: kda.decayed_gram(a, b, G, strict), (a, b, G))
+
+
+def test_decayed_gram_backward_closed_form():
+    """The kernel's backward uses dG = a * da - b * db; check it against autograd of the loop."""
+    from torchtitan_b200.ops.kda import decayed_gram
+
+    torch.manual_seed(0)
+    N, C, K = 3, 16, 8
+    a, b = torch.randn(N, C, K, dtype=torch.float64), torch.randn(N, C, K, dtype=torch.float64)
+    G = (-torch.rand(N, C, K, dtype=torch.float64)).cumsum(1)
+    for strict in (True, False):
+        dout = torch.randn(N, C, C, dtype=torch.float64)
+        aa, bb, gg = (t.clone().requires_grad_() for t in (a, b, G))
+        (decayed_gram(aa, bb, gg, strict) * dout).sum().backward()
+        i = torch.arange(C)
+        mask = (i[:, None] > i[None, :]) if strict else (i[:, None] >= i[None, :])
+        w = dout * mask
+        e = torch.exp((G[:, :, None, :] - G[:, None, :, :]).clamp(max=0))  # [N, i, j, K]
+        da = torch.einsum("nij,nijd,njd->nid", w, e, b)
+        db = torch.einsum("nij,nijd,nid->njd", w, e, a)
+        torch.testing.assert_close(aa.grad, da)
+        torch.testing.assert_close(bb.grad, db)
+        torch.testing.assert_close(gg.grad, a * da - b * db)

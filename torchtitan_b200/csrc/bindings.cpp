@@ -362,6 +362,25 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     ttb::gemm_mxfp8(a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), d.data_ptr(), M, N, K, stream());
     return d;
   });
+  m.def("kda_gram_fwd", [](Tensor a, Tensor b, Tensor G, bool strict) {
+    for (const Tensor* t : {&a, &b, &G})
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 3 &&
+                      t->sizes() == a.sizes(), "kda_gram: a, b, G contiguous fp32 [N, C, K]");
+    c10::cuda::CUDAGuard g(a.device());
+    auto out = torch::empty({a.size(0), a.size(1), a.size(1)}, a.options());
+    ttb::kda_gram_fwd(a.data_ptr<float>(), b.data_ptr<float>(), G.data_ptr<float>(), out.data_ptr<float>(),
+                      a.size(0), (int)a.size(1), (int)a.size(2), strict, stream());
+    return out;
+  });
+  m.def("kda_gram_bwd", [](Tensor dout, Tensor a, Tensor b, Tensor G, bool strict) {
+    TORCH_CHECK(dout.is_cuda() && dout.scalar_type() == at::kFloat && dout.is_contiguous(), "kda_gram: dout");
+    c10::cuda::CUDAGuard g(a.device());
+    auto da = torch::empty_like(a), db = torch::empty_like(b), dG = torch::empty_like(G);
+    ttb::kda_gram_bwd(dout.data_ptr<float>(), a.data_ptr<float>(), b.data_ptr<float>(), G.data_ptr<float>(),
+                      da.data_ptr<float>(), db.data_ptr<float>(), dG.data_ptr<float>(), a.size(0), (int)a.size(1),
+                      (int)a.size(2), strict, stream());
+    return std::vector<Tensor>{da, db, dG};
+  });
   m.def("mxgemm_error_code", &ttb::mxgemm_error_code, py::arg("reset") = true);
   m.def("dp_error_info", []() {
     int v[4];

@@ -86,6 +86,12 @@ void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, 
 int mxgemm_error_code(bool reset);
 void mx_quantize(const void* x, int64_t R, int64_t C, int64_t ldx, void* codes, void* sf, cudaStream_t s);
 
+// kda_gram.cu: decayed Gram matrices of chunked KDA (forward and backward)
+void kda_gram_fwd(const float* a, const float* b, const float* G, float* out, int64_t N, int C, int K, bool strict,
+                  cudaStream_t s);
+void kda_gram_bwd(const float* dout, const float* a, const float* b, const float* G, float* da, float* db,
+                  float* dG, int64_t N, int C, int K, bool strict, cudaStream_t s);
+
 // ep_comm.cu: expert-parallel row movement over NVLink peer memory
 void ep_scatter_rows(const void* src, int64_t n, int d, const int32_t* dest_rank, const int64_t* dest_row,
                      void* const* peer_bases, int world, cudaStream_t s);

@@ -28,12 +28,27 @@ import torch
 import torch.nn.functional as F
 
 
+def _use_gram_kernel(t: torch.Tensor) -> bool:
+    # csrc/kda_gram.cu is opt-in until validated on a B200
+    import os
+
+    return t.is_cuda and os.environ.get("TTB_KDA_KERNEL") == "1"
+
+
 class _DecayedGram(torch.autograd.Function):
     """out[n, i, j] = sum_d a[n,i,d] b[n,j,d] exp(G[n,i,d] - G[n,j,d]) for j < i
-    (``strict``) or j <= i, else 0.  a, b, G: [N, C, K] fp32."""
+    (``strict``) or j <= i, else 0.  a, b, G: [N, C, K] fp32.  On CUDA (opt-in)
+    one kernel per direction (``csrc/kda_gram.cu``); else a loop over columns."""
 
     @staticmethod
     def forward(ctx, a, b, G, strict):
+        if _use_gram_kernel(a):
+            from ._ext import ext
+
+            a, b, G = (t.float().contiguous() for t in (a, b, G))
+            ctx.save_for_backward(a, b, G)
+            ctx.strict = strict
+            return ext().kda_gram_fwd(a, b, G, strict)
         N, C, K = a.shape
         out = a.new_zeros(N, C, C)
         idx = torch.arange(C, device=a.device)
@@ -49,6 +64,11 @@ class _DecayedGram(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         a, b, G = ctx.saved_tensors
+        if _use_gram_kernel(a):
+            from ._ext import ext
+
+            da, db, dG = ext().kda_gram_bwd(dout.float().contiguous(), a, b, G, ctx.strict)
+            return da, db, dG, None
         N, C, K = a.shape
         da, db, dG = torch.zeros_like(a), torch.zeros_like(b), torch.zeros_like(G)
         idx = torch.arange(C, device=a.device)
