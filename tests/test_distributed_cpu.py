@@ -816,3 +816,23 @@ def _corrupt_resume(rank, world, out_dir):
 def test_corrupt_checkpoint_falls_back_to_previous_step():
     with tempfile.TemporaryDirectory() as d:
         _run(_corrupt_resume, 2, d)
+
+
+def _hf_backend(rank, world, out_dir):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", "hf_transformers", "--config", "hf_transformers_qwen3_debugmodel", "--training.steps", "3",
+        "--training.seq-len", "64", "--training.local-batch-size", "2", "--training.dtype", "float32",
+        "--training.mixed-precision-param", "float32", "--activation-checkpoint.mode", "full",
+        "--metrics.log-freq", "1", "--dump-folder", out_dir]))
+    t.train()
+    loss = t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"]
+    assert 6.0 < loss < 9.0
+    t.close()
+
+
+def test_hf_transformers_backend_trains_with_fsdp():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_hf_backend, 2, d)

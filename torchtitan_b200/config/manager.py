@@ -14,7 +14,7 @@ from typing import Any
 
 import tyro
 
-_SHORT_MODULES = ("llama3", "kimi_linear", "deepseek_v3", "qwen3", "llama4", "gpt_oss", "attention_residual")
+_SHORT_MODULES = ("llama3", "kimi_linear", "deepseek_v3", "qwen3", "llama4", "gpt_oss", "attention_residual", "hf_transformers")
 
 
 def split_module_and_config(args: list[str]) -> tuple[str | None, str | None, list[str]]:
