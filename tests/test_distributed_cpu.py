@@ -487,22 +487,25 @@ def test_kimi_tensor_parallel_matches_single_device():
         _run(_kimi_tp, 2, d)
 
 
-def _llama_tp_grads(rank, world, out_dir, sp):
+def _llama_tp_grads(rank, world, out_dir, sp, module="llama3", config="llama3_debugmodel_cpu"):
     from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
 
     from torchtitan_b200.components.loss import cross_entropy_loss
     from torchtitan_b200.config.manager import ConfigManager
-    from torchtitan_b200.models.llama3 import model_registry
     from torchtitan_b200.trainer import Trainer
 
     t = Trainer(ConfigManager().parse_args([
-        "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "1",
+        "--module", module, "--config", config, "--training.steps", "1",
         "--training.seq-len", "64", "--parallelism.tensor-parallel-degree", "2",
         "--parallelism.data-parallel-shard-degree", "1", "--debug.seed", "0", "--dump-folder", out_dir,
-        *([] if sp else ["--parallelism.no-enable-sequence-parallel"])]))
+        "--training.dtype", "float32", "--training.mixed-precision-param", "float32",
+        "--activation-checkpoint.mode", "none", *([] if sp else ["--parallelism.no-enable-sequence-parallel"])]))
     model = t.model_parts[0]
     full = get_model_state_dict(model, options=StateDictOptions(full_state_dict=True))
-    ref = model_registry("debugmodel").model.build()
+    import importlib
+
+    ref = importlib.import_module(f"torchtitan_b200.models.{module}").model_registry(
+        t.config.model_spec.flavor).model.build()
     ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in full.items()}, strict=False)
     ref.rope.init_weights()
     tokens = torch.randint(0, 2048, (2, 64), generator=torch.Generator().manual_seed(3))
@@ -519,9 +522,10 @@ def _llama_tp_grads(rank, world, out_dir, sp):
 
 
 @pytest.mark.parametrize("sp", [True, False])
-def test_llama_tensor_parallel_gradients(sp):
+@pytest.mark.parametrize("module,config", [("llama3", "llama3_debugmodel_cpu"), ("qwen3", "qwen3_debugmodel")])
+def test_tensor_parallel_gradients(sp, module, config):
     with tempfile.TemporaryDirectory() as d:
-        _run(_llama_tp_grads, 2, d, sp)
+        _run(_llama_tp_grads, 2, d, sp, module, config)
 
 
 # ---------------------------------------------------------------- context parallel, gradient-exact

@@ -41,8 +41,6 @@ def _apply_tp(model: nn.Module, tp_mesh, parallelism: Any) -> None:
         if not isinstance(getattr(blk, "attention", None), GQAttention) or getattr(blk, "moe", None) is not None:
             raise NotImplementedError(f"{type(model).__name__}: tensor parallelism covers GQA attention with dense "
                                       "MLP blocks; use EP/CP/FSDP for MoE or MLA blocks")
-        if getattr(blk.attention, "q_norm", None) is not None:
-            raise NotImplementedError("tensor parallelism with per-head q/k norms is not wired")
     apply_tp_llama(model, tp_mesh, loss_parallel=not parallelism.disable_loss_parallel,
                    sequence_parallel=parallelism.enable_sequence_parallel)
     maybe_enable_async_tp(parallelism, tp_mesh)

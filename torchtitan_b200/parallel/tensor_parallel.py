@@ -222,6 +222,9 @@ def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_p
         for lin in (att.wq, att.wk, att.wv):
             parallelize_linear(lin, "col", tp_mesh, sequence_parallel)
         parallelize_linear(att.wo, "row", tp_mesh, sequence_parallel)
+        for n in (getattr(att, "q_norm", None), getattr(att, "k_norm", None)):
+            if n is not None:  # per-head norms see only this rank's heads: reduce their weight grads
+                wrap_replicated_norm(n, tp_mesh)
         ff = blk.feed_forward
         parallelize_linear(ff.w1, "col", tp_mesh, sequence_parallel)
         parallelize_linear(ff.w3, "col", tp_mesh, sequence_parallel)
