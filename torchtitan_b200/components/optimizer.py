@@ -523,6 +523,9 @@ def build_optimizers_with_moe_load_balancing(optimizers: OptimizersContainer, mo
         mesh = parallel_dims.get_optional_mesh("loss") if parallel_dims is not None else None
         if mesh is not None:
             dist.all_reduce(counts, group=mesh.get_group())
+        tp_group = getattr(moes[0], "tp_count_group", None)
+        if tp_group is not None:  # sequence-parallel TP: each TP rank routed different tokens
+            dist.all_reduce(counts, group=tp_group)
         for m, c in zip(moes, counts):
             delta = m.load_balance_coeff * torch.sign(c.mean() - c)
             m.expert_bias.add_(delta - delta.mean())

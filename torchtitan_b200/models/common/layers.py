@@ -47,8 +47,14 @@ class Linear(nn.Module):
         if self.bias is not None:
             nn.init.zeros_(self.bias)
 
+    grad_reduce_group = None  # replicated over TP on sequence-sharded inputs: reduce weight grads
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         w = _local(self.weight)
+        if self.grad_reduce_group is not None:
+            from torchtitan_b200.parallel.tensor_parallel import grad_all_reduce
+
+            w = grad_all_reduce(w, self.grad_reduce_group)
         if self.tp_mode is None:
             y = ops.linear(x, w)
         else:

@@ -97,6 +97,7 @@ class _GradScale(torch.autograd.Function):
 
 class GroupedExperts(nn.Module):
     grad_scale = 1.0  # set by FSDP on gloo, where expert and dense reductions average over different meshes
+    grad_reduce_group = None  # tensor parallelism with sequence-sharded tokens: reduce weight grads over TP
 
     def __init__(self, dim: int, hidden_dim: int, num_experts: int):
         super().__init__()
@@ -115,6 +116,10 @@ class GroupedExperts(nn.Module):
 
     def weights(self):
         ws = [_local(w) for w in (self.w1, self.w2, self.w3)]
+        if self.grad_reduce_group is not None:
+            from torchtitan_b200.parallel.tensor_parallel import grad_all_reduce
+
+            ws = [grad_all_reduce(w, self.grad_reduce_group) for w in ws]
         if self.grad_scale != 1.0:
             ws = [_GradScale.apply(w, self.grad_scale) for w in ws]
         return ws

@@ -87,10 +87,12 @@ class Llama4Attention(GQAttention):
         return ops.attention(q, k, v, causal=True)
 
     def forward(self, x, cos, sin, attention_masks=None):
-        B, S, _ = x.shape
-        q = self.wq(x).view(B, S, -1, self.head_dim)
-        k = self.wk(x).view(B, S, -1, self.head_dim)
-        v = self.wv(x).view(B, S, -1, self.head_dim)
+        B = x.shape[0]
+        q, k, v = self.wq(x), self.wk(x), self.wv(x)
+        S = q.shape[1]  # the full sequence under sequence parallelism (the projections gather it)
+        q = q.view(B, S, -1, self.head_dim)
+        k = k.view(B, S, -1, self.head_dim)
+        v = v.view(B, S, -1, self.head_dim)
         if self.use_rope:
             q, k = ops.rope(q, cos, sin), ops.rope(k, cos, sin)
         if self.qk_l2:

@@ -37,12 +37,29 @@ def _apply_tp(model: nn.Module, tp_mesh, parallelism: Any) -> None:
     from torchtitan_b200.models.common import GQAttention
     from torchtitan_b200.parallel.tensor_parallel import apply_tp_llama, maybe_enable_async_tp
 
+    from torchtitan_b200.models.common.moe import MoE
+
+    sp = parallelism.enable_sequence_parallel
     for blk in model.layers.values():
-        if not isinstance(getattr(blk, "attention", None), GQAttention) or getattr(blk, "moe", None) is not None:
-            raise NotImplementedError(f"{type(model).__name__}: tensor parallelism covers GQA attention with dense "
-                                      "MLP blocks; use EP/CP/FSDP for MoE or MLA blocks")
-    apply_tp_llama(model, tp_mesh, loss_parallel=not parallelism.disable_loss_parallel,
-                   sequence_parallel=parallelism.enable_sequence_parallel)
+        if not isinstance(getattr(blk, "attention", None), GQAttention):
+            raise NotImplementedError(f"{type(model).__name__}: tensor parallelism covers GQA attention; use "
+                                      "EP/CP/FSDP for MLA blocks")
+        moe = getattr(blk, "moe", None)
+        if moe is not None and not isinstance(moe, MoE):
+            raise NotImplementedError(f"tensor parallelism for {type(moe).__name__} is not wired")
+    apply_tp_llama(model, tp_mesh, loss_parallel=not parallelism.disable_loss_parallel, sequence_parallel=sp)
+    group = tp_mesh.get_group()
+    for blk in model.layers.values():
+        moe = getattr(blk, "moe", None)
+        if moe is not None and sp:
+            # routed tokens are this rank's sequence shard; experts, router and shared experts are
+            # replicated over TP, so their weight gradients are summed over TP
+            moe.experts.grad_reduce_group = group
+            moe.router.gate.grad_reduce_group = group
+            if moe.shared_experts is not None:
+                for lin in (moe.shared_experts.w1, moe.shared_experts.w2, moe.shared_experts.w3):
+                    lin.grad_reduce_group = group
+            moe.tp_count_group = group  # token counts for the load-balancing bias cover all TP shards
     maybe_enable_async_tp(parallelism, tp_mesh)
 
 

@@ -225,10 +225,11 @@ def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_p
         for n in (getattr(att, "q_norm", None), getattr(att, "k_norm", None)):
             if n is not None:  # per-head norms see only this rank's heads: reduce their weight grads
                 wrap_replicated_norm(n, tp_mesh)
-        ff = blk.feed_forward
-        parallelize_linear(ff.w1, "col", tp_mesh, sequence_parallel)
-        parallelize_linear(ff.w3, "col", tp_mesh, sequence_parallel)
-        parallelize_linear(ff.w2, "row", tp_mesh, sequence_parallel)
+        ff = getattr(blk, "feed_forward", None)  # MoE blocks: experts are handled by the caller
+        if ff is not None:
+            parallelize_linear(ff.w1, "col", tp_mesh, sequence_parallel)
+            parallelize_linear(ff.w3, "col", tp_mesh, sequence_parallel)
+            parallelize_linear(ff.w2, "row", tp_mesh, sequence_parallel)
         if sequence_parallel:
             wrap_replicated_norm(blk.attention_norm, tp_mesh)
             wrap_replicated_norm(blk.ffn_norm, tp_mesh)
