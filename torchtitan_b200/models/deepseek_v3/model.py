@@ -114,8 +114,9 @@ class MLAttention(nn.Module):
         return ops.attention(q, k, v, causal=True, scale=self.softmax_scale)
 
     def forward(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, attention_masks=None) -> torch.Tensor:
-        B, S, _ = x.shape
+        B = x.shape[0]
         q = self.wq(x) if self.q_lora_rank == 0 else self.wq_b(self.q_norm(self.wq_a(x)))
+        S = q.shape[1]  # the full sequence under sequence parallelism (the projections gather it)
         q = q.view(B, S, -1, self.qk_dim)
         H = q.shape[2]
         q_nope, q_pe = q.split([self.nope, self.rope_dim], dim=-1)

@@ -41,9 +41,9 @@ def _apply_tp(model: nn.Module, tp_mesh, parallelism: Any) -> None:
 
     sp = parallelism.enable_sequence_parallel
     for blk in model.layers.values():
-        if not isinstance(getattr(blk, "attention", None), GQAttention):
-            raise NotImplementedError(f"{type(model).__name__}: tensor parallelism covers GQA attention; use "
-                                      "EP/CP/FSDP for MLA blocks")
+        att = getattr(blk, "attention", None)
+        if not isinstance(att, GQAttention) and not hasattr(att, "wkv_a"):
+            raise NotImplementedError(f"{type(model).__name__}: tensor parallelism covers GQA and MLA attention")
         moe = getattr(blk, "moe", None)
         if moe is not None and not isinstance(moe, MoE):
             raise NotImplementedError(f"tensor parallelism for {type(moe).__name__} is not wired")

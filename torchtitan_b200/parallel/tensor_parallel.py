@@ -115,6 +115,10 @@ def tp_linear(x: torch.Tensor, w: torch.Tensor, mode: str, group, sequence_paral
             return async_tp.ag_matmul(x, w, group)
         if mode == "row":
             return async_tp.matmul_rs(x, w, group)
+    if mode == "col_local":
+        # input already complete on every rank and its gradient left partial on purpose: the
+        # producer of the input reduces it (see apply_tp_mla)
+        return mm(x, w)
     if mode == "col":
         # replicated input: each rank's dgrad is a partial sum over its output shard
         x = all_gather_seq(x, group) if sequence_parallel else grad_all_reduce(x, group)
@@ -184,7 +188,7 @@ def _replicate_param(mod: nn.Module, name: str, mesh) -> None:
 def parallelize_linear(lin: nn.Module, mode: str, tp_mesh, sequence_parallel: bool) -> None:
     from torch.distributed.tensor import Shard
 
-    _shard_param(lin, "weight", tp_mesh, Shard(0 if mode == "col" else 1))
+    _shard_param(lin, "weight", tp_mesh, Shard(1 if mode == "row" else 0))
     lin.tp_mode = mode
     lin.tp_group = tp_mesh.get_group()
     lin.sequence_parallel = sequence_parallel
@@ -217,6 +221,16 @@ def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_p
     ws = tp_mesh.size()
     for blk in model.layers.values():
         att = blk.attention
+        if hasattr(att, "wkv_a"):  # multi-head latent attention
+            apply_tp_mla(att, tp_mesh, sequence_parallel)
+            for n in (blk.attention_norm, blk.ffn_norm) if sequence_parallel else ():
+                wrap_replicated_norm(n, tp_mesh)
+            ff = getattr(blk, "feed_forward", None)
+            if ff is not None:
+                parallelize_linear(ff.w1, "col", tp_mesh, sequence_parallel)
+                parallelize_linear(ff.w3, "col", tp_mesh, sequence_parallel)
+                parallelize_linear(ff.w2, "row", tp_mesh, sequence_parallel)
+            continue
         if att.n_kv_heads % ws or att.n_heads % ws:
             raise ValueError(f"TP degree {ws} must divide n_heads {att.n_heads} and n_kv_heads {att.n_kv_heads}")
         for lin in (att.wq, att.wk, att.wv):
@@ -263,6 +277,33 @@ def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_p
     model._tp_group = group
     model._tp_loss_parallel = loss_parallel
     model._sp_degree = ws if sequence_parallel else 1
+
+
+def apply_tp_mla(att: nn.Module, tp_mesh, sequence_parallel: bool) -> None:
+    """Multi-head latent attention (DeepSeek-V3): head projections ``wq``/``wq_b``/``wkv_b``
+    column-parallel and ``wo`` row-parallel; the latent projections ``wq_a``/``wkv_a`` keep
+    their full weight but take the column-parallel input path (sequence all-gather, or a
+    gradient all-reduce of a replicated input) so every rank sees the whole latent; their
+    weight gradients and those of the latent norms -- partial sums over this rank's heads --
+    are reduced over TP."""
+    ws = tp_mesh.size()
+    if att.n_heads % ws:
+        raise ValueError(f"TP degree {ws} must divide n_heads {att.n_heads}")
+    group = tp_mesh.get_group()
+    if att.q_lora_rank == 0:
+        parallelize_linear(att.wq, "col", tp_mesh, sequence_parallel)
+    else:
+        parallelize_linear(att.wq_b, "col_local", tp_mesh, sequence_parallel)
+    # wkv_b reads the gathered latent; its input gradient stays partial (as does that of the
+    # shared rope key, used by this rank's heads only) and wkv_a reduces both together
+    parallelize_linear(att.wkv_b, "col_local", tp_mesh, sequence_parallel)
+    parallelize_linear(att.wo, "row", tp_mesh, sequence_parallel)
+    latent = [att.wkv_a] + ([att.wq_a] if att.q_lora_rank else [])
+    for lin in latent:
+        lin.tp_mode, lin.tp_group, lin.sequence_parallel = "col", group, sequence_parallel
+        lin.grad_reduce_group = group
+    for n in [att.kv_norm] + ([att.q_norm] if att.q_lora_rank else []):
+        wrap_replicated_norm(n, tp_mesh)
 
 
 def apply_tp_kimi(model: nn.Module, tp_mesh, *, loss_parallel: bool) -> None:
