@@ -314,3 +314,25 @@ def test_grouped_swiglu_padded_matches_unpadded():
     yp = grouped_swiglu_padded(xp, w1, w2, w3, counts)
     torch.testing.assert_close(yp[:70], y[:70], rtol=0, atol=0)
     torch.testing.assert_close(yp[int(kst[2]):int(kst[2]) + 200], y[70:], rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_attention_lse_output_and_gradient(D):
+    """The flash kernel's log-sum-exp output and the dlse term of its backward (used for
+    attention sinks) against fp32 PyTorch."""
+    from torchtitan_b200.ops.attention import _attention_lse_ref, attention_with_lse
+
+    torch.manual_seed(0)
+    B, S, H, Hk = 1, 256, 8, 2
+    q, k, v = (torch.randn(B, S, h, D, device="cuda", dtype=torch.bfloat16) for h in (H, Hk, Hk))
+    go = torch.randn(B, S, H, D, device="cuda")
+    gl = torch.randn(B, S, H, device="cuda")
+    outs = []
+    for fn in (attention_with_lse, _attention_lse_ref):
+        qq, kk, vv = (t.detach().float().requires_grad_() if fn is _attention_lse_ref else
+                      t.detach().clone().requires_grad_() for t in (q, k, v))
+        o, lse = fn(qq, kk, vv, True, D ** -0.5)
+        ((o.float() * go).sum() + (lse.float() * gl).sum()).backward()
+        outs.append((o.float(), lse.float(), qq.grad.float(), kk.grad.float(), vv.grad.float()))
+    for a, b in zip(*outs):
+        torch.testing.assert_close(a, b, rtol=3e-2, atol=3e-2)

@@ -257,16 +257,20 @@ std::vector<Tensor> attn_fwd(Tensor q, Tensor k, Tensor v, bool causal, double s
 }
 
 std::vector<Tensor> attn_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, bool causal,
-                             double scale) {
+                             double scale, c10::optional<Tensor> dlse) {
   check_cuda_bf16(dout, "dout");
   const int B = q.size(0), Sq = q.size(1), H = q.size(2), Dqk = q.size(3);
   const int Sk = k.size(1), Hk = k.size(2), Dv = v.size(3);
   c10::cuda::CUDAGuard g(q.device());
   Tensor dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
   Tensor delta = torch::zeros({B, H, (Sq + 63) / 64 * 64}, q.options().dtype(at::kFloat));
+  if (dlse.has_value())
+    TORCH_CHECK(dlse->is_cuda() && dlse->scalar_type() == at::kFloat && dlse->is_contiguous() &&
+                    dlse->sizes() == delta.sizes(), "attn_bwd: dlse must be fp32 [B, H, padded Sq] like lse");
   ttb::attn_bwd(dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
                 dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), nullptr, delta.data_ptr<float>(), B, Sq, Sk, H, Hk, Dqk,
-                Dv, causal, static_cast<float>(scale), stream());
+                Dv, causal, static_cast<float>(scale), stream(),
+                dlse.has_value() ? dlse->data_ptr<float>() : nullptr);
   return {dq, dk, dv};
 }
 
@@ -390,5 +394,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("multi_sumsq", &multi_sumsq, "sum of squares over a list of fp32/bf16 tensors");
   m.def("multi_clip_scale", &multi_clip_scale, "scale tensors by min(1, max_norm/(sqrt(total)+1e-6))");
   m.def("attn_fwd", &attn_fwd);
-  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_bwd", &attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
+        py::arg("lse"), py::arg("causal"), py::arg("scale"), py::arg("dlse") = py::none());
 }

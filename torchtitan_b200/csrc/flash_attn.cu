@@ -824,8 +824,11 @@ void launch_fwd(const void* q, const void* k, const void* v, Params& p, int Dqk,
 //       S = Q K^T, dP = dO V^T, dS = P (dP - delta), dQ += dS K
 // ============================================================================
 
+// delta = rowsum(dO * O) - dlse: a gradient flowing into the log-sum-exp output adds
+// P * dlse to dS, i.e. shifts delta by -dlse (dlse laid out like lse; may be null)
 __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ o,
-                                      float* __restrict__ delta, int B, int S, int H, int Dv) {
+                                      float* __restrict__ delta, const float* __restrict__ dlse, int B, int S, int H,
+                                      int Dv) {
   // one warp per (b, s, h) row
   const int64_t row = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x % 32;
@@ -846,7 +849,8 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ dout, co
     const int64_t bs = row / H;
     const int sidx = bs % S;
     const int bidx = bs / S;
-    delta[((int64_t)bidx * H + h) * lse_stride(S) + sidx] = acc;
+    const int64_t at = ((int64_t)bidx * H + h) * lse_stride(S) + sidx;
+    delta[at] = dlse != nullptr ? acc - dlse[at] : acc;
   }
 }
 
@@ -1452,13 +1456,13 @@ void attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, 
 
 void attn_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
               void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int Sq, int Sk, int H, int Hk,
-              int Dqk, int Dv, bool causal, float scale, cudaStream_t s) {
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s, const float* dlse) {
   using namespace attn_impl;
   (void)dq_acc;
   if (B == 0 || Sq == 0 || Sk == 0) return;
   const int64_t rows = (int64_t)B * Sq * H;
   attn_bwd_delta_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, s>>>(
-      static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(o), delta, B, Sq, H, Dv);
+      static_cast<const __nv_bfloat16*>(dout), static_cast<const __nv_bfloat16*>(o), delta, dlse, B, Sq, H, Dv);
   check_cuda(cudaGetLastError(), "attn_bwd_delta");
   BwdParams p;
   p.B = B;

@@ -114,7 +114,7 @@ void attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, 
               int Dqk, int Dv, bool causal, float scale, cudaStream_t s);
 void attn_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
               void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int Sq, int Sk, int H, int Hk,
-              int Dqk, int Dv, bool causal, float scale, cudaStream_t s);
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s, const float* dlse = nullptr);
 int attn_error_code(bool reset);
 
 }  // namespace ttb

@@ -9,8 +9,10 @@
   ``(clamp(up, -L, L) + 1) * g * sigmoid(alpha * g)``, ``g = clamp(gate, max=L)``,
   with gate/up interleaved in one ``mlp1`` projection.
 
-The attention here is written out with PyTorch ops (sinks and windows are not
-in the tcgen05 flash kernel); its cost is O(S^2) memory per head.
+Full-attention layers run on the tcgen05 flash kernel: the sink only rescales
+each row by ``sigmoid(lse - sink)`` (differentiable through the kernel's LSE
+output).  Sliding-window layers (and CPU) use the PyTorch formulation, O(S^2)
+memory per head.
 """
 from __future__ import annotations
 
@@ -100,6 +102,12 @@ class GptOssAttention(nn.Module):
         nn.init.trunc_normal_(self.sinks, std=init_std)
 
     def inner_attention(self, q, k, v, attention_masks=None):
+        if q.is_cuda and not self.window:
+            # full layers on the flash kernel: a sink logit s only rescales each row by
+            # sum exp / (sum exp + exp s) = sigmoid(lse - s)
+            o, lse = ops.attention_with_lse(q, k, v, causal=True, scale=self.scale)
+            w = torch.sigmoid(lse - _local(self.sinks).float().view(1, 1, -1))
+            return (o.float() * w[..., None]).to(o.dtype)
         return sink_attention(q, k, v, _local(self.sinks), self.window, self.scale)
 
     def forward(self, x, cos, sin, attention_masks=None):

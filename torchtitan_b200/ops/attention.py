@@ -69,3 +69,58 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
         v = F.pad(v, (0, pv - dv))
         return _Attn.apply(q, k, v, causal, scale)[..., :dv]
     return _Attn.apply(q, k, v, causal, scale)
+
+
+class _AttnLse(torch.autograd.Function):
+    """Attention that also returns the per-row log-sum-exp ``[B, S, H]`` (natural log) and
+    backpropagates through both outputs: a gradient on the LSE shifts delta by -dlse."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        o, lse = torch.ops.tt_b200.attn_fwd(q, k, v, causal, scale)
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.causal, ctx.scale = causal, scale
+        S = q.shape[1]
+        return o, lse[:, :, :S].transpose(1, 2)
+
+    @staticmethod
+    def backward(ctx, do, dlse):
+        q, k, v, o, lse = ctx.saved_tensors
+        full = None
+        if dlse is not None:
+            full = torch.zeros_like(lse)
+            full[:, :, : q.shape[1]] = dlse.transpose(1, 2).float()
+        dq, dk, dv = _ext.ext().attn_bwd(do.contiguous(), q, k, v, o, lse, ctx.causal, ctx.scale, full)
+        return dq, dk, dv, None, None
+
+
+def _attention_lse_ref(q, k, v, causal, scale):
+    H, Hk = q.shape[2], k.shape[2]
+    if Hk != H:
+        k, v = k.repeat_interleave(H // Hk, dim=2), v.repeat_interleave(H // Hk, dim=2)
+    s = torch.einsum("bshd,bthd->bhst", q.float(), k.float()) * scale
+    if causal:
+        Sq, Sk = q.shape[1], k.shape[1]
+        keep = torch.ones(Sq, Sk, dtype=torch.bool, device=q.device).tril(diagonal=Sk - Sq)
+        s = s.masked_fill(~keep, float("-inf"))
+    lse = torch.logsumexp(s, -1)
+    o = torch.einsum("bhst,bthd->bshd", torch.exp(s - lse[..., None]), v.float())
+    return o.to(q.dtype), lse.transpose(1, 2)
+
+
+def attention_with_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+                       scale: float | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(o [B,S,H,Dv], lse [B,S,H] fp32); both differentiable."""
+    scale = float(scale if scale is not None else 1.0 / math.sqrt(q.shape[-1]))
+    if not q.is_cuda:
+        return _attention_lse_ref(q, k, v, causal, scale)
+    dqk, dv = q.shape[-1], v.shape[-1]
+    pq, pv = _padded_dims(dqk, dv)
+    if (pq, pv) != (dqk, dv):
+        F = torch.nn.functional
+        q, k = F.pad(q, (0, pq - dqk)), F.pad(k, (0, pq - dqk))
+        v = F.pad(v, (0, pv - dv))
+        o, lse = _AttnLse.apply(q, k, v, causal, scale)
+        return o[..., :dv], lse
+    return _AttnLse.apply(q, k, v, causal, scale)
