@@ -345,7 +345,7 @@ def _pp(rank, world, out_dir, module, config):
     from torchtitan_b200.trainer import Trainer
 
     t = Trainer(ConfigManager().parse_args([
-        "--module", module, "--config", config, "--training.steps", "2", "--training.seq-len", "128",
+        "--module", module, "--config", config, "--training.steps", "2", "--training.seq-len", "64",
         "--parallelism.pipeline-parallel-degree", "2", "--parallelism.data-parallel-shard-degree", "1",
         "--parallelism.pipeline-parallel-microbatch-size", "2", "--training.local-batch-size", "4",
         "--parallelism.pipeline-parallel-schedule", "Interleaved1F1B", "--training.dtype", "float32",
