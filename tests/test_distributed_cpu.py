@@ -487,7 +487,7 @@ def test_kimi_tensor_parallel_matches_single_device():
         _run(_kimi_tp, 2, d)
 
 
-def _llama_tp_grads(rank, world, out_dir, sp, module="llama3", config="llama3_debugmodel_cpu"):
+def _llama_tp_grads(rank, world, out_dir, sp, module="llama3", config="llama3_debugmodel_cpu", extra=()):
     from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
 
     from torchtitan_b200.components.loss import cross_entropy_loss
@@ -499,7 +499,8 @@ def _llama_tp_grads(rank, world, out_dir, sp, module="llama3", config="llama3_de
         "--training.seq-len", "64", "--parallelism.tensor-parallel-degree", "2",
         "--parallelism.data-parallel-shard-degree", "1", "--debug.seed", "0", "--dump-folder", out_dir,
         "--training.dtype", "float32", "--training.mixed-precision-param", "float32",
-        "--activation-checkpoint.mode", "none", *([] if sp else ["--parallelism.no-enable-sequence-parallel"])]))
+        "--activation-checkpoint.mode", "none", *([] if sp else ["--parallelism.no-enable-sequence-parallel"]),
+        *extra]))
     model = t.model_parts[0]
     full = get_model_state_dict(model, options=StateDictOptions(full_state_dict=True))
     import importlib
@@ -529,6 +530,13 @@ def _llama_tp_grads(rank, world, out_dir, sp, module="llama3", config="llama3_de
 def test_tensor_parallel_gradients(sp, module, config):
     with tempfile.TemporaryDirectory() as d:
         _run(_llama_tp_grads, 2, d, sp, module, config)
+
+
+@pytest.mark.parametrize("sp", [True, False])
+@pytest.mark.parametrize("module,config", [("qwen3", "qwen3_debugmodel_moe"), ("deepseek_v3", "deepseek_v3_debugmodel")])
+def test_expert_tensor_parallel_gradients(sp, module, config):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_llama_tp_grads, 2, d, sp, module, config, ("--parallelism.expert-tensor-parallel-degree", "2"))
 
 
 # ---------------------------------------------------------------- context parallel, gradient-exact

@@ -158,7 +158,22 @@ class MoE(nn.Module):
                 self.expert_bias.zero_()
             self.tokens_per_expert.zero_()
 
+    etp_group = None  # expert tensor parallelism: hidden dims of the experts sharded over TP
+    etp_sequence_parallel = False
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.etp_group is None:
+            return self._forward_core(x)
+        from torchtitan_b200.parallel import tensor_parallel as tp
+
+        # every TP rank routes all tokens and computes its slice of every expert's hidden
+        # dim; the partial outputs are summed (and re-sharded along the sequence)
+        g = self.etp_group
+        x = tp.all_gather_seq(x, g) if self.etp_sequence_parallel else tp.grad_all_reduce(x, g)
+        out = self._forward_core(x)
+        return tp.reduce_scatter_seq(out, g) if self.etp_sequence_parallel else tp.all_reduce(out, g)
+
+    def _forward_core(self, x: torch.Tensor) -> torch.Tensor:
         B, S, D = x.shape
         xf = x.reshape(-1, D)
         top, idx, counts, scores = self.router(xf, self.expert_bias)

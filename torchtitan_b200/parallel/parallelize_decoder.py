@@ -49,9 +49,16 @@ def _apply_tp(model: nn.Module, tp_mesh, parallelism: Any) -> None:
             raise NotImplementedError(f"tensor parallelism for {type(moe).__name__} is not wired")
     apply_tp_llama(model, tp_mesh, loss_parallel=not parallelism.disable_loss_parallel, sequence_parallel=sp)
     group = tp_mesh.get_group()
+    etp = parallelism.expert_tensor_parallel_degree
+    if etp not in (1, tp_mesh.size()):
+        raise ValueError(f"expert_tensor_parallel_degree must be 1 or the TP degree ({tp_mesh.size()})")
     for blk in model.layers.values():
         moe = getattr(blk, "moe", None)
-        if moe is not None and sp:
+        if moe is not None and etp > 1:
+            from torchtitan_b200.parallel.tensor_parallel import apply_etp
+
+            apply_etp(moe, tp_mesh, sp)
+        elif moe is not None and sp:
             # routed tokens are this rank's sequence shard; experts, router and shared experts are
             # replicated over TP, so their weight gradients are summed over TP
             moe.experts.grad_reduce_group = group

@@ -99,6 +99,11 @@ def reduce_scatter_seq(x, group):
     return _RSSeq.apply(x, group)
 
 
+def all_reduce(x, group):
+    """Sum over ``group`` in forward, identity in backward (row-parallel partial sums)."""
+    return _AllReduce.apply(x, group)
+
+
 def grad_all_reduce(x, group):
     return _GradAllReduce.apply(x, group)
 
@@ -115,6 +120,9 @@ def tp_linear(x: torch.Tensor, w: torch.Tensor, mode: str, group, sequence_paral
             return async_tp.ag_matmul(x, w, group)
         if mode == "row":
             return async_tp.matmul_rs(x, w, group)
+    if mode == "row_local":
+        # partial output summed by the caller together with other partial sums
+        return mm(x, w)
     if mode == "col_local":
         # input already complete on every rank and its gradient left partial on purpose: the
         # producer of the input reduces it (see apply_tp_mla)
@@ -188,7 +196,7 @@ def _replicate_param(mod: nn.Module, name: str, mesh) -> None:
 def parallelize_linear(lin: nn.Module, mode: str, tp_mesh, sequence_parallel: bool) -> None:
     from torch.distributed.tensor import Shard
 
-    _shard_param(lin, "weight", tp_mesh, Shard(1 if mode == "row" else 0))
+    _shard_param(lin, "weight", tp_mesh, Shard(1 if mode in ("row", "row_local") else 0))
     lin.tp_mode = mode
     lin.tp_group = tp_mesh.get_group()
     lin.sequence_parallel = sequence_parallel
@@ -277,6 +285,29 @@ def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_p
     model._tp_group = group
     model._tp_loss_parallel = loss_parallel
     model._sp_degree = ws if sequence_parallel else 1
+
+
+def apply_etp(moe: nn.Module, tp_mesh, sequence_parallel: bool) -> None:
+    """Expert tensor parallelism on the TP mesh (parity: reference ``ExpertTensorParallel``,
+    ``distributed/expert_parallel.py:232-340``, with etp = tp): routed experts shard their
+    hidden dim (w1/w3 ``Shard(1)``, w2 ``Shard(2)``), shared experts are column/row split
+    without their own collectives, the router is replicated (its weight gradient, a partial
+    sum over the hidden slices, is reduced over TP); the MoE block gathers its input and
+    reduces its output once (``MoE.etp_group``)."""
+    from torch.distributed.tensor import Shard, distribute_tensor
+
+    group = tp_mesh.get_group()
+    ex = moe.experts
+    for name, dim in (("w1", 1), ("w3", 1), ("w2", 2)):
+        p = getattr(ex, name)
+        setattr(ex, name, nn.Parameter(distribute_tensor(p.data, tp_mesh, [Shard(dim)])))
+    if moe.shared_experts is not None:
+        parallelize_linear(moe.shared_experts.w1, "col_local", tp_mesh, False)
+        parallelize_linear(moe.shared_experts.w3, "col_local", tp_mesh, False)
+        parallelize_linear(moe.shared_experts.w2, "row_local", tp_mesh, False)
+    moe.router.gate.grad_reduce_group = group
+    moe.etp_group = group
+    moe.etp_sequence_parallel = sequence_parallel
 
 
 def apply_tp_mla(att: nn.Module, tp_mesh, sequence_parallel: bool) -> None:
