@@ -526,7 +526,8 @@ def _llama_tp_grads(rank, world, out_dir, sp, module="llama3", config="llama3_de
 @pytest.mark.parametrize("module,config", [("llama3", "llama3_debugmodel_cpu"), ("qwen3", "qwen3_debugmodel"),
                                            ("qwen3", "qwen3_debugmodel_moe"), ("llama4", "llama4_debugmodel"),
                                            ("deepseek_v3", "deepseek_v3_debugmodel"),
-                                           ("deepseek_v3", "deepseek_v3_debugmodel_qlora")])
+                                           ("deepseek_v3", "deepseek_v3_debugmodel_qlora"),
+                                           ("gpt_oss", "gpt_oss_debugmodel")])
 def test_tensor_parallel_gradients(sp, module, config):
     with tempfile.TemporaryDirectory() as d:
         _run(_llama_tp_grads, 2, d, sp, module, config)

@@ -62,8 +62,16 @@ class Linear(nn.Module):
 
             y = tp.tp_linear(x, w, self.tp_mode, self.tp_group, self.sequence_parallel)
         if self.bias is not None:
-            y = y + _local(self.bias).to(y.dtype)
+            b = _local(self.bias)
+            g = self.bias_grad_reduce_group or self.grad_reduce_group
+            if g is not None:
+                from torchtitan_b200.parallel.tensor_parallel import grad_all_reduce
+
+                b = grad_all_reduce(b, g)
+            y = y + b.to(y.dtype)
         return y
+
+    bias_grad_reduce_group = None  # replicated bias of a row-parallel layer on sequence shards
 
     def extra_repr(self) -> str:
         return f"in={self.in_features}, out={self.out_features}, tp={self.tp_mode}"

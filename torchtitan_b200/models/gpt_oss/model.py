@@ -111,10 +111,12 @@ class GptOssAttention(nn.Module):
         return sink_attention(q, k, v, _local(self.sinks), self.window, self.scale)
 
     def forward(self, x, cos, sin, attention_masks=None):
-        B, S, _ = x.shape
-        q = ops.rope(self.wq(x).view(B, S, -1, self.head_dim), cos, sin)
-        k = ops.rope(self.wk(x).view(B, S, -1, self.head_dim), cos, sin)
-        v = self.wv(x).view(B, S, -1, self.head_dim)
+        B = x.shape[0]
+        q, k, v = self.wq(x), self.wk(x), self.wv(x)
+        S = q.shape[1]  # the full sequence under sequence parallelism (the projections gather it)
+        q = ops.rope(q.view(B, S, -1, self.head_dim), cos, sin)
+        k = ops.rope(k.view(B, S, -1, self.head_dim), cos, sin)
+        v = v.view(B, S, -1, self.head_dim)
         if self.cp_hook is not None:
             if self.window:
                 raise NotImplementedError("context parallelism with sliding-window layers is not wired")
@@ -145,8 +147,14 @@ class GptOssExperts(nn.Module):
         u = u.clamp(-self.limit, self.limit)
         return (u + 1) * g * torch.sigmoid(self.alpha * g)
 
+    grad_reduce_group = None  # replicated over TP on sequence-sharded tokens: reduce weight grads
+
     def forward(self, x: torch.Tensor, counts: list[int]) -> torch.Tensor:
         w1, b1, w2, b2 = (_local(t) for t in (self.mlp1_weight, self.mlp1_bias, self.mlp2_weight, self.mlp2_bias))
+        if self.grad_reduce_group is not None:
+            from torchtitan_b200.parallel.tensor_parallel import grad_all_reduce
+
+            w1, b1, w2, b2 = (grad_all_reduce(t, self.grad_reduce_group) for t in (w1, b1, w2, b2))
         outs, start = [], 0
         for e, n in enumerate(counts):
             if n:

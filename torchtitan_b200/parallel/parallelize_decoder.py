@@ -40,6 +40,15 @@ def _apply_tp(model: nn.Module, tp_mesh, parallelism: Any) -> None:
     from torchtitan_b200.models.common.moe import MoE
 
     sp = parallelism.enable_sequence_parallel
+    first = next(iter(model.layers.values()))
+    if type(first.attention).__name__ == "GptOssAttention":
+        from torchtitan_b200.parallel.tensor_parallel import apply_tp_gpt_oss
+
+        if parallelism.expert_tensor_parallel_degree > 1:
+            raise NotImplementedError("expert tensor parallelism for GPT-OSS experts is not wired")
+        apply_tp_gpt_oss(model, tp_mesh, loss_parallel=not parallelism.disable_loss_parallel, sequence_parallel=sp)
+        maybe_enable_async_tp(parallelism, tp_mesh)
+        return
     for blk in model.layers.values():
         att = getattr(blk, "attention", None)
         if not isinstance(att, GQAttention) and not hasattr(att, "wkv_a"):

@@ -197,6 +197,11 @@ def parallelize_linear(lin: nn.Module, mode: str, tp_mesh, sequence_parallel: bo
     from torch.distributed.tensor import Shard
 
     _shard_param(lin, "weight", tp_mesh, Shard(1 if mode in ("row", "row_local") else 0))
+    if getattr(lin, "bias", None) is not None:
+        if mode in ("col", "col_local"):
+            _shard_param(lin, "bias", tp_mesh, Shard(0))
+        elif sequence_parallel:  # added after the reduce-scatter: each rank sees its own tokens
+            lin.bias_grad_reduce_group = tp_mesh.get_group()
     lin.tp_mode = mode
     lin.tp_group = tp_mesh.get_group()
     lin.sequence_parallel = sequence_parallel
@@ -219,6 +224,43 @@ def wrap_replicated_norm(norm: nn.Module, tp_mesh) -> None:
         return _ops.rms_norm(x, w.to(x.dtype), _norm.eps)
 
     norm.forward = fwd
+
+
+def _tp_embed_and_head(model: nn.Module, tp_mesh, loss_parallel: bool, sequence_parallel: bool) -> None:
+    """Embedding replicated (embeds the local sequence shard under SP), final norm
+    sequence-parallel, output head column-parallel over the vocabulary."""
+    group = tp_mesh.get_group()
+    ws = tp_mesh.size()
+    if sequence_parallel and model.norm is not None:
+        wrap_replicated_norm(model.norm, tp_mesh)
+    if model.tok_embeddings is not None:
+        _replicate_param(model.tok_embeddings, "weight", tp_mesh)
+        emb = model.tok_embeddings
+
+        def emb_fwd(tokens, _emb=emb):
+            w = grad_all_reduce(_emb.weight.to_local(), group) if sequence_parallel else _emb.weight.to_local()
+            if sequence_parallel:
+                r, S = dist.get_rank(group), tokens.shape[1]
+                tokens = tokens[:, r * S // ws:(r + 1) * S // ws]
+            return nn.functional.embedding(tokens, w)
+
+        emb.forward = emb_fwd
+    if model.output is not None:
+        parallelize_linear(model.output, "col", tp_mesh, sequence_parallel)
+        model.output.loss_parallel = loss_parallel
+        if not loss_parallel:
+            orig = model.output.forward
+
+            def out_fwd(x, _orig=orig):
+                y = _orig(x)
+                outs = [torch.empty_like(y) for _ in range(ws)]
+                dist.all_gather(outs, y.contiguous(), group=group)
+                return torch.cat(outs, -1)
+
+            model.output.forward = out_fwd
+    model._tp_group = group
+    model._tp_loss_parallel = loss_parallel
+    model._sp_degree = ws if sequence_parallel else 1
 
 
 def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_parallel: bool = True) -> None:
@@ -255,36 +297,31 @@ def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_p
         if sequence_parallel:
             wrap_replicated_norm(blk.attention_norm, tp_mesh)
             wrap_replicated_norm(blk.ffn_norm, tp_mesh)
-    if sequence_parallel and model.norm is not None:
-        wrap_replicated_norm(model.norm, tp_mesh)
-    if model.tok_embeddings is not None:
-        _replicate_param(model.tok_embeddings, "weight", tp_mesh)
-        emb = model.tok_embeddings
+    _tp_embed_and_head(model, tp_mesh, loss_parallel, sequence_parallel)
 
-        def emb_fwd(tokens, _emb=emb):
-            w = grad_all_reduce(_emb.weight.to_local(), group) if sequence_parallel else _emb.weight.to_local()
-            if sequence_parallel:
-                r, S = dist.get_rank(group), tokens.shape[1]
-                tokens = tokens[:, r * S // ws:(r + 1) * S // ws]
-            return nn.functional.embedding(tokens, w)
 
-        emb.forward = emb_fwd
-    if model.output is not None:
-        parallelize_linear(model.output, "col", tp_mesh, sequence_parallel)
-        model.output.loss_parallel = loss_parallel
-        if not loss_parallel:
-            orig = model.output.forward
+def apply_tp_gpt_oss(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_parallel: bool) -> None:
+    """GPT-OSS: q/k/v column-parallel (weights and biases), o row-parallel, sinks sharded
+    with their heads; the MoE (router, experts with biases) is replicated over TP and, on
+    sequence shards, its gradients are summed over TP."""
+    from torch.distributed.tensor import Shard
 
-            def out_fwd(x, _orig=orig):
-                y = _orig(x)
-                outs = [torch.empty_like(y) for _ in range(ws)]
-                dist.all_gather(outs, y.contiguous(), group=group)
-                return torch.cat(outs, -1)
-
-            model.output.forward = out_fwd
-    model._tp_group = group
-    model._tp_loss_parallel = loss_parallel
-    model._sp_degree = ws if sequence_parallel else 1
+    group = tp_mesh.get_group()
+    ws = tp_mesh.size()
+    for blk in model.layers.values():
+        att = blk.attention
+        if att.sinks.shape[0] % ws or att.wk.out_features // att.head_dim % ws:
+            raise ValueError(f"TP degree {ws} must divide the query and key/value head counts")
+        for lin in (att.wq, att.wk, att.wv):
+            parallelize_linear(lin, "col", tp_mesh, sequence_parallel)
+        parallelize_linear(att.wo, "row", tp_mesh, sequence_parallel)
+        _shard_param(att, "sinks", tp_mesh, Shard(0))
+        if sequence_parallel:
+            wrap_replicated_norm(blk.attention_norm, tp_mesh)
+            wrap_replicated_norm(blk.ffn_norm, tp_mesh)
+            blk.moe.router.gate.grad_reduce_group = group
+            blk.moe.experts.grad_reduce_group = group
+    _tp_embed_and_head(model, tp_mesh, loss_parallel, sequence_parallel)
 
 
 def apply_etp(moe: nn.Module, tp_mesh, sequence_parallel: bool) -> None:
