@@ -40,6 +40,30 @@ class ForgeEngine:
         t.step += 1
         return t.train_step(iter(batches))
 
+    def step_with_loss(self, loss_fn) -> torch.Tensor:
+        """One optimizer step on ``loss_fn(model)``, any differentiable per-rank objective
+        (e.g. an RL surrogate).  The step minimises the mean of the ranks' objectives over
+        the data-parallel ranks, with the trainer's gradient finish, clipping, optimizer and
+        LR step.  Returns this rank's objective."""
+        t = self.trainer
+        pd = t.parallel_dims
+        if pd.pp_enabled:
+            raise NotImplementedError("custom objectives under pipeline parallelism are not wired")
+        t.optimizers.zero_grad()
+        model = t.model_parts[0]
+        dp_rt = getattr(model, "_dp_runtime", None)
+        if dp_rt is not None:
+            dp_rt.begin_microbatch(0, 1)
+        # data-parallel gradients are summed (not averaged) over the batch ranks
+        n_dp = pd.get_mesh("batch").size() if pd.dp_enabled else 1
+        comp = getattr(model, "_fsdp_grad_compensation", 1)
+        t.step += 1
+        with t.train_context():
+            loss = loss_fn(model)
+            (loss * (comp / n_dp)).backward()
+        t.apply_gradients()
+        return loss.detach()
+
     @torch.no_grad()
     def forward(self, input_dict: dict[str, torch.Tensor]) -> torch.Tensor:
         t = self.trainer

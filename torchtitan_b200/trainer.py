@@ -295,31 +295,12 @@ class Trainer(Stateful, Configurable):
             (loss * comp if comp != 1 else loss).backward()
         return loss
 
-    def train_step(self, data_iterator: Iterator) -> torch.Tensor:
-        self.optimizers.zero_grad()
-        lr = self.lr_schedulers.schedulers[0].get_last_lr()[0]
+    def apply_gradients(self) -> torch.Tensor:
+        """Everything after the backward passes of a step: data-parallel gradient finish,
+        global-norm clipping (fused into the optimizer where it supports it), optimizer,
+        semi-sync and LR-scheduler steps.  Returns the pre-clip gradient norm."""
         pd = self.parallel_dims
-        mbs = []
-        local_valid = 0
-        for _ in range(self.gradient_accumulation_steps):
-            inp, labels = next(data_iterator)
-            local_valid += int((labels != IGNORE_INDEX).sum())
-            mbs.append((inp, labels))
-        local_valid_t = torch.tensor(float(local_valid), device=self.device)
-        if pd.semi_sync_replicas:  # each replica normalises by its own tokens
-            global_valid = (dist_utils.dist_sum(local_valid_t, pd.get_mesh("dp_shard")) if pd.dp_shard > 1
-                            else local_valid_t)
-        else:
-            global_valid = dist_utils.dist_sum(local_valid_t, pd.get_mesh("batch")) if pd.dp_enabled else local_valid_t
-        losses = []
         dp_rt = getattr(self.model_parts[0], "_dp_runtime", None)
-        for i, (inp, labels) in enumerate(mbs):
-            if dp_rt is not None:
-                dp_rt.begin_microbatch(i, len(mbs))
-            inp = {k: (v.to(self.device, non_blocking=True) if torch.is_tensor(v) else v) for k, v in inp.items()}
-            labels = labels.to(self.device, non_blocking=True)
-            losses.append(self.forward_backward_step(input_dict=inp, labels=labels,
-                                                     global_valid_tokens=global_valid).detach())
         max_norm = self.config.training.max_norm
         if self.optimizers.config.early_step_in_backward:
             max_norm = 0.0  # parameters already stepped inside backward: nothing left to clip
@@ -348,6 +329,34 @@ class Trainer(Stateful, Configurable):
         if self.semi_sync is not None:
             self.semi_sync.after_step(self.step)
         self.lr_schedulers.step()
+        return grad_norm
+
+    def train_step(self, data_iterator: Iterator) -> torch.Tensor:
+        self.optimizers.zero_grad()
+        lr = self.lr_schedulers.schedulers[0].get_last_lr()[0]
+        pd = self.parallel_dims
+        mbs = []
+        local_valid = 0
+        for _ in range(self.gradient_accumulation_steps):
+            inp, labels = next(data_iterator)
+            local_valid += int((labels != IGNORE_INDEX).sum())
+            mbs.append((inp, labels))
+        local_valid_t = torch.tensor(float(local_valid), device=self.device)
+        if pd.semi_sync_replicas:  # each replica normalises by its own tokens
+            global_valid = (dist_utils.dist_sum(local_valid_t, pd.get_mesh("dp_shard")) if pd.dp_shard > 1
+                            else local_valid_t)
+        else:
+            global_valid = dist_utils.dist_sum(local_valid_t, pd.get_mesh("batch")) if pd.dp_enabled else local_valid_t
+        losses = []
+        dp_rt = getattr(self.model_parts[0], "_dp_runtime", None)
+        for i, (inp, labels) in enumerate(mbs):
+            if dp_rt is not None:
+                dp_rt.begin_microbatch(i, len(mbs))
+            inp = {k: (v.to(self.device, non_blocking=True) if torch.is_tensor(v) else v) for k, v in inp.items()}
+            labels = labels.to(self.device, non_blocking=True)
+            losses.append(self.forward_backward_step(input_dict=inp, labels=labels,
+                                                     global_valid_tokens=global_valid).detach())
+        grad_norm = self.apply_gradients()
         loss = torch.sum(torch.stack([l.reshape(()) for l in losses]))
         self.last_loss = loss
         wd = getattr(dp_rt, "watchdog", None)
