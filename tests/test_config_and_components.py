@@ -481,3 +481,17 @@ def test_mx_blocked_scale_layout_round_trip():
     ref = mx_dequantize_ref(codes, sf) @ mx_dequantize_ref(qw, sw).t()
     torch.testing.assert_close(y, ref.bfloat16().float())
     assert ((y - x @ w.t()).norm() / (x @ w.t()).norm()) < 0.08
+
+
+def test_document_attention_matches_block_causal_mask():
+    from torchtitan_b200 import ops
+    from torchtitan_b200.models.common.attention import document_causal_mask
+
+    torch.manual_seed(0)
+    doc = torch.tensor([[0] * 3 + [1] * 9 + [2] * 4, [0] * 16])
+    q, k, v = torch.randn(2, 16, 4, 8), torch.randn(2, 16, 2, 8), torch.randn(2, 16, 2, 8)
+    o = ops.document_attention(q, k, v, doc)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        q.transpose(1, 2), k.repeat_interleave(2, 2).transpose(1, 2), v.repeat_interleave(2, 2).transpose(1, 2),
+        attn_mask=document_causal_mask(doc)).transpose(1, 2)
+    assert torch.allclose(o, ref, atol=1e-5)

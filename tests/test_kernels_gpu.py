@@ -336,3 +336,30 @@ def test_attention_lse_output_and_gradient(D):
         outs.append((o.float(), lse.float(), qq.grad.float(), kk.grad.float(), vv.grad.float()))
     for a, b in zip(*outs):
         torch.testing.assert_close(a, b, rtol=3e-2, atol=3e-2)
+
+
+def test_document_attention(ext):
+    """Packed documents (block-causal masking) through the flash kernel, one document per launch."""
+    from torchtitan_b200 import ops
+    from torchtitan_b200.models.common.attention import document_causal_mask
+
+    torch.manual_seed(9)
+    B, S, H, Hk, D = 2, 320, 4, 2, 128
+    lens = [[1, 37, 130, 152], [320]]
+    doc = torch.tensor([sum(([i] * n for i, n in enumerate(r)), []) for r in lens], device="cuda")
+    q = torch.randn(B, S, H, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(B, S, Hk, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(B, S, Hk, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    o = ops.document_attention(q, k, v, doc)
+    g = torch.randn_like(o)
+    o.backward(g)
+    qr, kr, vr = (t.detach().float().requires_grad_() for t in (q, k, v))
+    orf = torch.nn.functional.scaled_dot_product_attention(
+        qr.transpose(1, 2), kr.repeat_interleave(2, 2).transpose(1, 2), vr.repeat_interleave(2, 2).transpose(1, 2),
+        attn_mask=document_causal_mask(doc)).transpose(1, 2)
+    orf.backward(g.float())
+    torch.cuda.synchronize()
+    assert ext.attn_error_code(True) == 0
+    assert _rel(o, orf) < 2e-2
+    for a, b in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
+        assert _rel(a, b) < 3e-2

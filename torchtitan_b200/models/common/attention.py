@@ -56,7 +56,7 @@ class GQAttention(nn.Module):
     def inner_attention(self, q, k, v, attention_masks=None):
         if self.mask_type == "block_causal" and attention_masks is not None:
             if q.is_cuda:
-                raise NotImplementedError("document masking on CUDA goes through varlen packing (not yet wired)")
+                return ops.document_attention(q, k, v, attention_masks)
             from torchtitan_b200.ops import reference as R
 
             H, Hk = q.shape[2], k.shape[2]

@@ -126,7 +126,7 @@ def cross_entropy_sum(logits: torch.Tensor, labels: torch.Tensor, ignore_index: 
 # ---------------------------------------------------------------- MoE experts
 from .moe import grouped_swiglu  # noqa: E402
 from .grouped import grouped_swiglu_padded  # noqa: E402
-from .attention import attention_with_lse  # noqa: E402
+from .attention import attention_with_lse, document_attention  # noqa: E402
 
 
 # -------------------------------------------------------------------------- AdamW

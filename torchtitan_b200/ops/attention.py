@@ -124,3 +124,28 @@ def attention_with_lse(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal
         o, lse = _AttnLse.apply(q, k, v, causal, scale)
         return o[..., :dv], lse
     return _AttnLse.apply(q, k, v, causal, scale)
+
+
+def document_segments(doc_ids: torch.Tensor) -> list[list[tuple[int, int]]]:
+    """[B, S] non-decreasing document ids -> per row, the (start, end) of each document."""
+    B, S = doc_ids.shape
+    change = torch.ones(B, S, dtype=torch.bool, device=doc_ids.device)
+    change[:, 1:] = doc_ids[:, 1:] != doc_ids[:, :-1]
+    rows = []
+    for starts in change.cpu():
+        s = starts.nonzero().flatten().tolist() + [S]
+        rows.append(list(zip(s[:-1], s[1:])))
+    return rows
+
+
+def document_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, doc_ids: torch.Tensor,
+                       scale: float | None = None) -> torch.Tensor:
+    """Causal attention within packed documents (reference ``models/common/attention.py:220``
+    varlen path): q [B,S,H,D], k/v [B,S,Hk,D]; ``doc_ids`` [B,S] labels each token's
+    document (contiguous runs).  Each document runs through the flash kernel on its own
+    rows, so no work is spent on cross-document tiles."""
+    parts = []
+    for b, segs in enumerate(document_segments(doc_ids)):
+        for s0, s1 in segs:
+            parts.append(attention(q[b:b + 1, s0:s1], k[b:b + 1, s0:s1], v[b:b + 1, s0:s1], True, scale))
+    return torch.cat([p[0] for p in parts]).view(*q.shape[:-1], v.shape[-1])
