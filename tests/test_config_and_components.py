@@ -495,3 +495,37 @@ def test_document_attention_matches_block_causal_mask():
         q.transpose(1, 2), k.repeat_interleave(2, 2).transpose(1, 2), v.repeat_interleave(2, 2).transpose(1, 2),
         attn_mask=document_causal_mask(doc)).transpose(1, 2)
     assert torch.allclose(o, ref, atol=1e-5)
+
+
+def test_patchify_matches_hf_qwen2vl_image_processor_layout():
+    """Flat patches in merge-block order: row r of block (bh, bw) and intra (mh, mw) holds
+    pixels [(bh*m+mh)*P : +P, (bw*m+mw)*P : +P] of every channel, repeated over T."""
+    from torchtitan_b200.components.mm_dataloader import patchify
+
+    img = torch.randn(3, 64, 96)
+    P, T, m = 16, 2, 2
+    x, grid = patchify(img, P, T, m)
+    assert grid == [1, 4, 6] and x.shape == (24, 3 * T * P * P)
+    r = 0
+    for bh in range(2):
+        for bw in range(3):
+            for mh in range(m):
+                for mw in range(m):
+                    y0, x0 = (bh * m + mh) * P, (bw * m + mw) * P
+                    want = img[:, y0:y0 + P, x0:x0 + P][:, None].expand(3, T, P, P).reshape(-1)
+                    assert torch.equal(x[r], want)
+                    r += 1
+
+
+def test_synthetic_image_text_loader_places_images():
+    from torchtitan_b200.components.mm_dataloader import SyntheticImageTextDataLoader
+    from torchtitan_b200.components.loss import IGNORE_INDEX
+
+    dl = SyntheticImageTextDataLoader(SyntheticImageTextDataLoader.Config(
+        images_per_sample=2, image_size=64, patch_size=16, vision_token_id=2046, vocab_size=2048),
+        dp_rank=0, dp_world_size=1, seq_len=64, local_batch_size=2)
+    inp, labels = next(iter(dl))
+    assert inp["pixel_values"].shape == (4 * 16, 3 * 2 * 16 * 16) and inp["grid_thw"].tolist() == [[1, 4, 4]] * 4
+    assert int((inp["input"] == 2046).sum()) == 2 * 2 * 4
+    assert bool((labels[:, :-1][inp["input"][:, 1:] == 2046] == IGNORE_INDEX).all())
+    assert not bool((labels == 2046).any())

@@ -137,3 +137,69 @@ def test_llama4_matches_hf():
         rope_parameters={"rope_type": "llama3", "rope_theta": a.rope_theta, "factor": a.rope_scaling_factor,
                          "low_freq_factor": 1.0, "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
     _compare(m, transformers.Llama4ForCausalLM(cfg), sd, a.vocab_size, seq=512)  # 2 attention chunks
+
+
+def _qwen3_vl_pair(**overrides):
+    a, m, sd = _ours("qwen3_vl", "debugmodel", **overrides)
+    vc = dict(depth=a.vision_layers, hidden_size=a.vision_dim, intermediate_size=a.vision_ffn_dim,
+              num_heads=a.vision_heads, patch_size=a.patch_size, temporal_patch_size=a.temporal_patch_size,
+              spatial_merge_size=a.spatial_merge_size, out_hidden_size=a.dim,
+              num_position_embeddings=a.num_position_embeddings,
+              deepstack_visual_indexes=list(a.deepstack_indices), hidden_act="gelu_pytorch_tanh")
+    tc = dict(vocab_size=a.vocab_size, hidden_size=a.dim, intermediate_size=a.hidden_dim,
+              num_hidden_layers=a.n_layers, num_attention_heads=a.n_heads, num_key_value_heads=a.n_kv_heads,
+              head_dim=a.head_dim, rms_norm_eps=a.norm_eps, max_position_embeddings=a.max_seq_len,
+              rope_parameters={"rope_type": "default", "rope_theta": a.rope_theta,
+                               "mrope_section": list(a.mrope_section)})
+    cfg = transformers.Qwen3VLConfig(vision_config=vc, text_config=tc, image_token_id=a.image_token_id,
+                                     video_token_id=a.video_token_id, tie_word_embeddings=False)
+    hf = transformers.Qwen3VLForConditionalGeneration(cfg)
+    res = hf.load_state_dict(sd, strict=False)
+    assert not res.missing_keys and not res.unexpected_keys, res
+    return a, m, hf.eval()
+
+
+def test_qwen3_vl_matches_hf():
+    from torchtitan_b200.components.mm_dataloader import patchify
+
+    a, m, hf = _qwen3_vl_pair()
+    g = torch.Generator().manual_seed(1)
+    # two images (4x6 and 2x2 merged tokens) in row 0, one (2x4) in row 1
+    shapes = [(128, 192), (64, 64), (64, 128)]
+    pix, grids = [], []
+    for H, W in shapes:
+        p, grid = patchify(torch.randn(3, H, W, generator=g), a.patch_size, a.temporal_patch_size,
+                           a.spatial_merge_size)
+        pix.append(p)
+        grids.append(grid)
+    S = 80
+    tok = torch.randint(0, 2000, (2, S), generator=g)
+    img = a.image_token_id
+    tok[0, 5:5 + 24] = img
+    tok[0, 40:44] = img
+    tok[1, 10:18] = img
+    pixel_values, grid_thw = torch.cat(pix), torch.tensor(grids)
+    mm = (tok == img).int()
+    with torch.no_grad():
+        ref = hf(input_ids=tok, pixel_values=pixel_values, image_grid_thw=grid_thw, mm_token_type_ids=mm).logits
+        out = m(tok, pixel_values=pixel_values, grid_thw=grid_thw)
+    err = float((ref - out).abs().max())
+    assert err <= 2e-5 * float(ref.abs().max()), err
+    # text only
+    t2 = torch.randint(0, 2000, (2, 32), generator=g)
+    with torch.no_grad():
+        assert torch.allclose(hf(input_ids=t2).logits, m(t2), atol=1e-4)
+
+
+def test_qwen3_vl_state_dict_roundtrip():
+    from torchtitan_b200.models.qwen3_vl import model_registry
+
+    spec = model_registry("debugmodel")
+    torch.manual_seed(0)
+    m = spec.model.build()
+    m.init_weights()
+    ad = spec.state_dict_adapter(spec.model, None)
+    sd = {k: v.detach() for k, v in m.state_dict().items()}
+    back = ad.from_hf(ad.to_hf(sd))
+    assert set(back) == set(sd)
+    assert all(torch.equal(back[k], sd[k]) for k in sd)

@@ -28,3 +28,39 @@ def test_family_bf16_forward_backward(module, flavor):
     assert torch.isfinite(loss) and 6.0 < float(loss) < 10.0
     grads = [p.grad for p in model.parameters()]
     assert all(g is not None and torch.isfinite(g).all() for g in grads)
+
+
+def test_qwen3_vl_bf16_forward_backward_with_images():
+    """Vision encoder (per-frame bidirectional flash attention, 2-D rotary) + MRoPE decoder
+    with DeepStack, bf16 on the kernels, against the same model in fp32 PyTorch on the CPU."""
+    from torchtitan_b200.components.mm_dataloader import patchify
+
+    spec = importlib.import_module("torchtitan_b200.models.qwen3_vl").model_registry("debugmodel")
+    a = spec.model
+    torch.manual_seed(0)
+    ref = a.build()
+    ref.init_weights()
+    with torch.device("cuda"):
+        model = a.build()
+    model.load_state_dict(ref.state_dict())
+    model.rope.init_weights(torch.device("cuda"))
+    model.vision_encoder.init_buffers(torch.device("cuda"))
+    model.mrope_axis = ref.mrope_axis.cuda()
+    for p in model.parameters():
+        p.data = p.data.bfloat16()
+    g = torch.Generator().manual_seed(1)
+    pix, grids = zip(*[patchify(torch.randn(3, 256, 256, generator=g), a.patch_size, a.temporal_patch_size,
+                                a.spatial_merge_size) for _ in range(2)])
+    tokens = torch.randint(0, 2000, (1, 512), generator=g)
+    tokens[0, 10:74] = a.image_token_id
+    tokens[0, 300:364] = a.image_token_id
+    kw = dict(pixel_values=torch.cat(pix), grid_thw=torch.tensor(grids))
+    with torch.no_grad():
+        want = ref(tokens, **kw)
+    logits = model(tokens.cuda(), pixel_values=kw["pixel_values"].cuda().bfloat16(), grid_thw=kw["grid_thw"])
+    rel = float((logits.float().cpu() - want).norm() / want.norm())
+    assert rel < 3e-2, rel
+    loss = F.cross_entropy(logits.flatten(0, 1).float(), tokens.cuda().roll(-1, 1).flatten())
+    loss.backward()
+    assert torch.isfinite(loss)
+    assert all(p.grad is not None and torch.isfinite(p.grad).all() for p in model.parameters())

@@ -73,5 +73,7 @@ class RotaryEmbedding(nn.Module):
     def tables(self, seq_len: int, positions: torch.Tensor | None = None):
         if positions is None:
             return self.cos[:seq_len], self.sin[:seq_len]
-        pos = positions[0] if positions.dim() == 2 else positions
-        return self.cos[pos], self.sin[pos]
+        if positions.dim() == 2 and positions.shape[0] == 1:
+            positions = positions[0]
+        # [S] -> [S, D/2]; per-row positions [B, S] -> [B, S, D/2]
+        return self.cos[positions], self.sin[positions]

@@ -73,7 +73,8 @@ class _Rope(torch.autograd.Function):
 
 
 def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """x: [B,S,H,D]; cos/sin: [S, D/2] fp32 (position-major)."""
+    """x: [B,S,H,D]; cos/sin: [S, D/2] fp32 (position-major), or [B, S, D/2] for per-row
+    positions (packed documents, multimodal 3-D positions)."""
     if not _cuda(x):
         return _ref.rope(x, cos, sin)
     return _Rope.apply(x, cos, sin)

@@ -17,11 +17,11 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """x: [B,S,H,D] with interleaved (re, im) pairs; cos/sin: [S, D/2]."""
+    """x: [B,S,H,D] with interleaved (re, im) pairs; cos/sin: [S, D/2] or per-row [B, S, D/2]."""
     xf = x.float().unflatten(-1, (-1, 2))
     re, im = xf[..., 0], xf[..., 1]
-    c = cos[None, :, None, :].float()
-    s = sin[None, :, None, :].float()
+    c = (cos[:, :, None, :] if cos.dim() == 3 else cos[None, :, None, :]).float()
+    s = (sin[:, :, None, :] if sin.dim() == 3 else sin[None, :, None, :]).float()
     out = torch.stack([re * c - im * s, re * s + im * c], -1).flatten(-2)
     return out.to(x.dtype)
 

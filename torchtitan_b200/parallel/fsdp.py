@@ -51,6 +51,8 @@ def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, redu
 
     _GLOO = dist.is_initialized() and dist.get_backend() == "gloo"
     model._fsdp_grad_compensation = dp_mesh.size() if _GLOO else 1
+    for unit in getattr(model, "fsdp_extra_units", ()):  # e.g. vision encoder blocks
+        _disable_grad_division(fully_shard(unit, **cfg, reshard_after_forward=reshard))
     first = getattr(model, "pp_first_module", "tok_embeddings")
     if getattr(model, first, None) is not None:
         _disable_grad_division(fully_shard(getattr(model, first), **cfg, reshard_after_forward=reshard))
