@@ -67,25 +67,34 @@ def _force_shapes(model: nn.Module, fqns: list[str]) -> set[tuple[int, int]]:
     return shapes
 
 
+def _blocks(model: nn.Module):
+    """(container, key, block) for every block: ``model.layers`` (a ModuleDict), or each
+    ModuleDict/ModuleList a model lists in ``ac_block_containers`` (e.g. FLUX's double
+    and single stream blocks)."""
+    for cont in getattr(model, "ac_block_containers", None) or [model.layers]:
+        items = list(cont.items()) if isinstance(cont, nn.ModuleDict) else list(enumerate(cont))
+        for k, blk in items:
+            yield cont, k, blk
+
+
 def apply_ac(model: nn.Module, ac: Any, **_: Any) -> None:
     if ac.mode == "none":
         return
-    layers = model.layers
     if ac.mode == "full":
-        for k, blk in list(layers.items()):
-            layers[k] = checkpoint_wrapper(blk, preserve_rng_state=ac.preserve_rng_state)
+        for cont, k, blk in _blocks(model):
+            cont[k] = checkpoint_wrapper(blk, preserve_rng_state=ac.preserve_rng_state)
         return
     if ac.mode == "memory_budget":
         raise NotImplementedError("memory_budget AC needs a tracing compiler; use 'selective' or 'full'")
     opt = ac.selective_ac_option
     if opt == "op":
         make_ctx = _op_sac_policy(_force_shapes(model, ac.per_op_sac_force_recompute_mm_shapes_by_fqns))
-        for k, blk in list(layers.items()):
-            layers[k] = checkpoint_wrapper(blk, context_fn=make_ctx, preserve_rng_state=ac.preserve_rng_state)
+        for cont, k, blk in _blocks(model):
+            cont[k] = checkpoint_wrapper(blk, context_fn=make_ctx, preserve_rng_state=ac.preserve_rng_state)
         return
     every = int(opt)
     if every <= 0:
         raise ValueError("selective_ac_option must be 'op' or a positive integer")
-    for i, (k, blk) in enumerate(list(layers.items())):
+    for i, (cont, k, blk) in enumerate(_blocks(model)):
         if i % every == 0:
-            layers[k] = checkpoint_wrapper(blk, preserve_rng_state=ac.preserve_rng_state)
+            cont[k] = checkpoint_wrapper(blk, preserve_rng_state=ac.preserve_rng_state)

@@ -13,8 +13,11 @@ from torchtitan_b200.utils.logging import init_logger, logger
 def main(trainer_cls=None) -> None:
     init_logger()
     cfg = ConfigManager().parse_args()
-    if trainer_cls is None:
-        from torchtitan_b200.trainer import Trainer as trainer_cls
+    if trainer_cls is None:  # the config names its trainer (e.g. FluxTrainer.Config)
+        from torchtitan_b200.trainer import Trainer
+
+        owner = getattr(type(cfg), "_owner", None)
+        trainer_cls = owner if isinstance(owner, type) and issubclass(owner, Trainer) else Trainer
     trainer = None
     try:
         trainer = trainer_cls(cfg)
