@@ -856,35 +856,39 @@ def test_hf_transformers_backend_trains_with_fsdp():
 
 
 # ---------------------------------------------------------------- Qwen3-VL, gradient-exact
-def _qwen3_vl_grads(rank, world, out_dir, mode):
+def _qwen3_vl_grads(rank, world, out_dir, mode, module="qwen3_vl"):
     from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
 
     from torchtitan_b200.components.loss import cross_entropy_loss
     from torchtitan_b200.config.manager import ConfigManager
-    from torchtitan_b200.models.qwen3_vl import model_registry
+    import importlib
+
     from torchtitan_b200.trainer import Trainer
 
+    model_registry = importlib.import_module(f"torchtitan_b200.models.{module}").model_registry
     par = (["--parallelism.tensor-parallel-degree", "2", "--parallelism.data-parallel-shard-degree", "1"]
            if mode == "tp" else ["--parallelism.data-parallel-shard-degree", "2"])
     t = Trainer(ConfigManager().parse_args([
-        "--module", "qwen3_vl", "--config", "qwen3_vl_debugmodel", "--training.steps", "1",
+        "--module", module, "--config", f"{module}_debugmodel", "--training.steps", "1",
         "--training.seq-len", "128", "--training.local-batch-size", "2", "--debug.seed", "0",
         "--dump-folder", out_dir, "--training.dtype", "float32", "--training.mixed-precision-param", "float32",
-        "--activation-checkpoint.mode", "none", *par]))
+        "--activation-checkpoint.mode", "none", "--dataloader.image-size", "64", *par]))
     model = t.model_parts[0]
     if mode == "fsdp":  # every vision block is its own FSDP unit
-        assert type(model.vision_encoder.blocks[0]).__name__.startswith("FSDP")
+        enc = model.vision_encoder.blocks if module == "qwen3_vl" else model.encoder.layers
+        assert type(enc[0]).__name__.startswith("FSDP")
     full = get_model_state_dict(model, options=StateDictOptions(full_state_dict=True))
     ref = model_registry("debugmodel").model.build()
     ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in full.items()}, strict=False)
     ref.rope.init_weights()
-    ref.vision_encoder.init_buffers()
+    if module == "qwen3_vl":
+        ref.vision_encoder.init_buffers()
     inp, labels = next(iter(t.dataloader))  # same batch on both ranks (seeded by dp rank 0 for tp)
     if mode == "fsdp":
         obj = [(inp, labels)]
         dist.broadcast_object_list(obj, src=0)
         inp, labels = obj[0]
-    kw = {"pixel_values": inp["pixel_values"], "grid_thw": inp["grid_thw"]}
+    kw = {k: v for k, v in inp.items() if k != "input"}
     cross_entropy_loss(ref(inp["input"], **kw), labels).backward()
     comp = getattr(model, "_fsdp_grad_compensation", 1)
     (t._loss(model(inp["input"], **kw), labels) * comp).backward()
@@ -897,10 +901,11 @@ def _qwen3_vl_grads(rank, world, out_dir, mode):
     t.close()
 
 
+@pytest.mark.parametrize("module", ["qwen3_vl", "vlm"])
 @pytest.mark.parametrize("mode", ["tp", "fsdp"])
-def test_qwen3_vl_parallel_gradients(mode):
+def test_vision_language_parallel_gradients(mode, module):
     with tempfile.TemporaryDirectory() as d:
-        _run(_qwen3_vl_grads, 2, d, mode)
+        _run(_qwen3_vl_grads, 2, d, mode, module)
 
 
 # ---------------------------------------------------------------- FLUX under FSDP2

@@ -203,3 +203,46 @@ def test_qwen3_vl_state_dict_roundtrip():
     back = ad.from_hf(ad.to_hf(sd))
     assert set(back) == set(sd)
     assert all(torch.equal(back[k], sd[k]) for k in sd)
+
+
+def test_siglip2_encoder_matches_hf():
+    """The VLM's SigLIP2 encoder on two images of different aspect ratios (padded batch)."""
+    from torchtitan_b200.components.mm_dataloader import patchify_raster
+
+    a, m, sd = _ours("vlm", "debugmodel")
+    cfg = transformers.Siglip2VisionConfig(hidden_size=a.vit_dim, intermediate_size=a.vit_ffn_dim,
+                                           num_hidden_layers=a.vit_layers, num_attention_heads=a.vit_heads,
+                                           num_channels=a.channels, patch_size=a.patch_size,
+                                           num_patches=a.n_pos_embs ** 2, layer_norm_eps=a.vit_eps,
+                                           hidden_act="gelu_pytorch_tanh", vision_use_head=False)
+    hf = transformers.Siglip2VisionModel(cfg).eval()
+    vsd = {k[len("vision_model."):]: v for k, v in sd.items() if k.startswith("vision_model.")}
+    res = hf.vision_model.load_state_dict(vsd, strict=False)
+    assert not res.missing_keys and not res.unexpected_keys, res
+    g = torch.Generator().manual_seed(2)
+    p1, g1 = patchify_raster(torch.randn(3, 96, 160, generator=g), a.patch_size)   # 6 x 10
+    p2, g2 = patchify_raster(torch.randn(3, 128, 64, generator=g), a.patch_size)   # 8 x 4
+    L = 64
+    pix = torch.zeros(2, L, p1.shape[1])
+    pix[0, :60], pix[1, :32] = p1, p2
+    mask = torch.zeros(2, L, dtype=torch.long)
+    mask[0, :60], mask[1, :32] = 1, 1
+    shapes = torch.tensor([g1, g2])
+    with torch.no_grad():
+        ref = hf(pixel_values=pix, pixel_attention_mask=mask, spatial_shapes=shapes).last_hidden_state
+        out = m.encoder(pix, shapes)
+    want = torch.cat([ref[0, :60], ref[1, :32]])
+    assert float((want - out).abs().max()) <= 2e-5 * float(want.abs().max()), float((want - out).abs().max())
+
+
+def test_vlm_state_dict_round_trip():
+    from torchtitan_b200.models.vlm import model_registry
+
+    spec = model_registry("debugmodel")
+    torch.manual_seed(0)
+    m = spec.model.build()
+    m.init_weights()
+    ad = spec.state_dict_adapter(spec.model, None)
+    sd = {k: v.detach() for k, v in m.state_dict().items()}
+    back = ad.from_hf(ad.to_hf(sd))
+    assert set(back) == set(sd) and all(torch.equal(back[k], sd[k]) for k in sd)

@@ -7,7 +7,8 @@ import torch.nn.functional as F
 
 FAMILIES = [("qwen3", "debugmodel"), ("qwen3", "debugmodel_moe"), ("deepseek_v3", "debugmodel"),
             ("deepseek_v3", "debugmodel_qlora"), ("llama4", "debugmodel"), ("gpt_oss", "debugmodel"),
-            ("attention_residual", "debugmodel"), ("attention_residual", "debugmodel_full"), ("qwen3_vl", "debugmodel")]
+            ("attention_residual", "debugmodel"), ("attention_residual", "debugmodel_full"), ("qwen3_vl", "debugmodel"),
+            ("vlm", "debugmodel")]
 
 
 def _build(module, flavor, seq=64):
@@ -122,7 +123,7 @@ def test_deepseek_mla_scale_and_shared_rope_key():
 
 @pytest.mark.parametrize("module,config", [("qwen3", "qwen3_debugmodel_moe"), ("deepseek_v3", "deepseek_v3_debugmodel"),
                                            ("llama4", "llama4_debugmodel"), ("gpt_oss", "gpt_oss_debugmodel"),
-                                           ("qwen3_vl", "qwen3_vl_debugmodel")])
+                                           ("qwen3_vl", "qwen3_vl_debugmodel"), ("vlm", "vlm_debugmodel")])
 def test_trainer_runs_family_configs(module, config, tmp_path):
     from torchtitan_b200.config.manager import ConfigManager
     from torchtitan_b200.trainer import Trainer

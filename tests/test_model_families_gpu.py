@@ -97,3 +97,38 @@ def test_flux_bf16_forward_backward():
     assert rel < 3e-2, rel
     out.float().pow(2).mean().backward()
     assert all(p.grad is not None and torch.isfinite(p.grad).all() for p in model.parameters())
+
+
+def test_vlm_bf16_forward_backward_with_images():
+    """Llama 3 + SigLIP2 (per-image bidirectional flash attention over unpadded patches)
+    against the same model in fp32 PyTorch on the CPU."""
+    from torchtitan_b200.components.mm_dataloader import patchify_raster
+
+    spec = importlib.import_module("torchtitan_b200.models.vlm").model_registry("debugmodel")
+    a = spec.model
+    torch.manual_seed(0)
+    ref = a.build()
+    ref.init_weights()
+    with torch.device("cuda"):
+        model = a.build()
+    model.load_state_dict(ref.state_dict())
+    model.rope.init_weights(torch.device("cuda"))
+    for p in model.parameters():
+        p.data = p.data.bfloat16()
+    g = torch.Generator().manual_seed(1)
+    p1, g1 = patchify_raster(torch.randn(3, 128, 192, generator=g), a.patch_size)  # 8 x 12
+    p2, g2 = patchify_raster(torch.randn(3, 64, 128, generator=g), a.patch_size)   # 4 x 8
+    pix = torch.zeros(2, 96, p1.shape[1])
+    pix[0, :96], pix[1, :32] = p1, p2
+    tokens = torch.randint(0, 2000, (1, 512), generator=g)
+    tokens[0, 20:116] = a.image_token_id
+    tokens[0, 300:332] = a.image_token_id
+    grid = torch.tensor([g1, g2])
+    with torch.no_grad():
+        want = ref(tokens, pixel_values=pix, grid_hw=grid)
+    logits = model(tokens.cuda(), pixel_values=pix.cuda().bfloat16(), grid_hw=grid)
+    rel = float((logits.float().cpu() - want).norm() / want.norm())
+    assert rel < 3e-2, rel
+    loss = F.cross_entropy(logits.flatten(0, 1).float(), tokens.cuda().roll(-1, 1).flatten())
+    loss.backward()
+    assert all(p.grad is not None and torch.isfinite(p.grad).all() for p in model.parameters())

@@ -56,6 +56,15 @@ def patchify(img: torch.Tensor, patch: int, temporal: int = 2, merge: int = 2) -
     return x.reshape(gh * gw, C * temporal * patch * patch), [1, gh, gw]
 
 
+def patchify_raster(img: torch.Tensor, patch: int) -> tuple[torch.Tensor, list[int]]:
+    """[C, H, W] -> (patches in raster order ``[gh*gw, P*P*C]``, each flattened as (row,
+    column, channel): the SigLIP2 processor layout), [gh, gw]."""
+    C, H, W = img.shape
+    gh, gw = H // patch, W // patch
+    x = img[:, : gh * patch, : gw * patch].reshape(C, gh, patch, gw, patch).permute(1, 3, 2, 4, 0)
+    return x.reshape(gh * gw, patch * patch * C), [gh, gw]
+
+
 class MultimodalDataLoader(BaseDataLoader):
     @dataclass(kw_only=True, slots=True)
     class Config(BaseDataLoader.Config):
@@ -187,6 +196,9 @@ class SyntheticImageTextDataLoader(BaseDataLoader):
         temporal_patch_size: int = 2
         merge_size: int = 2
         vision_token_id: int = 151655
+        layout: str = "patches"
+        """"patches": flat merge-ordered patches + ``grid_thw`` (Qwen3-VL);
+        "padded": ``[N, L, P*P*C]`` raster patches padded to L = (image_size/P)^2 + ``grid_hw`` (SigLIP2)."""
 
     def __init__(self, config: Config, **kw: Any):
         super().__init__(config, **kw)
@@ -194,7 +206,7 @@ class SyntheticImageTextDataLoader(BaseDataLoader):
         self.vocab_size = int(v)
         g = config.image_size // config.patch_size
         self.grid = [1, g, g]
-        self.tokens_per_image = (g // config.merge_size) ** 2
+        self.tokens_per_image = g * g if config.layout == "padded" else (g // config.merge_size) ** 2
         self.batches_emitted = 0
         if config.images_per_sample * self.tokens_per_image > self.seq_len:
             raise ValueError("images do not fit the sequence")
@@ -214,11 +226,17 @@ class SyntheticImageTextDataLoader(BaseDataLoader):
                 s = cut + k * self.tokens_per_image
                 row[s:s + self.tokens_per_image] = c.vision_token_id
                 img = torch.randn(3, c.image_size, c.image_size, generator=g)
-                pix.append(patchify(img, c.patch_size, c.temporal_patch_size, c.merge_size)[0])
+                if c.layout == "padded":
+                    pix.append(patchify_raster(img, c.patch_size)[0])
+                else:
+                    pix.append(patchify(img, c.patch_size, c.temporal_patch_size, c.merge_size)[0])
             ids.append(row)
         ids = torch.stack(ids)
         labels = ids[:, 1:].masked_fill(ids[:, 1:] == c.vision_token_id, IGNORE_INDEX)
         n = c.images_per_sample * self.local_batch_size
+        if c.layout == "padded":
+            return ({"input": ids[:, :-1], "pixel_values": torch.stack(pix),
+                     "grid_hw": torch.tensor([self.grid[1:]] * n, dtype=torch.long)}, labels)
         return ({"input": ids[:, :-1], "pixel_values": torch.cat(pix),
                  "grid_thw": torch.tensor([self.grid] * n, dtype=torch.long)}, labels)
 
