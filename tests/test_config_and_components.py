@@ -529,3 +529,23 @@ def test_synthetic_image_text_loader_places_images():
     assert int((inp["input"] == 2046).sum()) == 2 * 2 * 4
     assert bool((labels[:, :-1][inp["input"][:, 1:] == 2046] == IGNORE_INDEX).all())
     assert not bool((labels == 2046).any())
+
+
+def test_peer_dp_launches_buckets_in_index_order():
+    """Reduce-scatter kernels wait on the peers' kernels for the same bucket: every rank must
+    queue them in the same order, whatever order its gradients arrive in."""
+    from types import SimpleNamespace
+
+    from torchtitan_b200.parallel.peer_dp import PeerDataParallel
+
+    dp = PeerDataParallel.__new__(PeerDataParallel)
+    dp.buckets = [SimpleNamespace(pending=1, launched=False, index=i) for i in range(4)]
+    dp._next_launch = 0
+    order = []
+    dp._launch = lambda b: order.append(b.index)
+    for k in (2, 3, 0, 1):  # gradients complete out of order
+        dp.buckets[k].pending = 0
+        dp._launch_ready()
+        if k == 2:
+            assert order == []
+    assert order == [0, 1, 2, 3]

@@ -64,7 +64,11 @@ __device__ bool signal_and_wait(const PeerTable& t, int slot, uint32_t epoch, in
     asm volatile("fence.acq_rel.sys;" ::: "memory");
     st_release_sys(t.sig[threadIdx.x] + slot * t.world + t.rank, epoch);
   }
-  if (threadIdx.x == 0) {
+  // once any wait of this process gave up, later waits return at once: a failed step
+  // surfaces after one time limit instead of one limit per queued kernel
+  if (threadIdx.x == 0 && *static_cast<volatile int*>(&g_err) != 0) ok = 0;
+  __syncthreads();
+  if (threadIdx.x == 0 && ok) {
     const uint32_t* mine = t.sig[t.rank] + slot * t.world;
     const uint64_t t0 = now_ns();
     for (int j = 0; j < t.world; ++j) {

@@ -135,6 +135,7 @@ class PeerDataParallel:
         self.wait_limit_s = float(os.environ.get("TTB_DP_WAIT_S", "20"))
         self.sync = True
         self._got: list[bool] = []
+        self._next_launch = 0
         self._first_micro = True
         self._stream = torch.cuda.Stream(dev) if dev.type == "cuda" else None
         self._alloc_buffers()
@@ -207,6 +208,7 @@ class PeerDataParallel:
         for b in self.buckets:
             b.pending = len(b.params)
             b.launched = False
+        self._next_launch = 0
 
     def begin_microbatch(self, index: int, count: int) -> None:
         if index == 0:
@@ -233,8 +235,17 @@ class PeerDataParallel:
                 b = self._bucket_of[i]
                 b.pending -= 1
                 if b.pending == 0:
-                    self._launch(b)
+                    self._launch_ready()
         return hook
+
+    def _launch_ready(self) -> None:
+        """Launch complete buckets strictly in bucket-index order.  Every rank then issues the
+        same sequence of waiting kernels on its reduction stream whatever order its autograd
+        engine produced the gradients in: a rank waiting on bucket k never sits behind a
+        kernel for bucket j > k that a peer has queued after its own bucket k."""
+        while self._next_launch < len(self.buckets) and self.buckets[self._next_launch].pending == 0:
+            self._launch(self.buckets[self._next_launch])
+            self._next_launch += 1
 
     def _launch(self, b: Bucket) -> None:
         if b.launched:
@@ -263,6 +274,7 @@ class PeerDataParallel:
                         o = self.offsets[i]
                         self.gbuf[o:o + self.params[i].numel()].zero_()
                 self._launch(b)
+        self._next_launch = len(self.buckets)
         if self._stream is not None:
             torch.cuda.current_stream(self.device).wait_stream(self._stream)
 
