@@ -549,3 +549,19 @@ def test_peer_dp_launches_buckets_in_index_order():
         if k == 2:
             assert order == []
     assert order == [0, 1, 2, 3]
+
+
+def test_compile_flag_falls_back_cleanly_without_cuda(tmp_path):
+    """``--compile.enable`` asks for CUDA-graph capture; where it cannot apply (no GPU) the
+    trainer says why and trains uncaptured."""
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.parallel.cuda_graphs import cuda_graphs_applicable
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "1", "--compile.enable",
+        "--training.seq-len", "64", "--dump-folder", str(tmp_path)]))
+    assert cuda_graphs_applicable(t.parallel_dims, t.model_parts[0]) is not None
+    t.train()
+    assert t.step == 1
+    t.close()

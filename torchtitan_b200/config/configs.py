@@ -79,8 +79,9 @@ class ActivationCheckpointConfig:
 
 @dataclass(kw_only=True, slots=True)
 class CompileConfig:
-    """Accepted for CLI parity and ignored: this framework's hot path is
-    hand-written CUDA kernels, not a tracing compiler."""
+    """``enable`` with ``backend="cudagraph"`` captures every dense decoder block's forward
+    and backward in CUDA graphs (no tracing compiler: the kernels are hand-written);
+    ``components`` containing "model" selects it.  Other backends are not implemented."""
     enable: bool = False
     components: list[str] = field(default_factory=lambda: ["model", "loss"])
     backend: str = "cudagraph"

@@ -184,6 +184,8 @@ class Trainer(Stateful, Configurable):
 
             materialize_data_parallel(model)
             model.train()
+            if c.compile.enable and "model" in c.compile.components:
+                self._maybe_capture_cuda_graphs(model)
             self.model_parts = [model]
             self.pp_has_first_stage = self.pp_has_last_stage = True
 
@@ -222,6 +224,22 @@ class Trainer(Stateful, Configurable):
                     f"{self.gradient_accumulation_steps}, seq {c.training.seq_len}, steps {c.training.steps}")
 
     # --------------------------------------------------------------- helpers
+    def _maybe_capture_cuda_graphs(self, model: torch.nn.Module) -> None:
+        """``compile.enable`` with ``compile.backend=cudagraph``: capture each block's forward
+        and backward in CUDA graphs where the layout allows (else log why not)."""
+        from torchtitan_b200.parallel.cuda_graphs import apply_cuda_graphs, cuda_graphs_applicable
+
+        c = self.config
+        if c.compile.backend != "cudagraph":
+            logger.warning(f"compile.backend={c.compile.backend}: only 'cudagraph' is implemented; not compiling")
+            return
+        why = cuda_graphs_applicable(self.parallel_dims, model)
+        if why is not None:
+            logger.warning(f"compile.enable: blocks not captured in CUDA graphs ({why})")
+            return
+        apply_cuda_graphs(model, c.training.local_batch_size, c.training.seq_len,
+                          model.tok_embeddings.weight.dtype)
+
     def _loss(self, pred: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         m = self.model_parts[-1]
         if getattr(m, "_tp_loss_parallel", False):
