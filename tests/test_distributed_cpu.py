@@ -936,3 +936,48 @@ def _flux_fsdp(rank, world, out_dir):
 def test_flux_fsdp_training():
     with tempfile.TemporaryDirectory() as d:
         _run(_flux_fsdp, 2, d)
+
+
+# ---------------------------------------------------------------- ETP combined with EP
+def _etp_ep_grads(rank, world, out_dir, sp):
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.components.loss import cross_entropy_loss
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.models.qwen3 import model_registry
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", "qwen3", "--config", "qwen3_debugmodel_moe", "--training.steps", "1",
+        "--training.seq-len", "64", "--training.local-batch-size", "2", "--parallelism.tensor-parallel-degree", "2",
+        "--parallelism.data-parallel-shard-degree", "2", "--parallelism.expert-parallel-degree", "2",
+        "--parallelism.expert-tensor-parallel-degree", "2", "--debug.seed", "0", "--dump-folder", out_dir,
+        "--training.dtype", "float32", "--training.mixed-precision-param", "float32",
+        "--activation-checkpoint.mode", "none", *([] if sp else ["--parallelism.no-enable-sequence-parallel"])]))
+    model = t.model_parts[0]
+    w1 = next(iter(model.layers.values())).moe.experts.w1
+    assert tuple(w1.to_local().shape[:2]) == (w1.shape[0] // 2, w1.shape[1] // 2)  # [ep, etp] shards
+    full = get_model_state_dict(model, options=StateDictOptions(full_state_dict=True))
+    ref = model_registry("debugmodel_moe").model.build()
+    ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in full.items()}, strict=False)
+    ref.rope.init_weights()
+    for n, b in model.named_buffers():
+        if n.endswith("expert_bias"):
+            dict(ref.named_buffers())[n].copy_(b)
+    tokens = torch.randint(0, 2048, (2, 64), generator=torch.Generator().manual_seed(3))
+    labels = tokens.roll(-1, 1)
+    cross_entropy_loss(ref(tokens), labels).backward()
+    comp = getattr(model, "_fsdp_grad_compensation", 1)
+    (t._loss(model(tokens), labels) * comp).backward()
+    named = dict(ref.named_parameters())
+    for n, p in model.named_parameters():
+        g = p.grad.full_tensor() if hasattr(p.grad, "full_tensor") else p.grad
+        r = named[n.replace("_checkpoint_wrapped_module.", "")].grad * 2  # both data-parallel ranks see the batch
+        assert float((g - r).abs().max()) <= 2e-4 * float(r.abs().max()) + 1e-7, (n, sp)
+    t.close()
+
+
+@pytest.mark.parametrize("sp", [True, False])
+def test_expert_tensor_parallel_with_expert_parallel(sp):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_etp_ep_grads, 4, d, sp)

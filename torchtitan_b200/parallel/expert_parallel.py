@@ -57,12 +57,14 @@ def apply_ep(moe_modules: list[nn.Module], ep_mesh, backend: str = "standard") -
     (``parallel.ep_fused``)."""
     from torch.distributed.tensor import Shard, distribute_tensor
 
-    group = ep_mesh.get_group()
+    two_d = ep_mesh.ndim == 2  # [ep, etp]: expert dim over ep, hidden dim over etp
+    group = ep_mesh["ep"].get_group() if two_d else ep_mesh.get_group()
     for moe in moe_modules:
         ex = moe.experts
-        for name in ("w1", "w2", "w3"):
+        for name, hdim in (("w1", 1), ("w2", 2), ("w3", 1)):
             p = getattr(ex, name)
-            setattr(ex, name, nn.Parameter(distribute_tensor(p.data, ep_mesh, [Shard(0)])))
+            place = [Shard(0), Shard(hdim)] if two_d else [Shard(0)]
+            setattr(ex, name, nn.Parameter(distribute_tensor(p.data, ep_mesh, place)))
         if backend == "fused":
             from .ep_fused import make_fused_ep_dispatch
 

@@ -33,7 +33,7 @@ from torchtitan_b200.parallel.peer_dp import apply_peer_dp, peer_dp_applicable
 from torchtitan_b200.utils.logging import logger
 
 
-def _apply_tp(model: nn.Module, tp_mesh, parallelism: Any) -> None:
+def _apply_tp(model: nn.Module, tp_mesh, parallelism: Any, ep_degree: int = 1) -> None:
     from torchtitan_b200.models.common import GQAttention
     from torchtitan_b200.parallel.tensor_parallel import apply_tp_llama, maybe_enable_async_tp
 
@@ -66,7 +66,7 @@ def _apply_tp(model: nn.Module, tp_mesh, parallelism: Any) -> None:
         if moe is not None and etp > 1:
             from torchtitan_b200.parallel.tensor_parallel import apply_etp
 
-            apply_etp(moe, tp_mesh, sp)
+            apply_etp(moe, tp_mesh, sp, distribute_experts=ep_degree == 1)
         elif moe is not None and sp:
             # routed tokens are this rank's sequence shard; experts, router and shared experts are
             # replicated over TP, so their weight gradients are summed over TP
@@ -86,7 +86,7 @@ def parallelize_decoder(model: nn.Module, *, parallel_dims: Any, training: Any, 
     if training.seq_len % pd.seq_len_divisor:
         raise ValueError(f"seq_len {training.seq_len} must be divisible by 2*cp*tp = {pd.seq_len_divisor}")
     if pd.tp_enabled:
-        _apply_tp(model, pd.get_mesh("tp"), parallelism)
+        _apply_tp(model, pd.get_mesh("tp"), parallelism, pd.ep)
         logger.info(f"applied tensor parallel (tp={pd.tp})")
     if pd.cp_enabled:
         attns = [blk.attention for blk in model.layers.values()]
@@ -95,7 +95,9 @@ def parallelize_decoder(model: nn.Module, *, parallel_dims: Any, training: Any, 
         logger.info(f"applied context parallel ({parallelism.context_parallel_method}, cp={pd.cp})")
     moes = [blk.moe for blk in model.layers.values() if getattr(blk, "moe", None) is not None]
     if pd.ep_enabled and moes:
-        apply_ep(moes, pd.get_mesh("ep"), backend=parallelism.expert_parallel_comm_backend)
+        # with expert tensor parallelism the experts are sharded over [ep, etp] together
+        mesh = pd.get_mesh(["ep", "etp"]) if pd.etp_enabled else pd.get_mesh("ep")
+        apply_ep(moes, mesh, backend=parallelism.expert_parallel_comm_backend)
         logger.info(f"applied expert parallel (ep={pd.ep}) to {len(moes)} MoE layers")
     if ac_config.mode != "none":
         apply_ac(model, ac_config)

@@ -324,18 +324,19 @@ def apply_tp_gpt_oss(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence
     _tp_embed_and_head(model, tp_mesh, loss_parallel, sequence_parallel)
 
 
-def apply_etp(moe: nn.Module, tp_mesh, sequence_parallel: bool) -> None:
+def apply_etp(moe: nn.Module, tp_mesh, sequence_parallel: bool, distribute_experts: bool = True) -> None:
     """Expert tensor parallelism on the TP mesh (parity: reference ``ExpertTensorParallel``,
     ``distributed/expert_parallel.py:232-340``, with etp = tp): routed experts shard their
     hidden dim (w1/w3 ``Shard(1)``, w2 ``Shard(2)``), shared experts are column/row split
     without their own collectives, the router is replicated (its weight gradient, a partial
     sum over the hidden slices, is reduced over TP); the MoE block gathers its input and
-    reduces its output once (``MoE.etp_group``)."""
+    reduces its output once (``MoE.etp_group``).  With expert parallelism as well
+    (``distribute_experts=False``), ``apply_ep`` shards the experts over ``[ep, etp]`` in one go."""
     from torch.distributed.tensor import Shard, distribute_tensor
 
     group = tp_mesh.get_group()
     ex = moe.experts
-    for name, dim in (("w1", 1), ("w3", 1), ("w2", 2)):
+    for name, dim in ((("w1", 1), ("w3", 1), ("w2", 2)) if distribute_experts else ()):
         p = getattr(ex, name)
         setattr(ex, name, nn.Parameter(distribute_tensor(p.data, tp_mesh, [Shard(dim)])))
     if moe.shared_experts is not None:
