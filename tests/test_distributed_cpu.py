@@ -981,3 +981,48 @@ def _etp_ep_grads(rank, world, out_dir, sp):
 def test_expert_tensor_parallel_with_expert_parallel(sp):
     with tempfile.TemporaryDirectory() as d:
         _run(_etp_ep_grads, 4, d, sp)
+
+
+def _flux_cp(rank, world, out_dir):
+    """Ulysses context parallelism for FLUX: the sharded loss and gradients equal the
+    full-sequence ones of the same weights and batch."""
+    import pathlib
+
+    sys.path.insert(0, str(pathlib.Path(__file__).parent))
+    from test_flux_cpu import _small_cfg
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.models.flux.trainer import FluxTrainer
+
+    cfg = _small_cfg(pathlib.Path(out_dir), steps=1)
+    cfg.parallelism.context_parallel_degree = 2
+    cfg.parallelism.data_parallel_shard_degree = 1
+    cfg.training.max_norm = 0.0
+    t = FluxTrainer(cfg)
+    model = t.model_parts[0]
+    full = get_model_state_dict(model, options=StateDictOptions(full_state_dict=True))
+    ref = t.model_args.build()
+    ref.load_state_dict(full)
+    inp, labels = next(iter(t.dataloader))
+    t._microbatch = 0
+    f = t.flow_inputs(inp, labels)
+    target = f.pop("target")
+    loss_ref = t.loss_fn(ref(**f), target) / target.numel()
+    loss_ref.backward()
+    t._microbatch = 0
+    loss = t.forward_backward_step(input_dict=inp, labels=labels,
+                                   global_valid_tokens=torch.tensor(float(labels.numel())))
+    total = loss.detach().clone()
+    dist.all_reduce(total)
+    assert abs(float(total) - float(loss_ref)) < 1e-4 * abs(float(loss_ref)), (float(total), float(loss_ref))
+    named = dict(ref.named_parameters())
+    for n, p in model.named_parameters():
+        g = p.grad.full_tensor() if hasattr(p.grad, "full_tensor") else p.grad
+        r = named[n.replace("_checkpoint_wrapped_module.", "")].grad
+        assert float((g - r).abs().max()) <= 2e-4 * float(r.abs().max()) + 1e-7, n
+    t.close()
+
+
+def test_flux_context_parallel_matches_full_sequence():
+    with tempfile.TemporaryDirectory() as d:
+        _run(_flux_cp, 2, d)

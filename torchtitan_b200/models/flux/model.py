@@ -126,12 +126,20 @@ def _ln(x: torch.Tensor) -> torch.Tensor:
     return F.layer_norm(x, x.shape[-1:], eps=1e-6)
 
 
-def _attend(q, k, v, cos, sin):
-    """q/k/v [B, L, H, D]: rotary on q and k, bidirectional attention -> [B, L, H*D]."""
+def _attend(q, k, v, cos, sin, cp_group=None):
+    """q/k/v [B, L, H, D]: rotary on q and k, bidirectional attention -> [B, L, H*D].
+    Under context parallelism (Ulysses) each rank holds a slice of the token sequence:
+    an all-to-all trades it for all tokens of H/cp heads around the attention (the order
+    of tokens does not matter to bidirectional attention)."""
     q = ops.rope(q.contiguous(), cos, sin)
     k = ops.rope(k.contiguous(), cos, sin)
-    o = ops.attention(q, k, v.contiguous(), causal=False)
-    return o.flatten(2)
+    v = v.contiguous()
+    if cp_group is not None:
+        from torchtitan_b200.parallel.context_parallel import head_to_seq, seq_to_head
+
+        q, k, v = (seq_to_head(t, cp_group) for t in (q, k, v))
+        return head_to_seq(ops.attention(q, k, v, causal=False), cp_group).flatten(2)
+    return ops.attention(q, k, v, causal=False).flatten(2)
 
 
 class QKNorm(nn.Module):
@@ -170,6 +178,8 @@ class FluxMLP(nn.Module):
 
 
 class DoubleStreamBlock(nn.Module):
+    cp_group = None  # set by context parallelism
+
     def __init__(self, h: int, heads: int, mlp_ratio: float, qkv_bias: bool):
         super().__init__()
         mlp = int(h * mlp_ratio)
@@ -183,7 +193,7 @@ class DoubleStreamBlock(nn.Module):
         t_sh1, t_sc1, t_g1, t_sh2, t_sc2, t_g2 = self.txt_mod(vec)
         iq, ik, iv = self.img_attn.qkv_heads((1 + i_sc1) * _ln(img) + i_sh1)
         tq, tk, tv = self.txt_attn.qkv_heads((1 + t_sc1) * _ln(txt) + t_sh1)
-        o = _attend(torch.cat([tq, iq], 1), torch.cat([tk, ik], 1), torch.cat([tv, iv], 1), cos, sin)
+        o = _attend(torch.cat([tq, iq], 1), torch.cat([tk, ik], 1), torch.cat([tv, iv], 1), cos, sin, self.cp_group)
         t_o, i_o = o[:, :txt.shape[1]], o[:, txt.shape[1]:]
         img = img + i_g1 * self.img_attn.proj(i_o)
         img = img + i_g2 * self.img_mlp((1 + i_sc2) * _ln(img) + i_sh2)
@@ -193,6 +203,8 @@ class DoubleStreamBlock(nn.Module):
 
 
 class SingleStreamBlock(nn.Module):
+    cp_group = None  # set by context parallelism
+
     def __init__(self, h: int, heads: int, mlp_ratio: float):
         super().__init__()
         self.h, self.heads, self.mlp = h, heads, int(h * mlp_ratio)
@@ -207,7 +219,7 @@ class SingleStreamBlock(nn.Module):
         qkv, mlp = self.linear1((1 + scale) * _ln(x) + shift).split([3 * h, self.mlp], -1)
         q, k, v = qkv.reshape(B, L, 3, self.heads, h // self.heads).unbind(2)
         q, k = self.norm(q, k, v)
-        o = _attend(q, k, v, cos, sin)
+        o = _attend(q, k, v, cos, sin, self.cp_group)
         return x + gate * self.linear2(torch.cat([o, F.gelu(mlp, approximate="tanh")], -1))
 
 

@@ -57,26 +57,40 @@ class FluxTrainer(Trainer):
             lat = self.autoencoder.encode(images.to(self.device, self._enc_dtype)).float()
         return txt, vec, lat
 
-    def forward_backward_step(self, *, input_dict, labels, global_valid_tokens) -> torch.Tensor:
-        if self.parallel_dims.pp_enabled:
-            raise NotImplementedError("FLUX runs without pipeline parallelism")
-        model = self.model_parts[0]
+    def flow_inputs(self, input_dict, labels) -> dict[str, torch.Tensor]:
+        """Encoded, noised and packed model inputs of one microbatch (full sequences) and the
+        velocity target: keys img, img_ids, txt, txt_ids, timesteps, y, target."""
         txt, vec, x0 = self.encode_batch(input_dict["captions"], labels)
         B, C, h, w = x0.shape
         g = torch.Generator(device=self.device).manual_seed(
             hash((self.config.debug.seed or 0, self.step, self.dataloader.dp_rank, self._microbatch)) & (2**63 - 1))
-        self._microbatch += 1
         with torch.no_grad():
             noise = torch.randn(x0.shape, generator=g, device=self.device)
             t = torch.rand((B,), generator=g, device=self.device)
             xt = (1 - t.view(-1, 1, 1, 1)) * x0 + t.view(-1, 1, 1, 1) * noise
-            img = pack_latents(xt)
-            target = pack_latents(noise - x0)
+        return {"img": pack_latents(xt), "img_ids": latent_position_ids(B, h, w, self.device), "txt": txt,
+                "txt_ids": text_position_ids(B, txt.shape[1], self.device), "timesteps": t, "y": vec,
+                "target": pack_latents(noise - x0)}
+
+    def forward_backward_step(self, *, input_dict, labels, global_valid_tokens) -> torch.Tensor:
+        if self.parallel_dims.pp_enabled:
+            raise NotImplementedError("FLUX runs without pipeline parallelism")
+        model = self.model_parts[0]
+        f = self.flow_inputs(input_dict, labels)
+        self._microbatch += 1
         # global_valid_tokens counts image elements over the global batch; rescale to latent elements
-        norm = global_valid_tokens * (target.numel() / labels.numel())
+        norm = global_valid_tokens * (f["target"].numel() / labels.numel())
+        pd = self.parallel_dims
+        if pd.cp_enabled:  # every rank keeps its contiguous slice of the text and image tokens
+            mesh = pd.get_mesh("cp")
+            cp, r = mesh.size(), mesh.get_local_rank()
+            for k in ("img", "img_ids", "txt", "txt_ids", "target"):
+                if f[k].shape[1] % cp:
+                    raise ValueError(f"flux context parallel: {k} length {f[k].shape[1]} not divisible by cp={cp}")
+                f[k] = f[k].chunk(cp, dim=1)[r]
+        target = f.pop("target")
         with self.train_context():
-            pred = model(img=img, img_ids=latent_position_ids(B, h, w, self.device), txt=txt,
-                         txt_ids=text_position_ids(B, txt.shape[1], self.device), timesteps=t, y=vec)
+            pred = model(**f)
             loss = self.loss_fn(pred, target) / norm
             del pred
             comp = getattr(model, "_fsdp_grad_compensation", 1)
