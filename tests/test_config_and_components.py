@@ -565,3 +565,28 @@ def test_compile_flag_falls_back_cleanly_without_cuda(tmp_path):
     t.train()
     assert t.step == 1
     t.close()
+
+
+def test_bitwise_determinism_hashes(tmp_path):
+    """Two identically seeded debug runs end with bitwise-identical weights and optimizer
+    states; another seed does not (the hashes see every bit)."""
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+    from torchtitan_b200.utils.hashing import hash_model, hash_optimizer, hash_tensors
+
+    def run(seed):
+        t = Trainer(ConfigManager().parse_args([
+            "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "2",
+            "--training.seq-len", "64", "--debug.seed", str(seed), "--debug.deterministic",
+            "--dump-folder", str(tmp_path / str(seed))]))
+        t.train()
+        out = hash_model(t.model_parts[0]), hash_optimizer(t.optimizers.optimizers[0])
+        t.close()
+        return out
+
+    a, b, c = run(1), run(1), run(2)
+    assert a == b and a[0] != c[0]
+    x = torch.zeros(4, dtype=torch.bfloat16)
+    y = x.clone()
+    y.view(torch.int16)[2] = 1  # one bit
+    assert hash_tensors([("w", x)]) != hash_tensors([("w", y)])

@@ -800,6 +800,30 @@ def test_rank_delayed_past_timeout_surfaces_as_error():
     assert procs[0].exitcode == 0
 
 
+def _dropped_message(rank, world):
+    import datetime
+
+    pg = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=2))
+    t = torch.zeros(4)
+    if rank == 0:  # waits for a pipeline activation that rank 1 never sends
+        req = dist.irecv(t, src=1, group=pg)
+        with pytest.raises(Exception):
+            req.wait(timeout=datetime.timedelta(seconds=2))
+    dist.barrier()  # both ranks still answer afterwards
+
+
+def test_dropped_message_surfaces_as_error():
+    port = _port()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_entry, args=(r, 2, port, _dropped_message, ())) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(90)
+    assert all(not p.is_alive() for p in procs)
+    assert all(p.exitcode == 0 for p in procs)
+
+
 def _corrupt_resume(rank, world, out_dir):
     import glob
 
