@@ -590,3 +590,27 @@ def test_bitwise_determinism_hashes(tmp_path):
     y = x.clone()
     y.view(torch.int16)[2] = 1  # one bit
     assert hash_tensors([("w", x)]) != hash_tensors([("w", y)])
+
+
+def test_huggingface_tokenizer_files(tmp_path):
+    """tokenizer.json + tokenizer_config.json: special tokens, round trip, chat template."""
+    import json
+
+    from tokenizers import Tokenizer, models, pre_tokenizers
+
+    from torchtitan_b200.components.tokenizer import HuggingFaceTokenizer
+
+    vocab = {w: i for i, w in enumerate(["<unk>", "<s>", "</s>", "hello", "world", "user", "assistant", "hi"])}
+    tok = Tokenizer(models.WordLevel(vocab, unk_token="<unk>"))
+    tok.pre_tokenizer = pre_tokenizers.Whitespace()
+    tok.add_special_tokens(["<s>", "</s>"])
+    tok.save(str(tmp_path / "tokenizer.json"))
+    (tmp_path / "tokenizer_config.json").write_text(json.dumps({
+        "bos_token": "<s>", "eos_token": {"content": "</s>"},
+        "chat_template": "{{ bos_token }}{% for m in messages %}{{ m['role'] }} {{ m['content'] }} {% endfor %}"}))
+    t = HuggingFaceTokenizer(tokenizer_path=str(tmp_path))
+    assert (t.bos_id, t.eos_id) == (1, 2) and t.get_vocab_size() == 8
+    ids = t.encode("hello world", add_bos=True, add_eos=True)
+    assert ids == [1, 3, 4, 2] and t.decode(ids[1:3]) == "hello world"
+    chat = t.apply_chat_template([{"role": "user", "content": "hi"}, {"role": "assistant", "content": "hello"}])
+    assert chat == [1, 5, 7, 6, 3]

@@ -70,6 +70,7 @@ class HuggingFaceTokenizer(BaseTokenizer):
             raise FileNotFoundError(f"no tokenizer.json under '{tokenizer_path}'")
         self.tok = Tokenizer.from_file(path)
         self.bos_token = self.eos_token = None
+        self.chat_template: str | None = None
         cfg_path = os.path.join(tokenizer_path, "tokenizer_config.json")
         if os.path.exists(cfg_path):
             with open(cfg_path) as f:
@@ -79,6 +80,7 @@ class HuggingFaceTokenizer(BaseTokenizer):
                 return v.get("content") if isinstance(v, dict) else v
 
             self.bos_token, self.eos_token = _tok(tc.get("bos_token")), _tok(tc.get("eos_token"))
+            self.chat_template = tc.get("chat_template")
         vocab = self.tok.get_vocab(with_added_tokens=True)
         for cand in (self.bos_token, "<|begin_of_text|>", "<s>", "[BOS]"):
             if cand and cand in vocab:
@@ -102,3 +104,14 @@ class HuggingFaceTokenizer(BaseTokenizer):
 
     def get_vocab_size(self) -> int:
         return self.tok.get_vocab_size(with_added_tokens=True)
+
+    def apply_chat_template(self, messages: list[dict], add_generation_prompt: bool = False) -> list[int]:
+        """Render ``messages`` with the tokenizer's own chat template (jinja) and encode them."""
+        if not self.chat_template:
+            raise ValueError("this tokenizer has no chat_template")
+        import jinja2
+
+        text = jinja2.Template(self.chat_template).render(
+            messages=messages, add_generation_prompt=add_generation_prompt, bos_token=self.bos_token or "",
+            eos_token=self.eos_token or "")
+        return self.encode(text)
