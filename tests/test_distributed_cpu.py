@@ -592,19 +592,21 @@ def test_context_parallel_gradients_match_single_device(module, config, method):
         _run(_cp_grads, 2, d, module, config, method)
 
 
-def _pp_grads(rank, world, out_dir, schedule):
+def _pp_grads(rank, world, out_dir, schedule, module="llama3", config="llama3_debugmodel_cpu"):
     from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
 
     from torchtitan_b200.components.loss import cross_entropy_loss
     from torchtitan_b200.config.manager import ConfigManager
-    from torchtitan_b200.models.llama3 import model_registry
     from torchtitan_b200.trainer import Trainer
+    import importlib
 
+    model_registry = importlib.import_module(f"torchtitan_b200.models.{module}").model_registry
     t = Trainer(ConfigManager().parse_args([
-        "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "1",
+        "--module", module, "--config", config, "--training.steps", "1",
         "--training.seq-len", "64", "--parallelism.pipeline-parallel-degree", "2",
         "--parallelism.data-parallel-shard-degree", "1", "--parallelism.pipeline-parallel-microbatch-size", "1",
         "--training.local-batch-size", "4", "--parallelism.pipeline-parallel-schedule", schedule,
+        "--training.dtype", "float32", "--training.mixed-precision-param", "float32",
         "--debug.seed", "0", "--dump-folder", out_dir]))
     full = {}
     for part in t.model_parts:
@@ -614,10 +616,14 @@ def _pp_grads(rank, world, out_dir, schedule):
     merged = {}
     for d in gathered:
         merged.update(d)
-    ref = model_registry("debugmodel").model.build()
-    ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in merged.items()}, strict=False)
-    ref.rope.init_weights()
-    tokens = torch.randint(0, 2048, (4, 64), generator=torch.Generator().manual_seed(3))
+    ref = model_registry(t.config.model_spec.flavor).model.build()
+    res = ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in merged.items()},
+                              strict=False)
+    assert not res.unexpected_keys and all("tokens_per_expert" in k for k in res.missing_keys), res
+    if hasattr(ref, "rope"):
+        ref.rope.init_weights()
+    tokens = torch.randint(0, ref.model_args.vocab_size if hasattr(ref.model_args, "vocab_size") else 2048,
+                           (4, 64), generator=torch.Generator().manual_seed(3))
     labels = tokens.roll(-1, 1)
     loss_ref = cross_entropy_loss(ref(tokens), labels) / labels.numel()
     loss_ref.backward()
@@ -638,6 +644,15 @@ def _pp_grads(rank, world, out_dir, schedule):
 def test_pipeline_parallel_gradients_match_single_device(schedule):
     with tempfile.TemporaryDirectory() as d:
         _run(_pp_grads, 2, d, schedule)
+
+
+@pytest.mark.parametrize("module,config", [("kimi_linear", "kimi_linear_debugmodel_block_attn_res"),
+                                           ("attention_residual", "attention_residual_debugmodel")])
+def test_pipeline_parallel_attn_res_gradients_match_single_device(module, config):
+    """Attention-Residual models hand their whole residual state (completed blocks + the
+    partial block) from stage to stage, so the pipelined model is the unpipelined one."""
+    with tempfile.TemporaryDirectory() as d:
+        _run(_pp_grads, 2, d, "Interleaved1F1B", module, config)
 
 
 # ---------------------------------------------------------------- data parallel, gradient-exact

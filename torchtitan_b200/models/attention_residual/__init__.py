@@ -8,6 +8,7 @@ import copy
 
 from torchtitan_b200.components.loss import build_cross_entropy_loss
 from torchtitan_b200.models.llama3.parallelize import parallelize_llama
+from torchtitan_b200.parallel.pipeline import pipeline_llm
 from torchtitan_b200.protocols import ModelSpec
 
 from .model import AttnResModel, AttnResModelArgs
@@ -29,7 +30,7 @@ def model_registry(flavor: str) -> ModelSpec:
     if flavor not in attn_res_args:
         raise ValueError(f"unknown attention_residual flavor '{flavor}', available: {sorted(attn_res_args)}")
     return ModelSpec(name="attention_residual", flavor=flavor, model=copy.deepcopy(attn_res_args[flavor]),
-                     parallelize_fn=parallelize_llama, pipelining_fn=None, build_loss_fn=build_cross_entropy_loss)
+                     parallelize_fn=parallelize_llama, pipelining_fn=pipeline_llm, build_loss_fn=build_cross_entropy_loss)
 
 
 __all__ = ["AttnResModel", "AttnResModelArgs", "model_registry", "attn_res_args"]

@@ -72,6 +72,9 @@ class AttnResBlock(nn.Module):
 
 
 class AttnResModel(Decoder):
+    # pipeline stages: the last one also holds the final residual aggregation
+    pp_last_modules = ("final_res_query", "final_res_norm", "norm", "output")
+
     def __init__(self, a: AttnResModelArgs):
         super().__init__()
         self.model_args = a
@@ -91,18 +94,25 @@ class AttnResModel(Decoder):
             self.tok_embeddings.init_weights()
         for layer in self.layers.values():
             layer.init_weights()
-        self.final_res_query.weight.zero_()
-        self.final_res_norm.init_weights()
+        if self.final_res_query is not None:
+            self.final_res_query.weight.zero_()
+            self.final_res_norm.init_weights()
         if self.norm is not None:
             self.norm.init_weights()
         init_output(self, self.model_args.dim)
 
     def forward(self, tokens, attention_masks=None, positions=None):
-        h = self.tok_embeddings(tokens)
-        cos, sin = self._rope_tables(tokens.shape[1], positions)
-        state = ([], h)
+        from ..common.attn_res import pack_state, unpack_state
+
+        if self.tok_embeddings is not None:
+            state = ([], self.tok_embeddings(tokens))
+        else:  # a later pipeline stage: the residual state arrives packed as one tensor
+            state = unpack_state(tokens)
+        cos, sin = self._rope_tables(state[1].shape[1], positions)
         for layer in self.layers.values():
             state = layer(state, cos, sin, attention_masks)
+        if self.output is None:
+            return pack_state(state)
         blocks, partial = state
         h = block_attn_res(blocks, partial, self.final_res_query.weight, self.final_res_norm)
         return self.output(self.norm(h))

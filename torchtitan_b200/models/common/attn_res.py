@@ -25,3 +25,18 @@ def block_attn_res(blocks: list[torch.Tensor], partial: torch.Tensor, query: tor
     w = _local(query).reshape(-1).to(Kn.dtype)
     logits = torch.einsum("d,nbtd->nbt", w, Kn).float()
     return torch.einsum("nbt,nbtd->btd", torch.softmax(logits, 0).to(V.dtype), V)
+
+
+def pack_state(state) -> torch.Tensor:
+    """(completed blocks, partial block) -> one ``[n_blocks + 1, B, S, D]`` tensor, the form a
+    pipeline stage sends to the next one (its shape is fixed per stage boundary)."""
+    blocks, partial = state
+    return torch.stack(list(blocks) + [partial])
+
+
+def unpack_state(x: torch.Tensor):
+    """Inverse of ``pack_state``; a plain ``[B, S, D]`` hidden state starts with no blocks."""
+    if x.dim() == 3:
+        return [], x
+    parts = list(x.unbind(0))
+    return parts[:-1], parts[-1]

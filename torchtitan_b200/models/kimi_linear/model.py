@@ -325,7 +325,11 @@ class KimiDecoderLayer(nn.Module):
 class KimiLinearModel(BaseModel):
     # names used by the pipeline splitter
     pp_first_module = "embed_tokens"
-    pp_last_modules = ("norm", "lm_head")
+
+    @property
+    def pp_last_modules(self) -> tuple[str, ...]:
+        extra = ("final_res_proj", "final_res_norm") if self.model_args.attn_res_blocks > 0 else ()
+        return ("norm", "lm_head", *extra)
 
     def __init__(self, a: KimiLinearModelArgs):
         super().__init__()
@@ -360,9 +364,14 @@ class KimiLinearModel(BaseModel):
         else:
             h = self.embed_tokens(tokens) if self.embed_tokens is not None else tokens
         if self.model_args.attn_res_blocks > 0:
-            state = ([], h)
+            from ..common.attn_res import pack_state, unpack_state
+
+            # a pipeline stage after the first receives the residual state packed as one tensor
+            state = unpack_state(h) if self.embed_tokens is None and inputs_embeds is None else ([], h)
             for layer in self.layers.values():
                 state = layer(state)
+            if self.lm_head is None:  # not the last pipeline stage: hand the whole state on
+                return pack_state(state)
             blocks, partial = state
             if getattr(self, "final_res_proj", None) is not None:
                 h = block_attn_res(blocks, partial, self.final_res_proj.weight, self.final_res_norm)
