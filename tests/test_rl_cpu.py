@@ -49,3 +49,26 @@ def test_grpo_improves_reward(tmp_path):
     assert eng.step == 50
     assert sum(hist[-5:]) / 5 > sum(hist[:5]) / 5 + 0.08, hist
     eng.close()
+
+
+def test_generator_and_trainer_logprobs_are_bitwise_equal(tmp_path):
+    """Rollout log-probabilities (generator copy) and the trainer's own, on the same weights,
+    are bitwise equal, so the importance ratio is exactly 1 on the first update epoch
+    (the reference checks this parity between its inference engine and trainer)."""
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.forge import ForgeEngine
+    from torchtitan_b200.rl.grpo import token_logprobs
+
+    cfg = ConfigManager().parse_args([
+        "--module", "llama3", "--config", "llama3_debugmodel", "--training.seq-len", "64",
+        "--training.local-batch-size", "2", "--training.dtype", "float32", "--training.mixed-precision-param",
+        "float32", "--activation-checkpoint.mode", "none", "--dump-folder", str(tmp_path)])
+    eng = ForgeEngine(cfg)
+    tr = GRPOTrainer(eng, lambda p, c: torch.zeros(c.shape[0]), GRPOConfig(group_size=2, max_new_tokens=4))
+    tr.sync_weights()
+    seq = torch.randint(0, 2048, (4, 12), generator=torch.Generator().manual_seed(0))
+    with torch.no_grad():
+        a = token_logprobs(tr.generator, seq, 8)
+        b = token_logprobs(eng.model_parts[0], seq, 8)
+    assert torch.equal(a, b)
+    eng.close()

@@ -19,15 +19,21 @@ import torch
 from torchtitan_b200.config import TORCH_DTYPE_MAP
 from torchtitan_b200.trainer import Trainer
 
+from torchtitan_b200.utils.logging import logger
+
 from .autoencoder import build_autoencoder
 from .encoders import FluxEncoderConfig, FluxTextEncoders
 from .sampling import generate_latents, latent_position_ids, pack_latents, text_position_ids
+from .validate import FluxValidationConfig, validate_flux
 
 
 class FluxTrainer(Trainer):
     @dataclass(kw_only=True, slots=True)
     class Config(Trainer.Config):
         encoder: FluxEncoderConfig = field(default_factory=FluxEncoderConfig)
+        flux_validation: FluxValidationConfig = field(default_factory=FluxValidationConfig)
+        flux_validation_freq: int = 0
+        """Validate (fixed-noise-level flow loss, optional samples) every this many steps; 0 = never."""
 
     def __init__(self, config: Config, **kw: Any):
         super().__init__(config, **kw)
@@ -40,7 +46,6 @@ class FluxTrainer(Trainer):
 
     def batch_generator(self, data):
         # count transformer tokens (image patches + text), not pixels
-        a = self.model_args
         for inp, labels in super().batch_generator(data):
             lat = labels.shape[-1] // 8
             n = labels.shape[0] * ((lat // 2) ** 2 + self.config.encoder.max_t5_encoding_len)
@@ -99,7 +104,16 @@ class FluxTrainer(Trainer):
 
     def train_step(self, data_iterator):
         self._microbatch = 0
-        return super().train_step(data_iterator)
+        loss = super().train_step(data_iterator)
+        freq = self.config.flux_validation_freq
+        if freq > 0 and self.step % freq == 0:
+            if self.parallel_dims.cp_enabled:
+                logger.warning("flux validation runs full sequences: skipped under context parallelism")
+            else:
+                self.last_validation = validate_flux(self, self.config.flux_validation)
+                logger.info("validation step %d: %s", self.step,
+                            ", ".join(f"{k.split('/')[-1]} {v:.4f}" for k, v in self.last_validation.items()))
+        return loss
 
     @torch.no_grad()
     def generate(self, prompts: list[str], size: int = 256, steps: int = 50, cfg_scale: float | None = 5.0,
