@@ -28,3 +28,39 @@ def test_kda_gram_kernels_match_loop(strict, N, C, K, monkeypatch):
         outs[flag] = (y.detach(), aa.grad, bb.grad, gg.grad)
     for x, y in zip(outs["0"], outs["1"]):
         torch.testing.assert_close(y, x, rtol=2e-4, atol=2e-4)
+
+
+@pytest.mark.parametrize("BH,NT,C,K,V", [(3, 5, 64, 128, 128), (2, 3, 64, 64, 96)])
+def test_kda_chunk_scan_kernel_matches_loop(BH, NT, C, K, V):
+    """The inter-chunk recurrence kernels (forward and backward) against the batched-matmul loop."""
+    from torchtitan_b200.ops import kda
+
+    torch.manual_seed(1)
+    u = torch.randn(BH, NT, C, V, device="cuda")
+    w, qg, kd = (0.1 * torch.randn(BH, NT, C, K, device="cuda") for _ in range(3))
+    A = 0.1 * torch.randn(BH, NT, C, C, device="cuda").tril()
+    dec = torch.rand(BH, NT, K, device="cuda") * 0.5 + 0.5
+    do = torch.randn(BH, NT, C, V, device="cuda")
+    res = []
+    for fn in (kda._scan_ref, kda._ChunkScan.apply):
+        xs = [t.clone().requires_grad_() for t in (u, w, qg, A, kd, dec)]
+        o, S = fn(*xs)
+        (o * do).sum().backward()
+        res.append([o.detach(), S.detach()] + [x.grad for x in xs])
+    for got, want in zip(res[1], res[0]):
+        torch.testing.assert_close(got, want, rtol=1e-3, atol=1e-3)
+
+
+def test_chunk_kda_with_scan_kernel_matches_recurrence(monkeypatch):
+    from torchtitan_b200.ops import kda
+
+    torch.manual_seed(2)
+    B, T, H, K, V = 1, 200, 2, 64, 64
+    q, k = (torch.randn(B, T, H, K, device="cuda") for _ in range(2))
+    v = torch.randn(B, T, H, V, device="cuda")
+    g = -torch.rand(B, T, H, K, device="cuda") * 0.2
+    beta = torch.rand(B, T, H, device="cuda")
+    monkeypatch.setenv("TTB_KDA_KERNEL", "1")
+    o, _ = kda.chunk_kda(q, k, v, g, beta)
+    ref, _ = kda.naive_recurrent_kda(q, k, v, g, beta)
+    torch.testing.assert_close(o.float(), ref, rtol=2e-3, atol=2e-3)

@@ -385,6 +385,44 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                       (int)a.size(2), strict, stream());
     return std::vector<Tensor>{da, db, dG};
   });
+  // chunked-KDA inter-chunk recurrence: u [BH,NT,C,V], w/qg/kdec [BH,NT,C,K], Aqk [BH,NT,C,C], dec [BH,NT,K]
+  m.def("kda_scan_fwd", [](Tensor u, Tensor w, Tensor qg, Tensor Aqk, Tensor kdec, Tensor dec, int64_t vs) {
+    for (const Tensor* t : {&u, &w, &qg, &Aqk, &kdec, &dec})
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous(), "kda_scan: contiguous fp32");
+    TORCH_CHECK(u.dim() == 4 && w.dim() == 4 && Aqk.dim() == 4 && dec.dim() == 3, "kda_scan: ranks");
+    const int64_t BH = u.size(0), NT = u.size(1), C = u.size(2), V = u.size(3), K = w.size(3);
+    TORCH_CHECK(w.sizes() == qg.sizes() && w.sizes() == kdec.sizes() && w.size(0) == BH && w.size(1) == NT &&
+                    w.size(2) == C && Aqk.size(2) == C && Aqk.size(3) == C && dec.size(2) == K,
+                "kda_scan: shapes");
+    c10::cuda::CUDAGuard g(u.device());
+    auto o = torch::empty_like(u);
+    auto states = torch::empty({BH, NT, K, V}, u.options());
+    auto fin = torch::empty({BH, K, V}, u.options());
+    ttb::kda_scan_fwd(u.data_ptr<float>(), w.data_ptr<float>(), qg.data_ptr<float>(), Aqk.data_ptr<float>(),
+                      kdec.data_ptr<float>(), dec.data_ptr<float>(), o.data_ptr<float>(), states.data_ptr<float>(),
+                      fin.data_ptr<float>(), BH, (int)NT, (int)C, (int)K, (int)V, (int)vs, stream());
+    return std::vector<Tensor>{o, states, fin};
+  });
+  m.def("kda_scan_bwd", [](Tensor dO, Tensor u, Tensor w, Tensor qg, Tensor Aqk, Tensor kdec, Tensor dec,
+                           Tensor states, int64_t vs) {
+    TORCH_CHECK(dO.is_cuda() && dO.scalar_type() == at::kFloat && dO.is_contiguous() && dO.sizes() == u.sizes(),
+                "kda_scan: dO");
+    const int64_t BH = u.size(0), NT = u.size(1), C = u.size(2), V = u.size(3), K = w.size(3);
+    TORCH_CHECK(V % vs == 0, "kda_scan: V must be a multiple of the slice width");
+    const int64_t ns = V / vs;
+    c10::cuda::CUDAGuard g(u.device());
+    auto du = torch::empty_like(u);
+    auto dqg = torch::empty({ns, BH, NT, C, K}, u.options()), dw = torch::empty_like(dqg),
+         dkd = torch::empty_like(dqg);
+    auto dA = torch::empty({ns, BH, NT, C, C}, u.options());
+    auto dd = torch::empty({ns, BH, NT, K}, u.options());
+    ttb::kda_scan_bwd(dO.data_ptr<float>(), u.data_ptr<float>(), w.data_ptr<float>(), qg.data_ptr<float>(),
+                      Aqk.data_ptr<float>(), kdec.data_ptr<float>(), dec.data_ptr<float>(), states.data_ptr<float>(),
+                      du.data_ptr<float>(), dqg.data_ptr<float>(), dw.data_ptr<float>(), dkd.data_ptr<float>(),
+                      dA.data_ptr<float>(), dd.data_ptr<float>(), BH, (int)NT, (int)C, (int)K, (int)V, (int)vs,
+                      stream());
+    return std::vector<Tensor>{du, dqg.sum(0), dw.sum(0), dkd.sum(0), dA.sum(0), dd.sum(0)};
+  });
   m.def("mxgemm_error_code", &ttb::mxgemm_error_code, py::arg("reset") = true);
   m.def("dp_error_info", []() {
     int v[4];

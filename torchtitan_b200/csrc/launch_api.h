@@ -92,6 +92,15 @@ void kda_gram_fwd(const float* a, const float* b, const float* G, float* out, in
 void kda_gram_bwd(const float* dout, const float* a, const float* b, const float* G, float* da, float* db,
                   float* dG, int64_t N, int C, int K, bool strict, cudaStream_t s);
 
+// kda_scan.cu: inter-chunk state recurrence of chunked KDA (forward and backward)
+void kda_scan_fwd(const float* u, const float* w, const float* qg, const float* Aqk, const float* kdec,
+                  const float* dec, float* o, float* states, float* final_S, int64_t BH, int NT, int C, int K, int V,
+                  int VS, cudaStream_t s);
+void kda_scan_bwd(const float* dO, const float* u, const float* w, const float* qg, const float* Aqk,
+                  const float* kdec, const float* dec, const float* states, float* du, float* p_dqg, float* p_dw,
+                  float* p_dkdec, float* p_dA, float* p_dd, int64_t BH, int NT, int C, int K, int V, int VS,
+                  cudaStream_t s);
+
 // ep_comm.cu: expert-parallel row movement over NVLink peer memory
 void ep_scatter_rows(const void* src, int64_t n, int d, const int32_t* dest_rank, const int64_t* dest_row,
                      void* const* peer_bases, int world, cudaStream_t s);

@@ -147,16 +147,69 @@ def chunk_kda(q, k, v, g, beta, scale: float | None = None, chunk_size: int = 64
     qg = qc * G.exp()
     Glast = G[:, :, -1:, :]  # [BH, NT, 1, K]
     kdec = (Glast - G).exp() * kc
-    S = q.new_zeros(B * H, K, V) if initial_state is None else initial_state.float().reshape(B * H, K, V)
+    decay = Glast[:, :, 0, :].exp()  # [BH, NT, K]
+    if initial_state is None:
+        o, S = chunk_scan(u, w, qg, Aqk, kdec, decay)
+    else:
+        o, S = _scan_ref(u, w, qg, Aqk, kdec, decay, initial_state.float().reshape(B * H, K, V))
+    o = o.view(B, H, NT, C, V).permute(0, 2, 3, 1, 4).reshape(B, Tp, H, V)[:, :T]
+    final = S.view(B, H, K, V) if output_final_state else None
+    return o.to(dtype), final
+
+
+def _scan_ref(u, w, qg, Aqk, kdec, decay, S=None):
+    """Inter-chunk recurrence as a loop of batched matmuls (any device, autograd through it):
+    v' = u - w S;  o = qg S + Aqk v';  S <- diag(decay) S + kdec^T v'."""
+    BH, NT, C, V = u.shape
+    K = w.shape[-1]
+    S = u.new_zeros(BH, K, V) if S is None else S
     outs = []
     for n in range(NT):
         vn = u[:, n] - w[:, n] @ S
         outs.append(qg[:, n] @ S + Aqk[:, n] @ vn)
-        S = Glast[:, n, 0, :, None].exp() * S + kdec[:, n].transpose(1, 2) @ vn
-    o = torch.stack(outs, 1)  # [BH, NT, C, V]
-    o = o.view(B, H, NT, C, V).permute(0, 2, 3, 1, 4).reshape(B, Tp, H, V)[:, :T]
-    final = S.view(B, H, K, V) if output_final_state else None
-    return o.to(dtype), final
+        S = decay[:, n, :, None] * S + kdec[:, n].transpose(1, 2) @ vn
+    return torch.stack(outs, 1), S
+
+
+def _scan_slice_width(V: int) -> int:
+    for vs in (32, 16, 8, 4, 2, 1):
+        if V % vs == 0:
+            return vs
+    return 1
+
+
+class _ChunkScan(torch.autograd.Function):
+    """The recurrence of ``_scan_ref`` from a zero state as one kernel launch per direction
+    (``csrc/kda_scan.cu``; grid = V slices x heads, chunk-start states kept for the backward)."""
+
+    @staticmethod
+    def forward(ctx, u, w, qg, Aqk, kdec, decay):
+        from ._ext import ext
+
+        args = [t.float().contiguous() for t in (u, w, qg, Aqk, kdec, decay)]
+        vs = _scan_slice_width(u.shape[-1])
+        o, states, fin = ext().kda_scan_fwd(*args, vs)
+        ctx.save_for_backward(*args, states)
+        ctx.vs = vs
+        ctx.set_materialize_grads(False)  # an unused final state brings no gradient (and no sync)
+        return o, fin
+
+    @staticmethod
+    def backward(ctx, do, dfin):
+        from ._ext import ext
+
+        *args, states = ctx.saved_tensors
+        if dfin is not None:
+            raise NotImplementedError("kda_scan kernel: gradient of the final state is not supported")
+        du, dqg, dw, dkd, dA, dd = ext().kda_scan_bwd(do.float().contiguous(), *args, states, ctx.vs)
+        return du, dw, dqg, dA, dkd, dd
+
+
+def chunk_scan(u, w, qg, Aqk, kdec, decay):
+    """-> (o [BH, NT, C, V], final state [BH, K, V]); kernel on CUDA when opted in."""
+    if _use_gram_kernel(u):
+        return _ChunkScan.apply(u, w, qg, Aqk, kdec, decay)
+    return _scan_ref(u, w, qg, Aqk, kdec, decay)
 
 
 def naive_recurrent_kda(q, k, v, g, beta, scale=None, use_qk_l2norm: bool = True):
