@@ -1,14 +1,9 @@
 """CUDA-graph capture of decoder blocks (``compile.enable``, backend ``cudagraph``):
-a captured Llama debug model gives the same loss and gradients as the uncaptured one.
-Opt-in (``TTB_CUDA_GRAPH_TESTS=1``) until it has run on a B200."""
-import os
-
+a captured Llama debug model gives the same loss and gradients as the uncaptured one."""
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TTB_CUDA_GRAPH_TESTS") != "1",
-                                 reason="opt-in until validated on a B200")]
+pytestmark = pytest.mark.gpu
 
 
 def test_graphed_blocks_match_eager():

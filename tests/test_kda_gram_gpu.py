@@ -1,13 +1,9 @@
-"""The decayed-Gram KDA kernels against the column-loop formulation (fp32).
-New kernels, not yet validated on a B200: run with TTB_KDA_KERNEL_TESTS=1."""
-import os
-
+"""The decayed-Gram KDA kernels against the column-loop formulation (fp32),
+and the inter-chunk recurrence kernels against the batched-matmul loop."""
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TTB_KDA_KERNEL_TESTS") != "1",
-                                 reason="KDA Gram kernels not yet validated on a B200; opt in explicitly")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("strict", [True, False])

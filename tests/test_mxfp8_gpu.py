@@ -1,14 +1,12 @@
 """MXFP8 quantizer and block-scaled tcgen05 GEMM against the CPU definition of
-the format (``ops/mx_gemm.py``).  The block-scaled GEMM is new and has not yet
-been validated on a B200; these tests run only when TTB_MXFP8_KERNEL_TESTS=1."""
+the format (``ops/mx_gemm.py``), and the MXFP8 linear on the kernel against the same
+quantized operands on the bf16 GEMM."""
 import os
 
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TTB_MXFP8_KERNEL_TESTS") != "1",
-                                 reason="block-scaled GEMM not yet validated on a B200; opt in explicitly")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("R,C", [(128, 128), (130, 200), (1000, 4096)])
@@ -38,3 +36,23 @@ def test_mx_gemm_matches_dequantized_product(M, N, K):
     assert ext().mxgemm_error_code(True) == 0
     ref = (mx_dequantize_ref(qa, sa).cuda() @ mx_dequantize_ref(qb, sb).cuda().t())
     torch.testing.assert_close(d.float(), ref, rtol=2e-2, atol=2e-2 * float(ref.abs().max()) / 50)
+
+
+def test_mxfp8_linear_kernel_path_matches_fake_quant(monkeypatch):
+    """Forward and both backward GEMMs of the MXFP8 linear on the block-scaled kernel against
+    the same quantized operands multiplied on the bf16 GEMM."""
+    from torchtitan_b200.components.quantization.mx import _MXLinearFn
+
+    torch.manual_seed(3)
+    x = torch.randn(256, 512, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(384, 512, device="cuda") * 0.05).bfloat16()
+    dy = torch.randn(256, 384, device="cuda", dtype=torch.bfloat16)
+    res = {}
+    for flag in ("0", "1"):
+        monkeypatch.setenv("TTB_MXFP8_KERNEL", flag)
+        xx, ww = x.clone().requires_grad_(), w.clone().requires_grad_()
+        y = _MXLinearFn.apply(xx, ww)
+        y.backward(dy)
+        res[flag] = (y.float(), xx.grad.float(), ww.grad.float())
+    for a, b in zip(res["1"], res["0"]):
+        torch.testing.assert_close(a, b, rtol=2e-2, atol=2e-2 * float(b.abs().max()) / 20)

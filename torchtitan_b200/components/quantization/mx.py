@@ -20,8 +20,9 @@ from .utils import swap_linears
 
 
 def _use_block_scaled_kernel(t: torch.Tensor) -> bool:
-    # the tcgen05 block-scaled GEMM is opt-in until it has been validated on a B200
-    return t.is_cuda and os.environ.get("TTB_MXFP8_KERNEL") == "1"
+    # the tcgen05 block-scaled GEMM (TTB_MXFP8_KERNEL=0 multiplies the same quantized values
+    # on the bf16 GEMM instead)
+    return t.is_cuda and os.environ.get("TTB_MXFP8_KERNEL", "1") != "0"
 
 
 class _MXLinearFn(torch.autograd.Function):

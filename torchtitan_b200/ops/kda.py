@@ -29,10 +29,18 @@ import torch.nn.functional as F
 
 
 def _use_gram_kernel(t: torch.Tensor) -> bool:
-    # csrc/kda_gram.cu is opt-in until validated on a B200
+    # csrc/kda_gram.cu and csrc/kda_scan.cu on CUDA (TTB_KDA_KERNEL=0 selects the PyTorch loops)
     import os
 
-    return t.is_cuda and os.environ.get("TTB_KDA_KERNEL") == "1"
+    return t.is_cuda and os.environ.get("TTB_KDA_KERNEL", "1") != "0"
+
+
+def _fits_shared_memory(C: int, K: int, V: int = 0) -> bool:
+    """The kernels keep per-chunk tiles in shared memory (227 KB per CTA)."""
+    gram = 4 * (3 * C * (K + 1) + C * (C + 1))
+    vs = _scan_slice_width(V) if V else 1
+    scan = 4 * (2 * K * (vs + 1) + 3 * C * (K + 1) + C * (C + 1) + 3 * C * (vs + 1) + K)
+    return max(gram, scan) <= 227 * 1024
 
 
 class _DecayedGram(torch.autograd.Function):
@@ -42,7 +50,8 @@ class _DecayedGram(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, a, b, G, strict):
-        if _use_gram_kernel(a):
+        ctx.kernel = _use_gram_kernel(a) and _fits_shared_memory(a.shape[1], a.shape[2])
+        if ctx.kernel:
             from ._ext import ext
 
             a, b, G = (t.float().contiguous() for t in (a, b, G))
@@ -64,7 +73,7 @@ class _DecayedGram(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout):
         a, b, G = ctx.saved_tensors
-        if _use_gram_kernel(a):
+        if ctx.kernel:
             from ._ext import ext
 
             da, db, dG = ext().kda_gram_bwd(dout.float().contiguous(), a, b, G, ctx.strict)
@@ -207,7 +216,7 @@ class _ChunkScan(torch.autograd.Function):
 
 def chunk_scan(u, w, qg, Aqk, kdec, decay):
     """-> (o [BH, NT, C, V], final state [BH, K, V]); kernel on CUDA when opted in."""
-    if _use_gram_kernel(u):
+    if _use_gram_kernel(u) and _fits_shared_memory(u.shape[2], w.shape[-1], u.shape[-1]):
         return _ChunkScan.apply(u, w, qg, Aqk, kdec, decay)
     return _scan_ref(u, w, qg, Aqk, kdec, decay)
 

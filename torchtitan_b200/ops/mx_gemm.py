@@ -30,6 +30,7 @@ def mx_quantize_ref(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     xp = torch.zeros(R, Cp, dtype=torch.float32)
     xp[:, :C] = x.float().cpu()
     codes, e8 = _mx_codes(xp)                      # e8: [R, Cp/32] uint8
+    e8[:, (C + 31) // 32:] = 127                   # groups wholly in the column padding: scale 2^0
     sf = torch.full((Rp * Cp // 32,), 127, dtype=torch.uint8)
     sf[sf_byte_index(R, Cp)[:R].reshape(-1)] = e8.reshape(-1)
     return codes.view(torch.uint8), sf
