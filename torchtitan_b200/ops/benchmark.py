@@ -178,6 +178,28 @@ def mem_small(ext, out):
     print(json.dumps(out[-1]), flush=True)
 
 
+def bench_mxfp8(ext, out):
+    """Block-scaled MXFP8 GEMM (codes + E8M0 scales already quantized) next to our bf16 GEMM
+    and cuBLAS bf16 on the same shape, plus the quantizer's bandwidth."""
+    from torchtitan_b200.ops.mx_gemm import mx_quantize
+
+    for name, M, N, K in [("sq8192", 8192, 8192, 8192), ("w13_fwd", 8192, 28672, 4096), ("qkv_fwd", 8192, 6144, 4096)]:
+        a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+        qa, sa = mx_quantize(a)
+        qb, sb = mx_quantize(b)
+        mx = time_fn(lambda: ext.gemm_mxfp8(qa, sa, qb, sb))
+        bf = time_fn(lambda: ext.gemm(a, b, False, False))
+        lib = time_fn(lambda: torch.matmul(a, b.t()))
+        q = time_fn(lambda: mx_quantize(a))
+        fl = 2.0 * M * N * K
+        out.append({"kernel": "gemm_mxfp8", "case": name, "M": M, "N": N, "K": K, "ms": mx, "tflops": fl / mx / 1e9,
+                    "bf16_tcgen05_tflops": fl / bf / 1e9, "cublas_bf16_tflops": fl / lib / 1e9,
+                    "quantize_ms": q, "quantize_gbs": (a.numel() * 2 + a.numel() + a.numel() // 32) / q / 1e6,
+                    "err": ext.mxgemm_error_code(True)})
+        print(json.dumps(out[-1]), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,mem")
@@ -190,6 +212,8 @@ def main():
     sel = set(a.only.split(","))
     if "gemm" in sel:
         bench_gemm(ext, out)
+    if "mxfp8" in sel:
+        bench_mxfp8(ext, out)
     if "attn" in sel:
         bench_attn(ext, out)
     if "attn_large" in sel:
