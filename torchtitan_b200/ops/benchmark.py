@@ -200,6 +200,34 @@ def bench_mxfp8(ext, out):
         print(json.dumps(out[-1]), flush=True)
 
 
+def bench_kda(ext, out):
+    """Chunked KDA forward+backward (Kimi-Linear 48B layer shape: T 8192, 32 heads, K = V = 128)
+    with the KDA kernels and with the PyTorch loops."""
+    import os
+
+    from torchtitan_b200.ops import kda
+
+    B, T, H, K, V = 1, 8192, 32, 128, 128
+    q, k = (torch.randn(B, T, H, K, device="cuda", requires_grad=True) for _ in range(2))
+    v = torch.randn(B, T, H, V, device="cuda", requires_grad=True)
+    g = (-torch.rand(B, T, H, K, device="cuda") * 0.1).requires_grad_()
+    beta = torch.rand(B, T, H, device="cuda", requires_grad=True)
+    do = torch.randn(B, T, H, V, device="cuda")
+
+    def step():
+        o, _ = kda.chunk_kda(q, k, v, g, beta)
+        o.backward(do)
+
+    res = {}
+    for flag in ("1", "0"):
+        os.environ["TTB_KDA_KERNEL"] = flag
+        res[flag] = time_fn(step, iters=3, warmup=1, flush=False)
+    os.environ.pop("TTB_KDA_KERNEL")
+    out.append({"kernel": "kda_chunk", "case": f"B{B}_T{T}_H{H}_K{K}_V{V}", "fwd_bwd_ms_kernels": res["1"],
+                "fwd_bwd_ms_torch": res["0"], "speedup": res["0"] / res["1"]})
+    print(json.dumps(out[-1]), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,mem")
@@ -214,6 +242,8 @@ def main():
         bench_gemm(ext, out)
     if "mxfp8" in sel:
         bench_mxfp8(ext, out)
+    if "kda" in sel:
+        bench_kda(ext, out)
     if "attn" in sel:
         bench_attn(ext, out)
     if "attn_large" in sel:
