@@ -5,8 +5,10 @@
         [--checkpoint <dcp dir>] [--tokenizer <hf tokenizer dir>] --prompt "..." \\
         [--max-new-tokens 32] [--temperature 0] [--top-k 0] [--seed 0]
 
-Decoding re-runs the model over the growing sequence (no KV cache); with
-``--temperature 0`` it is greedy.  Without ``--tokenizer`` the prompt is a
+Decoder models whose layers use the common grouped-query attention decode with a
+KV cache (the prompt once, then one token per step; the flash kernel's bottom-right
+causal alignment lets one new query attend to every cached key); other models re-run
+over the growing sequence.  With ``--temperature 0`` decoding is greedy.  Without ``--tokenizer`` the prompt is a
 space-separated list of token ids.
 """
 from __future__ import annotations
@@ -18,27 +20,63 @@ import torch
 
 
 @torch.no_grad()
+def _sample(logits, temperature, top_k, generator):
+    if temperature <= 0:
+        return logits.argmax(-1)
+    logits = logits / temperature
+    if top_k > 0:
+        kth = logits.topk(top_k, -1).values[:, -1:]
+        logits = logits.masked_fill(logits < kth, float("-inf"))
+    return torch.multinomial(torch.softmax(logits, -1), 1, generator=generator)[:, 0]
+
+
+def _cache_layers(model) -> list | None:
+    """The attention modules to cache, or None when the model cannot decode incrementally."""
+    from torchtitan_b200.models.common.attention import GQAttention
+
+    layers = getattr(model, "layers", None)
+    if layers is None or not hasattr(model, "rope") or getattr(model, "tok_embeddings", None) is None:
+        return None
+    atts = []
+    for blk in layers.values():
+        att = getattr(blk, "attention", None)
+        if type(att) is not GQAttention or att.cp_hook is not None or att.mask_type != "causal":
+            return None
+        atts.append(att)
+    return atts
+
+
 def generate(model, prompt: torch.Tensor, max_new_tokens: int, temperature: float = 0.0, top_k: int = 0,
-             generator: torch.Generator | None = None, eos_id: int | None = None) -> torch.Tensor:
+             generator: torch.Generator | None = None, eos_id: int | None = None,
+             use_cache: bool = True) -> torch.Tensor:
     """prompt: [B, S] token ids -> [B, S + n] (stops early when every row emitted ``eos_id``)."""
     seq = prompt
     done = torch.zeros(prompt.shape[0], dtype=torch.bool, device=prompt.device)
-    for _ in range(max_new_tokens):
-        logits = model(seq)[:, -1].float()
-        if temperature <= 0:
-            nxt = logits.argmax(-1)
-        else:
-            logits = logits / temperature
-            if top_k > 0:
-                kth = logits.topk(top_k, -1).values[:, -1:]
-                logits = logits.masked_fill(logits < kth, float("-inf"))
-            nxt = torch.multinomial(torch.softmax(logits, -1), 1, generator=generator)[:, 0]
-        if eos_id is not None:
-            nxt = torch.where(done, torch.full_like(nxt, eos_id), nxt)
-            done |= nxt == eos_id
-        seq = torch.cat([seq, nxt[:, None]], 1)
-        if eos_id is not None and bool(done.all()):
-            break
+    atts = _cache_layers(model) if use_cache else None
+    if atts is not None:
+        for a in atts:
+            a.kv_cache = {}
+    try:
+        pos = 0
+        for _ in range(max_new_tokens):
+            if atts is None:
+                logits = model(seq)[:, -1].float()
+            else:
+                step = seq[:, pos:]
+                positions = torch.arange(pos, seq.shape[1], device=seq.device)[None]
+                logits = model(step, positions=positions)[:, -1].float()
+                pos = seq.shape[1]
+            nxt = _sample(logits, temperature, top_k, generator)
+            if eos_id is not None:
+                nxt = torch.where(done, torch.full_like(nxt, eos_id), nxt)
+                done |= nxt == eos_id
+            seq = torch.cat([seq, nxt[:, None]], 1)
+            if eos_id is not None and bool(done.all()):
+                break
+    finally:
+        if atts is not None:
+            for a in atts:
+                a.kv_cache = None
     return seq
 
 

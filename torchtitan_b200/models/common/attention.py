@@ -37,6 +37,7 @@ class GQAttention(nn.Module):
         self.wo = Linear(n_heads * self.head_dim, dim)
         self.mask_type = mask_type
         self.cp_hook = None  # set by context parallelism
+        self.kv_cache: dict | None = None  # set by generation (keys/values of earlier positions)
         if qk_norm:
             from .layers import RMSNorm
 
@@ -82,6 +83,11 @@ class GQAttention(nn.Module):
             k = self.k_norm(k)
         q = ops.rope(q, cos, sin)
         k = ops.rope(k, cos, sin)
+        if self.kv_cache is not None:  # incremental decoding: attend to every cached position too
+            if self.kv_cache:
+                k = torch.cat([self.kv_cache["k"], k], 1)
+                v = torch.cat([self.kv_cache["v"], v], 1)
+            self.kv_cache["k"], self.kv_cache["v"] = k, v
         if self.cp_hook is not None:
             o = self.cp_hook(self.inner_attention, q, k, v, attention_masks)
         else:
