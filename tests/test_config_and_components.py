@@ -614,3 +614,25 @@ def test_huggingface_tokenizer_files(tmp_path):
     assert ids == [1, 3, 4, 2] and t.decode(ids[1:3]) == "hello world"
     chat = t.apply_chat_template([{"role": "user", "content": "hi"}, {"role": "assistant", "content": "hello"}])
     assert chat == [1, 5, 7, 6, 3]
+
+
+def test_attnres_stage_cache_sends_only_missing_blocks():
+    """Round-robin stages of an AttnRes model: stage s receives only the blocks completed after
+    its rank's previous stage (s - pp), plus the partial block."""
+    import torch.nn as nn
+
+    from torchtitan_b200.models.common.attn_res import _held, completed_blocks, setup_stage_cache, stage_exit
+
+    assert [completed_blocks(n, 2) for n in range(6)] == [0, 1, 1, 2, 2, 3]
+    fqns = [["tok_embeddings", "layers.0"], ["layers.1", "layers.2"], ["layers.3", "layers.4"],
+            ["layers.5", "norm", "output"]]
+    parts = [nn.Module(), nn.Module()]
+    setup_stage_cache(parts, [0, 2], fqns, pp=2, n_microbatches=2, layers_per_block=2)
+    cfg = parts[0]._attnres_pp
+    assert cfg["counts"] == [1, 2, 3, 3]
+    assert [_held(cfg, s) for s in range(4)] == [0, 0, 1, 2]
+    # stage 2 (holding 1 block from stage 0) hands stage 3 (holding 2) one block + the partial
+    parts[1]._attnres_pp["mb"] = 0
+    blocks = [torch.randn(1, 4, 8) for _ in range(3)]
+    out = stage_exit(parts[1], (blocks, torch.randn(1, 4, 8)))
+    assert out.shape[0] == 2 and torch.equal(out[0], blocks[2])

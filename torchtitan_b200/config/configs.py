@@ -45,6 +45,9 @@ class ParallelismConfig:
     pipeline_parallel_layers_per_stage: int | None = None
     pipeline_parallel_schedule: str = "1F1B"
     pipeline_parallel_schedule_csv: str | None = ""
+    pipeline_parallel_attnres_cache: bool = True
+    """Attention-Residual models under round-robin stage placement: send each stage only the
+    residual blocks its rank does not hold from its previous stage."""
     pipeline_parallel_microbatch_size: int = 1
     context_parallel_degree: int = 1
     context_parallel_load_balancer: str | None = "headtail"

@@ -75,6 +75,11 @@ class AttnResModel(Decoder):
     # pipeline stages: the last one also holds the final residual aggregation
     pp_last_modules = ("final_res_query", "final_res_norm", "norm", "output")
 
+    @property
+    def attn_res_layers_per_block(self) -> int:
+        a = self.model_args
+        return max(1, a.n_layers // a.attn_res_blocks)
+
     def __init__(self, a: AttnResModelArgs):
         super().__init__()
         self.model_args = a
@@ -102,17 +107,17 @@ class AttnResModel(Decoder):
         init_output(self, self.model_args.dim)
 
     def forward(self, tokens, attention_masks=None, positions=None):
-        from ..common.attn_res import pack_state, unpack_state
+        from ..common.attn_res import stage_enter, stage_exit
 
         if self.tok_embeddings is not None:
-            state = ([], self.tok_embeddings(tokens))
+            state = stage_enter(self, state=([], self.tok_embeddings(tokens)))
         else:  # a later pipeline stage: the residual state arrives packed as one tensor
-            state = unpack_state(tokens)
+            state = stage_enter(self, tokens)
         cos, sin = self._rope_tables(state[1].shape[1], positions)
         for layer in self.layers.values():
             state = layer(state, cos, sin, attention_masks)
         if self.output is None:
-            return pack_state(state)
+            return stage_exit(self, state)
         blocks, partial = state
         h = block_attn_res(blocks, partial, self.final_res_query.weight, self.final_res_norm)
         return self.output(self.norm(h))

@@ -327,6 +327,11 @@ class KimiLinearModel(BaseModel):
     pp_first_module = "embed_tokens"
 
     @property
+    def attn_res_layers_per_block(self) -> int | None:
+        a = self.model_args
+        return max(1, a.num_hidden_layers // a.attn_res_blocks) if a.attn_res_blocks > 0 else None
+
+    @property
     def pp_last_modules(self) -> tuple[str, ...]:
         extra = ("final_res_proj", "final_res_norm") if self.model_args.attn_res_blocks > 0 else ()
         return ("norm", "lm_head", *extra)
@@ -364,14 +369,15 @@ class KimiLinearModel(BaseModel):
         else:
             h = self.embed_tokens(tokens) if self.embed_tokens is not None else tokens
         if self.model_args.attn_res_blocks > 0:
-            from ..common.attn_res import pack_state, unpack_state
+            from ..common.attn_res import stage_enter, stage_exit
 
             # a pipeline stage after the first receives the residual state packed as one tensor
-            state = unpack_state(h) if self.embed_tokens is None and inputs_embeds is None else ([], h)
+            first = self.embed_tokens is not None or inputs_embeds is not None
+            state = stage_enter(self, state=([], h)) if first else stage_enter(self, h)
             for layer in self.layers.values():
                 state = layer(state)
-            if self.lm_head is None:  # not the last pipeline stage: hand the whole state on
-                return pack_state(state)
+            if self.lm_head is None:  # not the last pipeline stage: hand the state on
+                return stage_exit(self, state)
             blocks, partial = state
             if getattr(self, "final_res_proj", None) is not None:
                 h = block_attn_res(blocks, partial, self.final_res_proj.weight, self.final_res_norm)

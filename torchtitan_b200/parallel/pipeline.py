@@ -128,6 +128,12 @@ def pipeline_llm(model: nn.Module, *, parallel_dims: Any, training: Any, paralle
     n_mb = training.local_batch_size // parallelism.pipeline_parallel_microbatch_size
     if n_mb < 1:
         raise ValueError("local_batch_size must be >= pipeline_parallel_microbatch_size")
+    lpb = getattr(model, "attn_res_layers_per_block", None)
+    if lpb and style == "loop" and parallelism.pipeline_parallel_attnres_cache:
+        from torchtitan_b200.models.common.attn_res import setup_stage_cache
+
+        sids = list(stage_ids_this_rank(pp_rank, parallel_dims.pp, n_stages, style))
+        setup_stage_cache(parts, sids, fqns, parallel_dims.pp, n_mb, lpb)
     if single:
         sched = sched_cls(stages[0], n_microbatches=n_mb, loss_fn=loss_fn, scale_grads=False)
     else:
