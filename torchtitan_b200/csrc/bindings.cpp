@@ -423,6 +423,25 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                       stream());
     return std::vector<Tensor>{du, dqg.sum(0), dw.sum(0), dkd.sum(0), dA.sum(0), dd.sum(0)};
   });
+  m.def("router_topk", [](Tensor logits, c10::optional<Tensor> bias, int64_t top_k, bool sigmoid, int64_t n_groups,
+                          int64_t n_limited) {
+    TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kFloat && logits.is_contiguous() && logits.dim() == 2,
+                "router_topk: logits contiguous fp32 [T, E]");
+    const int64_t T = logits.size(0), E = logits.size(1);
+    const float* b = nullptr;
+    Tensor bc;
+    if (bias.has_value()) {
+      bc = bias->to(at::kFloat).contiguous();
+      TORCH_CHECK(bc.is_cuda() && bc.numel() == E, "router_topk: bias [E]");
+      b = bc.data_ptr<float>();
+    }
+    c10::cuda::CUDAGuard g(logits.device());
+    auto idx = torch::empty({T, top_k}, logits.options().dtype(at::kLong));
+    auto counts = torch::empty({E}, logits.options().dtype(at::kInt));
+    ttb::router_topk(logits.data_ptr<float>(), b, T, (int)E, (int)top_k, sigmoid, (int)n_groups, (int)n_limited,
+                     idx.data_ptr<int64_t>(), counts.data_ptr<int32_t>(), stream());
+    return std::vector<Tensor>{idx, counts};
+  });
   m.def("mxgemm_error_code", &ttb::mxgemm_error_code, py::arg("reset") = true);
   m.def("dp_error_info", []() {
     int v[4];

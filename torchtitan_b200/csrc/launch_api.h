@@ -101,6 +101,10 @@ void kda_scan_bwd(const float* dO, const float* u, const float* w, const float* 
                   float* p_dkdec, float* p_dA, float* p_dd, int64_t BH, int NT, int C, int K, int V, int VS,
                   cudaStream_t s);
 
+// router_topk.cu: MoE routing selection (scores, bias, group limit, top-k, counts)
+void router_topk(const float* logits, const float* bias, int64_t T, int E, int top_k, bool sigmoid, int n_groups,
+                 int n_limited, int64_t* idx, int32_t* counts, cudaStream_t s);
+
 // ep_comm.cu: expert-parallel row movement over NVLink peer memory
 void ep_scatter_rows(const void* src, int64_t n, int d, const int32_t* dest_rank, const int64_t* dest_row,
                      void* const* peer_bases, int world, cudaStream_t s);

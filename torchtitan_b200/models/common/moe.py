@@ -43,6 +43,13 @@ class _AuxLossInjector(torch.autograd.Function):
         return g, torch.ones_like(aux)
 
 
+def _router_kernel_enabled() -> bool:
+    # csrc/router_topk.cu is opt-in until it has run on a B200
+    import os
+
+    return os.environ.get("TTB_ROUTER_KERNEL") == "1"
+
+
 class TokenChoiceTopKRouter(nn.Module):
     def __init__(self, dim: int, num_experts: int, top_k: int, score_func: str = "sigmoid",
                  route_norm: bool = False, route_scale: float = 1.0, num_expert_groups: int | None = None,
@@ -68,6 +75,17 @@ class TokenChoiceTopKRouter(nn.Module):
     def forward(self, x: torch.Tensor, expert_bias: torch.Tensor | None = None):
         logits = self.gate(x).float()
         scores = torch.sigmoid(logits) if self.score_func == "sigmoid" else F.softmax(logits, dim=-1)
+        if logits.is_cuda and not self.force_load_balance and _router_kernel_enabled():
+            # selection (bias, group limit, top-k, counts) in one kernel; weights stay in autograd
+            from torchtitan_b200.ops._ext import ext
+
+            G = self.num_expert_groups or 1
+            idx, counts = ext().router_topk(logits.detach().contiguous(), expert_bias, self.top_k,
+                                            self.score_func == "sigmoid", G, self.num_limited_groups or 1)
+            top = scores.gather(1, idx)
+            if self.route_norm:
+                top = top / (top.sum(-1, keepdim=True) + 1e-20)
+            return top * self.route_scale, idx, counts.long(), scores
         choice = scores if expert_bias is None else scores + expert_bias.float()
         if self.num_expert_groups is not None and self.num_expert_groups > 1:
             choice = self._group_limit(choice)
