@@ -442,6 +442,41 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                      idx.data_ptr<int64_t>(), counts.data_ptr<int32_t>(), stream());
     return std::vector<Tensor>{idx, counts};
   });
+  // block attention residuals: blocks = completed blocks + partial, each contiguous bf16 [T, D]
+  m.def("attn_res_fwd", [](std::vector<Tensor> blocks, Tensor u, double eps) {
+    TORCH_CHECK(!blocks.empty() && u.is_cuda() && u.scalar_type() == at::kFloat && u.is_contiguous(), "attn_res: u");
+    const int64_t D = u.numel(), T = blocks[0].numel() / D;
+    std::vector<const void*> ptrs;
+    for (auto& b : blocks) {
+      TORCH_CHECK(b.is_cuda() && b.scalar_type() == at::kBFloat16 && b.is_contiguous() && b.numel() == T * D,
+                  "attn_res: blocks contiguous bf16 of one shape");
+      ptrs.push_back(b.data_ptr());
+    }
+    c10::cuda::CUDAGuard g(u.device());
+    auto out = torch::empty_like(blocks[0]);
+    ttb::attn_res_fwd(ptrs.data(), (int)ptrs.size(), u.data_ptr<float>(), out.data_ptr(), T, (int)D, (float)eps,
+                      stream());
+    return out;
+  });
+  m.def("attn_res_bwd", [](std::vector<Tensor> blocks, Tensor u, Tensor dout, double eps) {
+    const int64_t D = u.numel(), T = blocks[0].numel() / D;
+    TORCH_CHECK(dout.is_cuda() && dout.scalar_type() == at::kBFloat16 && dout.is_contiguous() &&
+                    dout.numel() == T * D, "attn_res: dout");
+    std::vector<const void*> ptrs;
+    std::vector<void*> dptrs;
+    std::vector<Tensor> grads;
+    for (auto& b : blocks) {
+      ptrs.push_back(b.data_ptr());
+      grads.push_back(torch::empty_like(b));
+      dptrs.push_back(grads.back().data_ptr());
+    }
+    c10::cuda::CUDAGuard g(u.device());
+    auto du = torch::empty_like(u);
+    ttb::attn_res_bwd(ptrs.data(), dptrs.data(), (int)ptrs.size(), u.data_ptr<float>(), dout.data_ptr(),
+                      du.data_ptr<float>(), T, (int)D, (float)eps, stream());
+    grads.push_back(du);
+    return grads;
+  });
   m.def("mxgemm_error_code", &ttb::mxgemm_error_code, py::arg("reset") = true);
   m.def("dp_error_info", []() {
     int v[4];

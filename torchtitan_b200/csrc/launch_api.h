@@ -101,6 +101,12 @@ void kda_scan_bwd(const float* dO, const float* u, const float* w, const float* 
                   float* p_dkdec, float* p_dA, float* p_dd, int64_t BH, int NT, int C, int K, int V, int VS,
                   cudaStream_t s);
 
+// attn_res.cu: block attention-residual mixing (forward and backward), blocks read in place
+void attn_res_fwd(const void* const* blocks, int nb, const float* u, void* out, int64_t T, int D, float eps,
+                  cudaStream_t s);
+void attn_res_bwd(const void* const* blocks, void* const* dblocks, int nb, const float* u, const void* dout, float* du,
+                  int64_t T, int D, float eps, cudaStream_t s);
+
 // router_topk.cu: MoE routing selection (scores, bias, group limit, top-k, counts)
 void router_topk(const float* logits, const float* bias, int64_t T, int E, int top_k, bool sigmoid, int n_groups,
                  int n_limited, int64_t* idx, int32_t* counts, cudaStream_t s);

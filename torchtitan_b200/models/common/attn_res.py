@@ -18,8 +18,45 @@ import torch
 from .layers import RMSNorm, _local
 
 
+class _AttnResMix(torch.autograd.Function):
+    """``block_attn_res`` as one kernel per direction (``csrc/attn_res.cu``): the blocks are read
+    in place, the norm and pseudo-query enter as ``u = g * w``."""
+
+    @staticmethod
+    def forward(ctx, w, g, eps, *vs):
+        from torchtitan_b200.ops._ext import ext
+
+        vs = [v.contiguous() for v in vs]
+        u = (g.float() * w.float().reshape(-1)).contiguous()
+        ctx.save_for_backward(w, g, u, *vs)
+        ctx.eps = eps
+        return ext().attn_res_fwd(vs, u, eps)
+
+    @staticmethod
+    def backward(ctx, dout):
+        from torchtitan_b200.ops._ext import ext
+
+        w, g, u, *vs = ctx.saved_tensors
+        *dvs, du = ext().attn_res_bwd(vs, u, dout.contiguous(), ctx.eps)
+        dw = (du * g.float()).reshape(w.shape).to(w.dtype)
+        dg = (du * w.float().reshape(-1)).to(g.dtype)
+        return (dw, dg, None, *dvs)
+
+
+def _attn_res_kernel_ok(vs: list[torch.Tensor], query: torch.Tensor, norm) -> bool:
+    import os
+
+    if os.environ.get("TTB_ATTNRES_KERNEL") != "1":  # opt-in until it has run on a B200
+        return False
+    w = norm.weight
+    return (vs[0].is_cuda and all(v.dtype == torch.bfloat16 and v.shape == vs[0].shape for v in vs)
+            and len(vs) <= 17 and type(w).__name__ != "DTensor" and type(query).__name__ != "DTensor")
+
+
 def block_attn_res(blocks: list[torch.Tensor], partial: torch.Tensor, query: torch.Tensor, norm: RMSNorm):
     """softmax_n(<w, RMSNorm(V_n)>) weighted sum of V = blocks + [partial] (all [B,T,D])."""
+    if _attn_res_kernel_ok(blocks + [partial], query, norm):
+        return _AttnResMix.apply(query, norm.weight, norm.eps, *blocks, partial)
     V = torch.stack(blocks + [partial], 0)
     Kn = norm(V)
     w = _local(query).reshape(-1).to(Kn.dtype)
