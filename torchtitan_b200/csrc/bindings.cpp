@@ -477,6 +477,43 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     grads.push_back(du);
     return grads;
   });
+  m.def("kda_short_conv_fwd", [](Tensor x, Tensor w) {  // x [B, T, C] bf16, w [C, W] fp32
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 3, "short conv: x");
+    TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.size(0) == x.size(2), "short conv: w");
+    c10::cuda::CUDAGuard g(x.device());
+    auto y = torch::empty_like(x);
+    ttb::kda_short_conv_fwd(x.data_ptr(), w.data_ptr<float>(), y.data_ptr(), x.size(0), x.size(1), (int)x.size(2),
+                            (int)w.size(1), stream());
+    return y;
+  });
+  m.def("kda_short_conv_bwd", [](Tensor x, Tensor w, Tensor dy) {
+    TORCH_CHECK(dy.sizes() == x.sizes() && dy.is_contiguous() && dy.scalar_type() == at::kBFloat16, "short conv: dy");
+    c10::cuda::CUDAGuard g(x.device());
+    auto dx = torch::empty_like(x);
+    auto dw = torch::empty_like(w);
+    ttb::kda_short_conv_bwd(x.data_ptr(), w.data_ptr<float>(), dy.data_ptr(), dx.data_ptr(), dw.data_ptr<float>(),
+                            x.size(0), x.size(1), (int)x.size(2), (int)w.size(1), stream());
+    return std::vector<Tensor>{dx, dw};
+  });
+  m.def("kda_gated_norm_fwd", [](Tensor x, Tensor z, Tensor gw, double eps) {  // rows of width D = gw.numel()
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && z.sizes() == x.sizes() &&
+                    z.scalar_type() == at::kBFloat16 && z.is_contiguous(), "gated norm: x, z");
+    TORCH_CHECK(gw.scalar_type() == at::kFloat && gw.is_contiguous() && x.size(-1) == gw.numel(), "gated norm: g");
+    c10::cuda::CUDAGuard g(x.device());
+    auto y = torch::empty_like(x);
+    ttb::kda_gated_norm_fwd(x.data_ptr(), z.data_ptr(), gw.data_ptr<float>(), y.data_ptr(), x.numel() / gw.numel(),
+                            (int)gw.numel(), (float)eps, stream());
+    return y;
+  });
+  m.def("kda_gated_norm_bwd", [](Tensor x, Tensor z, Tensor gw, Tensor dy, double eps) {
+    TORCH_CHECK(dy.sizes() == x.sizes() && dy.is_contiguous() && dy.scalar_type() == at::kBFloat16, "gated norm: dy");
+    c10::cuda::CUDAGuard g(x.device());
+    auto dx = torch::empty_like(x), dz = torch::empty_like(z), dg = torch::empty_like(gw);
+    ttb::kda_gated_norm_bwd(x.data_ptr(), z.data_ptr(), gw.data_ptr<float>(), dy.data_ptr(), dx.data_ptr(),
+                            dz.data_ptr(), dg.data_ptr<float>(), x.numel() / gw.numel(), (int)gw.numel(), (float)eps,
+                            stream());
+    return std::vector<Tensor>{dx, dz, dg};
+  });
   m.def("mxgemm_error_code", &ttb::mxgemm_error_code, py::arg("reset") = true);
   m.def("dp_error_info", []() {
     int v[4];

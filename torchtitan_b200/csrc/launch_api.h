@@ -107,6 +107,15 @@ void attn_res_fwd(const void* const* blocks, int nb, const float* u, void* out, 
 void attn_res_bwd(const void* const* blocks, void* const* dblocks, int nb, const float* u, const void* dout, float* du,
                   int64_t T, int D, float eps, cudaStream_t s);
 
+// kda_eltwise.cu: KDA short causal conv + SiLU and gated RMSNorm (forward and backward)
+void kda_short_conv_fwd(const void* x, const float* w, void* y, int64_t B, int64_t T, int C, int W, cudaStream_t s);
+void kda_short_conv_bwd(const void* x, const float* w, const void* dy, void* dx, float* dw, int64_t B, int64_t T,
+                        int C, int W, cudaStream_t s);
+void kda_gated_norm_fwd(const void* x, const void* z, const float* g, void* y, int64_t R, int D, float eps,
+                        cudaStream_t s);
+void kda_gated_norm_bwd(const void* x, const void* z, const float* g, const void* dy, void* dx, void* dz, float* dg,
+                        int64_t R, int D, float eps, cudaStream_t s);
+
 // router_topk.cu: MoE routing selection (scores, bias, group limit, top-k, counts)
 void router_topk(const float* logits, const float* bias, int64_t T, int E, int top_k, bool sigmoid, int n_groups,
                  int n_limited, int64_t* idx, int32_t* counts, cudaStream_t s);

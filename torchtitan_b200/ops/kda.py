@@ -240,8 +240,57 @@ def naive_recurrent_kda(q, k, v, g, beta, scale=None, use_qk_l2norm: bool = True
     return o, S
 
 
+def _eltwise_kernels(x: torch.Tensor) -> bool:
+    # csrc/kda_eltwise.cu is opt-in until it has run on a B200
+    import os
+
+    return x.is_cuda and x.dtype == torch.bfloat16 and os.environ.get("TTB_KDA_ELTWISE") == "1"
+
+
+class _ShortConv(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight):
+        from ._ext import ext
+
+        x = x.contiguous()
+        w = weight.float().reshape(weight.shape[0], -1).contiguous()
+        ctx.save_for_backward(x, w)
+        ctx.wshape, ctx.wdtype = weight.shape, weight.dtype
+        return ext().kda_short_conv_fwd(x, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ._ext import ext
+
+        x, w = ctx.saved_tensors
+        dx, dw = ext().kda_short_conv_bwd(x, w, dy.contiguous())
+        return dx, dw.reshape(ctx.wshape).to(ctx.wdtype)
+
+
+class _GatedNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, gate, weight, eps):
+        from ._ext import ext
+
+        x, gate = x.contiguous(), gate.to(x.dtype).contiguous()
+        g = weight.float().contiguous()
+        ctx.save_for_backward(x, gate, g)
+        ctx.eps, ctx.wdtype, ctx.gdtype = eps, weight.dtype, gate.dtype
+        return ext().kda_gated_norm_fwd(x, gate, g, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ._ext import ext
+
+        x, gate, g = ctx.saved_tensors
+        dx, dz, dg = ext().kda_gated_norm_bwd(x, gate, g, dy.contiguous(), ctx.eps)
+        return dx, dz.to(ctx.gdtype), dg.to(ctx.wdtype), None
+
+
 def short_conv_silu(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """Causal depthwise conv (kernel [C, 1, W]) over time then SiLU; x: [B, T, C]."""
+    if _eltwise_kernels(x) and weight.shape[-1] <= 8:
+        return _ShortConv.apply(x, weight)
     W = weight.shape[-1]
     xt = F.pad(x.transpose(1, 2), (W - 1, 0))
     y = F.conv1d(xt, weight.to(x.dtype), groups=x.shape[-1])
@@ -250,6 +299,8 @@ def short_conv_silu(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
 
 def gated_rms_norm(x: torch.Tensor, gate: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """RMSNorm over the last dim, times weight, times sigmoid(gate)."""
+    if _eltwise_kernels(x) and type(weight).__name__ != "DTensor":
+        return _GatedNorm.apply(x, gate, weight, eps)
     xf = x.float()
     y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * weight.float()
     return (y * torch.sigmoid(gate.float())).to(x.dtype)
