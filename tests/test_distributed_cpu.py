@@ -535,7 +535,8 @@ def test_tensor_parallel_gradients(sp, module, config):
 
 
 @pytest.mark.parametrize("sp", [True, False])
-@pytest.mark.parametrize("module,config", [("qwen3", "qwen3_debugmodel_moe"), ("deepseek_v3", "deepseek_v3_debugmodel")])
+@pytest.mark.parametrize("module,config", [("qwen3", "qwen3_debugmodel_moe"), ("deepseek_v3", "deepseek_v3_debugmodel"),
+                                           ("gpt_oss", "gpt_oss_debugmodel")])
 def test_expert_tensor_parallel_gradients(sp, module, config):
     with tempfile.TemporaryDirectory() as d:
         _run(_llama_tp_grads, 2, d, sp, module, config, ("--parallelism.expert-tensor-parallel-degree", "2"))

@@ -148,6 +148,7 @@ class GptOssExperts(nn.Module):
         return (u + 1) * g * torch.sigmoid(self.alpha * g)
 
     grad_reduce_group = None  # replicated over TP on sequence-sharded tokens: reduce weight grads
+    etp_group = None  # expert tensor parallelism: hidden dims sharded, output bias added by TP rank 0
 
     def forward(self, x: torch.Tensor, counts: list[int]) -> torch.Tensor:
         w1, b1, w2, b2 = (_local(t) for t in (self.mlp1_weight, self.mlp1_bias, self.mlp2_weight, self.mlp2_bias))
@@ -155,6 +156,13 @@ class GptOssExperts(nn.Module):
             from torchtitan_b200.parallel.tensor_parallel import grad_all_reduce
 
             w1, b1, w2, b2 = (grad_all_reduce(t, self.grad_reduce_group) for t in (w1, b1, w2, b2))
+        if self.etp_group is not None:
+            import torch.distributed as dist
+
+            from torchtitan_b200.parallel.tensor_parallel import grad_all_reduce
+
+            # the partial outputs are summed over TP: the (replicated) output bias counts once
+            b2 = grad_all_reduce(b2, self.etp_group) * float(dist.get_rank(self.etp_group) == 0)
         outs, start = [], 0
         for e, n in enumerate(counts):
             if n:
@@ -178,7 +186,20 @@ class GptOssMoE(nn.Module):
         self.router.gate.init_weights(0.02)
         self.experts.init_weights(std)
 
+    etp_group = None  # expert tensor parallelism (see GptOssExperts)
+    etp_sequence_parallel = False
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.etp_group is None:
+            return self._forward_core(x)
+        from torchtitan_b200.parallel import tensor_parallel as tp
+
+        g = self.etp_group
+        x = tp.all_gather_seq(x, g) if self.etp_sequence_parallel else tp.grad_all_reduce(x, g)
+        out = self._forward_core(x)
+        return tp.reduce_scatter_seq(out, g) if self.etp_sequence_parallel else tp.all_reduce(out, g)
+
+    def _forward_core(self, x: torch.Tensor) -> torch.Tensor:
         B, S, D = x.shape
         xf = x.reshape(-1, D)
         logits = self.router.gate(xf).float()

@@ -44,9 +44,11 @@ def _apply_tp(model: nn.Module, tp_mesh, parallelism: Any, ep_degree: int = 1) -
     if type(first.attention).__name__ == "GptOssAttention":
         from torchtitan_b200.parallel.tensor_parallel import apply_tp_gpt_oss
 
-        if parallelism.expert_tensor_parallel_degree > 1:
-            raise NotImplementedError("expert tensor parallelism for GPT-OSS experts is not wired")
-        apply_tp_gpt_oss(model, tp_mesh, loss_parallel=not parallelism.disable_loss_parallel, sequence_parallel=sp)
+        etp = parallelism.expert_tensor_parallel_degree > 1
+        if etp and ep_degree > 1:
+            raise NotImplementedError("GPT-OSS experts: expert tensor parallelism with expert parallelism is not wired")
+        apply_tp_gpt_oss(model, tp_mesh, loss_parallel=not parallelism.disable_loss_parallel, sequence_parallel=sp,
+                         etp=etp)
         maybe_enable_async_tp(parallelism, tp_mesh)
         return
     for blk in model.layers.values():

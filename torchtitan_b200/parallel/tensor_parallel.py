@@ -300,10 +300,14 @@ def apply_tp_llama(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_p
     _tp_embed_and_head(model, tp_mesh, loss_parallel, sequence_parallel)
 
 
-def apply_tp_gpt_oss(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_parallel: bool) -> None:
+def apply_tp_gpt_oss(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence_parallel: bool,
+                     etp: bool = False) -> None:
     """GPT-OSS: q/k/v column-parallel (weights and biases), o row-parallel, sinks sharded
     with their heads; the MoE (router, experts with biases) is replicated over TP and, on
-    sequence shards, its gradients are summed over TP."""
+    sequence shards, its gradients are summed over TP.  With ``etp`` the experts shard their
+    hidden dim instead (mlp1 weight and bias along the interleaved gate/up rows, mlp2 along its
+    input), the MoE block gathers its input and reduces its output once, and the replicated
+    output bias is added by TP rank 0 only."""
     from torch.distributed.tensor import Shard
 
     group = tp_mesh.get_group()
@@ -319,6 +323,17 @@ def apply_tp_gpt_oss(model: nn.Module, tp_mesh, *, loss_parallel: bool, sequence
         if sequence_parallel:
             wrap_replicated_norm(blk.attention_norm, tp_mesh)
             wrap_replicated_norm(blk.ffn_norm, tp_mesh)
+        if etp:
+            ex = blk.moe.experts
+            if ex.mlp2_weight.shape[2] % ws:
+                raise ValueError(f"expert TP degree {ws} must divide the expert hidden dim")
+            _shard_param(ex, "mlp1_weight", tp_mesh, Shard(1))
+            _shard_param(ex, "mlp1_bias", tp_mesh, Shard(1))
+            _shard_param(ex, "mlp2_weight", tp_mesh, Shard(2))
+            ex.etp_group = group
+            blk.moe.etp_group, blk.moe.etp_sequence_parallel = group, sequence_parallel
+            blk.moe.router.gate.grad_reduce_group = group  # partial over the hidden slices
+        elif sequence_parallel:
             blk.moe.router.gate.grad_reduce_group = group
             blk.moe.experts.grad_reduce_group = group
     _tp_embed_and_head(model, tp_mesh, loss_parallel, sequence_parallel)
