@@ -1066,3 +1066,24 @@ def _flux_cp(rank, world, out_dir):
 def test_flux_context_parallel_matches_full_sequence():
     with tempfile.TemporaryDirectory() as d:
         _run(_flux_cp, 2, d)
+
+
+# ---------------------------------------------------------------- tensor-parallel generation
+def _tp_generate(rank, world):
+    from torchtitan_b200.generate import generate, make_tensor_parallel
+    from torchtitan_b200.models.llama3 import model_registry
+
+    torch.manual_seed(0)
+    m = model_registry("debugmodel").model.build()
+    m.init_weights()
+    m.eval()
+    p = torch.randint(0, 2048, (2, 9), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        ref = generate(m, p, 6, 1.0, 8, torch.Generator().manual_seed(2))
+        assert make_tensor_parallel(m) is not None
+        out = generate(m, p, 6, 1.0, 8, torch.Generator().manual_seed(2))
+    assert torch.equal(out, ref), (out, ref)
+
+
+def test_tensor_parallel_generation_matches_single_device():
+    _run(_tp_generate, 2)

@@ -8,7 +8,10 @@
 Decoder models whose layers use the common grouped-query attention decode with a
 KV cache (the prompt once, then one token per step; the flash kernel's bottom-right
 causal alignment lets one new query attend to every cached key); other models re-run
-over the growing sequence.  With ``--temperature 0`` decoding is greedy.  Without ``--tokenizer`` the prompt is a
+over the growing sequence.  With ``--temperature 0`` decoding is greedy.
+
+Launched with torchrun on N ranks, the model runs tensor-parallel over all of them (heads
+and MLP columns sharded, logits gathered); every rank decodes the same tokens.  Without ``--tokenizer`` the prompt is a
 space-separated list of token ids.
 """
 from __future__ import annotations
@@ -44,6 +47,28 @@ def _cache_layers(model) -> list | None:
             return None
         atts.append(att)
     return atts
+
+
+def make_tensor_parallel(model):
+    """Tensor-parallel inference over every rank of the default process group (dense
+    grouped-query-attention and MLA decoders): returns the rank's TP mesh, or None on one rank."""
+    import os
+
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world == 1:
+        return None
+    if not dist.is_initialized():
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo")
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from torchtitan_b200.parallel.tensor_parallel import apply_tp_llama
+
+    dev = "cuda" if torch.cuda.is_available() and dist.get_backend() == "nccl" else "cpu"
+    mesh = init_device_mesh(dev, (world,), mesh_dim_names=("tp",))
+    apply_tp_llama(model, mesh, loss_parallel=False, sequence_parallel=False)
+    return mesh
 
 
 def generate(model, prompt: torch.Tensor, max_new_tokens: int, temperature: float = 0.0, top_k: int = 0,
@@ -93,6 +118,11 @@ def main(argv: list[str] | None = None) -> None:
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--device", default="cuda" if torch.cuda.is_available() else "cpu")
     a = ap.parse_args(argv)
+    import os
+
+    if a.device == "cuda" and int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))  # one GPU per rank
+        a.device = f"cuda:{torch.cuda.current_device()}"
     spec = importlib.import_module(f"torchtitan_b200.models.{a.module}").model_registry(a.flavor)
     torch.manual_seed(a.seed)
     model = spec.model.build().to(a.device)
@@ -102,7 +132,8 @@ def main(argv: list[str] | None = None) -> None:
 
         sd = _load_dcp(a.checkpoint, {k: v.cpu() for k, v in model.state_dict().items()})
         model.load_state_dict(sd, strict=False)
-    if a.device == "cuda":
+    mesh = make_tensor_parallel(model)
+    if a.device.startswith("cuda"):
         model = model.to(torch.bfloat16)
         model.rope.init_weights(torch.device("cuda"))  # RoPE tables stay fp32
     model.eval()
@@ -118,7 +149,8 @@ def main(argv: list[str] | None = None) -> None:
     out = generate(model, torch.tensor([ids], device=a.device), a.max_new_tokens, a.temperature, a.top_k, g,
                    getattr(tok, "eos_id", None))
     new = out[0, len(ids):].tolist()
-    print(tok.decode(new) if tok else " ".join(map(str, new)))
+    if mesh is None or mesh.get_local_rank() == 0:
+        print(tok.decode(new) if tok else " ".join(map(str, new)))
 
 
 if __name__ == "__main__":
