@@ -1087,3 +1087,46 @@ def _tp_generate(rank, world):
 
 def test_tensor_parallel_generation_matches_single_device():
     _run(_tp_generate, 2)
+
+
+# ---------------------------------------------------------------- validation through the training layout
+def _validate_layout(rank, world, out_dir, extra):
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.components.loss import cross_entropy_loss
+    from torchtitan_b200.components.validate import Validator
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.models.llama3 import model_registry
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "1",
+        "--training.seq-len", "64", "--training.local-batch-size", "2", "--training.dtype", "float32",
+        "--training.mixed-precision-param", "float32", "--parallelism.data-parallel-shard-degree", "1",
+        "--validator.enable", "--validator.steps", "2", "--debug.seed", "0", "--dump-folder", out_dir, *extra]))
+    loss = t.validator.validate(t.model_parts, 0)
+    full = {}
+    for part in t.model_parts:
+        full.update(get_model_state_dict(part, options=StateDictOptions(full_state_dict=True)))
+    gathered = [None] * world
+    dist.all_gather_object(gathered, full)
+    merged = {}
+    for d in gathered:
+        merged.update(d)
+    ref = model_registry("debugmodel").model.build()
+    ref.load_state_dict({k.replace("_checkpoint_wrapped_module.", ""): v for k, v in merged.items()}, strict=False)
+    ref.rope.init_weights()
+    v = Validator(t.config.validator, seq_len=64, local_batch_size=2, loss_fn=cross_entropy_loss)
+    want = v.validate([ref], 0)
+    assert abs(loss - want) < 1e-5 * abs(want), (loss, want, extra)
+    t.close()
+
+
+@pytest.mark.parametrize("extra", [
+    ("--parallelism.tensor-parallel-degree", "2"),
+    ("--parallelism.pipeline-parallel-degree", "2", "--parallelism.pipeline-parallel-microbatch-size", "1"),
+    ("--parallelism.context-parallel-degree", "2"),
+])
+def test_validation_through_parallel_layouts(extra):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_validate_layout, 2, d, extra)

@@ -46,29 +46,46 @@ class Validator(BaseValidator):
             dp_world_size=dp_world_size, dp_rank=dp_rank, tokenizer=tokenizer, seq_len=seq_len,
             local_batch_size=local_batch_size)
 
+    loss_step = None
+    """Set by the trainer: ``loss_step(input_dict, labels) -> loss sum`` of this rank's share of
+    the batch through the training layout (pipeline ``eval`` schedule, context-parallel
+    sharding, vocabulary-parallel loss); 0 on pipeline stages without the loss."""
+
     @torch.no_grad()
     def validate(self, model_parts: list, step: int) -> float:
+        import torch.distributed as dist
+
+        was_training = [m.training for m in model_parts]
+        for m in model_parts:
+            m.eval()
         model = model_parts[0]
-        was_training = model.training
-        model.eval()
-        total, ntok = 0.0, 0
+        dev = self.device or next(model.parameters()).device
+        total = torch.zeros((), dtype=torch.float64)
+        ntok = 0
         for i, (inp, labels) in enumerate(self.dataloader):
             if 0 <= self.config.steps <= i:
                 break
-            dev = self.device or next(model.parameters()).device
-            tokens = inp["input"].to(dev)
+            inp = {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in inp.items()}
             labels = labels.to(dev)
-            pred = model(tokens)
-            total += float(self.loss_fn(pred, labels))
+            if self.loss_step is not None:
+                total += float(self.loss_step(inp, labels))
+            else:
+                total += float(self.loss_fn(model(inp["input"]), labels))
             ntok += int((labels != IGNORE_INDEX).sum())
-        if self.parallel_dims is not None and self.parallel_dims.dp_enabled:
-            mesh = self.parallel_dims.get_mesh("batch")
-            total = float(dist_utils.dist_sum(torch.tensor(total), mesh))
-            ntok = int(dist_utils.dist_sum(torch.tensor(float(ntok)), mesh))
-        loss = total / max(ntok, 1)
+        pd = self.parallel_dims
+        if pd is not None and pd.pp_enabled:  # only the last stage holds the loss
+            pp = pd.get_mesh("pp")
+            t = total.reshape(1).to(dev if dist.get_backend() != "gloo" else "cpu")
+            dist.broadcast(t, src=dist.get_global_rank(pp.get_group(), pp.size() - 1), group=pp.get_group())
+            total = t.reshape(()).cpu()
+        if pd is not None and pd.dp_cp_enabled:
+            total = dist_utils.dist_sum(total.float(), pd.get_mesh("loss"))  # dp and cp shards
+        if pd is not None and pd.dp_enabled:
+            ntok = int(dist_utils.dist_sum(torch.tensor(float(ntok)), pd.get_mesh("batch")))
+        loss = float(total) / max(ntok, 1)
         logger.info(f"validate step {step}: loss {loss:.5f}")
         if self.metrics_processor is not None:
             self.metrics_processor.logger.log({"validation_metrics/loss": loss}, step)
-        if was_training:
-            model.train()
+        for m, w in zip(model_parts, was_training):
+            m.train(w)
         return loss

@@ -220,6 +220,8 @@ class Trainer(Stateful, Configurable):
                                                metrics_processor=self.metrics_processor,
                                                seq_len=c.training.seq_len,
                                                local_batch_size=c.training.local_batch_size, device=self.device)
+        if self.validator is not None:
+            self.validator.loss_step = self._eval_loss_sum
         logger.info(f"trainer ready: local batch {c.training.local_batch_size}, global batch {gbs}, grad accum "
                     f"{self.gradient_accumulation_steps}, seq {c.training.seq_len}, steps {c.training.steps}")
 
@@ -247,6 +249,22 @@ class Trainer(Stateful, Configurable):
 
             return vocab_parallel_cross_entropy_sum(pred, labels, m._tp_group, IGNORE_INDEX)
         return self.loss_fn(pred, labels)
+
+    @torch.no_grad()
+    def _eval_loss_sum(self, input_dict: dict, labels: torch.Tensor) -> torch.Tensor:
+        """Summed validation loss of this rank's share of a batch, through the training layout."""
+        inputs, labels, extra_inputs, extra_kwargs = self.post_dataloading_process(input_dict, labels)
+        if self.parallel_dims.pp_enabled:
+            self._pp_token_norm = 1.0
+            comp = getattr(self.model_parts[0], "_fsdp_grad_compensation", 1)
+            targets, losses = (labels, []) if self.pp_has_last_stage else (None, None)
+            args = (inputs,) if self.pp_has_first_stage else ()
+            self.pp_schedule.eval(*args, **extra_kwargs, target=targets, losses=losses)
+            if self.pp_has_last_stage:
+                return torch.sum(torch.stack(losses)).float().cpu() / comp
+            return torch.zeros(())
+        pred = self.model_parts[0](inputs, **extra_inputs, **extra_kwargs)
+        return self._loss(pred, labels).float().cpu()
 
     def _pp_loss(self, pred, labels):
         # the schedule backpropagates this value: normalise by the step's global token count
