@@ -87,7 +87,7 @@ def test_forge_engine_steps_on_given_batches(tmp_path):
     eng.close()
 
 
-@pytest.mark.parametrize("module", ["llama3", "qwen3"])
+@pytest.mark.parametrize("module", ["llama3", "qwen3", "deepseek_v3"])
 def test_kv_cache_generation_equals_full_recompute(module):
     """Incremental decoding with the KV cache gives the same tokens as re-running the whole
     sequence, greedy and sampled, and leaves no cache behind."""

@@ -5,8 +5,8 @@
         [--checkpoint <dcp dir>] [--tokenizer <hf tokenizer dir>] --prompt "..." \\
         [--max-new-tokens 32] [--temperature 0] [--top-k 0] [--seed 0]
 
-Decoder models whose layers use the common grouped-query attention decode with a
-KV cache (the prompt once, then one token per step; the flash kernel's bottom-right
+Decoder models whose layers use the common grouped-query attention or multi-head latent
+attention decode with a KV cache (the prompt once, then one token per step; the flash kernel's bottom-right
 causal alignment lets one new query attend to every cached key); other models re-run
 over the growing sequence.  With ``--temperature 0`` decoding is greedy.
 
@@ -43,7 +43,9 @@ def _cache_layers(model) -> list | None:
     atts = []
     for blk in layers.values():
         att = getattr(blk, "attention", None)
-        if type(att) is not GQAttention or att.cp_hook is not None or att.mask_type != "causal":
+        if type(att) is not GQAttention and type(att).__name__ != "MLAttention":
+            return None
+        if att.cp_hook is not None or getattr(att, "mask_type", "causal") != "causal":
             return None
         atts.append(att)
     return atts

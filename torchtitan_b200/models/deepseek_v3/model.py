@@ -100,6 +100,7 @@ class MLAttention(nn.Module):
         self.wo = Linear(a.n_heads * self.vd, a.dim)
         self.softmax_scale = a.softmax_scale
         self.cp_hook = None
+        self.kv_cache: dict | None = None  # set by generation (keys/values of earlier positions)
 
     def init_weights(self, init_std: float) -> None:
         lins = [self.wkv_a, self.wkv_b] + ([self.wq] if self.q_lora_rank == 0 else [self.wq_a, self.wq_b])
@@ -129,6 +130,11 @@ class MLAttention(nn.Module):
         q = torch.cat([q_nope, q_pe], dim=-1)
         k = torch.cat([k_nope, k_pe.expand(B, S, H, self.rope_dim)], dim=-1)
         v = v.contiguous()
+        if self.kv_cache is not None:  # incremental decoding: attend to every cached position too
+            if self.kv_cache:
+                k = torch.cat([self.kv_cache["k"], k], 1)
+                v = torch.cat([self.kv_cache["v"], v], 1)
+            self.kv_cache["k"], self.kv_cache["v"] = k, v
         if self.cp_hook is not None:
             o = self.cp_hook(self.inner_attention, q, k, v, attention_masks)
         else:
