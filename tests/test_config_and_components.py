@@ -636,3 +636,18 @@ def test_attnres_stage_cache_sends_only_missing_blocks():
     blocks = [torch.randn(1, 4, 8) for _ in range(3)]
     out = stage_exit(parts[1], (blocks, torch.randn(1, 4, 8)))
     assert out.shape[0] == 2 and torch.equal(out[0], blocks[2])
+
+
+def test_nonfinite_canary_names_the_module(tmp_path):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    t = Trainer(ConfigManager().parse_args([
+        "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "1", "--training.seq-len", "64",
+        "--debug.nonfinite-check", "--activation-checkpoint.mode", "none", "--dump-folder", str(tmp_path)]))
+    t.train()  # finite: no error
+    with torch.no_grad():
+        t.model_parts[0].layers["2"].attention.wv.weight.fill_(float("nan"))
+    with pytest.raises(FloatingPointError, match=r"layers\.2\.attention\.wv"):
+        t.model_parts[0](torch.randint(0, 2048, (1, 16)))
+    t.close()

@@ -110,3 +110,6 @@ class DebugConfig:
     batch_invariant: bool = False
     print_config: bool = False
     save_config_file: str | None = None
+    nonfinite_check: bool = False
+    """Forward hooks on every module raise, naming the first module whose output holds a NaN
+    or Inf (costs one device-to-host read per module output: debugging only)."""

@@ -222,6 +222,11 @@ class Trainer(Stateful, Configurable):
                                                local_batch_size=c.training.local_batch_size, device=self.device)
         if self.validator is not None:
             self.validator.loss_step = self._eval_loss_sum
+        if c.debug.nonfinite_check:
+            from torchtitan_b200.utils.nonfinite import install_nonfinite_hooks
+
+            for m in self.model_parts:
+                install_nonfinite_hooks(m)
         logger.info(f"trainer ready: local batch {c.training.local_batch_size}, global batch {gbs}, grad accum "
                     f"{self.gradient_accumulation_steps}, seq {c.training.seq_len}, steps {c.training.steps}")
 
