@@ -183,3 +183,24 @@ def test_kimi_multimodal_splices_projected_patches():
     loss.backward()
     assert mm.projector.fc1.weight.grad is not None and tower.proj.weight.grad is None
     assert (labels[0, 4:9] == -100).all()
+
+
+@pytest.mark.parametrize("S,W", [(50, 8), (64, 16), (17, 16)])
+def test_gpt_oss_chunked_sliding_window_matches_masked_softmax(S, W):
+    """Sliding-window attention as two causal attentions per window chunk (lse merge, then the
+    sink) equals the masked softmax with the sink column, values and gradients."""
+    from torchtitan_b200.models.gpt_oss.model import sink_attention, sliding_window_attention_lse
+
+    torch.manual_seed(0)
+    q = torch.randn(2, S, 4, 16, requires_grad=True)
+    k, v = (torch.randn(2, S, 2, 16, requires_grad=True) for _ in range(2))
+    sinks = torch.randn(4)
+    o, lse = sliding_window_attention_lse(q, k, v, W, 0.25)
+    out = o * torch.sigmoid(lse - sinks.view(1, 1, -1))[..., None]
+    ref = sink_attention(q, k, v, sinks, W, 0.25)
+    assert torch.allclose(out, ref, atol=1e-5)
+    g = torch.randn_like(ref)
+    ga = torch.autograd.grad(out, (q, k, v), g)
+    gb = torch.autograd.grad(ref, (q, k, v), g)
+    for a, b in zip(ga, gb):
+        assert torch.allclose(a, b, atol=1e-5)

@@ -132,3 +132,18 @@ def test_vlm_bf16_forward_backward_with_images():
     loss = F.cross_entropy(logits.flatten(0, 1).float(), tokens.cuda().roll(-1, 1).flatten())
     loss.backward()
     assert all(p.grad is not None and torch.isfinite(p.grad).all() for p in model.parameters())
+
+
+@pytest.mark.skipif(__import__("os").environ.get("TTB_SWA_CHUNKED_TESTS") != "1",
+                    reason="chunked sliding-window path not yet run on a B200; opt in explicitly")
+def test_gpt_oss_chunked_sliding_window_on_flash_kernel():
+    from torchtitan_b200.models.gpt_oss.model import sink_attention, sliding_window_attention_lse
+
+    torch.manual_seed(0)
+    q = torch.randn(2, 1000, 8, 64, device="cuda", dtype=torch.bfloat16)
+    k, v = (torch.randn(2, 1000, 2, 64, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    sinks = torch.randn(8, device="cuda")
+    o, lse = sliding_window_attention_lse(q, k, v, 128, 0.125)
+    out = o.float() * torch.sigmoid(lse - sinks.view(1, 1, -1))[..., None]
+    ref = sink_attention(q.float(), k.float(), v.float(), sinks, 128, 0.125)
+    assert float((out - ref).norm() / ref.norm()) < 2e-2

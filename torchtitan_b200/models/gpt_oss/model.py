@@ -80,6 +80,64 @@ def sink_attention(q, k, v, sinks, window: int, scale: float):
     return torch.einsum("bhst,bthd->bshd", p, vv.float()).to(q.dtype)
 
 
+def sliding_window_attention_lse(q, k, v, window: int, scale: float):
+    """Causal attention limited to the last ``window`` keys (key j visible to query i when
+    i - window < j <= i) as two plain causal attentions per window-sized chunk, so the flash
+    kernel does the work in O(S * window):
+
+    * chunk c against itself: causal, every key within the window;
+    * chunk c against chunk c - 1: local query a sees local key b when b > a.  Reversing both
+      orders turns that into "b' < a'", i.e. causal with keys shifted by one: reversed queries
+      1..W-1 against reversed keys 0..W-2 (query a = W-1 sees no earlier key and is left out).
+
+    The two partial results merge through their log-sum-exps.  Returns (o, lse) like
+    ``ops.attention_with_lse``; q: [B, S, H, D], k/v: [B, S, Hk, D]."""
+    B, S, H, D = q.shape
+    W = window
+    pad = (-S) % W
+    F_ = torch.nn.functional
+    if pad:  # padded positions come after every real one: causal masking hides them
+        q, k, v = (F_.pad(t, (0, 0, 0, 0, 0, pad)) for t in (q, k, v))
+    NC = (S + pad) // W
+
+    def chunks(t):  # [B, NC*W, h, d] -> [B*NC, W, h, d]
+        return t.reshape(B * NC, W, *t.shape[2:])
+
+    qc, kc, vc = chunks(q), chunks(k), chunks(v)
+    o1, l1 = ops.attention_with_lse(qc, kc, vc, causal=True, scale=scale)
+    if NC > 1 and W > 1:
+        qp = q.reshape(B, NC, W, H, D)[:, 1:].flip(2)[:, :, 1:]                    # reversed queries 1..W-1
+        kp = k.reshape(B, NC, W, *k.shape[2:])[:, :-1].flip(2)[:, :, :-1]         # previous chunk, reversed 0..W-2
+        vp = v.reshape(B, NC, W, *v.shape[2:])[:, :-1].flip(2)[:, :, :-1]
+        o2, l2 = ops.attention_with_lse(qp.reshape(B * (NC - 1), W - 1, H, D).contiguous(),
+                                        kp.reshape(B * (NC - 1), W - 1, *k.shape[2:]).contiguous(),
+                                        vp.reshape(B * (NC - 1), W - 1, *v.shape[2:]).contiguous(),
+                                        causal=True, scale=scale)
+        # back to forward order: local queries 0..W-2 of chunks 1..NC-1; the rest see no earlier chunk
+        o2 = o2.view(B, NC - 1, W - 1, H, -1).flip(2)
+        l2 = l2.view(B, NC - 1, W - 1, H).flip(2)
+        neg = torch.full((B, NC, W, H), float("-inf"), device=q.device, dtype=l2.dtype)
+        lb = torch.cat([neg[:, :1], torch.cat([l2, neg[:, 1:, :1]], 2)], 1)
+        ob = torch.cat([torch.zeros_like(o2[:, :1]).expand(B, 1, W - 1, H, o2.shape[-1]),
+                        o2], 1)
+        ob = torch.cat([ob, torch.zeros_like(ob[:, :, :1])], 2)
+        la = l1.view(B, NC, W, H)
+        lse = torch.logaddexp(la, lb)
+        oa = o1.view(B, NC, W, H, -1).float()
+        o = oa * torch.exp(la - lse)[..., None] + ob.float() * torch.exp(lb - lse)[..., None]
+        o, lse = o.reshape(B, NC * W, H, -1), lse.reshape(B, NC * W, H)
+    else:
+        o, lse = o1.view(B, NC * W, H, -1).float(), l1.view(B, NC * W, H)
+    return o[:, :S].to(v.dtype), lse[:, :S]
+
+
+def _chunked_window_enabled(q: torch.Tensor) -> bool:
+    import os
+
+    # on a GPU opt-in (TTB_SWA_CHUNKED=1) until it has run on a B200
+    return not q.is_cuda or os.environ.get("TTB_SWA_CHUNKED") == "1"
+
+
 class GptOssAttention(nn.Module):
     def __init__(self, a: GptOssModelArgs, layer_id: int):
         super().__init__()
@@ -108,6 +166,10 @@ class GptOssAttention(nn.Module):
             o, lse = ops.attention_with_lse(q, k, v, causal=True, scale=self.scale)
             w = torch.sigmoid(lse - _local(self.sinks).float().view(1, 1, -1))
             return (o.float() * w[..., None]).to(o.dtype)
+        if self.window and q.shape[1] > self.window and _chunked_window_enabled(q):
+            o, lse = sliding_window_attention_lse(q, k, v, self.window, self.scale)
+            w = torch.sigmoid(lse - _local(self.sinks).float().view(1, 1, -1))
+            return (o.float() * w[..., None]).to(q.dtype)
         return sink_attention(q, k, v, _local(self.sinks), self.window, self.scale)
 
     def forward(self, x, cos, sin, attention_masks=None):
