@@ -107,6 +107,9 @@ def test_llama4_chunked_attention_is_block_causal():
     ref = F.scaled_dot_product_attention(q.transpose(1, 2), k.repeat_interleave(2, 2).transpose(1, 2),
                                          v.repeat_interleave(2, 2).transpose(1, 2), attn_mask=mask).transpose(1, 2)
     torch.testing.assert_close(out, ref, rtol=1e-4, atol=1e-4)
+    # a sequence that is not a multiple of the chunk stays chunked (the last chunk is short)
+    out = att.inner_attention(q[:, :10], k[:, :10], v[:, :10])
+    torch.testing.assert_close(out, ref[:, :10], rtol=1e-4, atol=1e-4)
 
 
 def test_deepseek_mla_scale_and_shared_rope_key():

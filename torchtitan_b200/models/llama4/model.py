@@ -79,11 +79,16 @@ class Llama4Attention(GQAttention):
 
     def inner_attention(self, q, k, v, attention_masks=None):
         B, S = q.shape[:2]
-        if self.block and S > self.block and S % self.block == 0:
-            n = S // self.block
+        if self.block and S > self.block:
+            # block-diagonal causal: fold the chunks into the batch (padding the last chunk at its
+            # end, where causal masking keeps it away from every real query)
+            pad = (-S) % self.block
+            if pad:
+                q, k, v = (torch.nn.functional.pad(t, (0, 0, 0, 0, 0, pad)) for t in (q, k, v))
+            n = (S + pad) // self.block
             fold = lambda t: t.reshape(B * n, self.block, *t.shape[2:])  # noqa: E731
             o = ops.attention(fold(q), fold(k), fold(v), causal=True)
-            return o.reshape(B, S, *o.shape[2:])
+            return o.reshape(B, S + pad, *o.shape[2:])[:, :S]
         return ops.attention(q, k, v, causal=True)
 
     def forward(self, x, cos, sin, attention_masks=None):
