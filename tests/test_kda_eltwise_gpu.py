@@ -46,3 +46,15 @@ def test_gated_norm_kernel(R, D, monkeypatch):
     res = _both(lambda a, b, c: kda.gated_rms_norm(a, b, c, 1e-6), (x, z, g), monkeypatch, (0, 1, 2))
     for a, b in zip(res["1"], res["0"]):
         torch.testing.assert_close(a, b, rtol=2e-2, atol=2e-2 * float(b.abs().max()))
+
+
+def test_kda_gate_kernel(monkeypatch):
+    from torchtitan_b200.ops import kda
+
+    torch.manual_seed(2)
+    x = torch.randn(2, 300, 4, 64, device="cuda", dtype=torch.bfloat16)
+    A = torch.randn(4, device="cuda")
+    b = 0.1 * torch.randn(4 * 64, device="cuda")
+    res = _both(kda.kda_gate, (x, A, b), monkeypatch, (0, 1, 2))
+    for a, c in zip(res["1"], res["0"]):
+        torch.testing.assert_close(a, c, rtol=2e-2, atol=2e-2 * float(c.abs().max()))

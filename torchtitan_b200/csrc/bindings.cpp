@@ -514,6 +514,33 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                             stream());
     return std::vector<Tensor>{dx, dz, dg};
   });
+  m.def("kda_gate_fwd", [](Tensor x, Tensor A, c10::optional<Tensor> b) {  // x [..., H, K] bf16, A [H], b [H*K]
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() >= 2, "kda gate: x");
+    const int64_t H = x.size(-2), K = x.size(-1);
+    TORCH_CHECK(A.scalar_type() == at::kFloat && A.is_contiguous() && A.numel() == H, "kda gate: A");
+    const float* bp = nullptr;
+    if (b.has_value()) {
+      TORCH_CHECK(b->scalar_type() == at::kFloat && b->is_contiguous() && b->numel() == H * K, "kda gate: bias");
+      bp = b->data_ptr<float>();
+    }
+    c10::cuda::CUDAGuard g(x.device());
+    auto out = torch::empty(x.sizes(), x.options().dtype(at::kFloat));
+    ttb::kda_gate_fwd(x.data_ptr(), A.data_ptr<float>(), bp, out.data_ptr<float>(), x.numel(), (int)H, (int)K,
+                      stream());
+    return out;
+  });
+  m.def("kda_gate_bwd", [](Tensor x, Tensor A, c10::optional<Tensor> b, Tensor dg) {
+    TORCH_CHECK(dg.scalar_type() == at::kFloat && dg.is_contiguous() && dg.sizes() == x.sizes(), "kda gate: dg");
+    const int64_t H = x.size(-2), K = x.size(-1);
+    c10::cuda::CUDAGuard g(x.device());
+    auto dx = torch::empty_like(x);
+    auto dA = torch::empty_like(A);
+    Tensor db = b.has_value() ? torch::empty_like(*b) : Tensor();
+    ttb::kda_gate_bwd(x.data_ptr(), A.data_ptr<float>(), b.has_value() ? b->data_ptr<float>() : nullptr,
+                      dg.data_ptr<float>(), dx.data_ptr(), dA.data_ptr<float>(),
+                      b.has_value() ? db.data_ptr<float>() : nullptr, x.numel(), (int)H, (int)K, stream());
+    return std::vector<Tensor>{dx, dA, b.has_value() ? db : torch::zeros({0}, A.options())};
+  });
   m.def("mxgemm_error_code", &ttb::mxgemm_error_code, py::arg("reset") = true);
   m.def("dp_error_info", []() {
     int v[4];

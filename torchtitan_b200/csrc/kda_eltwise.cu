@@ -2,6 +2,7 @@
 // one backward instead of a chain of PyTorch ops:
 //   short conv   y[b,t,c] = silu(sum_{j<W} w[c,j] x[b, t-W+1+j, c])      (causal, depthwise)
 //   gated norm   y[r,:]   = x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * g * sigmoid(z[r,:])
+//   decay gate   g[r,h,k] = -exp(A[h]) * softplus(x[r,h,k] + b[h,k])    (fp32 log decay)
 // bf16 storage, fp32 arithmetic.  Weight gradients are accumulated per CTA in shared
 // memory and added to an fp32 global buffer once per CTA.
 #include <cuda_bf16.h>
@@ -153,6 +154,42 @@ __global__ void __launch_bounds__(NT) gnorm_bwd(const __nv_bfloat16* __restrict_
   for (int d = threadIdx.x; d < D; d += NT) atomicAdd(dg + d, sdg[d]);
 }
 
+// one thread per element; the per-(h, k) parameter gradients accumulate per CTA in shared memory
+__global__ void __launch_bounds__(NT) gate_fwd(const __nv_bfloat16* __restrict__ x, const float* __restrict__ A,
+                                               const float* __restrict__ b, float* __restrict__ g, int64_t n, int H,
+                                               int K) {
+  for (int64_t i = blockIdx.x * (int64_t)NT + threadIdx.x; i < n; i += (int64_t)gridDim.x * NT) {
+    const int hk = static_cast<int>(i % (H * K));
+    const float v = bf(x[i]) + (b != nullptr ? b[hk] : 0.f);
+    const float sp = v > 20.f ? v : log1pf(__expf(v));
+    g[i] = -__expf(A[hk / K]) * sp;
+  }
+}
+
+__global__ void __launch_bounds__(NT) gate_bwd(const __nv_bfloat16* __restrict__ x, const float* __restrict__ A,
+                                               const float* __restrict__ b, const float* __restrict__ dg,
+                                               __nv_bfloat16* __restrict__ dx, float* __restrict__ dA,
+                                               float* __restrict__ db, int64_t n, int H, int K) {
+  extern __shared__ float acc[];  // [H*K] db partials, then [H] dA partials
+  for (int j = threadIdx.x; j < H * K + H; j += NT) acc[j] = 0.f;
+  __syncthreads();
+  for (int64_t i = blockIdx.x * (int64_t)NT + threadIdx.x; i < n; i += (int64_t)gridDim.x * NT) {
+    const int hk = static_cast<int>(i % (H * K));
+    const float v = bf(x[i]) + (b != nullptr ? b[hk] : 0.f);
+    const float sp = v > 20.f ? v : log1pf(__expf(v));
+    const float e = __expf(A[hk / K]);
+    const float d = dg[i];
+    const float dv = -d * e * sigm(v);
+    dx[i] = __float2bfloat16(dv);
+    atomicAdd(acc + hk, dv);
+    atomicAdd(acc + H * K + hk / K, -d * e * sp);
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < H * K; j += NT)
+    if (db != nullptr) atomicAdd(db + j, acc[j]);
+  for (int j = threadIdx.x; j < H; j += NT) atomicAdd(dA + j, acc[H * K + j]);
+}
+
 int sms() {
   int dev = 0, n = 148;
   cudaGetDevice(&dev);
@@ -215,6 +252,30 @@ void kda_gated_norm_bwd(const void* x, const void* z, const float* g, const void
                                            g, static_cast<const __nv_bfloat16*>(dy), static_cast<__nv_bfloat16*>(dx),
                                            static_cast<__nv_bfloat16*>(dz), dg, R, D, eps);
   check_cuda(cudaGetLastError(), "gated norm bwd launch");
+}
+
+void kda_gate_fwd(const void* x, const float* A, const float* b, float* g, int64_t n, int H, int K, cudaStream_t s) {
+  using namespace kelt;
+  if (n == 0) return;
+  const int64_t blocks = (n + NT - 1) / NT;
+  gate_fwd<<<(unsigned)(blocks < 16 * sms() ? blocks : 16 * sms()), NT, 0, s>>>(static_cast<const __nv_bfloat16*>(x),
+                                                                                A, b, g, n, H, K);
+  check_cuda(cudaGetLastError(), "kda gate fwd launch");
+}
+
+void kda_gate_bwd(const void* x, const float* A, const float* b, const float* dg, void* dx, float* dA, float* db,
+                  int64_t n, int H, int K, cudaStream_t s) {
+  using namespace kelt;
+  const size_t sm = sizeof(float) * (static_cast<size_t>(H) * K + H);
+  if (sm > 200 * 1024) throw std::runtime_error("kda gate: too many channels");
+  check_cuda(cudaMemsetAsync(dA, 0, sizeof(float) * H, s), "kda gate dA clear");
+  if (db != nullptr) check_cuda(cudaMemsetAsync(db, 0, sizeof(float) * H * K, s), "kda gate db clear");
+  if (n == 0) return;
+  check_cuda(cudaFuncSetAttribute(gate_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm), "kda gate smem");
+  const int64_t blocks = (n + NT - 1) / NT;
+  gate_bwd<<<(unsigned)(blocks < 4 * sms() ? blocks : 4 * sms()), NT, sm, s>>>(
+      static_cast<const __nv_bfloat16*>(x), A, b, dg, static_cast<__nv_bfloat16*>(dx), dA, db, n, H, K);
+  check_cuda(cudaGetLastError(), "kda gate bwd launch");
 }
 
 }  // namespace ttb

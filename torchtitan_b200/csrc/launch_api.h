@@ -115,6 +115,9 @@ void kda_gated_norm_fwd(const void* x, const void* z, const float* g, void* y, i
                         cudaStream_t s);
 void kda_gated_norm_bwd(const void* x, const void* z, const float* g, const void* dy, void* dx, void* dz, float* dg,
                         int64_t R, int D, float eps, cudaStream_t s);
+void kda_gate_fwd(const void* x, const float* A, const float* b, float* g, int64_t n, int H, int K, cudaStream_t s);
+void kda_gate_bwd(const void* x, const float* A, const float* b, const float* dg, void* dx, float* dA, float* db,
+                  int64_t n, int H, int K, cudaStream_t s);
 
 // router_topk.cu: MoE routing selection (scores, bias, group limit, top-k, counts)
 void router_topk(const float* logits, const float* bias, int64_t T, int E, int top_k, bool sigmoid, int n_groups,

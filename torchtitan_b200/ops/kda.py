@@ -100,8 +100,33 @@ def decayed_gram(a, b, G, strict: bool):
     return _DecayedGram.apply(a, b, G, strict)
 
 
+class _Gate(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, g_raw, A_log, dt_bias):
+        from ._ext import ext
+
+        x = g_raw.contiguous()
+        A = A_log.float().reshape(-1).contiguous()
+        b = dt_bias.float().reshape(-1).contiguous() if dt_bias is not None else None
+        ctx.save_for_backward(x, A, b)
+        ctx.shapes = (A_log.shape, A_log.dtype, None if dt_bias is None else (dt_bias.shape, dt_bias.dtype))
+        return ext().kda_gate_fwd(x, A, b)
+
+    @staticmethod
+    def backward(ctx, dg):
+        from ._ext import ext
+
+        x, A, b = ctx.saved_tensors
+        dx, dA, db = ext().kda_gate_bwd(x, A, b, dg.float().contiguous())
+        (ashape, adtype, bmeta) = ctx.shapes
+        dbias = None if bmeta is None else db.reshape(bmeta[0]).to(bmeta[1])
+        return dx, dA.reshape(ashape).to(adtype), dbias
+
+
 def kda_gate(g_raw: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor | None) -> torch.Tensor:
     """g = -exp(A_log[h]) * softplus(g_raw + dt_bias): [..., H, K] fp32 log decay."""
+    if _eltwise_kernels(g_raw) and type(A_log).__name__ != "DTensor" and type(dt_bias).__name__ != "DTensor":
+        return _Gate.apply(g_raw, A_log, dt_bias)
     H, K = g_raw.shape[-2:]
     x = g_raw.float()
     if dt_bias is not None:
