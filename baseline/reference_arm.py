@@ -39,6 +39,7 @@ def run(a, dist_env, max_over_ranks, ClockSampler, METRIC, BASELINE_TPS_PER_GPU)
     from torchtitan.components.checkpoint import CheckpointManager
     from torchtitan.components.dataloader import BaseDataLoader
     from torchtitan.components.metrics import MetricsProcessor
+    from torchtitan.distributed import utils as dist_utils
     from torchtitan.config import ActivationCheckpointConfig, CompileConfig, TrainingConfig
     from torchtitan.models.llama3 import config_registry as reg
     from torchtitan.models.llama3 import model_registry
@@ -115,7 +116,9 @@ def run(a, dist_env, max_over_ranks, ClockSampler, METRIC, BASELINE_TPS_PER_GPU)
     torch.cuda.synchronize()
     dev_s = max_over_ranks(e0.elapsed_time(e1) / 1e3)
     clk = clocks.stop()
-    # end to end: reference public API, loss read back each step
+    # end to end: the same sequence as the reference's ``Trainer.train_step`` (zero grad,
+    # inputs copied from pinned host memory, forward/backward, clip, optimizer and LR step)
+    # through its public methods, with the loss read back each step
     if dist.is_initialized():
         dist.barrier()
     t0 = time.perf_counter()
@@ -127,6 +130,8 @@ def run(a, dist_env, max_over_ranks, ClockSampler, METRIC, BASELINE_TPS_PER_GPU)
         labels = labels.to(trainer.device)
         n = torch.tensor(float(labels.numel()), device=trainer.device) * world
         loss = trainer.forward_backward_step(input_dict=inp, labels=labels, global_valid_tokens=n)
+        dist_utils.clip_grad_norm_([p for m in trainer.model_parts for p in m.parameters()],
+                                   trainer.config.training.max_norm, foreach=True)
         trainer.optimizers.step()
         trainer.lr_schedulers.step()
         _ = float(loss.item())

@@ -207,6 +207,8 @@ def run_ours(a):
                    "parallelism": (f"dp{world} (replicated bf16 weights, sharded fp32 AdamW, peer-memory reduce-scatter"
                                    " and optimizer-fused all-gather)"
                                    if getattr(trainer.model_parts[0], "_dp_runtime", None) is not None
+                                   else "single GPU (bf16 compute weights, fp32 masters in the fused AdamW; no sharding)"
+                                   if world == 1
                                    else f"fsdp{world} (reshard_after_forward={cfg.parallelism.fsdp_reshard_after_forward})"), "ac": a.ac, "optimizer": "AdamW (fused, fp32 master)",
                    "l2": "inputs larger than L2 (no flush)"},
         "mfu_pct": round(mfu, 2),
@@ -225,9 +227,29 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
+def _install_reference(ref):
+    """Offline install of the reference source tree into ``ref`` (the same command the
+    build notes record), for boxes where the git-ignored install was not carried over."""
+    import shutil
+    import subprocess
+
+    src = os.environ.get("TTB_REFERENCE_SRC", "/root/reference")
+    if not os.path.isdir(src):
+        return
+    subprocess.run([sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation",
+                    "--no-deps", "--find-links", "/opt/wheelhouse", "--target", ref, src],
+                   stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL, check=False)
+    tok = os.path.join(src, "tests", "assets", "tokenizer")
+    dst = os.path.join(ref, "assets", "tokenizer")
+    if os.path.isdir(tok) and not os.path.isdir(dst):
+        shutil.copytree(tok, dst)
+
+
 def run_reference(a):
     here = os.path.dirname(os.path.abspath(__file__))
     ref = os.path.join(here, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "torchtitan")):
+        _install_reference(ref)
     if not os.path.isdir(os.path.join(ref, "torchtitan")):
         print(json.dumps({"impl": "reference", "unavailable": "reference not installed under baseline/_ref"}))
         return

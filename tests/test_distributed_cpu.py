@@ -764,6 +764,69 @@ def test_resume_reproduces_uninterrupted_losses(extra):
         _run(_resume_exact, 2, d, extra)
 
 
+# ---------------------------------------------------------------- async checkpoint
+def _resume_async(rank, world, out_dir, mode):
+    import json
+
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    def make(steps, folder, extra=()):
+        return Trainer(ConfigManager().parse_args([
+            "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", str(steps),
+            "--training.seq-len", "64", "--metrics.log-freq", "1", "--metrics.enable-jsonl", "--debug.seed", "0",
+            "--dump-folder", os.path.join(out_dir, folder), *extra]))
+
+    def losses(folder):
+        with open(os.path.join(out_dir, folder, "tb", "rank_0", "metrics.jsonl")) as f:
+            return {r["step"]: r["loss_metrics/global_avg_loss"] for r in map(json.loads, f)}
+
+    ck = ("--checkpoint.enable", "--checkpoint.interval", "2", "--checkpoint.async-mode", mode,
+          "--checkpoint.no-last-save-model-only")
+    t = make(5, "straight", ck)  # step 2 is written in the background while steps 3-5 train
+    assert t.checkpointer._async_pg is not None
+    t.train()
+    t.close()
+    t = make(5, "straight", ck + ("--checkpoint.load-step", "2"))
+    t.checkpointer.load(step=2)
+    assert t.step == 2
+    t.train()
+    t.close()
+    if rank == 0:
+        a = losses("straight")
+        with open(os.path.join(out_dir, "straight", "tb", "rank_0", "metrics.jsonl")) as f:
+            rows = [json.loads(r) for r in f]
+        resumed = {r["step"]: r["loss_metrics/global_avg_loss"] for r in rows[5:]}
+        first = {r["step"]: r["loss_metrics/global_avg_loss"] for r in rows[:5]}
+        for s in (3, 4, 5):
+            assert first[s] == resumed[s], (s, first[s], resumed[s], mode, a)
+
+
+@pytest.mark.parametrize("mode", ["async", "async_with_pinned_mem"])
+def test_async_checkpoint_saved_while_training_resumes_exactly(mode):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_resume_async, 2, d, mode)
+
+
+def _uneven_stage(rank, world):
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.tensor import Shard, distribute_tensor
+
+    from torchtitan_b200.components.checkpoint import _to_pinned_host
+
+    mesh = init_device_mesh("cpu", (world,))
+    full = torch.arange(5 * 3, dtype=torch.float32).reshape(5, 3)  # 5 rows over 2 ranks: 3 + 2
+    dt = distribute_tensor(full, mesh, [Shard(0)])
+    staged = _to_pinned_host({"w": dt}, pin=False, copy_cpu=True)["w"]
+    assert staged.shape == full.shape and staged.stride() == dt.stride()
+    assert staged.to_local().data_ptr() != dt.to_local().data_ptr()
+    assert torch.equal(staged.full_tensor(), full)
+
+
+def test_pinned_staging_keeps_uneven_shard_shape():
+    _run(_uneven_stage, 2)
+
+
 # ---------------------------------------------------------------- gradient accumulation
 def _grad_accum(rank, world, out_dir, extra):
     from torchtitan_b200.config.manager import ConfigManager

@@ -116,6 +116,13 @@ class CheckpointManager(Configurable):
             self.states[DATALOADER] = dataloader
         self.states.update(states or {})
         self._pool = ThreadPoolExecutor(max_workers=1) if config.async_mode != "disabled" else None
+        # Background saves run DCP's planning collectives while the next steps issue their own
+        # NCCL collectives; on the default group the two threads could interleave differently on
+        # different ranks. They get a dedicated gloo group instead (parity: the reference's
+        # ``torchtitan/components/checkpoint.py:372,479-491``).
+        self._async_pg = None
+        if config.async_mode != "disabled" and config.enable and dist.is_initialized():
+            self._async_pg = dist.new_group(backend="gloo")
         self._pending: Future | None = None
         self._purge_lock = threading.Lock()
 
@@ -160,10 +167,11 @@ class CheckpointManager(Configurable):
             else:
                 dcp.save(state, checkpoint_id=path)
         elif self._pool is not None:
+            # Stage a host copy on this thread (the next step overwrites the device tensors), then
+            # write it from the background thread over the gloo group.
             state = {k: v.state_dict() if hasattr(v, "state_dict") else v for k, v in self.states.items()}
-            if self.config.async_mode == "async_with_pinned_mem":
-                state = _to_pinned_host(state)
-            self._pending = self._pool.submit(dcp.save, state, checkpoint_id=path)
+            state = _to_pinned_host(state, pin=self.config.async_mode == "async_with_pinned_mem", copy_cpu=True)
+            self._pending = self._pool.submit(dcp.save, state, checkpoint_id=path, process_group=self._async_pg)
         else:
             dcp.save(self.states, checkpoint_id=path)
         logger.info(f"checkpoint step {step} issued in {time.perf_counter() - t0:.2f}s -> {path}")
@@ -245,21 +253,28 @@ class CheckpointManager(Configurable):
             self._pool.shutdown(wait=True)
 
 
-def _to_pinned_host(obj: Any) -> Any:
+def _to_pinned_host(obj: Any, pin: bool = True, copy_cpu: bool = False) -> Any:
+    """Host copy of a (nested) state dict: device tensors (and, with ``copy_cpu``, host
+    tensors too) are copied into fresh, optionally pinned, host buffers. DTensors keep their
+    global shape and stride, which matters for uneven shards (dim 0 not divisible by the
+    mesh size), where the shape inferred from the local piece would be wrong."""
     if torch.is_tensor(obj):
-        local = obj.to_local() if hasattr(obj, "to_local") else obj
-        if local.is_cuda:
-            h = torch.empty(local.shape, dtype=local.dtype, pin_memory=True)
-            h.copy_(local, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
-            if hasattr(obj, "to_local"):
+        is_dt = hasattr(obj, "to_local")
+        local = obj.to_local() if is_dt else obj
+        if local.is_cuda or copy_cpu:
+            h = torch.empty(local.shape, dtype=local.dtype, pin_memory=pin and local.is_cuda)
+            h.copy_(local, non_blocking=local.is_cuda)
+            if local.is_cuda:
+                torch.cuda.current_stream().synchronize()
+            if is_dt:
                 from torch.distributed.tensor import DTensor
 
-                return DTensor.from_local(h, obj.device_mesh, obj.placements, run_check=False)
+                return DTensor.from_local(h, obj.device_mesh, obj.placements, run_check=False,
+                                          shape=obj.shape, stride=obj.stride())
             return h
         return obj
     if isinstance(obj, dict):
-        return {k: _to_pinned_host(v) for k, v in obj.items()}
+        return {k: _to_pinned_host(v, pin, copy_cpu) for k, v in obj.items()}
     if isinstance(obj, list):
-        return [_to_pinned_host(v) for v in obj]
+        return [_to_pinned_host(v, pin, copy_cpu) for v in obj]
     return obj
