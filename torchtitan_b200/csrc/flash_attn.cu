@@ -493,6 +493,14 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
       : "memory");
 }
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // D[tmem] (+)= A[tmem] * B[smem desc]
@@ -505,8 +513,15 @@ __device__ __forceinline__ void umma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a, u
       "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate));
 }
 
+constexpr int FWD2_THREADS = 384;  // warpgroup 0: producer, MMA, 2 idle; warpgroups 1, 2: softmax
+
+// 384 threads x 168 registers at launch >= 128 x (80 + 208 + 208): the softmax warpgroups hold
+// a whole 128-column score row in registers
+__device__ __forceinline__ void regs_dec_ctrl() { asm volatile("setmaxnreg.dec.sync.aligned.u32 80;"); }
+__device__ __forceinline__ void regs_inc_softmax() { asm volatile("setmaxnreg.inc.sync.aligned.u32 208;"); }
+
 template <int DQK, int DV>
-__global__ void __maxnreg__(192)
+__global__ void __launch_bounds__(FWD2_THREADS, 1)
     attn_fwd2_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, Params p) {
   using C = Cfg2<DQK, DV>;
@@ -555,6 +570,7 @@ __global__ void __maxnreg__(192)
   const uint32_t tmem = bar.tmem_base;
 
   if (warp == 0) {
+    regs_dec_ctrl();
     if (lane == 0 && nkv > 0) {
       mbar_arrive_expect_tx(&bar.q_full, 2 * C::Q_BYTES);
 #pragma unroll
@@ -582,31 +598,41 @@ __global__ void __maxnreg__(192)
       }
     }
   } else if (warp == 1) {
+    regs_dec_ctrl();
     if (lane == 0 && nkv > 0) {
       constexpr uint32_t idesc_s = umma_idesc_bf16(BM, BN, false, false);
       constexpr uint32_t idesc_pv = umma_idesc_bf16(BM, DV, false, true);
       bool ok = mbar_wait(&bar.q_full, 0, &bar.abort_flag, &g_err, 52);
+      // Ping-pong order: S_0(0) S_1(0) | PV_0(j) S_0(j+1) PV_1(j) S_1(j+1) | ...  While one
+      // tile's softmax warps work on S_t(j+1), the tensor cores run the other tile's PV and S.
+      // S_t(j+1) overwrites the columns PV_t(j) reads P_t(j) from; tcgen05.mma ops issued by
+      // one thread execute in issue order, so the read precedes the overwrite.
+      int k_ready = -1;
+      auto need_k = [&](int j) -> bool {
+        if (k_ready >= j) return true;
+        k_ready = j;
+        return mbar_wait(&bar.k_full[j & 1], (j >> 1) & 1, &bar.abort_flag, &g_err, 53);
+      };
+      auto issue_s = [&](int t, int j) {
+        const uint32_t k_addr = smem_u32(smem + C::K_OFF + (j & 1) * C::K_BYTES);
+        const uint32_t q_addr = smem_u32(smem + C::Q_OFF + t * C::Q_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < DQK / 16; ++kk) {
+          const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+          umma_bf16(tmem + t * 256, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&bar.s_full[t]);
+      };
+      if (ok) ok = need_k(0);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < 2; ++t)
+          if (nkv_t[t] > 0) issue_s(t, 0);
+        umma_commit(&bar.k_empty[0]);
+      }
       for (int j = 0; ok && j < nkv; ++j) {
         const int st = j & 1;
-        if (!mbar_wait(&bar.k_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 53)) break;
-        const uint32_t k_addr = smem_u32(smem + C::K_OFF + st * C::K_BYTES);
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          if (j >= nkv_t[t]) continue;
-          // S_t is overwritten: the previous PV_t (reading P_t from these columns) must be done
-          if (j > 0 && !mbar_wait(&bar.pv_done[t], (j - 1) & 1, &bar.abort_flag, &g_err, 54)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t q_addr = smem_u32(smem + C::Q_OFF + t * C::Q_BYTES);
-#pragma unroll
-          for (int kk = 0; kk < DQK / 16; ++kk) {
-            const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
-            umma_bf16(tmem + t * 256, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
-          }
-          umma_commit(&bar.s_full[t]);
-        }
-        if (!ok) break;
-        umma_commit(&bar.k_empty[st]);
         if (!mbar_wait(&bar.v_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 55)) break;
         const uint32_t v_addr = smem_u32(smem + C::V_OFF + st * C::V_BYTES);
 #pragma unroll
@@ -620,13 +646,22 @@ __global__ void __maxnreg__(192)
             umma_bf16_ts(tmem + t * 256 + 128, tmem + t * 256 + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&bar.pv_done[t]);
+          if (j + 1 < nkv_t[t]) {
+            if (!need_k(j + 1)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(t, j + 1);
+          }
         }
         if (!ok) break;
         umma_commit(&bar.v_empty[st]);
+        if (j + 1 < nkv) umma_commit(&bar.k_empty[(j + 1) & 1]);
       }
     }
+  } else if (warp < 4) {
+    regs_dec_ctrl();
   } else {
-    const int t = (warp - 2) >> 2;  // query tile of this warp
+    regs_inc_softmax();
+    const int t = (warp - 4) >> 2;  // query tile of this warp
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const int qrow = q0 + t * BM + r;
@@ -645,82 +680,71 @@ __global__ void __maxnreg__(192)
       tc_fence_after();
       const int k0 = j * BN;
       const bool need_mask = (p.causal && k0 + BN - 1 > qt0 + (p.Sk - p.Sq)) || (k0 + BN > p.Sk);
-      // pass 1: row max (S read 64 columns at a time to bound register use)
+      // S_t(j) row into registers once (four 32-column loads, one wait)
+      uint32_t sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c)
+        tmem_ld_32x32b_x32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
+      tmem_ld_wait();
+      if (need_mask) {  // keys k0 + e with e > lim are invisible (causal or past the end)
+        const int lim = p.causal ? min(p.Sk - 1, diag) - k0 : p.Sk - 1 - k0;
+#pragma unroll
+        for (int e = 0; e < BN; ++e)
+          if (e > lim) sv[e] = __float_as_uint(-INFINITY);
+      }
       float mc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sv[64];
-        tmem_ld_32x32b_x32(s_col + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld_32x32b_x32(s_col + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tmem_ld_wait();
-        if (need_mask) {
+      for (int e = 0; e < BN; e += 8) {
 #pragma unroll
-          for (int e = 0; e < 64; ++e) {
-            const int key = k0 + half * 64 + e;
-            if (key >= p.Sk || (p.causal && key > diag)) sv[e] = __float_as_uint(-INFINITY);
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < 64; e += 8) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            mc[u] = max3(mc[u], __uint_as_float(sv[e + 2 * u]), __uint_as_float(sv[e + 2 * u + 1]));
-        }
+        for (int u = 0; u < 4; ++u)
+          mc[u] = max3(mc[u], __uint_as_float(sv[e + 2 * u]), __uint_as_float(sv[e + 2 * u + 1]));
       }
       const float cand = max3(mc[0], mc[1], fmaxf(mc[2], mc[3])) * c2;
       // lazy rescale: only when the max grows by more than 8 (P stays <= 2^8)
       const bool grow = cand > (m_used == -INFINITY ? -INFINITY : m_used + 8.f);
-      if (__any_sync(0xffffffffu, grow)) {
+      const bool rescale = __any_sync(0xffffffffu, grow);
+      float alpha = 1.f;
+      if (rescale) {
         const float m_new = fmaxf(m_used, cand);
-        const float alpha = (m_used == -INFINITY || m_new == -INFINITY) ? 0.f : ex2(m_used - m_new);
+        alpha = (m_used == -INFINITY || m_new == -INFINITY) ? 0.f : ex2(m_used - m_new);
         l_run *= alpha;
-        if (j > 0) {  // O_t holds PV of earlier tiles (complete: S_t was issued after it)
-          const uint64_t al = pk2(alpha, alpha);
-#pragma unroll
-          for (int c = 0; c < DV / 32; ++c) {
-            uint32_t ov[32];
-            tmem_ld_32x32b_x32(o_col + c * 32, ov);
-            tmem_ld_wait();
-#pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              float a0, a1;
-              up2(mul2(pk2(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])), al), a0, a1);
-              ov[e] = __float_as_uint(a0);
-              ov[e + 1] = __float_as_uint(a1);
-            }
-            tmem_st_32x32b_x32(o_col + c * 32, ov);
-          }
-          tmem_st_wait();
-        }
         m_used = m_new;
       }
       const float m_eff = (m_used == -INFINITY) ? 0.f : m_used;
       const uint64_t cc = pk2(c2, c2), nm = pk2(-m_eff, -m_eff);
       uint64_t rs2 = pk2(0.f, 0.f);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t sv[64];
-        tmem_ld_32x32b_x32(s_col + half * 64, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld_32x32b_x32(s_col + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tmem_ld_wait();
-        if (need_mask) {
+      for (int qq = 0; qq < 4; ++qq) {
+        // P columns [qq*16, qq*16+16) hold keys [qq*32, qq*32+32) packed two per column
+        uint32_t pk[16];
 #pragma unroll
-          for (int e = 0; e < 64; ++e) {
-            const int key = k0 + half * 64 + e;
-            if (key >= p.Sk || (p.causal && key > diag)) sv[e] = __float_as_uint(-INFINITY);
-          }
-        }
-        uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 64; e += 2) {
-          const uint64_t x = fma2(pk2(__uint_as_float(sv[e]), __uint_as_float(sv[e + 1])), cc, nm);
+        for (int e = 0; e < 32; e += 2) {
+          const int ee = qq * 32 + e;
+          const uint64_t x = fma2(pk2(__uint_as_float(sv[ee]), __uint_as_float(sv[ee + 1])), cc, nm);
           const uint64_t pv = ((e & 7) == 6) ? exp2_poly2(x) : ex2_mufu2(x);
           rs2 = add2(rs2, pv);
           pk[e / 2] = pack_bf16x2_u64(pv);
         }
-        // P columns [half*32, half*32+32) hold keys [half*64, half*64+64); S of those keys was
-        // already read (pass 2 reads half 0 before writing it; half 1 columns 64.. are untouched)
-        tmem_st_32x32b_x32(s_col + half * 32, pk);
+        tmem_st_32x32b_x16(s_col + qq * 16, pk);
+      }
+      // O_t rescale after P is written (the scores are no longer live): PV_t(j) is issued only
+      // after this warp's p_full arrival, and PV_t(j-1) is complete because S_t(j) is.
+      if (rescale && j > 0) {
+        const uint64_t al = pk2(alpha, alpha);
+#pragma unroll 1
+        for (int c = 0; c < DV / 32; ++c) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(o_col + c * 32, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            float a0, a1;
+            up2(mul2(pk2(__uint_as_float(ov[e]), __uint_as_float(ov[e + 1])), al), a0, a1);
+            ov[e] = __float_as_uint(a0);
+            ov[e + 1] = __float_as_uint(a1);
+          }
+          tmem_st_32x32b_x32(o_col + c * 32, ov);
+        }
       }
       tmem_st_wait();
       float ra, rb;
@@ -787,7 +811,7 @@ void launch_fwd2(const void* q, const void* k, const void* v, Params& p, cudaStr
   const CUtensorMap tv = make_tmap_bf16_3d(v, (uint64_t)p.Hk * DV, p.Sk, p.B, (uint64_t)p.Hk * DV,
                                            (uint64_t)p.Sk * p.Hk * DV, 64, C::BN, 1);
   const int grid = p.B * p.H * ((p.num_qtiles + 1) / 2);
-  kern<<<grid, NUM_THREADS, C::SMEM, s>>>(tq, tk, tv, p);
+  kern<<<grid, FWD2_THREADS, C::SMEM, s>>>(tq, tk, tv, p);
   check_cuda(cudaGetLastError(), "attn_fwd2 launch");
 }
 
