@@ -182,8 +182,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
   // heaviest (causal) tiles first
-  const int qt = p.num_qtiles - 1 - (blockIdx.x % p.num_qtiles);
-  const int bh = blockIdx.x / p.num_qtiles;
+  // heaviest (causal) tiles first across the whole grid: CTAs launch in index order
+  const int qt = p.num_qtiles - 1 - static_cast<int>(blockIdx.x / (p.B * p.H));
+  const int bh = blockIdx.x % (p.B * p.H);
   const int h = bh % p.H, b = bh / p.H;
   const int hk = h / (p.H / p.Hk);
   const int q0 = qt * BM;
@@ -534,8 +535,9 @@ __global__ void __launch_bounds__(FWD2_THREADS, 1)
   Bars2& bar = *reinterpret_cast<Bars2*>(smem + C::BAR_OFF);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int npairs = (p.num_qtiles + 1) / 2;
-  const int qp = npairs - 1 - (blockIdx.x % npairs);  // heaviest pairs first
-  const int bh = blockIdx.x / npairs;
+  // heaviest pairs first across the whole grid (CTAs launch in index order)
+  const int qp = npairs - 1 - static_cast<int>(blockIdx.x / (p.B * p.H));
+  const int bh = blockIdx.x % (p.B * p.H);
   const int h = bh % p.H, b = bh / p.H;
   const int hk = h / (p.H / p.Hk);
   const int q0 = qp * 2 * BM;
@@ -942,8 +944,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nkt = (p.Sk + C::BK - 1) / C::BK;
-  const int kt = blockIdx.x % nkt;
-  const int bhk = blockIdx.x / nkt;
+  // under a causal mask the first key tiles see the most queries: launch them first, grid-wide
+  const int kt = blockIdx.x / (p.B * p.Hk);
+  const int bhk = blockIdx.x % (p.B * p.Hk);
   const int hk = bhk % p.Hk, b = bhk / p.Hk;
   const int group = p.H / p.Hk;
   const int k0 = kt * C::BK;
@@ -1222,8 +1225,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int nqt = (p.Sq + C::BQ - 1) / C::BQ;
-  const int qt = nqt - 1 - (blockIdx.x % nqt);
-  const int bh = blockIdx.x / nqt;
+  const int qt = nqt - 1 - static_cast<int>(blockIdx.x / (p.B * p.H));  // heaviest first, grid-wide
+  const int bh = blockIdx.x % (p.B * p.H);
   const int h = bh % p.H, b = bh / p.H;
   const int hk = h / (p.H / p.Hk);
   const int q0 = qt * C::BQ;
