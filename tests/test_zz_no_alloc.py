@@ -49,6 +49,12 @@ def test_no_alloc_matches_regular_entry_point():
         torch.cuda.synchronize()
         assert abs(loss.item() - ref_loss.item()) <= 1e-3 * abs(ref_loss.item())
         assert ((lse - ref_lse).norm() / ref_lse.norm()).item() < 1e-5
+        # and against plain fp32 PyTorch on the same bf16 logits
+        x32 = logits.float()
+        f32_loss = torch.nn.functional.cross_entropy(x32, labels, ignore_index=-100, reduction="sum")
+        f32_lse = torch.logsumexp(x32, dim=-1)
+        assert abs(loss.item() - f32_loss.item()) <= 1e-3 * abs(f32_loss.item())
+        assert ((lse - f32_lse).norm() / f32_lse.norm()).item() < 1e-5
 
 
 def test_no_alloc_rejects_oversize():

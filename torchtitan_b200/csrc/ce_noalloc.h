@@ -18,6 +18,12 @@
 //     the same device) race and give wrong results; serialise them;
 //   * the scratch keeps the previous call's contents; nothing needs to start
 //     at zero because every row of the current call is written before it is read;
+//   * labels outside [0, V) that are not ignore_index count as ignored rows (loss 0),
+//     unlike torch.nn.functional.cross_entropy, which rejects them; validate labels first
+//     if that matters;
+//   * host-thread safety: the per-device address cache is atomic and the last CUDA error
+//     code is kept per host thread, so concurrent calls are safe on the host side (they
+//     still race on the GPU, see above);
 //   * the first call on each device resolves the scratch array's device address
 //     (cudaGetSymbolAddress with that device current); make that first call
 //     before any stream capture.
@@ -43,7 +49,7 @@ int ttb_ce_fwd_noalloc(const void* logits, const int64_t* labels, int64_t T, int
                        float* lse, float* loss_sum, cudaStream_t stream);
 
 int ttb_ce_fwd_noalloc_max_rows(void);
-int ttb_ce_fwd_noalloc_last_cuda_error(void);
+int ttb_ce_fwd_noalloc_last_cuda_error(void);  // of the calling host thread
 
 #ifdef __cplusplus
 }

@@ -104,7 +104,8 @@ __global__ void __launch_bounds__(NT) ce_bwd_kernel(const bf16* __restrict__ log
                                                     bf16* __restrict__ dlogits, int64_t V, int64_t ignore_index) {
   const int64_t row = blockIdx.x;
   const int64_t lab = labels[row];
-  const bool valid = lab != ignore_index;
+  // rows the forward counts as loss 0 (ignore_index or a label outside [0, V)) get zero gradient
+  const bool valid = lab != ignore_index && lab >= 0 && lab < V;
   const float g = valid ? gscale[0] : 0.f;
   const float L = lse[row];
   const bf16* x = logits + row * V;
@@ -151,6 +152,7 @@ void ce_bwd(const void* logits, const int64_t* labels, const float* lse, const f
 // Allocation-free variant (declared in ce_noalloc.h): the per-row loss scratch
 // is a fixed device array in this file instead of a buffer from the caller's
 // allocator.
+#include <atomic>
 #include <cstdio>
 
 #include "ce_noalloc.h"
@@ -160,8 +162,10 @@ namespace {
 static __device__ __align__(256) float g_ce_rows_scratch[TTB_CE_NOALLOC_MAX_ROWS];
 
 constexpr int kMaxDevices = 64;
-float* g_scratch_ptr[kMaxDevices] = {nullptr};  // device address per device, resolved once
-int g_last_cuda_error = 0;
+// device address of the scratch array per device, resolved once; atomics make concurrent first
+// calls from several host threads safe (both resolve the same address; either store wins)
+std::atomic<float*> g_scratch_ptr[kMaxDevices] = {};
+thread_local int g_last_cuda_error = 0;  // per host thread, so threads do not overwrite each other's code
 
 }  // namespace
 
@@ -184,7 +188,8 @@ extern "C" int ttb_ce_fwd_noalloc(const void* logits, const int64_t* labels, int
     g_last_cuda_error = static_cast<int>(e);
     return TTB_CE_NOALLOC_ECUDA;
   }
-  if (g_scratch_ptr[dev] == nullptr) {
+  float* rows = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (rows == nullptr) {
     // host code only knows a stand-in for the array; ask the runtime for its address on this device
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_ce_rows_scratch);
@@ -192,9 +197,9 @@ extern "C" int ttb_ce_fwd_noalloc(const void* logits, const int64_t* labels, int
       g_last_cuda_error = static_cast<int>(e);
       return TTB_CE_NOALLOC_ECUDA;
     }
-    g_scratch_ptr[dev] = static_cast<float*>(p);
+    rows = static_cast<float*>(p);
+    g_scratch_ptr[dev].store(rows, std::memory_order_release);
   }
-  float* rows = g_scratch_ptr[dev];
   if (T > 0)
     ttb::ce_fwd_kernel<<<static_cast<unsigned>(T), ttb::NT, 0, stream>>>(
         static_cast<const __nv_bfloat16*>(logits), labels, rows, lse, V, ignore_index);
