@@ -33,18 +33,12 @@ def _single_process_env() -> None:
         s.close()
 
 
-def run(a, dist_env, max_over_ranks, ClockSampler, METRIC, BASELINE_TPS_PER_GPU):
-    _single_process_env()
-    import torch.distributed as dist
-    from torchtitan.components.checkpoint import CheckpointManager
+def synthetic_loader_config(vocab_size: int = 128256, seed: int = 1234):
+    """Config of a synthetic-token dataloader written against the reference's own
+    ``BaseDataLoader`` Configurable interface (there is no dataset on the box): uniform
+    tokens from a seeded generator per (rank, batch), pinned, yielded as
+    ``({"input": tokens[:, :-1]}, tokens[:, 1:])``."""
     from torchtitan.components.dataloader import BaseDataLoader
-    from torchtitan.components.metrics import MetricsProcessor
-    from torchtitan.distributed import utils as dist_utils
-    from torchtitan.config import ActivationCheckpointConfig, CompileConfig, TrainingConfig
-    from torchtitan.models.llama3 import config_registry as reg
-    from torchtitan.models.llama3 import model_registry
-    from torchtitan.tools.logging import init_logger
-    from torchtitan.tools.profiling import ProfilingConfig
 
     class SyntheticTokens(BaseDataLoader):
         @dataclass(kw_only=True, slots=True)
@@ -60,7 +54,9 @@ def run(a, dist_env, max_over_ranks, ClockSampler, METRIC, BASELINE_TPS_PER_GPU)
         def __iter__(self):
             while True:
                 g = torch.Generator().manual_seed(self.config.seed * 1_000_003 + self.rank * 7919 + self.i)
-                t = torch.randint(0, self.config.vocab_size, (self.bs, self.seq + 1), generator=g).pin_memory()
+                t = torch.randint(0, self.config.vocab_size, (self.bs, self.seq + 1), generator=g)
+                if torch.cuda.is_available():
+                    t = t.pin_memory()
                 self.i += 1
                 yield {"input": t[:, :-1]}, t[:, 1:]
 
@@ -69,6 +65,21 @@ def run(a, dist_env, max_over_ranks, ClockSampler, METRIC, BASELINE_TPS_PER_GPU)
 
         def load_state_dict(self, sd):
             self.i = sd.get("i", 0)
+
+    return SyntheticTokens.Config(vocab_size=vocab_size, seed=seed)
+
+
+def run(a, dist_env, max_over_ranks, ClockSampler, METRIC, BASELINE_TPS_PER_GPU):
+    _single_process_env()
+    import torch.distributed as dist
+    from torchtitan.components.checkpoint import CheckpointManager
+    from torchtitan.components.metrics import MetricsProcessor
+    from torchtitan.distributed import utils as dist_utils
+    from torchtitan.config import ActivationCheckpointConfig, CompileConfig, TrainingConfig
+    from torchtitan.models.llama3 import config_registry as reg
+    from torchtitan.models.llama3 import model_registry
+    from torchtitan.tools.logging import init_logger
+    from torchtitan.tools.profiling import ProfilingConfig
 
     init_logger()
     rank, world, local = dist_env()
@@ -79,7 +90,7 @@ def run(a, dist_env, max_over_ranks, ClockSampler, METRIC, BASELINE_TPS_PER_GPU)
     cfg.profiling = ProfilingConfig(enable_profiling=False)
     cfg.metrics = MetricsProcessor.Config(log_freq=10 ** 9, enable_tensorboard=False)
     cfg.training = TrainingConfig(local_batch_size=1, seq_len=a.seq_len, steps=a.warmup + 2 * a.steps + 2)
-    cfg.dataloader = SyntheticTokens.Config()
+    cfg.dataloader = synthetic_loader_config()
     cfg.checkpoint = CheckpointManager.Config(enable=False)
     cfg.activation_checkpoint = ActivationCheckpointConfig(mode=a.ac)
     cfg.validator.enable = False
