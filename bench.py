@@ -36,6 +36,8 @@ def _parse():
     ap.add_argument("--seq-len", type=int, default=8192)
     ap.add_argument("--flavor", default="8B")
     ap.add_argument("--ac", default="selective")
+    ap.add_argument("--sac-option", default="op_all_mm",
+                    help="per-op SAC variant of this framework's arm: op_all_mm keeps every GEMM output")
     ap.add_argument("--profile-out", default=None, help="write a per-kernel time table of one extra step here")
     return ap.parse_args()
 
@@ -131,7 +133,7 @@ def run_ours(a):
     cfg.model_spec = model_registry(a.flavor)
     cfg.training = TrainingConfig(local_batch_size=1, seq_len=a.seq_len, steps=a.warmup + 2 * a.steps + 2,
                                   dtype="float32", mixed_precision_param="bfloat16")
-    cfg.activation_checkpoint = ActivationCheckpointConfig(mode=a.ac)
+    cfg.activation_checkpoint = ActivationCheckpointConfig(mode=a.ac, selective_ac_option=a.sac_option)
     cfg.metrics = MetricsProcessor.Config(log_freq=10 ** 9)
     cfg.checkpoint = CheckpointManager.Config(enable=False)
     cfg.validator.enable = False
@@ -209,7 +211,7 @@ def run_ours(a):
                                    if getattr(trainer.model_parts[0], "_dp_runtime", None) is not None
                                    else "single GPU (bf16 compute weights, fp32 masters in the fused AdamW; no sharding)"
                                    if world == 1
-                                   else f"fsdp{world} (reshard_after_forward={cfg.parallelism.fsdp_reshard_after_forward})"), "ac": a.ac, "optimizer": "AdamW (fused, fp32 master)",
+                                   else f"fsdp{world} (reshard_after_forward={cfg.parallelism.fsdp_reshard_after_forward})"), "ac": a.ac if a.ac != "selective" else f"selective ({a.sac_option})", "optimizer": "AdamW (fused, fp32 master)",
                    "l2": "inputs larger than L2 (no flush)"},
         "mfu_pct": round(mfu, 2),
         "tokens_per_sec_per_gpu": round(value / world, 1),

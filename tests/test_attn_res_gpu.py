@@ -1,14 +1,12 @@
 """The fused block attention-residual kernel (``csrc/attn_res.cu``) against the PyTorch
-formulation, forward and backward (inputs, pseudo-query and norm weight).  New kernel, not
-yet run on a B200: opt in with TTB_ATTNRES_KERNEL_TESTS=1."""
+formulation, forward and backward (inputs, pseudo-query and norm weight).  The kernel is the
+default on CUDA (TTB_ATTNRES_KERNEL=0 selects PyTorch)."""
 import os
 
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TTB_ATTNRES_KERNEL_TESTS") != "1",
-                                 reason="attn-res kernel not yet validated on a B200; opt in explicitly")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("nb,D", [(1, 256), (5, 2304), (9, 4096)])

@@ -1,14 +1,12 @@
 """KDA short causal conv + SiLU and gated RMSNorm kernels (``csrc/kda_eltwise.cu``) against
-the PyTorch formulations, forward and backward.  New kernels, not yet run on a B200: opt in
-with TTB_KDA_ELTWISE_TESTS=1."""
+the PyTorch formulations, forward and backward.  The kernels are the default
+on CUDA (TTB_KDA_ELTWISE=0 selects PyTorch)."""
 import os
 
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TTB_KDA_ELTWISE_TESTS") != "1",
-                                 reason="KDA element-wise kernels not yet validated on a B200; opt in explicitly")]
+pytestmark = pytest.mark.gpu
 
 
 def _both(fn, args, monkeypatch, grads_of):

@@ -1,14 +1,12 @@
 """The fused routing-selection kernel (``csrc/router_topk.cu``) against the PyTorch router:
-same experts chosen (as sets per token) and the same per-expert counts.  New kernel, not yet
-run on a B200: opt in with TTB_ROUTER_KERNEL_TESTS=1."""
+same experts chosen (as sets per token) and the same per-expert counts.  The kernel is the
+default on CUDA (TTB_ROUTER_KERNEL=0 selects PyTorch)."""
 import os
 
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("TTB_ROUTER_KERNEL_TESTS") != "1",
-                                 reason="router kernel not yet validated on a B200; opt in explicitly")]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("E,k,score,groups", [(8, 2, "softmax", None), (64, 8, "sigmoid", None),

@@ -69,7 +69,8 @@ class ParallelismConfig:
 class ActivationCheckpointConfig:
     mode: Literal["selective", "full", "memory_budget", "none"] = "selective"
     selective_ac_option: str = "op"
-    """``op`` for per-op SAC, or an integer N to checkpoint every N-th block."""
+    """``op`` for per-op SAC (every second GEMM output kept), ``op_all_mm`` for per-op SAC that
+    keeps every GEMM output, or an integer N to checkpoint every N-th block."""
     per_op_sac_force_recompute_mm_shapes_by_fqns: list[str] = field(
         default_factory=lambda: ["moe.router.gate"]
     )

@@ -46,7 +46,7 @@ class _AttnResMix(torch.autograd.Function):
 def _attn_res_kernel_ok(vs: list[torch.Tensor], query: torch.Tensor, norm) -> bool:
     import os
 
-    if os.environ.get("TTB_ATTNRES_KERNEL") != "1":  # opt-in until it has run on a B200
+    if os.environ.get("TTB_ATTNRES_KERNEL", "1") == "0":  # TTB_ATTNRES_KERNEL=0 selects PyTorch
         return False
     w = norm.weight
     return (vs[0].is_cuda and all(v.dtype == torch.bfloat16 and v.shape == vs[0].shape for v in vs)

@@ -44,10 +44,10 @@ class _AuxLossInjector(torch.autograd.Function):
 
 
 def _router_kernel_enabled() -> bool:
-    # csrc/router_topk.cu is opt-in until it has run on a B200
+    # csrc/router_topk.cu by default (validated on a B200); TTB_ROUTER_KERNEL=0 selects PyTorch
     import os
 
-    return os.environ.get("TTB_ROUTER_KERNEL") == "1"
+    return os.environ.get("TTB_ROUTER_KERNEL", "1") != "0"
 
 
 class TokenChoiceTopKRouter(nn.Module):

@@ -134,8 +134,8 @@ def sliding_window_attention_lse(q, k, v, window: int, scale: float):
 def _chunked_window_enabled(q: torch.Tensor) -> bool:
     import os
 
-    # on a GPU opt-in (TTB_SWA_CHUNKED=1) until it has run on a B200
-    return not q.is_cuda or os.environ.get("TTB_SWA_CHUNKED") == "1"
+    # default everywhere; TTB_SWA_CHUNKED=0 selects the masked-softmax reference on a GPU
+    return not q.is_cuda or os.environ.get("TTB_SWA_CHUNKED", "1") != "0"
 
 
 class GptOssAttention(nn.Module):

@@ -266,10 +266,10 @@ def naive_recurrent_kda(q, k, v, g, beta, scale=None, use_qk_l2norm: bool = True
 
 
 def _eltwise_kernels(x: torch.Tensor) -> bool:
-    # csrc/kda_eltwise.cu is opt-in until it has run on a B200
+    # csrc/kda_eltwise.cu by default on CUDA; TTB_KDA_ELTWISE=0 selects the PyTorch formulation
     import os
 
-    return x.is_cuda and x.dtype == torch.bfloat16 and os.environ.get("TTB_KDA_ELTWISE") == "1"
+    return x.is_cuda and x.dtype == torch.bfloat16 and os.environ.get("TTB_KDA_ELTWISE", "1") != "0"
 
 
 class _ShortConv(torch.autograd.Function):
