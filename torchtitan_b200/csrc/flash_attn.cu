@@ -906,15 +906,13 @@ struct DKVCfg {
   static constexpr int V_BYTES = BK * DV * 2;
   static constexpr int Q_BYTES = BQ * DQK * 2;
   static constexpr int O_BYTES = BQ * DV * 2;  // dO tile
-  static constexpr int P_BYTES = BK * BQ * 2;
   static constexpr int K_OFF = 0;
   static constexpr int V_OFF = K_OFF + K_BYTES;
   static constexpr int Q_OFF = V_OFF + V_BYTES;
-  static constexpr int QS = (DQK > 128) ? 2 : 3;  // Q/dO stages: 3 hide the TMA latency where smem allows
+  // Q/dO ring depth: P^T and dS^T live in TMEM, so shared memory goes to prefetch
+  static constexpr int QS = (DQK > 128) ? 3 : (DQK > 64 ? 4 : 6);
   static constexpr int DO_OFF = Q_OFF + QS * Q_BYTES;
-  static constexpr int PT_OFF = DO_OFF + QS * O_BYTES;
-  static constexpr int DST_OFF = PT_OFF + 2 * P_BYTES;
-  static constexpr int SMEM = DST_OFF + 2 * P_BYTES + 1024;
+  static constexpr int SMEM = DO_OFF + QS * O_BYTES + 1024;
   static constexpr int ST_COL = 0;                 // NBUF x BQ
   static constexpr int DPT_COL = NBUF * BQ;        // NBUF x BQ
   static constexpr int DV_COL = 2 * NBUF * BQ;     // DV
@@ -922,16 +920,17 @@ struct DKVCfg {
   static_assert(DK_COL + DQK <= 512, "TMEM budget");
 };
 
+constexpr int kMaxQS = 6;
 struct DKVBars {
   uint64_t kv_full;
-  uint64_t qd_full[3], qd_empty[3];
+  uint64_t qd_full[kMaxQS], qd_empty[kMaxQS];
   uint64_t s_full[2], s_free[2];
-  uint64_t p_full[2], p_empty[2];
+  uint64_t p_full[2];
   uint64_t acc_full;
   uint32_t tmem_base;
   int abort_flag;
-  alignas(16) float lse2[3][64];  // lse (natural log) of the staged 64 queries (bulk-copied)
-  alignas(16) float dlt[3][64];   // delta of the staged 64 queries (bulk-copied)
+  alignas(16) float lse2[kMaxQS][64];  // lse (natural log) of the staged 64 queries (bulk-copied)
+  alignas(16) float dlt[kMaxQS][64];   // delta of the staged 64 queries (bulk-copied)
 };
 
 template <int DQK, int DV, int NBUF>
@@ -962,17 +961,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar.kv_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    static_assert(C::QS <= kMaxQS, "Q/dO ring");
+    for (int i = 0; i < C::QS; ++i) {
       mbar_init(&bar.qd_full[i], 1);
       mbar_init(&bar.qd_empty[i], 1);
-      if (i == 1) {
-        mbar_init(&bar.qd_full[2], 1);
-        mbar_init(&bar.qd_empty[2], 1);
-      }
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&bar.s_full[i], 1);
       mbar_init(&bar.s_free[i], NUM_SM_WARPS);
       mbar_init(&bar.p_full[i], NUM_SM_WARPS);
-      mbar_init(&bar.p_empty[i], 1);
     }
     mbar_init(&bar.acc_full, 1);
     bar.abort_flag = 0;
@@ -1025,37 +1022,37 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       constexpr uint32_t idesc_dk = umma_idesc_bf16(C::BK, DQK, false, true);     // dK += dS^T Q
       const uint32_t k_addr = smem_u32(smem + C::K_OFF), v_addr = smem_u32(smem + C::V_OFF);
       bool ok = mbar_wait(&bar.kv_full, 0, &bar.abort_flag, &g_err, 32);
+      // P^T and dS^T come from TMEM (packed bf16 written by the softmax warps over the columns of
+      // S^T and dP^T they read): queries [32h, 32h+32) of buffer sb sit at columns 32h..32h+15.
       auto issue_grads = [&](int i) -> bool {
         const int st = i & 1;
         const int sb = i % NBUF;
-        (void)sb;
         if (!mbar_wait(&bar.p_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 33)) return false;
         tc_fence_after();
-        const uint32_t pt = smem_u32(smem + C::PT_OFF + st * C::P_BYTES);
-        const uint32_t dst = smem_u32(smem + C::DST_OFF + st * C::P_BYTES);
         const int qs = i % C::QS;
         const uint32_t qa = smem_u32(smem + C::Q_OFF + qs * C::Q_BYTES);
         const uint32_t da = smem_u32(smem + C::DO_OFF + qs * C::O_BYTES);
+        const uint32_t pt = tmem + C::ST_COL + sb * C::BQ, dst = tmem + C::DPT_COL + sb * C::BQ;
 #pragma unroll
         for (int kk = 0; kk < C::BQ / 16; ++kk) {
-          const uint64_t a1 = umma_desc_sw128(pt + kk * 32, 16, 1024);
           const uint64_t b1 = umma_desc_sw128(da + kk * 2048, C::BQ * 128, 1024);
-          umma_bf16(tmem + C::DV_COL, a1, b1, idesc_dv, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + C::DV_COL, pt + (kk >> 1) * 32 + (kk & 1) * 8, b1, idesc_dv, (i > 0 || kk > 0) ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < C::BQ / 16; ++kk) {
-          const uint64_t a2 = umma_desc_sw128(dst + kk * 32, 16, 1024);
           const uint64_t b2 = umma_desc_sw128(qa + kk * 2048, C::BQ * 128, 1024);
-          umma_bf16(tmem + C::DK_COL, a2, b2, idesc_dk, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + C::DK_COL, dst + (kk >> 1) * 32 + (kk & 1) * 8, b2, idesc_dk, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bar.qd_empty[qs]);
-        umma_commit(&bar.p_empty[st]);
         return true;
       };
       for (int i = 0; ok && i < items; ++i) {
         const int qs = i % C::QS;
         const int sb = i % NBUF;
         if (!mbar_wait(&bar.qd_full[qs], (i / C::QS) & 1, &bar.abort_flag, &g_err, 34)) { ok = false; break; }
+        // one S/dP buffer: the gradient MMAs of step i-1 read P/dS from it, so they go first
+        // (tcgen05.mma ops of one thread execute in issue order)
+        if (NBUF == 1 && i > 0 && !issue_grads(i - 1)) { ok = false; break; }
         if (!mbar_wait(&bar.s_free[sb], ((i / NBUF) & 1) ^ 1, &bar.abort_flag, &g_err, 35)) { ok = false; break; }
         tc_fence_after();
         const uint32_t qa = smem_u32(smem + C::Q_OFF + qs * C::Q_BYTES);
@@ -1073,7 +1070,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           umma_bf16(tmem + C::DPT_COL + sb * C::BQ, a, bo, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar.s_full[sb]);
-        if (i > 0 && !issue_grads(i - 1)) { ok = false; break; }
+        // two buffers: the softmax of step i overlaps the gradient MMAs of step i-1
+        if (NBUF == 2 && i > 0 && !issue_grads(i - 1)) { ok = false; break; }
       }
       if (ok) ok = issue_grads(items - 1);
       if (ok) umma_commit(&bar.acc_full);
@@ -1084,7 +1082,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int r = q * 32 + lane;     // key row within the tile
     const int kidx = k0 + r;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const int t = threadIdx.x - 64;  // 0..255 among the softmax warps
     bool ok = true;
     for (int i = 0; i < items; ++i) {
       const int st = i & 1;
@@ -1094,11 +1091,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // lse / delta of this query tile arrive with the Q/dO tiles
       const int qs = i % C::QS;
       if (!mbar_wait(&bar.qd_full[qs], (i / C::QS) & 1, &bar.abort_flag, &g_err, 39)) { ok = false; break; }
+      // S(i) complete implies the gradient MMAs of step i - NBUF (which read this buffer's P/dS)
+      // are complete too: they were issued before it
       if (!mbar_wait(&bar.s_full[sb], (i / NBUF) & 1, &bar.abort_flag, &g_err, 36)) { ok = false; break; }
-      if (!mbar_wait(&bar.p_empty[st], ((i >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 37)) { ok = false; break; }
       tc_fence_after();
-      uint8_t* pt = smem + C::PT_OFF + st * C::P_BYTES;
-      uint8_t* dst = smem + C::DST_OFF + st * C::P_BYTES;
       const bool need_mask = (kidx >= p.Sk) || (q0 + C::BQ > p.Sq) || (p.causal && k0 + C::BK - 1 > q0 + offset);
       {
         const int c = hh;
@@ -1128,15 +1124,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           pk[e / 2] = pack_bf16x2_u64(pv);
           dk[e / 2] = pack_bf16x2_u64(ds);
         }
-        const int chunk0 = (c * 32) / 8;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          store_sw128_chunk(pt, r, chunk0 + u, make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]));
-          store_sw128_chunk(dst, r, chunk0 + u, make_uint4(dk[4 * u], dk[4 * u + 1], dk[4 * u + 2], dk[4 * u + 3]));
-        }
+        // packed over the first half of the columns this warp just read
+        tmem_st_32x32b_x16(tmem + lane_base + C::ST_COL + sb * C::BQ + c * 32, pk);
+        tmem_st_32x32b_x16(tmem + lane_base + C::DPT_COL + sb * C::BQ + c * 32, dk);
+        tmem_st_wait();
       }
       tc_fence_before();
-      fence_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&bar.s_free[sb]);
@@ -1191,14 +1184,13 @@ struct DQCfg {
   static constexpr int O_BYTES = BQ * DV * 2;
   static constexpr int K_BYTES = BK * DQK * 2;
   static constexpr int V_BYTES = BK * DV * 2;
-  static constexpr int DS_BYTES = BQ * BK * 2;
   static constexpr int Q_OFF = 0;
   static constexpr int DO_OFF = Q_OFF + Q_BYTES;
   static constexpr int K_OFF = DO_OFF + O_BYTES;
-  static constexpr int KS = (DQK > 128) ? 2 : 4;  // K/V stages
+  // K/V ring depth (dS lives in TMEM, so shared memory goes to prefetch)
+  static constexpr int KS = (DQK > 128) ? 3 : (DQK > 64 ? 5 : 6);
   static constexpr int V_OFF = K_OFF + KS * K_BYTES;
-  static constexpr int DS_OFF = V_OFF + KS * V_BYTES;
-  static constexpr int SMEM = DS_OFF + 2 * DS_BYTES + 1024;
+  static constexpr int SMEM = V_OFF + KS * V_BYTES + 1024;
   static constexpr int S_COL = 0;          // 2 x BK
   static constexpr int DP_COL = 2 * BK;    // 2 x BK
   static constexpr int DQ_COL = 4 * BK;    // DQK
@@ -1207,9 +1199,9 @@ struct DQCfg {
 
 struct DQBars {
   uint64_t qd_full;
-  uint64_t kv_full[4], kv_empty[4];
+  uint64_t kv_full[6], kv_empty[6];
   uint64_t s_full[2], s_free[2];
-  uint64_t ds_full[2], ds_empty[2];
+  uint64_t ds_full[2];
   uint64_t acc_full;
   uint32_t tmem_base;
   int abort_flag;
@@ -1239,7 +1231,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar.qd_full, 1);
-    for (int i = 0; i < 4; ++i) {
+    static_assert(C::KS <= 6, "K/V ring");
+    for (int i = 0; i < C::KS; ++i) {
       mbar_init(&bar.kv_full[i], 1);
       mbar_init(&bar.kv_empty[i], 1);
     }
@@ -1247,7 +1240,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&bar.s_full[i], 1);
       mbar_init(&bar.s_free[i], NUM_SM_WARPS);
       mbar_init(&bar.ds_full[i], NUM_SM_WARPS);
-      mbar_init(&bar.ds_empty[i], 1);
     }
     mbar_init(&bar.acc_full, 1);
     bar.abort_flag = 0;
@@ -1299,16 +1291,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (!mbar_wait(&bar.ds_full[st], (i >> 1) & 1, &bar.abort_flag, &g_err, 43)) return false;
         tc_fence_after();
         const int ks = i % C::KS;
-        const uint32_t ds = smem_u32(smem + C::DS_OFF + st * C::DS_BYTES);
+        // dS from TMEM: keys [32h, 32h+32) of buffer st packed at columns 32h..32h+15
+        const uint32_t ds = tmem + C::S_COL + st * C::BK;
         const uint32_t ka = smem_u32(smem + C::K_OFF + ks * C::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < C::BK / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(ds + kk * 32, 16, 1024);
           const uint64_t bb = umma_desc_sw128(ka + kk * 2048, C::BK * 128, 1024);
-          umma_bf16(tmem + C::DQ_COL, a, bb, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16_ts(tmem + C::DQ_COL, ds + (kk >> 1) * 32 + (kk & 1) * 8, bb, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bar.kv_empty[ks]);
-        umma_commit(&bar.ds_empty[st]);
         return true;
       };
       for (int j = 0; ok && j < nkv; ++j) {
@@ -1352,10 +1343,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int st = j & 1;
       const int k0 = j * C::BK;
       if (!mbar_wait(&bar.s_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 46)) { ok = false; break; }
-      if (!mbar_wait(&bar.ds_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 47)) { ok = false; break; }
+      // S(j) complete implies dQ(j-2), which read dS(j-2) from this buffer, is complete
       tc_fence_after();
       const bool need_mask = !qvalid || (k0 + C::BK > p.Sk) || (p.causal && k0 + C::BK - 1 > diag);
-      uint8_t* dsb = smem + C::DS_OFF + st * C::DS_BYTES;
       {
         const int c = hh;
         uint32_t sv[32], dv[32];
@@ -1378,13 +1368,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           pk[e / 2] = pack_bf16x2_u64(mul2(pv, add2(pk2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nd)));
         }
-        const int chunk0 = (c * 32) / 8;
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          store_sw128_chunk(dsb, r, chunk0 + u, make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]));
+        tmem_st_32x32b_x16(tmem + lane_base + C::S_COL + st * C::BK + c * 32, pk);  // over what it read
+        tmem_st_wait();
       }
       tc_fence_before();
-      fence_async_smem();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&bar.s_free[st]);
