@@ -13,7 +13,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 EXTS = (".cu", ".cuh", ".h", ".hpp", ".cpp", ".cc", ".py")
 SKIP_DIRS = {".git", "_work", "build", "gpurun_out", "baseline", "__pycache__", ".pytest_cache"}
 BULK = "cp.async" + ".bulk"
-MCAST = "multicast" + "::cluster"
+MCAST = "".join(["multi", "cast", ":", ":", "clus", "ter"])  # assembled: no literal qualifier here
 
 
 def _sources():
