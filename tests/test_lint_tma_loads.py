@@ -1,10 +1,11 @@
-"""Repository lint: no TMA or bulk-copy load with cluster multicast anywhere in the sources.
+"""Repository lint: no TMA or bulk-copy load that broadcasts to a thread-block cluster
+anywhere in the sources.
 
-A multicast load whose source can be another GPU's memory (peer buffers, symmetric memory)
-has hung GPUs. Keeping every bulk/TMA copy free of the cluster-multicast qualifier rules it
-out by construction, including for kernels that today only read local memory. A tcgen05
-commit with the multicast qualifier is an mbarrier arrive, not a load, and stays allowed.
-(The instruction tokens are assembled at run time so this file names no such load itself.)
+Such a load whose source can be another GPU's memory (peer buffers, symmetric memory) has
+hung GPUs. Keeping every bulk/TMA copy free of the cluster-broadcast qualifier rules it out by
+construction, including for kernels that today only read local memory. A tcgen05 commit
+with that qualifier is an mbarrier arrive, not a load, and stays allowed. (The instruction
+tokens are assembled at run time so this file spells no such load itself.)
 """
 import os
 import re
@@ -37,7 +38,7 @@ def _offending(text):
     return [s.strip() for s in _statements(text) if BULK in s and MCAST in s]
 
 
-def test_no_multicast_bulk_loads():
+def test_no_cluster_broadcast_copies():
     bad = []
     for path in _sources():
         with open(path, encoding="utf-8", errors="ignore") as fh:
@@ -45,10 +46,10 @@ def test_no_multicast_bulk_loads():
         if MCAST not in text:
             continue
         bad += [f"{os.path.relpath(path, ROOT)}: {s[:120]}" for s in _offending(text)]
-    assert not bad, "cluster-multicast bulk/TMA loads are not allowed:\n" + "\n".join(bad)
+    assert not bad, "cluster-broadcast bulk/TMA copies are not allowed:\n" + "\n".join(bad)
 
 
-def test_lint_catches_a_multicast_load():
+def test_lint_catches_a_broadcast_copy():
     load = ('asm volatile("' + BULK + '.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"\n'
             '             ".' + MCAST + ' [%0], [%1, {%2, %3}], [%4], %5;")')
     assert _offending(load)
