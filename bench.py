@@ -36,6 +36,8 @@ def _parse():
     ap.add_argument("--seq-len", type=int, default=8192)
     ap.add_argument("--flavor", default="8B")
     ap.add_argument("--ac", default="selective")
+    ap.add_argument("--dp-comm", default="auto", choices=["auto", "peer", "fsdp2"],
+                    help="data-parallel runtime of this framework's arm (auto: peer memory on one node)")
     ap.add_argument("--sac-option", default="op_all_mm",
                     help="per-op SAC variant of this framework's arm: op_all_mm keeps every GEMM output")
     ap.add_argument("--profile-out", default=None, help="write a per-kernel time table of one extra step here")
@@ -140,6 +142,7 @@ def run_ours(a):
     # where FSDP2 runs (8 ranks), keep the bf16 parameters gathered after the forward: 16 GB
     # per GPU buys back the backward's parameter all-gathers
     cfg.parallelism.fsdp_reshard_after_forward = os.environ.get("TTB_BENCH_RESHARD", "never")
+    cfg.parallelism.data_parallel_comm = a.dp_comm
     trainer = Trainer(cfg)
     it = trainer.batch_generator(trainer.dataloader)
     tokens_per_step = cfg.training.local_batch_size * cfg.training.seq_len * trainer.dp_degree

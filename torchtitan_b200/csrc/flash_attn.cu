@@ -28,6 +28,7 @@ namespace attn_impl {
 
 __device__ int g_err;
 
+
 // lse / delta rows are padded to a multiple of 64 queries (zero-filled by the
 // allocator) so 64-query slices can be bulk-copied without running off a row
 __host__ __device__ __forceinline__ int lse_stride(int Sq) { return (Sq + 63) / 64 * 64; }
@@ -152,6 +153,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2_u64(uint64_t v) {
   return pack_bf16x2(a, b);
 }
 
+// Advance a shared-memory descriptor by a byte offset (the start-address field holds bytes >> 4
+// and never carries: shared addresses stay below 2^18).  The base descriptor of a tile is built
+// once and every K-step adds a compile-time constant, which keeps the single MMA-issuing thread
+// from recomputing the whole descriptor per tcgen05.mma.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // number of KV tiles visible to query tile [q0, q0+BM)
@@ -255,8 +262,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t v_addr = smem_u32(smem + C::V_OFF + st * C::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(p_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024);
+          const uint64_t ad = desc_add(umma_desc_sw128(p_addr, 16, 1024), (kk >> 2) * (BM * 128) + (kk & 3) * 32);
+          const uint64_t bd = desc_add(umma_desc_sw128(v_addr, BN * 128, 1024), kk * 2048);
           umma_bf16(tmem + C::PV_COL + st * DV, ad, bd, idesc_pv, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar.pv_full[st]);
@@ -272,8 +279,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t k_addr = smem_u32(smem + C::K_OFF + st * C::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < DQK / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = desc_add(umma_desc_sw128(q_addr, 16, 1024), (kk >> 2) * (BM * 128) + (kk & 3) * 32);
+          const uint64_t bd = desc_add(umma_desc_sw128(k_addr, 16, 1024), (kk >> 2) * (BN * 128) + (kk & 3) * 32);
           umma_bf16(tmem + C::S_COL + st * BN, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar.s_full[st]);
@@ -620,8 +627,8 @@ __global__ void __launch_bounds__(FWD2_THREADS, 1)
         const uint32_t q_addr = smem_u32(smem + C::Q_OFF + t * C::Q_BYTES);
 #pragma unroll
         for (int kk = 0; kk < DQK / 16; ++kk) {
-          const uint64_t ad = umma_desc_sw128(q_addr + (kk >> 2) * (BM * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = umma_desc_sw128(k_addr + (kk >> 2) * (BN * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t ad = desc_add(umma_desc_sw128(q_addr, 16, 1024), (kk >> 2) * (BM * 128) + (kk & 3) * 32);
+          const uint64_t bd = desc_add(umma_desc_sw128(k_addr, 16, 1024), (kk >> 2) * (BN * 128) + (kk & 3) * 32);
           umma_bf16(tmem + t * 256, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar.s_full[t]);
@@ -644,7 +651,7 @@ __global__ void __launch_bounds__(FWD2_THREADS, 1)
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
-            const uint64_t bd = umma_desc_sw128(v_addr + kk * 2048, BN * 128, 1024);
+            const uint64_t bd = desc_add(umma_desc_sw128(v_addr, BN * 128, 1024), kk * 2048);
             umma_bf16_ts(tmem + t * 256 + 128, tmem + t * 256 + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&bar.pv_done[t]);
@@ -1035,12 +1042,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t pt = tmem + C::ST_COL + sb * C::BQ, dst = tmem + C::DPT_COL + sb * C::BQ;
 #pragma unroll
         for (int kk = 0; kk < C::BQ / 16; ++kk) {
-          const uint64_t b1 = umma_desc_sw128(da + kk * 2048, C::BQ * 128, 1024);
+          const uint64_t b1 = desc_add(umma_desc_sw128(da, C::BQ * 128, 1024), kk * 2048);
           umma_bf16_ts(tmem + C::DV_COL, pt + (kk >> 1) * 32 + (kk & 1) * 8, b1, idesc_dv, (i > 0 || kk > 0) ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < C::BQ / 16; ++kk) {
-          const uint64_t b2 = umma_desc_sw128(qa + kk * 2048, C::BQ * 128, 1024);
+          const uint64_t b2 = desc_add(umma_desc_sw128(qa, C::BQ * 128, 1024), kk * 2048);
           umma_bf16_ts(tmem + C::DK_COL, dst + (kk >> 1) * 32 + (kk & 1) * 8, b2, idesc_dk, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bar.qd_empty[qs]);
@@ -1059,14 +1066,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t da = smem_u32(smem + C::DO_OFF + qs * C::O_BYTES);
 #pragma unroll
         for (int kk = 0; kk < DQK / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(k_addr + (kk >> 2) * (C::BK * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bq = umma_desc_sw128(qa + (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t a = desc_add(umma_desc_sw128(k_addr, 16, 1024), (kk >> 2) * (C::BK * 128) + (kk & 3) * 32);
+          const uint64_t bq = desc_add(umma_desc_sw128(qa, 16, 1024), (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32);
           umma_bf16(tmem + C::ST_COL + sb * C::BQ, a, bq, idesc_s, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < DV / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(v_addr + (kk >> 2) * (C::BK * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bo = umma_desc_sw128(da + (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t a = desc_add(umma_desc_sw128(v_addr, 16, 1024), (kk >> 2) * (C::BK * 128) + (kk & 3) * 32);
+          const uint64_t bo = desc_add(umma_desc_sw128(da, 16, 1024), (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32);
           umma_bf16(tmem + C::DPT_COL + sb * C::BQ, a, bo, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar.s_full[sb]);
@@ -1296,7 +1303,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t ka = smem_u32(smem + C::K_OFF + ks * C::K_BYTES);
 #pragma unroll
         for (int kk = 0; kk < C::BK / 16; ++kk) {
-          const uint64_t bb = umma_desc_sw128(ka + kk * 2048, C::BK * 128, 1024);
+          const uint64_t bb = desc_add(umma_desc_sw128(ka, C::BK * 128, 1024), kk * 2048);
           umma_bf16_ts(tmem + C::DQ_COL, ds + (kk >> 1) * 32 + (kk & 1) * 8, bb, idesc_dq, (i > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(&bar.kv_empty[ks]);
@@ -1312,14 +1319,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const uint32_t va = smem_u32(smem + C::V_OFF + ks * C::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < DQK / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(qa + (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bb = umma_desc_sw128(ka + (kk >> 2) * (C::BK * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t a = desc_add(umma_desc_sw128(qa, 16, 1024), (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32);
+          const uint64_t bb = desc_add(umma_desc_sw128(ka, 16, 1024), (kk >> 2) * (C::BK * 128) + (kk & 3) * 32);
           umma_bf16(tmem + C::S_COL + st * C::BK, a, bb, idesc_s, kk > 0 ? 1u : 0u);
         }
 #pragma unroll
         for (int kk = 0; kk < DV / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(da + (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32, 16, 1024);
-          const uint64_t bb = umma_desc_sw128(va + (kk >> 2) * (C::BK * 128) + (kk & 3) * 32, 16, 1024);
+          const uint64_t a = desc_add(umma_desc_sw128(da, 16, 1024), (kk >> 2) * (C::BQ * 128) + (kk & 3) * 32);
+          const uint64_t bb = desc_add(umma_desc_sw128(va, 16, 1024), (kk >> 2) * (C::BK * 128) + (kk & 3) * 32);
           umma_bf16(tmem + C::DP_COL + st * C::BK, a, bb, idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit(&bar.s_full[st]);
