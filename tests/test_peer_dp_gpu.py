@@ -169,6 +169,7 @@ def _ep_peer(rank, world):
     from torchtitan_b200.ops._ext import ext
 
     assert ext().dp_error_code(True) == 0
+    assert ext().ep_error_code(True) == 0  # no peer row index fell outside its buffer
 
 
 @two_gpus

@@ -322,7 +322,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                 "sink: pinned host int32 tensor of >= 8 elements");
     ttb::dp_set_error_sink(sink.data_ptr());
   });
-  m.def("ep_scatter_rows", [](Tensor src, Tensor dest_rank, Tensor dest_row, std::vector<int64_t> bases) {
+  m.def("ep_scatter_rows", [](Tensor src, Tensor dest_rank, Tensor dest_row, std::vector<int64_t> bases,
+                              int64_t cap_rows) {
     check_cuda_bf16(src, "src");
     TORCH_CHECK(src.dim() == 2 && src.is_contiguous(), "src: contiguous [n, D]");
     TORCH_CHECK(dest_rank.scalar_type() == at::kInt && dest_row.scalar_type() == at::kLong, "index dtypes");
@@ -330,9 +331,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     c10::cuda::CUDAGuard g(src.device());
     ttb::ep_scatter_rows(src.data_ptr(), src.size(0), (int)src.size(1), dest_rank.data_ptr<int32_t>(),
                          dest_row.data_ptr<int64_t>(), reinterpret_cast<void* const*>(bases.data()),
-                         (int)bases.size(), stream());
+                         (int)bases.size(), cap_rows, stream());
   });
-  m.def("ep_gather_rows", [](Tensor dst, Tensor src_rank, Tensor src_row, std::vector<int64_t> bases) {
+  m.def("ep_gather_rows", [](Tensor dst, Tensor src_rank, Tensor src_row, std::vector<int64_t> bases,
+                             int64_t cap_rows) {
     check_cuda_bf16(dst, "dst");
     TORCH_CHECK(dst.dim() == 2 && dst.is_contiguous(), "dst: contiguous [n, D]");
     TORCH_CHECK(src_rank.scalar_type() == at::kInt && src_row.scalar_type() == at::kLong, "index dtypes");
@@ -340,8 +342,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     c10::cuda::CUDAGuard g(dst.device());
     ttb::ep_gather_rows(dst.data_ptr(), dst.size(0), (int)dst.size(1), src_rank.data_ptr<int32_t>(),
                         src_row.data_ptr<int64_t>(), reinterpret_cast<void* const*>(bases.data()),
-                        (int)bases.size(), stream());
+                        (int)bases.size(), cap_rows, stream());
   });
+  m.def("ep_error_code", &ttb::ep_error_code, "read (and optionally clear) the EP out-of-capacity row flag",
+        py::arg("reset") = true);
   m.def("mx_quantize", [](Tensor x) {
     check_cuda_bf16(x, "x");
     TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "mx_quantize: [R, C] with contiguous rows");

@@ -125,9 +125,10 @@ void router_topk(const float* logits, const float* bias, int64_t T, int E, int t
 
 // ep_comm.cu: expert-parallel row movement over NVLink peer memory
 void ep_scatter_rows(const void* src, int64_t n, int d, const int32_t* dest_rank, const int64_t* dest_row,
-                     void* const* peer_bases, int world, cudaStream_t s);
+                     void* const* peer_bases, int world, int64_t cap_rows, cudaStream_t s);
 void ep_gather_rows(void* dst, int64_t n, int d, const int32_t* src_rank, const int64_t* src_row,
-                    void* const* peer_bases, int world, cudaStream_t s);  // slot, epoch, source rank, flag value of the first failed wait
+                    void* const* peer_bases, int world, int64_t cap_rows, cudaStream_t s);
+int ep_error_code(bool reset);  // slot, epoch, source rank, flag value of the first failed wait
 
 struct SumSqTensor {
   const void* x;

@@ -266,10 +266,13 @@ def naive_recurrent_kda(q, k, v, g, beta, scale=None, use_qk_l2norm: bool = True
 
 
 def _eltwise_kernels(x: torch.Tensor) -> bool:
-    # csrc/kda_eltwise.cu by default on CUDA; TTB_KDA_ELTWISE=0 selects the PyTorch formulation
+    # csrc/kda_eltwise.cu by default on CUDA; TTB_KDA_ELTWISE=0 selects the PyTorch formulation.
+    # Its weight gradients are summed with fp32 atomics (order varies run to run), so under
+    # torch.use_deterministic_algorithms the PyTorch formulation runs instead.
     import os
 
-    return x.is_cuda and x.dtype == torch.bfloat16 and os.environ.get("TTB_KDA_ELTWISE", "1") != "0"
+    return (x.is_cuda and x.dtype == torch.bfloat16 and os.environ.get("TTB_KDA_ELTWISE", "1") != "0"
+            and not torch.are_deterministic_algorithms_enabled())
 
 
 class _ShortConv(torch.autograd.Function):

@@ -137,7 +137,7 @@ class EPPeerComm:
         self.barrier()  # every peer is done reading its matrix from the previous call
         self._ext.ep_scatter_rows(src, torch.arange(self.ep, dtype=torch.int32, device=counts.device),
                                   torch.full((self.ep,), self.me, dtype=torch.int64, device=counts.device),
-                                  self.cnt_ptrs)
+                                  self.cnt_ptrs, self.ep)
         self.barrier()
         return self.cnt.view(torch.int32)[:, :self.E].to(torch.int64).cpu()
 
@@ -155,7 +155,7 @@ class EPPeerComm:
             return out
         self._ensure_rows(rows.device, rows.shape[1], P_max)
         self.barrier()  # peers are done with this buffer's previous contents
-        self._ext.ep_scatter_rows(rows.contiguous(), dest_rank, dest_row, self.in_ptrs)
+        self._ext.ep_scatter_rows(rows.contiguous(), dest_rank, dest_row, self.in_ptrs, self.cap)
         self.barrier()  # every peer's rows have landed here
         return self.buf_in[:P].clone()
 
@@ -175,7 +175,7 @@ class EPPeerComm:
         self.buf_out[:local.shape[0]].copy_(local)
         self.barrier()  # every peer's outputs are exposed
         out = local.new_empty(src_row.shape[0], local.shape[1])
-        self._ext.ep_gather_rows(out, src_rank, src_row, self.out_ptrs)
+        self._ext.ep_gather_rows(out, src_rank, src_row, self.out_ptrs, self.cap)
         return out
 
 
