@@ -338,14 +338,18 @@ def test_attention_lse_output_and_gradient(D):
         torch.testing.assert_close(a, b, rtol=3e-2, atol=3e-2)
 
 
-def test_document_attention(ext):
-    """Packed documents (block-causal masking) through the flash kernel, one document per launch."""
+@pytest.mark.parametrize("S,lens,D", [(320, [[1, 37, 130, 152], [320]], 128),
+                                     (1000, [[300, 1, 255, 444], [129, 128, 743]], 64),
+                                     (777, [[500, 277], [1, 1, 775]], 96)])
+def test_document_attention(ext, S, lens, D):
+    """Packed documents: the block-causal mask applied inside the flash kernels (one launch,
+    per-token document start/end tables) against fp32 PyTorch with the dense mask, forward and
+    backward, for documents that start and end inside tiles."""
     from torchtitan_b200 import ops
     from torchtitan_b200.models.common.attention import document_causal_mask
 
     torch.manual_seed(9)
-    B, S, H, Hk, D = 2, 320, 4, 2, 128
-    lens = [[1, 37, 130, 152], [320]]
+    B, H, Hk = 2, 4, 2
     doc = torch.tensor([sum(([i] * n for i, n in enumerate(r)), []) for r in lens], device="cuda")
     q = torch.randn(B, S, H, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     k = torch.randn(B, S, Hk, D, device="cuda", dtype=torch.bfloat16, requires_grad=True)

@@ -237,7 +237,16 @@ void multi_clip_scale(std::vector<Tensor> xs, Tensor total, double max_norm) {
   ttb::multi_clip_scale(l.data(), (int)l.size(), total.data_ptr<float>(), static_cast<float>(max_norm), stream());
 }
 
-std::vector<Tensor> attn_fwd(Tensor q, Tensor k, Tensor v, bool causal, double scale) {
+// packed-document tables: int32 [B, S] on the device, contiguous
+static const int* doc_table(const c10::optional<Tensor>& t, int64_t B, int64_t S) {
+  if (!t.has_value()) return nullptr;
+  TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kInt && t->is_contiguous() && t->numel() == B * S,
+              "document table: contiguous int32 [B, S] on the device");
+  return t->data_ptr<int>();
+}
+
+std::vector<Tensor> attn_fwd(Tensor q, Tensor k, Tensor v, bool causal, double scale,
+                             c10::optional<Tensor> doc_start, c10::optional<Tensor> doc_end) {
   check_cuda_bf16(q, "q");
   check_cuda_bf16(k, "k");
   check_cuda_bf16(v, "v");
@@ -252,12 +261,14 @@ std::vector<Tensor> attn_fwd(Tensor q, Tensor k, Tensor v, bool causal, double s
   // rows padded to a multiple of 64 and zero-filled (the backward bulk-copies 64-query slices)
   Tensor lse = torch::zeros({B, H, (Sq + 63) / 64 * 64}, q.options().dtype(at::kFloat));
   ttb::attn_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(), B, Sq, Sk, H, Hk, Dqk,
-                Dv, causal, static_cast<float>(scale), stream());
+                Dv, causal, static_cast<float>(scale), stream(), doc_table(doc_start, B, Sq),
+                doc_table(doc_end, B, Sq));
   return {o, lse};
 }
 
 std::vector<Tensor> attn_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, bool causal,
-                             double scale, c10::optional<Tensor> dlse) {
+                             double scale, c10::optional<Tensor> dlse, c10::optional<Tensor> doc_start,
+                             c10::optional<Tensor> doc_end) {
   check_cuda_bf16(dout, "dout");
   const int B = q.size(0), Sq = q.size(1), H = q.size(2), Dqk = q.size(3);
   const int Sk = k.size(1), Hk = k.size(2), Dv = v.size(3);
@@ -270,7 +281,8 @@ std::vector<Tensor> attn_bwd(Tensor dout, Tensor q, Tensor k, Tensor v, Tensor o
   ttb::attn_bwd(dout.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr<float>(),
                 dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), nullptr, delta.data_ptr<float>(), B, Sq, Sk, H, Hk, Dqk,
                 Dv, causal, static_cast<float>(scale), stream(),
-                dlse.has_value() ? dlse->data_ptr<float>() : nullptr);
+                dlse.has_value() ? dlse->data_ptr<float>() : nullptr, doc_table(doc_start, B, Sq),
+                doc_table(doc_end, B, Sq));
   return {dq, dk, dv};
 }
 
@@ -553,7 +565,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   });
   m.def("multi_sumsq", &multi_sumsq, "sum of squares over a list of fp32/bf16 tensors");
   m.def("multi_clip_scale", &multi_clip_scale, "scale tensors by min(1, max_norm/(sqrt(total)+1e-6))");
-  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_fwd", &attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("causal"), py::arg("scale"),
+        py::arg("doc_start") = py::none(), py::arg("doc_end") = py::none());
   m.def("attn_bwd", &attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"),
-        py::arg("lse"), py::arg("causal"), py::arg("scale"), py::arg("dlse") = py::none());
+        py::arg("lse"), py::arg("causal"), py::arg("scale"), py::arg("dlse") = py::none(),
+        py::arg("doc_start") = py::none(), py::arg("doc_end") = py::none());
 }

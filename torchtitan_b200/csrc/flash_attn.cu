@@ -71,6 +71,10 @@ struct Params {
   __nv_bfloat16* o;
   float* lse;
   int num_qtiles;
+  // packed documents (self-attention, optional): per token, the first position of its document
+  // and one past its last; a query sees only keys of its own document
+  const int* doc_start;
+  const int* doc_end;
 };
 
 struct Bars {
@@ -548,9 +552,12 @@ __global__ void __launch_bounds__(FWD2_THREADS, 1)
   const int h = bh % p.H, b = bh / p.H;
   const int hk = h / (p.H / p.Hk);
   const int q0 = qp * 2 * BM;
+  // KV tiles j0 .. j0 + nkv_t[t] - 1: with packed documents the pair starts at the document of
+  // its first query (documents are contiguous, so later rows start no earlier)
+  const int j0 = p.doc_start != nullptr ? p.doc_start[static_cast<size_t>(b) * p.Sq + q0] / BN : 0;
   int nkv_t[2];
-  nkv_t[0] = kv_tiles(p, q0, BN);
-  nkv_t[1] = (q0 + BM < p.Sq) ? kv_tiles(p, q0 + BM, BN) : 0;
+  nkv_t[0] = max(kv_tiles(p, q0, BN) - j0, 0);
+  nkv_t[1] = (q0 + BM < p.Sq) ? max(kv_tiles(p, q0 + BM, BN) - j0, 0) : 0;
   const int nkv = max(nkv_t[0], nkv_t[1]);
 
   if (threadIdx.x == 0) {
@@ -591,7 +598,7 @@ __global__ void __launch_bounds__(FWD2_THREADS, 1)
       for (int j = 0; j < nkv; ++j) {
         const int st = j & 1;
         if (!mbar_wait(&bar.k_empty[st], ((j >> 1) & 1) ^ 1, &bar.abort_flag, &g_err, 51)) break;
-        const int k0 = j * BN;
+        const int k0 = (j0 + j) * BN;
         mbar_arrive_expect_tx(&bar.k_full[st], C::K_BYTES);
 #pragma unroll
         for (int c = 0; c < DQK / 64; ++c)
@@ -680,6 +687,7 @@ __global__ void __launch_bounds__(FWD2_THREADS, 1)
     const uint32_t o_col = s_col + 128;
     const int diag = qrow + (p.Sk - p.Sq);
     const int qt0 = q0 + t * BM;
+    const int dstart = p.doc_start != nullptr ? p.doc_start[static_cast<size_t>(b) * p.Sq + min(qrow, p.Sq - 1)] : 0;
     const float c2 = p.scale_log2;
     float m_used = -INFINITY;  // max (log2 units) that P and O are currently normalised to
     float l_run = 0.f;
@@ -687,19 +695,20 @@ __global__ void __launch_bounds__(FWD2_THREADS, 1)
     for (int j = 0; j < nk; ++j) {
       if (!mbar_wait(&bar.s_full[t], j & 1, &bar.abort_flag, &g_err, 57)) { ok = false; break; }
       tc_fence_after();
-      const int k0 = j * BN;
+      const int k0 = (j0 + j) * BN;
       const bool need_mask = (p.causal && k0 + BN - 1 > qt0 + (p.Sk - p.Sq)) || (k0 + BN > p.Sk);
+      const int lo = dstart - k0;  // keys k0 + e with e < lo belong to earlier documents
       // S_t(j) row into registers once (four 32-column loads, one wait)
       uint32_t sv[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c)
         tmem_ld_32x32b_x32(s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[c * 32]));
       tmem_ld_wait();
-      if (need_mask) {  // keys k0 + e with e > lim are invisible (causal or past the end)
+      if (need_mask || lo > 0) {  // keys k0 + e with e > lim are invisible (causal or past the end)
         const int lim = p.causal ? min(p.Sk - 1, diag) - k0 : p.Sk - 1 - k0;
 #pragma unroll
         for (int e = 0; e < BN; ++e)
-          if (e > lim) sv[e] = __float_as_uint(-INFINITY);
+          if (e > lim || e < lo) sv[e] = __float_as_uint(-INFINITY);
       }
       float mc[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
@@ -897,6 +906,8 @@ struct BwdParams {
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   __nv_bfloat16* dq;
+  const int* doc_start;  // as in Params (optional)
+  const int* doc_end;
 };
 
 
@@ -963,7 +974,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int first_q = k0 - offset;  // smallest query that sees key k0
     qt_first = first_q <= 0 ? 0 : first_q / C::BQ;
   }
-  const int per_head = nqt > qt_first ? nqt - qt_first : 0;
+  int qt_last = nqt - 1;
+  if (p.doc_end != nullptr) {  // no query past the end of the last key's document sees this tile
+    const int kl = min(k0 + C::BK, p.Sk) - 1;
+    qt_last = min(qt_last, (p.doc_end[static_cast<size_t>(b) * p.Sk + kl] - 1) / C::BQ);
+  }
+  const int per_head = qt_last >= qt_first ? qt_last - qt_first + 1 : 0;
   const int items = per_head * group;
 
   if (threadIdx.x == 0) {
@@ -1088,6 +1104,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int hh = (warp - 2) >> 2;  // which 32-query half of the tile this warp handles
     const int r = q * 32 + lane;     // key row within the tile
     const int kidx = k0 + r;
+    const int dend = p.doc_end != nullptr ? p.doc_end[static_cast<size_t>(b) * p.Sk + min(kidx, p.Sk - 1)] : 0x7fffffff;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     bool ok = true;
     for (int i = 0; i < items; ++i) {
@@ -1102,7 +1119,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       // are complete too: they were issued before it
       if (!mbar_wait(&bar.s_full[sb], (i / NBUF) & 1, &bar.abort_flag, &g_err, 36)) { ok = false; break; }
       tc_fence_after();
-      const bool need_mask = (kidx >= p.Sk) || (q0 + C::BQ > p.Sq) || (p.causal && k0 + C::BK - 1 > q0 + offset);
+      const bool need_mask = (kidx >= p.Sk) || (q0 + C::BQ > p.Sq) || (p.causal && k0 + C::BK - 1 > q0 + offset) ||
+                             (q0 + C::BQ > dend);
       {
         const int c = hh;
         uint32_t sv[32], dv[32];
@@ -1123,8 +1141,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             float a0, a1;
             up2(pv, a0, a1);
             const int qi = q0 + col;
-            if (kidx >= p.Sk || qi >= p.Sq || (p.causal && kidx > qi + offset)) a0 = 0.f;
-            if (kidx >= p.Sk || qi + 1 >= p.Sq || (p.causal && kidx > qi + 1 + offset)) a1 = 0.f;
+            if (kidx >= p.Sk || qi >= p.Sq || qi >= dend || (p.causal && kidx > qi + offset)) a0 = 0.f;
+            if (kidx >= p.Sk || qi + 1 >= p.Sq || qi + 1 >= dend || (p.causal && kidx > qi + 1 + offset)) a1 = 0.f;
             pv = pk2(a0, a1);
           }
           const uint64_t ds = mul2(pv, add2(pk2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), pk2(-dl.x, -dl.y)));
@@ -1235,6 +1253,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int last_key = q0 + C::BQ - 1 + offset;
     nkv = last_key < 0 ? 0 : min(nkv, last_key / C::BK + 1);
   }
+  // packed documents: key tiles start at the document of the tile's first query
+  const int j0 = p.doc_start != nullptr ? p.doc_start[static_cast<size_t>(b) * p.Sq + q0] / C::BK : 0;
+  nkv = max(nkv - j0, 0);
 
   if (threadIdx.x == 0) {
     mbar_init(&bar.qd_full, 1);
@@ -1280,11 +1301,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
         for (int c = 0; c < DQK / 64; ++c)
           tma_load_3d(smem + C::K_OFF + st * C::K_BYTES + c * (C::BK * 128), &tk, &bar.kv_full[st], hk * DQK + c * 64,
-                      j * C::BK, b);
+                      (j0 + j) * C::BK, b);
 #pragma unroll
         for (int c = 0; c < DV / 64; ++c)
           tma_load_3d(smem + C::V_OFF + st * C::V_BYTES + c * (C::BK * 128), &tv, &bar.kv_full[st], hk * DV + c * 64,
-                      j * C::BK, b);
+                      (j0 + j) * C::BK, b);
       }
     }
   } else if (warp == 1) {
@@ -1345,14 +1366,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const float lse2 = qvalid ? p.lse[((size_t)b * p.H + h) * lse_stride(p.Sq) + qi] * 1.4426950408889634f : INFINITY;
     const float dl = qvalid ? p.delta[((size_t)b * p.H + h) * lse_stride(p.Sq) + qi] : 0.f;
     const int diag = qi + offset;
+    const int dstart = p.doc_start != nullptr ? p.doc_start[static_cast<size_t>(b) * p.Sq + min(qi, p.Sq - 1)] : 0;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int st = j & 1;
-      const int k0 = j * C::BK;
+      const int k0 = (j0 + j) * C::BK;
       if (!mbar_wait(&bar.s_full[st], (j >> 1) & 1, &bar.abort_flag, &g_err, 46)) { ok = false; break; }
       // S(j) complete implies dQ(j-2), which read dS(j-2) from this buffer, is complete
       tc_fence_after();
-      const bool need_mask = !qvalid || (k0 + C::BK > p.Sk) || (p.causal && k0 + C::BK - 1 > diag);
+      const bool need_mask = !qvalid || (k0 + C::BK > p.Sk) || (p.causal && k0 + C::BK - 1 > diag) || (k0 < dstart);
       {
         const int c = hh;
         uint32_t sv[32], dv[32];
@@ -1369,8 +1391,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             float a0, a1;
             up2(pv, a0, a1);
             const int key = k0 + c * 32 + e;
-            if (!qvalid || key >= p.Sk || (p.causal && key > diag)) a0 = 0.f;
-            if (!qvalid || key + 1 >= p.Sk || (p.causal && key + 1 > diag)) a1 = 0.f;
+            if (!qvalid || key >= p.Sk || key < dstart || (p.causal && key > diag)) a0 = 0.f;
+            if (!qvalid || key + 1 >= p.Sk || key + 1 < dstart || (p.causal && key + 1 > diag)) a1 = 0.f;
             pv = pk2(a0, a1);
           }
           pk[e / 2] = pack_bf16x2_u64(mul2(pv, add2(pk2(__uint_as_float(dv[e]), __uint_as_float(dv[e + 1])), nd)));
@@ -1455,10 +1477,15 @@ void launch_bwd(const void* dout, const void* q, const void* k, const void* v, B
 }  // namespace attn_impl
 
 void attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Sq, int Sk, int H, int Hk,
-              int Dqk, int Dv, bool causal, float scale, cudaStream_t s) {
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s, const int* doc_start,
+              const int* doc_end) {
   using namespace attn_impl;
   if (B == 0 || Sq == 0) return;
+  if (doc_start != nullptr && (Sq != Sk || !causal || !((Dqk == 128 && Dv == 128) || (Dqk == 64 && Dv == 64))))
+    throw std::runtime_error("attention: packed-document masks need causal self-attention with head dims 64 or 128");
   Params p;
+  p.doc_start = doc_start;
+  p.doc_end = doc_end;
   p.B = B;
   p.Sq = Sq;
   p.Sk = Sk;
@@ -1477,9 +1504,12 @@ void attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, 
 
 void attn_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
               void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int Sq, int Sk, int H, int Hk,
-              int Dqk, int Dv, bool causal, float scale, cudaStream_t s, const float* dlse) {
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s, const float* dlse, const int* doc_start,
+              const int* doc_end) {
   using namespace attn_impl;
   (void)dq_acc;
+  if (doc_start != nullptr && (Sq != Sk || !causal))
+    throw std::runtime_error("attention bwd: packed-document masks need causal self-attention");
   if (B == 0 || Sq == 0 || Sk == 0) return;
   const int64_t rows = (int64_t)B * Sq * H;
   attn_bwd_delta_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, s>>>(
@@ -1499,6 +1529,8 @@ void attn_bwd(const void* dout, const void* q, const void* k, const void* v, con
   p.dk = static_cast<__nv_bfloat16*>(dk);
   p.dv = static_cast<__nv_bfloat16*>(dv);
   p.dq = static_cast<__nv_bfloat16*>(dq);
+  p.doc_start = doc_start;
+  p.doc_end = doc_end;
   if (Dqk == 128 && Dv == 128) launch_bwd<128, 128, 2>(dout, q, k, v, p, s);
   else if (Dqk == 64 && Dv == 64) launch_bwd<64, 64, 2>(dout, q, k, v, p, s);
   else if (Dqk == 192 && Dv == 128) launch_bwd<192, 128, 1>(dout, q, k, v, p, s);

@@ -143,10 +143,12 @@ void multi_clip_scale(const SumSqTensor* list, int count, const float* total, fl
 
 // flash_attn.cu
 void attn_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int Sq, int Sk, int H, int Hk,
-              int Dqk, int Dv, bool causal, float scale, cudaStream_t s);
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s, const int* doc_start = nullptr,
+              const int* doc_end = nullptr);
 void attn_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
               void* dq, void* dk, void* dv, float* dq_acc, float* delta, int B, int Sq, int Sk, int H, int Hk,
-              int Dqk, int Dv, bool causal, float scale, cudaStream_t s, const float* dlse = nullptr);
+              int Dqk, int Dv, bool causal, float scale, cudaStream_t s, const float* dlse = nullptr,
+              const int* doc_start = nullptr, const int* doc_end = nullptr);
 int attn_error_code(bool reset);
 
 }  // namespace ttb
