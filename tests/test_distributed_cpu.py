@@ -179,19 +179,30 @@ def _distmuon(rank, world):
 
     mesh = init_device_mesh("cpu", (world,), mesh_dim_names=("fsdp",))
     torch.manual_seed(0)
-    w = torch.randn(8, 6)
-    g = torch.randn(8, 6)
-    p_ref = torch.nn.Parameter(w.clone())
-    p_ref.grad = g.clone()
-    Muon([{"params": [p_ref], "use_muon": True}], lr=0.02).step()
-    p = torch.nn.Parameter(distribute_tensor(w.clone(), mesh, [Shard(0)]))
-    p.grad = distribute_tensor(g.clone(), mesh, [Shard(0)])
-    Muon([{"params": [p], "use_muon": True}], lr=0.02, distributed=True).step()
-    assert torch.allclose(p.full_tensor(), p_ref.detach(), atol=1e-5)
+    # several matrices (uneven row splits, equal shapes batched together) and a 3-D expert stack
+    shapes = [(8, 6), (7, 12), (8, 6), (5, 3, 4), (16, 16), (3, 10)]
+    ws = [torch.randn(s) for s in shapes]
+    gs = [torch.randn(s) for s in shapes]
+    refs = [torch.nn.Parameter(w.clone()) for w in ws]
+    for p, g in zip(refs, gs):
+        p.grad = g.clone()
+    opt_ref = Muon([{"params": refs, "use_muon": True}], lr=0.02)
+    ps = [torch.nn.Parameter(distribute_tensor(w.clone(), mesh, [Shard(0)])) for w in ws]
+    opt = Muon([{"params": ps, "use_muon": True}], lr=0.02, distributed=True)
+    for _ in range(2):  # two steps: momentum buffers carry over
+        for p, g in zip(ps, gs):
+            p.grad = distribute_tensor(g.clone(), mesh, [Shard(0)])
+        for p, g in zip(refs, gs):
+            p.grad = g.clone()
+        opt_ref.step()
+        opt.step()
+    for p, r in zip(ps, refs):
+        assert torch.allclose(p.full_tensor(), r.detach(), atol=1e-5), (p.shape,)
 
 
-def test_distmuon_matches_muon():
-    _run(_distmuon, 2)
+@pytest.mark.parametrize("world", [2, 3])
+def test_distmuon_matches_muon(world):
+    _run(_distmuon, world)
 
 
 # ---------------------------------------------------------------- failure detection

@@ -367,3 +367,22 @@ def test_document_attention(ext, S, lens, D):
     assert _rel(o, orf) < 2e-2
     for a, b in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
         assert _rel(a, b) < 3e-2
+
+
+def test_grouped_bmm_and_batched_newton_schulz(ext):
+    """Equal-shape stacks through one grouped GEMM (the batched path of ops.matmul used by
+    Muon's Newton-Schulz on expert stacks) against fp32 torch.bmm, and the batched iteration
+    against the per-matrix one."""
+    from torchtitan_b200.components.optimizer import zeropower_via_newtonschulz5
+    from torchtitan_b200.ops.gemm import bmm_grouped
+
+    torch.manual_seed(4)
+    a = torch.randn(6, 256, 192, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(6, 192, 320, device="cuda", dtype=torch.bfloat16)
+    want = torch.bmm(a.float(), b.float())
+    assert _rel(bmm_grouped(a, b), want) < 1e-2
+    x = torch.randn(8, 128, 384, device="cuda")
+    with torch.no_grad():
+        batched = zeropower_via_newtonschulz5(x)
+        single = torch.stack([zeropower_via_newtonschulz5(m) for m in x])
+    assert _rel(batched, single) < 2e-2

@@ -121,6 +121,8 @@ class AdamW(torch.optim.Optimizer):
 
     def load_state_dict(self, state_dict):
         _load_keeping_fp32(self, state_dict)
+        for g in self.param_groups:  # re-read the step count from the loaded state on next use
+            g.pop("_host_step", None)
 
 
 class PeerShardedAdamW(torch.optim.Optimizer):
@@ -231,9 +233,19 @@ class Muon(torch.optim.Optimizer):
         if not self.distributed or not any(isinstance(u, DTensor) for _, u in items):
             return [zeropower_via_newtonschulz5(_full(u), ns_steps) for _, u in items]
         out: list[torch.Tensor | None] = [None] * len(items)
-        # group by process group of the sharded mesh dim
-        for idx, (p, u) in enumerate(items):
-            out[idx] = _dist_orthogonalize(u, idx, ns_steps)
+        by_group: dict[Any, list[tuple[int, DTensor]]] = {}
+        for idx, (_, u) in enumerate(items):
+            if not isinstance(u, DTensor):
+                out[idx] = zeropower_via_newtonschulz5(u, ns_steps)
+                continue
+            shard_dims = [i for i, pl in enumerate(u.placements) if isinstance(pl, Shard)]
+            if len(shard_dims) == 1 and u.placements[shard_dims[0]].dim == 0:
+                by_group.setdefault(u.device_mesh.get_group(shard_dims[0]), []).append((idx, u))
+            else:
+                out[idx] = _dist_orthogonalize(u, idx, ns_steps)
+        for pg, lst in by_group.items():
+            for idx, res in _dist_orthogonalize_bucketed(pg, lst, ns_steps).items():
+                out[idx] = res
         return out  # type: ignore
 
     @torch.no_grad()
@@ -261,8 +273,15 @@ class Muon(torch.optim.Optimizer):
                     gs.append(_local(p.grad))
                     ms.append(_local(st["exp_avg"])); vs.append(_local(st["exp_avg_sq"]))
                 b1, b2 = group["betas"]
+                # the step count is mirrored on the host so the kernel launch needs no device sync
+                host_step = group.get("_host_step")
+                if host_step is None:
+                    host_step = int(self.state[params[0]]["step"].item())
+                else:
+                    host_step += 1
+                group["_host_step"] = host_step
                 ops.fused_adamw_(ps, gs, ms, vs, lr=lr, beta1=b1, beta2=b2, eps=group["eps"], weight_decay=wd,
-                                 step=int(self.state[params[0]]["step"].item()),
+                                 step=host_step,
                                  copies=copies if any(c is not None for c in copies) else None)
                 continue
             mom = group["momentum"]
@@ -290,6 +309,98 @@ class Muon(torch.optim.Optimizer):
 
 def _full(t: torch.Tensor) -> torch.Tensor:
     return t.full_tensor() if isinstance(t, DTensor) else t
+
+
+def _ns_batched(mats: list[torch.Tensor], ns_steps: int) -> list[torch.Tensor]:
+    """Newton-Schulz on many matrices: equal trailing shapes are stacked and iterated together
+    (on CUDA each iteration's products are single grouped GEMMs over the whole stack)."""
+    out: list[torch.Tensor | None] = [None] * len(mats)
+    by_shape: dict[tuple[int, int], list[int]] = {}
+    for i, m in enumerate(mats):
+        by_shape.setdefault(tuple(m.shape[-2:]), []).append(i)
+    for shape, ids in by_shape.items():
+        stack = torch.cat([mats[i].reshape(-1, *shape) for i in ids])
+        res = zeropower_via_newtonschulz5(stack, ns_steps)
+        pos = 0
+        for i in ids:
+            n = mats[i].numel() // (shape[0] * shape[1])
+            out[i] = res[pos:pos + n].reshape(mats[i].shape)
+            pos += n
+    return out  # type: ignore
+
+
+def _dist_orthogonalize_bucketed(pg, lst: list[tuple[int, "DTensor"]], ns_steps: int) -> dict[int, torch.Tensor]:
+    """DistMuon over one process group for every Shard(0) matrix at once.
+
+    Owners are assigned greedily by size (largest first, to the least-loaded rank), so every
+    rank orthogonalises its share concurrently. One all-to-all carries every rank's row chunk of
+    every matrix to its owner, the owner runs batched Newton-Schulz on all of its matrices, and
+    a second all-to-all returns the row chunks: two collectives per step, not two per parameter.
+    (The reference has no distributed Muon: its optimizer registry stops at AdamW/Adam,
+    ``torchtitan/components/optimizer.py:130-134``.)
+    """
+    world, rank = dist.get_world_size(pg), dist.get_rank(pg)
+    any_u = lst[0][1]
+    dev = any_u.to_local().device
+    wire = torch.bfloat16 if dev.type == "cuda" else torch.float32  # NS runs in bf16 on CUDA
+    order = sorted(range(len(lst)), key=lambda j: -lst[j][1].numel())
+    load = [0] * world
+    owner = [0] * len(lst)
+    for j in order:
+        o = min(range(world), key=lambda r: load[r])
+        owner[j] = o
+        load[o] += lst[j][1].numel()
+    rows = [u.shape[0] for _, u in lst]
+    inner = [u.numel() // max(u.shape[0], 1) for _, u in lst]
+    chunk = [(r + world - 1) // world for r in rows]
+    cnum = [c * i for c, i in zip(chunk, inner)]
+    mine = [j for j in range(len(lst)) if owner[j] == rank]
+    # ---- chunks to owners
+    send = []
+    for dst in range(world):
+        for j in range(len(lst)):
+            if owner[j] != dst:
+                continue
+            loc = lst[j][1].to_local().reshape(-1, inner[j]).to(wire)
+            buf = torch.zeros(chunk[j], inner[j], dtype=wire, device=dev)
+            buf[:loc.shape[0]].copy_(loc)
+            send.append(buf.reshape(-1))
+    in_splits = [sum(cnum[j] for j in range(len(lst)) if owner[j] == dst) for dst in range(world)]
+    out_splits = [sum(cnum[j] for j in mine)] * world
+    send_t = torch.cat(send) if send else torch.zeros(0, dtype=wire, device=dev)
+    recv = torch.empty(sum(out_splits), dtype=wire, device=dev)
+    dist.all_to_all_single(recv, send_t, out_splits, in_splits, group=pg)
+    # ---- owner: assemble, orthogonalise (batched), cut into row chunks
+    per_src = recv.split(out_splits) if out_splits[0] else [recv] * world
+    fulls = []
+    for k, j in enumerate(mine):
+        off = sum(cnum[jj] for jj in mine[:k])
+        parts = [per_src[src][off:off + cnum[j]].view(chunk[j], inner[j]) for src in range(world)]
+        fulls.append(torch.cat(parts)[:rows[j]].reshape(lst[j][1].shape))
+    results = _ns_batched(fulls, ns_steps) if fulls else []
+    back = []
+    for dst in range(world):
+        for k, j in enumerate(mine):
+            r2 = results[k].reshape(rows[j], inner[j])
+            buf = torch.zeros(chunk[j], inner[j], dtype=wire, device=dev)
+            seg = r2[dst * chunk[j]:(dst + 1) * chunk[j]]
+            buf[:seg.shape[0]].copy_(seg)
+            back.append(buf.reshape(-1))
+    back_t = torch.cat(back) if back else torch.zeros(0, dtype=wire, device=dev)
+    recv2 = torch.empty(sum(in_splits), dtype=wire, device=dev)
+    dist.all_to_all_single(recv2, back_t, in_splits, out_splits, group=pg)
+    # ---- this rank's rows of every matrix, in the order of the owners' sends
+    out: dict[int, torch.Tensor] = {}
+    pos = 0
+    for src in range(world):
+        for j in range(len(lst)):
+            if owner[j] != src:
+                continue
+            loc = lst[j][1].to_local()
+            piece = recv2[pos:pos + cnum[j]].view(chunk[j], inner[j])[:loc.shape[0]]
+            out[lst[j][0]] = piece.reshape(loc.shape).to(loc.dtype)
+            pos += cnum[j]
+    return out
 
 
 def _dist_orthogonalize(u: "DTensor", idx: int, ns_steps: int) -> torch.Tensor:

@@ -228,6 +228,66 @@ def bench_kda(ext, out):
     print(json.dumps(out[-1]), flush=True)
 
 
+def bench_kda_vs_fla(ext, out):
+    """Chunked KDA forward+backward against the fla library's ``chunk_kda`` (Triton, the
+    reference's path: ``kimi_linear/model.py:559-571``) on the same inputs: H 32, K = V = 128,
+    T 4096 and 131072; relative error of the outputs between the two."""
+    from torchtitan_b200.ops import kda
+
+    try:
+        from fla.ops.kda import chunk_kda as fla_chunk_kda
+    except Exception as e:  # noqa: BLE001
+        out.append({"kernel": "kda_vs_fla", "unavailable": f"{type(e).__name__}: {e}"})
+        print(json.dumps(out[-1]), flush=True)
+        return
+    for T in (4096, 131072):
+        B, H, K, V = 1, 32, 128, 128
+        torch.manual_seed(0)
+        q, k = (torch.randn(B, T, H, K, device="cuda", dtype=torch.bfloat16, requires_grad=True) for _ in range(2))
+        v = torch.randn(B, T, H, V, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        g = (-torch.rand(B, T, H, K, device="cuda") * 0.1).requires_grad_()
+        beta = torch.rand(B, T, H, device="cuda", requires_grad=True)
+        do = torch.randn(B, T, H, V, device="cuda", dtype=torch.bfloat16)
+
+        def ours():
+            o, _ = kda.chunk_kda(q, k, v, g, beta, use_qk_l2norm=True)
+            o.backward(do)
+            return o
+
+        def theirs():
+            o, _ = fla_chunk_kda(q, k, v, g, beta, use_qk_l2norm_in_kernel=True)
+            o.backward(do)
+            return o
+
+        with torch.no_grad():
+            a = kda.chunk_kda(q, k, v, g, beta, use_qk_l2norm=True)[0].float()
+            b = fla_chunk_kda(q, k, v, g, beta, use_qk_l2norm_in_kernel=True)[0].float()
+        rel = float((a - b).norm() / b.norm())
+        t_ours = time_fn(ours, iters=3, warmup=1, flush=False)
+        t_fla = time_fn(theirs, iters=3, warmup=1, flush=False)
+        out.append({"kernel": "kda_vs_fla", "case": f"B{B}_T{T}_H{H}_K{K}_V{V}", "fwd_bwd_ms_ours": t_ours,
+                    "fwd_bwd_ms_fla": t_fla, "ours_over_fla_speed": t_fla / t_ours, "out_rel_err": rel})
+        print(json.dumps(out[-1]), flush=True)
+        del q, k, v, g, beta, do
+        torch.cuda.empty_cache()
+
+
+def bench_muon(ext, out):
+    """Newton-Schulz (5 iterations) on a stack of 32 expert matrices of the Kimi-Linear 48B
+    shape (1024 x 2304): batched through grouped GEMMs vs one matrix at a time."""
+    from torchtitan_b200.components.optimizer import zeropower_via_newtonschulz5
+
+    x = torch.randn(32, 1024, 2304, device="cuda")
+    m, n = 1024, 2304
+    flops = 32 * 5 * (2 * m * m * n * 2 + 2 * m * m * m)
+    with torch.no_grad():
+        t_b = time_fn(lambda: zeropower_via_newtonschulz5(x), iters=5, warmup=2, flush=False)
+        t_l = time_fn(lambda: [zeropower_via_newtonschulz5(mm) for mm in x], iters=5, warmup=2, flush=False)
+    out.append({"kernel": "muon_newton_schulz", "case": "32x1024x2304", "batched_ms": t_b, "loop_ms": t_l,
+                "batched_tflops": flops / t_b / 1e9, "loop_tflops": flops / t_l / 1e9})
+    print(json.dumps(out[-1]), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,mem")
@@ -244,6 +304,10 @@ def main():
         bench_mxfp8(ext, out)
     if "kda" in sel:
         bench_kda(ext, out)
+    if "kda_fla" in sel:
+        bench_kda_vs_fla(ext, out)
+    if "muon" in sel:
+        bench_muon(ext, out)
     if "attn" in sel:
         bench_attn(ext, out)
     if "attn_large" in sel:

@@ -93,11 +93,28 @@ class _Matmul(torch.autograd.Function):
         return da, db
 
 
+def bmm_grouped(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Batched ``a @ b`` for equal-shape stacks a [E, m, k], b [E, k, n] (no autograd) as ONE
+    grouped tcgen05 GEMM: the grouped-reduction mode computes D_g = A_g^T B_g over row ranges
+    of stacked operands, so A_g = a_g^T and B_g = b_g."""
+    E, m, k = a.shape
+    n = b.shape[-1]
+    at = a.mT.contiguous().reshape(E * k, m)
+    bt = b.contiguous().reshape(E * k, n)
+    ks = torch.arange(0, E * k, k, dtype=torch.int32, device=a.device)
+    kl = torch.full((E,), k, dtype=torch.int32, device=a.device)
+    return _ext.ext().gemm_grouped_k(at, bt, ks, kl)
+
+
 def matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    """2-D ``a @ b`` (bf16 on CUDA), or batched via a loop over leading dims."""
+    """2-D ``a @ b`` (bf16 on CUDA); 3-D stacks go through one grouped GEMM when no gradient
+    is needed and the shapes allow it (row lengths multiples of 8), else a loop."""
     if not a.is_cuda:
         return a @ b
     if a.dim() > 2:
+        if (a.dim() == 3 and b.dim() == 3 and a.shape[0] == b.shape[0] and not torch.is_grad_enabled()
+                and a.shape[1] % 8 == 0 and b.shape[2] % 8 == 0):
+            return bmm_grouped(a.bfloat16(), b.bfloat16()).to(a.dtype)
         return torch.stack([matmul(x, y) for x, y in zip(a.unbind(0), b.unbind(0))])
     if a.dtype != torch.bfloat16:
         return _Matmul.apply(a.bfloat16(), b.bfloat16()).to(a.dtype)
