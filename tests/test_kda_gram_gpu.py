@@ -60,3 +60,54 @@ def test_chunk_kda_with_scan_kernel_matches_recurrence(monkeypatch):
     o, _ = kda.chunk_kda(q, k, v, g, beta)
     ref, _ = kda.naive_recurrent_kda(q, k, v, g, beta)
     torch.testing.assert_close(o.float(), ref, rtol=2e-3, atol=2e-3)
+
+
+def _rel(a, b):
+    return float((a.float() - b.float()).norm() / (b.float().norm() + 1e-12))
+
+
+@pytest.mark.parametrize("BH,NT,with_state", [(3, 5, False), (2, 9, True)])
+def test_kda_state_kernels_match_loop(BH, NT, with_state):
+    """The tcgen05 state-passing recurrence (bf16 operands, fp32 state) against the fp32
+    batched-matmul loop: outputs, final state, and the gradients of every input including the
+    initial state, with a gradient on the final state too."""
+    from torchtitan_b200.ops import kda
+
+    torch.manual_seed(3)
+    C, K, V = 64, 128, 128
+    u = torch.randn(BH, NT, C, V, device="cuda")
+    w, qg, kd = (0.05 * torch.randn(BH, NT, C, K, device="cuda") for _ in range(3))
+    A = 0.1 * torch.randn(BH, NT, C, C, device="cuda").tril()
+    dec = torch.rand(BH, NT, K, device="cuda") * 0.5 + 0.5
+    S0 = torch.randn(BH, K, V, device="cuda") if with_state else None
+    do = torch.randn(BH, NT, C, V, device="cuda")
+    dfin = torch.randn(BH, K, V, device="cuda")
+    res = []
+    for fn in (lambda *x: kda._scan_ref(*x), lambda *x: kda._StateScan.apply(*x)):
+        xs = [t.clone().requires_grad_() for t in (u, w, qg, A, kd, dec)]
+        s0 = S0.clone().requires_grad_() if with_state else None
+        o, S = fn(*xs, s0)
+        ((o * do).sum() + (S * dfin).sum()).backward()
+        res.append([o.detach(), S.detach()] + [x.grad for x in xs] + ([s0.grad] if with_state else []))
+    from torchtitan_b200.ops._ext import ext
+
+    assert ext().kda_state_error_code(True) == 0
+    names = ["o", "S", "du", "dw", "dqg", "dA", "dkd", "ddec", "dS0"]
+    for n, got, want in zip(names, res[1], res[0]):
+        assert _rel(got, want) < 3e-2, (n, _rel(got, want))
+
+
+def test_chunk_kda_state_kernel_matches_recurrence():
+    """Whole chunked KDA at K = V = 128 (the tcgen05 state path) against the token recurrence,
+    with a sequence that is not a multiple of the chunk."""
+    from torchtitan_b200.ops import kda
+
+    torch.manual_seed(2)
+    B, T, H, K, V = 1, 300, 2, 128, 128
+    q, k = (torch.randn(B, T, H, K, device="cuda") for _ in range(2))
+    v = torch.randn(B, T, H, V, device="cuda")
+    g = -torch.rand(B, T, H, K, device="cuda") * 0.2
+    beta = torch.rand(B, T, H, device="cuda")
+    o, S = kda.chunk_kda(q, k, v, g, beta, output_final_state=True)
+    ref, Sref = kda.naive_recurrent_kda(q, k, v, g, beta)
+    assert _rel(o, ref) < 2e-2 and _rel(S, Sref) < 2e-2

@@ -401,6 +401,54 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                       (int)a.size(2), strict, stream());
     return std::vector<Tensor>{da, db, dG};
   });
+  // chunked-KDA state recurrence on tcgen05 (C = 64, K = V = 128): bf16 w / kdec [BH,NT,C,K],
+  // u^T [BH,NT,V,C]; fp32 dec [BH,NT,K], optional S0^T [BH,V,K].
+  // Returns states^T [BH,NT,V,K] bf16 (state at each chunk start), v'^T [BH,NT,V,C] bf16, final S^T fp32.
+  m.def("kda_state_fwd", [](Tensor w, Tensor kd, Tensor uT, Tensor dec, c10::optional<Tensor> S0) {
+    for (const Tensor* t : {&w, &kd, &uT})
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous(), "kda_state: bf16");
+    TORCH_CHECK(dec.is_cuda() && dec.scalar_type() == at::kFloat && dec.is_contiguous(), "kda_state: dec fp32");
+    const int64_t BH = w.size(0), NT = w.size(1);
+    TORCH_CHECK(w.dim() == 4 && w.size(2) == 64 && w.size(3) == 128 && kd.sizes() == w.sizes() &&
+                    uT.sizes() == at::IntArrayRef({BH, NT, 128, 64}) && dec.sizes() == at::IntArrayRef({BH, NT, 128}),
+                "kda_state: shapes (C = 64, K = V = 128)");
+    if (S0.has_value())
+      TORCH_CHECK(S0->is_cuda() && S0->scalar_type() == at::kFloat && S0->is_contiguous() &&
+                      S0->sizes() == at::IntArrayRef({BH, 128, 128}), "kda_state: S0 fp32 [BH, V, K]");
+    c10::cuda::CUDAGuard g(w.device());
+    auto states = torch::empty({BH, NT, 128, 128}, w.options());
+    auto vnT = torch::empty({BH, NT, 128, 64}, w.options());
+    auto fin = torch::empty({BH, 128, 128}, dec.options());
+    ttb::kda_state_fwd(w.data_ptr(), kd.data_ptr(), uT.data_ptr(), dec.data_ptr<float>(),
+                       S0.has_value() ? S0->data_ptr<float>() : nullptr, states.data_ptr(), vnT.data_ptr(),
+                       fin.data_ptr<float>(), (int)BH, (int)NT, stream());
+    return std::vector<Tensor>{states, vnT, fin};
+  });
+  // backward: bf16 qg / w / kdec [BH,NT,C,K], dO [BH,NT,C,V], Aqk [BH,NT,C,C]; fp32 dec, optional dSfin^T.
+  // Returns dstates^T [BH,NT,V,K] bf16 (gradient of the state after each chunk), dv'^T fp32, dS0^T fp32.
+  m.def("kda_state_bwd", [](Tensor qg, Tensor w, Tensor kd, Tensor dO, Tensor Aqk, Tensor dec,
+                            c10::optional<Tensor> dSfin) {
+    for (const Tensor* t : {&qg, &w, &kd, &dO, &Aqk})
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous(), "kda_state: bf16");
+    const int64_t BH = w.size(0), NT = w.size(1);
+    TORCH_CHECK(w.dim() == 4 && w.size(2) == 64 && w.size(3) == 128 && qg.sizes() == w.sizes() &&
+                    kd.sizes() == w.sizes() && dO.sizes() == at::IntArrayRef({BH, NT, 64, 128}) &&
+                    Aqk.sizes() == at::IntArrayRef({BH, NT, 64, 64}) && dec.sizes() == at::IntArrayRef({BH, NT, 128}),
+                "kda_state_bwd: shapes (C = 64, K = V = 128)");
+    TORCH_CHECK(dec.is_cuda() && dec.scalar_type() == at::kFloat && dec.is_contiguous(), "kda_state: dec fp32");
+    if (dSfin.has_value())
+      TORCH_CHECK(dSfin->is_cuda() && dSfin->scalar_type() == at::kFloat && dSfin->is_contiguous() &&
+                      dSfin->sizes() == at::IntArrayRef({BH, 128, 128}), "kda_state: dSfin fp32 [BH, V, K]");
+    c10::cuda::CUDAGuard g(w.device());
+    auto dstates = torch::empty({BH, NT, 128, 128}, w.options());
+    auto duT = torch::empty({BH, NT, 128, 64}, dec.options());
+    auto dS0 = torch::empty({BH, 128, 128}, dec.options());
+    ttb::kda_state_bwd(qg.data_ptr(), w.data_ptr(), kd.data_ptr(), dO.data_ptr(), Aqk.data_ptr(),
+                       dec.data_ptr<float>(), dSfin.has_value() ? dSfin->data_ptr<float>() : nullptr,
+                       dstates.data_ptr(), duT.data_ptr<float>(), dS0.data_ptr<float>(), (int)BH, (int)NT, stream());
+    return std::vector<Tensor>{dstates, duT, dS0};
+  });
+  m.def("kda_state_error_code", &ttb::kda_state_error_code, py::arg("reset") = true);
   // chunked-KDA inter-chunk recurrence: u [BH,NT,C,V], w/qg/kdec [BH,NT,C,K], Aqk [BH,NT,C,C], dec [BH,NT,K]
   m.def("kda_scan_fwd", [](Tensor u, Tensor w, Tensor qg, Tensor Aqk, Tensor kdec, Tensor dec, int64_t vs) {
     for (const Tensor* t : {&u, &w, &qg, &Aqk, &kdec, &dec})

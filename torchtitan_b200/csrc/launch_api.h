@@ -92,6 +92,13 @@ void kda_gram_fwd(const float* a, const float* b, const float* G, float* out, in
 void kda_gram_bwd(const float* dout, const float* a, const float* b, const float* G, float* da, float* db,
                   float* dG, int64_t N, int C, int K, bool strict, cudaStream_t s);
 
+// kda_state.cu: the chunked-KDA state recurrence on tcgen05 (C = 64, K = V = 128, bf16 operands)
+void kda_state_fwd(const void* w, const void* kd, const void* uT, const float* dec, const float* S0, void* states,
+                   void* vnT, float* Sfin, int BH, int NT, cudaStream_t s);
+void kda_state_bwd(const void* qg, const void* w, const void* kd, const void* dO, const void* Aqk, const float* dec,
+                   const float* dSfin, void* dstates, float* duT, float* dS0, int BH, int NT, cudaStream_t s);
+int kda_state_error_code(bool reset);
+
 // kda_scan.cu: inter-chunk state recurrence of chunked KDA (forward and backward)
 void kda_scan_fwd(const float* u, const float* w, const float* qg, const float* Aqk, const float* kdec,
                   const float* dec, float* o, float* states, float* final_S, int64_t BH, int NT, int C, int K, int V,

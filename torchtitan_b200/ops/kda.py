@@ -182,10 +182,8 @@ def chunk_kda(q, k, v, g, beta, scale: float | None = None, chunk_size: int = 64
     Glast = G[:, :, -1:, :]  # [BH, NT, 1, K]
     kdec = (Glast - G).exp() * kc
     decay = Glast[:, :, 0, :].exp()  # [BH, NT, K]
-    if initial_state is None:
-        o, S = chunk_scan(u, w, qg, Aqk, kdec, decay)
-    else:
-        o, S = _scan_ref(u, w, qg, Aqk, kdec, decay, initial_state.float().reshape(B * H, K, V))
+    S0 = None if initial_state is None else initial_state.float().reshape(B * H, K, V)
+    o, S = chunk_scan(u, w, qg, Aqk, kdec, decay, S0)
     o = o.view(B, H, NT, C, V).permute(0, 2, 3, 1, 4).reshape(B, Tp, H, V)[:, :T]
     final = S.view(B, H, K, V) if output_final_state else None
     return o.to(dtype), final
@@ -239,11 +237,67 @@ class _ChunkScan(torch.autograd.Function):
         return du, dw, dqg, dA, dkd, dd
 
 
-def chunk_scan(u, w, qg, Aqk, kdec, decay):
-    """-> (o [BH, NT, C, V], final state [BH, K, V]); kernel on CUDA when opted in."""
-    if _use_gram_kernel(u) and _fits_shared_memory(u.shape[2], w.shape[-1], u.shape[-1]):
+class _StateScan(torch.autograd.Function):
+    """The recurrence of ``_scan_ref`` split the state-passing way: the tcgen05 kernels of
+    ``csrc/kda_state.cu`` walk the chunks of each head carrying only the state (forward: S_n and
+    v'_n; backward: dS_{n+1} and dv'_n), and everything that does not depend on the walk is a
+    batched GEMM over all chunks at once: o = qg S + Aqk v', and the gradients of qg, w, kdec,
+    Aqk and the decay.  bf16 operands, fp32 accumulation; the state stays fp32 in TMEM.
+    (C = 64 and K = V = 128.)"""
+
+    @staticmethod
+    def forward(ctx, u, w, qg, Aqk, kdec, decay, S0):
+        from ._ext import ext
+
+        bf = torch.bfloat16
+        wb, kdb, qgb, Ab = (t.to(bf).contiguous() for t in (w, kdec, qg, Aqk))
+        uT = u.transpose(-1, -2).to(bf).contiguous()
+        dec = decay.float().contiguous()
+        s0 = None if S0 is None else S0.float().transpose(-1, -2).contiguous()
+        states, vnT, fin = ext().kda_state_fwd(wb, kdb, uT, dec, s0)
+        # o = qg S_n + Aqk v'_n  (S_n^T and v'^T are what the kernel stored)
+        o = torch.matmul(qgb, states.transpose(-1, -2)).float() + torch.matmul(Ab, vnT.transpose(-1, -2)).float()
+        ctx.save_for_backward(qgb, wb, kdb, Ab, dec, states, vnT)
+        ctx.has_s0 = S0 is not None
+        ctx.set_materialize_grads(False)
+        return o, fin.transpose(-1, -2)
+
+    @staticmethod
+    def backward(ctx, do, dfin):
+        from ._ext import ext
+
+        qgb, wb, kdb, Ab, dec, states, vnT = ctx.saved_tensors
+        BH, NT, C, K = qgb.shape
+        V = states.shape[2]
+        dob = (do if do is not None else qgb.new_zeros(BH, NT, C, V)).to(torch.bfloat16).contiguous()
+        dfT = None if dfin is None else dfin.float().transpose(-1, -2).contiguous()
+        dstates, duT, dS0 = ext().kda_state_bwd(qgb, wb, kdb, dob, Ab, dec, dfT)
+        du = duT.transpose(-1, -2)
+        dub = du.to(torch.bfloat16)
+        # gradients of everything outside the walk, as GEMMs over all chunks
+        dqg = torch.matmul(dob, states).float()                                # dO S_n^T
+        dw = -torch.matmul(dub, states).float()                                # -dv' S_n^T
+        dkdec = torch.matmul(vnT.transpose(-1, -2), dstates).float()           # v' dS_{n+1}^T
+        dAqk = torch.matmul(dob, vnT).float()                                  # dO v'^T
+        ddec = (dstates.float() * states.float()).sum(-2)                      # sum_v dS_{n+1} o S_n
+        dS0 = dS0.transpose(-1, -2) if ctx.has_s0 else None
+        return du, dw, dqg, dAqk, dkdec, ddec, dS0
+
+
+def _state_kernel_ok(u, w) -> bool:
+    return (_use_gram_kernel(u) and u.shape[2] == 64 and w.shape[-1] == 128 and u.shape[-1] == 128
+            and __import__("os").environ.get("TTB_KDA_STATE", "1") != "0")
+
+
+def chunk_scan(u, w, qg, Aqk, kdec, decay, S0=None):
+    """-> (o [BH, NT, C, V], final state [BH, K, V]); on CUDA the tcgen05 state kernels for
+    C = 64, K = V = 128 (``TTB_KDA_STATE=0`` selects the fp32 SIMT recurrence kernels), the SIMT
+    kernels for other shapes, and the batched-matmul loop elsewhere."""
+    if _state_kernel_ok(u, w):
+        return _StateScan.apply(u, w, qg, Aqk, kdec, decay, S0)
+    if S0 is None and _use_gram_kernel(u) and _fits_shared_memory(u.shape[2], w.shape[-1], u.shape[-1]):
         return _ChunkScan.apply(u, w, qg, Aqk, kdec, decay)
-    return _scan_ref(u, w, qg, Aqk, kdec, decay)
+    return _scan_ref(u, w, qg, Aqk, kdec, decay, S0)
 
 
 def naive_recurrent_kda(q, k, v, g, beta, scale=None, use_qk_l2norm: bool = True):
