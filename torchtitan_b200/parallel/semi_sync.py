@@ -45,6 +45,17 @@ class FaultToleranceConfig:
     outer_lr: float = 0.7
     outer_momentum: float = 0.9
     outer_nesterov: bool = True
+    # dynamic replica groups (no semi_sync_method): each replica is its own job; replicas meet
+    # at a lighthouse store and agree on a quorum every step (``parallel/ft.py``)
+    lighthouse: str = ""
+    """host:port of the lighthouse (``python -m torchtitan_b200.parallel.ft --port P``)."""
+    replica_id: int = 0
+    group_size: int = 0
+    """Maximum number of replicas (data is sharded over ``group_size`` x the replica's DP degree)."""
+    min_replica_size: int = 1
+    quorum_timeout_s: float = 30.0
+    process_group: Literal["gloo", "nccl"] = "gloo"
+    process_group_timeout_ms: int = 10000
 
 
 def _local(t: torch.Tensor) -> torch.Tensor:

@@ -121,6 +121,20 @@ class Trainer(Stateful, Configurable):
         else:
             dp_degree, dp_rank = 1, 0
         self.dp_degree = dp_degree
+        self.ft = None
+        if ft.enable and not ft.semi_sync_method and ft.lighthouse:
+            from torchtitan_b200.parallel.ft import FTManager
+
+            if c.parallelism.data_parallel_comm == "peer":
+                raise ValueError("dynamic fault-tolerant replicas work with FSDP2/DDP data parallelism, not the "
+                                 "peer-memory runtime")
+            c.parallelism.data_parallel_comm = "fsdp2"
+            self.ft = FTManager(ft.lighthouse, ft.replica_id, max(ft.group_size, ft.replica_id + 1),
+                                min_replica_size=ft.min_replica_size, quorum_timeout_s=ft.quorum_timeout_s,
+                                collective_timeout_s=ft.process_group_timeout_ms / 1000, backend=ft.process_group)
+            dp_degree, dp_rank = self.ft.data_parallel_info(dp_degree, dp_rank)
+            logger.info(f"fault-tolerant replica {ft.replica_id} of up to {self.ft.group_size} "
+                        f"(min {ft.min_replica_size}), lighthouse {ft.lighthouse}")
         self.gc_handler = dev_utils.GarbageCollection(gc_freq=c.training.gc_freq, debug=c.training.gc_debug)
         dist_utils.set_determinism(pd, self.device, c.debug, distinct_seed_mesh_dims=["pp"])
 
@@ -342,6 +356,14 @@ class Trainer(Stateful, Configurable):
         semi-sync and LR-scheduler steps.  Returns the pre-clip gradient norm."""
         pd = self.parallel_dims
         dp_rt = getattr(self.model_parts[0], "_dp_runtime", None)
+        if self.ft is not None:
+            # cross-replica average, then every participant votes; a failed step is dropped everywhere
+            ok = self.ft.allreduce_gradients(self.model_parts)
+            if not self.ft.should_commit(ok):
+                logger.warning(f"step {self.step}: a replica failed during the step; dropping it")
+                self.optimizers.zero_grad()
+                self.step -= 1
+                return torch.zeros((), device=self.device)
         max_norm = self.config.training.max_norm
         if self.optimizers.config.early_step_in_backward:
             max_norm = 0.0  # parameters already stepped inside backward: nothing left to clip
@@ -373,6 +395,11 @@ class Trainer(Stateful, Configurable):
         return grad_norm
 
     def train_step(self, data_iterator: Iterator) -> torch.Tensor:
+        if self.ft is not None:
+            q = self.ft.start_quorum(self.step - 1)
+            if self.ft.heal(self.model_parts, self.optimizers, self.lr_schedulers):
+                logger.info(f"healed from replica {q.source} at step {q.source_step}")
+                self.step = q.source_step + 1
         self.optimizers.zero_grad()
         lr = self.lr_schedulers.schedulers[0].get_last_lr()[0]
         pd = self.parallel_dims
