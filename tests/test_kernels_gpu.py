@@ -386,3 +386,29 @@ def test_grouped_bmm_and_batched_newton_schulz(ext):
         batched = zeropower_via_newtonschulz5(x)
         single = torch.stack([zeropower_via_newtonschulz5(m) for m in x])
     assert _rel(batched, single) < 2e-2
+
+
+def test_adamw_and_sumsq_device_table_path(ext):
+    """Updates with more chunks than one kernel-argument table holds go through the device-memory
+    chunk table and one persistent launch: two steps on the same tensors (table reused), then a
+    different tensor set (table rebuilt), against fp32 PyTorch; same for the sum of squares."""
+    from torchtitan_b200 import ops
+    from torchtitan_b200.ops import reference as R
+
+    torch.manual_seed(12)
+    kw = dict(lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1)
+    for n_t in (700, 650):
+        shapes = [(1000 + 8 * (i % 5),) for i in range(n_t)] + [(70000 * 3,)]
+        ps = [torch.randn(s, device="cuda") for s in shapes]
+        gs = [torch.randn(s, device="cuda").bfloat16() for s in shapes]
+        ms = [torch.zeros(s, device="cuda") for s in shapes]
+        vs = [torch.zeros(s, device="cuda") for s in shapes]
+        rp, rm, rv = [p.clone() for p in ps], [m.clone() for m in ms], [v.clone() for v in vs]
+        for step in (1, 2):
+            ops.fused_adamw_(ps, gs, ms, vs, step=step, **kw)
+            R.adamw_(rp, [g.float() for g in gs], rm, rv, step=step, **kw)
+        for p, r in zip(ps[::50], rp[::50]):
+            assert _rel(p, r) < 1e-5
+        tot = ext.multi_sumsq(gs)
+        ref = sum(float(g.float().pow(2).sum()) for g in gs)
+        assert abs(tot.item() - ref) / ref < 1e-5
