@@ -356,6 +356,36 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                         src_row.data_ptr<int64_t>(), reinterpret_cast<void* const*>(bases.data()),
                         (int)bases.size(), cap_rows, stream());
   });
+  // fused tensor-parallel GEMM (mode 0: all-gather -> GEMM, 1: GEMM -> reduce-scatter); pointers
+  // of symmetric buffers as integers (every rank's mapping)
+  m.def("tp_gemm", [](int64_t mode, std::vector<int64_t> shards, c10::optional<Tensor> land,
+                      c10::optional<Tensor> ready, c10::optional<Tensor> D, Tensor B, bool b_mn,
+                      std::vector<int64_t> recv, std::vector<int64_t> done, c10::optional<Tensor> out,
+                      int64_t parity, std::vector<int64_t> sig, int64_t tp, int64_t rank, int64_t epoch, int64_t Ms,
+                      int64_t N, int64_t K) {
+    check_cuda_bf16(B, "B");
+    TORCH_CHECK(B.is_contiguous(), "tp_gemm: B contiguous");
+    TORCH_CHECK((int64_t)sig.size() == tp && (int64_t)shards.size() == tp, "tp_gemm: one pointer per rank");
+    if (mode == 0) {
+      TORCH_CHECK(land.has_value() && ready.has_value() && D.has_value(), "tp_gemm: ag buffers");
+    } else {
+      TORCH_CHECK(out.has_value() && (int64_t)recv.size() == tp && (int64_t)done.size() == tp, "tp_gemm: rs buffers");
+    }
+    c10::cuda::CUDAGuard g(B.device());
+    auto vp = [](const std::vector<int64_t>& v) {
+      std::vector<void*> r(v.size());
+      for (size_t i = 0; i < v.size(); ++i) r[i] = reinterpret_cast<void*>(v[i]);
+      return r;
+    };
+    auto sh = vp(shards), rc = vp(recv), dn = vp(done), sg = vp(sig);
+    ttb::tp_gemm((int)mode, sh.data(), land.has_value() ? land->data_ptr() : nullptr,
+                 ready.has_value() ? reinterpret_cast<unsigned*>(ready->data_ptr<int>()) : nullptr,
+                 D.has_value() ? D->data_ptr() : nullptr, B.data_ptr(), b_mn, rc.data(),
+                 reinterpret_cast<unsigned* const*>(dn.data()), out.has_value() ? out->data_ptr() : nullptr,
+                 (int)parity, reinterpret_cast<unsigned* const*>(sg.data()), (int)tp, (int)rank,
+                 static_cast<uint32_t>(epoch), Ms, N, K, stream());
+  });
+  m.def("tp_gemm_error_code", &ttb::tp_gemm_error_code, py::arg("reset") = true);
   m.def("ep_error_code", &ttb::ep_error_code, "read (and optionally clear) the EP out-of-capacity row flag",
         py::arg("reset") = true);
   m.def("mx_quantize", [](Tensor x) {

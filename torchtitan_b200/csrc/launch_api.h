@@ -135,7 +135,13 @@ void ep_scatter_rows(const void* src, int64_t n, int d, const int32_t* dest_rank
                      void* const* peer_bases, int world, int64_t cap_rows, cudaStream_t s);
 void ep_gather_rows(void* dst, int64_t n, int d, const int32_t* src_rank, const int64_t* src_row,
                     void* const* peer_bases, int world, int64_t cap_rows, cudaStream_t s);
-int ep_error_code(bool reset);  // slot, epoch, source rank, flag value of the first failed wait
+int ep_error_code(bool reset);
+
+// tp_gemm.cu: tensor-parallel GEMMs fused with their all-gather / reduce-scatter over peer memory
+void tp_gemm(int mode, const void* const* shards, void* land, unsigned* chunk_ready, void* D, const void* B, bool b_mn,
+             void* const* recv, unsigned* const* done, void* out, int parity, unsigned* const* sig, int tp, int rank,
+             uint32_t epoch, int64_t Ms, int64_t N, int64_t K, cudaStream_t s);
+int tp_gemm_error_code(bool reset);  // slot, epoch, source rank, flag value of the first failed wait
 
 struct SumSqTensor {
   const void* x;

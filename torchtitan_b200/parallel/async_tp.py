@@ -114,8 +114,17 @@ class MatmulRS(torch.autograd.Function):
 
 
 def ag_matmul(x, w, group):
+    """On B200s over NCCL the fused kernel (``parallel/tp_fused.py``); else the P2P ring."""
+    from . import tp_fused
+
+    if tp_fused.fused_available(x, group) and tp_fused.shapes_ok(x, w.shape[0], w.shape[1]):
+        return tp_fused.FusedAGMatmul.apply(x, w, group)
     return AGMatmul.apply(x, w, group)
 
 
 def matmul_rs(x, w, group):
+    from . import tp_fused
+
+    if tp_fused.fused_available(x, group) and tp_fused.shapes_ok(x, w.shape[0], w.shape[1]):
+        return tp_fused.FusedMatmulRS.apply(x, w, group)
     return MatmulRS.apply(x, w, group)
