@@ -288,6 +288,51 @@ def bench_muon(ext, out):
     print(json.dumps(out[-1]), flush=True)
 
 
+def profile_case(ext, case: str) -> None:
+    """Small fixed workloads for ncu captures of one kernel (``--only case:<name>``):
+    gemm2 (bf16 4096^3), attn_fwd / attn_bwd (causal B1 S4096 H32/8 D128), kda (B1 T4096 H32
+    K=V=128 forward+backward), adamw (4 x 64 Mi fp32 params, bf16 grads). Each runs the op a few
+    times so ``-s`` can skip warm-up launches."""
+    from torchtitan_b200 import ops
+
+    torch.manual_seed(0)
+    if case == "gemm2":
+        a = torch.randn(4096, 4096, device="cuda").bfloat16()
+        b = torch.randn(4096, 4096, device="cuda").bfloat16()
+        for _ in range(3):
+            ext.gemm(a, b, False, False)
+    elif case in ("attn_fwd", "attn_bwd"):
+        q = torch.randn(1, 4096, 32, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        k = torch.randn(1, 4096, 8, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        v = torch.randn(1, 4096, 8, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        for _ in range(3):
+            o = ops.attention(q, k, v, causal=True)
+            if case == "attn_bwd":
+                o.backward(torch.randn_like(o))
+    elif case == "kda":
+        from torchtitan_b200.ops import kda
+
+        q, k = (torch.randn(1, 4096, 32, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+                for _ in range(2))
+        v = torch.randn(1, 4096, 32, 128, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+        g = (-torch.rand(1, 4096, 32, 128, device="cuda") * 0.1).requires_grad_()
+        beta = torch.rand(1, 4096, 32, device="cuda", requires_grad=True)
+        for _ in range(2):
+            o, _ = kda.chunk_kda(q, k, v, g, beta)
+            o.backward(torch.randn_like(o))
+    elif case == "adamw":
+        n = 64 * 2 ** 20
+        ps = [torch.randn(n, device="cuda") for _ in range(4)]
+        gs = [torch.randn(n, device="cuda").bfloat16() for _ in range(4)]
+        ms = [torch.zeros(n, device="cuda") for _ in range(4)]
+        vs = [torch.zeros(n, device="cuda") for _ in range(4)]
+        for s in range(1, 4):
+            ops.fused_adamw_(ps, gs, ms, vs, lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, step=s)
+    else:
+        raise ValueError(f"unknown profile case {case}")
+    torch.cuda.synchronize()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm,attn,mem")
@@ -298,6 +343,9 @@ def main():
     ext = _e()
     out: list = []
     sel = set(a.only.split(","))
+    for item in sel:
+        if item.startswith("case:"):
+            profile_case(ext, item[5:])
     if "gemm" in sel:
         bench_gemm(ext, out)
     if "mxfp8" in sel:
