@@ -32,6 +32,23 @@ class DataloaderExhaustedError(Exception):
     """Raised by the trainer's batch generator when the data runs out."""
 
 
+def _local_tensor_mode_active() -> bool:
+    try:
+        from torch.distributed._local_tensor import local_tensor_mode
+    except ImportError:
+        return False
+    return local_tensor_mode() is not None
+
+
+def _simulated_ranks(dp_rank: Any) -> dict[int, int] | None:
+    """``{global rank: dp rank}`` when ``dp_rank`` is a per-rank integer of LocalTensorMode, else None."""
+    if isinstance(dp_rank, torch.SymInt):
+        local = getattr(dp_rank.node, "_local_ints", None)
+        if local is not None:
+            return dict(local)
+    return None
+
+
 class BaseDataLoader(Stateful, ABC, Configurable):
     @dataclass(kw_only=True, slots=True)
     class Config(Configurable.Config):
@@ -90,12 +107,26 @@ class SyntheticDataLoader(BaseDataLoader):
         self.batches_emitted = 0
 
     def _batch(self, index: int) -> torch.Tensor:
+        if not _local_tensor_mode_active():
+            return self._batch_for(index, self.dp_rank)
+        # one process simulating every rank (comm mode local_tensor): the host batch is drawn
+        # outside the mode (inside it every rank would draw its own random numbers); with
+        # several dp ranks each rank's batch becomes one shard of a LocalTensor
+        from torch.distributed._local_tensor import LocalTensor, maybe_disable_local_tensor_mode
+
+        ranks = _simulated_ranks(self.dp_rank)
+        with maybe_disable_local_tensor_mode():
+            if ranks is None:
+                return self._batch_for(index, int(self.dp_rank))
+            return LocalTensor({r: self._batch_for(index, d) for r, d in ranks.items()})
+
+    def _batch_for(self, index: int, dp_rank: int) -> torch.Tensor:
         # every sample is seeded by its own index, so the token stream does not depend on how it
         # is cut into batches (a batch of 4 equals two consecutive batches of 2)
         rows = []
         for j in range(self.local_batch_size):
             sample = index * self.local_batch_size + j
-            g = torch.Generator().manual_seed(hash((self.config.seed, self.dp_rank, sample)) & (2**63 - 1))
+            g = torch.Generator().manual_seed(hash((self.config.seed, dp_rank, sample)) & (2**63 - 1))
             rows.append(torch.randint(0, self.vocab_size, (self.seq_len + 1,), generator=g))
         t = torch.stack(rows)
         if self.config.pin_memory and torch.cuda.is_available():

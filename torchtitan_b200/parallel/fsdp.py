@@ -28,9 +28,24 @@ def _disable_grad_division(m) -> None:
             mod.set_gradient_divide_factor(1.0)
 
 
+def _local_tensor_mode_active() -> bool:
+    try:
+        from torch.distributed._local_tensor import local_tensor_mode
+    except ImportError:
+        return False
+    return local_tensor_mode() is not None
+
+
 def apply_fsdp(model: nn.Module, dp_mesh: Any, *, param_dtype: torch.dtype, reduce_dtype: torch.dtype,
                pp_enabled: bool = False, cpu_offload: bool = False, reshard_after_forward_policy: str = "default",
                ep_degree: int = 1, edp_mesh: Any = None) -> nn.Module:
+    if _local_tensor_mode_active():
+        # FSDP2 frees and regrows parameter storage, which LocalTensor (one process simulating
+        # every rank) does not have: a data-parallel mesh of one needs no wrap there
+        if dp_mesh is None or dp_mesh.size() == 1:
+            return model
+        raise NotImplementedError("comm.mode=local_tensor with FSDP (dp_shard > 1): torch's FSDP2 cannot resize "
+                                  "LocalTensor storage; simulate TP/CP/PP meshes with dp_shard = 1 or use gloo ranks")
     # forward inputs are not cast: activations are already in the param dtype
     # (bf16 embedding output) and the fp32 RoPE tables must stay fp32
     mp = MixedPrecisionPolicy(param_dtype=param_dtype, reduce_dtype=reduce_dtype, cast_forward_inputs=False)

@@ -138,26 +138,39 @@ def tp_linear(x: torch.Tensor, w: torch.Tensor, mode: str, group, sequence_paral
 
 
 # ------------------------------------------------------------ vocab-parallel CE
+def _per_rank(fn):
+    """Run ``fn`` once per simulated rank under LocalTensorMode (rank-dependent offsets into a
+    plain tensor); unchanged otherwise."""
+    try:
+        from torch.distributed._local_tensor import maybe_run_for_local_tensor
+    except ImportError:
+        return fn
+    return maybe_run_for_local_tensor(fn)
+
+
+@_per_rank
+def _shift_labels(labels: torch.Tensor, rank: int, vloc: int) -> torch.Tensor:
+    return labels - rank * vloc
+
+
 class _VocabParallelCE(torch.autograd.Function):
     """Sum CE over tokens with logits sharded on the vocab dim across ``group``."""
 
     @staticmethod
-    def forward(ctx, logits, labels, group, ignore_index):
+    def forward(ctx, logits, labels, group, ignore_index, rank):
         lf = logits.float()
-        rank, ws = dist.get_rank(group), dist.get_world_size(group)
+        ws = dist.get_world_size(group)
         vloc = lf.shape[-1]
-        lo = rank * vloc
         mx = lf.max(-1).values
         dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
         ex = torch.exp(lf - mx[:, None])
         se = ex.sum(-1)
         dist.all_reduce(se, group=group)
         valid = labels != ignore_index
-        local_lab = labels - lo
+        local_lab = _shift_labels(labels, rank, vloc)
         mine = valid & (local_lab >= 0) & (local_lab < vloc)
-        tgt = torch.zeros_like(mx)
         idx = local_lab.clamp(0, vloc - 1)
-        tgt[mine] = lf.gather(1, idx[:, None])[:, 0][mine]
+        tgt = torch.where(mine, lf.gather(1, idx[:, None])[:, 0], 0.0)
         dist.all_reduce(tgt, group=group)
         lse = mx + se.log()
         loss = ((lse - tgt) * valid).sum()
@@ -169,13 +182,17 @@ class _VocabParallelCE(torch.autograd.Function):
     def backward(ctx, g):
         ex, se, idx, mine, valid = ctx.saved_tensors
         p = ex / se[:, None]
-        p[mine, idx[mine]] -= 1.0
+        p.scatter_add_(1, idx[:, None], -mine.to(p.dtype)[:, None])
         p *= (valid.float() * g)[:, None]
-        return p.to(ctx.dtype), None, None, None
+        return p.to(ctx.dtype), None, None, None, None
 
 
-def vocab_parallel_cross_entropy_sum(logits, labels, group, ignore_index=-100):
-    return _VocabParallelCE.apply(logits.flatten(0, -2), labels.flatten(), group, ignore_index)
+def vocab_parallel_cross_entropy_sum(logits, labels, group, ignore_index=-100, rank=None):
+    """``rank``: this rank's index in ``group`` (default ``dist.get_rank(group)``; the mesh's
+    ``get_local_rank()`` carries the per-rank value when one process simulates every rank)."""
+    if rank is None:
+        rank = dist.get_rank(group)
+    return _VocabParallelCE.apply(logits.flatten(0, -2), labels.flatten(), group, ignore_index, rank)
 
 
 # ---------------------------------------------------------------- application
@@ -226,6 +243,12 @@ def wrap_replicated_norm(norm: nn.Module, tp_mesh) -> None:
     norm.forward = fwd
 
 
+@_per_rank
+def _seq_shard(tokens: torch.Tensor, r: int, ws: int) -> torch.Tensor:
+    S = tokens.shape[1]
+    return tokens[:, r * S // ws:(r + 1) * S // ws]
+
+
 def _tp_embed_and_head(model: nn.Module, tp_mesh, loss_parallel: bool, sequence_parallel: bool) -> None:
     """Embedding replicated (embeds the local sequence shard under SP), final norm
     sequence-parallel, output head column-parallel over the vocabulary."""
@@ -240,8 +263,8 @@ def _tp_embed_and_head(model: nn.Module, tp_mesh, loss_parallel: bool, sequence_
         def emb_fwd(tokens, _emb=emb):
             w = grad_all_reduce(_emb.weight.to_local(), group) if sequence_parallel else _emb.weight.to_local()
             if sequence_parallel:
-                r, S = dist.get_rank(group), tokens.shape[1]
-                tokens = tokens[:, r * S // ws:(r + 1) * S // ws]
+                r = tp_mesh.get_local_rank()  # per rank under LocalTensorMode too
+                tokens = _seq_shard(tokens, r, ws)
             return nn.functional.embedding(tokens, w)
 
         emb.forward = emb_fwd
@@ -259,6 +282,7 @@ def _tp_embed_and_head(model: nn.Module, tp_mesh, loss_parallel: bool, sequence_
 
             model.output.forward = out_fwd
     model._tp_group = group
+    model._tp_rank = tp_mesh.get_local_rank()
     model._tp_loss_parallel = loss_parallel
     model._sp_degree = ws if sequence_parallel else 1
 
@@ -424,6 +448,7 @@ def apply_tp_kimi(model: nn.Module, tp_mesh, *, loss_parallel: bool) -> None:
 
             model.lm_head.forward = out_fwd
     model._tp_group = group
+    model._tp_rank = tp_mesh.get_local_rank()
     model._tp_loss_parallel = loss_parallel
     model._sp_degree = 1
 

@@ -38,6 +38,9 @@ def _ensure_env_single_process() -> None:
         s.close()
 
 
+_LOCAL_TENSOR_MODE = None
+
+
 def init_distributed(comm: Any, *, enable_cpu_backend: bool = False, base_folder: str = "",
                      backend: str | None = None) -> int:
     """Initialise the default process group and return the world size."""
@@ -52,9 +55,20 @@ def init_distributed(comm: Any, *, enable_cpu_backend: bool = False, base_folder
         dist.init_process_group("fake", store=FakeStore(), rank=0, world_size=ws)
         return ws
     if mode == "local_tensor":
-        raise NotImplementedError("comm.mode=local_tensor (all ranks simulated numerically in one process) is "
-                                  "not supported: this framework's CUDA kernels have no LocalTensor dispatch; use "
-                                  "fake_backend for dry runs or gloo ranks on CPU")
+        # One process simulates every rank: a fake process group carries the collectives and
+        # LocalTensorMode runs each rank's shard of every DTensor op numerically
+        # (reference: distributed/utils.py:296-336). CPU debugging only; CUDA kernels of this
+        # package have no LocalTensor dispatch, so the model falls back to PyTorch ops.
+        from torch.distributed import _local_tensor
+        from torch.testing._internal.distributed.fake_pg import FakeStore
+
+        ws = int(os.environ.get("NGPU", os.environ["WORLD_SIZE"]))
+        dist.init_process_group("fake", store=FakeStore(), rank=0, world_size=ws)
+        lm = _local_tensor.LocalTensorMode(ws)
+        lm.__enter__()
+        global _LOCAL_TENSOR_MODE
+        _LOCAL_TENSOR_MODE = lm
+        return ws
     if backend is None:
         backend = "nccl" if torch.cuda.is_available() else "gloo"
         if enable_cpu_backend and backend == "nccl":

@@ -266,7 +266,7 @@ class Trainer(Stateful, Configurable):
         if getattr(m, "_tp_loss_parallel", False):
             from torchtitan_b200.parallel.tensor_parallel import vocab_parallel_cross_entropy_sum
 
-            return vocab_parallel_cross_entropy_sum(pred, labels, m._tp_group, IGNORE_INDEX)
+            return vocab_parallel_cross_entropy_sum(pred, labels, m._tp_group, IGNORE_INDEX, getattr(m, "_tp_rank", None))
         return self.loss_fn(pred, labels)
 
     @torch.no_grad()
