@@ -53,12 +53,14 @@ def test_linear_autograd():
     assert _rel(w.grad, wr.grad) < 1e-2
 
 
-@pytest.mark.parametrize("dim", [256, 4096, 2304])
-def test_rmsnorm(dim):
+@pytest.mark.parametrize("rows,dim", [(300, 256), (300, 4096), (300, 2304), (5000, 4096), (3001, 8192),
+                                      (1500, 16384), (7001, 1024)])
+def test_rmsnorm(rows, dim):
+    """Includes row counts above the persistent grid (several rows per CTA, odd tails)."""
     from torchtitan_b200 import ops
 
     torch.manual_seed(2)
-    x = torch.randn(300, dim, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    x = torch.randn(rows, dim, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     w = (1 + 0.1 * torch.randn(dim, device="cuda")).to(torch.bfloat16).requires_grad_()
     y = ops.rms_norm(x, w, 1e-5)
     g = torch.randn_like(y)

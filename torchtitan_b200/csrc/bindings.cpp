@@ -93,8 +93,7 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor w, Tensor rstd) {
   Tensor dx = torch::empty_like(x);
   const int64_t rows = x.size(0), dim = x.size(1);
   int dev = x.get_device();
-  int nparts = static_cast<int>(std::min<int64_t>(rows, 2 * ttb::num_sms(dev)));
-  nparts = std::max(nparts, 1);
+  const int nparts = ttb::rmsnorm_bwd_parts(rows, dim, ttb::num_sms(dev));
   Tensor part = torch::empty({nparts, dim}, x.options().dtype(at::kFloat));
   Tensor dw = torch::empty({dim}, x.options().dtype(at::kFloat));
   if (rows > 0) {

@@ -26,6 +26,39 @@ __device__ __forceinline__ void merge(float& m, float& s, float m2, float s2) {
   m = mn;
 }
 
+__device__ __forceinline__ float ex2f(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Online (max, sum-exp) of 8 logits into a thread's running pair: the sum is kept relative to
+// the running maximum and rescaled only when that maximum grows (one exponential per logit;
+// exponentials as exp2 of x*log2(e) - m*log2(e), one FMA each).
+__device__ __forceinline__ void accum8(const V8& v, float& m, float& s) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  float f[8];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 t = __bfloat1622float2(v.h[j]);
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+  const float lm = fmaxf(fmaxf(fmaxf(f[0], f[1]), fmaxf(f[2], f[3])), fmaxf(fmaxf(f[4], f[5]), fmaxf(f[6], f[7])));
+  if (lm > m) {
+    s *= ex2f((m - lm) * kLog2e);  // m = -inf: s is 0 and stays 0
+    m = lm;
+  }
+  const float mb = -m * kLog2e;
+  float a = 0.f, b = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    a += ex2f(fmaf(f[j], kLog2e, mb));
+    b += ex2f(fmaf(f[j + 1], kLog2e, mb));
+  }
+  s += a + b;
+}
+
 __global__ void __launch_bounds__(NT) ce_fwd_kernel(const bf16* __restrict__ logits, const int64_t* __restrict__ labels,
                                                     float* __restrict__ loss_rows, float* __restrict__ lse_out,
                                                     int64_t V, int64_t ignore_index) {
@@ -33,23 +66,14 @@ __global__ void __launch_bounds__(NT) ce_fwd_kernel(const bf16* __restrict__ log
   const bf16* x = logits + row * V;
   float m = -INFINITY, s = 0.f;
   const int64_t nv = V / 8;
-  for (int64_t i = threadIdx.x; i < nv; i += NT) {
-    V8 v = reinterpret_cast<const V8*>(x)[i];
-    float f[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 t = __bfloat1622float2(v.h[j]);
-      f[2 * j] = t.x;
-      f[2 * j + 1] = t.y;
-    }
-    float lm = f[0];
-#pragma unroll
-    for (int j = 1; j < 8; ++j) lm = fmaxf(lm, f[j]);
-    float ls = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ls += __expf(f[j] - lm);
-    merge(m, s, lm, ls);
+  const V8* xv = reinterpret_cast<const V8*>(x);
+  int64_t i = threadIdx.x;
+  for (; i + NT < nv; i += 2 * NT) {  // two independent 16-byte loads in flight per thread
+    const V8 v0 = xv[i], v1 = xv[i + NT];
+    accum8(v0, m, s);
+    accum8(v1, m, s);
   }
+  if (i < nv) accum8(xv[i], m, s);
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     const float m2 = __shfl_xor_sync(0xffffffffu, m, o);

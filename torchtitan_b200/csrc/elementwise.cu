@@ -62,104 +62,146 @@ __device__ __forceinline__ float block_sum(float v, float* scratch) {
   return r;
 }
 
-// One CTA per row; each thread owns VPT vectors of 8 elements kept in registers.
-template <int NT, int VPT>
-__global__ void __launch_bounds__(NT) rmsnorm_fwd_kernel(const bf16* __restrict__ x, const void* __restrict__ w,
-                                                         bf16* __restrict__ y, float* __restrict__ rstd_out, int dim,
-                                                         float eps, int w_fp32) {
-  __shared__ float scratch[32];
-  const int64_t row = blockIdx.x;
-  const bf16* xr = x + row * dim;
-  float v[VPT][8];
-  float ss = 0.f;
+__device__ __forceinline__ void unpack8(const V8& v, float (&f)[8]) {
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = (threadIdx.x + i * NT) * 8;
-    if (c < dim) {
-      load8(xr + c, v[i]);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
-    }
-  }
-  ss = block_sum<NT>(ss, scratch);
-  const float r = rsqrtf(ss / dim + eps);
-  if (threadIdx.x == 0) rstd_out[row] = r;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = (threadIdx.x + i * NT) * 8;
-    if (c < dim) {
-      float wf[8], o[8];
-      loadw8(w, w_fp32, c, wf);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = v[i][j] * r * wf[j];
-      store8(y + row * dim + c, o);
-    }
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(v.h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
   }
 }
 
-// Persistent CTAs stride over rows; dw partial sums per CTA in registers.
-template <int NT, int VPT>
-__global__ void __launch_bounds__(NT) rmsnorm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
-                                                         const void* __restrict__ w, const float* __restrict__ rstd,
-                                                         bf16* __restrict__ dx, float* __restrict__ dw_partial,
-                                                         int64_t rows, int dim, int w_fp32) {
-  __shared__ float scratch[32];
-  float dwacc[VPT][8];
-  float wf[VPT][8];
+// RMSNorm: a group of WPR warps owns one row at a time (no CTA-wide barrier); each lane keeps
+// VPL 16-byte vectors of the row packed in registers, so one row is read once and written once.
+// Groups stride over rows (persistent grid); the sum of squares (forward) or of dy*w*x
+// (backward) is reduced by shuffles and, for WPR > 1, through a double-buffered shared slot
+// with one named barrier per row and group. The backward keeps the weight-gradient partial sums
+// of its columns in registers and writes one partial row per group at the end.
+constexpr int kNormThreads = 256;
+
+template <int WPR>
+__device__ __forceinline__ float group_sum(float v, float (*slot)[8], int parity, int group, int sub) {
+  v = warp_sum(v);
+  if constexpr (WPR == 1) {
+    return v;
+  } else {
+    if ((threadIdx.x & 31) == 0) slot[parity][group * WPR + sub] = v;
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + group), "r"(32 * WPR) : "memory");
+    float t = 0.f;
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = (threadIdx.x + i * NT) * 8;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) dwacc[i][j] = 0.f;
-    if (c < dim) loadw8(w, w_fp32, c, wf[i]);
+    for (int k = 0; k < WPR; ++k) t += slot[parity][group * WPR + k];
+    return t;
   }
-  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
-    const float r = rstd[row];
-    float xv[VPT][8], gv[VPT][8];
-    float dot = 0.f;
+}
+
+template <int WPR, int VPL, bool BWD, int MINB>
+__global__ void __launch_bounds__(kNormThreads, MINB) rmsnorm_rows_kernel(
+    const bf16* __restrict__ x, const bf16* __restrict__ dy, const void* __restrict__ w, float* __restrict__ rstd,
+    bf16* __restrict__ out, float* __restrict__ dw_partial, int64_t rows, int dim, float eps, int w_fp32) {
+  constexpr int kGroups = kNormThreads / 32 / WPR;
+  __shared__ float slot[2][8];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int group = warp / WPR, sub = warp % WPR;
+  const int v0 = sub * 32 + lane;  // this lane's first vector; the others follow every 32*WPR
+  float dwacc[BWD ? VPL : 1][8];
+  if constexpr (BWD) {
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int c = (threadIdx.x + i * NT) * 8;
+    for (int i = 0; i < VPL; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dwacc[i][j] = 0.f;
+  }
+  int parity = 0;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kGroups + group; row < rows;
+       row += static_cast<int64_t>(gridDim.x) * kGroups, parity ^= 1) {
+    V8 xv8[VPL], gv8[BWD ? VPL : 1];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = (v0 + i * 32 * WPR) * 8;
       if (c < dim) {
-        load8(x + row * dim + c, xv[i]);
-        load8(dy + row * dim + c, gv[i]);
+        xv8[i] = *reinterpret_cast<const V8*>(x + row * dim + c);
+        if constexpr (BWD) gv8[i] = *reinterpret_cast<const V8*>(dy + row * dim + c);
+      }
+    }
+    const float r_in = BWD ? rstd[row] : 0.f;
+    float acc = 0.f;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float xh = xv[i][j] * r;
-          dot += gv[i][j] * wf[i][j] * xh;
-          dwacc[i][j] += gv[i][j] * xh;
+    for (int i = 0; i < VPL; ++i) {
+      const int c = (v0 + i * 32 * WPR) * 8;
+      if (c < dim) {
+        float xv[8];
+        unpack8(xv8[i], xv);
+        if constexpr (BWD) {
+          float gv[8], wf[8];
+          unpack8(gv8[i], gv);
+          loadw8(w, w_fp32, c, wf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float xh = xv[j] * r_in;
+            acc += gv[j] * wf[j] * xh;
+            dwacc[i][j] += gv[j] * xh;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc += xv[j] * xv[j];
         }
       }
     }
-    dot = block_sum<NT>(dot, scratch) / dim;
+    acc = group_sum<WPR>(acc, slot, parity, group, sub);
+    const float r = BWD ? r_in : rsqrtf(acc / dim + eps);
+    const float dot = BWD ? acc / dim : 0.f;
+    if (!BWD && sub == 0 && lane == 0) rstd[row] = r;
 #pragma unroll
-    for (int i = 0; i < VPT; ++i) {
-      const int c = (threadIdx.x + i * NT) * 8;
+    for (int i = 0; i < VPL; ++i) {
+      const int c = (v0 + i * 32 * WPR) * 8;
       if (c < dim) {
-        float o[8];
+        float xv[8], wf[8], o[8];
+        unpack8(xv8[i], xv);
+        loadw8(w, w_fp32, c, wf);
+        if constexpr (BWD) {
+          float gv[8];
+          unpack8(gv8[i], gv);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = r * (gv[i][j] * wf[i][j] - xv[i][j] * r * dot);
-        store8(dx + row * dim + c, o);
+          for (int j = 0; j < 8; ++j) o[j] = r * (gv[j] * wf[j] - xv[j] * r * dot);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = xv[j] * r * wf[j];
+        }
+        store8(out + row * dim + c, o);
       }
     }
   }
+  if constexpr (BWD) {
+    float* dst_row = dw_partial + (static_cast<int64_t>(blockIdx.x) * kGroups + group) * dim;
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = (threadIdx.x + i * NT) * 8;
-    if (c < dim) {
-      float* dst = dw_partial + static_cast<int64_t>(blockIdx.x) * dim + c;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) dst[j] = dwacc[i][j];
+    for (int i = 0; i < VPL; ++i) {
+      const int c = (v0 + i * 32 * WPR) * 8;
+      if (c < dim) {
+        float4* dst = reinterpret_cast<float4*>(dst_row + c);
+        dst[0] = make_float4(dwacc[i][0], dwacc[i][1], dwacc[i][2], dwacc[i][3]);
+        dst[1] = make_float4(dwacc[i][4], dwacc[i][5], dwacc[i][6], dwacc[i][7]);
+      }
     }
   }
 }
 
-__global__ void reduce_rows_kernel(const float* __restrict__ p, float* __restrict__ out, int64_t nparts, int64_t dim) {
-  const int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-  if (c >= dim) return;
+// Column sums of a [nparts, dim] fp32 matrix: 32 columns per CTA, 8 warps split the rows and
+// combine through shared memory (coalesced 128-byte row segments per warp).
+__global__ void __launch_bounds__(256) reduce_rows_kernel(const float* __restrict__ p, float* __restrict__ out,
+                                                         int64_t nparts, int64_t dim) {
+  __shared__ float part[8][33];
+  const int lane = threadIdx.x % 32, wp = threadIdx.x / 32;
+  const int64_t c = blockIdx.x * 32LL + lane;
   float s = 0.f;
-  for (int64_t i = 0; i < nparts; ++i) s += p[i * dim + c];
-  out[c] = s;
+  if (c < dim)
+    for (int64_t i = wp; i < nparts; i += 8) s += p[i * dim + c];
+  part[wp][lane] = s;
+  __syncthreads();
+  if (wp == 0) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += part[k][lane];
+    if (c < dim) out[c] = t;
+  }
 }
 
 // x: [B,S,H,D] bf16 contiguous; rotate interleaved pairs (2i, 2i+1) by angle
@@ -223,19 +265,56 @@ __global__ void swiglu_bwd_kernel(const bf16* __restrict__ dy, const bf16* __res
   store8(db + t * 8, ob);
 }
 
-template <int NT, int VPT>
-void launch_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows, int64_t dim, float eps, int w_fp32,
-                cudaStream_t s) {
-  rmsnorm_fwd_kernel<NT, VPT><<<static_cast<unsigned>(rows), NT, 0, s>>>(
-      static_cast<const bf16*>(x), w, static_cast<bf16*>(y), rstd, static_cast<int>(dim), eps, w_fp32);
+// Row-group shapes: (warps per row, vectors per lane, resident CTAs per SM). The forward keeps
+// up to 8 vectors (128 bytes) of x per lane, the backward up to 4 of x and 4 of dy (plus the
+// 32 fp32 weight-gradient sums); 16384-wide rows use 8 warps and 8 vectors.
+struct NormShape {
+  int wpr, vpl, minb;
+};
+NormShape norm_shape(int64_t dim, bool bwd) {
+  const int64_t vecs = dim / 8;
+  const int cap = bwd ? 4 : 8;
+  int wpr = 1;
+  while (wpr < 8 && vecs > 32LL * wpr * cap) wpr *= 2;
+  int vpl = static_cast<int>((vecs + 32LL * wpr - 1) / (32LL * wpr));
+  vpl = vpl <= 1 ? 1 : vpl <= 2 ? 2 : vpl <= 4 ? 4 : 8;
+  const int minb = bwd ? (vpl <= 2 ? 4 : (vpl == 4 ? 2 : 1)) : (vpl <= 4 ? 4 : 3);
+  return {wpr, vpl, minb};
 }
 
-template <int NT, int VPT>
-void launch_bwd(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dwp, int64_t rows,
-                int64_t dim, int w_fp32, int nparts, cudaStream_t s) {
-  rmsnorm_bwd_kernel<NT, VPT><<<nparts, NT, 0, s>>>(static_cast<const bf16*>(dy), static_cast<const bf16*>(x), w,
-                                                    rstd, static_cast<bf16*>(dx), dwp, rows, static_cast<int>(dim),
-                                                    w_fp32);
+template <int WPR, int VPL, bool BWD, int MINB>
+void launch_rows(const void* x, const void* dy, const void* w, float* rstd, void* out, float* dwp, int64_t rows,
+                 int64_t dim, float eps, int w_fp32, int grid, cudaStream_t s) {
+  rmsnorm_rows_kernel<WPR, VPL, BWD, MINB><<<static_cast<unsigned>(grid), kNormThreads, 0, s>>>(
+      static_cast<const bf16*>(x), static_cast<const bf16*>(dy), w, rstd, static_cast<bf16*>(out), dwp, rows,
+      static_cast<int>(dim), eps, w_fp32);
+}
+
+template <bool BWD>
+void dispatch_rows(const void* x, const void* dy, const void* w, float* rstd, void* out, float* dwp, int64_t rows,
+                   int64_t dim, float eps, int w_fp32, int grid, cudaStream_t s) {
+  const NormShape sh = norm_shape(dim, BWD);
+#define TTB_NORM_CASE(W, V, M)                                                                \
+  if (sh.wpr == W && sh.vpl == V && sh.minb == M) {                                           \
+    launch_rows<W, V, BWD, M>(x, dy, w, rstd, out, dwp, rows, dim, eps, w_fp32, grid, s); \
+    return;                                                                                   \
+  }
+  if constexpr (BWD) {
+    TTB_NORM_CASE(1, 1, 4) TTB_NORM_CASE(1, 2, 4) TTB_NORM_CASE(1, 4, 2) TTB_NORM_CASE(2, 4, 2)
+    TTB_NORM_CASE(4, 4, 2) TTB_NORM_CASE(8, 4, 2) TTB_NORM_CASE(8, 8, 1)
+  } else {
+    TTB_NORM_CASE(1, 1, 4) TTB_NORM_CASE(1, 2, 4) TTB_NORM_CASE(1, 4, 4) TTB_NORM_CASE(1, 8, 3)
+    TTB_NORM_CASE(2, 8, 3) TTB_NORM_CASE(4, 8, 3) TTB_NORM_CASE(8, 8, 3)
+  }
+#undef TTB_NORM_CASE
+  throw std::runtime_error("rmsnorm: no kernel for this width");
+}
+
+int norm_grid(int64_t rows, int64_t dim, bool bwd, int sms) {
+  const NormShape sh = norm_shape(dim, bwd);
+  const int64_t groups = kNormThreads / 32 / sh.wpr;
+  const int64_t need = (rows + groups - 1) / groups;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(need, static_cast<int64_t>(sms) * sh.minb)));
 }
 
 }  // namespace
@@ -243,32 +322,32 @@ void launch_bwd(const void* dy, const void* x, const void* w, const float* rstd,
 void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int64_t rows, int64_t dim, float eps, int w_fp32,
                  cudaStream_t s) {
   if (dim % 8) throw std::runtime_error("rmsnorm: dim must be a multiple of 8");
-  const int64_t vecs = dim / 8;
+  if (dim > 16384) throw std::runtime_error("rmsnorm: dim > 16384 unsupported");
   if (rows == 0) return;
-  if (vecs <= 128) launch_fwd<128, 1>(x, w, y, rstd, rows, dim, eps, w_fp32, s);
-  else if (vecs <= 256) launch_fwd<256, 1>(x, w, y, rstd, rows, dim, eps, w_fp32, s);
-  else if (vecs <= 512) launch_fwd<256, 2>(x, w, y, rstd, rows, dim, eps, w_fp32, s);
-  else if (vecs <= 1024) launch_fwd<256, 4>(x, w, y, rstd, rows, dim, eps, w_fp32, s);
-  else if (vecs <= 2048) launch_fwd<512, 4>(x, w, y, rstd, rows, dim, eps, w_fp32, s);
-  else throw std::runtime_error("rmsnorm: dim > 16384 unsupported");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  dispatch_rows<false>(x, nullptr, w, rstd, y, nullptr, rows, dim, eps, w_fp32, norm_grid(rows, dim, false, num_sms(dev)),
+                       s);
   check_cuda(cudaGetLastError(), "rmsnorm_fwd");
+}
+
+int rmsnorm_bwd_parts(int64_t rows, int64_t dim, int sms) {
+  return norm_grid(rows, dim, true, sms) * (kNormThreads / 32 / norm_shape(dim, true).wpr);
 }
 
 void rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw_partial,
                  int64_t rows, int64_t dim, int w_fp32, int nparts, cudaStream_t s) {
   if (dim % 8) throw std::runtime_error("rmsnorm: dim must be a multiple of 8");
-  const int64_t vecs = dim / 8;
-  if (vecs <= 128) launch_bwd<128, 1>(dy, x, w, rstd, dx, dw_partial, rows, dim, w_fp32, nparts, s);
-  else if (vecs <= 256) launch_bwd<256, 1>(dy, x, w, rstd, dx, dw_partial, rows, dim, w_fp32, nparts, s);
-  else if (vecs <= 512) launch_bwd<256, 2>(dy, x, w, rstd, dx, dw_partial, rows, dim, w_fp32, nparts, s);
-  else if (vecs <= 1024) launch_bwd<256, 4>(dy, x, w, rstd, dx, dw_partial, rows, dim, w_fp32, nparts, s);
-  else if (vecs <= 2048) launch_bwd<512, 4>(dy, x, w, rstd, dx, dw_partial, rows, dim, w_fp32, nparts, s);
-  else throw std::runtime_error("rmsnorm: dim > 16384 unsupported");
+  if (dim > 16384) throw std::runtime_error("rmsnorm: dim > 16384 unsupported");
+  const int groups = kNormThreads / 32 / norm_shape(dim, true).wpr;
+  if (nparts % groups) throw std::runtime_error("rmsnorm_bwd: partial rows must come from rmsnorm_bwd_parts");
+  dispatch_rows<true>(x, dy, w, const_cast<float*>(rstd), dx, dw_partial, rows, dim, 0.f, w_fp32, nparts / groups,
+                      s);
   check_cuda(cudaGetLastError(), "rmsnorm_bwd");
 }
 
 void reduce_rows_f32(const float* partial, float* out, int64_t nparts, int64_t dim, cudaStream_t s) {
-  reduce_rows_kernel<<<static_cast<unsigned>((dim + 255) / 256), 256, 0, s>>>(partial, out, nparts, dim);
+  reduce_rows_kernel<<<static_cast<unsigned>((dim + 31) / 32), 256, 0, s>>>(partial, out, nparts, dim);
   check_cuda(cudaGetLastError(), "reduce_rows");
 }
 

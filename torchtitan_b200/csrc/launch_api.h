@@ -42,6 +42,7 @@ void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int64_t row
                  cudaStream_t s);
 void rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw_partial,
                  int64_t rows, int64_t dim, int w_fp32, int nparts, cudaStream_t s);
+int rmsnorm_bwd_parts(int64_t rows, int64_t dim, int sms);
 void reduce_rows_f32(const float* partial, float* out, int64_t nparts, int64_t dim, cudaStream_t s);
 void rope_apply(const void* x, void* y, const float* cos, const float* sin, int64_t B, int64_t S, int64_t H,
                 int64_t D, int64_t cs_batch_stride, bool inverse, cudaStream_t s);

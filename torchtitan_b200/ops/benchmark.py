@@ -98,9 +98,19 @@ def bench_memory_bound(ext, out):
     T, Dm, V = 8192, 4096, 128256
     x = torch.randn(T, Dm, device="cuda", dtype=torch.bfloat16)
     w = torch.ones(Dm, device="cuda", dtype=torch.bfloat16)
-    ms = time_fn(lambda: ext.rmsnorm_fwd(x, w, 1e-5))
-    out.append({"kernel": "rmsnorm_fwd", "ms": ms, "gbs": 2 * x.numel() * 2 / ms / 1e6})
-    print(json.dumps(out[-1]), flush=True)
+    # rows x 4096: 8192 rows (64 MB, the 8B step's shape) and 65536 rows (512 MB, well above
+    # L2, so the dirty lines of the L2 flush no longer dominate)
+    for rows in (T, 8 * T):
+        xr = torch.randn(rows, Dm, device="cuda", dtype=torch.bfloat16)
+        ms = time_fn(lambda: ext.rmsnorm_fwd(xr, w, 1e-5))
+        out.append({"kernel": "rmsnorm_fwd", "rows": rows, "ms": ms, "gbs": 2 * xr.numel() * 2 / ms / 1e6})
+        print(json.dumps(out[-1]), flush=True)
+        _, rstd = ext.rmsnorm_fwd(xr, w, 1e-5)
+        dy = torch.randn_like(xr)
+        ms = time_fn(lambda: ext.rmsnorm_bwd(dy, xr, w, rstd))
+        out.append({"kernel": "rmsnorm_bwd", "rows": rows, "ms": ms, "gbs": 3 * xr.numel() * 2 / ms / 1e6})
+        print(json.dumps(out[-1]), flush=True)
+        del xr, dy
     a = torch.randn(T, 14336, device="cuda", dtype=torch.bfloat16)
     b = torch.randn_like(a)
     ms = time_fn(lambda: ext.swiglu_fwd(a, b))
@@ -291,7 +301,8 @@ def bench_muon(ext, out):
 def profile_case(ext, case: str) -> None:
     """Small fixed workloads for ncu captures of one kernel (``--only case:<name>``):
     gemm2 (bf16 4096^3), attn_fwd / attn_bwd (causal B1 S4096 H32/8 D128), kda (B1 T4096 H32
-    K=V=128 forward+backward), adamw (4 x 64 Mi fp32 params, bf16 grads). Each runs the op a few
+    K=V=128 forward+backward), adamw (4 x 64 Mi fp32 params, bf16 grads), rmsnorm (16384 x 4096
+    forward and backward). Each runs the op a few
     times so ``-s`` can skip warm-up launches."""
     from torchtitan_b200 import ops
 
@@ -320,6 +331,12 @@ def profile_case(ext, case: str) -> None:
         for _ in range(2):
             o, _ = kda.chunk_kda(q, k, v, g, beta)
             o.backward(torch.randn_like(o))
+    elif case == "rmsnorm":
+        x = torch.randn(16384, 4096, device="cuda", dtype=torch.bfloat16)
+        w = torch.ones(4096, device="cuda", dtype=torch.bfloat16)
+        for _ in range(3):
+            _, rstd = ext.rmsnorm_fwd(x, w, 1e-5)
+            ext.rmsnorm_bwd(x, x, w, rstd)
     elif case == "adamw":
         n = 64 * 2 ** 20
         ps = [torch.randn(n, device="cuda") for _ in range(4)]
