@@ -21,8 +21,12 @@ def test_mx_quantize_matches_reference(R, C):
     assert torch.equal(sf.cpu(), rs)
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 384, 512), (300, 200, 1024), (4096, 4096, 4096)])
-def test_mx_gemm_matches_dequantized_product(M, N, K):
+@pytest.mark.parametrize("tile_n", [128, 256])
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 384, 512), (300, 200, 1024), (4096, 4096, 4096),
+                                   (640, 1280, 384)])
+def test_mx_gemm_matches_dequantized_product(M, N, K, tile_n):
+    """Both tile widths; N = 384 and 200 leave the last 256-wide tile with one or no second
+    scale record."""
     from torchtitan_b200.ops._ext import ext
     from torchtitan_b200.ops.mx_gemm import mx_dequantize_ref, mx_gemm, mx_quantize
 
@@ -31,7 +35,7 @@ def test_mx_gemm_matches_dequantized_product(M, N, K):
     b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.1
     qa, sa = mx_quantize(a)
     qb, sb = mx_quantize(b)
-    d = mx_gemm(qa, sa, qb, sb)
+    d = ext().gemm_mxfp8(qa, sa, qb, sb, tile_n)
     torch.cuda.synchronize()
     assert ext().mxgemm_error_code(True) == 0
     ref = (mx_dequantize_ref(qa, sa).cuda() @ mx_dequantize_ref(qb, sb).cuda().t())

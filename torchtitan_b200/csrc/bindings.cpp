@@ -398,7 +398,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     ttb::mx_quantize(x.data_ptr(), R, C, x.stride(0), codes.data_ptr(), sf.data_ptr(), stream());
     return std::vector<Tensor>{codes, sf};
   });
-  m.def("gemm_mxfp8", [](Tensor a, Tensor sfa, Tensor b, Tensor sfb) {
+  m.def("gemm_mxfp8", [](Tensor a, Tensor sfa, Tensor b, Tensor sfb, int64_t tile_n) {
     TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kByte && b.scalar_type() == at::kByte,
                 "gemm_mxfp8: uint8 FP8 codes on CUDA");
     TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.is_contiguous() && b.is_contiguous(),
@@ -408,9 +408,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                 "gemm_mxfp8: scale records too small");
     c10::cuda::CUDAGuard g(a.device());
     auto d = torch::empty({M, N}, a.options().dtype(at::kBFloat16));
-    ttb::gemm_mxfp8(a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), d.data_ptr(), M, N, K, stream());
+    ttb::gemm_mxfp8(a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), d.data_ptr(), M, N, K, stream(),
+                    static_cast<int>(tile_n));
     return d;
-  });
+  }, py::arg("a"), py::arg("sfa"), py::arg("b"), py::arg("sfb"), py::arg("tile_n") = 0);
   m.def("kda_gram_fwd", [](Tensor a, Tensor b, Tensor G, bool strict) {
     for (const Tensor* t : {&a, &b, &G})
       TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 3 &&

@@ -11,14 +11,22 @@
 // for the j-th 32-element group -- i.e. each 32-bit word holds the four
 // scales one row needs for 128 K, which is the TMEM word the MMA reads.
 //
-// Tile 128x128x128 (one scale record per operand per stage), 6-stage ring:
-//   warp 0      producer: TMA for the A/B tiles (128-byte swizzle) and two
-//               512-byte bulk copies for the scale records, one mbarrier
-//   warp 1      TMEM allocator + MMA issuer: per stage, tcgen05.cp of the two
-//               scale records into TMEM (32x128b, broadcast to the 4 lane
-//               quadrants), then 4 MMAs of K=32 selecting scale byte j
-//   warps 2..5  epilogue: TMEM -> registers -> bf16 -> global
-// Two 128-column accumulators let the epilogue of tile i overlap tile i+1.
+// Two tile shapes, one template:
+//   BN = 128: 128x128x128 tiles, 6-stage ring, two 128-column accumulators (the epilogue of
+//             tile i overlaps the MMAs of tile i+1), 4 epilogue warps.
+//   BN = 256: 128x256x128 tiles, 4-stage ring, one 256-column accumulator (the other half of
+//             TMEM holds the scale records). Eight epilogue warps (two per TMEM lane quadrant,
+//             128 columns each) copy the whole accumulator into registers and release it at
+//             once, so the next tile's MMAs wait only for the TMEM reads; the bf16 conversion
+//             and the global stores overlap them. Per MMA of K = 32 the tensor core reads
+//             4 KB of A and 8 KB of B from shared memory for 2*128*256*32 FLOPs, twice the
+//             work per byte of the 128-wide tile, which the shared-memory bandwidth bounds.
+//   warp 0      producer: TMA for the A/B tiles (128-byte swizzle) and 512-byte bulk copies
+//               of the scale records (one for A, BN/128 for B), one mbarrier per stage
+//   warp 1      TMEM allocator + MMA issuer: per stage, tcgen05.cp of the scale records into
+//               TMEM (32x128b, broadcast to the 4 lane quadrants; B's second record four
+//               columns after the first), then 4 MMAs of K=32 selecting scale byte j
+//   warps 2..   epilogue: TMEM -> registers -> bf16 -> global
 // Every wait is bounded; a timeout sets mxgemm_error_code() and the kernel
 // returns after releasing TMEM.  K must be a multiple of 128 (callers pad).
 #include <stdexcept>
@@ -30,23 +38,34 @@
 namespace ttb {
 namespace mx_impl {
 
-constexpr int BM = 128, BN = 128, BK = 128, STAGES = 6;
+constexpr int BM = 128, BK = 128;
 constexpr int A_BYTES = BM * BK;  // fp8
-constexpr int B_BYTES = BN * BK;
 constexpr int SF_BYTES = 512;     // one blocked scale record
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGES * 2 * SF_BYTES + 1024;
-constexpr int NUM_THREADS = 192;
 constexpr int GROUP_M = 8;
 constexpr int TMEM_COLS = 512;
-constexpr int ACC_COLS = BN;                 // fp32 accumulator columns per tile
-constexpr int SF_COL0 = 2 * ACC_COLS;        // scale records after the two accumulators
-constexpr int SF_COLS_PER_STAGE = 8;         // 4 columns SFA + 4 columns SFB
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int ACC_STAGES = BN == 256 ? 1 : 2;
+  static constexpr int EPI_WARPS = BN == 256 ? 8 : 4;
+  static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int B_BYTES = BN * BK;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int SF_STAGE = SF_BYTES * (1 + BN / 128);  // A record + B records
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + STAGES * SF_STAGE + 1024;
+  static constexpr int ACC_COLS = BN;                          // fp32 accumulator columns per tile
+  static constexpr int SF_COL0 = ACC_STAGES * ACC_COLS;        // scale records after the accumulators
+  static constexpr int SF_COLS_PER_STAGE = 4 + 4 * (BN / 128);
+  static_assert(SF_COL0 + STAGES * SF_COLS_PER_STAGE <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
 
 __device__ int g_err;
 
 struct Params {
   int M, N, K;
+  int b_records;  // 128-row scale-record blocks of B (rows rounded up to 128)
   int num_m, num_n, num_k;
   const uint8_t* sfa;  // blocked scale records of A
   const uint8_t* sfb;
@@ -55,12 +74,12 @@ struct Params {
 };
 
 struct Shared {
-  uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
+  uint64_t full[6], empty[6], tfull[2], tempty[2];
   uint32_t tmem_base;
   int abort_flag;
 };
 
-__device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int& tn) {
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int& tn) {  // grouped raster
   const int per_group = GROUP_M * p.num_n;
   const int g = t / per_group;
   const int first_m = g * GROUP_M;
@@ -113,62 +132,72 @@ __device__ __forceinline__ void umma_mx(uint32_t tmem_d, uint64_t adesc, uint64_
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
 }
 
+template <int BN>
 __device__ __forceinline__ void run_producer(const CUtensorMap* tmA, const CUtensorMap* tmB, const Params& p,
                                              Shared& sh, uint8_t* sA, uint8_t* sB, uint8_t* sSF) {
+  using C = Cfg<BN>;
   int stage = 0;
   uint32_t phase = 0;
   const int tiles = p.num_m * p.num_n;
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     int tm, tn;
     tile_coords(t, p, tm, tn);
+    // B's scale records of this tile: 128-row blocks tn*BN/128 .. ; blocks past the padded
+    // rows are not copied (their TMEM columns only scale output columns >= N)
+    const int rb0 = tn * (BN / 128);
+    const int nrec = min(BN / 128, p.b_records - rb0);
     for (int kb = 0; kb < p.num_k; ++kb) {
       if (!mbar_wait(&sh.empty[stage], phase ^ 1, &sh.abort_flag, &g_err, 1)) return;
-      mbar_arrive_expect_tx(&sh.full[stage], STAGE_BYTES + 2 * SF_BYTES);
+      mbar_arrive_expect_tx(&sh.full[stage], C::STAGE_BYTES + (1 + nrec) * SF_BYTES);
       tma_load_2d(sA + stage * A_BYTES, tmA, &sh.full[stage], kb * BK, tm * BM);
-      tma_load_2d(sB + stage * B_BYTES, tmB, &sh.full[stage], kb * BK, tn * BN);
-      uint8_t* sf = sSF + stage * 2 * SF_BYTES;
+      tma_load_2d(sB + stage * C::B_BYTES, tmB, &sh.full[stage], kb * BK, tn * BN);
+      uint8_t* sf = sSF + stage * C::SF_STAGE;
       bulk_load(sf, p.sfa + (static_cast<size_t>(tm) * p.num_k + kb) * SF_BYTES, SF_BYTES, &sh.full[stage]);
-      bulk_load(sf + SF_BYTES, p.sfb + (static_cast<size_t>(tn) * p.num_k + kb) * SF_BYTES, SF_BYTES,
-                &sh.full[stage]);
-      if (++stage == STAGES) {
+      for (int r = 0; r < nrec; ++r)
+        bulk_load(sf + (1 + r) * SF_BYTES, p.sfb + (static_cast<size_t>(rb0 + r) * p.num_k + kb) * SF_BYTES,
+                  SF_BYTES, &sh.full[stage]);
+      if (++stage == C::STAGES) {
         stage = 0;
         phase ^= 1;
       }
     }
   }
-  for (int s = 0; s < STAGES; ++s) {  // drain: every filled stage consumed
+  for (int s = 0; s < C::STAGES; ++s) {  // drain: every filled stage consumed
     if (!mbar_wait(&sh.empty[stage], phase ^ 1, &sh.abort_flag, &g_err, 2)) return;
-    if (++stage == STAGES) {
+    if (++stage == C::STAGES) {
       stage = 0;
       phase ^= 1;
     }
   }
 }
 
+template <int BN>
 __device__ __forceinline__ void run_mma(const Params& p, Shared& sh, uint8_t* sA, uint8_t* sB, uint8_t* sSF) {
+  using C = Cfg<BN>;
   int stage = 0;
   uint32_t phase = 0;
   int it = 0;
   const int tiles = p.num_m * p.num_n;
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-    const int acc = it & 1;
-    const uint32_t acc_phase = (it >> 1) & 1;
+    const int acc = it % C::ACC_STAGES;
+    const uint32_t acc_phase = (it / C::ACC_STAGES) & 1;
     ++it;
     if (!mbar_wait(&sh.tempty[acc], acc_phase ^ 1, &sh.abort_flag, &g_err, 3)) return;
     tc_fence_after();
-    const uint32_t d_tmem = sh.tmem_base + acc * ACC_COLS;
+    const uint32_t d_tmem = sh.tmem_base + acc * C::ACC_COLS;
     for (int kb = 0; kb < p.num_k; ++kb) {
       if (!mbar_wait(&sh.full[stage], phase, &sh.abort_flag, &g_err, 4)) return;
       tc_fence_after();
       const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-      const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
-      const uint32_t sf_addr = smem_u32(sSF + stage * 2 * SF_BYTES);
-      const uint32_t tsfa = sh.tmem_base + SF_COL0 + stage * SF_COLS_PER_STAGE;
+      const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
+      const uint32_t sf_addr = smem_u32(sSF + stage * C::SF_STAGE);
+      const uint32_t tsfa = sh.tmem_base + C::SF_COL0 + stage * C::SF_COLS_PER_STAGE;
       const uint32_t tsfb = tsfa + 4;
       // scale records -> TMEM; tcgen05 operations of this thread execute in issue order,
       // so the copies land before the MMAs below read them
       tmem_cp_32x128b_x4(tsfa, sf_desc(sf_addr));
-      tmem_cp_32x128b_x4(tsfb, sf_desc(sf_addr + SF_BYTES));
+#pragma unroll
+      for (int r = 0; r < BN / 128; ++r) tmem_cp_32x128b_x4(tsfb + 4 * r, sf_desc(sf_addr + (1 + r) * SF_BYTES));
 #pragma unroll
       for (int j = 0; j < BK / 32; ++j) {
         const uint64_t ad = umma_desc_sw128(a_addr + j * 32, 16, 1024);
@@ -176,7 +205,7 @@ __device__ __forceinline__ void run_mma(const Params& p, Shared& sh, uint8_t* sA
         umma_mx(d_tmem, ad, bd, idesc_mx(BM, BN, j, j), tsfa, tsfb, (kb | j) != 0 ? 1u : 0u);
       }
       umma_commit(&sh.empty[stage]);
-      if (++stage == STAGES) {
+      if (++stage == C::STAGES) {
         stage = 0;
         phase ^= 1;
       }
@@ -185,8 +214,31 @@ __device__ __forceinline__ void run_mma(const Params& p, Shared& sh, uint8_t* sA
   }
 }
 
+__device__ __forceinline__ void store_row32(__nv_bfloat16* drow, int col, int N, bool vec_ok, const uint32_t* r) {
+  if (vec_ok && col + 32 <= N) {
+    uint4* dst = reinterpret_cast<uint4*>(drow + col);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      uint4 o;
+      o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
+      o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
+      o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
+      o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
+      dst[v] = o;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col + j < N) drow[col + j] = __float2bfloat16(__uint_as_float(r[j]));
+  }
+}
+
+template <int BN>
 __device__ __forceinline__ void run_epilogue(const Params& p, Shared& sh, int warp, int lane) {
-  const int q = warp & 3;  // TMEM lane quarter this warp may access
+  using C = Cfg<BN>;
+  const int q = warp & 3;                                   // TMEM lane quarter this warp may access
+  constexpr int COLS = BN / (C::EPI_WARPS / 4);             // accumulator columns of this warp
+  const int col0 = ((warp - 2) / 4) * COLS;
   int it = 0;
   const int tiles = p.num_m * p.num_n;
   const bool vec_ok = (p.ldd % 8) == 0;
@@ -195,59 +247,63 @@ __device__ __forceinline__ void run_epilogue(const Params& p, Shared& sh, int wa
     tile_coords(t, p, tm, tn);
     const int row = tm * BM + q * 32 + lane;
     __nv_bfloat16* drow = p.D + static_cast<size_t>(row) * p.ldd;
-    const int acc = it & 1;
-    const uint32_t acc_phase = (it >> 1) & 1;
+    const int acc = it % C::ACC_STAGES;
+    const uint32_t acc_phase = (it / C::ACC_STAGES) & 1;
     ++it;
     if (!mbar_wait(&sh.tfull[acc], acc_phase, &sh.abort_flag, &g_err, 5)) return;
     tc_fence_after();
-#pragma unroll 1
-    for (int c = 0; c < BN / 32; ++c) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(sh.tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * ACC_COLS + c * 32, r);
+    const uint32_t tbase = sh.tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::ACC_COLS + col0;
+    if constexpr (C::ACC_STAGES == 1) {
+      // the whole slice into registers, release the accumulator, then convert and store
+      uint32_t r[COLS];
+#pragma unroll
+      for (int c = 0; c < COLS / 32; ++c) tmem_ld_32x32b_x32(tbase + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + 32 * c));
       tmem_ld_wait();
-      const int col = tn * BN + c * 32;
-      if (row < p.M && col < p.N) {
-        if (vec_ok && col + 32 <= p.N) {
-          uint4* dst = reinterpret_cast<uint4*>(drow + col);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tempty[acc]);
+      if (row < p.M) {
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 o;
-            o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
-            o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
-            o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
-            o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
-            dst[v] = o;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (col + j < p.N) drow[col + j] = __float2bfloat16(__uint_as_float(r[j]));
+        for (int c = 0; c < COLS / 32; ++c) {
+          const int col = tn * BN + col0 + c * 32;
+          if (col < p.N) store_row32(drow, col, p.N, vec_ok, r + 32 * c);
         }
       }
+    } else {
+#pragma unroll 1
+      for (int c = 0; c < COLS / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tbase + c * 32, r);
+        tmem_ld_wait();
+        const int col = tn * BN + col0 + c * 32;
+        if (row < p.M && col < p.N) store_row32(drow, col, p.N, vec_ok, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.tempty[acc]);
     }
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&sh.tempty[acc]);
   }
 }
 
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+template <int BN>
+__global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
     mx_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p) {
+  using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ Shared sh;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint8_t* sSF = sB + STAGES * B_BYTES;  // 1024-aligned: the stage tiles are 16 KB each
+  uint8_t* sB = smem + C::STAGES * A_BYTES;
+  uint8_t* sSF = sB + C::STAGES * C::B_BYTES;  // 1024-aligned: the stage tiles are multiples of 16 KB
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&sh.full[s], 1);
       mbar_init(&sh.empty[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < C::ACC_STAGES; ++a) {
       mbar_init(&sh.tfull[a], 1);
-      mbar_init(&sh.tempty[a], 4);
+      mbar_init(&sh.tempty[a], C::EPI_WARPS);
     }
     sh.abort_flag = 0;
     fence_barrier_init();
@@ -261,11 +317,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 0) {
-    if (lane == 0) run_producer(&tmA, &tmB, p, sh, sA, sB, sSF);
+    if (lane == 0) run_producer<BN>(&tmA, &tmB, p, sh, sA, sB, sSF);
   } else if (warp == 1) {
-    if (lane == 0) run_mma(p, sh, sA, sB, sSF);
+    if (lane == 0) run_mma<BN>(p, sh, sA, sB, sSF);
   } else {
-    run_epilogue(p, sh, warp, lane);
+    run_epilogue<BN>(p, sh, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -275,22 +331,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   }
 }
 
-}  // namespace mx_impl
-
-void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
-                int64_t K, cudaStream_t stream) {
-  using namespace mx_impl;
-  if (M == 0 || N == 0) return;
-  if (K % BK) throw std::runtime_error("gemm_mxfp8: K must be a multiple of 128");
-  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) throw std::runtime_error("gemm_mxfp8: dims");
-  if ((reinterpret_cast<uintptr_t>(sfa) & 15) || (reinterpret_cast<uintptr_t>(sfb) & 15))
-    throw std::runtime_error("gemm_mxfp8: scale records must be 16-byte aligned");
+template <int BN>
+void launch_mx(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
+               int64_t K, cudaStream_t stream) {
+  using C = Cfg<BN>;
   const CUtensorMap ta = make_tmap_u8_2d(A, M, K, K, BM, BK);
   const CUtensorMap tb = make_tmap_u8_2d(B, N, K, K, BN, BK);
   Params p;
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
+  p.b_records = (int)((N + 127) / 128);
   p.num_m = (int)((M + BM - 1) / BM);
   p.num_n = (int)((N + BN - 1) / BN);
   p.num_k = (int)(K / BK);
@@ -300,7 +351,7 @@ void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, 
   p.ldd = (int)N;
   static bool attr_set = false;
   if (!attr_set) {
-    check_cuda(cudaFuncSetAttribute(mx_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+    check_cuda(cudaFuncSetAttribute(mx_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES),
                "mx gemm smem attr");
     attr_set = true;
   }
@@ -311,8 +362,24 @@ void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, 
     sms = num_sms(dev);
   }
   const int tiles = p.num_m * p.num_n;
-  mx_gemm_kernel<<<tiles < sms ? tiles : sms, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, p);
+  mx_gemm_kernel<BN><<<tiles < sms ? tiles : sms, C::NUM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, p);
   check_cuda(cudaGetLastError(), "mx gemm launch");
+}
+
+}  // namespace mx_impl
+
+void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
+                int64_t K, cudaStream_t stream, int tile_n) {
+  using namespace mx_impl;
+  if (M == 0 || N == 0) return;
+  if (K % BK) throw std::runtime_error("gemm_mxfp8: K must be a multiple of 128");
+  if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) throw std::runtime_error("gemm_mxfp8: dims");
+  if ((reinterpret_cast<uintptr_t>(sfa) & 15) || (reinterpret_cast<uintptr_t>(sfb) & 15))
+    throw std::runtime_error("gemm_mxfp8: scale records must be 16-byte aligned");
+  if (tile_n == 0) tile_n = N >= 256 ? 256 : 128;  // the wide tile wherever N has 256 columns
+  if (tile_n == 256) launch_mx<256>(A, B, sfa, sfb, D, M, N, K, stream);
+  else if (tile_n == 128) launch_mx<128>(A, B, sfa, sfb, D, M, N, K, stream);
+  else throw std::runtime_error("gemm_mxfp8: tile_n must be 0, 128 or 256");
 }
 
 int mxgemm_error_code(bool reset) {

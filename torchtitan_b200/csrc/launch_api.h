@@ -83,7 +83,7 @@ void dp_error_info(int* out4);
 
 // gemm_mxfp8.cu / mx_quant.cu: MXFP8 block-scaled GEMM and its quantizer
 void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
-                int64_t K, cudaStream_t stream);
+                int64_t K, cudaStream_t stream, int tile_n = 0);
 int mxgemm_error_code(bool reset);
 void mx_quantize(const void* x, int64_t R, int64_t C, int64_t ldx, void* codes, void* sf, cudaStream_t s);
 
