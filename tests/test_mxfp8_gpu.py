@@ -60,3 +60,52 @@ def test_mxfp8_linear_kernel_path_matches_fake_quant(monkeypatch):
         res[flag] = (y.float(), xx.grad.float(), ww.grad.float())
     for a, b in zip(res["1"], res["0"]):
         torch.testing.assert_close(a, b, rtol=2e-2, atol=2e-2 * float(b.abs().max()) / 20)
+
+
+@pytest.mark.parametrize("rowwise", [False, True])
+def test_f8_quantize_matches_fake_quant(rowwise):
+    """E4M3 codes and inverse scales against the fp32 definition (scale = 448 / amax, round to
+    nearest even, saturate). The hardware conversion (cvt.rn.satfinite.e4m3x2.f32) rounds a
+    product lying within a few fp32 ulps above or below an E4M3 tie as the tie itself, so a
+    small fraction of codes may sit one E4M3 step from the correctly rounded value."""
+    from torchtitan_b200.ops._ext import ext
+
+    torch.manual_seed(1)
+    x = (torch.randn(300, 200, device="cuda") * torch.logspace(-2, 2, 200, device="cuda")).bfloat16()
+    codes, inv = ext().f8_quantize(x, rowwise)
+    assert codes.shape == (300, 256) and not codes[:, 200:].any()
+    xf = x.float()
+    amax = xf.abs().amax(-1, keepdim=True) if rowwise else xf.abs().amax()
+    scale = 448.0 / amax.clamp_min(1e-12)
+    ref = (xf * scale).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8).int()
+    got = codes[:, :200].int()
+    torch.testing.assert_close(inv.view(-1), (1.0 / scale).view(-1), rtol=2e-7, atol=0)
+    assert torch.equal(got >> 7, ref >> 7)                      # signs
+    step = ((got & 0x7F) - (ref & 0x7F)).abs()                  # magnitudes are monotone codes
+    assert int(step.max()) <= 1 and float((step > 0).float().mean()) < 5e-3, float((step > 0).float().mean())
+
+
+@pytest.mark.parametrize("recipe", ["tensorwise", "rowwise", "rowwise_with_gw_hp"])
+def test_float8_linear_kernel_path_matches_fake_quant(monkeypatch, recipe):
+    """Forward and both backward GEMMs of the Float8 linear on the E4M3 tensor-core kernel
+    against the quantize-dequantize emulation on the bf16 GEMM."""
+    from torchtitan_b200.components.quantization.float8 import _F8LinearFn
+    from torchtitan_b200.ops._ext import ext
+
+    torch.manual_seed(4)
+    x = torch.randn(2, 192, 512, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(640, 512, device="cuda") * 0.05).bfloat16()
+    dy = torch.randn(2, 192, 640, device="cuda", dtype=torch.bfloat16)
+    res = {}
+    for flag in ("0", "1"):
+        monkeypatch.setenv("TTB_FLOAT8_KERNEL", flag)
+        xx, ww = x.clone().requires_grad_(), w.clone().requires_grad_()
+        y = _F8LinearFn.apply(xx, ww, recipe)
+        y.backward(dy)
+        res[flag] = (y.detach().float(), xx.grad.float(), ww.grad.float())
+    torch.cuda.synchronize()
+    assert ext().mxgemm_error_code(True) == 0
+    # relative error of the whole tensor: the kernel multiplies exact E4M3 products, the emulation
+    # rounds the dequantized operands to bf16 first; both sit ~1e-2 from each other at K = 512
+    for a, b in zip(res["1"], res["0"]):
+        assert float((a - b).norm() / b.norm()) < 2e-2

@@ -18,12 +18,33 @@ from torchtitan_b200.utils.logging import logger
 from .utils import swap_linears
 
 
+def _kernel_path(x: torch.Tensor) -> bool:
+    """E4M3 GEMMs on the tensor cores (``gemm_f8``: the block-scaled tcgen05 kernel with unit
+    block scales and the fp32 row / tensor scales applied in its epilogue); ``TTB_FLOAT8_KERNEL=0``
+    selects the quantize-dequantize emulation on the bf16 GEMM."""
+    import os
+
+    return x.is_cuda and os.environ.get("TTB_FLOAT8_KERNEL", "1") != "0"
+
+
+def _f8_mm(a: torch.Tensor, b: torch.Tensor, rowwise: bool) -> torch.Tensor:
+    """``a @ b.T`` with both operands quantized along the contraction (last) dimension."""
+    from torchtitan_b200.ops._ext import ext
+
+    qa, ia = ext().f8_quantize(a.contiguous(), rowwise)
+    qb, ib = ext().f8_quantize(b.contiguous(), rowwise)
+    return ext().gemm_f8(qa, ia, qb, ib)
+
+
 class _F8LinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, recipe):
         ctx.save_for_backward(x, w)
         ctx.recipe = recipe
         g = "tensorwise" if recipe == "tensorwise" else "rowwise"
+        if _kernel_path(x) and x.dtype == torch.bfloat16:
+            x2 = x.reshape(-1, x.shape[-1])
+            return _f8_mm(x2, w.to(x.dtype), g == "rowwise").view(*x.shape[:-1], w.shape[0])
         return ops.linear(float8_fake_quant(x, g, -1), float8_fake_quant(w, g, -1))
 
     @staticmethod
@@ -32,6 +53,15 @@ class _F8LinearFn(torch.autograd.Function):
         r = ctx.recipe
         g = "tensorwise" if r == "tensorwise" else "rowwise"
         x2, dy2 = x.reshape(-1, x.shape[-1]), dy.reshape(-1, dy.shape[-1])
+        if _kernel_path(x) and x.dtype == torch.bfloat16:
+            rw = g == "rowwise"
+            wb = w.to(x.dtype)
+            dx = _f8_mm(dy2.to(x.dtype), wb.t(), rw).view(x.shape)
+            if r == "rowwise_with_gw_hp":
+                dw = ops.matmul(dy2.t().contiguous(), x2)
+            else:
+                dw = _f8_mm(dy2.to(x.dtype).t(), x2.t(), rw)
+            return dx, dw.to(w.dtype), None
         dx = ops.matmul(float8_fake_quant(dy2, g, -1), float8_fake_quant(w, g, 0)).view(x.shape)
         if r == "rowwise_with_gw_hp":  # weight gradient kept in high precision
             dw = ops.matmul(dy2.t().contiguous(), x2)

@@ -412,6 +412,39 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                     static_cast<int>(tile_n));
     return d;
   }, py::arg("a"), py::arg("sfa"), py::arg("b"), py::arg("sfb"), py::arg("tile_n") = 0);
+  m.def("f8_quantize", [](Tensor x, bool rowwise) {
+    check_cuda_bf16(x, "x");
+    TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "f8_quantize: [R, C] with contiguous rows");
+    c10::cuda::CUDAGuard g(x.device());
+    const int64_t R = x.size(0), C = x.size(1), Cp = (C + 127) / 128 * 128;
+    auto codes = torch::empty({R, Cp}, x.options().dtype(at::kByte));
+    auto inv = torch::empty({rowwise ? R : 1}, x.options().dtype(at::kFloat));
+    auto word = torch::empty({1}, x.options().dtype(at::kInt));
+    ttb::f8_quantize(x.data_ptr(), R, C, x.stride(0), rowwise, codes.data_ptr(), inv.data_ptr<float>(),
+                     reinterpret_cast<unsigned int*>(word.data_ptr<int>()), stream());
+    return std::vector<Tensor>{codes, inv};
+  });
+  m.def("gemm_f8", [](Tensor a, Tensor a_inv, Tensor b, Tensor b_inv, int64_t tile_n) {
+    TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kByte && b.scalar_type() == at::kByte,
+                "gemm_f8: uint8 E4M3 codes on CUDA");
+    TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.is_contiguous() && b.is_contiguous(),
+                "gemm_f8: A [M, K], B [N, K] contiguous");
+    const int64_t M = a.size(0), N = b.size(0), K = a.size(1);
+    TORCH_CHECK(a_inv.scalar_type() == at::kFloat && b_inv.scalar_type() == at::kFloat && a_inv.is_contiguous() &&
+                    b_inv.is_contiguous() && (a_inv.numel() == M || a_inv.numel() == 1) &&
+                    (b_inv.numel() == N || b_inv.numel() == 1),
+                "gemm_f8: fp32 inverse scales, one per row or one per operand");
+    c10::cuda::CUDAGuard g(a.device());
+    auto d = torch::empty({M, N}, a.options().dtype(at::kBFloat16));
+    ttb::MxEpilogue ep;
+    ep.sa = a_inv.data_ptr<float>();
+    ep.sb = b_inv.data_ptr<float>();
+    ep.sa_rows = a_inv.numel() == M && M > 1;
+    ep.sb_rows = b_inv.numel() == N && N > 1;
+    ttb::gemm_mxfp8(a.data_ptr(), b.data_ptr(), nullptr, nullptr, d.data_ptr(), M, N, K, stream(),
+                    static_cast<int>(tile_n), ep);
+    return d;
+  }, py::arg("a"), py::arg("a_inv"), py::arg("b"), py::arg("b_inv"), py::arg("tile_n") = 0);
   m.def("kda_gram_fwd", [](Tensor a, Tensor b, Tensor G, bool strict) {
     for (const Tensor* t : {&a, &b, &G})
       TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 3 &&

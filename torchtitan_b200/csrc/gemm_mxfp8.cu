@@ -71,7 +71,13 @@ struct Params {
   const uint8_t* sfb;
   __nv_bfloat16* D;
   int ldd;
+  int sf_unit;          // scale records are all 2^0: every stage copies the one unit record
+  const float* sa;      // optional output scales: D[m, n] *= sa[m or 0] * sb[n or 0]
+  const float* sb;
+  int sa_rows, sb_rows;  // 1: one scale per row of A / of B; 0: one scale for the operand
 };
+
+__device__ __align__(128) uint8_t g_unit_sf[SF_BYTES];  // E8M0 127 (= 2^0) bytes, set on first use
 
 struct Shared {
   uint64_t full[6], empty[6], tfull[2], tempty[2];
@@ -152,9 +158,10 @@ __device__ __forceinline__ void run_producer(const CUtensorMap* tmA, const CUten
       tma_load_2d(sA + stage * A_BYTES, tmA, &sh.full[stage], kb * BK, tm * BM);
       tma_load_2d(sB + stage * C::B_BYTES, tmB, &sh.full[stage], kb * BK, tn * BN);
       uint8_t* sf = sSF + stage * C::SF_STAGE;
-      bulk_load(sf, p.sfa + (static_cast<size_t>(tm) * p.num_k + kb) * SF_BYTES, SF_BYTES, &sh.full[stage]);
+      const size_t ua = p.sf_unit ? 0 : 1;  // unit records: always record 0 of the unit buffer
+      bulk_load(sf, p.sfa + ua * (static_cast<size_t>(tm) * p.num_k + kb) * SF_BYTES, SF_BYTES, &sh.full[stage]);
       for (int r = 0; r < nrec; ++r)
-        bulk_load(sf + (1 + r) * SF_BYTES, p.sfb + (static_cast<size_t>(rb0 + r) * p.num_k + kb) * SF_BYTES,
+        bulk_load(sf + (1 + r) * SF_BYTES, p.sfb + ua * (static_cast<size_t>(rb0 + r) * p.num_k + kb) * SF_BYTES,
                   SF_BYTES, &sh.full[stage]);
       if (++stage == C::STAGES) {
         stage = 0;
@@ -214,22 +221,37 @@ __device__ __forceinline__ void run_mma(const Params& p, Shared& sh, uint8_t* sA
   }
 }
 
-__device__ __forceinline__ void store_row32(__nv_bfloat16* drow, int col, int N, bool vec_ok, const uint32_t* r) {
-  if (vec_ok && col + 32 <= N) {
+// 32 accumulator columns of one output row -> bf16, times the optional row / column scales
+__device__ __forceinline__ void store_row32(__nv_bfloat16* drow, int col, const Params& p, bool vec_ok, float fr,
+                                            const uint32_t* r) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * fr;
+  if (p.sb) {
+    if (p.sb_rows) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= (col + j < p.N) ? __ldg(p.sb + col + j) : 0.f;
+    } else {
+      const float s = __ldg(p.sb);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= s;
+    }
+  }
+  if (vec_ok && col + 32 <= p.N) {
     uint4* dst = reinterpret_cast<uint4*>(drow + col);
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
+    for (int q = 0; q < 4; ++q) {
       uint4 o;
-      o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]), __uint_as_float(r[8 * v + 1]));
-      o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]), __uint_as_float(r[8 * v + 3]));
-      o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]), __uint_as_float(r[8 * v + 5]));
-      o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]), __uint_as_float(r[8 * v + 7]));
-      dst[v] = o;
+      o.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+      o.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+      o.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+      o.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+      dst[q] = o;
     }
   } else {
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-      if (col + j < N) drow[col + j] = __float2bfloat16(__uint_as_float(r[j]));
+      if (col + j < p.N) drow[col + j] = __float2bfloat16(v[j]);
   }
 }
 
@@ -252,6 +274,7 @@ __device__ __forceinline__ void run_epilogue(const Params& p, Shared& sh, int wa
     ++it;
     if (!mbar_wait(&sh.tfull[acc], acc_phase, &sh.abort_flag, &g_err, 5)) return;
     tc_fence_after();
+    const float fr = !p.sa ? 1.f : (p.sa_rows ? (row < p.M ? __ldg(p.sa + row) : 0.f) : __ldg(p.sa));
     const uint32_t tbase = sh.tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * C::ACC_COLS + col0;
     if constexpr (C::ACC_STAGES == 1) {
       // the whole slice into registers, release the accumulator, then convert and store
@@ -266,7 +289,7 @@ __device__ __forceinline__ void run_epilogue(const Params& p, Shared& sh, int wa
 #pragma unroll
         for (int c = 0; c < COLS / 32; ++c) {
           const int col = tn * BN + col0 + c * 32;
-          if (col < p.N) store_row32(drow, col, p.N, vec_ok, r + 32 * c);
+          if (col < p.N) store_row32(drow, col, p, vec_ok, fr, r + 32 * c);
         }
       }
     } else {
@@ -276,7 +299,7 @@ __device__ __forceinline__ void run_epilogue(const Params& p, Shared& sh, int wa
         tmem_ld_32x32b_x32(tbase + c * 32, r);
         tmem_ld_wait();
         const int col = tn * BN + col0 + c * 32;
-        if (row < p.M && col < p.N) store_row32(drow, col, p.N, vec_ok, r);
+        if (row < p.M && col < p.N) store_row32(drow, col, p, vec_ok, fr, r);
       }
       tc_fence_before();
       __syncwarp();
@@ -333,7 +356,7 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
 
 template <int BN>
 void launch_mx(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
-               int64_t K, cudaStream_t stream) {
+               int64_t K, cudaStream_t stream, const MxEpilogue& ep) {
   using C = Cfg<BN>;
   const CUtensorMap ta = make_tmap_u8_2d(A, M, K, K, BM, BK);
   const CUtensorMap tb = make_tmap_u8_2d(B, N, K, K, BN, BK);
@@ -349,6 +372,23 @@ void launch_mx(const void* A, const void* B, const void* sfa, const void* sfb, v
   p.sfb = static_cast<const uint8_t*>(sfb);
   p.D = static_cast<__nv_bfloat16*>(D);
   p.ldd = (int)N;
+  p.sf_unit = sfa == nullptr;
+  if (p.sf_unit) {
+    static bool unit_set = false;  // fill the unit record once per process
+    if (!unit_set) {
+      uint8_t host[SF_BYTES];
+      for (int i = 0; i < SF_BYTES; ++i) host[i] = 127;
+      check_cuda(cudaMemcpyToSymbol(g_unit_sf, host, SF_BYTES), "mx unit scales");
+      unit_set = true;
+    }
+    void* unit = nullptr;
+    check_cuda(cudaGetSymbolAddress(&unit, g_unit_sf), "mx unit scales address");
+    p.sfa = p.sfb = static_cast<const uint8_t*>(unit);
+  }
+  p.sa = ep.sa;
+  p.sb = ep.sb;
+  p.sa_rows = ep.sa_rows;
+  p.sb_rows = ep.sb_rows;
   static bool attr_set = false;
   if (!attr_set) {
     check_cuda(cudaFuncSetAttribute(mx_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES),
@@ -369,16 +409,17 @@ void launch_mx(const void* A, const void* B, const void* sfa, const void* sfb, v
 }  // namespace mx_impl
 
 void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
-                int64_t K, cudaStream_t stream, int tile_n) {
+                int64_t K, cudaStream_t stream, int tile_n, const MxEpilogue& ep) {
   using namespace mx_impl;
   if (M == 0 || N == 0) return;
   if (K % BK) throw std::runtime_error("gemm_mxfp8: K must be a multiple of 128");
   if (M >= (1ll << 31) || N >= (1ll << 31) || K >= (1ll << 31)) throw std::runtime_error("gemm_mxfp8: dims");
+  if ((sfa == nullptr) != (sfb == nullptr)) throw std::runtime_error("gemm_mxfp8: both or neither scale records");
   if ((reinterpret_cast<uintptr_t>(sfa) & 15) || (reinterpret_cast<uintptr_t>(sfb) & 15))
     throw std::runtime_error("gemm_mxfp8: scale records must be 16-byte aligned");
   if (tile_n == 0) tile_n = N >= 256 ? 256 : 128;  // the wide tile wherever N has 256 columns
-  if (tile_n == 256) launch_mx<256>(A, B, sfa, sfb, D, M, N, K, stream);
-  else if (tile_n == 128) launch_mx<128>(A, B, sfa, sfb, D, M, N, K, stream);
+  if (tile_n == 256) launch_mx<256>(A, B, sfa, sfb, D, M, N, K, stream, ep);
+  else if (tile_n == 128) launch_mx<128>(A, B, sfa, sfb, D, M, N, K, stream, ep);
   else throw std::runtime_error("gemm_mxfp8: tile_n must be 0, 128 or 256");
 }
 

@@ -82,8 +82,20 @@ void dp_set_error_sink(void* host_mapped_int8);  // pinned host int[8] written o
 void dp_error_info(int* out4);
 
 // gemm_mxfp8.cu / mx_quant.cu: MXFP8 block-scaled GEMM and its quantizer
+// Optional epilogue scales of the block-scaled GEMM: D[m, n] *= sa[m] (or sa[0]) * sb[n] (or
+// sb[0]); null pointers mean 1. Null scale records (sfa = sfb = nullptr) mean E8M0 2^0
+// everywhere, which turns the kernel into a plain FP8 GEMM (Float8 tensorwise / rowwise).
+struct MxEpilogue {
+  const float* sa = nullptr;
+  const float* sb = nullptr;
+  int sa_rows = 0, sb_rows = 0;
+};
 void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
-                int64_t K, cudaStream_t stream, int tile_n = 0);
+                int64_t K, cudaStream_t stream, int tile_n = 0, const MxEpilogue& ep = MxEpilogue());
+// Float8 (E4M3) quantization along rows: scale = 448 / max(amax, 1e-12) per row (rowwise) or
+// per tensor; writes codes [R, Cp] (columns zero padded to 128) and inv = 1 / scale ([R] or [1]).
+void f8_quantize(const void* x, int64_t R, int64_t C, int64_t ldx, bool rowwise, void* codes, float* inv,
+                 unsigned int* amax_word, cudaStream_t s);
 int mxgemm_error_code(bool reset);
 void mx_quantize(const void* x, int64_t R, int64_t C, int64_t ldx, void* codes, void* sf, cudaStream_t s);
 

@@ -200,12 +200,17 @@ def bench_mxfp8(ext, out):
         qb, sb = mx_quantize(b)
         mx = time_fn(lambda: ext.gemm_mxfp8(qa, sa, qb, sb))
         mx128 = time_fn(lambda: ext.gemm_mxfp8(qa, sa, qb, sb, 128))
+        fa, ia = ext.f8_quantize(a, True)
+        fb, ib = ext.f8_quantize(b, True)
+        f8 = time_fn(lambda: ext.gemm_f8(fa, ia, fb, ib))
+        f8q = time_fn(lambda: ext.f8_quantize(a, True))
         bf = time_fn(lambda: ext.gemm(a, b, False, False))
         lib = time_fn(lambda: torch.matmul(a, b.t()))
         q = time_fn(lambda: mx_quantize(a))
         fl = 2.0 * M * N * K
         out.append({"kernel": "gemm_mxfp8", "case": name, "M": M, "N": N, "K": K, "ms": mx, "tflops": fl / mx / 1e9,
-                    "tile128_tflops": fl / mx128 / 1e9, "bf16_tcgen05_tflops": fl / bf / 1e9, "cublas_bf16_tflops": fl / lib / 1e9,
+                    "tile128_tflops": fl / mx128 / 1e9, "f8_rowwise_tflops": fl / f8 / 1e9,
+                    "f8_quantize_gbs": a.numel() * 3 / f8q / 1e6, "bf16_tcgen05_tflops": fl / bf / 1e9, "cublas_bf16_tflops": fl / lib / 1e9,
                     "quantize_ms": q, "quantize_gbs": (a.numel() * 2 + a.numel() + a.numel() // 32) / q / 1e6,
                     "err": ext.mxgemm_error_code(True)})
         print(json.dumps(out[-1]), flush=True)
