@@ -24,6 +24,8 @@ import tempfile
 import time
 
 BASELINE_TPS_PER_GPU = 8307.5  # reference, 8x B200 bf16, bs1 seq 8192, FSDP2 + SAC (docs/mxfp8.md:148-152)
+# same table, quantized linears: mxfp8_cublas 9,969 and fp8 tensorwise 10,417 tokens/s (docs/mxfp8.md:153-155)
+BASELINE_QUANT_TPS_PER_GPU = {"mxfp8": 9969.0, "float8": 10417.0}
 METRIC = "tokens/sec (whole job) for Llama-3 8B FSDP2 bf16 training"
 
 
@@ -40,6 +42,8 @@ def _parse():
                     help="data-parallel runtime of this framework's arm (auto: peer memory on one node)")
     ap.add_argument("--sac-option", default="op_all_mm",
                     help="per-op SAC variant of this framework's arm: op_all_mm keeps every GEMM output")
+    ap.add_argument("--quant", default="none", choices=["none", "mxfp8", "float8", "float8_rowwise"],
+                    help="quantized linears (all but the output head), as the reference's converters")
     ap.add_argument("--profile-out", default=None, help="write a per-kernel time table of one extra step here")
     return ap.parse_args()
 
@@ -143,6 +147,8 @@ def run_ours(a):
     # per GPU buys back the backward's parameter all-gathers
     cfg.parallelism.fsdp_reshard_after_forward = os.environ.get("TTB_BENCH_RESHARD", "never")
     cfg.parallelism.data_parallel_comm = a.dp_comm
+    if a.quant != "none":
+        cfg.model_converters.names = [a.quant]
     trainer = Trainer(cfg)
     it = trainer.batch_generator(trainer.dataloader)
     tokens_per_step = cfg.training.local_batch_size * cfg.training.seq_len * trainer.dp_degree
@@ -205,8 +211,10 @@ def run_ours(a):
         "ms_per_step": round(1e3 * dev_s / a.steps, 2),
         "higher_is_better": True,
         "scaling": "weak",
-        "vs_baseline": round(value / (BASELINE_TPS_PER_GPU * world), 4),
-        "dtype": "bf16",
+        "vs_baseline": (round(value / (BASELINE_TPS_PER_GPU * world), 4) if a.quant == "none"
+                        else round(value / (BASELINE_QUANT_TPS_PER_GPU[a.quant] * world), 4)
+                        if a.quant in BASELINE_QUANT_TPS_PER_GPU else None),
+        "dtype": "bf16" if a.quant == "none" else f"{a.quant} linears (bf16 master weights, bf16 attention)",
         "data": "synthetic uniform tokens, random-init weights",
         "config": {"model": f"llama3_{a.flavor}", "global_batch": world, "seq_len": a.seq_len,
                    "parallelism": (f"dp{world} (replicated bf16 weights, sharded fp32 AdamW, peer-memory reduce-scatter"
@@ -215,7 +223,7 @@ def run_ours(a):
                                    else "single GPU (bf16 compute weights, fp32 masters in the fused AdamW; no sharding)"
                                    if world == 1
                                    else f"fsdp{world} (reshard_after_forward={cfg.parallelism.fsdp_reshard_after_forward})"), "ac": a.ac if a.ac != "selective" else f"selective ({a.sac_option})", "optimizer": "AdamW (fused, fp32 master)",
-                   "l2": "inputs larger than L2 (no flush)"},
+                   "l2": "inputs larger than L2 (no flush)", "quant": a.quant},
         "mfu_pct": round(mfu, 2),
         "tokens_per_sec_per_gpu": round(value / world, 1),
         "peak_mem_gib": round(peak_mem, 2),
@@ -251,6 +259,10 @@ def _install_reference(ref):
 
 
 def run_reference(a):
+    if a.quant != "none":
+        print(json.dumps({"impl": "reference", "unavailable": "the reference's Float8/MX converters need torchao, "
+                          "which is not installed on this image"}))
+        return
     here = os.path.dirname(os.path.abspath(__file__))
     ref = os.path.join(here, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "torchtitan")):
