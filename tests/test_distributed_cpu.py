@@ -424,7 +424,7 @@ def test_fused_ep_plan_layout():
     from torchtitan_b200.parallel.ep_fused import Plan
 
     M = torch.tensor([[3, 0, 5, 1], [2, 130, 0, 4]])  # 2 ranks x 4 experts (2 per rank)
-    p0, p1 = Plan(M, 0, torch.device("cpu")), Plan(M, 1, torch.device("cpu"))
+    p0, p1 = Plan(M, 0, torch.device("cpu")).finalize(M), Plan(M, 1, torch.device("cpu")).finalize(M)
     # owner 0: expert 0 gets 3 + 2 rows -> [0, 128); expert 1 gets 130 -> [128, 384)
     assert p0.P == 384 and p1.P == 256 and p0.P_max == 384
     assert p0.local_counts.tolist() == [5, 130]

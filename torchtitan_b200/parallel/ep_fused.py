@@ -8,8 +8,13 @@ owner's padded expert-major buffer (the layout the grouped tcgen05 GEMM
 reads), and fetches expert outputs directly back into token order:
 
 1. counts: every rank stores its ``[E]`` per-expert counts into every peer's
-   ``[ep, E]`` matrix (one P2P row store), epoch barrier, one small D2H copy of
-   the matrix (the reference's dispatch has the same host sync);
+   ``[ep, E]`` matrix (one P2P row store), epoch barrier; the destination of every
+   routed row is computed from the matrix on the device and the row stores of step 3
+   are queued at once, while an asynchronous copy brings the matrix to pinned host
+   memory; the host waits for that copy (the sizes of the padded expert buffer) only
+   after the dispatch is in flight. The receive buffers are reserved once per batch
+   shape for the worst case (all routed rows of all ranks on one owner), so no count
+   ever triggers a collective allocation;
 2. layout (identical on all ranks, from the matrix): for the owner ``d`` of
    expert ``e = d*El + j`` the rows of expert ``j`` start at a multiple of 128
    and are ordered by source rank; row ``k`` of source ``s`` for expert ``e``
@@ -37,31 +42,45 @@ TILE = 128
 
 
 class Plan:
-    """Per-call layout; all index tensors live on the routed rows' device."""
+    """Per-call layout. ``dest_rank`` / ``dest_row`` (where each of my routed rows goes) are
+    computed on the device from the count matrix, so the dispatch can be launched before the
+    host has seen the counts; ``finalize`` adds the host-side sizes (padded rows received here)
+    once the matrix's copy to pinned host memory has landed."""
 
-    def __init__(self, M: torch.Tensor, me: int, device: torch.device):
+    def __init__(self, M: torch.Tensor, me: int, device: torch.device, n_rows: int | None = None):
+        M = M.to(device)
         ep, E = M.shape
         El = E // ep
+        n_rows = int(M[me].sum()) if n_rows is None else n_rows
         T = M.sum(0).view(ep, El)                       # rows per (owner, local expert)
         pad = (T + TILE - 1) // TILE * TILE
         pstart = torch.cumsum(pad, 1) - pad             # [ep, El]
         before = torch.cumsum(M, 0) - M                 # rows of earlier sources, per expert [ep, E]
         off = pstart.reshape(-1)[None, :] + before      # [ep(src), E] first row of (src, e)
         mine = M[me]                                     # my rows per global expert
-        e_of_row = torch.repeat_interleave(torch.arange(E), mine)
+        e_of_row = torch.repeat_interleave(torch.arange(E, device=device), mine, output_size=n_rows)
         first_of_e = torch.cumsum(mine, 0) - mine
-        k = torch.arange(int(mine.sum())) - first_of_e[e_of_row]
-        self.dest_rank = (e_of_row // El).to(torch.int32).to(device)
-        self.dest_row = (off[me][e_of_row] + k).to(torch.int64).to(device)
-        self.local_counts = T[me].to(device)            # rows of each of my experts
+        k = torch.arange(n_rows, device=device) - first_of_e[e_of_row]
+        self.dest_rank = (e_of_row // El).to(torch.int32)
+        self.dest_row = (off[me][e_of_row] + k).to(torch.int64)
+        self.local_counts = T[me]                        # rows of each of my experts (device)
+        self.me, self.El, self.device = me, El, device
+
+    def finalize(self, M_host: torch.Tensor) -> "Plan":
+        ep, E = M_host.shape
+        T = M_host.sum(0).view(ep, self.El)
+        pad = (T + TILE - 1) // TILE * TILE
+        pstart = torch.cumsum(pad, 1) - pad
+        me = self.me
         self.P = int(pad[me].sum())                      # padded rows I receive
         self.P_max = int(pad.sum(1).max())               # largest receive buffer over ranks
         real = torch.zeros(self.P, dtype=torch.bool)
-        for j in range(El):
-            s = int(pstart[me, j])
-            real[s:s + int(T[me, j])] = True
-        self.pad_rows = (~real).nonzero().flatten().to(device)
-        self.real_rows = real.nonzero().flatten().to(device)
+        for j in range(self.El):
+            s0 = int(pstart[me, j])
+            real[s0:s0 + int(T[me, j])] = True
+        self.pad_rows = (~real).nonzero().flatten().to(self.device, non_blocking=True)
+        self.real_rows = real.nonzero().flatten().to(self.device, non_blocking=True)
+        return self
 
 
 class EPPeerComm:
@@ -115,6 +134,15 @@ class EPPeerComm:
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)
 
+    def reserve(self, device: torch.device, dim: int, routed_rows: int) -> None:
+        """Size the receive buffers once for the worst case of this batch shape: every rank's
+        ``routed_rows`` (tokens x top-k, the same on all ranks) landing on one owner, plus one
+        partial tile per local expert. The allocation is collective, so it happens at the
+        first dispatch (and again only if the batch shape grows), never because of a count."""
+        if self.comm != "peer":
+            return
+        self._ensure_rows(device, dim, self.ep * routed_rows + (self.E // self.ep) * TILE)
+
     def barrier(self) -> None:
         if self.comm == "peer":
             self._epoch += 1
@@ -124,13 +152,16 @@ class EPPeerComm:
             dist.barrier(group=self.group)
 
     # ---------------------------------------------------------------- operations
-    def exchange_counts(self, counts: torch.Tensor) -> torch.Tensor:
-        """[E] routed rows per global expert on this rank -> [ep, E] int64 matrix (host)."""
+    def exchange_counts(self, counts: torch.Tensor):
+        """[E] routed rows per global expert on this rank -> ([ep, E] int64 on the device,
+        the same matrix in host memory: a CPU tensor (collective mode) or, on CUDA, a pinned
+        tensor filled by an asynchronous copy and the event that marks its completion)."""
         self._setup_counts(counts.device)
         if self.comm == "collective":
             out = [torch.empty_like(counts) for _ in range(self.ep)]
             dist.all_gather(out, counts.contiguous(), group=self.group)
-            return torch.stack(out).to(torch.int64).cpu()
+            m = torch.stack(out).to(torch.int64).cpu()
+            return m, m, None
         row = torch.zeros(self.cnt.shape[1] // 2, dtype=torch.int32, device=counts.device)
         row[:self.E] = counts.to(torch.int32)
         src = row.view(torch.bfloat16)[None].expand(self.ep, -1).contiguous()
@@ -139,7 +170,12 @@ class EPPeerComm:
                                   torch.full((self.ep,), self.me, dtype=torch.int64, device=counts.device),
                                   self.cnt_ptrs, self.ep)
         self.barrier()
-        return self.cnt.view(torch.int32)[:, :self.E].to(torch.int64).cpu()
+        m_dev = self.cnt.view(torch.int32)[:, :self.E].to(torch.int64)
+        m_host = torch.empty(m_dev.shape, dtype=torch.int64, pin_memory=True)
+        m_host.copy_(m_dev, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        return m_dev, m_host, ev
 
     def scatter(self, rows: torch.Tensor, dest_rank: torch.Tensor, dest_row: torch.Tensor, P: int,
                 P_max: int) -> torch.Tensor:
@@ -153,11 +189,18 @@ class EPPeerComm:
             out = rows.new_zeros(P, rows.shape[1])
             out[ridx] = recv
             return out
-        self._ensure_rows(rows.device, rows.shape[1], P_max)
+        self.launch_scatter(rows, dest_rank, dest_row, P_max)
+        return self.buf_in[:P].clone()
+
+    def launch_scatter(self, rows: torch.Tensor, dest_rank: torch.Tensor, dest_row: torch.Tensor,
+                       P_max: int | None = None) -> None:
+        """Peer mode: queue the row stores and their barriers (no host information needed
+        beyond the reserved capacity; ``ep_scatter_rows`` checks every row against it)."""
+        if P_max is not None:
+            self._ensure_rows(rows.device, rows.shape[1], P_max)
         self.barrier()  # peers are done with this buffer's previous contents
         self._ext.ep_scatter_rows(rows.contiguous(), dest_rank, dest_row, self.in_ptrs, self.cap)
         self.barrier()  # every peer's rows have landed here
-        return self.buf_in[:P].clone()
 
     def gather(self, local: torch.Tensor, src_rank: torch.Tensor, src_row: torch.Tensor, P_max: int) -> torch.Tensor:
         """Expose ``local`` [P, D]; return rows ``src_row[i]`` of rank ``src_rank[i]``'s exposed rows."""
@@ -195,7 +238,10 @@ class _Dispatch(torch.autograd.Function):
     @staticmethod
     def forward(ctx, routed, comm: EPPeerComm, plan: Plan):
         ctx.comm, ctx.plan = comm, plan
-        xp = comm.scatter(routed, plan.dest_rank, plan.dest_row, plan.P, plan.P_max)
+        if getattr(plan, "scattered", False):  # the stores were queued before the host saw the counts
+            xp = comm.buf_in[:plan.P].clone()
+        else:
+            xp = comm.scatter(routed, plan.dest_rank, plan.dest_row, plan.P, plan.P_max)
         if plan.pad_rows.numel():
             xp[plan.pad_rows] = 0
         return xp
@@ -233,10 +279,17 @@ def make_fused_ep_dispatch(ep_group, num_experts: int, comm: str | None = None):
         from torchtitan_b200 import ops
         from torchtitan_b200.models.common.moe import GroupedExperts
 
-        M = pc.exchange_counts(counts)
-        plan = Plan(M, pc.me, routed.device)
+        m_dev, m_host, ev = pc.exchange_counts(counts)  # (decides the comm mode on first use)
         if pc.comm == "peer" and routed.dtype != torch.bfloat16:
             routed = routed.to(torch.bfloat16)
+        plan = Plan(m_dev, pc.me, routed.device, n_rows=routed.shape[0])
+        if pc.comm == "peer":
+            # the row stores go out while the count matrix travels to the host
+            pc.reserve(routed.device, routed.shape[1], routed.shape[0])
+            pc.launch_scatter(routed.contiguous(), plan.dest_rank, plan.dest_row)
+            plan.scattered = True
+            ev.synchronize()
+        plan.finalize(m_host)
         xp = _Dispatch.apply(routed.contiguous(), pc, plan)
         if type(experts) is GroupedExperts:
             yp = ops.grouped_swiglu_padded(xp, *experts.weights(), plan.local_counts)
