@@ -7,13 +7,15 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("strict", [True, False])
-@pytest.mark.parametrize("N,C,K", [(5, 64, 128), (40, 64, 64)])
-def test_kda_gram_kernels_match_loop(strict, N, C, K, monkeypatch):
+@pytest.mark.parametrize("N,C,K,rate", [(5, 64, 128, 0.3), (40, 64, 64, 0.3), (7, 32, 128, 0.3),
+                                        (5, 64, 128, 5.0)])
+def test_kda_gram_kernels_match_loop(strict, N, C, K, rate, monkeypatch):
+    """rate 5.0: log decay down to -320 over a chunk (factorised exponentials stay <= 1)."""
     from torchtitan_b200.ops import kda
 
     torch.manual_seed(0)
     a, b = (torch.randn(N, C, K, device="cuda") for _ in range(2))
-    G = (-torch.rand(N, C, K, device="cuda") * 0.3).cumsum(1)
+    G = (-torch.rand(N, C, K, device="cuda") * rate).cumsum(1)
     dout = torch.randn(N, C, C, device="cuda")
     outs = {}
     for flag in ("0", "1"):

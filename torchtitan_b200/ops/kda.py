@@ -37,7 +37,7 @@ def _use_gram_kernel(t: torch.Tensor) -> bool:
 
 def _fits_shared_memory(C: int, K: int, V: int = 0) -> bool:
     """The kernels keep per-chunk tiles in shared memory (227 KB per CTA)."""
-    gram = 4 * (3 * C * (K + 1) + C * (C + 1))
+    gram = 4 * (6 * C * (K + 1) + C * (C + 1))  # backward: tiles, scaled rows, dout, accumulators
     vs = _scan_slice_width(V) if V else 1
     scan = 4 * (2 * K * (vs + 1) + 3 * C * (K + 1) + C * (C + 1) + 3 * C * (vs + 1) + K)
     return max(gram, scan) <= 227 * 1024
