@@ -113,3 +113,28 @@ def test_chunk_kda_state_kernel_matches_recurrence():
     o, S = kda.chunk_kda(q, k, v, g, beta, output_final_state=True)
     ref, Sref = kda.naive_recurrent_kda(q, k, v, g, beta)
     assert _rel(o, ref) < 2e-2 and _rel(S, Sref) < 2e-2
+
+
+@pytest.mark.parametrize("T", [200, 256])
+def test_chunk_kda_prep_kernel_matches_torch_ops(T, monkeypatch):
+    """The one-pass chunk preparation (csrc/kda_prep.cu) against the PyTorch ops it replaces:
+    outputs, final state and the gradients of q, k, v, g, beta (T = 200 pads the last chunk)."""
+    from torchtitan_b200.ops import kda
+
+    torch.manual_seed(5)
+    B, H, K, V = 2, 3, 64, 64
+    base = [torch.randn(B, T, H, K, device="cuda"), torch.randn(B, T, H, K, device="cuda"),
+            torch.randn(B, T, H, V, device="cuda"), -torch.rand(B, T, H, K, device="cuda") * 0.3,
+            torch.rand(B, T, H, device="cuda")]
+    s0 = torch.randn(B, H, K, V, device="cuda") * 0.1
+    do = torch.randn(B, T, H, V, device="cuda")
+    dS = torch.randn(B, H, K, V, device="cuda")
+    res = {}
+    for flag in ("0", "1"):
+        monkeypatch.setenv("TTB_KDA_PREP", flag)
+        xs = [t.clone().requires_grad_() for t in base]
+        o, S = kda.chunk_kda(*xs, initial_state=s0, output_final_state=True)
+        ((o.float() * do).sum() + (S * dS).sum()).backward()
+        res[flag] = [o.detach().float(), S.detach()] + [x.grad for x in xs]
+    for name, a, b in zip(["o", "S", "dq", "dk", "dv", "dg", "dbeta"], res["1"], res["0"]):
+        assert _rel(a, b) < 1e-4, (name, _rel(a, b))

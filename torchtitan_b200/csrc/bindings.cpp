@@ -467,6 +467,40 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   // chunked-KDA state recurrence on tcgen05 (C = 64, K = V = 128): bf16 w / kdec [BH,NT,C,K],
   // u^T [BH,NT,V,C]; fp32 dec [BH,NT,K], optional S0^T [BH,V,K].
   // Returns states^T [BH,NT,V,K] bf16 (state at each chunk start), v'^T [BH,NT,V,C] bf16, final S^T fp32.
+  m.def("kda_prep_fwd", [](Tensor q, Tensor k, Tensor g, int64_t C) {
+    for (const Tensor* t : {&q, &k, &g})
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 4 &&
+                      t->sizes() == q.sizes(),
+                  "kda_prep_fwd: q, k, g fp32 contiguous [B, T, H, K] of one shape");
+    c10::cuda::CUDAGuard guard(q.device());
+    const int64_t B = q.size(0), T = q.size(1), H = q.size(2), K = q.size(3), NT = (T + C - 1) / C;
+    auto o = q.options();
+    auto qc = torch::empty({B * H, NT, C, K}, o), kc = torch::empty_like(qc), G = torch::empty_like(qc);
+    auto kg = torch::empty_like(qc), qg = torch::empty_like(qc), kd = torch::empty_like(qc);
+    auto decay = torch::empty({B * H, NT, K}, o);
+    ttb::kda_prep_fwd(q.data_ptr<float>(), k.data_ptr<float>(), g.data_ptr<float>(), (int)B, (int)T, (int)H, (int)K,
+                      (int)C, qc.data_ptr<float>(), kc.data_ptr<float>(), G.data_ptr<float>(), kg.data_ptr<float>(),
+                      qg.data_ptr<float>(), kd.data_ptr<float>(), decay.data_ptr<float>(), stream());
+    return std::vector<Tensor>{qc, kc, G, kg, qg, kd, decay};
+  });
+  m.def("kda_prep_bwd", [](Tensor q, Tensor k, Tensor G, int64_t C, c10::optional<Tensor> dqc,
+                           c10::optional<Tensor> dkc, c10::optional<Tensor> dG, c10::optional<Tensor> dkg,
+                           c10::optional<Tensor> dqg, c10::optional<Tensor> dkd, c10::optional<Tensor> ddecay) {
+    c10::cuda::CUDAGuard guard(q.device());
+    auto ptr = [&](const c10::optional<Tensor>& t, const char* name) -> const float* {
+      if (!t.has_value() || !t->defined()) return nullptr;
+      TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous(), "kda_prep_bwd: ", name,
+                  " must be fp32 contiguous");
+      return t->data_ptr<float>();
+    };
+    const int64_t B = q.size(0), T = q.size(1), H = q.size(2), K = q.size(3);
+    auto dq = torch::empty_like(q), dk = torch::empty_like(q), dg = torch::empty_like(q);
+    ttb::kda_prep_bwd(q.data_ptr<float>(), k.data_ptr<float>(), G.data_ptr<float>(), (int)B, (int)T, (int)H, (int)K,
+                      (int)C, ptr(dqc, "dqc"), ptr(dkc, "dkc"), ptr(dG, "dG"), ptr(dkg, "dkg"), ptr(dqg, "dqg"),
+                      ptr(dkd, "dkd"), ptr(ddecay, "ddecay"), dq.data_ptr<float>(), dk.data_ptr<float>(),
+                      dg.data_ptr<float>(), stream());
+    return std::vector<Tensor>{dq, dk, dg};
+  });
   m.def("kda_state_fwd", [](Tensor w, Tensor kd, Tensor uT, Tensor dec, c10::optional<Tensor> S0) {
     for (const Tensor* t : {&w, &kd, &uT})
       TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous(), "kda_state: bf16");

@@ -106,6 +106,12 @@ void kda_gram_bwd(const float* dout, const float* a, const float* b, const float
                   float* dG, int64_t N, int C, int K, bool strict, cudaStream_t s);
 
 // kda_state.cu: the chunked-KDA state recurrence on tcgen05 (C = 64, K = V = 128, bf16 operands)
+// kda_prep.cu: chunk preparation of the chunked KDA (layouts and formulas in the file)
+void kda_prep_fwd(const float* q, const float* k, const float* g, int B, int T, int H, int K, int C, float* qc,
+                  float* kc, float* G, float* kg, float* qg, float* kd, float* decay, cudaStream_t s);
+void kda_prep_bwd(const float* q, const float* k, const float* G, int B, int T, int H, int K, int C,
+                  const float* dqc, const float* dkc, const float* dG, const float* dkg, const float* dqg,
+                  const float* dkd, const float* ddecay, float* dq, float* dk, float* dg, cudaStream_t s);
 void kda_state_fwd(const void* w, const void* kd, const void* uT, const float* dec, const float* S0, void* states,
                    void* vnT, float* Sfin, int BH, int NT, cudaStream_t s);
 void kda_state_bwd(const void* qg, const void* w, const void* kd, const void* dO, const void* Aqk, const float* dec,

@@ -24,6 +24,8 @@ Reference semantics: ``fla/ops/kda/naive.py`` (naive_recurrent_kda).
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 
@@ -139,6 +141,35 @@ def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
     return xf * torch.rsqrt(xf.pow(2).sum(-1, keepdim=True) + eps)
 
 
+def _prep_kernel(x: torch.Tensor) -> bool:
+    # csrc/kda_prep.cu (TTB_KDA_PREP=0 selects the PyTorch ops)
+    return x.is_cuda and os.environ.get("TTB_KDA_PREP", "1") != "0"
+
+
+class _Prep(torch.autograd.Function):
+    """Chunk layout, within-chunk cumulative decay and the decayed q/k operands of every chunk
+    in one pass (``csrc/kda_prep.cu``): q, k, g [B, T, H, K] fp32 -> qc, kc, G, exp(G) k,
+    exp(G) q, exp(G_last - G) k ([B*H, NT, C, K]) and exp(G_last) ([B*H, NT, K])."""
+
+    @staticmethod
+    def forward(ctx, q, k, g, C):
+        from ._ext import ext
+
+        outs = ext().kda_prep_fwd(q, k, g, C)
+        ctx.save_for_backward(q, k, outs[2])
+        ctx.C = C
+        return tuple(outs)
+
+    @staticmethod
+    def backward(ctx, dqc, dkc, dG, dkg, dqg, dkd, ddecay):
+        from ._ext import ext
+
+        q, k, G = ctx.saved_tensors
+        c = [None if t is None else t.float().contiguous() for t in (dqc, dkc, dG, dkg, dqg, dkd, ddecay)]
+        dq, dk, dg = ext().kda_prep_bwd(q, k, G, ctx.C, *c)
+        return dq, dk, dg, None
+
+
 def chunk_kda(q, k, v, g, beta, scale: float | None = None, chunk_size: int = 64,
               initial_state: torch.Tensor | None = None, output_final_state: bool = False,
               use_qk_l2norm: bool = True):
@@ -156,9 +187,13 @@ def chunk_kda(q, k, v, g, beta, scale: float | None = None, chunk_size: int = 64
     q = q.float() * scale
     k, v, g, beta = k.float(), v.float(), g.float(), beta.float()
     pad = (-T) % C
+    prep = _prep_kernel(q)
     if pad:
-        # padded steps: g = 0 (no decay), k = v = q = 0, beta = 0 -> state unchanged
-        q, k, v, g = (F.pad(x, (0, 0, 0, 0, 0, pad)) for x in (q, k, v, g))
+        # padded steps: g = 0 (no decay), k = v = q = 0, beta = 0 -> state unchanged (the prep
+        # kernel reads rows past T as zeros itself)
+        if not prep:
+            q, k, g = (F.pad(x, (0, 0, 0, 0, 0, pad)) for x in (q, k, g))
+        v = F.pad(v, (0, 0, 0, 0, 0, pad))
         beta = F.pad(beta, (0, 0, 0, pad))
     Tp = T + pad
     NT = Tp // C
@@ -166,22 +201,27 @@ def chunk_kda(q, k, v, g, beta, scale: float | None = None, chunk_size: int = 64
     def chunks(x):  # [B, Tp, H, D] -> [B*H, NT, C, D]
         return x.view(B, NT, C, H, -1).permute(0, 3, 1, 2, 4).reshape(B * H, NT, C, -1)
 
-    qc, kc, vc, gc = chunks(q), chunks(k), chunks(v), chunks(g)
     bc = beta.view(B, NT, C, H).permute(0, 3, 1, 2).reshape(B * H, NT, C)
-    G = gc.cumsum(2)
+    vc = chunks(v)
     N = B * H * NT
+    if prep:
+        qc, kc, G, kg, qg, kdec, decay = _Prep.apply(q.contiguous(), k.contiguous(), g.contiguous(), C)
+    else:
+        qc, kc, gc = chunks(q), chunks(k), chunks(g)
+        G = gc.cumsum(2)
+        kg = G.exp() * kc
+        qg = qc * G.exp()
+        Glast = G[:, :, -1:, :]  # [BH, NT, 1, K]
+        kdec = (Glast - G).exp() * kc
+        decay = Glast[:, :, 0, :].exp()  # [BH, NT, K]
     Akk = decayed_gram(kc.reshape(N, C, K), kc.reshape(N, C, K), G.reshape(N, C, K), True).view(B * H, NT, C, C)
     Akk = Akk * bc[..., :, None]
     eye = torch.eye(C, device=q.device, dtype=torch.float32)
     Tm = torch.linalg.solve_triangular(eye + Akk, eye.expand_as(Akk), upper=False, unitriangular=True)
     Tm = Tm * bc[..., None, :]
-    w = Tm @ (G.exp() * kc)
+    w = Tm @ kg
     u = Tm @ vc
     Aqk = decayed_gram(qc.reshape(N, C, K), kc.reshape(N, C, K), G.reshape(N, C, K), False).view(B * H, NT, C, C)
-    qg = qc * G.exp()
-    Glast = G[:, :, -1:, :]  # [BH, NT, 1, K]
-    kdec = (Glast - G).exp() * kc
-    decay = Glast[:, :, 0, :].exp()  # [BH, NT, K]
     S0 = None if initial_state is None else initial_state.float().reshape(B * H, K, V)
     o, S = chunk_scan(u, w, qg, Aqk, kdec, decay, S0)
     o = o.view(B, H, NT, C, V).permute(0, 2, 3, 1, 4).reshape(B, Tp, H, V)[:, :T]
