@@ -132,3 +132,48 @@ def test_trainer_async_tp_on_fused_kernels_matches_sync_tp(tmp_path):
     sync_loss, fused_loss, calls, code = torch.load(tmp_path / "t0.pt")
     assert code == 0 and calls > 0, (calls, code)
     assert abs(sync_loss - fused_loss) < 2e-2 * abs(sync_loss), (sync_loss, fused_loss)
+
+
+def _ulysses_trainer(rank, world, port, out):
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.ops._ext import ext
+    from torchtitan_b200.parallel import tp_fused
+    from torchtitan_b200.trainer import Trainer
+
+    res = []
+    for flag in ("0", "1"):
+        os.environ["TTB_ULYSSES_FUSED"] = flag
+        t = Trainer(ConfigManager().parse_args([
+            "--module", "llama3", "--config", "llama3_debugmodel", "--training.steps", "3",
+            "--training.seq-len", "512", "--training.local-batch-size", "1",
+            "--parallelism.context-parallel-degree", "2", "--parallelism.context-parallel-method", "ulysses",
+            "--parallelism.data-parallel-shard-degree", "1",
+            "--activation-checkpoint.mode", "none", "--metrics.log-freq", "1", "--debug.seed", "0",
+            "--dump-folder", os.path.join(out, flag)]))
+        calls = []
+        orig = tp_fused._GroupComm.ag_gemm
+        tp_fused._GroupComm.ag_gemm = lambda self, *a, **k: (calls.append(1), orig(self, *a, **k))[1]
+        t.train()
+        tp_fused._GroupComm.ag_gemm = orig
+        res.append(t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"])
+        res.append(len(calls))
+        t.close()
+    torch.cuda.synchronize()
+    res.append(ext().tp_gemm_error_code(True))
+    torch.save(res, os.path.join(out, f"u{rank}.pt"))
+    dist.destroy_process_group()
+
+
+def test_ulysses_on_fused_kernels_matches_all_to_all(tmp_path):
+    """Llama-3 debug model, Ulysses CP = 2: three training steps with the head sharding carried
+    by the fused AG->GEMM / GEMM->RS kernels match the all-to-all formulation (bf16 tolerance)."""
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    mp.spawn(_ulysses_trainer, args=(2, port, str(tmp_path)), nprocs=2, join=True)
+    a2a_loss, a2a_calls, fused_loss, fused_calls, code = torch.load(tmp_path / "u0.pt")
+    assert code == 0 and a2a_calls == 0 and fused_calls > 0, (a2a_calls, fused_calls, code)
+    assert abs(a2a_loss - fused_loss) < 2e-2 * abs(a2a_loss), (a2a_loss, fused_loss)

@@ -24,6 +24,12 @@ def document_causal_mask(doc_ids: torch.Tensor) -> torch.Tensor:
     return (causal & same)[:, None]
 
 
+def _ulysses_fused_enabled() -> bool:
+    import os
+
+    return os.environ.get("TTB_ULYSSES_FUSED", "1") != "0"
+
+
 class GQAttention(nn.Module):
     def __init__(self, dim: int, n_heads: int, n_kv_heads: int | None = None, head_dim: int | None = None,
                  qk_norm: bool = False, norm_eps: float = 1e-5, mask_type: str = "causal"):
@@ -71,6 +77,13 @@ class GQAttention(nn.Module):
 
     def forward(self, x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, attention_masks=None) -> torch.Tensor:
         B, S, _ = x.shape
+        g = getattr(self, "cp_group", None)
+        if (g is not None and attention_masks is None and self.kv_cache is None and self.mask_type == "causal"
+                and _ulysses_fused_enabled()):
+            from torchtitan_b200.parallel import context_parallel as cpx
+
+            if cpx._ulysses_fused_ok(self, x, g):
+                return cpx.ulysses_fused_forward(self, x, cos, sin, g)
         q = self.wq(x)
         k = self.wk(x)
         v = self.wv(x)

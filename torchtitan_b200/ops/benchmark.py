@@ -244,6 +244,48 @@ def bench_kda(ext, out):
     print(json.dumps(out[-1]), flush=True)
 
 
+def bench_grouped_experts(ext, out):
+    """Routed SwiGLU experts, forward + backward, on our grouped tcgen05 GEMMs against ATen's
+    grouped GEMM (``torch._grouped_mm``, CUTLASS sm100) with the same SwiGLU. Shapes of the
+    Kimi-Linear 48B layer per EP=8 rank: 32 local experts, hidden 2304, expert FFN 1024,
+    65,536 routed rows (8,192 tokens x top-8) spread unevenly over the experts."""
+    from torchtitan_b200.ops.moe import grouped_swiglu
+
+    torch.manual_seed(0)
+    E, D, H, rows = 32, 2304, 1024, 65536
+    w = torch.rand(E, device="cuda") + 0.5
+    counts = (w / w.sum() * rows).floor().long()
+    counts[0] += rows - int(counts.sum())
+    x = (torch.randn(rows, D, device="cuda") * 0.5).bfloat16().requires_grad_()
+    w1, w3 = ((torch.randn(E, H, D, device="cuda") * 0.02).bfloat16().requires_grad_() for _ in range(2))
+    w2 = (torch.randn(E, D, H, device="cuda") * 0.02).bfloat16().requires_grad_()
+    dy = torch.randn(rows, D, device="cuda").bfloat16()
+    offs = torch.cumsum(counts, 0).to(torch.int32)
+
+    def ours():
+        y = grouped_swiglu(x, w1, w2, w3, counts)
+        y.backward(dy)
+
+    def aten():
+        h1 = torch._grouped_mm(x, w1.transpose(-2, -1), offs=offs)
+        h3 = torch._grouped_mm(x, w3.transpose(-2, -1), offs=offs)
+        a = torch.nn.functional.silu(h1) * h3
+        y = torch._grouped_mm(a, w2.transpose(-2, -1), offs=offs)
+        y.backward(dy)
+
+    fl = 3 * 2 * 3 * rows * D * H  # three GEMMs, forward + two backward GEMMs each
+    res = {"kernel": "grouped_swiglu_fwd_bwd", "E": E, "D": D, "H": H, "rows": rows}
+    res["ours_ms"] = time_fn(ours)
+    res["ours_tflops"] = fl / res["ours_ms"] / 1e9
+    try:
+        res["aten_grouped_mm_ms"] = time_fn(aten)
+        res["aten_tflops"] = fl / res["aten_grouped_mm_ms"] / 1e9
+    except Exception as e:  # noqa: BLE001 - record why the comparison is missing
+        res["aten_error"] = repr(e)[:200]
+    out.append(res)
+    print(json.dumps(out[-1]), flush=True)
+
+
 def bench_kda_vs_fla(ext, out):
     """Chunked KDA forward+backward against the fla library's ``chunk_kda`` (Triton, the
     reference's path: ``kimi_linear/model.py:559-571``) on the same inputs: H 32, K = V = 128,
@@ -377,6 +419,8 @@ def main():
         bench_kda(ext, out)
     if "kda_fla" in sel:
         bench_kda_vs_fla(ext, out)
+    if "grouped" in sel:
+        bench_grouped_experts(ext, out)
     if "muon" in sel:
         bench_muon(ext, out)
     if "attn" in sel:

@@ -83,6 +83,73 @@ def ulysses_hook(group):
     return hook
 
 
+# ------------------------------------------- Ulysses on the fused AG->GEMM / GEMM->RS kernels
+# Ulysses shards attention by heads over the cp group with the full sequence per rank. The
+# same sharding follows from sequence-parallel head-parallel projections: rank r computes
+#   q_r, k_r, v_r = AllGather_seq(x) . W{q,k,v}[heads_r]^T      [B, S, H/cp, D]
+#   out_r         = ReduceScatter_seq(o_r . Wo[:, heads_r]^T)     [B, S/cp, dim]
+# with each collective inside one persistent tcgen05 GEMM over NVLink peer memory
+# (``parallel/tp_fused.py``). The weights stay replicated over cp: rank r's gradient covers its
+# head slice over the whole sequence (zero elsewhere) and the FSDP reduction over
+# dp_shard x cp sums the slices, which equals the a2a formulation's per-sequence-shard sum.
+# Per rank the GEMM FLOPs are those of the a2a form; the bytes over NVLink are the gathered
+# input and the reduce-scattered output instead of the q/k/v and o shards.
+_ROPE_FULL: dict = {}
+
+
+def _gather_seq_table(t: torch.Tensor, group) -> torch.Tensor:
+    """cos / sin of the local positions -> the full sequence (rank order = sequence order)."""
+    key = (t.data_ptr(), tuple(t.shape), group.group_name)
+    hit = _ROPE_FULL.get(key)
+    if hit is not None and hit[0] is t:
+        return hit[1]
+    cp = dist.get_world_size(group)
+    parts = [torch.empty_like(t) for _ in range(cp)]
+    dist.all_gather(parts, t.contiguous(), group=group)
+    full = torch.cat(parts, dim=t.dim() - 2)
+    _ROPE_FULL.clear()  # one table pair per step is live
+    _ROPE_FULL[key] = (t, full)
+    return full
+
+
+def _ulysses_fused_ok(attn, x, group) -> bool:
+    from torchtitan_b200.parallel import tp_fused
+
+    if not tp_fused.fused_available(x, group) or x.dtype != torch.bfloat16:
+        return False
+    cp = dist.get_world_size(group)
+    hq, hk = attn.n_heads, attn.n_kv_heads
+    if hq % cp or hk % cp or getattr(attn, "q_norm", None) is not None:
+        return False
+    lins = (attn.wq, attn.wk, attn.wv, attn.wo)
+    if any(getattr(l, "bias", None) is not None or getattr(l, "tp_mode", None) for l in lins):
+        return False
+    D = attn.head_dim
+    return (tp_fused.shapes_ok(x, hq // cp * D, x.shape[-1]) and tp_fused.shapes_ok(x, hk // cp * D, x.shape[-1])
+            and (hq // cp * D) % 64 == 0)
+
+
+def ulysses_fused_forward(attn, x, cos, sin, group):
+    """Attention of ``attn`` (wq/wk/wv/wo, RoPE, causal) on sequence-sharded ``x``
+    [B, S/cp, dim] with the Ulysses head sharding carried by the fused kernels."""
+    from torchtitan_b200.models.common.layers import _local
+    from torchtitan_b200.parallel.tp_fused import FusedAGMatmul, FusedMatmulRS
+
+    cp, r = dist.get_world_size(group), dist.get_rank(group)
+    D = attn.head_dim
+    hq, hk = attn.n_heads // cp, attn.n_kv_heads // cp
+    wq, wk, wv, wo = (_local(l.weight).to(x.dtype) for l in (attn.wq, attn.wk, attn.wv, attn.wo))
+    B = x.shape[0]
+    q = FusedAGMatmul.apply(x, wq[r * hq * D:(r + 1) * hq * D], group).view(B, -1, hq, D)
+    k = FusedAGMatmul.apply(x, wk[r * hk * D:(r + 1) * hk * D], group).view(B, -1, hk, D)
+    v = FusedAGMatmul.apply(x, wv[r * hk * D:(r + 1) * hk * D], group).view(B, -1, hk, D)
+    cf, sf = _gather_seq_table(cos, group), _gather_seq_table(sin, group)
+    q, k = ops.rope(q, cf, sf), ops.rope(k, cf, sf)
+    o = attn.inner_attention(q, k, v, None)
+    return FusedMatmulRS.apply(o.reshape(B, o.shape[1], hq * D), wo[:, r * hq * D:(r + 1) * hq * D].contiguous(),
+                               group)
+
+
 # ------------------------------------------------------------ ring (allgather)
 class _AllGatherSeqCP(torch.autograd.Function):
     @staticmethod
@@ -141,6 +208,8 @@ def apply_cp_to_attention_modules(modules: list, cp_mesh, method: str = "ring", 
     group = cp_mesh.get_group()
     for m in modules:
         m.cp_hook = ulysses_hook(group) if method == "ulysses" else ring_hook(group, load_balance)
+        if method == "ulysses":
+            m.cp_group = group  # enables the fused-kernel path where it applies (see Attention.forward)
 
 
 def prepare_context_parallel_input(inputs: torch.Tensor, labels: torch.Tensor, extra_kwargs: dict[str, Any],
