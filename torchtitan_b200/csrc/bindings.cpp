@@ -300,6 +300,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("reset") = true);
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("gather_rows", [](Tensor src, Tensor idx) {
+    check_cuda_bf16(src, "src");
+    TORCH_CHECK(src.dim() == 2 && src.is_contiguous() && idx.scalar_type() == at::kLong && idx.is_cuda() &&
+                    idx.dim() == 1 && idx.is_contiguous(),
+                "gather_rows: src [n, d] contiguous bf16, idx [rows] int64 (negative = zero row)");
+    c10::cuda::CUDAGuard g(src.device());
+    auto out = torch::empty({idx.size(0), src.size(1)}, src.options());
+    ttb::gather_rows_bf16(src.data_ptr(), src.size(0), idx.data_ptr<int64_t>(), out.data_ptr(), idx.size(0), src.size(1),
+                          stream());
+    return out;
+  });
   m.def("rope", &rope);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);

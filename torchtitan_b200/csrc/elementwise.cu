@@ -265,6 +265,26 @@ __global__ void swiglu_bwd_kernel(const bf16* __restrict__ dy, const bf16* __res
   store8(db + t * 8, ob);
 }
 
+// out[p] = src[idx[p]] (idx < 0: a zero row); bf16 rows of d elements, 16-byte vectors, one
+// warp per output row
+__global__ void __launch_bounds__(256) gather_rows_kernel(const bf16* __restrict__ src, const int64_t* __restrict__ idx,
+                                                          bf16* __restrict__ out, int64_t rows, int d8,
+                                                          int64_t n_src) {
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * 8 + threadIdx.x / 32;
+  if (p >= rows) return;
+  const int64_t sr = idx[p];
+  const int lane = threadIdx.x % 32;
+  V8* o = reinterpret_cast<V8*>(out) + p * d8;
+  if (sr < 0 || sr >= n_src) {  // (an index past the source also reads as a zero row)
+    V8 z;
+    for (int i = 0; i < 4; ++i) z.h[i] = __floats2bfloat162_rn(0.f, 0.f);
+    for (int c = lane; c < d8; c += 32) o[c] = z;
+  } else {
+    const V8* s = reinterpret_cast<const V8*>(src) + sr * d8;
+    for (int c = lane; c < d8; c += 32) o[c] = s[c];
+  }
+}
+
 // Row-group shapes: (warps per row, vectors per lane, resident CTAs per SM). The forward keeps
 // up to 8 vectors (128 bytes) of x per lane, the backward up to 4 of x and 4 of dy (plus the
 // 32 fp32 weight-gradient sums); 16384-wide rows use 8 warps and 8 vectors.
@@ -344,6 +364,15 @@ void rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd
   dispatch_rows<true>(x, dy, w, const_cast<float*>(rstd), dx, dw_partial, rows, dim, 0.f, w_fp32, nparts / groups,
                       s);
   check_cuda(cudaGetLastError(), "rmsnorm_bwd");
+}
+
+void gather_rows_bf16(const void* src, int64_t n_src, const int64_t* idx, void* out, int64_t rows, int64_t d,
+                      cudaStream_t s) {
+  if (d % 8) throw std::runtime_error("gather_rows: row length must be a multiple of 8");
+  if (rows == 0) return;
+  gather_rows_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, s>>>(
+      static_cast<const bf16*>(src), idx, static_cast<bf16*>(out), rows, static_cast<int>(d / 8), n_src);
+  check_cuda(cudaGetLastError(), "gather_rows");
 }
 
 void reduce_rows_f32(const float* partial, float* out, int64_t nparts, int64_t dim, cudaStream_t s) {

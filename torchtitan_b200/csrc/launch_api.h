@@ -42,6 +42,9 @@ void rmsnorm_fwd(const void* x, const void* w, void* y, float* rstd, int64_t row
                  cudaStream_t s);
 void rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw_partial,
                  int64_t rows, int64_t dim, int w_fp32, int nparts, cudaStream_t s);
+// out[p] = src[idx[p]] or a zero row where idx[p] < 0 (bf16, row length a multiple of 8)
+void gather_rows_bf16(const void* src, int64_t n_src, const int64_t* idx, void* out, int64_t rows, int64_t d,
+                      cudaStream_t s);
 int rmsnorm_bwd_parts(int64_t rows, int64_t dim, int sms);
 void reduce_rows_f32(const float* partial, float* out, int64_t nparts, int64_t dim, cudaStream_t s);
 void rope_apply(const void* x, void* y, const float* cos, const float* sin, int64_t B, int64_t S, int64_t H,

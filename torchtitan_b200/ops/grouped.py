@@ -1,7 +1,7 @@
 """Grouped SwiGLU experts on the grouped tcgen05 GEMM.
 
-Rows arrive sorted by expert with ``counts[e]`` rows each.  They are copied
-into a padded buffer where expert e's rows start at a multiple of 128 (the
+Rows arrive sorted by expert with ``counts[e]`` rows each.  They are copied (one row
+gather kernel; padding rows written as zeros) into a padded buffer where expert e's rows start at a multiple of 128 (the
 GEMM's M tile), so every 128-row tile belongs to exactly one expert and every
 expert's K range (for the weight gradient) is 128-aligned.  The layout is
 computed on the device from ``counts`` with a fixed upper bound on the padded
@@ -45,33 +45,32 @@ class _GroupedSwiGLU(torch.autograd.Function):
         E, H, D = w1.shape
         n = x.shape[0]
         dest, tg, kst, kln, P = padded_layout(counts, n)
-        xp = x.new_zeros(P, D)
-        xp[dest] = x
+        src_of = torch.full((P,), -1, dtype=torch.int64, device=x.device)  # padding rows read as zeros
+        src_of[dest] = torch.arange(n, device=x.device)
+        xp = ext.gather_rows(x, src_of)
         w1f, w3f, w2f = w1.reshape(E * H, D), w3.reshape(E * H, D), w2.reshape(E * D, H)
         h1 = ext.gemm_grouped_rows(xp, w1f, tg, H, H, False)
         h3 = ext.gemm_grouped_rows(xp, w3f, tg, H, H, False)
         a = ext.swiglu_fwd(h1, h3)
         yp = ext.gemm_grouped_rows(a, w2f, tg, D, D, False)
-        ctx.save_for_backward(xp, h1, h3, a, w1, w2, w3, dest, tg, kst, kln)
-        return yp[dest]
+        ctx.save_for_backward(xp, h1, h3, a, w1, w2, w3, dest, src_of, tg, kst, kln)
+        return ext.gather_rows(yp, dest)
 
     @staticmethod
     def backward(ctx, dy):
         ext = _ext.ext()
-        xp, h1, h3, a, w1, w2, w3, dest, tg, kst, kln = ctx.saved_tensors
+        xp, h1, h3, a, w1, w2, w3, dest, src_of, tg, kst, kln = ctx.saved_tensors
         E, H, D = w1.shape
-        P = xp.shape[0]
-        dyp = dy.new_zeros(P, D)
-        dyp[dest] = dy.contiguous()
+        dyp = ext.gather_rows(dy.contiguous(), src_of)
         # dgrad through w2: B = W2[e] read as [D(red), H(out)] rows of the stacked [E*D, H]
         da = ext.gemm_grouped_rows(dyp, w2.reshape(E * D, H), tg, H, D, True)
         dh1, dh3 = ext.swiglu_bwd(da, h1, h3)
         dx = ext.gemm_grouped_rows(dh1, w1.reshape(E * H, D), tg, D, H, True)
-        dx = dx + ext.gemm_grouped_rows(dh3, w3.reshape(E * H, D), tg, D, H, True)
+        dx.add_(ext.gemm_grouped_rows(dh3, w3.reshape(E * H, D), tg, D, H, True))
         dw2 = ext.gemm_grouped_k(dyp, a, kst, kln)    # [E, D, H]
         dw1 = ext.gemm_grouped_k(dh1, xp, kst, kln)   # [E, H, D]
         dw3 = ext.gemm_grouped_k(dh3, xp, kst, kln)
-        return dx[dest], dw1.to(w1.dtype), dw2.to(w2.dtype), dw3.to(w3.dtype), None
+        return ext.gather_rows(dx, dest), dw1.to(w1.dtype), dw2.to(w2.dtype), dw3.to(w3.dtype), None
 
 
 def grouped_swiglu_cuda(x, w1, w2, w3, counts):
@@ -116,7 +115,7 @@ class _GroupedSwiGLUPadded(torch.autograd.Function):
         da = ext.gemm_grouped_rows(dyp, w2.reshape(E * D, H), tg, H, D, True)
         dh1, dh3 = ext.swiglu_bwd(da, h1, h3)
         dx = ext.gemm_grouped_rows(dh1, w1.reshape(E * H, D), tg, D, H, True)
-        dx = dx + ext.gemm_grouped_rows(dh3, w3.reshape(E * H, D), tg, D, H, True)
+        dx.add_(ext.gemm_grouped_rows(dh3, w3.reshape(E * H, D), tg, D, H, True))
         dw2 = ext.gemm_grouped_k(dyp, a, kst, kln)
         dw1 = ext.gemm_grouped_k(dh1, xp, kst, kln)
         dw3 = ext.gemm_grouped_k(dh3, xp, kst, kln)
