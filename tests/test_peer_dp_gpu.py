@@ -159,12 +159,13 @@ def _ep_peer(rank, world):
     for name in ("w1", "w2", "w3"):
         setattr(e, name, torch.nn.Parameter(getattr(e, name).data[rank * 4:(rank + 1) * 4].clone()))
     m.ep_dispatch = make_fused_ep_dispatch(dist.group.WORLD, E)
-    xr = x.detach().clone().requires_grad_()
-    out = m(xr)
-    assert m.ep_dispatch.comm.comm == "peer"
-    torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
-    out.float().square().sum().backward()
-    torch.testing.assert_close(xr.grad.float(), gx_ref.float(), rtol=5e-2, atol=5e-2)
+    for _ in range(2):  # the second call queues its row stores before the host sees the counts
+        xr = x.detach().clone().requires_grad_()
+        out = m(xr)
+        assert m.ep_dispatch.comm.comm == "peer"
+        torch.testing.assert_close(out.float(), ref.float(), rtol=2e-2, atol=2e-2)
+        out.float().square().sum().backward()
+        torch.testing.assert_close(xr.grad.float(), gx_ref.float(), rtol=5e-2, atol=5e-2)
     torch.cuda.synchronize()
     from torchtitan_b200.ops._ext import ext
 

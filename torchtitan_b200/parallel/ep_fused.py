@@ -65,6 +65,7 @@ class Plan:
         self.dest_row = (off[me][e_of_row] + k).to(torch.int64)
         self.local_counts = T[me]                        # rows of each of my experts (device)
         self.me, self.El, self.device = me, El, device
+        self.scattered = False  # set when the row stores were queued before finalize
 
     def finalize(self, M_host: torch.Tensor) -> "Plan":
         ep, E = M_host.shape
@@ -93,6 +94,7 @@ class EPPeerComm:
         self.cap = 0
         self.dim = 0
         self._epoch = 0
+        self.last_max_rows = 0  # largest routed rows of one rank seen in a count matrix
 
     # ---------------------------------------------------------------- buffers
     def _symm(self):
@@ -134,14 +136,17 @@ class EPPeerComm:
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)
 
-    def reserve(self, device: torch.device, dim: int, routed_rows: int) -> None:
-        """Size the receive buffers once for the worst case of this batch shape: every rank's
-        ``routed_rows`` (tokens x top-k, the same on all ranks) landing on one owner, plus one
-        partial tile per local expert. The allocation is collective, so it happens at the
-        first dispatch (and again only if the batch shape grows), never because of a count."""
-        if self.comm != "peer":
-            return
-        self._ensure_rows(device, dim, self.ep * routed_rows + (self.E // self.ep) * TILE)
+    def bound(self, max_routed_rows: int) -> int:
+        """Receive rows that cover any routing of ``max_routed_rows`` rows per source: all of
+        them on one owner, plus one partial tile per local expert."""
+        return self.ep * max_routed_rows + (self.E // self.ep) * TILE
+
+    def reserve(self, device: torch.device, dim: int, max_routed_rows: int) -> None:
+        """Size the receive buffers for the worst case of ``max_routed_rows`` (a value every
+        rank holds: it comes from a count matrix all ranks share). The allocation is
+        collective, so it happens when the largest per-rank batch grows, never per call."""
+        if self.comm == "peer":
+            self._ensure_rows(device, dim, self.bound(max_routed_rows))
 
     def barrier(self) -> None:
         if self.comm == "peer":
@@ -238,7 +243,7 @@ class _Dispatch(torch.autograd.Function):
     @staticmethod
     def forward(ctx, routed, comm: EPPeerComm, plan: Plan):
         ctx.comm, ctx.plan = comm, plan
-        if getattr(plan, "scattered", False):  # the stores were queued before the host saw the counts
+        if plan.scattered:  # the stores were queued before the host saw the counts
             xp = comm.buf_in[:plan.P].clone()
         else:
             xp = comm.scatter(routed, plan.dest_rank, plan.dest_row, plan.P, plan.P_max)
@@ -283,13 +288,29 @@ def make_fused_ep_dispatch(ep_group, num_experts: int, comm: str | None = None):
         if pc.comm == "peer" and routed.dtype != torch.bfloat16:
             routed = routed.to(torch.bfloat16)
         plan = Plan(m_dev, pc.me, routed.device, n_rows=routed.shape[0])
-        if pc.comm == "peer":
-            # the row stores go out while the count matrix travels to the host
-            pc.reserve(routed.device, routed.shape[1], routed.shape[0])
+        # decided from what every rank shares (the reserved size and earlier count matrices), so
+        # all ranks take the same branch and issue the same barriers
+        early = (pc.comm == "peer" and pc.dim == routed.shape[1] and pc.last_max_rows > 0
+                 and pc.cap >= pc.bound(pc.last_max_rows))
+        if early:
+            # the row stores go out while the count matrix travels to the host; they are
+            # bounds-checked against the reserved rows
             pc.launch_scatter(routed.contiguous(), plan.dest_rank, plan.dest_row)
             plan.scattered = True
+        if ev is not None:
             ev.synchronize()
         plan.finalize(m_host)
+        if pc.comm == "peer":
+            rows_per_rank = m_host.sum(1)
+            pc.last_max_rows = max(pc.last_max_rows, int(rows_per_rank.max()))
+            if early and plan.P_max > pc.cap:
+                # more rows than any earlier call: rows past the reserved buffer were skipped
+                # (and flagged); every rank sees the same matrix, grows and stores again
+                torch.cuda.synchronize(routed.device)
+                pc._ext.ep_error_code(True)
+                plan.scattered = False
+            if not plan.scattered:
+                pc.reserve(routed.device, routed.shape[1], pc.last_max_rows)
         xp = _Dispatch.apply(routed.contiguous(), pc, plan)
         if type(experts) is GroupedExperts:
             yp = ops.grouped_swiglu_padded(xp, *experts.weights(), plan.local_counts)
