@@ -1204,3 +1204,60 @@ def _validate_layout(rank, world, out_dir, extra):
 def test_validation_through_parallel_layouts(extra):
     with tempfile.TemporaryDirectory() as d:
         _run(_validate_layout, 2, d, extra)
+
+
+# ---------------------------------------------------------------- forge engine under pipeline parallelism
+def _forge_pp(rank, world, out_dir, schedule):
+    from torch.distributed.checkpoint.state_dict import StateDictOptions, get_model_state_dict
+
+    from torchtitan_b200.components.loss import cross_entropy_loss
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.forge import ForgeEngine
+    from torchtitan_b200.models.llama3 import model_registry
+
+    eng = ForgeEngine(ConfigManager().parse_args([
+        "--module", "llama3", "--config", "llama3_debugmodel_cpu", "--training.steps", "4",
+        "--training.seq-len", "32", "--parallelism.pipeline-parallel-degree", "2",
+        "--parallelism.data-parallel-shard-degree", "1", "--parallelism.pipeline-parallel-microbatch-size", "1",
+        "--training.local-batch-size", "2", "--parallelism.pipeline-parallel-schedule", schedule,
+        "--training.dtype", "float32", "--training.mixed-precision-param", "float32",
+        "--activation-checkpoint.mode", "none", "--debug.seed", "0", "--dump-folder", out_dir]))
+    full = {}
+    for part in eng.model_parts:
+        full.update(get_model_state_dict(part, options=StateDictOptions(full_state_dict=True)))
+    gathered = [None] * world
+    dist.all_gather_object(gathered, full)
+    merged = {k: v for d in gathered for k, v in d.items()}
+    ref = model_registry(eng.config.model_spec.flavor).model.build()
+    ref.load_state_dict(merged, strict=False)
+    ref.rope.init_weights()
+    tokens = torch.randint(0, 2048, (2, 33), generator=torch.Generator().manual_seed(5))
+    inp, labels = tokens[:, :-1], tokens[:, 1:]
+    # forward only: every pipeline rank gets the last stage's logits, equal to the whole model's
+    logits = eng.forward({"input": inp})
+    with torch.no_grad():
+        want = ref(inp)
+    torch.testing.assert_close(logits, want, rtol=1e-5, atol=1e-5)
+    # a custom objective (half the cross entropy, normalised by twice the token count) trains
+    # through the schedule's last stage
+    loss = eng.train_on_batches([({"input": inp}, labels)],
+                                loss_fn=lambda pred, lab: 0.5 * cross_entropy_loss(pred, lab),
+                                count_valid=lambda lab: 2 * lab.numel())
+    if eng.pp_has_last_stage:
+        exp = 0.25 * cross_entropy_loss(want, labels) / labels.numel()
+        torch.testing.assert_close(loss.reshape(()), exp, rtol=1e-5, atol=1e-6)
+    assert eng.step == 1 and eng.trainer.loss_fn is not None and "count_valid" not in eng.trainer.__dict__
+    after = eng.forward({"input": inp})
+    assert not torch.allclose(after, logits)  # the step changed the weights
+    # the default objective is back: the next step's loss is the plain mean cross entropy
+    loss2 = eng.train_on_batches([({"input": inp}, labels)])
+    if eng.pp_has_last_stage:
+        torch.testing.assert_close(loss2.reshape(()), cross_entropy_loss(after, labels) / labels.numel(),
+                                   rtol=1e-5, atol=1e-6)
+    eng.close()
+
+
+@pytest.mark.parametrize("schedule", ["1F1B", "Interleaved1F1B"])
+def test_forge_engine_pipeline_forward_and_custom_objective(schedule):
+    with tempfile.TemporaryDirectory() as d:
+        _run(_forge_pp, 2, d, schedule)

@@ -108,3 +108,26 @@ def test_kv_cache_generation_equals_full_recompute(module):
         a = generate(m, p, 6, 1.0, 5, torch.Generator().manual_seed(1))
         b = generate(m, p, 6, 1.0, 5, torch.Generator().manual_seed(1), use_cache=False)
     assert torch.equal(a, b) and all(x.kv_cache is None for x in atts)
+
+
+def test_forge_example_loop_matches_trainer(tmp_path):
+    """The engine-driven loop reproduces the trainer's own loop on the same config."""
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.forge import ForgeEngine, example_train
+    from torchtitan_b200.trainer import Trainer
+
+    args = ["--module", "llama3", "--config", "llama3_debugmodel", "--training.seq-len", "64",
+            "--training.local-batch-size", "2", "--training.dtype", "float32", "--training.steps", "3",
+            "--training.mixed-precision-param", "float32", "--activation-checkpoint.mode", "none",
+            "--debug.seed", "0"]
+    eng = ForgeEngine(ConfigManager().parse_args(args + ["--dump-folder", str(tmp_path / "a")]))
+    got = example_train(eng)
+    eng.close()
+    t = Trainer(ConfigManager().parse_args(args + ["--dump-folder", str(tmp_path / "b")]))
+    want = []
+    it = t.batch_generator(t.dataloader)
+    while t.step < 3:
+        t.step += 1
+        want.append(float(t.train_step(it)))
+    t.close()
+    assert got == want and len(got) == 3

@@ -261,6 +261,11 @@ class Trainer(Stateful, Configurable):
         apply_cuda_graphs(model, c.training.local_batch_size, c.training.seq_len,
                           model.tok_embeddings.weight.dtype)
 
+    @staticmethod
+    def count_valid(labels: torch.Tensor) -> torch.Tensor:
+        """Tokens of a microbatch that count toward the step's loss normalisation."""
+        return (labels != IGNORE_INDEX).sum()
+
     def _loss(self, pred: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         m = self.model_parts[-1]
         if getattr(m, "_tp_loss_parallel", False):
@@ -407,7 +412,7 @@ class Trainer(Stateful, Configurable):
         local_valid = 0
         for _ in range(self.gradient_accumulation_steps):
             inp, labels = next(data_iterator)
-            local_valid += int((labels != IGNORE_INDEX).sum())
+            local_valid += int(self.count_valid(labels))
             mbs.append((inp, labels))
         local_valid_t = torch.tensor(float(local_valid), device=self.device)
         if pd.semi_sync_replicas:  # each replica normalises by its own tokens
