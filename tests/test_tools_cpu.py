@@ -36,14 +36,53 @@ def test_loss_compare_detects_differences(tmp_path):
     assert compare({1: 1.0, 2: 0.5}, {1: 1.0, 2: 0.5}, True, 0.0) == []
     assert len(compare({1: 1.0, 2: 0.5}, {1: 1.0, 2: 0.50001}, True, 0.0)) == 1
     assert compare({1: 1.0}, {1: 1.00001}, False, 1e-4) == []
-    args = ("--module llama3 --config llama3_debugmodel --training.seq-len 64 --training.local-batch-size 2 "
-            "--training.dtype float32 --training.mixed-precision-param float32 --activation-checkpoint.mode none")
-    rc = main(["--baseline", args, "--test", args, "--steps", "3", "--assert-equal", "--output-folder",
-               str(tmp_path)])
-    assert rc == 0
-    rc = main(["--baseline", args, "--test", args + " --optimizer.lr 1e-2", "--steps", "3", "--assert-equal",
-               "--output-folder", str(tmp_path / "b")])
+    opts = ("--training.seq-len 64 --training.local-batch-size 2 --training.dtype float32 "
+            "--training.mixed-precision-param float32 --activation-checkpoint.mode none")
+    common = [".", ".", "--baseline-config", "llama3_debugmodel", "--steps", "3", "--baseline-options", opts]
+    exp = tmp_path / "losses.txt"
+    rc = main(common + ["--test-options", opts, "--assert-equal", "--output-folder", str(tmp_path / "a"),
+                        "--export-result", str(exp)])
+    assert rc == 0 and len(exp.read_text().splitlines()) == 3
+    assert (tmp_path / "a" / "seed" / "checkpoint" / "step-0" / ".metadata").exists()
+    rc = main(common + ["--test-options", opts + " --optimizer.lr 1e-2", "--assert-equal", "--output-folder",
+                        str(tmp_path / "b")])
     assert rc == 1
+    # recorded curve: the baseline alone must reproduce it
+    assert main(common + ["--baseline-only", "--import-result", str(exp), "--assert-equal"]) == 0
+
+
+def test_loss_compare_seed_checkpoint_across_layouts(tmp_path):
+    """From one seed checkpoint, one process and two tensor-parallel ranks (gloo, same data on
+    both) give the same curve within fp32 reduction-order tolerance."""
+    from torchtitan_b200.loss_compare import main
+
+    opts = ("--training.seq-len 64 --training.local-batch-size 2 --training.dtype float32 "
+            "--training.mixed-precision-param float32 --activation-checkpoint.mode none")
+    rc = main([".", ".", "--baseline-config", "llama3_debugmodel_cpu", "--steps", "3", "--baseline-options", opts,
+               "--test-options", opts + " --parallelism.tensor-parallel-degree 2 "
+               "--parallelism.data-parallel-shard-degree 1", "--test-ngpus", "2", "--rtol", "1e-4",
+               "--output-folder", str(tmp_path)])
+    assert rc == 0, (tmp_path / "summary.txt").read_text()
+
+
+def test_seed_checkpoint_sets_initial_weights(tmp_path):
+    """A seed checkpoint (model only, step 0) gives a run with another seed the same weights."""
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    args = ["--module", "llama3", "--config", "llama3_debugmodel", "--training.seq-len", "64",
+            "--training.dtype", "float32", "--training.mixed-precision-param", "float32", "--checkpoint.enable"]
+    a = Trainer(ConfigManager().parse_args(args + ["--debug.seed", "1", "--dump-folder", str(tmp_path / "a")]))
+    path = a.checkpointer.save_seed()
+    wa = {k: v.detach().clone() for k, v in a.model_parts[0].state_dict().items()}
+    a.close()
+    b = Trainer(ConfigManager().parse_args(args + ["--debug.seed", "2", "--dump-folder", str(tmp_path / "b"),
+                                                   "--checkpoint.initial-load-path", path]))
+    wb = b.model_parts[0].state_dict()
+    assert any(not torch.equal(wa[k], wb[k]) for k in wa)  # different seeds, different weights
+    assert b.checkpointer.load()
+    assert all(torch.equal(wa[k], b.model_parts[0].state_dict()[k]) for k in wa)
+    b.close()
 
 
 def test_generate_greedy_and_eos():
@@ -131,3 +170,29 @@ def test_forge_example_loop_matches_trainer(tmp_path):
         want.append(float(t.train_step(it)))
     t.close()
     assert got == want and len(got) == 3
+
+
+def test_loss_compare_checks_out_a_revision(tmp_path):
+    """A git revision runs from its own temporary worktree, which is removed afterwards."""
+    import subprocess
+
+    from torchtitan_b200 import loss_compare
+
+    r = subprocess.run(["git", "rev-parse", "--verify", "HEAD"], cwd=loss_compare.HERE, capture_output=True)
+    if r.returncode:
+        pytest.skip("not a git checkout")
+    seen = []
+    real = loss_compare._launch
+    loss_compare._launch = lambda tree, args, n, log: (seen.append(tree), real(tree, args, n, log))[1]
+    try:
+        opts = ("--training.seq-len 32 --training.local-batch-size 1 --training.dtype float32 "
+                "--training.mixed-precision-param float32 --activation-checkpoint.mode none")
+        rc = loss_compare.main(["HEAD", ".", "--steps", "1", "--no-seed-checkpoint", "--baseline-options", opts,
+                                "--test-options", opts, "--rtol", "1.0"])
+    finally:
+        loss_compare._launch = real
+    assert rc == 0
+    assert seen[0] != loss_compare.HERE and seen[1] == loss_compare.HERE
+    assert not os.path.exists(seen[0])
+    wt = subprocess.run(["git", "worktree", "list"], cwd=loss_compare.HERE, capture_output=True, text=True).stdout
+    assert seen[0] not in wt

@@ -177,6 +177,16 @@ class CheckpointManager(Configurable):
         logger.info(f"checkpoint step {step} issued in {time.perf_counter() - t0:.2f}s -> {path}")
         self._purge()
 
+    def save_seed(self) -> str:
+        """Write the freshly initialised model, full precision and model only, as step 0 (parity:
+        the reference's ``--checkpoint.create_seed_checkpoint``).  A later run in the same dump
+        folder, or any run given this step directory as ``initial_load_path``, starts from
+        these weights whatever its own seed or parallel layout (DCP reshards on load)."""
+        path = self._step_dir(0)
+        dcp.save(self.states[MODEL].state_dict(), checkpoint_id=path)
+        logger.info(f"seed checkpoint -> {path}")
+        return path
+
     def _save_hf(self, state: dict[str, Any], path: str) -> None:
         from safetensors.torch import save_file
 
@@ -219,6 +229,12 @@ class CheckpointManager(Configurable):
             try:
                 if not os.path.exists(os.path.join(path, ".metadata")):
                     raise FileNotFoundError(f"no checkpoint at {path}")
+                if s == 0:  # a seed checkpoint holds the model's weights alone
+                    sd = self.states[MODEL].state_dict()
+                    dcp.load(sd, checkpoint_id=path)
+                    self.states[MODEL].load_state_dict(sd)
+                    logger.info(f"loaded seed checkpoint from {path}")
+                    return True
                 dcp.load({k: self.states[k] for k in keys}, checkpoint_id=path)
             except (Exception, CheckpointException) as e:  # noqa: BLE001 - reported, then an older step is tried
                 errors.append(f"step {s}: {type(e).__name__}: {e}")

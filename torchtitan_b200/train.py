@@ -26,7 +26,7 @@ def main(trainer_cls=None) -> None:
                 raise ValueError("seed checkpoints must be created on a single device")
             if not cfg.checkpoint.enable:
                 raise ValueError("enable checkpointing to create a seed checkpoint")
-            trainer.checkpointer.save(step=1, last_step=False)
+            trainer.checkpointer.save_seed()
             logger.info("created seed checkpoint")
         else:
             trainer.train()
