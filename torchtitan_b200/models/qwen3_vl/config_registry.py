@@ -62,3 +62,20 @@ def qwen3_vl_30b_a3b() -> Trainer.Config:
     c.training.steps = 1000
     c.parallelism.expert_parallel_degree = 8
     return c
+
+
+def qwen3_vl_debugmodel_cc12m() -> Trainer.Config:
+    """Debug model on CC12M-format WebDataset shards (``--dataloader.dataset-path <dir of .tar>``;
+    ``--dataloader.dataset obelics`` reads OBELICS parquet/JSONL instead)."""
+    from torchtitan_b200.components.mm_datasets import MMDataLoader
+
+    c = qwen3_vl_debugmodel()
+    a = c.model_spec.model
+    c.training.local_batch_size, c.training.seq_len = 2, 1024
+    c.dataloader = MMDataLoader.Config(dataset="cc12m", dataset_path="./data/cc12m", patch_size=a.patch_size,
+                                       temporal_patch_size=a.temporal_patch_size,
+                                       spatial_merge_size=a.spatial_merge_size, min_pixels=64 * 64,
+                                       max_pixels=256 * 256, packing_buffer_size=16,
+                                       image_token_id=a.image_token_id, video_token_id=a.video_token_id,
+                                       vision_start_id=a.vocab_size - 8, vision_end_id=a.vocab_size - 7)
+    return c
