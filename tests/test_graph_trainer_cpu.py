@@ -1,0 +1,195 @@
+"""Graph trainer on CPU/gloo: SimpleFSDP gradients against an unsharded model, every graph
+pass exact against the eager step, and the GraphTrainer loop against its eager mode."""
+import copy
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(fn, world, *args):
+    mp.spawn(_entry, args=(world, _port(), fn, args), nprocs=world, join=True)
+
+
+def _entry(rank, world, port, fn, args):
+    os.environ.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        fn(rank, world, *args)
+    finally:
+        dist.destroy_process_group()
+
+
+def _model(vocab=131):
+    from torchtitan_b200.models.llama3 import Llama3ModelArgs
+
+    torch.manual_seed(0)
+    m = Llama3ModelArgs(dim=64, n_layers=2, n_heads=4, n_kv_heads=2, vocab_size=vocab, max_seq_len=64).build()
+    m.init_weights()
+    return m
+
+
+def _loss_fn(pred, labels):
+    from torchtitan_b200 import ops
+
+    return ops.cross_entropy_sum(pred.flatten(0, 1).float(), labels.flatten())
+
+
+def _shard(t, rank, world):
+    per = -(-t.shape[0] // world)
+    return t[rank * per:(rank + 1) * per]
+
+
+def _batch(world):
+    g = torch.Generator().manual_seed(1)
+    tok = torch.randint(0, 131, (2 * world, 32), generator=g)
+    lab = torch.randint(0, 131, (2 * world, 32), generator=g)
+    return tok, lab
+
+
+def _sfsdp_vs_unsharded(rank, world, mode):
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from torchtitan_b200.graph.simple_fsdp import data_parallel, disable_active_parametrization
+
+    ref = _model()
+    m = copy.deepcopy(ref)
+    if mode == "hybrid_shard":
+        mesh = init_device_mesh("cpu", (2, world // 2), mesh_dim_names=("dp_replicate", "fsdp"))
+        shard_rank, shard_world = mesh.get_local_rank(1), world // 2
+    else:
+        mesh = init_device_mesh("cpu", (world,))
+        shard_rank, shard_world = (rank, world) if mode == "fully_shard" else (0, 1)
+    data_parallel(m, mesh, mode)
+    with disable_active_parametrization():
+        assert type(m.tok_embeddings.weight).__name__ == "DTensor"
+    tok, lab = _batch(world)
+    norm = float(lab.numel())
+    loss = _loss_fn(m(tok[2 * rank:2 * rank + 2]), lab[2 * rank:2 * rank + 2]) / norm
+    loss.backward()
+    (_loss_fn(ref(tok), lab) / norm).backward()
+    for (n, p), q in zip(m.named_parameters(), ref.parameters()):
+        want = _shard(q.grad, shard_rank, shard_world)
+        torch.testing.assert_close(p.grad.to_local(), want, rtol=1e-5, atol=1e-6, msg=n)
+
+
+@pytest.mark.parametrize("mode,world", [("fully_shard", 2), ("fully_shard", 3), ("replicate", 2),
+                                        ("hybrid_shard", 4)])
+def test_simple_fsdp_matches_unsharded(mode, world):
+    _run(_sfsdp_vs_unsharded, world, mode)
+
+
+def _passes_exact(rank, world, pass_sets):
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from torchtitan_b200.graph import passes as P
+    from torchtitan_b200.graph.simple_fsdp import data_parallel
+    from torchtitan_b200.graph.tracer import GraphStepRunner, trace_train_step
+
+    m = _model()
+    data_parallel(m, init_device_mesh("cpu", (world,)), "fully_shard")
+    tok, lab = _batch(world)
+    tok, lab = tok[2 * rank:2 * rank + 2], lab[2 * rank:2 * rank + 2]
+    norm = torch.tensor(float(lab.numel() * world))
+    eager_loss = _loss_fn(m(tok), lab) / norm
+    eager_loss.backward()
+    want = [p.grad.to_local().clone() for p in m.parameters()]
+    n_params = len(want)
+    for names in pass_sets:
+        m.zero_grad()
+        tr = trace_train_step(m, _loss_fn, tok, lab, norm)
+        ag0 = sum(1 for n in tr.gm.graph.nodes if n.target == P.AG)
+        assert ag0 == n_params  # one gather per parameter as traced
+        P.apply_passes(tr, P.DEFAULT_PASSES + names)
+        nodes = list(tr.gm.graph.nodes)
+        ags = [n for n in nodes if n.target == P.AG]
+        rss = [n for n in nodes if n.target == P.RS]
+        if "transformer_block_bucketing" in names:
+            # one bucket per block and per top-level module (x2 when backward re-gathers)
+            n_buckets = 2 + 2 + 1  # tok_embeddings, layers.0, layers.1, norm, output
+            assert len(rss) == n_buckets
+            # backward re-gathers every bucket but the embedding (its backward needs no weight)
+            assert len(ags) == (n_buckets + 4 if "reshard_after_forward" in names else n_buckets)
+            # reductions are waited on only at the end of the graph
+            waits = [i for i, n in enumerate(nodes) if n.target == P.WAIT and n.args[0] in rss]
+            assert min(waits) > max(i for i, n in enumerate(nodes) if n.target == P.RS)
+        elif "reshard_after_forward" in names:
+            assert len(ags) > n_params
+        loss = GraphStepRunner(m, tr)(tok, lab, norm)
+        torch.testing.assert_close(loss, eager_loss.detach(), rtol=1e-6, atol=1e-6)
+        for p, w in zip(m.parameters(), want):
+            torch.testing.assert_close(p.grad.to_local(), w, rtol=1e-5, atol=1e-6)
+
+
+def test_graph_passes_exact():
+    _run(_passes_exact, 2, [[], ["reshard_after_forward"], ["transformer_block_bucketing"],
+                            ["reshard_after_forward", "transformer_block_bucketing"],
+                            ["selective_recompute", "auto_bucketing"]])
+
+
+def test_selective_recompute_moves_cheap_ops_to_backward():
+    """Single process: recompute re-creates elementwise forward ops in the backward and
+    the traced step still matches eager autograd."""
+    from torchtitan_b200.graph import passes as P
+    from torchtitan_b200.graph.tracer import GraphStepRunner, backward_nodes, trace_train_step
+
+    m = _model()
+    tok, lab = _batch(1)
+    norm = torch.tensor(float(lab.numel()))
+    (_loss_fn(m(tok), lab) / norm).backward()
+    want = [p.grad.clone() for p in m.parameters()]
+    m.zero_grad()
+    tr = trace_train_step(m, _loss_fn, tok, lab, norm)
+    P.apply_passes(tr, P.DEFAULT_PASSES)
+    n_before = len(tr.gm.graph.nodes)
+    copied = P.selective_recompute(tr)
+    assert copied > 0 and len(tr.gm.graph.nodes) > n_before
+    bwd = backward_nodes(tr.gm, tr.loss_node)
+    # no GEMM is recomputed: every mm in the backward is a backward GEMM (dgrad / wgrad)
+    n_mm_fwd = sum(1 for n in tr.gm.graph.nodes if n.target == torch.ops.aten.mm.default and n not in bwd)
+    n_mm_bwd = sum(1 for n in tr.gm.graph.nodes if n.target == torch.ops.aten.mm.default and n in bwd)
+    assert n_mm_bwd <= 2 * n_mm_fwd
+    GraphStepRunner(m, tr)(tok, lab, norm)
+    for p, w in zip(m.parameters(), want):
+        torch.testing.assert_close(p.grad, w, rtol=1e-5, atol=1e-6)
+
+
+def _trainer_modes(rank, world, out):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.graph.trainer import GraphTrainer
+
+    losses = {}
+    for mode in ("eager", "aot_fx_trace"):
+        cfg = ConfigManager().parse_args(["--module", "graph", "--config", "graph_trainer_llama3_debugmodel_cpu",
+                                          "--training.steps", "3", "--training.seq_len", "64",
+                                          "--training.local_batch_size", "2", "--checkpoint.no-enable",
+                                          "--validator.no-enable", "--compile.mode", mode,
+                                          "--debug.seed", "7", "--dump-folder", out])
+        assert isinstance(cfg, GraphTrainer.Config)
+        t = GraphTrainer(cfg)
+        it = t.batch_generator(t.dataloader)
+        vals = []
+        while t.step < 3:
+            t.step += 1
+            vals.append(float(t.train_step(it)))
+        losses[mode] = vals
+        t.close()
+    torch.testing.assert_close(torch.tensor(losses["aot_fx_trace"]), torch.tensor(losses["eager"]),
+                               rtol=1e-5, atol=1e-6)
+
+
+def test_graph_trainer_matches_eager_mode(tmp_path):
+    _run(_trainer_modes, 2, str(tmp_path))

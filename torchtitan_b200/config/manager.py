@@ -47,6 +47,8 @@ def split_module_and_config(args: list[str]) -> tuple[str | None, str | None, li
 
 def import_config_registry(module: str):
     candidates = []
+    if module in ("graph", "graph_trainer"):  # the graph trainer's registry
+        candidates.append("torchtitan_b200.graph.config_registry")
     if module in _SHORT_MODULES or "." not in module:
         candidates.append(f"torchtitan_b200.models.{module}.config_registry")
     candidates += [f"{module}.config_registry", module]

@@ -10,10 +10,13 @@ import importlib
 
 _mod = None
 _err: Exception | None = None
+_trace_ns = None  # set by ``graph.traceable.traceable_kernels()`` while a step is being traced
 
 
 def ext():
     global _mod, _err
+    if _trace_ns is not None:
+        return _trace_ns
     if _mod is None and _err is None:
         try:
             _mod = importlib.import_module("torchtitan_b200._C")
