@@ -1,0 +1,92 @@
+"""AutoParallel planner: constraints, memory feasibility, and a trainer run with the chosen layout."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from torchtitan_b200.parallel.auto_parallel import Hardware, estimate, model_shape, plan_parallelism
+
+
+def _shape(flavor, seq=8192):
+    from torchtitan_b200.models.llama3 import llama3_args
+
+    a = llama3_args[flavor]
+    with torch.device("meta"):
+        m = a.build()
+    return model_shape(m, a, seq)
+
+
+def test_plans_respect_constraints():
+    sh = _shape("8B")
+    plans = plan_parallelism(sh, 8, 8, 8192)
+    assert plans
+    for p in plans:
+        assert p.dp_replicate * p.dp_shard * p.cp * p.tp == 8
+        assert sh.n_heads % p.tp == 0 and sh.n_kv_heads % p.tp == 0
+        assert 8192 % (2 * p.cp * p.tp) == 0
+        assert p.memory_bytes <= Hardware().hbm_bytes * Hardware().memory_fraction
+    assert plans == sorted(plans, key=lambda p: p.step_s)
+
+
+def test_small_model_prefers_pure_data_parallel():
+    best = plan_parallelism(_shape("8B"), 8, 8, 8192)[0]
+    assert best.tp == 1 and best.cp == 1 and best.dp_replicate * best.dp_shard == 8
+
+
+def test_memory_forces_model_parallelism_or_accumulation():
+    sh = _shape("70B")
+    best = plan_parallelism(sh, 8, 8, 8192)[0]
+    # replicated 70B parameters + Adam states cannot fit one GPU: something must shard them
+    assert best.dp_shard * best.cp * best.tp == 8
+    # a smaller HBM makes every 8-GPU layout infeasible
+    with pytest.raises(ValueError, match="no parallel layout"):
+        plan_parallelism(sh, 8, 8, 8192, hw=Hardware(hbm_bytes=40e9))
+
+
+def test_estimate_monotone_in_recompute():
+    sh = _shape("8B")
+    from torchtitan_b200.parallel.auto_parallel import Plan
+
+    hw = Hardware()
+    base = dict(dp_replicate=1, dp_shard=8, cp=1, tp=1, sequence_parallel=False, async_tp=False,
+                reshard_after_forward=True)
+    t = {m: estimate(sh, hw, Plan(**base, ac_mode=m), 8, 8192) for m in ("none", "selective", "full")}
+    assert t["none"].step_s < t["selective"].step_s < t["full"].step_s
+    assert t["none"].memory_bytes > t["selective"].memory_bytes > t["full"].memory_bytes
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _entry(rank, world, port, out):
+    os.environ.update(RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE=str(world), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    torch.set_num_threads(1)
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.trainer import Trainer
+
+    cfg = ConfigManager().parse_args(["--module", "llama3", "--config", "llama3_debugmodel_cpu",
+                                      "--training.steps", "2", "--training.seq_len", "128",
+                                      "--training.local_batch_size", "2", "--checkpoint.no-enable",
+                                      "--validator.no-enable", "--parallelism.auto-parallel", "--dump-folder", out])
+    t = Trainer(cfg)
+    pd = t.parallel_dims
+    assert pd.dp_replicate * pd.dp_shard * pd.cp * pd.tp == world
+    assert cfg.training.global_batch_size == 2 * world
+    t.train()
+    loss = t.metrics_processor.last_metrics["loss_metrics/global_avg_loss"]
+    assert 5.0 < loss < 9.0
+    t.close()
+    dist.destroy_process_group()
+
+
+def test_trainer_runs_auto_parallel_plan(tmp_path):
+    mp.spawn(_entry, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)

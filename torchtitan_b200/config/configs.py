@@ -58,6 +58,9 @@ class ParallelismConfig:
     expert_tensor_parallel_degree: int = 1
     expert_parallel_comm_backend: Literal["standard", "fused"] = "standard"
     """``standard`` = NCCL all-to-all; ``fused`` = peer-memory dispatch/combine kernels."""
+    auto_parallel: bool = False
+    """Choose the layout (dp_replicate/dp_shard/cp/tp, SP, async TP, reshard, AC mode, gradient
+    accumulation) with the cost model of ``parallel/auto_parallel.py``, overriding those fields."""
     data_parallel_comm: Literal["auto", "fsdp2", "peer"] = "auto"
     """Pure data parallelism: ``peer`` = replicated bf16 weights + sharded optimizer with
     reduce-scatter / all-gather kernels over NVLink peer memory; ``fsdp2`` = FSDP2 over

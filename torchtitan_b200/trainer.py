@@ -108,6 +108,11 @@ class Trainer(Stateful, Configurable):
             dist_utils.apply_batch_invariant_env()
         world = dist_utils.init_distributed(c.comm, enable_cpu_backend=c.training.enable_cpu_offload,
                                             base_folder=c.dump_folder)
+        if c.parallelism.auto_parallel:
+            from torchtitan_b200.parallel.auto_parallel import auto_parallelize_config
+
+            plan = auto_parallelize_config(c, world)
+            logger.info(f"auto parallel: {plan.describe()}")
         self.parallel_dims = pd = ParallelDims.from_config(c.parallelism, world)
         ft = c.fault_tolerance
         pd.semi_sync_replicas = bool(ft.enable and ft.semi_sync_method)
