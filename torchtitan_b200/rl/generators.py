@@ -156,7 +156,10 @@ class VLLMGenerator:
     def __init__(self, family: str, model_args: Any, adapter: Any, state: dict[str, torch.Tensor], workdir: str,
                  tokenizer_path: str | None = None, gpu_memory_utilization: float = 0.3, seed: int = 0,
                  enforce_eager: bool = True):
-        os.environ.setdefault("VLLM_ALLOW_INSECURE_SERIALIZATION", "1")  # apply_model ships a closure
+        # the engine runs in this process (the generator is already its own actor process), so
+        # weight pushes through apply_model need no serialisation and no forked CUDA context
+        os.environ.setdefault("VLLM_ENABLE_V1_MULTIPROCESSING", "0")
+        os.environ.setdefault("VLLM_ALLOW_INSECURE_SERIALIZATION", "1")
         from vllm import LLM
 
         self.adapter = adapter
