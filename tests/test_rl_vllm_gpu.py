@@ -10,7 +10,9 @@ def _ours(margs, state):
     with torch.device("cuda"):
         m = margs.build()
     m.load_state_dict(state, strict=False)
-    return m.to(torch.bfloat16).eval()
+    for p in m.parameters():  # bf16 weights; the RoPE tables (buffers) stay fp32
+        p.data = p.data.to(torch.bfloat16)
+    return m.eval()
 
 
 def _logprobs(model, eps):
