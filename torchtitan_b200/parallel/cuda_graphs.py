@@ -12,7 +12,9 @@ Requirements, checked before capture:
   parallel runtime, or replicated DDP-style weights; not FSDP2 (it re-materialises
   parameters every step), and no tensor/context/pipeline/expert parallelism
   (their collectives and host-side routing are outside the graph);
-* dense blocks (MoE routing reads expert counts on the host);
+* MoE blocks only with the fused routing kernel and without forced load balancing: then
+  routing, the padded expert layout and the grouped GEMMs run without a device-to-host
+  read (the PyTorch routing fallback sizes ``bincount`` on the host);
 * fixed shapes: the graphs are captured for ``[local_batch_size, seq_len, dim]``;
   the RoPE tables are read from the model's buffers at fixed addresses.
 Gradients leave the graphed backward through the normal AccumulateGrad nodes, so
@@ -70,8 +72,12 @@ def cuda_graphs_applicable(parallel_dims: Any, model: nn.Module) -> str | None:
     if not hasattr(model, "layers") or not hasattr(model, "rope"):
         return "only decoder models with model.layers and RoPE tables are captured"
     for blk in model.layers.values():
-        if getattr(blk, "moe", None) is not None:
-            return "MoE blocks route on the host"
+        moe = getattr(blk, "moe", None)
+        if moe is not None:
+            from torchtitan_b200.models.common.moe import _router_kernel_enabled
+
+            if not _router_kernel_enabled() or getattr(moe.router, "force_load_balance", False):
+                return "MoE routing without the fused routing kernel reads expert counts on the host"
     return None
 
 
