@@ -109,3 +109,59 @@ def test_float8_linear_kernel_path_matches_fake_quant(monkeypatch, recipe):
     # rounds the dequantized operands to bf16 first; both sit ~1e-2 from each other at K = 512
     for a, b in zip(res["1"], res["0"]):
         assert float((a - b).norm() / b.norm()) < 2e-2
+
+
+@pytest.mark.parametrize("tile_n", [128, 256])
+def test_mx_gemm_grouped_rows_matches_dequantized_product(tile_n):
+    """Grouped-rows mode: every 128-row tile of A against its group's rows of the stacked B
+    (a skipped tile, an empty group and the last group included) vs the CPU dequantized product."""
+    from torchtitan_b200.ops._ext import ext
+    from torchtitan_b200.ops.mx_gemm import mx_gemm_grouped, mx_quantize
+
+    torch.manual_seed(0)
+    G, n, K = 3, 256, 384
+    P = 128 * 6
+    tg = torch.tensor([0, 0, 2, -1, 2, 1], dtype=torch.int32, device="cuda")
+    a = torch.randn(P, K, device="cuda").bfloat16()
+    b = torch.randn(G * n, K, device="cuda").bfloat16()
+    qa, sa = mx_quantize(a)
+    qb, sb = mx_quantize(b)
+    got = ext().gemm_mxfp8_grouped(qa, sa, qb, sb, tg, n, tile_n).float().cpu()
+    want = mx_gemm_grouped(qa.cpu(), sa.cpu(), qb.cpu(), sb.cpu(), tg.cpu(), n).float()
+    keep = (tg.cpu() >= 0).repeat_interleave(128)
+    err = (got[keep] - want[keep]).norm() / want[keep].norm()
+    assert err < 1e-2, err
+
+
+def test_mxfp8_grouped_experts_kernel_path():
+    """MXFP8 routed SwiGLU on the grouped block-scaled kernel: forward against the same
+    quantized operands on the bf16 grouped GEMM; input and weight gradients against fp32."""
+    from torchtitan_b200 import ops
+    from torchtitan_b200.ops.grouped import mx_grouped_swiglu_cuda
+    from torchtitan_b200.ops.quant import mx_fake_quant
+
+    torch.manual_seed(0)
+    E, D, H = 4, 256, 512
+    counts = torch.tensor([300, 0, 517, 183], device="cuda")
+    n = int(counts.sum())
+    x = (torch.randn(n, D, device="cuda") * 0.5).bfloat16().requires_grad_()
+    w1, w3 = ((torch.randn(E, H, D, device="cuda") * 0.05).bfloat16().requires_grad_() for _ in range(2))
+    w2 = (torch.randn(E, D, H, device="cuda") * 0.05).bfloat16().requires_grad_()
+    y = mx_grouped_swiglu_cuda(x, w1, w2, w3, counts)
+    with torch.no_grad():
+        want = ops.grouped_swiglu(mx_fake_quant(x, -1), mx_fake_quant(w1, -1), mx_fake_quant(w2, -1),
+                                  mx_fake_quant(w3, -1), counts)
+    assert (y.float() - want.float()).norm() / want.float().norm() < 3e-2
+    g = torch.randn_like(y)
+    y.backward(g)
+    # fp32 reference of the unquantized experts
+    xs, ws = x.detach().float().requires_grad_(), [w.detach().float().requires_grad_() for w in (w1, w2, w3)]
+    outs, o = [], 0
+    for e, c in enumerate(counts.tolist()):
+        h = torch.nn.functional.silu(xs[o:o + c] @ ws[0][e].t()) * (xs[o:o + c] @ ws[2][e].t())
+        outs.append(h @ ws[1][e].t())
+        o += c
+    torch.cat(outs).backward(g.float())
+    for got, ref in ((x.grad, xs.grad), (w1.grad, ws[0].grad), (w2.grad, ws[1].grad), (w3.grad, ws[2].grad)):
+        err = (got.float() - ref).norm() / ref.norm()
+        assert err < 0.1, err

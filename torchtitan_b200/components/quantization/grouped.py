@@ -1,14 +1,17 @@
 """Quantized routed experts (parity: reference ``quantization/float8.py``
 ``Float8GroupedMMConverter`` and the MX grouped-mm path of ``quantization/mx.py``).
 
-The expert weights and the routed tokens are quantized to the recipe's codes
-(MXFP8 1x32 blocks along the contraction dim, or Float8 rowwise) before the
-grouped SwiGLU; gradients pass straight through the quantizers, so the
-backward GEMMs run on the quantized forward operands and high-precision
-output gradients (the "weight gradient in high precision" variant).
+MXFP8 on CUDA (expert dims multiples of 128): the forward and data-gradient GEMMs run at FP8
+rate on the block-scaled tcgen05 kernel in grouped-rows mode (``ops.grouped._MXGroupedSwiGLU``),
+weight gradients in bf16.  Otherwise (CPU, Float8 rowwise, other dims) the expert weights and
+routed tokens are quantized to the recipe's codes and dequantized before the bf16 grouped
+SwiGLU; gradients pass straight through the quantizers, so the backward GEMMs run on the
+quantized forward operands and high-precision output gradients (the "weight gradient in high
+precision" variant).
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -47,6 +50,12 @@ class QuantGroupedExperts(GroupedExperts):
         w1, w2, w3 = self.weights()
         if x.shape[-1] % 32 or w2.shape[-1] % 32:
             return super().forward(x, counts)
+        if (self.recipe == "mxfp8" and x.is_cuda and os.environ.get("TTB_MXFP8_KERNEL", "1") != "0"
+                and x.shape[-1] % 128 == 0 and w2.shape[-1] % 128 == 0):
+            from torchtitan_b200.ops.grouped import mx_grouped_swiglu_cuda
+
+            # FP8-rate grouped GEMMs (block-scaled tcgen05 kernel, grouped-rows mode)
+            return mx_grouped_swiglu_cuda(x, w1, w2, w3, counts)
         # w1/w3 [E, H, D] contract over D (last); w2 [E, D, H] contracts over H (last)
         return ops.grouped_swiglu(_q(x, self.recipe, -1), _q(w1, self.recipe, -1), _q(w2, self.recipe, -1),
                                   _q(w3, self.recipe, -1), counts)

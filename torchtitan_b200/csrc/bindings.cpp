@@ -423,6 +423,30 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                     static_cast<int>(tile_n));
     return d;
   }, py::arg("a"), py::arg("sfa"), py::arg("b"), py::arg("sfb"), py::arg("tile_n") = 0);
+  m.def("gemm_mxfp8_grouped", [](Tensor a, Tensor sfa, Tensor b, Tensor sfb, Tensor tile_group, int64_t n,
+                                 int64_t tile_n) {
+    // a [P, K] rows padded per group to 128; b [G*n, K] stacked groups; tile_group [P/128] int32
+    TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kByte && b.scalar_type() == at::kByte,
+                "gemm_mxfp8_grouped: uint8 FP8 codes on CUDA");
+    TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1) && a.is_contiguous() && b.is_contiguous(),
+                "gemm_mxfp8_grouped: A [P, K], B [G*N, K] contiguous");
+    const int64_t M = a.size(0), K = a.size(1);
+    TORCH_CHECK(n > 0 && n % 128 == 0 && b.size(0) % n == 0, "gemm_mxfp8_grouped: N per group a multiple of 128");
+    TORCH_CHECK(M % 128 == 0, "gemm_mxfp8_grouped: rows padded to 128");
+    TORCH_CHECK(tile_group.is_cuda() && tile_group.scalar_type() == at::kInt && tile_group.is_contiguous() &&
+                    tile_group.numel() == M / 128, "gemm_mxfp8_grouped: tile_group int32 [P/128]");
+    const int64_t G = b.size(0) / n;
+    TORCH_CHECK(sfa.numel() >= M * K / 32 && sfb.numel() >= G * n * K / 32, "gemm_mxfp8_grouped: scale records too small");
+    c10::cuda::CUDAGuard g(a.device());
+    auto d = torch::empty({M, n}, a.options().dtype(at::kBFloat16));
+    ttb::MxEpilogue ep;
+    ep.tile_group = tile_group.data_ptr<int>();
+    ep.num_groups = static_cast<int>(G);
+    ttb::gemm_mxfp8(a.data_ptr(), b.data_ptr(), sfa.data_ptr(), sfb.data_ptr(), d.data_ptr(), M, n, K, stream(),
+                    static_cast<int>(tile_n), ep);
+    return d;
+  }, py::arg("a"), py::arg("sfa"), py::arg("b"), py::arg("sfb"), py::arg("tile_group"), py::arg("n"),
+     py::arg("tile_n") = 0);
   m.def("f8_quantize", [](Tensor x, bool rowwise) {
     check_cuda_bf16(x, "x");
     TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "f8_quantize: [R, C] with contiguous rows");

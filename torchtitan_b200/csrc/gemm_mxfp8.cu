@@ -27,6 +27,9 @@
 //               TMEM (32x128b, broadcast to the 4 lane quadrants; B's second record four
 //               columns after the first), then 4 MMAs of K=32 selecting scale byte j
 //   warps 2..   epilogue: TMEM -> registers -> bf16 -> global
+// Grouped rows (routed experts): B is the stack of num_groups [N, K] matrices and M-tile tm
+// multiplies group tile_group[tm] (N a multiple of 128, so every group starts on a scale-record
+// block); tiles whose group is negative are skipped by all three roles alike.
 // Every wait is bounded; a timeout sets mxgemm_error_code() and the kernel
 // returns after releasing TMEM.  K must be a multiple of 128 (callers pad).
 #include <stdexcept>
@@ -75,7 +78,10 @@ struct Params {
   const float* sa;      // optional output scales: D[m, n] *= sa[m or 0] * sb[n or 0]
   const float* sb;
   int sa_rows, sb_rows;  // 1: one scale per row of A / of B; 0: one scale for the operand
+  const int* tile_group;  // grouped rows: B group of each M-tile (nullptr: group 0 everywhere)
 };
+
+__device__ __forceinline__ int tile_group_of(const Params& p, int tm) { return p.tile_group ? p.tile_group[tm] : 0; }
 
 __device__ __align__(128) uint8_t g_unit_sf[SF_BYTES];  // E8M0 127 (= 2^0) bytes, set on first use
 
@@ -148,15 +154,17 @@ __device__ __forceinline__ void run_producer(const CUtensorMap* tmA, const CUten
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     int tm, tn;
     tile_coords(t, p, tm, tn);
-    // B's scale records of this tile: 128-row blocks tn*BN/128 .. ; blocks past the padded
-    // rows are not copied (their TMEM columns only scale output columns >= N)
-    const int rb0 = tn * (BN / 128);
-    const int nrec = min(BN / 128, p.b_records - rb0);
+    const int g = tile_group_of(p, tm);
+    if (g < 0) continue;
+    // B's scale records of this tile: 128-row blocks tn*BN/128 .. of group g; blocks past the
+    // group's padded rows are not copied (their TMEM columns only scale output columns >= N)
+    const int rb0 = g * p.b_records + tn * (BN / 128);
+    const int nrec = min(BN / 128, p.b_records - tn * (BN / 128));
     for (int kb = 0; kb < p.num_k; ++kb) {
       if (!mbar_wait(&sh.empty[stage], phase ^ 1, &sh.abort_flag, &g_err, 1)) return;
       mbar_arrive_expect_tx(&sh.full[stage], C::STAGE_BYTES + (1 + nrec) * SF_BYTES);
       tma_load_2d(sA + stage * A_BYTES, tmA, &sh.full[stage], kb * BK, tm * BM);
-      tma_load_2d(sB + stage * C::B_BYTES, tmB, &sh.full[stage], kb * BK, tn * BN);
+      tma_load_2d(sB + stage * C::B_BYTES, tmB, &sh.full[stage], kb * BK, g * p.N + tn * BN);
       uint8_t* sf = sSF + stage * C::SF_STAGE;
       const size_t ua = p.sf_unit ? 0 : 1;  // unit records: always record 0 of the unit buffer
       bulk_load(sf, p.sfa + ua * (static_cast<size_t>(tm) * p.num_k + kb) * SF_BYTES, SF_BYTES, &sh.full[stage]);
@@ -186,6 +194,11 @@ __device__ __forceinline__ void run_mma(const Params& p, Shared& sh, uint8_t* sA
   int it = 0;
   const int tiles = p.num_m * p.num_n;
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    if (p.tile_group) {
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      if (tile_group_of(p, tm) < 0) continue;
+    }
     const int acc = it % C::ACC_STAGES;
     const uint32_t acc_phase = (it / C::ACC_STAGES) & 1;
     ++it;
@@ -267,6 +280,7 @@ __device__ __forceinline__ void run_epilogue(const Params& p, Shared& sh, int wa
   for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
     int tm, tn;
     tile_coords(t, p, tm, tn);
+    if (tile_group_of(p, tm) < 0) continue;
     const int row = tm * BM + q * 32 + lane;
     __nv_bfloat16* drow = p.D + static_cast<size_t>(row) * p.ldd;
     const int acc = it % C::ACC_STAGES;
@@ -359,7 +373,7 @@ void launch_mx(const void* A, const void* B, const void* sfa, const void* sfb, v
                int64_t K, cudaStream_t stream, const MxEpilogue& ep) {
   using C = Cfg<BN>;
   const CUtensorMap ta = make_tmap_u8_2d(A, M, K, K, BM, BK);
-  const CUtensorMap tb = make_tmap_u8_2d(B, N, K, K, BN, BK);
+  const CUtensorMap tb = make_tmap_u8_2d(B, N * ep.num_groups, K, K, BN, BK);
   Params p;
   p.M = (int)M;
   p.N = (int)N;
@@ -389,6 +403,7 @@ void launch_mx(const void* A, const void* B, const void* sfa, const void* sfb, v
   p.sb = ep.sb;
   p.sa_rows = ep.sa_rows;
   p.sb_rows = ep.sb_rows;
+  p.tile_group = ep.tile_group;
   static bool attr_set = false;
   if (!attr_set) {
     check_cuda(cudaFuncSetAttribute(mx_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES),
@@ -417,6 +432,8 @@ void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, 
   if ((sfa == nullptr) != (sfb == nullptr)) throw std::runtime_error("gemm_mxfp8: both or neither scale records");
   if ((reinterpret_cast<uintptr_t>(sfa) & 15) || (reinterpret_cast<uintptr_t>(sfb) & 15))
     throw std::runtime_error("gemm_mxfp8: scale records must be 16-byte aligned");
+  if (ep.tile_group != nullptr && (N % 128 || ep.num_groups < 1))
+    throw std::runtime_error("gemm_mxfp8 grouped: N per group must be a multiple of 128");
   if (tile_n == 0) tile_n = N >= 256 ? 256 : 128;  // the wide tile wherever N has 256 columns
   if (tile_n == 256) launch_mx<256>(A, B, sfa, sfb, D, M, N, K, stream, ep);
   else if (tile_n == 128) launch_mx<128>(A, B, sfa, sfb, D, M, N, K, stream, ep);

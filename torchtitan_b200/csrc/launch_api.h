@@ -92,6 +92,10 @@ struct MxEpilogue {
   const float* sa = nullptr;
   const float* sb = nullptr;
   int sa_rows = 0, sb_rows = 0;
+  // grouped rows (routed experts): M-tile tm multiplies B rows [g*N, g*N + N) with
+  // g = tile_group[tm]; g < 0 skips the tile (its output rows are left unwritten)
+  const int* tile_group = nullptr;
+  int num_groups = 1;
 };
 void gemm_mxfp8(const void* A, const void* B, const void* sfa, const void* sfb, void* D, int64_t M, int64_t N,
                 int64_t K, cudaStream_t stream, int tile_n = 0, const MxEpilogue& ep = MxEpilogue());

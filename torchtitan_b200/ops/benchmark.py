@@ -266,6 +266,12 @@ def bench_grouped_experts(ext, out):
         y = grouped_swiglu(x, w1, w2, w3, counts)
         y.backward(dy)
 
+    def ours_mxfp8():
+        from torchtitan_b200.ops.grouped import mx_grouped_swiglu_cuda
+
+        y = mx_grouped_swiglu_cuda(x, w1, w2, w3, counts)
+        y.backward(dy)
+
     def aten():
         h1 = torch._grouped_mm(x, w1.transpose(-2, -1), offs=offs)
         h3 = torch._grouped_mm(x, w3.transpose(-2, -1), offs=offs)
@@ -277,6 +283,9 @@ def bench_grouped_experts(ext, out):
     res = {"kernel": "grouped_swiglu_fwd_bwd", "E": E, "D": D, "H": H, "rows": rows}
     res["ours_ms"] = time_fn(ours)
     res["ours_tflops"] = fl / res["ours_ms"] / 1e9
+    # MXFP8: forward and data-gradient GEMMs at FP8 rate (incl. quantization), weight grads bf16
+    res["ours_mxfp8_ms"] = time_fn(ours_mxfp8)
+    res["ours_mxfp8_tflops"] = fl / res["ours_mxfp8_ms"] / 1e9
     try:
         res["aten_grouped_mm_ms"] = time_fn(aten)
         res["aten_tflops"] = fl / res["aten_grouped_mm_ms"] / 1e9

@@ -73,6 +73,61 @@ class _GroupedSwiGLU(torch.autograd.Function):
         return ext.gather_rows(dx, dest), dw1.to(w1.dtype), dw2.to(w2.dtype), dw3.to(w3.dtype), None
 
 
+class _MXGroupedSwiGLU(torch.autograd.Function):
+    """Routed SwiGLU experts at MXFP8 rate: the forward GEMMs and both data-gradient GEMMs run
+    on the block-scaled tcgen05 kernel in grouped-rows mode, every operand quantized (1x32
+    E8M0 blocks) along its GEMM's contraction dim; the weight gradients stay in bf16 on the
+    grouped-K kernel (high-precision weight gradient)."""
+
+    @staticmethod
+    def forward(ctx, x, w1, w2, w3, counts):
+        from .mx_gemm import mx_gemm_grouped, mx_quantize
+
+        ext = _ext.ext()
+        E, H, D = w1.shape
+        n = x.shape[0]
+        dest, tg, kst, kln, P = padded_layout(counts, n)
+        src_of = torch.full((P,), -1, dtype=torch.int64, device=x.device)
+        src_of[dest] = torch.arange(n, device=x.device)
+        xp = ext.gather_rows(x, src_of)
+        qx = mx_quantize(xp)
+        h1 = mx_gemm_grouped(*qx, *mx_quantize(w1.reshape(E * H, D)), tg, H)
+        h3 = mx_gemm_grouped(*qx, *mx_quantize(w3.reshape(E * H, D)), tg, H)
+        a = ext.swiglu_fwd(h1, h3)
+        yp = mx_gemm_grouped(*mx_quantize(a), *mx_quantize(w2.reshape(E * D, H)), tg, D)
+        ctx.save_for_backward(xp, h1, h3, a, w1, w2, w3, dest, src_of, tg, kst, kln)
+        return ext.gather_rows(yp, dest)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from .mx_gemm import mx_gemm_grouped, mx_quantize
+
+        ext = _ext.ext()
+        xp, h1, h3, a, w1, w2, w3, dest, src_of, tg, kst, kln = ctx.saved_tensors
+        E, H, D = w1.shape
+        dyp = ext.gather_rows(dy.contiguous(), src_of)
+        # da = dY W2[e]: contraction over D, so W2[e]^T [H, D] is quantized along D
+        da = mx_gemm_grouped(*mx_quantize(dyp), *mx_quantize(w2.transpose(1, 2).reshape(E * H, D).contiguous()),
+                             tg, H)
+        dh1, dh3 = ext.swiglu_bwd(da, h1, h3)
+        # dX = dh1 W1[e] + dh3 W3[e]: contraction over H, W^T [D, H] quantized along H
+        dx = mx_gemm_grouped(*mx_quantize(dh1), *mx_quantize(w1.transpose(1, 2).reshape(E * D, H).contiguous()),
+                             tg, D)
+        dx.add_(mx_gemm_grouped(*mx_quantize(dh3),
+                                *mx_quantize(w3.transpose(1, 2).reshape(E * D, H).contiguous()), tg, D))
+        dw2 = ext.gemm_grouped_k(dyp, a, kst, kln)
+        dw1 = ext.gemm_grouped_k(dh1, xp, kst, kln)
+        dw3 = ext.gemm_grouped_k(dh3, xp, kst, kln)
+        return ext.gather_rows(dx, dest), dw1.to(w1.dtype), dw2.to(w2.dtype), dw3.to(w3.dtype), None
+
+
+def mx_grouped_swiglu_cuda(x, w1, w2, w3, counts):
+    """MXFP8 routed experts on CUDA; expert dims (D, H) must be multiples of 128."""
+    dt = torch.bfloat16
+    return _MXGroupedSwiGLU.apply(x.to(dt).contiguous(), w1.to(dt).contiguous(), w2.to(dt).contiguous(),
+                                  w3.to(dt).contiguous(), counts)
+
+
 def grouped_swiglu_cuda(x, w1, w2, w3, counts):
     dt = torch.bfloat16
     return _GroupedSwiGLU.apply(x.to(dt).contiguous(), w1.to(dt).contiguous(), w2.to(dt).contiguous(),

@@ -60,6 +60,23 @@ def mx_gemm(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tens
     return (mx_dequantize_ref(a, sfa) @ mx_dequantize_ref(b, sfb).t()).to(torch.bfloat16)
 
 
+def mx_gemm_grouped(a: torch.Tensor, sfa: torch.Tensor, b: torch.Tensor, sfb: torch.Tensor,
+                    tile_group: torch.Tensor, n: int) -> torch.Tensor:
+    """Grouped rows: A codes [P, Kp] (rows padded per group to 128) times group
+    ``tile_group[i]`` of the stacked B codes [G*n, Kp] for every 128-row tile ``i``
+    (negative: tile skipped, its rows undefined) -> bf16 [P, n]."""
+    if a.is_cuda:
+        from ._ext import ext
+
+        return ext().gemm_mxfp8_grouped(a, sfa, b, sfb, tile_group, n)
+    A, B = mx_dequantize_ref(a, sfa), mx_dequantize_ref(b, sfb)
+    out = torch.zeros(a.shape[0], n)
+    for i, g in enumerate(tile_group.tolist()):
+        if g >= 0:
+            out[i * 128:(i + 1) * 128] = A[i * 128:(i + 1) * 128] @ B[g * n:(g + 1) * n].t()
+    return out.to(torch.bfloat16)
+
+
 def mx_linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """``x @ w.T`` with both operands MXFP8-quantized along the contraction dim."""
     x2 = x.reshape(-1, x.shape[-1])
@@ -68,5 +85,5 @@ def mx_linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return mx_gemm(qa, sa, qb, sb).view(*x.shape[:-1], w.shape[0])
 
 
-__all__ = ["E4M3_MAX", "mx_quantize", "mx_gemm", "mx_linear", "mx_quantize_ref", "mx_dequantize_ref",
+__all__ = ["E4M3_MAX", "mx_quantize", "mx_gemm", "mx_gemm_grouped", "mx_linear", "mx_quantize_ref", "mx_dequantize_ref",
            "sf_byte_index"]
