@@ -359,7 +359,7 @@ def profile_case(ext, case: str) -> None:
     """Small fixed workloads for ncu captures of one kernel (``--only case:<name>``):
     gemm2 (bf16 4096^3), attn_fwd / attn_bwd (causal B1 S4096 H32/8 D128), kda (B1 T4096 H32
     K=V=128 forward+backward), adamw (4 x 64 Mi fp32 params, bf16 grads), rmsnorm (16384 x 4096
-    forward and backward). Each runs the op a few
+    forward and backward), grouped (routed SwiGLU experts forward+backward). Each runs the op a few
     times so ``-s`` can skip warm-up launches."""
     from torchtitan_b200 import ops
 
@@ -388,6 +388,17 @@ def profile_case(ext, case: str) -> None:
         for _ in range(2):
             o, _ = kda.chunk_kda(q, k, v, g, beta)
             o.backward(torch.randn_like(o))
+    elif case == "grouped":
+        # routed SwiGLU experts, Kimi-Linear 48B per-rank shape (32 experts, 2304 -> 1024, 65,536 rows)
+        E, D, H, rows = 32, 2304, 1024, 65536
+        w = torch.rand(E, device="cuda") + 0.5
+        counts = (w / w.sum() * rows).floor().long()
+        counts[0] += rows - int(counts.sum())
+        x = (torch.randn(rows, D, device="cuda") * 0.5).bfloat16().requires_grad_()
+        w1, w3 = ((torch.randn(E, H, D, device="cuda") * 0.02).bfloat16().requires_grad_() for _ in range(2))
+        w2 = (torch.randn(E, D, H, device="cuda") * 0.02).bfloat16().requires_grad_()
+        for _ in range(2):
+            ops.grouped_swiglu(x, w1, w2, w3, counts).backward(torch.ones(rows, D, device="cuda").bfloat16())
     elif case == "rmsnorm":
         x = torch.randn(16384, 4096, device="cuda", dtype=torch.bfloat16)
         w = torch.ones(4096, device="cuda", dtype=torch.bfloat16)
