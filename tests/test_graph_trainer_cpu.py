@@ -193,3 +193,32 @@ def _trainer_modes(rank, world, out):
 
 def test_graph_trainer_matches_eager_mode(tmp_path):
     _run(_trainer_modes, 2, str(tmp_path))
+
+
+def _precompile(rank, world, out):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.graph.trainer import GraphTrainer
+
+    runs = []
+    for _ in range(2):
+        cfg = ConfigManager().parse_args(["--module", "graph", "--config", "graph_trainer_llama3_debugmodel_cpu",
+                                          "--training.steps", "2", "--training.seq_len", "64",
+                                          "--training.local_batch_size", "2", "--checkpoint.no-enable",
+                                          "--validator.no-enable", "--debug.seed", "3", "--dump-folder", out,
+                                          "--compile.precompile-artifact-dir", os.path.join(out, "artifacts")])
+        t = GraphTrainer(cfg)
+        it = t.batch_generator(t.dataloader)
+        losses = []
+        while t.step < 2:
+            t.step += 1
+            losses.append(float(t.train_step(it)))
+        runs.append((losses, getattr(t, "loaded_artifacts", 0)))
+        t.close()
+    assert runs[0][1] == 0 and runs[1][1] == 1  # the second run loads the first run's graph
+    assert os.path.exists(os.path.join(out, "artifacts")) and \
+        sum(f.endswith(f"rank{rank}.pt") for f in os.listdir(os.path.join(out, "artifacts"))) == 1
+    assert runs[0][0] == runs[1][0]
+
+
+def test_graph_trainer_precompiled_artifacts(tmp_path):
+    _run(_precompile, 2, str(tmp_path))

@@ -45,6 +45,10 @@ class GraphCompileConfig(CompileConfig):
     """False: run the traced graph as traced (no cleanups, no passes)."""
     bucket_bytes: int = 64 << 20
     """Bucket size of ``auto_bucketing``."""
+    precompile_artifact_dir: str = ""
+    """Directory of traced-and-passed step graphs: a run stores one per rank and input shape
+    (keyed by model, shapes, passes, layout and torch version) and later runs load it instead of
+    tracing.  Per rank, because uneven parameter shards bake rank-specific sizes into the graph."""
 
 
 def parallelize_simple_fsdp(model: nn.Module, *, parallel_dims: Any, training: Any, parallelism: Any,
@@ -102,17 +106,48 @@ class GraphTrainer(Trainer):
         if unknown:
             raise ValueError(f"unknown graph passes {unknown}; available: {sorted(graph_passes.PASSES)} + cudagraph")
 
+    def _artifact_path(self, key: tuple) -> str:
+        import hashlib
+        import os
+
+        import torch.distributed as dist
+
+        c = self.config
+        ident = repr((c.model_spec.name, c.model_spec.flavor, repr(self.model_args), key, self._passes,
+                      c.compile.enable_passes, c.compile.bucket_bytes, c.training.mixed_precision_param,
+                      c.training.mixed_precision_reduce, c.training.dtype, dist.get_world_size() if
+                      dist.is_initialized() else 1, self.device.type, torch.__version__))
+        h = hashlib.sha256(ident.encode()).hexdigest()[:16]
+        rank = dist.get_rank() if dist.is_initialized() else 0
+        return os.path.join(c.compile.precompile_artifact_dir, f"step-{h}-rank{rank}.pt")
+
+    def _trace(self, key: tuple, inputs, labels, norm):
+        import os
+
+        cc = self.config.compile
+        path = self._artifact_path(key) if cc.precompile_artifact_dir else None
+        if path and os.path.exists(path):
+            traced = torch.load(path, weights_only=False)
+            self.loaded_artifacts = getattr(self, "loaded_artifacts", 0) + 1
+            logger.info(f"graph trainer: loaded the traced step from {path}")
+            return traced, len(traced.gm.graph.nodes)
+        traced = trace_train_step(self.model_parts[0], self._loss, inputs, labels, norm)
+        n0 = len(traced.gm.graph.nodes)
+        if cc.enable_passes:
+            graph_passes.apply_passes(traced, graph_passes.DEFAULT_PASSES + self._passes, bucket_bytes=cc.bucket_bytes)
+        if path:
+            os.makedirs(os.path.dirname(path), exist_ok=True)
+            tmp = path + ".tmp"
+            torch.save(traced, tmp)
+            os.replace(tmp, path)
+        return traced, n0
+
     def _runner(self, inputs: torch.Tensor, labels: torch.Tensor, norm: torch.Tensor) -> GraphStepRunner:
         key = (tuple(inputs.shape), inputs.dtype, tuple(labels.shape))
         run = self._steps.get(key)
         if run is None:
             model = self.model_parts[0]
-            traced = trace_train_step(model, self._loss, inputs, labels, norm)
-            n0 = len(traced.gm.graph.nodes)
-            cc = self.config.compile
-            if cc.enable_passes:
-                graph_passes.apply_passes(traced, graph_passes.DEFAULT_PASSES + self._passes,
-                                          bucket_bytes=cc.bucket_bytes)
+            traced, n0 = self._trace(key, inputs, labels, norm)
             executor = None
             if self._cudagraph:
                 from .cudagraph import CUDAGraphExecutor
