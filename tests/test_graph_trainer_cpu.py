@@ -222,3 +222,40 @@ def _precompile(rank, world, out):
 
 def test_graph_trainer_precompiled_artifacts(tmp_path):
     _run(_precompile, 2, str(tmp_path))
+
+
+def _fp8_gather(rank, world):
+    import torch.nn as nn
+    from torch.distributed.device_mesh import init_device_mesh
+
+    from torchtitan_b200.graph.simple_fsdp import MixedPrecisionPolicy, _fp8_rows, data_parallel
+
+    class Lin(nn.Linear):
+        pass
+
+    torch.manual_seed(0)
+    ref = nn.Sequential(Lin(16, 37, bias=True), nn.Tanh(), nn.Linear(37, 5))
+    m = copy.deepcopy(ref)
+    data_parallel(m, init_device_mesh("cpu", (world,)), "fully_shard",
+                  MixedPrecisionPolicy(fp8_all_gather_modules=(Lin,)))
+    w = m[0].weight  # gathered through FP8 codes with per-row scales
+    codes, inv = _fp8_rows(ref[0].weight.detach())
+    want = codes.view(torch.float8_e4m3fn).float() * inv[:, None]
+    assert torch.equal(w.detach(), want)
+    assert not torch.equal(w.detach(), ref[0].weight.detach())  # it is really quantized
+    torch.testing.assert_close(m[2].weight.detach(), ref[2].weight.detach())  # other modules: exact
+    torch.testing.assert_close(m[0].bias.detach(), ref[0].bias.detach())     # 1-D: exact
+    # gradients pass straight through the quantizer and are reduce-scattered as usual
+    x = torch.randn(4, 16, generator=torch.Generator().manual_seed(rank))
+    m(x).sum().backward()
+    xs = torch.cat([torch.randn(4, 16, generator=torch.Generator().manual_seed(r)) for r in range(world)])
+    q = copy.deepcopy(ref)
+    with torch.no_grad():
+        q[0].weight.copy_(want)
+    q(xs).sum().backward()
+    torch.testing.assert_close(m[0]._parameters["weight"].grad.to_local(),
+                               _shard(q[0].weight.grad, rank, world), rtol=1e-5, atol=1e-6)
+
+
+def test_simple_fsdp_fp8_all_gather():
+    _run(_fp8_gather, 2)

@@ -58,6 +58,18 @@ class MixedPrecisionPolicy:
     """dtype of the gathered compute weight (None: the stored dtype)."""
     reduce_dtype: torch.dtype | None = None
     """dtype the gradient is reduced in (None: the compute dtype)."""
+    fp8_all_gather_modules: tuple[type, ...] = ()
+    """Parameters (2-D and up) of modules of these types are all-gathered as FP8 E4M3 codes with
+    one fp32 scale per row (448 / row amax), half the bytes of bf16, and dequantized to
+    ``param_dtype`` after the gather.  Rows never straddle ranks, so no cross-rank amax is needed."""
+
+
+def _fp8_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Rowwise E4M3 codes (as uint8) and inverse scales of a [rows, ...] tensor."""
+    xf = x.float().reshape(x.shape[0], -1)
+    scale = 448.0 / xf.abs().amax(1).clamp_min(1e-12)
+    codes = (xf * scale[:, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+    return codes, (1.0 / scale)
 
 
 class _GatherParam(torch.autograd.Function):
@@ -69,6 +81,16 @@ class _GatherParam(torch.autograd.Function):
         x = local if spec.param_dtype is None else local.to(spec.param_dtype)
         if spec.shard_group is None:
             return x.clone() if x is local else x
+        if spec.fp8 and x.dim() >= 2:
+            codes, inv = _fp8_rows(local)
+            pad = spec.shard_rows - codes.shape[0]
+            if pad:
+                codes = torch.nn.functional.pad(codes, (0, 0, 0, pad))
+                inv = torch.nn.functional.pad(inv, (0, pad))
+            codes = funcol.all_gather_tensor(codes.contiguous(), 0, spec.shard_group)[: spec.full_rows]
+            inv = funcol.all_gather_tensor(inv.contiguous(), 0, spec.shard_group)[: spec.full_rows]
+            full = codes.view(torch.float8_e4m3fn).float() * inv[:, None]
+            return full.to(x.dtype).reshape((spec.full_rows,) + tuple(x.shape[1:]))
         pad = spec.shard_rows - x.shape[0]
         if pad:
             x = torch.nn.functional.pad(x, (0, 0) * (x.dim() - 1) + (0, pad))
@@ -101,6 +123,7 @@ class _DPSpec:
     full_rows: int
     param_dtype: torch.dtype | None
     reduce_dtype: torch.dtype | None
+    fp8: bool = False
 
 
 def _gather(stored: torch.Tensor, spec: _DPSpec) -> torch.Tensor:
@@ -178,8 +201,9 @@ def data_parallel(model: nn.Module, device_mesh, mode: str = "fully_shard",
             else:
                 dt = distribute_tensor(p.data, device_mesh, placements)
             mod.register_parameter(name, nn.Parameter(dt, requires_grad=p.requires_grad))
+            fp8 = bool(mp.fp8_all_gather_modules) and isinstance(mod, mp.fp8_all_gather_modules) and p.dim() >= 2
             specs[name] = _DPSpec(shard_group, rep_group, shard_size, -(-rows // shard_size), rows,
-                                  mp.param_dtype, mp.reduce_dtype)
+                                  mp.param_dtype, mp.reduce_dtype, fp8)
             names.append(name)
         if names:
             mod._simple_fsdp_specs = specs

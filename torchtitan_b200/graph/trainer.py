@@ -52,7 +52,7 @@ class GraphCompileConfig(CompileConfig):
 
 
 def parallelize_simple_fsdp(model: nn.Module, *, parallel_dims: Any, training: Any, parallelism: Any,
-                            ac_config: Any = None, **_: Any) -> nn.Module:
+                            ac_config: Any = None, model_converters: Any = None, **_: Any) -> nn.Module:
     """SimpleFSDP on the data-parallel mesh (parity: ``graph_trainer/llama3/parallelize.py``)."""
     pd = parallel_dims
     if pd.tp_enabled or pd.cp_enabled or pd.pp_enabled or pd.ep_enabled:
@@ -60,8 +60,16 @@ def parallelize_simple_fsdp(model: nn.Module, *, parallel_dims: Any, training: A
                                   "(tensor/context/pipeline/expert parallelism use the eager Trainer)")
     if ac_config is not None and ac_config.mode != "none":
         raise ValueError("graph trainer: use the selective_recompute pass instead of activation_checkpoint.mode")
+    fp8_types: tuple = ()
+    conv = model_converters if model_converters is not None else None
+    for c in getattr(conv, "converters", None) or []:
+        if getattr(c, "enable_fsdp_float8_all_gather", False) and c.enable_fsdp_float8_all_gather:
+            from torchtitan_b200.components.quantization.float8 import Float8Linear
+
+            fp8_types = (Float8Linear,)  # the Float8 converter's linears gather FP8 codes
     mp = MixedPrecisionPolicy(param_dtype=TORCH_DTYPE_MAP[training.mixed_precision_param],
-                              reduce_dtype=TORCH_DTYPE_MAP[training.mixed_precision_reduce])
+                              reduce_dtype=TORCH_DTYPE_MAP[training.mixed_precision_reduce],
+                              fp8_all_gather_modules=fp8_types)
     if pd.dp_replicate > 1 and pd.dp_shard > 1:
         mesh, mode = pd.get_mesh(["dp_replicate", "fsdp"]), "hybrid_shard"
     elif pd.dp_replicate > 1:
