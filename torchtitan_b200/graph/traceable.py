@@ -7,7 +7,8 @@ even try to read a data pointer), so while a step is traced :func:`traceable_ker
 functions.  Running the traced graph then calls the same kernels through those ops.
 
 Covered: every kernel of the dense decoder step (GEMM, attention forward/backward, RMSNorm,
-RoPE, SwiGLU, cross entropy).  Any other attribute falls through to the extension itself,
+RoPE, SwiGLU, cross entropy) and of the routed experts (routing selection, row gathers, grouped
+GEMMs).  Any other attribute falls through to the extension itself,
 which fails loudly under fake tensors.
 """
 from __future__ import annotations
@@ -116,6 +117,50 @@ def _(dout, q, k, v, o, lse, causal, scale, dlse=None, doc_start=None, doc_end=N
     return torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
 
+@torch.library.custom_op("tt_b200_graph::router_topk", mutates_args=())
+def router_topk(logits: torch.Tensor, bias: torch.Tensor | None, top_k: int, sigmoid: bool, n_groups: int,
+                limit_groups: int) -> tuple[torch.Tensor, torch.Tensor]:
+    idx, counts = _C().router_topk(logits, bias, top_k, sigmoid, n_groups, limit_groups)
+    return idx, counts
+
+
+@router_topk.register_fake
+def _(logits, bias, top_k, sigmoid, n_groups, limit_groups):
+    return (logits.new_empty((logits.shape[0], top_k), dtype=torch.int64),
+            logits.new_empty((logits.shape[1],), dtype=torch.int32))
+
+
+@torch.library.custom_op("tt_b200_graph::gather_rows", mutates_args=())
+def gather_rows(src: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+    return _C().gather_rows(src, idx)
+
+
+@gather_rows.register_fake
+def _(src, idx):
+    return src.new_empty((idx.shape[0], src.shape[1]))
+
+
+@torch.library.custom_op("tt_b200_graph::gemm_grouped_rows", mutates_args=())
+def gemm_grouped_rows(a: torch.Tensor, b: torch.Tensor, tile_group: torch.Tensor, n_out: int, b_group_rows: int,
+                      b_mn: bool) -> torch.Tensor:
+    return _C().gemm_grouped_rows(a, b, tile_group, n_out, b_group_rows, b_mn)
+
+
+@gemm_grouped_rows.register_fake
+def _(a, b, tile_group, n_out, b_group_rows, b_mn):
+    return a.new_empty((a.shape[0], n_out))
+
+
+@torch.library.custom_op("tt_b200_graph::gemm_grouped_k", mutates_args=())
+def gemm_grouped_k(a: torch.Tensor, b: torch.Tensor, kstart: torch.Tensor, klen: torch.Tensor) -> torch.Tensor:
+    return _C().gemm_grouped_k(a, b, kstart, klen)
+
+
+@gemm_grouped_k.register_fake
+def _(a, b, kstart, klen):
+    return a.new_empty((kstart.shape[0], a.shape[1], b.shape[1]))
+
+
 class _TraceableKernels:
     """Stand-in for the extension module while tracing: the dense-step kernels as custom ops."""
 
@@ -127,6 +172,13 @@ class _TraceableKernels:
     ce_fwd = staticmethod(lambda lg, lb, ii: torch.ops.tt_b200_graph.ce_fwd(lg, lb, int(ii)))
     ce_bwd = staticmethod(lambda lg, lb, lse, g, ii: torch.ops.tt_b200_graph.ce_bwd(lg, lb, lse, g, int(ii)))
     gemm = staticmethod(lambda a, b, am, bm: torch.ops.tt_b200.gemm(a, b, bool(am), bool(bm)))
+    # routed experts (the padded expert layout needs no host read, so MoE steps trace too)
+    router_topk = staticmethod(lambda lg, bias, k, sig, g, lim: torch.ops.tt_b200_graph.router_topk(
+        lg, bias, int(k), bool(sig), int(g), int(lim)))
+    gather_rows = staticmethod(lambda src, idx: torch.ops.tt_b200_graph.gather_rows(src, idx))
+    gemm_grouped_rows = staticmethod(lambda a, b, tg, n, rows, bmn: torch.ops.tt_b200_graph.gemm_grouped_rows(
+        a, b, tg, int(n), int(rows), bool(bmn)))
+    gemm_grouped_k = staticmethod(lambda a, b, ks, kl: torch.ops.tt_b200_graph.gemm_grouped_k(a, b, ks, kl))
 
     @staticmethod
     def attn_fwd(q, k, v, causal, scale, doc_start=None, doc_end=None):
