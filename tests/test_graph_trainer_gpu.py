@@ -58,14 +58,17 @@ def test_traced_step_matches_eager(cudagraph):
         assert run.executor.graph is not None
 
 
-def test_traced_moe_step_matches_eager():
-    """Qwen3-MoE debug model: routing kernel, padded expert layout and grouped GEMMs traced as
-    custom-op nodes; the traced step equals the eager step on the same kernels."""
+@pytest.mark.parametrize("family,flavor", [("qwen3", "debugmodel_moe"), ("deepseek_v3", "debugmodel")])
+def test_traced_moe_step_matches_eager(family, flavor):
+    """MoE debug models (Qwen3-MoE; DeepSeek-V3 with MLA): routing kernel, padded expert layout
+    and grouped GEMMs traced as custom-op nodes; the traced step equals the eager step on the
+    same kernels."""
+    import importlib
+
     from torchtitan_b200.graph import passes as P
     from torchtitan_b200.graph.tracer import GraphStepRunner, trace_train_step
-    from torchtitan_b200.models.qwen3 import model_registry
 
-    spec = model_registry("debugmodel_moe")
+    spec = importlib.import_module(f"torchtitan_b200.models.{family}").model_registry(flavor)
     torch.manual_seed(0)
     with torch.device("cuda"):
         m = spec.model.build()

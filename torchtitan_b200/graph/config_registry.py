@@ -10,6 +10,7 @@ from __future__ import annotations
 import dataclasses
 
 from torchtitan_b200.config import ActivationCheckpointConfig
+from torchtitan_b200.models.deepseek_v3 import config_registry as deepseek_v3_configs
 from torchtitan_b200.models.llama3 import config_registry as llama3_configs
 from torchtitan_b200.models.qwen3 import config_registry as qwen3_configs
 
@@ -47,3 +48,17 @@ def graph_trainer_qwen3_debugmodel() -> GraphTrainer.Config:
 
 def graph_trainer_qwen3_8b() -> GraphTrainer.Config:
     return to_graph_trainer_config(qwen3_configs.qwen3_8b())
+
+
+def graph_trainer_qwen3_debugmodel_moe() -> GraphTrainer.Config:
+    """MoE on one node without expert parallelism: routing and the padded expert layout trace
+    without host reads (CUDA)."""
+    return to_graph_trainer_config(qwen3_configs.qwen3_debugmodel_moe())
+
+
+def graph_trainer_deepseek_v3_debugmodel() -> GraphTrainer.Config:
+    return to_graph_trainer_config(deepseek_v3_configs.deepseek_v3_debugmodel())
+
+
+def graph_trainer_deepseek_v3_16b() -> GraphTrainer.Config:
+    return to_graph_trainer_config(deepseek_v3_configs.deepseek_v3_16b())
