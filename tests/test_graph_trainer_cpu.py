@@ -259,3 +259,42 @@ def _fp8_gather(rank, world):
 
 def test_simple_fsdp_fp8_all_gather():
     _run(_fp8_gather, 2)
+
+
+def _resume(rank, world, out):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.graph.trainer import GraphTrainer
+
+    def cfg(steps, folder, ckpt):
+        args = ["--module", "graph", "--config", "graph_trainer_llama3_debugmodel_cpu",
+                "--training.steps", str(steps), "--training.seq_len", "64", "--training.local_batch_size", "2",
+                "--validator.no-enable", "--debug.seed", "5", "--dump-folder", folder]
+        args += ["--checkpoint.enable", "--checkpoint.interval", "2"] if ckpt else ["--checkpoint.no-enable"]
+        return ConfigManager().parse_args(args)
+
+    def losses(t, upto):
+        it = t.batch_generator(t.dataloader)
+        out_ = []
+        while t.step < upto:
+            t.step += 1
+            out_.append(float(t.train_step(it)))
+            t.checkpointer.save(t.step, last_step=t.step == upto)
+        return out_
+
+    straight = GraphTrainer(cfg(3, os.path.join(out, "a"), False))
+    ref = losses(straight, 3)
+    straight.close()
+    first = GraphTrainer(cfg(2, os.path.join(out, "b"), True))
+    losses(first, 2)
+    first.close()
+    second = GraphTrainer(cfg(3, os.path.join(out, "b"), True))
+    second.checkpointer.load()
+    assert second.step == 2
+    resumed = losses(second, 3)
+    second.close()
+    torch.testing.assert_close(torch.tensor(resumed), torch.tensor(ref[2:]), rtol=1e-5, atol=1e-6)
+
+
+def test_graph_trainer_checkpoint_resume(tmp_path):
+    """SimpleFSDP's DTensor shards go through DCP: a resumed run continues the straight run."""
+    _run(_resume, 2, str(tmp_path))
