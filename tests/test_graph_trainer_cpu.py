@@ -298,3 +298,32 @@ def _resume(rank, world, out):
 def test_graph_trainer_checkpoint_resume(tmp_path):
     """SimpleFSDP's DTensor shards go through DCP: a resumed run continues the straight run."""
     _run(_resume, 2, str(tmp_path))
+
+
+def _bitwise(rank, world, out):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.graph.trainer import GraphTrainer
+    from torchtitan_b200.utils.hashing import hash_model
+
+    hashes = []
+    for _ in range(2):
+        cfg = ConfigManager().parse_args(["--module", "graph", "--config", "graph_trainer_llama3_debugmodel_cpu",
+                                          "--training.steps", "3", "--training.seq_len", "64",
+                                          "--training.local_batch_size", "2", "--checkpoint.no-enable",
+                                          "--validator.no-enable", "--debug.seed", "11", "--debug.deterministic",
+                                          "--dump-folder", out, "--compile.passes", "selective_recompute",
+                                          "reshard_after_forward", "auto_bucketing"])
+        t = GraphTrainer(cfg)
+        it = t.batch_generator(t.dataloader)
+        while t.step < 3:
+            t.step += 1
+            t.train_step(it)
+        hashes.append(hash_model(t.model_parts[0]))
+        t.close()
+    assert hashes[0] == hashes[1]
+
+
+def test_graph_trainer_bitwise_deterministic(tmp_path):
+    """Two runs of the traced, bucketed, recomputing step from the same seed end with bitwise
+    identical weights (parity: the reference graph trainer's bitwise-determinism test)."""
+    _run(_bitwise, 2, str(tmp_path))
