@@ -329,19 +329,22 @@ def _ns_batched(mats: list[torch.Tensor], ns_steps: int) -> list[torch.Tensor]:
     return out  # type: ignore
 
 
-def _dist_orthogonalize_bucketed(pg, lst: list[tuple[int, "DTensor"]], ns_steps: int) -> dict[int, torch.Tensor]:
+def _dist_orthogonalize_bucketed(pg, lst: list[tuple[int, "DTensor"]], ns_steps: int,
+                                 waves: int = 2) -> dict[int, torch.Tensor]:
     """DistMuon over one process group for every Shard(0) matrix at once.
 
     Owners are assigned greedily by size (largest first, to the least-loaded rank), so every
     rank orthogonalises its share concurrently. One all-to-all carries every rank's row chunk of
     every matrix to its owner, the owner runs batched Newton-Schulz on all of its matrices, and
-    a second all-to-all returns the row chunks: two collectives per step, not two per parameter.
+    a second all-to-all returns the row chunks: two collectives per wave, not two per parameter.
+    The matrices are split into ``waves`` size-balanced waves that are pipelined: the
+    all-to-all bringing wave w+1 to its owners and the one returning wave w-1 run (asynchronously,
+    on the communicator's stream) while wave w is orthogonalised.
     (The reference has no distributed Muon: its optimizer registry stops at AdamW/Adam,
     ``torchtitan/components/optimizer.py:130-134``.)
     """
     world, rank = dist.get_world_size(pg), dist.get_rank(pg)
-    any_u = lst[0][1]
-    dev = any_u.to_local().device
+    dev = lst[0][1].to_local().device
     wire = torch.bfloat16 if dev.type == "cuda" else torch.float32  # NS runs in bf16 on CUDA
     order = sorted(range(len(lst)), key=lambda j: -lst[j][1].numel())
     load = [0] * world
@@ -354,52 +357,75 @@ def _dist_orthogonalize_bucketed(pg, lst: list[tuple[int, "DTensor"]], ns_steps:
     inner = [u.numel() // max(u.shape[0], 1) for _, u in lst]
     chunk = [(r + world - 1) // world for r in rows]
     cnum = [c * i for c, i in zip(chunk, inner)]
-    mine = [j for j in range(len(lst)) if owner[j] == rank]
-    # ---- chunks to owners
-    send = []
-    for dst in range(world):
-        for j in range(len(lst)):
-            if owner[j] != dst:
-                continue
-            loc = lst[j][1].to_local().reshape(-1, inner[j]).to(wire)
-            buf = torch.zeros(chunk[j], inner[j], dtype=wire, device=dev)
-            buf[:loc.shape[0]].copy_(loc)
-            send.append(buf.reshape(-1))
-    in_splits = [sum(cnum[j] for j in range(len(lst)) if owner[j] == dst) for dst in range(world)]
-    out_splits = [sum(cnum[j] for j in mine)] * world
-    send_t = torch.cat(send) if send else torch.zeros(0, dtype=wire, device=dev)
-    recv = torch.empty(sum(out_splits), dtype=wire, device=dev)
-    dist.all_to_all_single(recv, send_t, out_splits, in_splits, group=pg)
-    # ---- owner: assemble, orthogonalise (batched), cut into row chunks
-    per_src = recv.split(out_splits) if out_splits[0] else [recv] * world
-    fulls = []
-    for k, j in enumerate(mine):
-        off = sum(cnum[jj] for jj in mine[:k])
-        parts = [per_src[src][off:off + cnum[j]].view(chunk[j], inner[j]) for src in range(world)]
-        fulls.append(torch.cat(parts)[:rows[j]].reshape(lst[j][1].shape))
-    results = _ns_batched(fulls, ns_steps) if fulls else []
-    back = []
-    for dst in range(world):
+    # waves: the size order dealt round-robin, so every wave carries a similar share
+    nw = max(1, min(waves, len(lst)))
+    wave_of = {j: k % nw for k, j in enumerate(order)}
+
+    def start_gather(w: int):
+        js = [j for j in range(len(lst)) if wave_of[j] == w]
+        mine = [j for j in js if owner[j] == rank]
+        send = []
+        for dst in range(world):
+            for j in js:
+                if owner[j] != dst:
+                    continue
+                loc = lst[j][1].to_local().reshape(-1, inner[j]).to(wire)
+                buf = torch.zeros(chunk[j], inner[j], dtype=wire, device=dev)
+                buf[:loc.shape[0]].copy_(loc)
+                send.append(buf.reshape(-1))
+        in_splits = [sum(cnum[j] for j in js if owner[j] == dst) for dst in range(world)]
+        out_splits = [sum(cnum[j] for j in mine)] * world
+        send_t = torch.cat(send) if send else torch.zeros(0, dtype=wire, device=dev)
+        recv = torch.empty(sum(out_splits), dtype=wire, device=dev)
+        work = dist.all_to_all_single(recv, send_t, out_splits, in_splits, group=pg, async_op=True)
+        return js, mine, in_splits, out_splits, recv, send_t, work
+
+    def orthogonalise(state):
+        js, mine, in_splits, out_splits, recv, _send, work = state
+        work.wait()
+        per_src = recv.split(out_splits) if out_splits[0] else [recv] * world
+        fulls = []
         for k, j in enumerate(mine):
-            r2 = results[k].reshape(rows[j], inner[j])
-            buf = torch.zeros(chunk[j], inner[j], dtype=wire, device=dev)
-            seg = r2[dst * chunk[j]:(dst + 1) * chunk[j]]
-            buf[:seg.shape[0]].copy_(seg)
-            back.append(buf.reshape(-1))
-    back_t = torch.cat(back) if back else torch.zeros(0, dtype=wire, device=dev)
-    recv2 = torch.empty(sum(in_splits), dtype=wire, device=dev)
-    dist.all_to_all_single(recv2, back_t, in_splits, out_splits, group=pg)
-    # ---- this rank's rows of every matrix, in the order of the owners' sends
+            off = sum(cnum[jj] for jj in mine[:k])
+            parts = [per_src[src][off:off + cnum[j]].view(chunk[j], inner[j]) for src in range(world)]
+            fulls.append(torch.cat(parts)[:rows[j]].reshape(lst[j][1].shape))
+        results = _ns_batched(fulls, ns_steps) if fulls else []
+        back = []
+        for dst in range(world):
+            for k, j in enumerate(mine):
+                r2 = results[k].reshape(rows[j], inner[j])
+                buf = torch.zeros(chunk[j], inner[j], dtype=wire, device=dev)
+                seg = r2[dst * chunk[j]:(dst + 1) * chunk[j]]
+                buf[:seg.shape[0]].copy_(seg)
+                back.append(buf.reshape(-1))
+        back_t = torch.cat(back) if back else torch.zeros(0, dtype=wire, device=dev)
+        recv2 = torch.empty(sum(in_splits), dtype=wire, device=dev)
+        work2 = dist.all_to_all_single(recv2, back_t, in_splits, out_splits, group=pg, async_op=True)
+        return js, recv2, back_t, work2
+
     out: dict[int, torch.Tensor] = {}
-    pos = 0
-    for src in range(world):
-        for j in range(len(lst)):
-            if owner[j] != src:
-                continue
-            loc = lst[j][1].to_local()
-            piece = recv2[pos:pos + cnum[j]].view(chunk[j], inner[j])[:loc.shape[0]]
-            out[lst[j][0]] = piece.reshape(loc.shape).to(loc.dtype)
-            pos += cnum[j]
+
+    def finish(state):
+        js, recv2, _back, work2 = state
+        work2.wait()
+        pos = 0  # this rank's rows of every matrix of the wave, in the order of the owners' sends
+        for src in range(world):
+            for j in js:
+                if owner[j] != src:
+                    continue
+                loc = lst[j][1].to_local()
+                piece = recv2[pos:pos + cnum[j]].view(chunk[j], inner[j])[:loc.shape[0]]
+                out[lst[j][0]] = piece.reshape(loc.shape).to(loc.dtype)
+                pos += cnum[j]
+
+    pending = start_gather(0)
+    returning = []
+    for w in range(nw):
+        nxt = start_gather(w + 1) if w + 1 < nw else None  # next wave in flight during this NS
+        returning.append(orthogonalise(pending))
+        pending = nxt
+    for st in returning:
+        finish(st)
     return out
 
 
