@@ -145,3 +145,20 @@ def test_trainer_replicas_train_in_lockstep():
         w = [torch.load(os.path.join(d, f"w{r}.pt")) for r in (0, 1)]
     assert w[0]["step"] == w[1]["step"] == 4
     assert torch.equal(w[0]["w"], w[1]["w"])
+
+
+def test_membership_run_start_is_the_same_for_every_participant():
+    """The first round of a membership run comes from the store's closed lists, so a replica
+    that missed rounds (and so never saw the membership change) agrees with one that took part
+    in every round; both then build the cross-replica group under the same prefix."""
+    from torchtitan_b200.parallel.ft import FTManager, Lighthouse
+
+    lh = Lighthouse(0)
+    for r, parts in enumerate(["0,1", "0,1", "1,2", "0,1", "0,1"]):
+        lh.store.set(f"q/{r}/closed", parts)
+    steady = FTManager(lh.address, 0, 3)
+    late = FTManager(lh.address, 1, 3)
+    # the steady replica walked through rounds 0..4; the late one only sees round 4
+    assert [steady._membership_since(r, [int(x) for x in p.split(",")])
+            for r, p in enumerate(["0,1", "0,1", "1,2", "0,1", "0,1"])] == [0, 0, 2, 3, 3]
+    assert late._membership_since(4, [0, 1]) == 3

@@ -46,6 +46,7 @@ class Quorum:
     source: int               # the most advanced participant (state donor for healing)
     behind: list[int]         # participants whose step is behind the source's
     source_step: int = 0      # the source's completed step count (what a healed replica adopts)
+    since: int = 0            # first round of the unbroken run of rounds with these participants
 
     @property
     def size(self) -> int:
@@ -90,6 +91,8 @@ class FTManager:
         self._pgs: dict[tuple, dist.ProcessGroup] = {}
         self._retired: list[dist.ProcessGroup] = []
         self._last: list[int] = []
+        self._closed_seen: dict[int, str] = {}  # round -> closed participant list (store values)
+        self._since_seen: dict[int, int] = {}   # round -> first round of its membership run
         self._round: int | None = None  # quorum rounds are numbered by the lighthouse, not by steps
         self._fresh = True  # never synchronised with another replica: copy state at the first quorum
         self.quorum: Quorum | None = None
@@ -140,6 +143,30 @@ class FTManager:
         steps = {r: tuple(int(x) for x in s.get(f"q/{step}/join/{r}").decode().split(",")) for r in participants}
         return step, participants, steps  # one quorum per round: the round is its id
 
+    def _membership_since(self, qid: int, parts: list[int]) -> int:
+        """First round of the unbroken run of closed rounds ending at ``qid`` whose participants
+        equal ``parts``.  Computed from the store's closed lists, which never change, so every
+        participant gets the same answer whichever earlier rounds it took part in."""
+        s = self.store
+        closed = ",".join(str(r) for r in parts)
+        r = qid
+        while r > 0:
+            prev = self._closed_seen.get(r - 1)
+            if prev is None:
+                if not s.check([f"q/{r - 1}/closed"]):
+                    break
+                prev = s.get(f"q/{r - 1}/closed").decode()
+                self._closed_seen[r - 1] = prev
+            if prev != closed:
+                break
+            if (r - 1) in self._since_seen:
+                r = self._since_seen[r - 1]
+                break
+            r -= 1
+        self._closed_seen[qid] = closed
+        self._since_seen[qid] = r
+        return r
+
     def start_quorum(self, my_step: int) -> Quorum:
         """Form (or learn) the next quorum; ``my_step`` is this replica's completed step count
         (what healing compares). A replica that arrives after a round closed joins the next
@@ -147,13 +174,13 @@ class FTManager:
         if self.local_rank == 0:
             qid, parts, steps = self._leader_quorum(my_step)
             self._round = qid + 1
-            payload = [qid, parts, steps]
+            payload = [qid, parts, steps, self._membership_since(qid, parts)]
         else:
-            payload = [None, None, None]
+            payload = [None, None, None, None]
         if self.local_world > 1:
             dist.broadcast_object_list(payload, src=dist.get_global_rank(self.local_group, 0)
                                        if self.local_group is not None else 0, group=self.local_group)
-        qid, parts, steps = payload
+        qid, parts, steps, since = payload
         if self.replica_id not in parts:
             raise RuntimeError(f"replica {self.replica_id} found no quorum to join (last: {parts})")
         if len(parts) < self.min_replica_size:
@@ -165,7 +192,7 @@ class FTManager:
         behind = [r for r in parts if r != best and (steps[r][0] < steps[best][0] or steps[r][1])]
         self._last = parts
         self._fresh = False
-        self.quorum = Quorum(qid, qid, parts, best, behind, steps[best][0])
+        self.quorum = Quorum(qid, qid, parts, best, behind, steps[best][0], since)
         return self.quorum
 
     @property
@@ -179,12 +206,15 @@ class FTManager:
         assert q is not None, "start_quorum first"
         if q.size == 1:
             return None
-        # one group per membership: reused while the participants stay the same, rebuilt (under
-        # the prefix of the round where the new membership starts) when they change
-        key = tuple(q.participants)
+        # one group per run of rounds with the same participants: reused within the run, rebuilt
+        # (under the prefix of the run's first round) when it changes.  The run's first round
+        # comes from the store, not from this replica's history: a replica that missed a round
+        # (arrived after it closed) must not reuse a group its peers have replaced.
+        key = (q.since, tuple(q.participants))
         pg = self._pgs.get(key)
         if pg is None:
-            prefix = dist.PrefixStore(f"pg/{q.qid}/{','.join(map(str, q.participants))}/{self.local_rank}", self.store)
+            prefix = dist.PrefixStore(f"pg/{q.since}/{','.join(map(str, q.participants))}/{self.local_rank}",
+                                      self.store)
             rank = q.participants.index(self.replica_id)
             timeout = datetime.timedelta(seconds=self.collective_timeout_s)
             if self.backend == "gloo":
