@@ -167,7 +167,7 @@ def test_selective_recompute_moves_cheap_ops_to_backward():
         torch.testing.assert_close(p.grad, w, rtol=1e-5, atol=1e-6)
 
 
-def _trainer_modes(rank, world, out):
+def _trainer_modes(rank, world, out, accum=1):
     from torchtitan_b200.config.manager import ConfigManager
     from torchtitan_b200.graph.trainer import GraphTrainer
 
@@ -177,6 +177,7 @@ def _trainer_modes(rank, world, out):
                                           "--training.steps", "3", "--training.seq_len", "64",
                                           "--training.local_batch_size", "2", "--checkpoint.no-enable",
                                           "--validator.no-enable", "--compile.mode", mode,
+                                          "--training.global_batch_size", str(2 * world * accum),
                                           "--debug.seed", "7", "--dump-folder", out])
         assert isinstance(cfg, GraphTrainer.Config)
         t = GraphTrainer(cfg)
@@ -193,6 +194,11 @@ def _trainer_modes(rank, world, out):
 
 def test_graph_trainer_matches_eager_mode(tmp_path):
     _run(_trainer_modes, 2, str(tmp_path))
+
+
+def test_graph_trainer_gradient_accumulation(tmp_path):
+    """Two microbatches per step: the traced step's gradients accumulate like eager ones."""
+    _run(_trainer_modes, 2, str(tmp_path), 2)
 
 
 def _precompile(rank, world, out):
