@@ -447,6 +447,48 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return d;
   }, py::arg("a"), py::arg("sfa"), py::arg("b"), py::arg("sfb"), py::arg("tile_group"), py::arg("n"),
      py::arg("tile_n") = 0);
+  m.def("moe_combine_fwd", [](c10::optional<Tensor> base, Tensor y, Tensor pos, c10::optional<Tensor> w) {
+    // out[t] = base[t] + sum_j w[t, j] * y[pos[t, j]]: y [R, D] bf16, pos [T, k] int64, w [T, k] fp32
+    check_cuda_bf16(y, "y");
+    TORCH_CHECK(y.dim() == 2 && y.is_contiguous(), "moe_combine: y [R, D] contiguous");
+    TORCH_CHECK(pos.is_cuda() && pos.scalar_type() == at::kLong && pos.dim() == 2 && pos.is_contiguous(),
+                "moe_combine: pos [T, k] int64");
+    const int64_t T = pos.size(0), k = pos.size(1), D = y.size(1);
+    if (base.has_value()) {
+      check_cuda_bf16(*base, "base");
+      TORCH_CHECK(base->is_contiguous() && base->size(0) == T && base->size(1) == D, "moe_combine: base [T, D]");
+    }
+    if (w.has_value())
+      TORCH_CHECK(w->is_cuda() && w->scalar_type() == at::kFloat && w->is_contiguous() && w->numel() == T * k,
+                  "moe_combine: w [T, k] fp32");
+    c10::cuda::CUDAGuard g(y.device());
+    auto out = torch::empty({T, D}, y.options());
+    ttb::moe_combine_fwd(base.has_value() ? base->data_ptr() : nullptr, y.data_ptr(), pos.data_ptr<int64_t>(),
+                         w.has_value() ? w->data_ptr<float>() : nullptr, out.data_ptr(), T, (int)k, D, y.size(0),
+                         stream());
+    return out;
+  });
+  m.def("moe_combine_bwd", [](Tensor dout, Tensor y, Tensor pos, Tensor token_of, c10::optional<Tensor> scale,
+                              bool need_dw) {
+    // dy [R, D] = scale[r] * dout[token_of[r]]; dw [T, k] = dot(dout[t], y[pos[t, j]]) if need_dw
+    check_cuda_bf16(dout, "dout");
+    check_cuda_bf16(y, "y");
+    TORCH_CHECK(dout.is_contiguous() && y.is_contiguous() && dout.size(1) == y.size(1), "moe_combine_bwd: rows");
+    TORCH_CHECK(pos.scalar_type() == at::kLong && pos.is_contiguous() && token_of.scalar_type() == at::kLong &&
+                    token_of.is_contiguous() && token_of.numel() == y.size(0), "moe_combine_bwd: indices");
+    if (scale.has_value())
+      TORCH_CHECK(scale->scalar_type() == at::kFloat && scale->is_contiguous() && scale->numel() == y.size(0),
+                  "moe_combine_bwd: scale [R] fp32");
+    const int64_t T = pos.size(0), k = pos.size(1), D = y.size(1), R = y.size(0);
+    TORCH_CHECK(dout.size(0) == T, "moe_combine_bwd: dout [T, D]");
+    c10::cuda::CUDAGuard g(y.device());
+    auto dy = torch::empty({R, D}, y.options());
+    auto dw = torch::empty({need_dw ? T : 0, need_dw ? k : 0}, y.options().dtype(at::kFloat));
+    ttb::moe_combine_bwd(dout.data_ptr(), y.data_ptr(), pos.data_ptr<int64_t>(), token_of.data_ptr<int64_t>(),
+                         scale.has_value() ? scale->data_ptr<float>() : nullptr, dy.data_ptr(),
+                         need_dw ? dw.data_ptr<float>() : nullptr, T, (int)k, D, R, stream());
+    return std::vector<Tensor>{dy, dw};
+  });
   m.def("f8_quantize", [](Tensor x, bool rowwise) {
     check_cuda_bf16(x, "x");
     TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "f8_quantize: [R, C] with contiguous rows");

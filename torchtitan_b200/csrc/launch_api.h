@@ -45,6 +45,12 @@ void rmsnorm_bwd(const void* dy, const void* x, const void* w, const float* rstd
 // out[p] = src[idx[p]] or a zero row where idx[p] < 0 (bf16, row length a multiple of 8)
 void gather_rows_bf16(const void* src, int64_t n_src, const int64_t* idx, void* out, int64_t rows, int64_t d,
                       cudaStream_t s);
+// moe_combine.cu: deterministic MoE combine (per-token gather-sum of the routed rows) and backward
+void moe_combine_fwd(const void* base, const void* y, const int64_t* pos, const float* w, void* out, int64_t T,
+                     int k, int64_t D, int64_t R, cudaStream_t s);
+void moe_combine_bwd(const void* dout, const void* y, const int64_t* pos, const int64_t* token_of,
+                     const float* scale, void* dy, float* dw, int64_t T, int k, int64_t D, int64_t R,
+                     cudaStream_t s);
 int rmsnorm_bwd_parts(int64_t rows, int64_t dim, int sms);
 void reduce_rows_f32(const float* partial, float* out, int64_t nparts, int64_t dim, cudaStream_t s);
 void rope_apply(const void* x, void* y, const float* cos, const float* sin, int64_t B, int64_t S, int64_t H,

@@ -8,7 +8,7 @@ functions.  Running the traced graph then calls the same kernels through those o
 
 Covered: every kernel of the dense decoder step (GEMM, attention forward/backward, RMSNorm,
 RoPE, SwiGLU, cross entropy) and of the routed experts (routing selection, row gathers, grouped
-GEMMs).  Any other attribute falls through to the extension itself,
+GEMMs, dispatch / combine).  Any other attribute falls through to the extension itself,
 which fails loudly under fake tensors.
 """
 from __future__ import annotations
@@ -161,6 +161,30 @@ def _(a, b, kstart, klen):
     return a.new_empty((kstart.shape[0], a.shape[1], b.shape[1]))
 
 
+@torch.library.custom_op("tt_b200_graph::moe_combine_fwd", mutates_args=())
+def moe_combine_fwd(base: torch.Tensor | None, y: torch.Tensor, pos: torch.Tensor,
+                    w: torch.Tensor | None) -> torch.Tensor:
+    return _C().moe_combine_fwd(base, y, pos, w)
+
+
+@moe_combine_fwd.register_fake
+def _(base, y, pos, w):
+    return y.new_empty((pos.shape[0], y.shape[1]))
+
+
+@torch.library.custom_op("tt_b200_graph::moe_combine_bwd", mutates_args=())
+def moe_combine_bwd(dout: torch.Tensor, y: torch.Tensor, pos: torch.Tensor, token_of: torch.Tensor,
+                    scale: torch.Tensor | None, need_dw: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    dy, dw = _C().moe_combine_bwd(dout, y, pos, token_of, scale, need_dw)
+    return dy, dw
+
+
+@moe_combine_bwd.register_fake
+def _(dout, y, pos, token_of, scale, need_dw):
+    shape = tuple(pos.shape) if need_dw else (0, 0)
+    return torch.empty_like(y), y.new_empty(shape, dtype=torch.float32)
+
+
 class _TraceableKernels:
     """Stand-in for the extension module while tracing: the dense-step kernels as custom ops."""
 
@@ -179,6 +203,9 @@ class _TraceableKernels:
     gemm_grouped_rows = staticmethod(lambda a, b, tg, n, rows, bmn: torch.ops.tt_b200_graph.gemm_grouped_rows(
         a, b, tg, int(n), int(rows), bool(bmn)))
     gemm_grouped_k = staticmethod(lambda a, b, ks, kl: torch.ops.tt_b200_graph.gemm_grouped_k(a, b, ks, kl))
+    moe_combine_fwd = staticmethod(lambda base, y, pos, w: torch.ops.tt_b200_graph.moe_combine_fwd(base, y, pos, w))
+    moe_combine_bwd = staticmethod(lambda dout, y, pos, tok, scale, need: torch.ops.tt_b200_graph.moe_combine_bwd(
+        dout, y, pos, tok, scale, bool(need)))
 
     @staticmethod
     def attn_fwd(q, k, v, causal, scale, doc_start=None, doc_end=None):

@@ -201,17 +201,30 @@ class MoE(nn.Module):
         order = torch.argsort(flat, stable=True)
         token_of = order // self.top_k
         gates = top.flatten()[order]
-        routed = xf[token_of]
+        kernels = ops.combine_kernel_enabled(xf)
+        if kernels:
+            # deterministic gather / gather-sum kernels in both directions (no atomics)
+            pos = ops.slot_positions(order, self.top_k)
+            routed = ops.moe_dispatch(xf, token_of, pos)
+        else:
+            routed = xf[token_of]
         if self.score_before_experts:
             routed = (routed.float() * gates[:, None]).to(x.dtype)
         if self.ep_dispatch is not None:
             out_routed = self.ep_dispatch(routed, counts, self.experts)
         else:
             out_routed = self.experts(routed, counts)
-        if not self.score_before_experts:
-            out_routed = (out_routed.float() * gates[:, None]).to(x.dtype)
-        out = self.shared_experts(x).reshape(-1, D) if self.shared_experts is not None else torch.zeros_like(xf)
-        out = out.index_add(0, token_of, out_routed.to(out.dtype)).view(B, S, D)
+        if kernels and out_routed.dtype == torch.bfloat16:
+            base = self.shared_experts(x).reshape(-1, D) if self.shared_experts is not None else None
+            if base is not None and base.dtype != torch.bfloat16:
+                base = base.to(torch.bfloat16)
+            w = None if self.score_before_experts else top
+            out = ops.moe_combine(base, out_routed, w, pos, token_of, order).to(x.dtype).view(B, S, D)
+        else:
+            if not self.score_before_experts:
+                out_routed = (out_routed.float() * gates[:, None]).to(x.dtype)
+            out = self.shared_experts(x).reshape(-1, D) if self.shared_experts is not None else torch.zeros_like(xf)
+            out = out.index_add(0, token_of, out_routed.to(out.dtype)).view(B, S, D)
         if self.aux_loss_coeff > 0 and self.training:
             p = scores / (scores.sum(-1, keepdim=True) + 1e-20)
             f = counts.float() / max(flat.numel(), 1)

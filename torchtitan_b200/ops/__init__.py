@@ -125,7 +125,7 @@ def cross_entropy_sum(logits: torch.Tensor, labels: torch.Tensor, ignore_index: 
 
 
 # ---------------------------------------------------------------- MoE experts
-from .moe import grouped_swiglu  # noqa: E402
+from .moe import combine_kernel_enabled, grouped_swiglu, moe_combine, moe_dispatch, slot_positions  # noqa: E402
 from .grouped import grouped_swiglu_padded  # noqa: E402
 from .attention import attention_with_lse, document_attention  # noqa: E402
 
