@@ -13,7 +13,7 @@ import torch
 
 
 def _replica(rid, address, group_size, steps, out, stop_after=None, start_delay=0.0, seed=0, wait_for=(),
-             step_time=0.0):
+             step_time=0.0, join_after_round=None):
     import torch.nn as nn
 
     from torchtitan_b200.parallel.ft import FTManager
@@ -26,6 +26,9 @@ def _replica(rid, address, group_size, steps, out, stop_after=None, start_delay=
     # process start-up takes seconds: replicas that should start together wait for each other
     ft.store.set(f"ready/{rid}", "1")
     ft.store.wait([f"ready/{r}" for r in wait_for])
+    if join_after_round is not None:  # a late replica: arrive once the others have trained a while
+        while not (ft.store.check(["latest"]) and int(ft.store.get("latest").decode()) >= join_after_round):
+            time.sleep(0.01)
     my_step, log, commits = 0, [], 0
     while my_step < steps:
         q = ft.start_quorum(my_step)
@@ -85,7 +88,7 @@ def test_replica_loss_leaves_survivors_in_lockstep():
 
 def test_late_replica_heals_from_peer():
     pair = {"wait_for": (0, 1), "step_time": 0.05}
-    res = _run([(0, pair), (1, pair), (2, {"start_delay": 2.0, "seed": 7, "step_time": 0.05})], group_size=3,
+    res = _run([(0, pair), (1, pair), (2, {"join_after_round": 20, "seed": 7, "step_time": 0.05})], group_size=3,
                steps=200)
     for rid in (0, 1, 2):
         assert res[rid]["step"] == 200, (rid, res[rid]["step"])
@@ -105,7 +108,8 @@ def _trainer_replica(rid, address, port, out):
         "--training.seq-len", "64", "--metrics.log-freq", "1", "--dump-folder", os.path.join(out, f"r{rid}"),
         "--fault-tolerance.enable", "--fault-tolerance.lighthouse", address,
         "--fault-tolerance.replica-id", str(rid), "--fault-tolerance.group-size", "2",
-        "--fault-tolerance.min-replica-size", "2", "--fault-tolerance.quorum-timeout-s", "20"]))
+        "--fault-tolerance.min-replica-size", "2", "--fault-tolerance.quorum-timeout-s", "20",
+        "--fault-tolerance.process-group-timeout-ms", "60000"]))
     t.ft.store.set(f"ready/{rid}", "1")
     t.ft.store.wait(["ready/0", "ready/1"])
     t.train()
