@@ -53,25 +53,29 @@ def step_inputs(model: nn.Module, param_names: list[str], buffer_names: list[str
 
 
 def trace_train_step(model: nn.Module, loss_fn: Callable, inputs: torch.Tensor, labels: torch.Tensor,
-                     norm: torch.Tensor) -> TracedStep:
-    """``loss_fn(pred, labels)`` returns the summed loss; the traced loss is that sum / ``norm``."""
+                     norm: torch.Tensor, extra_kwargs: dict[str, torch.Tensor] | None = None) -> TracedStep:
+    """``loss_fn(pred, labels)`` returns the summed loss; the traced loss is that sum / ``norm``.
+    ``extra_kwargs`` (tensors, e.g. per-token positions and document ids of packed sequences)
+    become trailing graph inputs in sorted-name order and are passed to the model by name."""
     param_names = [n for n, p in model.named_parameters() if p.requires_grad]
     buffer_names = [n for n, _ in model.named_buffers()]
+    extra_names = sorted(extra_kwargs or {})
 
-    def step(params, buffers, tokens, lbl, nrm):
+    def step(params, buffers, tokens, lbl, nrm, *extras):
         state = dict(zip(param_names, params))
         state.update(zip(buffer_names, buffers))
-        pred = torch.func.functional_call(model, state, (tokens,))
+        pred = torch.func.functional_call(model, state, (tokens,), dict(zip(extra_names, extras)))
         loss = loss_fn(pred, lbl) / nrm
         grads = torch.autograd.grad(loss, params, allow_unused=True)
         return [loss] + [g if g is not None else torch.zeros_like(p) for g, p in zip(grads, params)]
 
     params, buffers = step_inputs(model, param_names, buffer_names)
     with traceable_kernels():
-        gm = make_fx(step, tracing_mode="fake", _allow_non_fake_inputs=False)(params, buffers, inputs, labels, norm)
+        gm = make_fx(step, tracing_mode="fake", _allow_non_fake_inputs=False)(
+            params, buffers, inputs, labels, norm, *[extra_kwargs[n] for n in extra_names])
     out = next(n for n in gm.graph.nodes if n.op == "output")
     loss_node = out.args[0][0].name
-    return TracedStep(gm, param_names, buffer_names, len(param_names), loss_node)
+    return TracedStep(gm, param_names, buffer_names, len(param_names), loss_node, {"extra_names": extra_names})
 
 
 def backward_nodes(gm: fx.GraphModule, loss_node: str) -> set[fx.Node]:
@@ -102,10 +106,14 @@ class GraphStepRunner:
         needed when a later microbatch of the same step replays the graph again."""
 
     @torch.no_grad()
-    def __call__(self, inputs: torch.Tensor, labels: torch.Tensor, norm: torch.Tensor) -> torch.Tensor:
+    def __call__(self, inputs: torch.Tensor, labels: torch.Tensor, norm: torch.Tensor,
+                 extra_kwargs: dict[str, torch.Tensor] | None = None) -> torch.Tensor:
         locs = [_local(p) for p in self.params]
         bufs = [_local(b) for b in self.buffers]
-        outs = self.executor(locs, bufs, inputs, labels, norm)
+        names = self.traced.meta.get("extra_names", [])
+        if sorted(extra_kwargs or {}) != names:
+            raise ValueError(f"traced step takes extra inputs {names}, got {sorted(extra_kwargs or {})}")
+        outs = self.executor(locs, bufs, inputs, labels, norm, *[extra_kwargs[n] for n in names])
         loss, grads = outs[0], outs[1:]
         static = getattr(self.executor, "outputs_are_static", False)
         for p, g in zip(self.params, grads):

@@ -129,7 +129,7 @@ class GraphTrainer(Trainer):
         rank = dist.get_rank() if dist.is_initialized() else 0
         return os.path.join(c.compile.precompile_artifact_dir, f"step-{h}-rank{rank}.pt")
 
-    def _trace(self, key: tuple, inputs, labels, norm):
+    def _trace(self, key: tuple, inputs, labels, norm, extra):
         import os
 
         cc = self.config.compile
@@ -139,7 +139,7 @@ class GraphTrainer(Trainer):
             self.loaded_artifacts = getattr(self, "loaded_artifacts", 0) + 1
             logger.info(f"graph trainer: loaded the traced step from {path}")
             return traced, len(traced.gm.graph.nodes)
-        traced = trace_train_step(self.model_parts[0], self._loss, inputs, labels, norm)
+        traced = trace_train_step(self.model_parts[0], self._loss, inputs, labels, norm, extra)
         n0 = len(traced.gm.graph.nodes)
         if cc.enable_passes:
             graph_passes.apply_passes(traced, graph_passes.DEFAULT_PASSES + self._passes, bucket_bytes=cc.bucket_bytes)
@@ -150,12 +150,14 @@ class GraphTrainer(Trainer):
             os.replace(tmp, path)
         return traced, n0
 
-    def _runner(self, inputs: torch.Tensor, labels: torch.Tensor, norm: torch.Tensor) -> GraphStepRunner:
-        key = (tuple(inputs.shape), inputs.dtype, tuple(labels.shape))
+    def _runner(self, inputs: torch.Tensor, labels: torch.Tensor, norm: torch.Tensor,
+                extra: dict[str, torch.Tensor]) -> GraphStepRunner:
+        key = (tuple(inputs.shape), inputs.dtype, tuple(labels.shape),
+               tuple((n, tuple(v.shape), v.dtype) for n, v in sorted(extra.items())))
         run = self._steps.get(key)
         if run is None:
             model = self.model_parts[0]
-            traced, n0 = self._trace(key, inputs, labels, norm)
+            traced, n0 = self._trace(key, inputs, labels, norm, extra)
             executor = None
             if self._cudagraph:
                 from .cudagraph import CUDAGraphExecutor
@@ -175,7 +177,10 @@ class GraphTrainer(Trainer):
             return super().forward_backward_step(input_dict=input_dict, labels=labels,
                                                  global_valid_tokens=global_valid_tokens)
         inputs, labels, extra_inputs, extra_kwargs = self.post_dataloading_process(input_dict, labels)
-        if extra_inputs or extra_kwargs:
-            raise NotImplementedError("graph trainer: extra model inputs (document masks, images) are not traced")
+        if extra_inputs:
+            raise NotImplementedError("graph trainer: extra model inputs (images) are not traced")
+        extra = dict(extra_kwargs)
+        if any(not torch.is_tensor(v) for v in extra.values()):
+            raise NotImplementedError("graph trainer: non-tensor model keyword arguments are not traced")
         norm = global_valid_tokens.to(torch.float32).reshape(())
-        return self._runner(inputs, labels, norm)(inputs, labels, norm)
+        return self._runner(inputs, labels, norm, extra)(inputs, labels, norm, extra)
