@@ -90,3 +90,11 @@ def _entry(rank, world, port, out):
 
 def test_trainer_runs_auto_parallel_plan(tmp_path):
     mp.spawn(_entry, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
+
+
+def test_planner_command_line(capsys):
+    from torchtitan_b200.parallel.auto_parallel import main
+
+    plans = main(["--ngpu", "8", "--top", "2", "--module", "llama3", "--config", "llama3_8b"])
+    out = capsys.readouterr().out
+    assert out.startswith("1. ") and "2. " in out and len(plans) >= 2

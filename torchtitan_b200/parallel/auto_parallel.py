@@ -241,3 +241,33 @@ def auto_parallelize_config(config: Any, world: int) -> Plan:
     t.local_batch_size = gbs // dp // best.grad_accum
     apply_plan(config, best)
     return best
+
+
+def main(argv: list[str] | None = None) -> list[Plan]:
+    """``python -m torchtitan_b200.parallel.auto_parallel --ngpu 8 [--top 5] --module M --config C
+    [--section.key value ...]``: print the cheapest feasible layouts for a registered config."""
+    import argparse
+    import sys
+
+    import torch
+
+    from torchtitan_b200.config.manager import ConfigManager
+
+    p = argparse.ArgumentParser(description=main.__doc__.splitlines()[0])
+    p.add_argument("--ngpu", type=int, default=8)
+    p.add_argument("--top", type=int, default=5)
+    args, rest = p.parse_known_args(sys.argv[1:] if argv is None else argv)
+    cfg = ConfigManager().parse_args(rest)
+    margs = cfg.model_spec.model
+    with torch.device("meta"):
+        model = margs.build()
+    t = cfg.training
+    gbs = t.global_batch_size if t.global_batch_size > 0 else t.local_batch_size * args.ngpu
+    plans = plan_parallelism(model_shape(model, margs, t.seq_len), args.ngpu, gbs, t.seq_len)
+    for i, plan in enumerate(plans[: args.top]):
+        print(f"{i + 1}. {plan.describe()}")
+    return plans
+
+
+if __name__ == "__main__":
+    main()
