@@ -361,3 +361,22 @@ def test_traced_step_with_packed_documents():
     GraphStepRunner(m, tr)(tok, lab, norm, extra)
     for p, w in zip(m.parameters(), want):
         torch.testing.assert_close(p.grad, w, rtol=1e-5, atol=1e-6)
+
+
+def test_reshard_policy_maps_to_the_graph_pass(tmp_path, monkeypatch):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.graph.trainer import GraphTrainer
+
+    monkeypatch.setenv("LOCAL_RANK", "0")
+    got = {}
+    for policy in ("never", "always"):
+        cfg = ConfigManager().parse_args(["--module", "graph", "--config", "graph_trainer_llama3_debugmodel_cpu",
+                                          "--training.steps", "1", "--checkpoint.no-enable", "--validator.no-enable",
+                                          "--parallelism.fsdp-reshard-after-forward", policy,
+                                          "--compile.passes", "transformer_block_bucketing",
+                                          "--dump-folder", str(tmp_path)])
+        t = GraphTrainer(cfg)
+        got[policy] = list(t._passes)
+        t.close()
+    assert "reshard_after_forward" not in got["never"]
+    assert got["always"][0] == "reshard_after_forward"

@@ -109,6 +109,12 @@ class GraphTrainer(Trainer):
         self._steps: dict[tuple, GraphStepRunner] = {}
         cc = c.compile
         self._passes = [p for p in cc.passes if p != "cudagraph"]
+        # --parallelism.fsdp_reshard_after_forward maps onto the graph pass of the same role
+        policy = c.parallelism.fsdp_reshard_after_forward
+        if policy == "never":
+            self._passes = [p for p in self._passes if p != "reshard_after_forward"]
+        elif policy == "always" and "reshard_after_forward" not in self._passes:
+            self._passes.insert(0, "reshard_after_forward")
         self._cudagraph = "cudagraph" in cc.passes and self.device.type == "cuda"
         unknown = [p for p in self._passes if p not in graph_passes.PASSES]
         if unknown:
