@@ -380,3 +380,36 @@ def test_reshard_policy_maps_to_the_graph_pass(tmp_path, monkeypatch):
         t.close()
     assert "reshard_after_forward" not in got["never"]
     assert got["always"][0] == "reshard_after_forward"
+
+
+def _hsdp_trainer(rank, world, out):
+    from torchtitan_b200.config.manager import ConfigManager
+    from torchtitan_b200.graph.trainer import GraphTrainer
+
+    losses = {}
+    for mode in ("eager", "aot_fx_trace"):
+        cfg = ConfigManager().parse_args(["--module", "graph", "--config", "graph_trainer_llama3_debugmodel_cpu",
+                                          "--training.steps", "2", "--training.seq_len", "64",
+                                          "--training.local_batch_size", "1", "--checkpoint.no-enable",
+                                          "--validator.no-enable", "--compile.mode", mode,
+                                          "--parallelism.data-parallel-replicate-degree", "2",
+                                          "--parallelism.data-parallel-shard-degree", "2",
+                                          "--debug.seed", "9", "--dump-folder", out])
+        t = GraphTrainer(cfg)
+        w = t.model_parts[0].tok_embeddings._parameters["weight"]
+        assert w.device_mesh.ndim == 2  # [dp_replicate, fsdp]
+        it = t.batch_generator(t.dataloader)
+        vals = []
+        while t.step < 2:
+            t.step += 1
+            vals.append(float(t.train_step(it)))
+        losses[mode] = vals
+        t.close()
+    torch.testing.assert_close(torch.tensor(losses["aot_fx_trace"]), torch.tensor(losses["eager"]),
+                               rtol=1e-5, atol=1e-6)
+
+
+def test_graph_trainer_hsdp(tmp_path):
+    """HSDP (2 replicas x 2 shards): the traced step with its reduce-scatter + all-reduce nodes
+    matches SimpleFSDP's eager step."""
+    _run(_hsdp_trainer, 4, str(tmp_path))
