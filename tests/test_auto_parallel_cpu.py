@@ -98,3 +98,25 @@ def test_planner_command_line(capsys):
     plans = main(["--ngpu", "8", "--top", "2", "--module", "llama3", "--config", "llama3_8b"])
     out = capsys.readouterr().out
     assert out.startswith("1. ") and "2. " in out and len(plans) >= 2
+
+
+def test_peer_memory_data_parallel_is_a_candidate():
+    """On 2-4 GPUs of one node the peer-memory runtime (no FSDP2 copy passes, bf16 traffic) is
+    chosen for the 8B model, as measured; at 8 GPUs FSDP2 shards enough to win; without peer
+    memory (CPU/gloo) it is never offered."""
+    from torchtitan_b200.parallel.auto_parallel import Plan, apply_plan
+
+    sh = _shape("8B")
+    assert plan_parallelism(sh, 2, 2, 8192, hw=Hardware())[0].dp_comm == "peer"
+    assert plan_parallelism(sh, 8, 8, 8192, hw=Hardware())[0].dp_comm == "fsdp2"
+    assert all(p.dp_comm == "fsdp2" for p in plan_parallelism(sh, 2, 2, 8192, hw=Hardware(peer_memory=False)))
+
+    class _C:  # the two config sections apply_plan writes
+        class parallelism:
+            pass
+
+        class activation_checkpoint:
+            mode = "none"
+
+    apply_plan(_C, Plan(1, 2, 1, 1, False, False, False, "selective", 1, "peer"))
+    assert _C.parallelism.data_parallel_comm == "peer" and _C.activation_checkpoint.mode == "selective"

@@ -19,6 +19,10 @@ mode.  Each candidate gets an analytic step time and a per-GPU memory estimate:
   memory    fp32 master + grad + Adam moments over the sharding degree, gathered bf16
             weights, activations per token for the AC mode, logits; must fit the HBM budget
 
+For 2-4 ranks of pure data parallelism the peer-memory runtime is a candidate too (replicated
+bf16 weights and gradient buckets, sharded fp32 optimizer state; bf16 reduce-scatter and
+weight stores over NVLink; no FSDP2 copy-in/copy-out passes).
+
 The cheapest feasible candidate wins (ties go to fewer model-parallel dims).  Rates come from
 ``MEASURED_PEAKS.json`` when present (sustained GEMM TFLOP/s) and the pool's measured NVLink
 peer-copy bandwidth otherwise.
@@ -54,10 +58,13 @@ class ModelShape:
 @dataclass(frozen=True)
 class Hardware:
     gemm_tflops: float = GEMM_TFLOPS_FALLBACK
+    hbm_gbs: float = 6500.0
     nvlink_gbs: float = NVLINK_GBS
     hbm_bytes: float = HBM_BYTES
     gpus_per_node: int = 8
     memory_fraction: float = 0.9
+    peer_memory: bool = True
+    """GPUs of one node reach each other's memory (the peer-memory data-parallel runtime)."""
 
 
 @dataclass(frozen=True)
@@ -71,6 +78,9 @@ class Plan:
     reshard_after_forward: bool
     ac_mode: str
     grad_accum: int = 1
+    dp_comm: str = "fsdp2"
+    """``fsdp2`` or ``peer`` (replicated bf16 weights, sharded fp32 optimizer state, gradient
+    reduce-scatter kernel and all-gather fused into AdamW over NVLink peer memory)."""
     step_s: float = 0.0
     memory_bytes: float = 0.0
     breakdown: dict = field(default_factory=dict, compare=False, hash=False)
@@ -79,7 +89,7 @@ class Plan:
         b = self.breakdown
         return (f"dp_replicate={self.dp_replicate} dp_shard={self.dp_shard} cp={self.cp} tp={self.tp} "
                 f"sp={self.sequence_parallel} async_tp={self.async_tp} reshard={self.reshard_after_forward} "
-                f"ac={self.ac_mode} ga={self.grad_accum}: {self.step_s * 1e3:.1f} ms/step, {self.memory_bytes / 2**30:.1f} GiB/GPU "
+                f"ac={self.ac_mode} ga={self.grad_accum} dp_comm={self.dp_comm}: {self.step_s * 1e3:.1f} ms/step, {self.memory_bytes / 2**30:.1f} GiB/GPU "
                 f"(compute {b.get('compute', 0) * 1e3:.1f} ms, exposed comm {b.get('comm', 0) * 1e3:.1f} ms)")
 
 
@@ -89,7 +99,8 @@ def default_hardware() -> Hardware:
     try:
         with open(path) as f:
             peaks = json.load(f)
-        return Hardware(gemm_tflops=float(peaks.get("bf16_tflops_sustained") or GEMM_TFLOPS_FALLBACK))
+        return Hardware(gemm_tflops=float(peaks.get("bf16_tflops_sustained") or GEMM_TFLOPS_FALLBACK),
+                        hbm_gbs=float(peaks.get("hbm_gbs") or 6500.0))
     except (OSError, ValueError):
         return Hardware()
 
@@ -133,11 +144,20 @@ def estimate(shape: ModelShape, hw: Hardware, plan: Plan, global_batch: int, seq
     p_local = shape.n_params / plan.tp           # parameters a TP rank holds before DP sharding
     fs = plan.dp_shard * plan.cp                 # FSDP shards over the data and context dims
     fsdp = 0.0
-    if fs > 1:
+    hbm = hw.hbm_gbs * 1e9
+    copies = 0.0  # memory passes of the data-parallel runtime itself (not hidden by overlap)
+    if plan.dp_comm == "peer":
+        frac = (fs - 1) / fs
+        # bf16 gradient reduce-scatter per microbatch + bf16 weight stores fused into AdamW
+        fsdp = p_local * frac * 2 / bw * plan.grad_accum + p_local * frac * 2 / bw
+        copies = p_local * 2 * plan.grad_accum / hbm          # gradients into the bucket buffer
+    elif fs > 1:
         frac = (fs - 1) / fs
         n_ag = 2 if plan.reshard_after_forward else 1
         # gathers and reductions repeat per microbatch
         fsdp = p_local * frac * (2 * n_ag + 4) / bw * plan.grad_accum
+        # FSDP2 copy-in of the gathered bf16 parameters and copy-out of fp32 gradient shards
+        copies = p_local * (2 * n_ag + 4) * plan.grad_accum / hbm
     if plan.dp_replicate > 1:
         frac = 2 * (plan.dp_replicate - 1) / plan.dp_replicate
         fsdp += p_local / fs * 4 * frac / bw
@@ -154,11 +174,16 @@ def estimate(shape: ModelShape, hw: Hardware, plan: Plan, global_batch: int, seq
     if plan.cp > 1:
         kv = tokens_dp / plan.cp * 2 * shape.n_kv_heads * shape.head_dim * 2 / plan.tp
         cp_comm = shape.n_layers * 3 * kv * (plan.cp - 1) / bw * 0.3   # overlapped with the tiles
-    exposed = max(0.0, fsdp - 0.85 * compute) + tp_comm + cp_comm
+    exposed = max(0.0, fsdp - 0.85 * compute) + tp_comm + cp_comm + copies
     step = compute + exposed
 
-    states = shape.n_params * 16 / (fs * plan.tp)
-    gathered = 2 * p_local * (2.0 / shape.n_layers if plan.reshard_after_forward else 1.0) if fs > 1 else 0.0
+    if plan.dp_comm == "peer":
+        # fp32 master + Adam moments sharded; full bf16 weights and bf16 gradient buckets
+        states = shape.n_params * 12 / fs + shape.n_params * 4
+        gathered = 0.0
+    else:
+        states = shape.n_params * 16 / (fs * plan.tp)
+        gathered = 2 * p_local * (2.0 / shape.n_layers if plan.reshard_after_forward else 1.0) if fs > 1 else 0.0
     acts = shape.n_layers * tokens_gpu_act * shape.dim * _ACT_BYTES_PER_DIM[plan.ac_mode]
     if plan.tp > 1 and not plan.sequence_parallel:
         acts = acts / plan.tp * 1.5  # head/hidden-sharded tensors shrink, replicated norms do not
@@ -190,6 +215,9 @@ def candidates(shape: ModelShape, hw: Hardware, world: int, global_batch: int, s
                             for ac in ac_modes:
                                 for ga in _divisors(per_rank):
                                     out.append(Plan(rep, shard, cp, tp, sp, atp, reshard, ac, ga))
+                                    # peer-memory DP: pure data parallelism on one node, 2-4 ranks
+                                    if hw.peer_memory and tp == cp == rep == 1 and 2 <= shard <= 4 and reshard:
+                                        out.append(Plan(rep, shard, cp, tp, sp, atp, False, ac, ga, "peer"))
     return out
 
 
@@ -218,6 +246,7 @@ def apply_plan(config: Any, plan: Plan) -> None:
     par.enable_sequence_parallel = plan.sequence_parallel
     par.enable_async_tensor_parallel = plan.async_tp
     par.fsdp_reshard_after_forward = "always" if plan.reshard_after_forward else "never"
+    par.data_parallel_comm = plan.dp_comm
     config.activation_checkpoint.mode = plan.ac_mode
 
 
@@ -232,7 +261,10 @@ def auto_parallelize_config(config: Any, world: int) -> Plan:
     dp_guess = world
     gbs = t.global_batch_size if t.global_batch_size > 0 else t.local_batch_size * dp_guess
     shape = model_shape(model, margs, t.seq_len)
-    plans = plan_parallelism(shape, world, gbs, t.seq_len)
+    hw = default_hardware()
+    if not torch.cuda.is_available():  # gloo / CPU runs: no peer memory
+        hw = replace(hw, peer_memory=False)
+    plans = plan_parallelism(shape, world, gbs, t.seq_len, hw=hw)
     best = plans[0]
     dp = best.dp_replicate * best.dp_shard
     # the global batch stays what the config implied; each data-parallel rank runs it in
