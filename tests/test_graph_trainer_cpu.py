@@ -413,3 +413,20 @@ def test_graph_trainer_hsdp(tmp_path):
     """HSDP (2 replicas x 2 shards): the traced step with its reduce-scatter + all-reduce nodes
     matches SimpleFSDP's eager step."""
     _run(_hsdp_trainer, 4, str(tmp_path))
+
+
+def test_graph_trainer_configs_are_data_parallel():
+    """Every registered graph-trainer config builds and asks only for the parallelism the graph
+    trainer composes (SimpleFSDP data parallelism)."""
+    from torchtitan_b200.graph import config_registry as reg
+    from torchtitan_b200.graph.trainer import GraphTrainer
+
+    names = [n for n in dir(reg) if n.startswith("graph_trainer_")]
+    assert len(names) >= 12
+    for n in names:
+        c = getattr(reg, n)()
+        assert isinstance(c, GraphTrainer.Config), n
+        p = c.parallelism
+        assert (p.tensor_parallel_degree, p.context_parallel_degree, p.pipeline_parallel_degree,
+                p.expert_parallel_degree) == (1, 1, 1, 1), n
+        assert c.activation_checkpoint.mode == "none", n

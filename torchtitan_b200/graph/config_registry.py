@@ -61,4 +61,30 @@ def graph_trainer_deepseek_v3_debugmodel() -> GraphTrainer.Config:
 
 
 def graph_trainer_deepseek_v3_16b() -> GraphTrainer.Config:
-    return to_graph_trainer_config(deepseek_v3_configs.deepseek_v3_16b())
+    return _data_parallel_only(to_graph_trainer_config(deepseek_v3_configs.deepseek_v3_16b()))
+
+
+def _data_parallel_only(c: GraphTrainer.Config) -> GraphTrainer.Config:
+    """The graph trainer shards over data-parallel ranks only: model-parallel degrees of the
+    base config fold into FSDP."""
+    p = c.parallelism
+    p.tensor_parallel_degree = p.context_parallel_degree = p.pipeline_parallel_degree = 1
+    p.expert_parallel_degree = p.expert_tensor_parallel_degree = 1
+    return c
+
+
+def graph_trainer_llama3_debugmodel_flex_attn() -> GraphTrainer.Config:
+    """Packed documents (block-causal masks): positions and document ids are graph inputs."""
+    return to_graph_trainer_config(llama3_configs.llama3_debugmodel_flex_attn())
+
+
+def graph_trainer_llama3_70b() -> GraphTrainer.Config:
+    return _data_parallel_only(to_graph_trainer_config(llama3_configs.llama3_70b()))
+
+
+def graph_trainer_llama3_405b() -> GraphTrainer.Config:
+    return _data_parallel_only(to_graph_trainer_config(llama3_configs.llama3_405b()))
+
+
+def graph_trainer_deepseek_v3_671b() -> GraphTrainer.Config:
+    return _data_parallel_only(to_graph_trainer_config(deepseek_v3_configs.deepseek_v3_671b()))
